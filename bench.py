@@ -1,0 +1,357 @@
+"""Benchmark of the sparse-convolution hot path.
+
+Workload (one "step" = one pass of the whole path over one object): the
+64^3 ellipsoid-shell active set (seed 0), C = 256:
+  coordinate hash -> submanifold kernel map -> subm conv3 (+ GroupNorm partial
+  sums) -> GroupNorm(32) finalize -> SiLU -> subm conv3 -> + skip,
+bf16 tcgen05 MMAs with f32 accumulation. Metric: active-voxel outputs/s, one
+unit = one output voxel of one conv layer (2 * N per step).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Multi-GPU (torchrun, one rank per GPU): objects are independent, so each rank
+runs its own object (seed = rank) with no data-path collective ("weak"
+scaling); timing is the max over ranks.
+
+`--impl reference` times the reference path on the host cores instead: the
+reference's own table builder (oracle/_ref, when it was built) plus the CPU
+restatement of its GGML op order, all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for sub in ("sam3d.cpp_b200", "oracle"):
+    sys.path.insert(0, os.path.join(ROOT, sub))
+
+METRIC = "active-voxel outputs/s per GPU (C=256 subm conv)"
+UNIT = "voxel-outputs/s"
+L2_FLUSH_BYTES = 512 << 20  # > 126 MB L2
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        return pk["hbm_gbs"], pk["bf16_tflops"], pk.get("bf16_tflops_sustained"), "measured"
+    except Exception:
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples during the timed region (recipe's clocks line)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# our path
+# ---------------------------------------------------------------------------
+class ResBlockPath:
+    """Config-2 residual block through the s3dsp C-ABI (device-resident)."""
+
+    def __init__(self, s3dsp, ctx, cfg, torch, device):
+        self.s, self.ctx, self.torch = s3dsp, ctx, torch
+        t = torch
+        c = cfg["channels"]
+        n = len(cfg["coords"])
+        self.n, self.c = n, c
+        dev = lambda a: t.from_numpy(np.ascontiguousarray(a)).to(device)  # noqa: E731
+        self.coords = dev(cfg["coords"])
+        self.x = dev(cfg["feats"])
+        P = s3dsp.PREC_BF16
+        self.w1 = t.empty(s3dsp.Context.packed_bytes(P, 27, c, c), dtype=t.uint8, device=device)
+        self.w2 = t.empty_like(self.w1)
+        ctx.weights_pack(t.from_numpy(cfg["w1"]), s3dsp.LAYOUT_SLAT_ROW, 27, c, c, P, self.w1)
+        ctx.weights_pack(t.from_numpy(cfg["w2"]), s3dsp.LAYOUT_SLAT_ROW, 27, c, c, P, self.w2)
+        self.b1, self.b2 = dev(cfg["b1"]), dev(cfg["b2"])
+        self.gamma, self.beta = dev(cfg["gamma"]), dev(cfg["beta"])
+        self.part = t.empty(s3dsp.Context.gn_partials_count(n, c, 32), dtype=t.float64, device=device)
+        self.sub, self.mul, self.add = (t.empty(c, device=device) for _ in range(3))
+        self.xb = t.empty((n, c), dtype=t.bfloat16, device=device)
+        self.y1 = t.empty((n, c), dtype=t.float32, device=device)
+        self.hb = t.empty((n, c), dtype=t.bfloat16, device=device)
+        self.out = t.empty((n, c), dtype=t.float32, device=device)
+        self.conv_events = []
+        self.launches_per_step = 8  # insert, self-row, kmap, convert, conv1, finalize, affine, conv2
+
+    def step(self, time_convs=False, coords=None, x=None):
+        s, ctx, t = self.s, self.ctx, self.torch
+        coords = self.coords if coords is None else coords
+        x = self.x if x is None else x
+        h = ctx.hash_build(coords)
+        k = ctx.kmap_subm3(h)
+        ctx.convert(x, self.xb)
+        ev = None
+        if time_convs:
+            ev = [t.cuda.Event(enable_timing=True) for _ in range(4)]
+            ev[0].record()
+        ctx.conv(k, 27, s.PREC_BF16, self.xb, self.w1, self.b1, self.y1, self.c, gn_partials=self.part, gn_groups=32)
+        if time_convs:
+            ev[1].record()
+        ctx.gn_finalize(self.part, self.n, self.c, 32, 1e-5, self.gamma, self.beta, self.sub, self.mul, self.add)
+        ctx.channel_affine(self.y1, self.sub, self.mul, self.add, True, self.hb)
+        if time_convs:
+            ev[2].record()
+        ctx.conv(k, 27, s.PREC_BF16, self.hb, self.w2, self.b2, self.out, self.c, residual=x)
+        if time_convs:
+            ev[3].record()
+            self.conv_events.append(ev)
+        return h, k
+
+
+def pairs_of(ctx, path, torch):
+    """Valid (in, out) pairs of the kernel map, counted by the library itself."""
+    h = ctx.hash_build(path.coords)
+    k = ctx.kmap_subm3(h)
+    cap = 27 * path.n
+    pin = torch.empty(cap, dtype=torch.int32, device=path.coords.device)
+    pout = torch.empty_like(pin)
+    return int(ctx.kmap_pairs(k, pin, pout)[27])
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import s3dsp
+    import workloads
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    cfg = workloads.config2(seed=0)
+    if rank > 0:  # every rank its own object (independent objects, weak scaling)
+        cfg["coords"] = workloads.ellipsoid_shell(64, rank)
+        cfg["feats"] = workloads.normal((len(cfg["coords"]), cfg["channels"]), 1000 + rank)
+    ctx = s3dsp.Context(local_rank, flags=s3dsp.CONTEXT_DEFERRED_CHECKS)
+    path = ResBlockPath(s3dsp, ctx, cfg, torch, device)
+    n, c = path.n, path.c
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    for _ in range(args.warmup):
+        path.step()
+        flush.fill_(1.0)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.3)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        starts[i].record(stream)
+        path.step(time_convs=True)
+        ends[i].record(stream)
+        flush.fill_(1.0)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    dev_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    conv_ms = [(ev[0].elapsed_time(ev[1]), ev[2].elapsed_time(ev[3])) for ev in path.conv_events]
+
+    # ---- e2e: host buffers in, host result out, through the same C-ABI calls ----
+    coords_h = torch.from_numpy(cfg["coords"]).pin_memory()
+    x_h = torch.from_numpy(cfg["feats"]).pin_memory()
+    out_h = torch.empty((n, c), dtype=torch.float32).pin_memory()
+    coords_d = torch.empty_like(path.coords)
+    x_d = torch.empty_like(path.x)
+    e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for i in range(args.steps + args.warmup):
+        j = i - args.warmup
+        if j >= 0:
+            e_starts[j].record(stream)
+        coords_d.copy_(coords_h, non_blocking=True)
+        x_d.copy_(x_h, non_blocking=True)
+        path.step(coords=coords_d, x=x_d)
+        out_h.copy_(path.out, non_blocking=True)
+        if j >= 0:
+            e_ends[j].record(stream)
+        flush.fill_(1.0)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    e2e_ms = sum(s.elapsed_time(e) for s, e in zip(e_starts, e_ends))
+    h2d = coords_h.numel() * 4 + x_h.numel() * 4
+    d2h = out_h.numel() * 4
+    ctx.check()
+
+    # max over ranks
+    vals = torch.tensor([dev_ms, e2e_ms], dtype=torch.float64, device=device)
+    units = torch.tensor([2.0 * n * args.steps], dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX)
+        torch.distributed.all_reduce(units, op=torch.distributed.ReduceOp.SUM)
+    dev_ms, e2e_ms = vals.tolist()
+    total_units = units.item()
+    if rank != 0:
+        return None
+
+    value = total_units / (dev_ms / 1e3)
+    e2e_value = total_units / (e2e_ms / 1e3)
+    hbm, tflops, tflops_sus, peak_src = load_peaks()
+    P = pairs_of(ctx, path, torch)
+    flops = 2.0 * c * c * P  # algorithmic: valid (in, out) pairs only
+    conv_avg_ms = float(np.mean([a for a, b in conv_ms] + [b for a, b in conv_ms]))
+    achieved = flops / (conv_avg_ms / 1e3) / 1e12
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded ellipsoid shells, random-init weights)",
+        "config": {"workload": "config2: 64^3 shell res block C=256 (subm conv3 -> GN32 -> SiLU -> subm conv3 -> "
+                               "+skip), hash + kmap rebuilt every step",
+                   "voxels": n, "pairs": P, "channels": c, "objects_per_gpu": 1, "parallelism": f"objects-dp{world}",
+                   "l2": "flushed between steps (512 MiB write)"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": tflops, "unit": "TFLOP/s",
+                     "frac": achieved / tflops, "traffic": None,
+                     "kernel": "conv_tc_kernel", "flops_per_launch": flops, "avg_launch_ms": conv_avg_ms,
+                     "peak_source": f"{peak_src} bf16_tflops (burst)"},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": path.launches_per_step * (args.steps * 2 + args.warmup * 2),
+        "clocks": clocks,
+        "wall_s": wall,
+    }
+    if world == 1:
+        line["cpu_baseline"] = cpu_baseline(cfg, sample_only=True)
+    return line
+
+
+# ---------------------------------------------------------------------------
+# CPU path (reference arm and cpu_baseline)
+# ---------------------------------------------------------------------------
+def cpu_step(cfg, threads):
+    import oracle
+    coords = cfg["coords"]
+    n = len(coords)
+    use_ref = oracle.ref_available()
+    t = oracle.slat_tables(coords, use_ref=use_ref)
+    nbr = t["conv_fine"].reshape(n, 27)
+    out = oracle.resblock_gn(cfg["feats"], nbr, cfg["w1"], cfg["b1"], cfg["gamma"], cfg["beta"], cfg["w2"],
+                             cfg["b2"], threads=threads)
+    return out, use_ref
+
+
+def cpu_baseline(cfg, sample_only=False, steps=1, warmup=0):
+    threads = os.cpu_count() or 1
+    for _ in range(warmup):
+        cpu_step(cfg, threads)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        _, use_ref = cpu_step(cfg, threads)
+    dt = (time.perf_counter() - t0) / steps
+    n = len(cfg["coords"])
+    return {"value": 2.0 * n / dt, "unit": UNIT, "cores": threads,
+            "kind": "reference" if use_ref else "port",
+            "sample": f"one full config-2 step ({n} voxels, 2 conv layers) per timing; tables by "
+                      f"{'the reference sparse_ops.cpp' if use_ref else 'the oracle restatement'}, float ops by "
+                      "the oracle's restatement of the GGML op order (f32)",
+            "s_per_step": dt}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    import workloads
+    cfg = workloads.config2(seed=0)
+    steps = max(1, min(args.steps, 3))
+    cb = cpu_baseline(cfg, steps=steps, warmup=min(args.warmup, 1))
+    return {
+        "metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": world, "steps": steps,
+        "warmup": min(args.warmup, 1), "ms_per_step": cb["s_per_step"] * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config2: 64^3 shell res block C=256, hash/tables + block per step",
+                   "voxels": len(cfg["coords"]), "channels": cfg["channels"]},
+        "impl": "reference",
+        "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+    else:
+        if world > 1:
+            import datetime
+            import torch
+            torch.cuda.set_device(local_rank)
+            torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                                 device_id=torch.device("cuda", local_rank))
+        line = run_ours(args, rank, world, local_rank)
+        if world > 1:
+            import torch
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,230 @@
+/*
+ * s3dsp — B200 (sm_100a) sparse-convolution library for the SAM 3D Objects
+ * structured-latent path: coordinate hash, kernel maps, implicit-gather
+ * GEMM convolutions and their fused epilogues.
+ *
+ * Drop-in boundary. In sam3d.cpp this path is reached through internal C++:
+ *   - decode_object_mesh            src/objects_runtime/session.cpp:895-996
+ *   - the SLat sampling loop        src/objects_runtime/session.cpp:1564-1763
+ * which build host tables (src/objects_runtime/sparse_ops.hpp:11-78) and GGML
+ * graphs (mesh_decoder_graph.cpp:42-132, slat_flow_graph.cpp:112-275) and run
+ * them through Backend (backend.hpp:16-92). Each entry point below names the
+ * reference piece it replaces.
+ *
+ * Conventions mirror the reference's public C API (include/sam3d.h:20-40):
+ *   - every fallible call returns s3d_status and takes a caller-owned error
+ *     buffer (error, error_capacity): success clears it, failure writes a
+ *     truncated NUL-terminated message; NULL,0 discards diagnostics;
+ *   - opaque handles with create/free; no exceptions, STL or struct layouts
+ *     cross the ABI; plain pointers and sizes only;
+ *   - device pointers passed in are caller-owned and must stay valid until the
+ *     work queued on the context's stream has finished;
+ *   - a context (and everything created from it) is not thread-safe; separate
+ *     contexts may be used concurrently.
+ * All work is queued on the context's CUDA stream. Unless stated otherwise a
+ * call returns once the work is queued (stream order), not completed.
+ */
+#ifndef S3DSP_H
+#define S3DSP_H
+
+#include <stdint.h>
+
+#define S3DSP_API __attribute__((visibility("default")))
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same values as include/sam3d.h:22-26 in the reference. */
+typedef uint32_t s3d_status;
+#define S3D_OK UINT32_C(0)
+#define S3D_INVALID_ARGUMENT UINT32_C(1)
+#define S3D_OUT_OF_MEMORY UINT32_C(2)
+#define S3D_INTERNAL_ERROR UINT32_C(3)
+
+typedef struct s3dsp_context s3dsp_context;
+typedef struct s3dsp_hash s3dsp_hash;
+typedef struct s3dsp_kmap s3dsp_kmap;
+
+/* element types */
+#define S3DSP_F32 UINT32_C(0)
+#define S3DSP_BF16 UINT32_C(1)
+#define S3DSP_F16 UINT32_C(2)
+
+/* arithmetic of a convolution */
+#define S3DSP_PREC_F32_STRICT UINT32_C(0) /* f32 FMA, f32 accumulation */
+#define S3DSP_PREC_BF16 UINT32_C(1)       /* bf16 tcgen05 MMA, f32 accumulation in TMEM */
+
+/* weight layouts accepted by s3dsp_weights_pack (all row-major as stored in GGUF) */
+#define S3DSP_LAYOUT_SLAT_ROW UINT32_C(0)    /* (Cout, 27, Cin): scripts/objects/gguf_schema.py:326-334 */
+#define S3DSP_LAYOUT_MESH_PACKED UINT32_C(1) /* (kvol, Cout, Cin): convert_sam3d_to_gguf.py:481-492 */
+#define S3DSP_LAYOUT_LINEAR UINT32_C(2)      /* (Cout, Cin): gb_linear weights, graph_builder.cpp:44-54 */
+#define S3DSP_LAYOUT_SPCONV_1X1 UINT32_C(3)  /* raw spconv (Cout,1,1,1,Cin) buffer read as (Cin, Cout),
+                                                the 1x1 quirk of convert_sam3d_to_gguf.py:483-488 */
+#define S3DSP_LAYOUT_TRANSPOSED_2X2X2 UINT32_C(4) /* (8, Cout, Cin): learned stride-2 subdivide, child
+                                                     j = xb*4+yb*2+zb (no reference counterpart) */
+
+/* dense neighbour-table export formats */
+#define S3DSP_SENTINEL_SLAT_N UINT32_C(0)   /* missing -> n (zero row), sparse_ops.hpp:24-29 */
+#define S3DSP_SENTINEL_MESH_NEG1 UINT32_C(1) /* missing -> -1, sparse_ops.cpp:367 */
+
+/* conv epilogue / prologue flags */
+#define S3DSP_EPI_SILU UINT32_C(1)      /* apply SiLU after bias (and residual) */
+#define S3DSP_PRO_AFFINE_SILU UINT32_C(2) /* gathered x -> silu((x - sub[c]) * mul[c] + add[c]) */
+
+/* context flags */
+#define S3DSP_CONTEXT_DEFERRED_CHECKS UINT32_C(1) /* device-detected input errors are reported by
+                                                     s3dsp_context_check instead of at each call */
+
+S3DSP_API uint32_t s3dsp_abi_version(void);
+
+/* ---------------------------------------------------------------------------
+ * Context: one CUDA device + one stream (replaces the per-stage Backend,
+ * backend.cpp:44-118). `stream` is a cudaStream_t or NULL for a new stream.
+ * ------------------------------------------------------------------------- */
+S3DSP_API s3d_status s3dsp_context_create(int32_t device, void *stream, uint32_t flags,
+                                          s3dsp_context **out, char *error,
+                                          uint64_t error_capacity);
+S3DSP_API void s3dsp_context_free(s3dsp_context *ctx);
+S3DSP_API void *s3dsp_context_stream(const s3dsp_context *ctx);
+/* Waits for the stream and reports (then clears) any device-detected input
+ * error recorded since the last check. */
+S3DSP_API s3d_status s3dsp_context_check(s3dsp_context *ctx, char *error, uint64_t error_capacity);
+
+/* ---------------------------------------------------------------------------
+ * K1 coordinate hash. Replaces the std::map / unordered_map indexes of
+ * SlatTables::build (sparse_ops.cpp:119-124) and MeshSubdivideTables::build
+ * (sparse_ops.cpp:299-333; FNV key hash :32-45).
+ * d_coords: device int32 [n, 4] rows (batch, x, y, z); the hash keeps its own
+ * copy. Domain: 0 <= batch < 32768 and -32768 <= x, y, z < 32768. Duplicate
+ * coordinates keep the first row (the reference's std::map emplace rule);
+ * `reject_duplicates` makes them an error instead (MeshSubdivideTables,
+ * sparse_ops.cpp:325-333). Synchronous check unless DEFERRED_CHECKS.
+ * ------------------------------------------------------------------------- */
+S3DSP_API s3d_status s3dsp_hash_build(s3dsp_context *ctx, const int32_t *d_coords, int64_t n,
+                                      int32_t reject_duplicates, s3dsp_hash **out, char *error,
+                                      uint64_t error_capacity);
+S3DSP_API void s3dsp_hash_free(s3dsp_context *ctx, s3dsp_hash *hash);
+S3DSP_API int64_t s3dsp_hash_size(const s3dsp_hash *hash);
+/* d_rows[i] = first row whose coords equal d_query[i], or -1. */
+S3DSP_API s3d_status s3dsp_hash_lookup(s3dsp_context *ctx, const s3dsp_hash *hash,
+                                       const int32_t *d_query, int64_t m, int32_t *d_rows,
+                                       char *error, uint64_t error_capacity);
+
+/* ---------------------------------------------------------------------------
+ * K2 kernel maps. A kmap holds, per kernel offset o (o = kd*9 + kh*3 + kw with
+ * (dx,dy,dz) = (kd-1, kh-1, kw-1), sparse_ops.cpp:132), the input row feeding
+ * every output row (offset-major [kvol][n_out], -1 = none) plus a per-tile
+ * bitmask of offsets that have any neighbour.
+ * ------------------------------------------------------------------------- */
+/* Submanifold 3x3x3 map of a coordinate set onto itself: SlatTables
+ * conv_fine / conv_coarse (sparse_ops.cpp:126-142). Rows that duplicate an
+ * earlier row's coordinates get no neighbours (reference behaviour). */
+S3DSP_API s3d_status s3dsp_kmap_build_subm3(s3dsp_context *ctx, const s3dsp_hash *hash,
+                                            s3dsp_kmap **out, char *error,
+                                            uint64_t error_capacity);
+/* Stride-2 subdivide of a parent set: MeshSubdivideTables::build
+ * (sparse_ops.cpp:272-404). Writes the 8*n child coords (child row =
+ * parent*8 + xb*4 + yb*2 + zb, coords 2p + bits) to d_child_coords [8n, 4]
+ * and returns the child submanifold map. `parents` must be built with
+ * reject_duplicates. */
+S3DSP_API s3d_status s3dsp_subdivide(s3dsp_context *ctx, const s3dsp_hash *parents,
+                                     int32_t *d_child_coords, s3dsp_kmap **out_child_kmap,
+                                     char *error, uint64_t error_capacity);
+S3DSP_API void s3dsp_kmap_free(s3dsp_context *ctx, s3dsp_kmap *kmap);
+S3DSP_API int64_t s3dsp_kmap_rows(const s3dsp_kmap *kmap);
+/* Dense row-major [n_out, 27] table in the reference's format (bit-exact with
+ * SlatTables::conv_fine for SLAT_N, MeshSubdivideTables::neighbors for
+ * MESH_NEG1). d_out is a device buffer of n_out*27 int32. */
+S3DSP_API s3d_status s3dsp_kmap_export_dense(s3dsp_context *ctx, const s3dsp_kmap *kmap,
+                                             uint32_t sentinel_mode, int32_t *d_out, char *error,
+                                             uint64_t error_capacity);
+/* Offset-sorted (in, out) pair lists: for each offset o in order, the pairs
+ * with a neighbour, sorted by output row. d_in/d_out hold capacity int32
+ * each (27*n_out always suffices); h_offsets receives kvol+1 host int64
+ * start offsets. Synchronous. */
+S3DSP_API s3d_status s3dsp_kmap_pairs(s3dsp_context *ctx, const s3dsp_kmap *kmap, int32_t *d_in,
+                                      int32_t *d_out, int64_t capacity, int64_t *h_offsets,
+                                      char *error, uint64_t error_capacity);
+
+/* ---------------------------------------------------------------------------
+ * Weights. Converts a GGUF-layout weight (host or device `src`, f32/f16/bf16)
+ * into the device layout a conv of `precision` consumes, at d_dst (size from
+ * s3dsp_weights_packed_bytes). kvol = 27 (subm), 8 (transposed 2x2x2) or 1.
+ * Replaces the load-time as_f32 casts (mesh_decoder_graph.cpp:10-12,
+ * slat_flow_graph.cpp:14-41).
+ * ------------------------------------------------------------------------- */
+S3DSP_API int64_t s3dsp_weights_packed_bytes(uint32_t precision, int32_t kvol, int64_t cin,
+                                             int64_t cout);
+S3DSP_API s3d_status s3dsp_weights_pack(s3dsp_context *ctx, const void *src, uint32_t src_dtype,
+                                        int32_t src_on_host, uint32_t layout, int32_t kvol,
+                                        int64_t cin, int64_t cout, uint32_t precision,
+                                        void *d_dst, char *error, uint64_t error_capacity);
+
+/* ---------------------------------------------------------------------------
+ * K3+K4 sparse convolution (implicit gather GEMM, no atomics on outputs):
+ *   out[r] = epi( sum_o W_o * pro(in[nbr_o(r) >> in_shift]) + bias
+ *                 + residual[r >> res_shift] )
+ * kmap == NULL means the identity map with kvol 1 (a Linear / 1x1 conv,
+ * gb_linear graph_builder.cpp:44-54, or the mesh skip mesh_decoder_graph.cpp:
+ * 126-129 with in_shift 3). Replaces the conv lambda of slat_flow_graph.cpp:
+ * 112-155 and the convolution lambda of mesh_decoder_graph.cpp:81-103;
+ * in_shift = 3 fuses repeat_children (:32-38).
+ *   in:        [n_in, cin] of in_dtype (BF16 precision needs BF16 input)
+ *   weight:    packed by s3dsp_weights_pack for `precision`
+ *   bias:      f32 [cout] or NULL
+ *   residual:  [*, cout] of res_dtype or NULL
+ *   out:       [n_out, cout] of out_dtype
+ *   pro_sub/pro_mul/pro_add: f32 [cin] when flags has PRO_AFFINE_SILU
+ *   gn_partials: NULL, or f64 [s3dsp_gn_partials_count(n_out, cout, groups)]
+ *              receiving per-tile GroupNorm sums of the output (pre-SiLU)
+ * ------------------------------------------------------------------------- */
+S3DSP_API int64_t s3dsp_gn_partials_count(int64_t n_rows, int64_t channels, int32_t groups);
+S3DSP_API s3d_status s3dsp_conv(s3dsp_context *ctx, const s3dsp_kmap *kmap, int32_t kvol,
+                                uint32_t precision, const void *in, uint32_t in_dtype,
+                                int64_t n_in, int64_t cin, int32_t in_shift, const void *weight,
+                                const float *bias, const void *residual, uint32_t res_dtype,
+                                int32_t res_shift, void *out, uint32_t out_dtype, int64_t n_out,
+                                int64_t cout, uint32_t flags, const float *pro_sub,
+                                const float *pro_mul, const float *pro_add, double *gn_partials,
+                                int32_t gn_groups, char *error, uint64_t error_capacity);
+
+/* ---------------------------------------------------------------------------
+ * K4 normalisations (sparse_group_norm mesh_decoder_graph.cpp:16-30;
+ * gb_layer_norm graph_builder.cpp:56-62; modulate slat_flow_graph.cpp:55-59).
+ * ------------------------------------------------------------------------- */
+/* GroupNorm statistics of x [n, c] into f64 partials (same buffer format the
+ * conv epilogue writes). */
+S3DSP_API s3d_status s3dsp_gn_stats(s3dsp_context *ctx, const void *x, uint32_t dtype, int64_t n,
+                                    int64_t c, int32_t groups, double *gn_partials, char *error,
+                                    uint64_t error_capacity);
+/* Reduces partials into per-channel sub/mul/add such that
+ * (x - sub) * mul + add == ((x - mean_g) * rstd_g) * gamma_c + beta_c. */
+S3DSP_API s3d_status s3dsp_gn_finalize(s3dsp_context *ctx, const double *gn_partials,
+                                       int64_t n_rows, int64_t c, int32_t groups, float eps,
+                                       const float *gamma, const float *beta, float *d_sub,
+                                       float *d_mul, float *d_add, char *error,
+                                       uint64_t error_capacity);
+/* y = act((x - sub[c]) * mul[c] + add[c]) with act = SiLU when silu != 0. */
+S3DSP_API s3d_status s3dsp_channel_affine(s3dsp_context *ctx, const void *x, uint32_t x_dtype,
+                                          int64_t n, int64_t c, const float *sub,
+                                          const float *mul, const float *add, int32_t silu,
+                                          void *y, uint32_t y_dtype, char *error,
+                                          uint64_t error_capacity);
+/* Per-row LayerNorm (eps), optional affine gamma/beta, optional modulate
+ * h*(1+scale)+shift, optional SiLU. */
+S3DSP_API s3d_status s3dsp_layer_norm(s3dsp_context *ctx, const void *x, uint32_t x_dtype,
+                                      int64_t n, int64_t c, float eps, const float *gamma,
+                                      const float *beta, const float *mod_scale,
+                                      const float *mod_shift, int32_t silu, void *y,
+                                      uint32_t y_dtype, char *error, uint64_t error_capacity);
+/* Element type conversion of count elements. */
+S3DSP_API s3d_status s3dsp_convert(s3dsp_context *ctx, const void *x, uint32_t x_dtype, void *y,
+                                   uint32_t y_dtype, int64_t count, char *error,
+                                   uint64_t error_capacity);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* S3DSP_H */

@@ -1,0 +1,276 @@
+"""TEST INFRASTRUCTURE ONLY: ctypes front-end of the CPU oracle.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg import
+this module, as the checker or as the timed CPU comparator — never the product
+path. Two libraries are reachable from here:
+
+* ``libs3d_oracle.so`` — our restatement (oracle/s3d_oracle.cpp). Integer
+  tables are pinned bit-exactly to the reference; the float ops restate the
+  reference's GGML op order and are PARITY UNPINNED against GGML itself (the
+  GGML submodule is absent), cross-checked against dense float64 torch ops.
+* ``_ref/libsparse_ops_ref.so`` — the reference's own sparse_ops.cpp
+  (SlatTables::build, MeshSubdivideTables::build) compiled unchanged, when it
+  was built (it needs the reference tree at build time).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "libs3d_oracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libsparse_ops_ref.so")
+
+_i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_c_i64 = ctypes.c_int64
+_c_i32 = ctypes.c_int32
+_vp = ctypes.c_void_p
+
+_lib = None
+_ref = None
+
+
+def build_oracle() -> str:
+    """Compile the restatement (gcc only; works on any box with the image)."""
+    subprocess.run(["make", "-s", "-C", HERE, "libs3d_oracle.so"], check=True)
+    return ORACLE_SO
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(ORACLE_SO) or (
+                os.path.getmtime(ORACLE_SO) < os.path.getmtime(os.path.join(HERE, "s3d_oracle.cpp"))):
+            build_oracle()
+        L = ctypes.CDLL(ORACLE_SO)
+        L.oracle_slat_tables.restype = _c_i64
+        L.oracle_slat_tables.argtypes = [_i32p, _c_i64, _i32p, _i32p, _f32p, _i32p, _i32p, _i32p]
+        L.oracle_mesh_subdivide.restype = _c_i32
+        L.oracle_mesh_subdivide.argtypes = [_i32p, _c_i64, _i32p, _i32p]
+        L.oracle_subm_conv_slat.restype = None
+        L.oracle_subm_conv_slat.argtypes = [_f32p, _c_i64, _c_i64, _i32p, _c_i64, _f32p, _vp,
+                                            _c_i64, _f32p, _c_i32, _c_i32]
+        L.oracle_subm_conv_mesh.restype = None
+        L.oracle_subm_conv_mesh.argtypes = [_f32p, _c_i64, _c_i64, _vp, _c_i32, _c_i32, _c_i64,
+                                            _f32p, _vp, _c_i64, _f32p, _c_i32, _c_i32]
+        L.oracle_linear.restype = None
+        L.oracle_linear.argtypes = [_f32p, _c_i64, _c_i64, _c_i32, _f32p, _vp, _c_i64, _f32p,
+                                    _c_i32]
+        L.oracle_group_norm.restype = None
+        L.oracle_group_norm.argtypes = [_f32p, _c_i64, _c_i64, _c_i32, ctypes.c_float, _vp, _vp,
+                                        _c_i32, _f32p]
+        L.oracle_layer_norm.restype = None
+        L.oracle_layer_norm.argtypes = [_f32p, _c_i64, _c_i64, ctypes.c_float, _vp, _vp, _vp, _vp,
+                                        _c_i32, _f32p]
+        L.oracle_downsample_mean.restype = None
+        L.oracle_downsample_mean.argtypes = [_f32p, _c_i64, _c_i64, _i32p, _f32p, _c_i64, _f32p]
+        L.oracle_upsample_nearest.restype = None
+        L.oracle_upsample_nearest.argtypes = [_f32p, _c_i64, _c_i64, _i32p, _c_i64, _f32p]
+        _lib = L
+    return _lib
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_SO)
+
+
+def ref_lib():
+    global _ref
+    if _ref is None:
+        if not ref_available():
+            raise FileNotFoundError("reference table builder not built: " + REF_SO)
+        L = ctypes.CDLL(REF_SO)
+        L.ref_slat_tables.restype = _c_i64
+        L.ref_slat_tables.argtypes = [_i32p, _c_i64, _c_i32, _i32p, _i32p, _f32p, _i32p, _i32p]
+        L.ref_mesh_subdivide.restype = _c_i32
+        L.ref_mesh_subdivide.argtypes = [_i32p, _c_i64, _i32p, _i32p]
+        _ref = L
+    return _ref
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _c(a, dt):
+    return np.ascontiguousarray(a, dtype=dt)
+
+
+# ---------------------------------------------------------------------------
+# integer tables
+# ---------------------------------------------------------------------------
+def slat_tables(coords: np.ndarray, use_ref: bool = False) -> dict | None:
+    """SlatTables (sparse_ops.cpp:49-173). Returns None when the builder fails."""
+    coords = _c(coords, np.int32).reshape(-1, 4)
+    nf = len(coords)
+    f2c = np.zeros(max(nf, 1), np.int32)
+    ch = np.zeros(max(8 * nf, 1), np.int32)
+    inv = np.zeros(max(nf, 1), np.float32)
+    cf = np.zeros(max(27 * nf, 1), np.int32)
+    cc = np.zeros(max(27 * nf, 1), np.int32)
+    if use_ref:
+        nc = ref_lib().ref_slat_tables(coords.reshape(-1) if nf else np.zeros(4, np.int32), nf, 6,
+                                       f2c, ch, inv, cf, cc)
+        ccoords = None
+    else:
+        ccoords = np.zeros(max(4 * nf, 1), np.int32)
+        nc = lib().oracle_slat_tables(coords.reshape(-1) if nf else np.zeros(4, np.int32), nf,
+                                      f2c, ch, inv, cf, cc, ccoords)
+    if nc < 0:
+        return None
+    out = dict(nf=nf, nc=int(nc), fine_to_coarse=f2c[:nf], coarse_children=ch[:8 * nc],
+               coarse_inv_count=inv[:nc], conv_fine=cf[:27 * nf], conv_coarse=cc[:27 * nc])
+    if ccoords is not None:
+        out["coarse_coords"] = ccoords[:4 * nc].reshape(nc, 4)
+    return out
+
+
+def mesh_subdivide(parents: np.ndarray, use_ref: bool = False):
+    """MeshSubdivideTables (sparse_ops.cpp:272-404) -> (child_coords [8N,4],
+    neighbors [8N,27]) or None when the builder rejects the input."""
+    parents = _c(parents, np.int32).reshape(-1, 4)
+    n = len(parents)
+    cc = np.zeros(max(32 * n, 4), np.int32)
+    nb = np.zeros(max(8 * 27 * n, 1), np.int32)
+    src = parents.reshape(-1) if n else np.zeros(4, np.int32)
+    ok = (ref_lib().ref_mesh_subdivide if use_ref else lib().oracle_mesh_subdivide)(src, n, cc, nb)
+    if not ok:
+        return None
+    return cc[:32 * n].reshape(8 * n, 4), nb[:8 * 27 * n].reshape(8 * n, 27)
+
+
+# ---------------------------------------------------------------------------
+# float ops (GGML order restatement; see module docstring)
+# ---------------------------------------------------------------------------
+def subm_conv_slat(feat, nbr, w_slat, bias, accum64=False, threads=0):
+    """SLat SubMConv3d: feat [n_in, Cin], nbr [n_out, 27] (entries outside
+    [0, n_in) read zeros), w_slat [Cout, 27*Cin] -> [n_out, Cout]."""
+    feat = _c(feat, np.float32)
+    n_in, cin = feat.shape
+    nbr = _c(nbr, np.int32).reshape(-1, 27)
+    cout = w_slat.shape[0]
+    out = np.empty((len(nbr), cout), np.float32)
+    lib().oracle_subm_conv_slat(feat.reshape(-1), n_in, cin, nbr.reshape(-1), len(nbr),
+                                _c(w_slat, np.float32).reshape(-1),
+                                _ptr(_c(bias, np.float32) if bias is not None else None), cout,
+                                out.reshape(-1), int(accum64), threads)
+    return out
+
+
+def subm_conv_mesh(feat, nbr, w_packed, bias, cout, kvol=27, gather_shift=0, n_out=None,
+                   accum64=False, threads=0):
+    """mesh SubMConv3d: per-offset GEMMs summed o=0..kvol-1, then bias.
+    w_packed [kvol, Cout*Cin]; nbr [n_out, 27] with -1 = missing (ignored for
+    kvol == 1); gathered rows are (src >> gather_shift)."""
+    feat = _c(feat, np.float32)
+    n_in, cin = feat.shape
+    if kvol == 1:
+        nbr_arr = None
+        assert n_out is not None
+    else:
+        nbr_arr = _c(nbr, np.int32).reshape(-1, 27)
+        n_out = len(nbr_arr)
+    out = np.empty((n_out, cout), np.float32)
+    keep = bias if bias is None else _c(bias, np.float32)
+    lib().oracle_subm_conv_mesh(feat.reshape(-1), n_in, cin, _ptr(nbr_arr), kvol, gather_shift,
+                                n_out, _c(w_packed, np.float32).reshape(-1), _ptr(keep), cout,
+                                out.reshape(-1), int(accum64), threads)
+    return out
+
+
+def linear(x, w, bias, row_shift=0, n_out=None, threads=0):
+    """gb_linear: x [n_in, Cin] @ W[Cout, Cin]^T + b; row r reads x[r >> row_shift]."""
+    x = _c(x, np.float32)
+    cin = x.shape[1]
+    cout = w.shape[0]
+    n_out = len(x) << row_shift if n_out is None else n_out
+    out = np.empty((n_out, cout), np.float32)
+    keep = bias if bias is None else _c(bias, np.float32)
+    lib().oracle_linear(x.reshape(-1), n_out, cin, row_shift, _c(w, np.float32).reshape(-1),
+                        _ptr(keep), cout, out.reshape(-1), threads)
+    return out
+
+
+def group_norm(x, groups, eps=1e-5, gamma=None, beta=None, silu=False):
+    x = _c(x, np.float32)
+    n, c = x.shape
+    out = np.empty_like(x)
+    g = None if gamma is None else _c(gamma, np.float32)
+    b = None if beta is None else _c(beta, np.float32)
+    lib().oracle_group_norm(x.reshape(-1), n, c, groups, eps, _ptr(g), _ptr(b), int(silu),
+                            out.reshape(-1))
+    return out
+
+
+def layer_norm(x, eps=1e-6, gamma=None, beta=None, mod_scale=None, mod_shift=None, silu=False):
+    x = _c(x, np.float32)
+    n, c = x.shape
+    out = np.empty_like(x)
+    keep = [None if a is None else _c(a, np.float32) for a in (gamma, beta, mod_scale, mod_shift)]
+    lib().oracle_layer_norm(x.reshape(-1), n, c, eps, *[_ptr(a) for a in keep], int(silu),
+                            out.reshape(-1))
+    return out
+
+
+def silu(x):
+    x = np.asarray(x, np.float32)
+    return (x / (np.float32(1.0) + np.exp(-x))).astype(np.float32)
+
+
+def downsample_mean(x, children, inv_count):
+    x = _c(x, np.float32)
+    nf, ch = x.shape
+    nc = len(inv_count)
+    out = np.empty((nc, ch), np.float32)
+    lib().oracle_downsample_mean(x.reshape(-1), nf, ch, _c(children, np.int32).reshape(-1),
+                                 _c(inv_count, np.float32), nc, out.reshape(-1))
+    return out
+
+
+def upsample_nearest(x, f2c):
+    x = _c(x, np.float32)
+    nc, ch = x.shape
+    f2c = _c(f2c, np.int32)
+    out = np.empty((len(f2c), ch), np.float32)
+    lib().oracle_upsample_nearest(x.reshape(-1), nc, ch, f2c, len(f2c), out.reshape(-1))
+    return out
+
+
+# ---------------------------------------------------------------------------
+# composite blocks (op sequences of the reference graphs)
+# ---------------------------------------------------------------------------
+def resblock_gn(feats, nbr_slat, w1, b1, gamma, beta, w2, b2, groups=32, eps=1e-5, threads=0):
+    """Config 2 residual block: conv3 -> GroupNorm(32) -> SiLU -> conv3 -> + x.
+    GroupNorm/SiLU follow mesh_decoder_graph.cpp:16-30/:117-121, the convs the
+    SLat single-GEMM form (slat_flow_graph.cpp:112-155)."""
+    h = subm_conv_slat(feats, nbr_slat, w1, b1, threads=threads)
+    h = group_norm(h, groups, eps, gamma, beta, silu=True)
+    h = subm_conv_slat(h, nbr_slat, w2, b2, threads=threads)
+    return h + feats
+
+
+def mesh_upsample_level(x, neighbors, p, threads=0, taps=None):
+    """MeshUpsampleGraph::build (mesh_decoder_graph.cpp:42-132) for one level.
+    x [Np, Cin] parent features, neighbors [8Np, 27] child table (-1 missing),
+    p: dict of gn1_w, gn1_b, conv1_w (packed [27, Cout*Cin]), conv1_b, gn2_w,
+    gn2_b, conv2_w, conv2_b, skip_w ([1, Cout*Cin] packed 1x1), skip_b."""
+    cin = x.shape[1]
+    cout = len(p["conv1_b"])
+    n_child = len(neighbors)
+    h = group_norm(x, 32, 1e-5, p["gn1_w"], p["gn1_b"], silu=True)          # norm1, silu1
+    h = subm_conv_mesh(h, neighbors, p["conv1_w"], p["conv1_b"], cout, 27, 3, threads=threads)
+    if taps is not None:
+        taps["conv1"] = h
+    h = group_norm(h, 32, 1e-5, p["gn2_w"], p["gn2_b"], silu=True)          # norm2, silu2
+    h = subm_conv_mesh(h, neighbors, p["conv2_w"], p["conv2_b"], cout, 27, 0, threads=threads)
+    if taps is not None:
+        taps["conv2"] = h
+    skip = subm_conv_mesh(x, None, p["skip_w"], p["skip_b"], cout, 1, 3, n_out=n_child,
+                          threads=threads)
+    if taps is not None:
+        taps["skip"] = skip
+    return h + skip

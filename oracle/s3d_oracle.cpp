@@ -1,0 +1,528 @@
+// TEST INFRASTRUCTURE ONLY — the CPU oracle for the sparse-convolution path.
+//
+// Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg load
+// this library, and only as the checker (or as the timed CPU comparator). The
+// product library never links, loads or falls back to it.
+//
+// What it restates (reference file:line in the sam3d.cpp tree):
+//   * integer tables
+//       - SlatTables::build            src/objects_runtime/sparse_ops.cpp:49-173
+//       - MeshSubdivideTables::build   src/objects_runtime/sparse_ops.cpp:272-404
+//     PINNED: tests compare these bit-exactly with the reference's own
+//     sparse_ops.cpp compiled into oracle/_ref, and with committed goldens.
+//   * float ops, in GGML graph order (GGML itself is an un-vendored submodule,
+//     ggml-org/ggml @ e91ded11 / v0.23.0, absent here)
+//       - SLat SubMConv3d as ONE K=27*Cin dot + bias
+//                                      src/objects_runtime/slat_flow_graph.cpp:112-155
+//       - mesh SubMConv3d as 27 per-offset GEMMs summed o=0..26, then bias
+//                                      src/objects_runtime/mesh_decoder_graph.cpp:81-103
+//       - sparse GroupNorm (all tokens of the object, eps 1e-5, then gamma/beta)
+//                                      src/objects_runtime/mesh_decoder_graph.cpp:16-30
+//       - LayerNorm (ggml_norm, eps 1e-6, optional affine)
+//                                      src/objects_runtime/graph_builder.cpp:56-62
+//       - SiLU, modulate h*(1+s)+sh    src/objects_runtime/slat_flow_graph.cpp:55-59
+//       - 2x mean-pool / nearest up    src/objects_runtime/slat_flow_graph.cpp:159-190
+//       - Linear (mul_mat + bias)      src/objects_runtime/graph_builder.cpp:44-54
+//     PARITY UNPINNED against GGML (its CPU kernels cannot be built here); the
+//     conv/norm semantics are instead cross-checked in tests against an
+//     independent dense torch.conv3d / group_norm / layer_norm in float64.
+//
+// Layouts follow GGML's ne order with channels fastest: a feature matrix of
+// (C, N) in GGML is stored here as N rows of C floats.
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <numeric>
+#include <thread>
+#include <vector>
+
+namespace {
+
+// ---------------------------------------------------------------------------
+// tiny parallel-for over [0, n) in contiguous chunks
+// ---------------------------------------------------------------------------
+template <class F>
+void parallel_for(int64_t n, int threads, F&& body) {
+    if (threads <= 0) threads = (int)std::max(1u, std::thread::hardware_concurrency());
+    if (n <= 0) return;
+    if (threads == 1 || n < 2 * threads) {
+        body(0, n);
+        return;
+    }
+    std::vector<std::thread> pool;
+    const int64_t chunk = (n + threads - 1) / threads;
+    for (int t = 0; t < threads; ++t) {
+        const int64_t lo = t * chunk, hi = std::min(n, lo + chunk);
+        if (lo >= hi) break;
+        pool.emplace_back([&, lo, hi] { body(lo, hi); });
+    }
+    for (auto& th : pool) th.join();
+}
+
+struct Coord {
+    int32_t b, x, y, z;
+};
+
+inline bool coord_less(const Coord& a, const Coord& c) {
+    if (a.b != c.b) return a.b < c.b;
+    if (a.x != c.x) return a.x < c.x;
+    if (a.y != c.y) return a.y < c.y;
+    return a.z < c.z;
+}
+inline bool coord_eq(const Coord& a, const Coord& c) {
+    return a.b == c.b && a.x == c.x && a.y == c.y && a.z == c.z;
+}
+
+// Sorted unique key set with "first row" payload: a sorted vector searched by
+// binary search. (The reference uses std::map; only the lookup semantics —
+// exact key match, first inserted row wins — matter.)
+struct SortedIndex {
+    std::vector<Coord> keys;
+    std::vector<int32_t> rows;
+
+    void build(const std::vector<Coord>& pts) {
+        std::vector<int32_t> order(pts.size());
+        std::iota(order.begin(), order.end(), 0);
+        // stable: among equal keys the smallest row comes first
+        std::stable_sort(order.begin(), order.end(), [&](int32_t a, int32_t c) {
+            return coord_less(pts[(size_t)a], pts[(size_t)c]);
+        });
+        keys.clear();
+        rows.clear();
+        for (int32_t i : order) {
+            if (!keys.empty() && coord_eq(keys.back(), pts[(size_t)i])) continue;
+            keys.push_back(pts[(size_t)i]);
+            rows.push_back(i);
+        }
+    }
+    int32_t find(const Coord& k) const {
+        auto it = std::lower_bound(keys.begin(), keys.end(), k, coord_less);
+        if (it == keys.end() || !coord_eq(*it, k)) return -1;
+        return rows[(size_t)(it - keys.begin())];
+    }
+};
+
+// Offset o in [0,27): (dx, dy, dz) = (o/9-1, (o/3)%3-1, o%3-1) on (x, y, z).
+// sparse_ops.cpp:132 (SLat) and :351-352 / :375-377 (mesh).
+inline void offset_delta(int o, int& dx, int& dy, int& dz) {
+    dx = o / 9 - 1;
+    dy = (o / 3) % 3 - 1;
+    dz = o % 3 - 1;
+}
+
+inline int64_t floor_div2(int64_t v) { return v >= 0 ? v / 2 : -((-v + 1) / 2); }
+
+}  // namespace
+
+extern "C" {
+
+// ---------------------------------------------------------------------------
+// SlatTables restatement (sparse_ops.cpp:49-173, without the APE table)
+//
+// coords: nf rows of (b, x, y, z). Outputs sized by the caller for nc <= nf:
+//   fine_to_coarse[nf], coarse_children[8*nc], coarse_inv_count[nc],
+//   conv_fine[27*nf] (sentinel nf), conv_coarse[27*nc] (sentinel nc),
+//   coarse_coords[4*nc] (row order; not part of the reference struct but
+//   useful for tests). Returns nc, or -1 when nf <= 0 (sparse_ops.cpp:51).
+// ---------------------------------------------------------------------------
+int64_t oracle_slat_tables(const int32_t* coords, int64_t nf, int32_t* fine_to_coarse,
+                           int32_t* coarse_children, float* coarse_inv_count,
+                           int32_t* conv_fine, int32_t* conv_coarse, int32_t* coarse_coords) {
+    if (nf <= 0) return -1;
+    std::vector<Coord> fine((size_t)nf), coarse_of((size_t)nf);
+    for (int64_t i = 0; i < nf; ++i) {
+        const int32_t* c = coords + 4 * i;
+        fine[(size_t)i] = {c[0], c[1], c[2], c[3]};
+        // C++ integer division truncates toward zero (sparse_ops.cpp:63-64)
+        coarse_of[(size_t)i] = {c[0], c[1] / 2, c[2] / 2, c[3] / 2};
+    }
+    // coarse rows = sorted unique coarse keys (sparse_ops.cpp:53-71)
+    SortedIndex coarse;
+    coarse.build(coarse_of);
+    const int64_t nc = (int64_t)coarse.keys.size();
+    for (int64_t c = 0; c < nc; ++c) coarse.rows[(size_t)c] = (int32_t)c;  // row id = rank
+    std::vector<int32_t> counts((size_t)nc, 0);
+    for (int64_t i = 0; i < nf; ++i) {
+        const int32_t c = coarse.find(coarse_of[(size_t)i]);
+        fine_to_coarse[i] = c;
+        // children in increasing fine row order, at most 8 kept (:84-90)
+        const int32_t slot = counts[(size_t)c]++;
+        if (slot < 8) coarse_children[(size_t)c * 8 + slot] = (int32_t)i;
+    }
+    for (int64_t c = 0; c < nc; ++c) {
+        for (int32_t j = std::min(counts[(size_t)c], 8); j < 8; ++j)
+            coarse_children[(size_t)c * 8 + j] = (int32_t)nf;  // sentinel = zero row
+        // torch scatter_reduce "mean" counts the initial zero too (:93-96)
+        coarse_inv_count[c] = 1.0f / (float)(counts[(size_t)c] + 1);
+        if (coarse_coords) {
+            const Coord& k = coarse.keys[(size_t)c];
+            coarse_coords[4 * c + 0] = k.b;
+            coarse_coords[4 * c + 1] = k.x;
+            coarse_coords[4 * c + 2] = k.y;
+            coarse_coords[4 * c + 3] = k.z;
+        }
+    }
+    // submanifold neighbour tables (sparse_ops.cpp:117-142): only the first
+    // row of a duplicated key is filled; every other entry is the sentinel.
+    SortedIndex fidx;
+    fidx.build(fine);
+    auto fill = [](const SortedIndex& idx, int64_t n, int32_t* table) {
+        for (int64_t i = 0; i < 27 * n; ++i) table[i] = (int32_t)n;
+        for (size_t u = 0; u < idx.keys.size(); ++u) {
+            const Coord& k = idx.keys[u];
+            const int32_t row = idx.rows[u];
+            for (int o = 0; o < 27; ++o) {
+                int dx, dy, dz;
+                offset_delta(o, dx, dy, dz);
+                const int32_t hit = idx.find({k.b, k.x + dx, k.y + dy, k.z + dz});
+                if (hit >= 0) table[(size_t)row * 27 + o] = hit;
+            }
+        }
+    };
+    fill(fidx, nf, conv_fine);
+    fill(coarse, nc, conv_coarse);
+    return nc;
+}
+
+// ---------------------------------------------------------------------------
+// MeshSubdivideTables restatement (sparse_ops.cpp:272-404)
+//
+// Child row = parent*8 + (xb*4 + yb*2 + zb), coords 2p + bits (:334-343).
+// Neighbours are derived here from the CHILD geometry (floor division of the
+// neighbour child coordinate by two gives its parent), an independent route
+// to the same table the reference builds from 27 parent probes plus its
+// adjacent_offset/adjacent_child tables (:346-402). Missing -> -1.
+// Returns 1, or 0 on count <= 0, count > INT32_MAX/8, or a duplicate parent.
+// ---------------------------------------------------------------------------
+int32_t oracle_mesh_subdivide(const int32_t* parents, int64_t count, int32_t* child_coords,
+                              int32_t* neighbors) {
+    if (!parents || count <= 0 || count > INT32_MAX / 8) return 0;
+    std::vector<Coord> pts((size_t)count);
+    for (int64_t p = 0; p < count; ++p)
+        pts[(size_t)p] = {parents[4 * p], parents[4 * p + 1], parents[4 * p + 2], parents[4 * p + 3]};
+    SortedIndex idx;
+    idx.build(pts);
+    if ((int64_t)idx.keys.size() != count) return 0;  // duplicate parent (:325-333)
+    for (int64_t p = 0; p < count; ++p) {
+        const Coord& P = pts[(size_t)p];
+        for (int j = 0; j < 8; ++j) {
+            int32_t* cc = child_coords + 4 * (p * 8 + j);
+            cc[0] = P.b;
+            cc[1] = P.x * 2 + j / 4;
+            cc[2] = P.y * 2 + (j / 2) % 2;
+            cc[3] = P.z * 2 + j % 2;
+        }
+    }
+    for (int64_t p = 0; p < count; ++p) {
+        const Coord& P = pts[(size_t)p];
+        for (int j = 0; j < 8; ++j) {
+            const int64_t cx = (int64_t)P.x * 2 + j / 4, cy = (int64_t)P.y * 2 + (j / 2) % 2,
+                          cz = (int64_t)P.z * 2 + j % 2;
+            int32_t* row = neighbors + (p * 8 + j) * 27;
+            for (int o = 0; o < 27; ++o) {
+                int dx, dy, dz;
+                offset_delta(o, dx, dy, dz);
+                const int64_t tx = cx + dx, ty = cy + dy, tz = cz + dz;
+                const int32_t hit = idx.find({P.b, (int32_t)floor_div2(tx), (int32_t)floor_div2(ty),
+                                              (int32_t)floor_div2(tz)});
+                if (hit < 0) {
+                    row[o] = -1;
+                } else {
+                    const int bits = (int)((tx - 2 * floor_div2(tx)) * 4 + (ty - 2 * floor_div2(ty)) * 2 +
+                                           (tz - 2 * floor_div2(tz)));
+                    row[o] = hit * 8 + bits;
+                }
+            }
+        }
+    }
+    return 1;
+}
+
+// ---------------------------------------------------------------------------
+// Register-blocked f32 micro-kernel shared by both conv formulations:
+// acc[i][j] (+)= sum_k a_i[k] * wt[k][j] for 4 rows i and a 32-wide slab of
+// output channels j, k ascending (one sequential f32 sum per element).
+// wt is K-major [K][cout]. Rows with a null pointer contribute zeros.
+// ---------------------------------------------------------------------------
+constexpr int kRowBlk = 4;
+constexpr int kColBlk = 32;
+
+static inline void micro_axpy(const float* const a[kRowBlk], const float* wt, int64_t K,
+                              int64_t cout, int64_t co0, int64_t ncol,
+                              float acc[kRowBlk][kColBlk]) {
+    for (int i = 0; i < kRowBlk; ++i)
+        for (int j = 0; j < kColBlk; ++j) acc[i][j] = 0.0f;
+    if (ncol == kColBlk) {
+        for (int64_t k = 0; k < K; ++k) {
+            const float* wk = wt + k * cout + co0;
+            for (int i = 0; i < kRowBlk; ++i) {
+                const float av = a[i] ? a[i][k] : 0.0f;
+                for (int j = 0; j < kColBlk; ++j) acc[i][j] += av * wk[j];
+            }
+        }
+    } else {
+        for (int64_t k = 0; k < K; ++k) {
+            const float* wk = wt + k * cout + co0;
+            for (int i = 0; i < kRowBlk; ++i) {
+                const float av = a[i] ? a[i][k] : 0.0f;
+                for (int j = 0; j < ncol; ++j) acc[i][j] += av * wk[j];
+            }
+        }
+    }
+}
+
+static void transpose_w(const float* w, int64_t rows, int64_t cols, std::vector<float>& wt) {
+    wt.resize((size_t)(rows * cols));
+    for (int64_t r = 0; r < rows; ++r)
+        for (int64_t c = 0; c < cols; ++c) wt[(size_t)(c * rows + r)] = w[r * cols + c];
+}
+
+// ---------------------------------------------------------------------------
+// SLat SubMConv3d, GGML order (slat_flow_graph.cpp:112-155)
+//   xc = concat(feat, zero row); g = get_rows(xc, idx[27n]) -> (27*Cin, n);
+//   out = mul_mat(W[Cout, 27*Cin], g) + bias.
+// Each output element is ONE K = 27*Cin dot product in (offset, channel)
+// order, then the bias add. nbr entries outside [0, n_in) read the zero row
+// (the reference's sentinel is exactly n_in). accum64 != 0 accumulates in
+// double (a high-precision check); otherwise one sequential f32 sum.
+// ---------------------------------------------------------------------------
+void oracle_subm_conv_slat(const float* feat, int64_t n_in, int64_t cin, const int32_t* nbr,
+                           int64_t n_out, const float* w, const float* bias, int64_t cout,
+                           float* out, int32_t accum64, int32_t threads) {
+    const int64_t K = 27 * cin;
+    if (accum64) {
+        parallel_for(n_out, threads, [&](int64_t lo, int64_t hi) {
+            for (int64_t r = lo; r < hi; ++r)
+                for (int64_t co = 0; co < cout; ++co) {
+                    double acc = 0.0;
+                    for (int o = 0; o < 27; ++o) {
+                        const int32_t s = nbr[r * 27 + o];
+                        if (s < 0 || s >= n_in) continue;
+                        const float* xr = feat + (int64_t)s * cin;
+                        const float* wr = w + co * K + o * cin;
+                        for (int64_t k = 0; k < cin; ++k) acc += (double)wr[k] * (double)xr[k];
+                    }
+                    out[r * cout + co] = (float)acc + (bias ? bias[co] : 0.0f);
+                }
+        });
+        return;
+    }
+    std::vector<float> wt;
+    transpose_w(w, cout, K, wt);  // [K][cout]
+    const int64_t nblk = (n_out + kRowBlk - 1) / kRowBlk;
+    parallel_for(nblk, threads, [&](int64_t lo, int64_t hi) {
+        std::vector<float> g((size_t)(kRowBlk * K));
+        float acc[kRowBlk][kColBlk];
+        for (int64_t b = lo; b < hi; ++b) {
+            const float* a[kRowBlk];
+            for (int i = 0; i < kRowBlk; ++i) {
+                const int64_t r = b * kRowBlk + i;
+                a[i] = nullptr;
+                if (r >= n_out) continue;
+                float* gi = g.data() + (size_t)i * K;
+                for (int o = 0; o < 27; ++o) {
+                    const int32_t s = nbr[r * 27 + o];
+                    if (s >= 0 && s < n_in)
+                        std::memcpy(gi + o * cin, feat + (int64_t)s * cin, (size_t)cin * 4);
+                    else
+                        std::memset(gi + o * cin, 0, (size_t)cin * 4);
+                }
+                a[i] = gi;
+            }
+            for (int64_t co0 = 0; co0 < cout; co0 += kColBlk) {
+                const int64_t nc = std::min<int64_t>(kColBlk, cout - co0);
+                micro_axpy(a, wt.data(), K, cout, co0, nc, acc);
+                for (int i = 0; i < kRowBlk; ++i) {
+                    const int64_t r = b * kRowBlk + i;
+                    if (r >= n_out) continue;
+                    for (int64_t j = 0; j < nc; ++j)
+                        out[r * cout + co0 + j] = acc[i][j] + (bias ? bias[co0 + j] : 0.0f);
+                }
+            }
+        }
+    });
+}
+
+// ---------------------------------------------------------------------------
+// mesh SubMConv3d, GGML order (mesh_decoder_graph.cpp:81-103)
+//   for o in 0..kvol-1: v_o = mul_mat(W_o[Cout,Cin], get_rows(x, idx_o) * mask_o)
+//   sum = ((v_0 + v_1) + v_2) + ...; out = sum + bias
+// idx/mask come from neighbors[row*27+o] (mesh_decoder_graph.cpp:68-79):
+// idx = src<0 ? 0 : src, mask = src<0 ? 0 : 1. The gathered row index is
+// (src >> gather_shift): gather_shift = 3 reads the PARENT row of a child,
+// which equals reading the child of repeat_children(x) (:32-38). kvol == 1
+// is the 1x1 skip conv: no gather, row r reads x[r >> gather_shift].
+// w_packed is [kvol][Cout][Cin] (convert_sam3d_to_gguf.py:481-492 layout).
+// ---------------------------------------------------------------------------
+void oracle_subm_conv_mesh(const float* feat, int64_t n_in, int64_t cin, const int32_t* nbr,
+                           int32_t kvol, int32_t gather_shift, int64_t n_out,
+                           const float* w_packed, const float* bias, int64_t cout, float* out,
+                           int32_t accum64, int32_t threads) {
+    auto src_row = [&](int64_t r, int o) -> const float* {
+        if (kvol == 1) return feat + (r >> gather_shift) * cin;
+        const int32_t s = nbr[r * 27 + o];
+        if (s < 0) return nullptr;  // masked to zero
+        return feat + (int64_t)(s >> gather_shift) * cin;
+    };
+    if (accum64) {
+        parallel_for(n_out, threads, [&](int64_t lo, int64_t hi) {
+            std::vector<double> sum((size_t)cout);
+            for (int64_t r = lo; r < hi; ++r) {
+                for (int o = 0; o < kvol; ++o) {
+                    const float* xr = src_row(r, o);
+                    for (int64_t co = 0; co < cout; ++co) {
+                        double acc = 0.0;
+                        if (xr) {
+                            const float* wr = w_packed + ((int64_t)o * cout + co) * cin;
+                            for (int64_t k = 0; k < cin; ++k) acc += (double)wr[k] * (double)xr[k];
+                        }
+                        sum[(size_t)co] = o == 0 ? acc : sum[(size_t)co] + acc;
+                    }
+                }
+                for (int64_t co = 0; co < cout; ++co)
+                    out[r * cout + co] = (float)sum[(size_t)co] + (bias ? bias[co] : 0.0f);
+            }
+        });
+        return;
+    }
+    std::vector<float> wt((size_t)(kvol * cin * cout));
+    for (int o = 0; o < kvol; ++o) {
+        std::vector<float> t;
+        transpose_w(w_packed + (int64_t)o * cout * cin, cout, cin, t);
+        std::memcpy(wt.data() + (size_t)o * cin * cout, t.data(), t.size() * 4);
+    }
+    const int64_t nblk = (n_out + kRowBlk - 1) / kRowBlk;
+    parallel_for(nblk, threads, [&](int64_t lo, int64_t hi) {
+        float acc[kRowBlk][kColBlk];
+        std::vector<float> sum((size_t)(kRowBlk * cout));
+        for (int64_t b = lo; b < hi; ++b) {
+            for (int o = 0; o < kvol; ++o) {
+                const float* a[kRowBlk];
+                for (int i = 0; i < kRowBlk; ++i) {
+                    const int64_t r = b * kRowBlk + i;
+                    a[i] = r < n_out ? src_row(r, o) : nullptr;
+                }
+                for (int64_t co0 = 0; co0 < cout; co0 += kColBlk) {
+                    const int64_t nc = std::min<int64_t>(kColBlk, cout - co0);
+                    micro_axpy(a, wt.data() + (size_t)o * cin * cout, cin, cout, co0, nc, acc);
+                    for (int i = 0; i < kRowBlk; ++i)
+                        for (int64_t j = 0; j < nc; ++j) {
+                            float& s = sum[(size_t)(i * cout + co0 + j)];
+                            s = o == 0 ? acc[i][j] : s + acc[i][j];
+                        }
+                }
+            }
+            for (int i = 0; i < kRowBlk; ++i) {
+                const int64_t r = b * kRowBlk + i;
+                if (r >= n_out) continue;
+                for (int64_t co = 0; co < cout; ++co)
+                    out[r * cout + co] = sum[(size_t)(i * cout + co)] + (bias ? bias[co] : 0.0f);
+            }
+        }
+    });
+    (void)n_in;
+}
+
+// ---------------------------------------------------------------------------
+// Linear (gb_linear: mul_mat + bias, graph_builder.cpp:44-54); W is [Cout][Cin].
+// row_shift reads x[r >> row_shift] (the 1x1 skip on repeated parents).
+// ---------------------------------------------------------------------------
+void oracle_linear(const float* x, int64_t n, int64_t cin, int32_t row_shift, const float* w,
+                   const float* bias, int64_t cout, float* out, int32_t threads) {
+    oracle_subm_conv_mesh(x, n, cin, nullptr, 1, row_shift, n, w, bias, cout, out, 0, threads);
+}
+
+// ---------------------------------------------------------------------------
+// GroupNorm over every token of one object (mesh_decoder_graph.cpp:16-30):
+// groups split C into equal consecutive channel ranges; mean and variance in
+// double over (tokens x channels-of-group), variance = mean((x-mean)^2),
+// y = (x-mean) * (1/sqrtf(var+eps)), then * gamma[c] + beta[c].
+// Optional silu fuses ggml_silu (mesh_decoder_graph.cpp:109, :121).
+// ---------------------------------------------------------------------------
+void oracle_group_norm(const float* x, int64_t n, int64_t c, int32_t groups, float eps,
+                       const float* gamma, const float* beta, int32_t silu, float* out) {
+    const int64_t gs = c / groups;
+    for (int32_t g = 0; g < groups; ++g) {
+        double sum = 0.0;
+        for (int64_t r = 0; r < n; ++r)
+            for (int64_t k = g * gs; k < (g + 1) * gs; ++k) sum += x[r * c + k];
+        const double cnt = (double)n * (double)gs;
+        const float mean = (float)(sum / cnt);
+        double sum2 = 0.0;
+        for (int64_t r = 0; r < n; ++r)
+            for (int64_t k = g * gs; k < (g + 1) * gs; ++k) {
+                const float v = x[r * c + k] - mean;
+                sum2 += (double)v * (double)v;
+            }
+        const float scale = 1.0f / sqrtf((float)(sum2 / cnt) + eps);
+        for (int64_t r = 0; r < n; ++r)
+            for (int64_t k = g * gs; k < (g + 1) * gs; ++k) {
+                float v = (x[r * c + k] - mean) * scale;
+                if (gamma) v *= gamma[k];
+                if (beta) v += beta[k];
+                if (silu) v = v / (1.0f + expf(-v));
+                out[r * c + k] = v;
+            }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// LayerNorm per token (ggml_norm + optional mul/add, graph_builder.cpp:56-62),
+// optional modulate h*(1+scale)+shift (slat_flow_graph.cpp:55-59) and SiLU.
+// ---------------------------------------------------------------------------
+void oracle_layer_norm(const float* x, int64_t n, int64_t c, float eps, const float* gamma,
+                       const float* beta, const float* mod_scale, const float* mod_shift,
+                       int32_t silu, float* out) {
+    for (int64_t r = 0; r < n; ++r) {
+        const float* xr = x + r * c;
+        double sum = 0.0;
+        for (int64_t k = 0; k < c; ++k) sum += xr[k];
+        const float mean = (float)(sum / (double)c);
+        double sum2 = 0.0;
+        for (int64_t k = 0; k < c; ++k) {
+            const float v = xr[k] - mean;
+            sum2 += (double)v * (double)v;
+        }
+        const float scale = 1.0f / sqrtf((float)(sum2 / (double)c) + eps);
+        for (int64_t k = 0; k < c; ++k) {
+            float v = (xr[k] - mean) * scale;
+            if (gamma) v *= gamma[k];
+            if (beta) v += beta[k];
+            if (mod_scale) v = v * mod_scale[k] + v;
+            if (mod_shift) v += mod_shift[k];
+            if (silu) v = v / (1.0f + expf(-v));
+            out[r * c + k] = v;
+        }
+    }
+}
+
+// SparseDownsample mean (slat_flow_graph.cpp:159-183): out[c] = (sum over the
+// 8 children slots of xc[child]) * inv_count[c]; slots == nf read zeros.
+void oracle_downsample_mean(const float* x, int64_t nf, int64_t ch, const int32_t* children,
+                            const float* inv_count, int64_t nc, float* out) {
+    for (int64_t c = 0; c < nc; ++c) {
+        for (int64_t k = 0; k < ch; ++k) {
+            float s = 0.0f;
+            for (int j = 0; j < 8; ++j) {
+                const int32_t f = children[c * 8 + j];
+                const float v = (f >= 0 && f < nf) ? x[(int64_t)f * ch + k] : 0.0f;
+                s = j == 0 ? v : s + v;
+            }
+            out[c * ch + k] = s * inv_count[c];
+        }
+    }
+}
+
+// SparseUpsample nearest (slat_flow_graph.cpp:186-190): out[i] = x[f2c[i]].
+void oracle_upsample_nearest(const float* x, int64_t nc, int64_t ch, const int32_t* f2c,
+                             int64_t nf, float* out) {
+    for (int64_t i = 0; i < nf; ++i) {
+        const int32_t c = f2c[i];
+        for (int64_t k = 0; k < ch; ++k)
+            out[i * ch + k] = (c >= 0 && c < nc) ? x[(int64_t)c * ch + k] : 0.0f;
+    }
+}
+
+}  // extern "C"

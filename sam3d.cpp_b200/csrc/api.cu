@@ -1,0 +1,94 @@
+// Context management and status reporting for the s3dsp C ABI.
+#include "s3dsp_internal.h"
+
+using namespace s3dsp;
+
+extern "C" S3DSP_API uint32_t s3dsp_abi_version(void) { return 1u; }
+
+extern "C" S3DSP_API s3d_status s3dsp_context_create(int32_t device, void* stream, uint32_t flags,
+                                                     s3dsp_context** out, char* error,
+                                                     uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!out) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "out is NULL");
+    *out = nullptr;
+    int count = 0;
+    S3DSP_CUDA(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
+    if (device < 0 || device >= count)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "device %d out of range [0,%d)",
+                    device, count);
+    S3DSP_CUDA(cudaSetDevice(device), "cudaSetDevice");
+    cudaDeviceProp prop;
+    S3DSP_CUDA(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+    if (prop.major != 10)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT,
+                    "device %d is sm_%d%d; this library is built for sm_100a only", device,
+                    prop.major, prop.minor);
+    auto* ctx = new (std::nothrow) s3dsp_context();
+    if (!ctx) return fail(error, error_capacity, S3D_OUT_OF_MEMORY, "context allocation");
+    ctx->device = device;
+    ctx->flags = flags;
+    ctx->sm_count = prop.multiProcessorCount;
+    if (stream) {
+        ctx->stream = (cudaStream_t)stream;
+    } else {
+        cudaError_t e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
+        if (e != cudaSuccess) {
+            delete ctx;
+            return cuda_fail(error, error_capacity, e, "cudaStreamCreate");
+        }
+        ctx->owns_stream = true;
+    }
+    cudaError_t e = cudaMalloc(&ctx->d_status, 4 * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMemsetAsync(ctx->d_status, 0, 4 * sizeof(uint32_t), ctx->stream);
+    if (e != cudaSuccess) {
+        s3dsp_context_free(ctx);
+        return cuda_fail(error, error_capacity, e, "status buffer");
+    }
+    *out = ctx;
+    return S3D_OK;
+}
+
+extern "C" S3DSP_API void s3dsp_context_free(s3dsp_context* ctx) {
+    if (!ctx) return;
+    cudaSetDevice(ctx->device);
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    if (ctx->d_status) cudaFree(ctx->d_status);
+    if (ctx->owns_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
+    delete ctx;
+}
+
+extern "C" S3DSP_API void* s3dsp_context_stream(const s3dsp_context* ctx) {
+    return ctx ? (void*)ctx->stream : nullptr;
+}
+
+namespace s3dsp {
+s3d_status check_status(s3dsp_context* ctx, char* error, uint64_t error_capacity) {
+    uint32_t st[4] = {0, 0, 0, 0};
+    S3DSP_CUDA(cudaMemcpyAsync(st, ctx->d_status, sizeof(st), cudaMemcpyDeviceToHost, ctx->stream),
+               "status readback");
+    S3DSP_CUDA(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    if (st[0] == 0) return S3D_OK;
+    S3DSP_CUDA(cudaMemsetAsync(ctx->d_status, 0, sizeof(st), ctx->stream), "status reset");
+    if (st[0] & kErrCoordRange)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT,
+                    "coordinate outside the supported domain (0 <= batch < 32768, "
+                    "-32768 <= x,y,z < 32768)");
+    if (st[0] & kErrDuplicate)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT,
+                    "duplicate coordinate (%u rows repeat an earlier row)", st[1]);
+    if (st[0] & kErrHashFull)
+        return fail(error, error_capacity, S3D_INTERNAL_ERROR, "coordinate hash probe bound exceeded");
+    if (st[0] & kErrPipelineTimeout)
+        return fail(error, error_capacity, S3D_INTERNAL_ERROR,
+                    "a device pipeline wait timed out (kernel aborted)");
+    return fail(error, error_capacity, S3D_INTERNAL_ERROR, "device status 0x%x", st[0]);
+}
+}  // namespace s3dsp
+
+extern "C" S3DSP_API s3d_status s3dsp_context_check(s3dsp_context* ctx, char* error,
+                                                    uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "ctx is NULL");
+    S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    return check_status(ctx, error, error_capacity);
+}

@@ -1,0 +1,77 @@
+// s3dsp_conv: argument validation and dispatch to the F32-strict (FP32 FMA)
+// or BF16 (tcgen05) implicit-gather kernels.
+#include "s3dsp_internal.h"
+
+using namespace s3dsp;
+
+extern "C" S3DSP_API s3d_status s3dsp_conv(s3dsp_context* ctx, const s3dsp_kmap* kmap, int32_t kvol,
+                                           uint32_t precision, const void* in, uint32_t in_dtype, int64_t n_in,
+                                           int64_t cin, int32_t in_shift, const void* weight, const float* bias,
+                                           const void* residual, uint32_t res_dtype, int32_t res_shift, void* out,
+                                           uint32_t out_dtype, int64_t n_out, int64_t cout, uint32_t flags,
+                                           const float* pro_sub, const float* pro_mul, const float* pro_add,
+                                           double* gn_partials, int32_t gn_groups, char* error,
+                                           uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx || !in || !weight || !out) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
+    if (kmap) {
+        if (kvol != kmap->kvol)
+            return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "kvol %d != kmap kvol %d", kvol, kmap->kvol);
+        if (n_out != kmap->n_out)
+            return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "n_out %lld != kmap rows %lld", (long long)n_out,
+                        (long long)kmap->n_out);
+    } else if (kvol != 1) {
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "identity conv (kmap NULL) needs kvol 1");
+    }
+    if (n_out < 0 || n_in < 0 || cin <= 0 || cout <= 0 || cin > 65536 || cout > 65536)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "bad shape");
+    if (n_out == 0) return S3D_OK;
+    if (n_out > (1ll << 31) - 128) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "n_out too large");
+    if (in_shift < 0 || in_shift > 8 || res_shift < 0 || res_shift > 8)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "shift out of range");
+    if (!kmap && ((n_out - 1) >> in_shift) >= n_in)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "identity conv reads past n_in");
+    // every gathered row index is < kmap->n_in, read as (index >> in_shift)
+    if (kmap && kmap->n_in > 0 && ((kmap->n_in - 1) >> in_shift) >= n_in)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT,
+                    "kmap gathers rows up to %lld (>> %d) but the input has %lld rows",
+                    (long long)kmap->n_in - 1, in_shift, (long long)n_in);
+    if (!dtype_ok(out_dtype) || (residual && !dtype_ok(res_dtype)))
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "bad dtype");
+    if (gn_partials && (gn_groups <= 0 || gn_groups > 64 || cout % gn_groups))
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "GroupNorm groups %d must divide cout %lld (<= 64)",
+                    gn_groups, (long long)cout);
+    if ((flags & S3DSP_PRO_AFFINE_SILU) && (!pro_sub || !pro_mul || !pro_add))
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "prologue arrays missing");
+    S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+
+    cudaError_t e;
+    if (precision == S3DSP_PREC_F32_STRICT) {
+        if (in_dtype != S3DSP_F32)
+            return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "F32_STRICT needs f32 input");
+        if (cin % 4 || ((uintptr_t)in & 15))
+            return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "F32_STRICT needs cin %% 4 == 0 and 16-byte rows");
+        e = launch_conv_f32(ctx, kmap, kvol, (const float*)in, n_in, (int)cin, in_shift, (const float*)weight, bias,
+                            residual, res_dtype, res_shift, out, out_dtype, n_out, (int)cout, flags, pro_sub, pro_mul,
+                            pro_add, gn_partials, gn_groups);
+        if (e != cudaSuccess) return cuda_fail(error, error_capacity, e, "conv_f32_kernel");
+        return S3D_OK;
+    }
+    if (precision == S3DSP_PREC_BF16) {
+        if (in_dtype != S3DSP_BF16)
+            return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "BF16 precision needs bf16 input");
+        if (flags & S3DSP_PRO_AFFINE_SILU)
+            return fail(error, error_capacity, S3D_INVALID_ARGUMENT,
+                        "BF16 conv takes pre-normalised input (use s3dsp_channel_affine)");
+        if (cin % 8 || ((uintptr_t)in & 15) || ((uintptr_t)weight & 15))
+            return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "BF16 needs cin %% 8 == 0 and 16-byte alignment");
+        s3d_status st = S3D_OK;
+        e = launch_conv_tc(ctx, kmap, kvol, (const __nv_bfloat16*)in, n_in, (int)cin, in_shift,
+                           (const __nv_bfloat16*)weight, bias, residual, res_dtype, res_shift, out, out_dtype, n_out,
+                           (int)cout, flags, gn_partials, gn_groups, error, error_capacity, &st);
+        if (st != S3D_OK) return st;
+        if (e != cudaSuccess) return cuda_fail(error, error_capacity, e, "conv_tc_kernel");
+        return S3D_OK;
+    }
+    return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "unknown precision %u", precision);
+}

@@ -1,0 +1,542 @@
+// K1 coordinate hash and K2 kernel-map construction.
+//
+// Hash: open addressing with linear probing over a power-of-two table of
+// 64-bit packed keys (load factor <= 1/2) plus a parallel int32 value array
+// holding the FIRST row of each key (atomicMin), which reproduces the
+// std::map::emplace "first insert wins" rule of SlatTables::build
+// (src/objects_runtime/sparse_ops.cpp:119-124). Coordinates are read as one
+// int4 per row (coalesced 16-byte loads) and probes read two adjacent slots
+// per 16-byte load, so a probe sequence s0, s0+1, ... costs one load per two
+// slots. Every probe loop is bounded by the table size.
+//
+// Kernel maps are stored offset-major, nbr[o * n_out + r] (-1 = none), so the
+// conv's gather loader reads 128 consecutive output rows of one offset with
+// one coalesced 512-byte load, and a per-128-row-tile bitmask records which
+// offsets have any neighbour (the conv skips empty offsets).
+#include "s3dsp_internal.h"
+
+using namespace s3dsp;
+
+namespace {
+
+constexpr unsigned long long kEmptyKey = ~0ull;
+
+__device__ __forceinline__ bool pack_key(int32_t b, int32_t x, int32_t y, int32_t z,
+                                         unsigned long long& key) {
+    if ((uint32_t)b > 32767u) return false;
+    if (x < -32768 || x > 32767 || y < -32768 || y > 32767 || z < -32768 || z > 32767) return false;
+    // b in bits 48..62 (bit 63 clear -> never equals kEmptyKey); the +32768
+    // offsets keep the packed order equal to lexicographic (b, x, y, z)
+    key = ((unsigned long long)(uint32_t)b << 48) | ((unsigned long long)(uint32_t)(x + 32768) << 32) |
+          ((unsigned long long)(uint32_t)(y + 32768) << 16) | (unsigned long long)(uint32_t)(z + 32768);
+    return true;
+}
+
+__device__ __forceinline__ unsigned long long mix64(unsigned long long k) {
+    // 64-bit finaliser (MurmurHash3 fmix64): full avalanche, so spatially
+    // clustered keys spread uniformly over the table
+    k ^= k >> 33;
+    k *= 0xff51afd7ed558ccdull;
+    k ^= k >> 33;
+    k *= 0xc4ceb9fe1a85ec53ull;
+    k ^= k >> 33;
+    return k;
+}
+
+struct HashView {
+    const unsigned long long* keys;
+    const int32_t* vals;
+    unsigned long long mask;
+
+    __device__ __forceinline__ int32_t find(unsigned long long key) const {
+        unsigned long long s = mix64(key) & mask & ~1ull;
+        for (unsigned long long p = 0; p <= mask; p += 2) {
+            const ulonglong2 kk = __ldg(reinterpret_cast<const ulonglong2*>(keys + s));
+            if (kk.x == key) return __ldg(vals + s);
+            if (kk.x == kEmptyKey) return -1;
+            if (kk.y == key) return __ldg(vals + s + 1);
+            if (kk.y == kEmptyKey) return -1;
+            s = (s + 2) & mask;
+        }
+        return -1;
+    }
+    __device__ __forceinline__ int32_t find_coord(int32_t b, int32_t x, int32_t y, int32_t z) const {
+        unsigned long long key;
+        if (!pack_key(b, x, y, z, key)) return -1;  // outside the domain -> cannot be present
+        return find(key);
+    }
+};
+
+__global__ void hash_insert_kernel(const int4* __restrict__ coords, int64_t n,
+                                   unsigned long long* keys, int32_t* vals,
+                                   unsigned long long mask, int32_t reject_dups,
+                                   uint32_t* status) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int4 c = coords[i];
+        unsigned long long key;
+        if (!pack_key(c.x, c.y, c.z, c.w, key)) {
+            atomicOr(status, kErrCoordRange);
+            continue;
+        }
+        unsigned long long s = mix64(key) & mask & ~1ull;
+        bool placed = false;
+        for (unsigned long long p = 0; p <= mask; ++p) {
+            const unsigned long long prev = atomicCAS(keys + s, kEmptyKey, key);
+            if (prev == kEmptyKey || prev == key) {
+                atomicMin(vals + s, (int32_t)i);
+                if (prev == key) {
+                    atomicAdd(status + 1, 1u);
+                    if (reject_dups) atomicOr(status, kErrDuplicate);
+                }
+                placed = true;
+                break;
+            }
+            s = (s + 1) & mask;
+        }
+        if (!placed) atomicOr(status, kErrHashFull);
+    }
+}
+
+__global__ void hash_self_kernel(const int4* __restrict__ coords, int64_t n, HashView h,
+                                 int32_t* __restrict__ self_row) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int4 c = coords[i];
+        self_row[i] = h.find_coord(c.x, c.y, c.z, c.w);
+    }
+}
+
+__global__ void hash_lookup_kernel(const int4* __restrict__ q, int64_t m, HashView h,
+                                   int32_t* __restrict__ rows) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < m;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int4 c = q[i];
+        rows[i] = h.find_coord(c.x, c.y, c.z, c.w);
+    }
+}
+
+// Submanifold 3x3x3 map, offset-major. grid.y = offset. Whole warps iterate
+// together so the tile-mask ballot always sees 32 lanes.
+__global__ void kmap_subm3_kernel(const int4* __restrict__ coords, const int32_t* __restrict__ self_row,
+                                  int64_t n, HashView h, int32_t* __restrict__ nbr,
+                                  uint32_t* __restrict__ tile_mask) {
+    const int o = blockIdx.y;
+    const int dx = o / 9 - 1, dy = (o / 3) % 3 - 1, dz = o % 3 - 1;
+    const int lane = threadIdx.x & 31;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t base = blockIdx.x * (int64_t)blockDim.x + (threadIdx.x & ~31); base < n; base += stride) {
+        const int64_t r = base + lane;
+        int32_t res = -1;
+        if (r < n) {
+            // only the first row of a duplicated key gets neighbours
+            // (sparse_ops.cpp:129-139 iterates the unique map entries)
+            if (self_row[r] == (int32_t)r) {
+                const int4 c = coords[r];
+                res = h.find_coord(c.x, c.y + dx, c.z + dy, c.w + dz);
+            }
+            nbr[o * n + r] = res;
+        }
+        const unsigned any = __ballot_sync(0xffffffffu, res >= 0);
+        if (lane == 0 && any) atomicOr(tile_mask + (base / kTileRows), 1u << o);
+    }
+}
+
+// Child geometry of MeshSubdivideTables (sparse_ops.cpp:346-365): for child
+// bits j and offset o, which of the parent's 27 neighbours holds the target
+// child, and which of its 8 children it is.
+__constant__ uint8_t c_adj_parent[8][27];
+__constant__ uint8_t c_adj_child[8][27];
+
+// One block = 32 parents = 256 children. Phase 1: 27 probes per parent into
+// shared memory. Phase 2: 27 x 256 child entries written offset-major
+// (coalesced), child coords written as int4.
+__global__ void __launch_bounds__(256) subdivide_kernel(const int4* __restrict__ parents, int64_t np,
+                                                        HashView h, int4* __restrict__ child_coords,
+                                                        int32_t* __restrict__ nbr,
+                                                        uint32_t* __restrict__ tile_mask) {
+    __shared__ int32_t padj[32][28];
+    const int64_t p0 = (int64_t)blockIdx.x * 32;
+    for (int t = threadIdx.x; t < 32 * 27; t += blockDim.x) {
+        const int pl = t / 27, o = t % 27;
+        const int64_t p = p0 + pl;
+        int32_t res = -1;
+        if (p < np) {
+            const int4 c = parents[p];
+            res = h.find_coord(c.x, c.y + o / 9 - 1, c.z + (o / 3) % 3 - 1, c.w + o % 3 - 1);
+        }
+        padj[pl][o] = res;
+    }
+    const int c = threadIdx.x;
+    const int pl = c >> 3, j = c & 7;
+    const int64_t p = p0 + pl;
+    const int64_t nc = np * 8;
+    const int64_t child = p0 * 8 + c;
+    if (p < np) {
+        const int4 pc = parents[p];
+        child_coords[child] = make_int4(pc.x, pc.y * 2 + (j >> 2), pc.z * 2 + ((j >> 1) & 1), pc.w * 2 + (j & 1));
+    }
+    __syncthreads();
+    for (int o = 0; o < 27; ++o) {
+        int32_t v = -1;
+        if (p < np) {
+            const int32_t tp = padj[pl][c_adj_parent[j][o]];
+            if (tp >= 0) v = tp * 8 + c_adj_child[j][o];
+            nbr[o * nc + child] = v;
+        }
+        const unsigned any = __ballot_sync(0xffffffffu, v >= 0);
+        if ((c & 31) == 0 && any) atomicOr(tile_mask + (child / kTileRows), 1u << o);
+    }
+}
+
+__global__ void export_dense_kernel(const int32_t* __restrict__ nbr, int64_t n, int32_t kvol,
+                                    int32_t sentinel, int32_t* __restrict__ out) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n * 27;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / 27;
+        const int o = (int)(i - r * 27);
+        int32_t v = o < kvol ? nbr[o * n + r] : -1;
+        out[i] = v < 0 ? sentinel : v;
+    }
+}
+
+// pair lists: counts per (offset, block) -> exclusive scan -> scatter
+constexpr int kPairBlock = 1024;
+
+__global__ void pair_count_kernel(const int32_t* __restrict__ nbr, int64_t n, int32_t* counts,
+                                  int64_t nblk) {
+    const int o = blockIdx.y;
+    const int64_t r = blockIdx.x * (int64_t)kPairBlock + threadIdx.x;
+    const int valid = (r < n) && nbr[o * n + r] >= 0;
+    const int c = __syncthreads_count(valid);
+    if (threadIdx.x == 0) counts[o * nblk + blockIdx.x] = c;
+}
+
+// single-block exclusive scan of m ints into int64 starts (m is small:
+// 27 * ceil(n / 1024))
+__global__ void pair_scan_kernel(const int32_t* counts, int64_t m, int64_t* starts) {
+    __shared__ int64_t carry;
+    __shared__ int64_t warp_sums[32];
+    if (threadIdx.x == 0) carry = 0;
+    __syncthreads();
+    for (int64_t base = 0; base < m; base += blockDim.x) {
+        const int64_t i = base + threadIdx.x;
+        int64_t v = i < m ? counts[i] : 0;
+        // inclusive warp scan
+        const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+        for (int d = 1; d < 32; d <<= 1) {
+            const int64_t t = __shfl_up_sync(0xffffffffu, v, d);
+            if (lane >= d) v += t;
+        }
+        if (lane == 31) warp_sums[w] = v;
+        __syncthreads();
+        if (w == 0) {
+            int64_t s = lane < (int)(blockDim.x >> 5) ? warp_sums[lane] : 0;
+            for (int d = 1; d < 32; d <<= 1) {
+                const int64_t t = __shfl_up_sync(0xffffffffu, s, d);
+                if (lane >= d) s += t;
+            }
+            warp_sums[lane] = s;
+        }
+        __syncthreads();
+        const int64_t incl = v + (w > 0 ? warp_sums[w - 1] : 0);
+        const int64_t excl = incl - (i < m ? counts[i] : 0);
+        if (i < m) starts[i] = carry + excl;
+        __syncthreads();
+        if (threadIdx.x == blockDim.x - 1) carry += incl;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) starts[m] = carry;
+}
+
+__global__ void pair_write_kernel(const int32_t* __restrict__ nbr, int64_t n, const int64_t* starts,
+                                  int64_t nblk, int32_t* __restrict__ pin, int32_t* __restrict__ pout) {
+    __shared__ int warp_cnt[kPairBlock / 32];
+    const int o = blockIdx.y;
+    const int64_t r = blockIdx.x * (int64_t)kPairBlock + threadIdx.x;
+    const int32_t v = r < n ? nbr[o * n + r] : -1;
+    const unsigned bal = __ballot_sync(0xffffffffu, v >= 0);
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    if (lane == 0) warp_cnt[w] = __popc(bal);
+    __syncthreads();
+    int before = 0;
+    for (int k = 0; k < w; ++k) before += warp_cnt[k];
+    if (v >= 0) {
+        const int64_t pos = starts[o * nblk + blockIdx.x] + before + __popc(bal & ((1u << lane) - 1));
+        pin[pos] = v;
+        pout[pos] = (int32_t)r;
+    }
+}
+
+inline int grid_for(int64_t n, int threads, int sm_count) {
+    int64_t g = (n + threads - 1) / threads;
+    const int64_t cap = (int64_t)sm_count * 16;
+    if (g > cap) g = cap;
+    return (int)(g < 1 ? 1 : g);
+}
+
+HashView view_of(const s3dsp_hash* h) { return HashView{h->keys, h->vals, h->capacity - 1}; }
+
+bool g_adj_uploaded[64] = {};
+
+cudaError_t upload_adjacency(int device) {
+    if (device >= 0 && device < 64 && g_adj_uploaded[device]) return cudaSuccess;
+    uint8_t par[8][27], chl[8][27];
+    for (int j = 0; j < 8; ++j) {
+        const int bits[3] = {j >> 2, (j >> 1) & 1, j & 1};
+        for (int o = 0; o < 27; ++o) {
+            const int d[3] = {o / 9 - 1, (o / 3) % 3 - 1, o % 3 - 1};
+            int pd[3], tb[3];
+            for (int a = 0; a < 3; ++a) {
+                const int t = bits[a] + d[a];            // in [-1, 2]
+                pd[a] = t < 0 ? -1 : (t > 1 ? 1 : 0);    // floor(t / 2)
+                tb[a] = t - 2 * pd[a];                   // t mod 2
+            }
+            par[j][o] = (uint8_t)((pd[0] + 1) * 9 + (pd[1] + 1) * 3 + (pd[2] + 1));
+            chl[j][o] = (uint8_t)(tb[0] * 4 + tb[1] * 2 + tb[2]);
+        }
+    }
+    cudaError_t e = cudaMemcpyToSymbol(c_adj_parent, par, sizeof(par));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(c_adj_child, chl, sizeof(chl));
+    if (e == cudaSuccess && device >= 0 && device < 64) g_adj_uploaded[device] = true;
+    return e;
+}
+
+s3dsp_kmap* new_kmap(s3dsp_context* ctx, int64_t n_out, int64_t n_in, int kvol, cudaError_t* err) {
+    auto* k = new (std::nothrow) s3dsp_kmap();
+    if (!k) {
+        *err = cudaErrorMemoryAllocation;
+        return nullptr;
+    }
+    k->n_out = n_out;
+    k->n_in = n_in;
+    k->kvol = kvol;
+    k->n_tiles = (n_out + kTileRows - 1) / kTileRows;
+    *err = cudaMallocAsync(&k->nbr, sizeof(int32_t) * (size_t)kvol * (size_t)(n_out > 0 ? n_out : 1), ctx->stream);
+    if (*err == cudaSuccess)
+        *err = cudaMallocAsync(&k->tile_mask, sizeof(uint32_t) * (size_t)(k->n_tiles > 0 ? k->n_tiles : 1), ctx->stream);
+    if (*err == cudaSuccess && k->n_tiles > 0)
+        *err = cudaMemsetAsync(k->tile_mask, 0, sizeof(uint32_t) * (size_t)k->n_tiles, ctx->stream);
+    if (*err != cudaSuccess) {
+        if (k->nbr) cudaFreeAsync(k->nbr, ctx->stream);
+        if (k->tile_mask) cudaFreeAsync(k->tile_mask, ctx->stream);
+        delete k;
+        return nullptr;
+    }
+    return k;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+extern "C" S3DSP_API s3d_status s3dsp_hash_build(s3dsp_context* ctx, const int32_t* d_coords,
+                                                 int64_t n, int32_t reject_duplicates,
+                                                 s3dsp_hash** out, char* error,
+                                                 uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx || !out) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "ctx/out is NULL");
+    *out = nullptr;
+    if (n <= 0) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "coordinate count %lld <= 0", (long long)n);
+    if (n > (1ll << 30)) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "coordinate count %lld > 2^30", (long long)n);
+    if (!d_coords || ((uintptr_t)d_coords & 15))
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "d_coords must be a 16-byte aligned device pointer");
+    S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    auto* h = new (std::nothrow) s3dsp_hash();
+    if (!h) return fail(error, error_capacity, S3D_OUT_OF_MEMORY, "hash allocation");
+    h->n = n;
+    h->reject_duplicates = reject_duplicates;
+    uint64_t cap = 64;
+    while (cap < 2 * (uint64_t)n) cap <<= 1;
+    h->capacity = cap;
+    cudaStream_t st = ctx->stream;
+    cudaError_t e = cudaMallocAsync(&h->keys, cap * 8, st);
+    if (e == cudaSuccess) e = cudaMallocAsync(&h->vals, cap * 4, st);
+    if (e == cudaSuccess) e = cudaMallocAsync(&h->coords, (size_t)n * 16, st);
+    if (e == cudaSuccess) e = cudaMallocAsync(&h->self_row, (size_t)n * 4, st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(h->keys, 0xff, cap * 8, st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(h->vals, 0x7f, cap * 4, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(h->coords, d_coords, (size_t)n * 16, cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) {
+        s3dsp_hash_free(ctx, h);
+        return cuda_fail(error, error_capacity, e, "hash allocation");
+    }
+    const int threads = 256;
+    hash_insert_kernel<<<grid_for(n, threads, ctx->sm_count), threads, 0, st>>>(
+        reinterpret_cast<const int4*>(h->coords), n, h->keys, h->vals, cap - 1, reject_duplicates,
+        ctx->d_status);
+    hash_self_kernel<<<grid_for(n, threads, ctx->sm_count), threads, 0, st>>>(
+        reinterpret_cast<const int4*>(h->coords), n, view_of(h), h->self_row);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        s3dsp_hash_free(ctx, h);
+        return cuda_fail(error, error_capacity, e, "hash kernels");
+    }
+    if (!(ctx->flags & S3DSP_CONTEXT_DEFERRED_CHECKS)) {
+        const s3d_status s = check_status(ctx, error, error_capacity);
+        if (s != S3D_OK) {
+            s3dsp_hash_free(ctx, h);
+            return s;
+        }
+    }
+    *out = h;
+    return S3D_OK;
+}
+
+extern "C" S3DSP_API void s3dsp_hash_free(s3dsp_context* ctx, s3dsp_hash* h) {
+    if (!h) return;
+    cudaStream_t st = ctx ? ctx->stream : nullptr;
+    if (h->keys) cudaFreeAsync(h->keys, st);
+    if (h->vals) cudaFreeAsync(h->vals, st);
+    if (h->coords) cudaFreeAsync(h->coords, st);
+    if (h->self_row) cudaFreeAsync(h->self_row, st);
+    delete h;
+}
+
+extern "C" S3DSP_API int64_t s3dsp_hash_size(const s3dsp_hash* h) { return h ? h->n : 0; }
+
+extern "C" S3DSP_API s3d_status s3dsp_hash_lookup(s3dsp_context* ctx, const s3dsp_hash* h,
+                                                  const int32_t* d_query, int64_t m, int32_t* d_rows,
+                                                  char* error, uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx || !h) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "ctx/hash is NULL");
+    if (m < 0) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "negative query count");
+    if (m == 0) return S3D_OK;
+    if (!d_query || ((uintptr_t)d_query & 15) || !d_rows)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "query/rows pointers invalid");
+    S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    hash_lookup_kernel<<<grid_for(m, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
+        reinterpret_cast<const int4*>(d_query), m, view_of(h), d_rows);
+    S3DSP_LAUNCH_CHECK("hash_lookup_kernel");
+    return S3D_OK;
+}
+
+extern "C" S3DSP_API s3d_status s3dsp_kmap_build_subm3(s3dsp_context* ctx, const s3dsp_hash* h,
+                                                       s3dsp_kmap** out, char* error,
+                                                       uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx || !h || !out) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
+    *out = nullptr;
+    S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    cudaError_t e;
+    s3dsp_kmap* k = new_kmap(ctx, h->n, h->n, 27, &e);
+    if (!k) return cuda_fail(error, error_capacity, e, "kmap allocation");
+    const int threads = 256;
+    int gx = (int)((h->n + threads - 1) / threads);
+    const int cap = ctx->sm_count * 8;
+    if (gx > cap) gx = cap;
+    kmap_subm3_kernel<<<dim3(gx, 27), threads, 0, ctx->stream>>>(
+        reinterpret_cast<const int4*>(h->coords), h->self_row, h->n, view_of(h), k->nbr, k->tile_mask);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        s3dsp_kmap_free(ctx, k);
+        return cuda_fail(error, error_capacity, e, "kmap_subm3_kernel");
+    }
+    *out = k;
+    return S3D_OK;
+}
+
+extern "C" S3DSP_API s3d_status s3dsp_subdivide(s3dsp_context* ctx, const s3dsp_hash* parents,
+                                                int32_t* d_child_coords, s3dsp_kmap** out,
+                                                char* error, uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx || !parents || !out || !d_child_coords)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
+    *out = nullptr;
+    if (((uintptr_t)d_child_coords & 15))
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "d_child_coords must be 16-byte aligned");
+    if (!parents->reject_duplicates)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT,
+                    "subdivide needs a parent hash built with reject_duplicates");
+    if (parents->n > INT32_MAX / 8)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "parent count exceeds INT32_MAX/8");
+    S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    S3DSP_CUDA(upload_adjacency(ctx->device), "adjacency tables");
+    cudaError_t e;
+    const int64_t np = parents->n;
+    s3dsp_kmap* k = new_kmap(ctx, np * 8, np * 8, 27, &e);
+    if (!k) return cuda_fail(error, error_capacity, e, "kmap allocation");
+    const int64_t blocks = (np + 31) / 32;
+    subdivide_kernel<<<(unsigned)blocks, 256, 0, ctx->stream>>>(
+        reinterpret_cast<const int4*>(parents->coords), np, view_of(parents),
+        reinterpret_cast<int4*>(d_child_coords), k->nbr, k->tile_mask);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        s3dsp_kmap_free(ctx, k);
+        return cuda_fail(error, error_capacity, e, "subdivide_kernel");
+    }
+    *out = k;
+    return S3D_OK;
+}
+
+extern "C" S3DSP_API void s3dsp_kmap_free(s3dsp_context* ctx, s3dsp_kmap* k) {
+    if (!k) return;
+    cudaStream_t st = ctx ? ctx->stream : nullptr;
+    if (k->nbr) cudaFreeAsync(k->nbr, st);
+    if (k->tile_mask) cudaFreeAsync(k->tile_mask, st);
+    delete k;
+}
+
+extern "C" S3DSP_API int64_t s3dsp_kmap_rows(const s3dsp_kmap* k) { return k ? k->n_out : 0; }
+
+extern "C" S3DSP_API s3d_status s3dsp_kmap_export_dense(s3dsp_context* ctx, const s3dsp_kmap* k,
+                                                        uint32_t sentinel_mode, int32_t* d_out,
+                                                        char* error, uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx || !k || !d_out) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
+    if (sentinel_mode != S3DSP_SENTINEL_SLAT_N && sentinel_mode != S3DSP_SENTINEL_MESH_NEG1)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "unknown sentinel mode %u", sentinel_mode);
+    S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    const int32_t sentinel = sentinel_mode == S3DSP_SENTINEL_SLAT_N ? (int32_t)k->n_in : -1;
+    export_dense_kernel<<<grid_for(k->n_out * 27, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
+        k->nbr, k->n_out, k->kvol, sentinel, d_out);
+    S3DSP_LAUNCH_CHECK("export_dense_kernel");
+    return S3D_OK;
+}
+
+extern "C" S3DSP_API s3d_status s3dsp_kmap_pairs(s3dsp_context* ctx, const s3dsp_kmap* k,
+                                                 int32_t* d_in, int32_t* d_out, int64_t capacity,
+                                                 int64_t* h_offsets, char* error,
+                                                 uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx || !k || !d_in || !d_out || !h_offsets)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
+    S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    const int64_t nblk = (k->n_out + kPairBlock - 1) / kPairBlock;
+    const int64_t m = nblk * k->kvol;
+    int32_t* counts = nullptr;
+    int64_t* starts = nullptr;
+    S3DSP_CUDA(cudaMallocAsync(&counts, sizeof(int32_t) * (size_t)(m > 0 ? m : 1), ctx->stream), "pairs scratch");
+    cudaError_t e = cudaMallocAsync(&starts, sizeof(int64_t) * (size_t)(m + 1), ctx->stream);
+    if (e != cudaSuccess) {
+        cudaFreeAsync(counts, ctx->stream);
+        return cuda_fail(error, error_capacity, e, "pairs scratch");
+    }
+    if (nblk > 0)
+        pair_count_kernel<<<dim3((unsigned)nblk, k->kvol), kPairBlock, 0, ctx->stream>>>(k->nbr, k->n_out, counts, nblk);
+    pair_scan_kernel<<<1, 1024, 0, ctx->stream>>>(counts, m, starts);
+    // per-offset starts = starts[o * nblk]
+    int64_t* host_starts = new int64_t[(size_t)m + 1];
+    e = cudaMemcpyAsync(host_starts, starts, sizeof(int64_t) * (size_t)(m + 1), cudaMemcpyDeviceToHost, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    s3d_status st = S3D_OK;
+    if (e != cudaSuccess) {
+        st = cuda_fail(error, error_capacity, e, "pair counts");
+    } else if (host_starts[m] > capacity) {
+        st = fail(error, error_capacity, S3D_INVALID_ARGUMENT, "pair capacity %lld < %lld needed",
+                  (long long)capacity, (long long)host_starts[m]);
+    } else {
+        for (int o = 0; o < k->kvol; ++o) h_offsets[o] = host_starts[o * nblk];
+        h_offsets[k->kvol] = host_starts[m];
+        if (nblk > 0)
+            pair_write_kernel<<<dim3((unsigned)nblk, k->kvol), kPairBlock, 0, ctx->stream>>>(
+                k->nbr, k->n_out, starts, nblk, d_in, d_out);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) st = cuda_fail(error, error_capacity, e, "pair_write_kernel");
+    }
+    delete[] host_starts;
+    cudaFreeAsync(counts, ctx->stream);
+    cudaFreeAsync(starts, ctx->stream);
+    return st;
+}

@@ -1,0 +1,382 @@
+// K4 normalisation kernels (GroupNorm statistics / finalize / apply, LayerNorm
+// with modulate and SiLU), dtype conversion and weight packing.
+//
+// GroupNorm follows sparse_group_norm (src/objects_runtime/mesh_decoder_graph.cpp
+// :16-30): one object, `groups` equal channel ranges, statistics over every
+// token, eps 1e-5, then gamma/beta. Statistics are accumulated as per-128-row
+// tile partial sums in double ([tiles][groups][2]); the finalize kernel reduces
+// them in a fixed order (deterministic) and emits per-channel (sub, mul, add)
+// with (x - sub) * mul + add == ((x - mean) * rstd) * gamma + beta.
+// LayerNorm follows ggml_norm + mul/add (graph_builder.cpp:56-62) and modulate
+// (slat_flow_graph.cpp:55-59): y = silu(((x-mean)*rstd*g + b) * (1+s) + sh).
+#include "s3dsp_internal.h"
+
+using namespace s3dsp;
+
+namespace {
+
+__device__ __forceinline__ float ld_f(const void* p, uint32_t dt, int64_t i) {
+    if (dt == S3DSP_F32) return reinterpret_cast<const float*>(p)[i];
+    if (dt == S3DSP_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+    return __half2float(reinterpret_cast<const __half*>(p)[i]);
+}
+__device__ __forceinline__ void st_f(void* p, uint32_t dt, int64_t i, float v) {
+    if (dt == S3DSP_F32)
+        reinterpret_cast<float*>(p)[i] = v;
+    else if (dt == S3DSP_BF16)
+        reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16(v);
+    else
+        reinterpret_cast<__half*>(p)[i] = __float2half(v);
+}
+__device__ __forceinline__ float silu_f(float v) { return v / (1.0f + __expf(-v)); }
+
+// stats of x [n, c]: one block per 128-row tile; block-local double sums per
+// group written (not accumulated) to partials[tile][g][2]
+__global__ void gn_stats_kernel(const void* __restrict__ x, uint32_t dt, int64_t n, int c, int groups,
+                                double* __restrict__ partials) {
+    __shared__ double acc[64][2];
+    for (int i = threadIdx.x; i < 128; i += blockDim.x) (&acc[0][0])[i] = 0.0;
+    __syncthreads();
+    const int gs = c / groups;
+    const int64_t r0 = (int64_t)blockIdx.x * 128;
+    const int64_t rows = min((int64_t)128, n - r0);
+    // thread -> channel column stripe; accumulate per channel then per group
+    for (int ch = threadIdx.x; ch < c; ch += blockDim.x) {
+        double s1 = 0.0, s2 = 0.0;
+        for (int64_t r = 0; r < rows; ++r) {
+            const double v = ld_f(x, dt, (r0 + r) * c + ch);
+            s1 += v;
+            s2 += v * v;
+        }
+        atomicAdd(&acc[ch / gs][0], s1);
+        atomicAdd(&acc[ch / gs][1], s2);
+    }
+    __syncthreads();
+    for (int g = threadIdx.x; g < groups; g += blockDim.x) {
+        partials[((int64_t)blockIdx.x * groups + g) * 2 + 0] = acc[g][0];
+        partials[((int64_t)blockIdx.x * groups + g) * 2 + 1] = acc[g][1];
+    }
+}
+
+// one block per group: fixed-order tree reduction over tiles
+__global__ void gn_finalize_kernel(const double* __restrict__ partials, int64_t tiles, int64_t n_rows, int c,
+                                   int groups, float eps, const float* __restrict__ gamma,
+                                   const float* __restrict__ beta, float* __restrict__ sub, float* __restrict__ mul,
+                                   float* __restrict__ add) {
+    __shared__ double s1s[256], s2s[256];
+    const int g = blockIdx.x;
+    double s1 = 0.0, s2 = 0.0;
+    for (int64_t t = threadIdx.x; t < tiles; t += blockDim.x) {
+        s1 += partials[(t * groups + g) * 2 + 0];
+        s2 += partials[(t * groups + g) * 2 + 1];
+    }
+    s1s[threadIdx.x] = s1;
+    s2s[threadIdx.x] = s2;
+    __syncthreads();
+    for (int d = blockDim.x / 2; d > 0; d >>= 1) {
+        if ((int)threadIdx.x < d) {
+            s1s[threadIdx.x] += s1s[threadIdx.x + d];
+            s2s[threadIdx.x] += s2s[threadIdx.x + d];
+        }
+        __syncthreads();
+    }
+    const int gs = c / groups;
+    if ((int)threadIdx.x < gs) {
+        const double cnt = (double)n_rows * (double)gs;
+        const double mean = s1s[0] / cnt;
+        double var = s2s[0] / cnt - mean * mean;
+        if (var < 0.0) var = 0.0;
+        const float rstd = 1.0f / sqrtf((float)var + eps);
+        const int ch = g * gs + threadIdx.x;
+        const float gm = gamma ? gamma[ch] : 1.0f;
+        sub[ch] = (float)mean;
+        mul[ch] = rstd * gm;
+        add[ch] = beta ? beta[ch] : 0.0f;
+    }
+}
+
+__global__ void channel_affine_kernel(const void* __restrict__ x, uint32_t xd, int64_t n, int c,
+                                      const float* __restrict__ sub, const float* __restrict__ mul,
+                                      const float* __restrict__ add, int silu, void* __restrict__ y, uint32_t yd) {
+    const int64_t total = n * c;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int ch = (int)(i % c);
+        float v = (ld_f(x, xd, i) - sub[ch]) * mul[ch] + add[ch];
+        if (silu) v = silu_f(v);
+        st_f(y, yd, i, v);
+    }
+}
+
+// vectorised variant: f32 in, bf16 out, c % 8 == 0
+__global__ void channel_affine_f32_bf16_kernel(const float4* __restrict__ x, int64_t n, int c,
+                                               const float* __restrict__ sub, const float* __restrict__ mul,
+                                               const float* __restrict__ add, int silu, uint4* __restrict__ y) {
+    const int64_t total8 = n * c / 8;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total8; i += (int64_t)gridDim.x * blockDim.x) {
+        const float4 a = x[2 * i], b = x[2 * i + 1];
+        const int ch = (int)((i * 8) % c);
+        float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        uint32_t w[4];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            v[q] = (v[q] - sub[ch + q]) * mul[ch + q] + add[ch + q];
+            if (silu) v[q] = silu_f(v[q]);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * q], v[2 * q + 1]);
+            w[q] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        y[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+// one warp per row; two passes over the row (mean, then centred variance),
+// both in double like ggml_norm's ggml_float sums
+__global__ void layer_norm_kernel(const void* __restrict__ x, uint32_t xd, int64_t n, int c, float eps,
+                                  const float* __restrict__ gamma, const float* __restrict__ beta,
+                                  const float* __restrict__ ms, const float* __restrict__ msh, int silu,
+                                  void* __restrict__ y, uint32_t yd) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= n) return;
+    const int64_t base = row * c;
+    double s = 0.0;
+    for (int k = lane; k < c; k += 32) s += ld_f(x, xd, base + k);
+    for (int d = 16; d > 0; d >>= 1) s += __shfl_xor_sync(0xffffffffu, s, d);
+    const float mean = (float)(s / c);
+    double s2 = 0.0;
+    for (int k = lane; k < c; k += 32) {
+        const float v = ld_f(x, xd, base + k) - mean;
+        s2 += (double)v * v;
+    }
+    for (int d = 16; d > 0; d >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, d);
+    const float rstd = 1.0f / sqrtf((float)(s2 / c) + eps);
+    for (int k = lane; k < c; k += 32) {
+        float v = (ld_f(x, xd, base + k) - mean) * rstd;
+        if (gamma) v *= gamma[k];
+        if (beta) v += beta[k];
+        if (ms) v = v * ms[k] + v;
+        if (msh) v += msh[k];
+        if (silu) v = silu_f(v);
+        st_f(y, yd, base + k, v);
+    }
+}
+
+__global__ void convert_kernel(const void* __restrict__ x, uint32_t xd, void* __restrict__ y, uint32_t yd,
+                               int64_t count) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x)
+        st_f(y, yd, i, ld_f(x, xd, i));
+}
+
+__global__ void convert_f32_bf16_kernel(const float4* __restrict__ x, uint2* __restrict__ y, int64_t count4) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count4; i += (int64_t)gridDim.x * blockDim.x) {
+        const float4 v = x[i];
+        const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+        y[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+    }
+}
+
+// Weight packing. Source element (o, co, ci) of each layout, as stored in GGUF:
+//   SLAT_ROW      (Cout, 27, Cin)      src[(co*kvol + o)*cin + ci]
+//   MESH_PACKED   (kvol, Cout, Cin)    src[(o*cout + co)*cin + ci]
+//   LINEAR        (Cout, Cin), kvol 1  src[co*cin + ci]
+//   SPCONV_1X1    buffer read as (Cin, Cout) then transposed: src[ci*cout + co]
+//   TRANSPOSED_2X2X2 (8, Cout, Cin) == MESH_PACKED with kvol 8
+// Destinations: F32_STRICT -> [kvol][cin_pad16][cout_pad64] f32 (zero padded)
+//               BF16       -> [kvol][cout_pad16][cin_pad64] bf16 (K-major)
+__global__ void pack_kernel(const void* __restrict__ src, uint32_t sd, uint32_t layout, int kvol, int cin,
+                            int cout, uint32_t prec, int cin_pad, int cout_pad, void* __restrict__ dst) {
+    const int64_t total = (int64_t)kvol * cin_pad * cout_pad;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        int o, ci, co;
+        if (prec == S3DSP_PREC_F32_STRICT) {
+            co = (int)(i % cout_pad);
+            ci = (int)((i / cout_pad) % cin_pad);
+            o = (int)(i / ((int64_t)cout_pad * cin_pad));
+        } else {
+            ci = (int)(i % cin_pad);
+            co = (int)((i / cin_pad) % cout_pad);
+            o = (int)(i / ((int64_t)cout_pad * cin_pad));
+        }
+        float v = 0.0f;
+        if (ci < cin && co < cout) {
+            int64_t s;
+            switch (layout) {
+                case S3DSP_LAYOUT_SLAT_ROW: s = ((int64_t)co * kvol + o) * cin + ci; break;
+                case S3DSP_LAYOUT_SPCONV_1X1: s = (int64_t)ci * cout + co; break;
+                case S3DSP_LAYOUT_LINEAR: s = (int64_t)co * cin + ci; break;
+                default: s = ((int64_t)o * cout + co) * cin + ci; break;  // MESH_PACKED / TRANSPOSED
+            }
+            v = ld_f(src, sd, s);
+        }
+        if (prec == S3DSP_PREC_F32_STRICT)
+            reinterpret_cast<float*>(dst)[i] = v;
+        else
+            reinterpret_cast<__nv_bfloat16*>(dst)[i] = __float2bfloat16(v);
+    }
+}
+
+inline int grid_for(int64_t n, int threads, int sm_count) {
+    int64_t g = (n + threads - 1) / threads;
+    const int64_t cap = (int64_t)sm_count * 16;
+    if (g > cap) g = cap;
+    return (int)(g < 1 ? 1 : g);
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+extern "C" S3DSP_API int64_t s3dsp_gn_partials_count(int64_t n_rows, int64_t channels, int32_t groups) {
+    (void)channels;
+    return ((n_rows + 127) / 128) * (int64_t)groups * 2;
+}
+
+extern "C" S3DSP_API s3d_status s3dsp_gn_stats(s3dsp_context* ctx, const void* x, uint32_t dtype, int64_t n,
+                                               int64_t c, int32_t groups, double* partials, char* error,
+                                               uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx || !x || !partials) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
+    if (!dtype_ok(dtype) || n <= 0 || c <= 0 || groups <= 0 || groups > 64 || c % groups)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "bad GroupNorm shape n=%lld c=%lld groups=%d",
+                    (long long)n, (long long)c, groups);
+    S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    const int64_t tiles = (n + 127) / 128;
+    gn_stats_kernel<<<(unsigned)tiles, 256, 0, ctx->stream>>>(x, dtype, n, (int)c, groups, partials);
+    S3DSP_LAUNCH_CHECK("gn_stats_kernel");
+    return S3D_OK;
+}
+
+extern "C" S3DSP_API s3d_status s3dsp_gn_finalize(s3dsp_context* ctx, const double* partials, int64_t n_rows,
+                                                  int64_t c, int32_t groups, float eps, const float* gamma,
+                                                  const float* beta, float* sub, float* mul, float* add,
+                                                  char* error, uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx || !partials || !sub || !mul || !add)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
+    if (n_rows <= 0 || c <= 0 || groups <= 0 || groups > 64 || c % groups || c / groups > 256)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "bad GroupNorm shape");
+    S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    gn_finalize_kernel<<<groups, 256, 0, ctx->stream>>>(partials, (n_rows + 127) / 128, n_rows, (int)c, groups, eps,
+                                                        gamma, beta, sub, mul, add);
+    S3DSP_LAUNCH_CHECK("gn_finalize_kernel");
+    return S3D_OK;
+}
+
+extern "C" S3DSP_API s3d_status s3dsp_channel_affine(s3dsp_context* ctx, const void* x, uint32_t xd, int64_t n,
+                                                     int64_t c, const float* sub, const float* mul,
+                                                     const float* add, int32_t silu, void* y, uint32_t yd,
+                                                     char* error, uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx || !x || !y || !sub || !mul || !add)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
+    if (!dtype_ok(xd) || !dtype_ok(yd) || n < 0 || c <= 0)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "bad shape/dtype");
+    if (n == 0) return S3D_OK;
+    S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    if (xd == S3DSP_F32 && yd == S3DSP_BF16 && c % 8 == 0 && !((uintptr_t)x & 15) && !((uintptr_t)y & 15)) {
+        channel_affine_f32_bf16_kernel<<<grid_for(n * c / 8, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
+            reinterpret_cast<const float4*>(x), n, (int)c, sub, mul, add, silu, reinterpret_cast<uint4*>(y));
+    } else {
+        channel_affine_kernel<<<grid_for(n * c, 256, ctx->sm_count), 256, 0, ctx->stream>>>(x, xd, n, (int)c, sub, mul,
+                                                                                          add, silu, y, yd);
+    }
+    S3DSP_LAUNCH_CHECK("channel_affine_kernel");
+    return S3D_OK;
+}
+
+extern "C" S3DSP_API s3d_status s3dsp_layer_norm(s3dsp_context* ctx, const void* x, uint32_t xd, int64_t n, int64_t c,
+                                                 float eps, const float* gamma, const float* beta,
+                                                 const float* ms, const float* msh, int32_t silu, void* y,
+                                                 uint32_t yd, char* error, uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx || !x || !y) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
+    if (!dtype_ok(xd) || !dtype_ok(yd) || n < 0 || c <= 0)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "bad shape/dtype");
+    if (n == 0) return S3D_OK;
+    S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    const int64_t blocks = (n + 7) / 8;
+    layer_norm_kernel<<<(unsigned)blocks, 256, 0, ctx->stream>>>(x, xd, n, (int)c, eps, gamma, beta, ms, msh, silu, y,
+                                                                 yd);
+    S3DSP_LAUNCH_CHECK("layer_norm_kernel");
+    return S3D_OK;
+}
+
+extern "C" S3DSP_API s3d_status s3dsp_convert(s3dsp_context* ctx, const void* x, uint32_t xd, void* y, uint32_t yd,
+                                              int64_t count, char* error, uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx || !x || !y) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
+    if (!dtype_ok(xd) || !dtype_ok(yd) || count < 0)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "bad dtype/count");
+    if (count == 0) return S3D_OK;
+    S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    if (xd == S3DSP_F32 && yd == S3DSP_BF16 && count % 4 == 0 && !((uintptr_t)x & 15) && !((uintptr_t)y & 7))
+        convert_f32_bf16_kernel<<<grid_for(count / 4, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
+            reinterpret_cast<const float4*>(x), reinterpret_cast<uint2*>(y), count / 4);
+    else
+        convert_kernel<<<grid_for(count, 256, ctx->sm_count), 256, 0, ctx->stream>>>(x, xd, y, yd, count);
+    S3DSP_LAUNCH_CHECK("convert_kernel");
+    return S3D_OK;
+}
+
+namespace {
+void packed_dims(uint32_t prec, int64_t cin, int64_t cout, int64_t& cin_pad, int64_t& cout_pad) {
+    if (prec == S3DSP_PREC_F32_STRICT) {
+        cin_pad = (cin + 15) / 16 * 16;
+        cout_pad = (cout + 63) / 64 * 64;
+    } else {
+        cin_pad = (cin + 63) / 64 * 64;
+        cout_pad = (cout + 15) / 16 * 16;
+    }
+}
+}  // namespace
+
+extern "C" S3DSP_API int64_t s3dsp_weights_packed_bytes(uint32_t prec, int32_t kvol, int64_t cin, int64_t cout) {
+    int64_t cp, op;
+    packed_dims(prec, cin, cout, cp, op);
+    return (int64_t)kvol * cp * op * (prec == S3DSP_PREC_F32_STRICT ? 4 : 2);
+}
+
+extern "C" S3DSP_API s3d_status s3dsp_weights_pack(s3dsp_context* ctx, const void* src, uint32_t sd, int32_t on_host,
+                                                   uint32_t layout, int32_t kvol, int64_t cin, int64_t cout,
+                                                   uint32_t prec, void* dst, char* error, uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx || !src || !dst) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
+    if (!dtype_ok(sd)) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "bad source dtype");
+    if (prec != S3DSP_PREC_F32_STRICT && prec != S3DSP_PREC_BF16)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "unknown precision %u", prec);
+    if (layout > S3DSP_LAYOUT_TRANSPOSED_2X2X2) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "unknown layout");
+    if (cin <= 0 || cout <= 0 || (kvol != 1 && kvol != 8 && kvol != 27))
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "bad weight shape");
+    if ((layout == S3DSP_LAYOUT_LINEAR || layout == S3DSP_LAYOUT_SPCONV_1X1) && kvol != 1)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "linear layouts need kvol 1");
+    if (layout == S3DSP_LAYOUT_SLAT_ROW && kvol != 27)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "SLAT_ROW layout needs kvol 27");
+    if (layout == S3DSP_LAYOUT_TRANSPOSED_2X2X2 && kvol != 8)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "TRANSPOSED_2X2X2 layout needs kvol 8");
+    S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    int64_t cp, op;
+    packed_dims(prec, cin, cout, cp, op);
+    const void* dsrc = src;
+    void* staged = nullptr;
+    if (on_host) {
+        const size_t bytes = (size_t)kvol * cin * cout * dtype_size(sd);
+        S3DSP_CUDA(cudaMallocAsync(&staged, bytes, ctx->stream), "weight staging");
+        cudaError_t e = cudaMemcpyAsync(staged, src, bytes, cudaMemcpyHostToDevice, ctx->stream);
+        if (e != cudaSuccess) {
+            cudaFreeAsync(staged, ctx->stream);
+            return cuda_fail(error, error_capacity, e, "weight upload");
+        }
+        dsrc = staged;
+    }
+    const int64_t total = (int64_t)kvol * cp * op;
+    pack_kernel<<<grid_for(total, 256, ctx->sm_count), 256, 0, ctx->stream>>>(dsrc, sd, layout, kvol, (int)cin,
+                                                                             (int)cout, prec, (int)cp, (int)op, dst);
+    cudaError_t e = cudaGetLastError();
+    if (staged) cudaFreeAsync(staged, ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(error, error_capacity, e, "pack_kernel");
+    if (on_host) S3DSP_CUDA(cudaStreamSynchronize(ctx->stream), "weight upload sync");
+    return S3D_OK;
+}

@@ -1,0 +1,110 @@
+// Internal declarations shared by the s3dsp translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <new>
+
+#include "s3dsp.h"
+
+// ---------------------------------------------------------------------------
+// device status words (written by kernels that validate their inputs)
+// ---------------------------------------------------------------------------
+enum : uint32_t {
+    kErrCoordRange = 1u << 0,   // coordinate outside the packed key domain
+    kErrHashFull = 1u << 1,     // probe bound exceeded (never with load <= 1/2)
+    kErrDuplicate = 1u << 2,    // duplicate coordinate where duplicates are rejected
+    kErrPipelineTimeout = 1u << 3,  // a bounded device wait gave up
+};
+
+struct s3dsp_context {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    bool owns_stream = false;
+    uint32_t flags = 0;
+    int sm_count = 0;
+    uint32_t* d_status = nullptr;  // [4] error bits, duplicate count, ...
+};
+
+struct s3dsp_hash {
+    int64_t n = 0;
+    uint64_t capacity = 0;               // power of two >= 2n
+    unsigned long long* keys = nullptr;  // [capacity]
+    int32_t* vals = nullptr;             // [capacity] first row per key
+    int32_t* coords = nullptr;           // [n, 4] own copy
+    int32_t* self_row = nullptr;         // [n] first row holding the same key
+    int32_t reject_duplicates = 0;
+};
+
+struct s3dsp_kmap {
+    int64_t n_out = 0;
+    int64_t n_in = 0;
+    int32_t kvol = 27;
+    int32_t* nbr = nullptr;         // [kvol][n_out], -1 = none
+    uint32_t* tile_mask = nullptr;  // [ceil(n_out / 128)] bit o = any neighbour at offset o
+    int64_t n_tiles = 0;
+};
+
+namespace s3dsp {
+
+constexpr int kTileRows = 128;  // rows per conv tile (tcgen05 M) == tile_mask granularity
+
+// error-buffer helpers (reference convention: include/sam3d.h:32-34)
+inline void clear_error(char* error, uint64_t cap) {
+    if (error && cap) error[0] = '\0';
+}
+inline s3d_status fail(char* error, uint64_t cap, s3d_status st, const char* fmt, ...) {
+    if (error && cap) {
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(error, (size_t)cap, fmt, ap);
+        va_end(ap);
+        error[cap - 1] = '\0';
+    }
+    return st;
+}
+inline s3d_status cuda_fail(char* error, uint64_t cap, cudaError_t e, const char* what) {
+    return fail(error, cap, e == cudaErrorMemoryAllocation ? S3D_OUT_OF_MEMORY : S3D_INTERNAL_ERROR,
+                "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define S3DSP_CUDA(call, what)                                              \
+    do {                                                                    \
+        cudaError_t e_ = (call);                                            \
+        if (e_ != cudaSuccess) return ::s3dsp::cuda_fail(error, error_capacity, e_, what); \
+    } while (0)
+
+#define S3DSP_LAUNCH_CHECK(what)                                            \
+    do {                                                                    \
+        cudaError_t e_ = cudaGetLastError();                                \
+        if (e_ != cudaSuccess) return ::s3dsp::cuda_fail(error, error_capacity, e_, what); \
+    } while (0)
+
+inline size_t dtype_size(uint32_t dt) { return dt == S3DSP_F32 ? 4 : 2; }
+inline bool dtype_ok(uint32_t dt) { return dt == S3DSP_F32 || dt == S3DSP_BF16 || dt == S3DSP_F16; }
+
+// Reads back the device status words and turns them into a status.
+s3d_status check_status(s3dsp_context* ctx, char* error, uint64_t error_capacity);
+
+// launch helpers implemented in the .cu files
+cudaError_t launch_conv_f32(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol, const float* in,
+                            int64_t n_in, int cin, int in_shift, const float* w,
+                            const float* bias, const void* residual, uint32_t res_dtype,
+                            int res_shift, void* out, uint32_t out_dtype, int64_t n_out, int cout,
+                            uint32_t flags, const float* pro_sub, const float* pro_mul,
+                            const float* pro_add, double* gn_partials, int gn_groups);
+cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
+                           const __nv_bfloat16* in, int64_t n_in, int cin, int in_shift,
+                           const __nv_bfloat16* w, const float* bias, const void* residual,
+                           uint32_t res_dtype, int res_shift, void* out, uint32_t out_dtype,
+                           int64_t n_out, int cout, uint32_t flags, double* gn_partials,
+                           int gn_groups, char* error, uint64_t error_capacity, s3d_status* st);
+
+}  // namespace s3dsp

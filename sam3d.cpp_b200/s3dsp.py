@@ -1,0 +1,253 @@
+"""Python front-end of libs3dsp.so (the C-ABI CUDA library), via ctypes.
+
+This is the host-side mirror of the reference's internal C++ surface for the
+sparse-convolution path (src/objects_runtime/sparse_ops.hpp table builders,
+mesh_decoder_graph.cpp / slat_flow_graph.cpp graph pieces, session.cpp
+decode_object_mesh). Device memory is owned by the caller (torch tensors are
+the convenient allocator here); the library never falls back to the CPU: if
+libs3dsp.so is missing or no sm_100 GPU is present, every entry point raises.
+
+Error handling mirrors the reference C API (include/sam3d.h:20-40): each call
+returns an s3d_status and fills an error buffer; non-zero statuses raise
+S3dError carrying both.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libs3dsp.so")
+
+S3D_OK, S3D_INVALID_ARGUMENT, S3D_OUT_OF_MEMORY, S3D_INTERNAL_ERROR = 0, 1, 2, 3
+F32, BF16, F16 = 0, 1, 2
+PREC_F32_STRICT, PREC_BF16 = 0, 1
+LAYOUT_SLAT_ROW, LAYOUT_MESH_PACKED, LAYOUT_LINEAR, LAYOUT_SPCONV_1X1, LAYOUT_TRANSPOSED_2X2X2 = 0, 1, 2, 3, 4
+SENTINEL_SLAT_N, SENTINEL_MESH_NEG1 = 0, 1
+EPI_SILU, PRO_AFFINE_SILU = 1, 2
+CONTEXT_DEFERRED_CHECKS = 1
+
+# every symbol include/s3dsp.h declares (tests check the library exports them)
+EXPORTED = [
+    "s3dsp_abi_version", "s3dsp_context_create", "s3dsp_context_free", "s3dsp_context_stream",
+    "s3dsp_context_check", "s3dsp_hash_build", "s3dsp_hash_free", "s3dsp_hash_size",
+    "s3dsp_hash_lookup", "s3dsp_kmap_build_subm3", "s3dsp_subdivide", "s3dsp_kmap_free",
+    "s3dsp_kmap_rows", "s3dsp_kmap_export_dense", "s3dsp_kmap_pairs",
+    "s3dsp_weights_packed_bytes", "s3dsp_weights_pack", "s3dsp_gn_partials_count", "s3dsp_conv",
+    "s3dsp_gn_stats", "s3dsp_gn_finalize", "s3dsp_channel_affine", "s3dsp_layer_norm",
+    "s3dsp_convert",
+]
+
+
+class S3dError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"s3d_status {status}: {message}")
+        self.status = status
+        self.message = message
+
+
+_lib = None
+_vp = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_i32 = ctypes.c_int32
+_u32 = ctypes.c_uint32
+_u64 = ctypes.c_uint64
+_cp = ctypes.c_char_p
+_f = ctypes.c_float
+
+
+def load(path: str = LIB_PATH):
+    """Load libs3dsp.so (raises if it was not built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise FileNotFoundError(f"{path} not built (run __graft_entry__.build())")
+    L = ctypes.CDLL(path)
+    sig = {
+        "s3dsp_abi_version": (_u32, []),
+        "s3dsp_context_create": (_u32, [_i32, _vp, _u32, ctypes.POINTER(_vp), _cp, _u64]),
+        "s3dsp_context_free": (None, [_vp]),
+        "s3dsp_context_stream": (_vp, [_vp]),
+        "s3dsp_context_check": (_u32, [_vp, _cp, _u64]),
+        "s3dsp_hash_build": (_u32, [_vp, _vp, _i64, _i32, ctypes.POINTER(_vp), _cp, _u64]),
+        "s3dsp_hash_free": (None, [_vp, _vp]),
+        "s3dsp_hash_size": (_i64, [_vp]),
+        "s3dsp_hash_lookup": (_u32, [_vp, _vp, _vp, _i64, _vp, _cp, _u64]),
+        "s3dsp_kmap_build_subm3": (_u32, [_vp, _vp, ctypes.POINTER(_vp), _cp, _u64]),
+        "s3dsp_subdivide": (_u32, [_vp, _vp, _vp, ctypes.POINTER(_vp), _cp, _u64]),
+        "s3dsp_kmap_free": (None, [_vp, _vp]),
+        "s3dsp_kmap_rows": (_i64, [_vp]),
+        "s3dsp_kmap_export_dense": (_u32, [_vp, _vp, _u32, _vp, _cp, _u64]),
+        "s3dsp_kmap_pairs": (_u32, [_vp, _vp, _vp, _vp, _i64, ctypes.POINTER(_i64), _cp, _u64]),
+        "s3dsp_weights_packed_bytes": (_i64, [_u32, _i32, _i64, _i64]),
+        "s3dsp_weights_pack": (_u32, [_vp, _vp, _u32, _i32, _u32, _i32, _i64, _i64, _u32, _vp, _cp, _u64]),
+        "s3dsp_gn_partials_count": (_i64, [_i64, _i64, _i32]),
+        "s3dsp_conv": (_u32, [_vp, _vp, _i32, _u32, _vp, _u32, _i64, _i64, _i32, _vp, _vp, _vp, _u32, _i32,
+                              _vp, _u32, _i64, _i64, _u32, _vp, _vp, _vp, _vp, _i32, _cp, _u64]),
+        "s3dsp_gn_stats": (_u32, [_vp, _vp, _u32, _i64, _i64, _i32, _vp, _cp, _u64]),
+        "s3dsp_gn_finalize": (_u32, [_vp, _vp, _i64, _i64, _i32, _f, _vp, _vp, _vp, _vp, _vp, _cp, _u64]),
+        "s3dsp_channel_affine": (_u32, [_vp, _vp, _u32, _i64, _i64, _vp, _vp, _vp, _i32, _vp, _u32, _cp, _u64]),
+        "s3dsp_layer_norm": (_u32, [_vp, _vp, _u32, _i64, _i64, _f, _vp, _vp, _vp, _vp, _i32, _vp, _u32, _cp,
+                                    _u64]),
+        "s3dsp_convert": (_u32, [_vp, _vp, _u32, _vp, _u32, _i64, _cp, _u64]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def _call(fn, *args):
+    buf = ctypes.create_string_buffer(512)
+    st = fn(*args, buf, ctypes.c_uint64(len(buf)))
+    if st != S3D_OK:
+        raise S3dError(st, buf.value.decode(errors="replace"))
+
+
+def ptr(t) -> int | None:
+    """Device (or host) address of a torch tensor, or None."""
+    if t is None:
+        return None
+    return t.data_ptr()
+
+
+def dtype_code(t) -> int:
+    import torch
+    return {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}[t.dtype]
+
+
+class Kmap:
+    def __init__(self, ctx: "Context", handle: int, rows: int):
+        self.ctx, self.handle, self.rows = ctx, handle, rows
+
+    def free(self):
+        if self.handle:
+            load().s3dsp_kmap_free(self.ctx.handle, self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class Hash:
+    def __init__(self, ctx: "Context", handle: int, n: int):
+        self.ctx, self.handle, self.n = ctx, handle, n
+
+    def free(self):
+        if self.handle:
+            load().s3dsp_hash_free(self.ctx.handle, self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class Context:
+    """One device + one CUDA stream (default: torch's current stream)."""
+
+    def __init__(self, device: int = 0, stream: int | None = None, flags: int = 0):
+        L = load()
+        if stream is None:
+            import torch
+            stream = torch.cuda.current_stream(device).cuda_stream
+        h = _vp()
+        _call(L.s3dsp_context_create, device, stream, flags, ctypes.byref(h))
+        self.handle = h.value
+        self.device = device
+
+    def close(self):
+        if getattr(self, "handle", None):
+            load().s3dsp_context_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def check(self):
+        _call(load().s3dsp_context_check, self.handle)
+
+    # ---- K1 / K2 --------------------------------------------------------
+    def hash_build(self, coords, reject_duplicates: bool = False) -> Hash:
+        h = _vp()
+        _call(load().s3dsp_hash_build, self.handle, ptr(coords), coords.shape[0], int(reject_duplicates),
+              ctypes.byref(h))
+        return Hash(self, h.value, coords.shape[0])
+
+    def hash_lookup(self, hsh: Hash, query, rows_out):
+        _call(load().s3dsp_hash_lookup, self.handle, hsh.handle, ptr(query), query.shape[0], ptr(rows_out))
+
+    def kmap_subm3(self, hsh: Hash) -> Kmap:
+        k = _vp()
+        _call(load().s3dsp_kmap_build_subm3, self.handle, hsh.handle, ctypes.byref(k))
+        return Kmap(self, k.value, hsh.n)
+
+    def subdivide(self, parents: Hash, child_coords_out) -> Kmap:
+        k = _vp()
+        _call(load().s3dsp_subdivide, self.handle, parents.handle, ptr(child_coords_out), ctypes.byref(k))
+        return Kmap(self, k.value, parents.n * 8)
+
+    def kmap_export_dense(self, kmap: Kmap, sentinel_mode: int, out):
+        _call(load().s3dsp_kmap_export_dense, self.handle, kmap.handle, sentinel_mode, ptr(out))
+
+    def kmap_pairs(self, kmap: Kmap, pin, pout):
+        offs = (ctypes.c_int64 * 28)()
+        _call(load().s3dsp_kmap_pairs, self.handle, kmap.handle, ptr(pin), ptr(pout), pin.numel(), offs)
+        return list(offs)
+
+    # ---- weights ---------------------------------------------------------
+    @staticmethod
+    def packed_bytes(precision: int, kvol: int, cin: int, cout: int) -> int:
+        return load().s3dsp_weights_packed_bytes(precision, kvol, cin, cout)
+
+    def weights_pack(self, src, layout: int, kvol: int, cin: int, cout: int, precision: int, dst):
+        on_host = 0 if src.is_cuda else 1
+        _call(load().s3dsp_weights_pack, self.handle, ptr(src), dtype_code(src), on_host, layout, kvol, cin, cout,
+              precision, ptr(dst))
+
+    # ---- conv ------------------------------------------------------------
+    def conv(self, kmap: Kmap | None, kvol: int, precision: int, x, weight, bias, out, cout: int,
+             in_shift: int = 0, residual=None, res_shift: int = 0, flags: int = 0, pro=None,
+             gn_partials=None, gn_groups: int = 0, n_out: int | None = None):
+        n_out = out.shape[0] if n_out is None else n_out
+        sub, mul, add = pro if pro is not None else (None, None, None)
+        _call(load().s3dsp_conv, self.handle, kmap.handle if kmap else None, kvol, precision, ptr(x),
+              dtype_code(x), x.shape[0], x.shape[1], in_shift, ptr(weight), ptr(bias), ptr(residual),
+              dtype_code(residual) if residual is not None else 0, res_shift, ptr(out), dtype_code(out), n_out,
+              cout, flags, ptr(sub), ptr(mul), ptr(add), ptr(gn_partials), gn_groups)
+
+    # ---- norms -----------------------------------------------------------
+    @staticmethod
+    def gn_partials_count(n_rows: int, channels: int, groups: int) -> int:
+        return load().s3dsp_gn_partials_count(n_rows, channels, groups)
+
+    def gn_stats(self, x, groups: int, partials):
+        _call(load().s3dsp_gn_stats, self.handle, ptr(x), dtype_code(x), x.shape[0], x.shape[1], groups,
+              ptr(partials))
+
+    def gn_finalize(self, partials, n_rows: int, c: int, groups: int, eps: float, gamma, beta, sub, mul, add):
+        _call(load().s3dsp_gn_finalize, self.handle, ptr(partials), n_rows, c, groups, eps, ptr(gamma), ptr(beta),
+              ptr(sub), ptr(mul), ptr(add))
+
+    def channel_affine(self, x, sub, mul, add, silu: bool, y):
+        _call(load().s3dsp_channel_affine, self.handle, ptr(x), dtype_code(x), x.shape[0], x.shape[1], ptr(sub),
+              ptr(mul), ptr(add), int(silu), ptr(y), dtype_code(y))
+
+    def layer_norm(self, x, eps: float, y, gamma=None, beta=None, mod_scale=None, mod_shift=None,
+                   silu: bool = False):
+        _call(load().s3dsp_layer_norm, self.handle, ptr(x), dtype_code(x), x.shape[0], x.shape[1], eps, ptr(gamma),
+              ptr(beta), ptr(mod_scale), ptr(mod_shift), int(silu), ptr(y), dtype_code(y))
+
+    def convert(self, x, y):
+        _call(load().s3dsp_convert, self.handle, ptr(x), dtype_code(x), ptr(y), dtype_code(y), x.numel())
