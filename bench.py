@@ -131,27 +131,29 @@ class ResBlockPath:
         self.conv_events = []
         self.launches_per_step = 8  # insert, self-row, kmap, convert, conv1, finalize, affine, conv2
 
+    PHASES = ("hash", "kmap", "convert", "conv1", "gn_finalize+affine", "conv2")
+
     def step(self, time_convs=False, coords=None, x=None):
         s, ctx, t = self.s, self.ctx, self.torch
         coords = self.coords if coords is None else coords
         x = self.x if x is None else x
+        ev = [t.cuda.Event(enable_timing=True) for _ in range(7)] if time_convs else None
+        mark = (lambda i: ev[i].record()) if time_convs else (lambda i: None)
+        mark(0)
         h = ctx.hash_build(coords)
+        mark(1)
         k = ctx.kmap_subm3(h)
+        mark(2)
         ctx.convert(x, self.xb)
-        ev = None
-        if time_convs:
-            ev = [t.cuda.Event(enable_timing=True) for _ in range(4)]
-            ev[0].record()
+        mark(3)
         ctx.conv(k, 27, s.PREC_BF16, self.xb, self.w1, self.b1, self.y1, self.c, gn_partials=self.part, gn_groups=32)
-        if time_convs:
-            ev[1].record()
+        mark(4)
         ctx.gn_finalize(self.part, self.n, self.c, 32, 1e-5, self.gamma, self.beta, self.sub, self.mul, self.add)
         ctx.channel_affine(self.y1, self.sub, self.mul, self.add, True, self.hb)
-        if time_convs:
-            ev[2].record()
+        mark(5)
         ctx.conv(k, 27, s.PREC_BF16, self.hb, self.w2, self.b2, self.out, self.c, residual=x)
+        mark(6)
         if time_convs:
-            ev[3].record()
             self.conv_events.append(ev)
         return h, k
 
@@ -205,7 +207,9 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     wall = time.perf_counter() - t0
     dev_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
-    conv_ms = [(ev[0].elapsed_time(ev[1]), ev[2].elapsed_time(ev[3])) for ev in path.conv_events]
+    phase_ms = np.array([[ev[i].elapsed_time(ev[i + 1]) for i in range(6)] for ev in path.conv_events])
+    conv_ms = [(row[3], row[5]) for row in phase_ms]
+    breakdown = {name: float(v) for name, v in zip(ResBlockPath.PHASES, phase_ms.mean(0))}
 
     # ---- e2e: host buffers in, host result out, through the same C-ABI calls ----
     coords_h = torch.from_numpy(cfg["coords"]).pin_memory()
@@ -268,6 +272,7 @@ def run_ours(args, rank, world, local_rank):
         "gpu_launches": path.launches_per_step * (args.steps * 2 + args.warmup * 2),
         "clocks": clocks,
         "wall_s": wall,
+        "breakdown_ms": breakdown,
     }
     if world == 1:
         line["cpu_baseline"] = cpu_baseline(cfg, sample_only=True)

@@ -75,12 +75,15 @@ typedef struct s3dsp_kmap s3dsp_kmap;
 /* context flags */
 #define S3DSP_CONTEXT_DEFERRED_CHECKS UINT32_C(1) /* device-detected input errors are reported by
                                                      s3dsp_context_check instead of at each call */
+#define S3DSP_CONTEXT_OWN_STREAM UINT32_C(2)      /* create (and own) a new non-blocking stream */
 
 S3DSP_API uint32_t s3dsp_abi_version(void);
 
 /* ---------------------------------------------------------------------------
  * Context: one CUDA device + one stream (replaces the per-stage Backend,
- * backend.cpp:44-118). `stream` is a cudaStream_t or NULL for a new stream.
+ * backend.cpp:44-118). `stream` is a cudaStream_t; NULL is the legacy default
+ * stream, as everywhere in CUDA. With S3DSP_CONTEXT_OWN_STREAM the context
+ * creates its own non-blocking stream instead and `stream` is ignored.
  * ------------------------------------------------------------------------- */
 S3DSP_API s3d_status s3dsp_context_create(int32_t device, void *stream, uint32_t flags,
                                           s3dsp_context **out, char *error,

@@ -28,8 +28,8 @@ extern "C" S3DSP_API s3d_status s3dsp_context_create(int32_t device, void* strea
     ctx->device = device;
     ctx->flags = flags;
     ctx->sm_count = prop.multiProcessorCount;
-    if (stream) {
-        ctx->stream = (cudaStream_t)stream;
+    if (!(flags & S3DSP_CONTEXT_OWN_STREAM)) {
+        ctx->stream = (cudaStream_t)stream;  // NULL = the legacy default stream
     } else {
         cudaError_t e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
         if (e != cudaSuccess) {
@@ -37,6 +37,14 @@ extern "C" S3DSP_API s3d_status s3dsp_context_create(int32_t device, void* strea
             return cuda_fail(error, error_capacity, e, "cudaStreamCreate");
         }
         ctx->owns_stream = true;
+    }
+    // Keep memory freed by cudaFreeAsync in the device pool instead of
+    // returning it at every synchronisation: hash tables and kernel maps are
+    // rebuilt per object, and re-mapping pool memory costs milliseconds.
+    cudaMemPool_t pool;
+    if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess) {
+        uint64_t keep = ~0ull;
+        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
     }
     cudaError_t e = cudaMalloc(&ctx->d_status, 4 * sizeof(uint32_t));
     if (e == cudaSuccess) e = cudaMemsetAsync(ctx->d_status, 0, 4 * sizeof(uint32_t), ctx->stream);

@@ -63,8 +63,10 @@ extern "C" S3DSP_API s3d_status s3dsp_conv(s3dsp_context* ctx, const s3dsp_kmap*
         if (flags & S3DSP_PRO_AFFINE_SILU)
             return fail(error, error_capacity, S3D_INVALID_ARGUMENT,
                         "BF16 conv takes pre-normalised input (use s3dsp_channel_affine)");
-        if (cin % 8 || ((uintptr_t)in & 15) || ((uintptr_t)weight & 15))
-            return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "BF16 needs cin %% 8 == 0 and 16-byte alignment");
+        if (cin % 8 || ((uintptr_t)in & 15) || ((uintptr_t)weight & 15) || ((uintptr_t)out & 15) ||
+            ((uintptr_t)residual & 15))
+            return fail(error, error_capacity, S3D_INVALID_ARGUMENT,
+                        "BF16 needs cin %% 8 == 0 and 16-byte aligned in/weight/out/residual");
         s3d_status st = S3D_OK;
         e = launch_conv_tc(ctx, kmap, kvol, (const __nv_bfloat16*)in, n_in, (int)cin, in_shift,
                            (const __nv_bfloat16*)weight, bias, residual, res_dtype, res_shift, out, out_dtype, n_out,

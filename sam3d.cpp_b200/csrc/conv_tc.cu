@@ -3,22 +3,27 @@
 //
 // Tile: 128 output rows x BN output channels per CTA (BN = a multiple of 16,
 // <= 256). The reduction walks (active offset, 64-channel chunk) steps. Per
-// step, stage s of a multi-stage shared-memory ring receives
+// step, stage s of a shared-memory ring receives
 //   A: the 128 gathered input rows (64 bf16 = 128 B each) by cp.async from
-//      the gather index (16-byte copies, zero-filled for missing neighbours),
-//      written in the 128-byte-swizzled K-major layout the MMA descriptor
-//      expects;
-//   B: the BN x 64 weight tile W[o][n0:n0+BN][k0:k0+64] by one TMA tensor
-//      load (128-byte swizzle), no multicast.
-// One elected thread issues 4 tcgen05.mma (M=128, N=BN, K=16) per step and
-// releases the stage with tcgen05.commit. The epilogue warps read the
-// accumulator back with tcgen05.ld, add bias / residual, optionally SiLU,
-// accumulate GroupNorm partial sums and store; nothing is accumulated
-// through atomics on the output.
+//      512 producer threads (8 threads per row, 16 B each, zero-filled for a
+//      missing neighbour); each thread's copies complete onto the stage's
+//      mbarrier (cp.async.mbarrier.arrive.noinc), so producers run ahead;
+//   B: the BN x 64 weight tile W[o][n0:n0+BN][k0:k0+64] as NB TMA tile loads
+//      of BN/NB rows, issued by NB different warps: one thread's TMA ops are
+//      serialised (a few hundred cycles each), separate issuers overlap.
+// Both use the 128-byte swizzle that the MMA smem descriptors describe. One
+// elected thread issues 4 tcgen05.mma (M=128, N=BN, K=16) per step and frees
+// the stage with tcgen05.commit.
 //
-// Warp roles (192 threads): warps 0-3 gather A and then run the epilogue
-// (warp w owns TMEM lanes 32w..32w+31 = tile rows); warp 4 issues the weight
-// TMA; warp 5 owns the TMEM allocation and issues the MMAs.
+// Epilogue: the accumulator is read back with tcgen05.ld into a padded
+// shared-memory tile (each warp its 32 TMEM lanes = rows), then written out
+// row by row with coalesced vector loads/stores: bias, residual, GroupNorm
+// partial sums (f64) and SiLU are applied on the way. Outputs are written
+// once; nothing accumulates through atomics.
+//
+// Warp roles (672 threads): warps 0-15 gather A, and warps 0-3 then run the
+// epilogue (warp w reads TMEM lanes 32*w .. +31); warps 16-19 issue the
+// weight TMA loads (lane 0 each); warp 20 owns TMEM and issues the MMAs.
 //
 // Every mbarrier wait is bounded (about two seconds of %globaltimer); on
 // timeout the CTA records kErrPipelineTimeout, stops issuing work and exits
@@ -32,13 +37,19 @@
 
 #include <cudaTypedefs.h>
 
+#include <type_traits>
+
 using namespace s3dsp;
 
 namespace {
 
-constexpr int kThreads = 192;
+constexpr int kProdWarps = 16;      // A gather warps (512 threads)
+constexpr int kBWarp0 = 16;         // first weight-TMA warp
+constexpr int kMaxBWarps = 4;
+constexpr int kMmaWarp = 20;
+constexpr int kThreads = 21 * 32;
+constexpr int kEpiWarp0 = 0;        // first of the 4 epilogue warps
 constexpr int kAStage = 128 * 128;  // bytes: 128 rows x 64 bf16
-constexpr int kLag = 2;             // cp.async groups kept in flight per producer thread
 constexpr int kMaxKvol = 27;
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s
 
@@ -51,6 +62,7 @@ struct TcParams {
     int kvol;
     int cout_pad;               // packed weight rows per offset
     int bn;
+    int nb;                     // weight TMA loads per stage (issuer warps)
     int stages;
     uint32_t idesc;
     const float* bias;
@@ -80,9 +92,6 @@ __device__ __forceinline__ unsigned long long global_ns() {
 }
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 __device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
@@ -116,23 +125,19 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
         }
     }
 }
-__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-__device__ __forceinline__ void fence_proxy_async() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
         "l"((unsigned long long)map), "r"(x), "r"(y), "r"(bar)
         : "memory");
+}
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+// arrive on `bar` once all of this thread's prior cp.async copies have landed
+// (counts as one of the barrier's expected arrivals)
+__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -156,7 +161,8 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                  : "memory");
 }
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&f)[16]) {
+    uint32_t v[16];
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
         : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
@@ -164,14 +170,134 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
         : "r"(taddr)
         : "memory");
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int j = 0; j < 16; ++j) f[j] = __uint_as_float(v[j]);
 }
 
 __device__ __forceinline__ float silu_f(float v) { return v / (1.0f + __expf(-v)); }
 
-__device__ __forceinline__ float load_as_f32(const void* p, uint32_t dt, int64_t i) {
+__device__ __forceinline__ float load1(const void* p, uint32_t dt, int64_t i) {
     if (dt == S3DSP_F32) return reinterpret_cast<const float*>(p)[i];
     if (dt == S3DSP_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
     return __half2float(reinterpret_cast<const __half*>(p)[i]);
+}
+__device__ __forceinline__ void store1(void* p, uint32_t dt, int64_t i, float v) {
+    if (dt == S3DSP_F32)
+        reinterpret_cast<float*>(p)[i] = v;
+    else if (dt == S3DSP_BF16)
+        reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16(v);
+    else
+        reinterpret_cast<__half*>(p)[i] = __float2half(v);
+}
+
+
+// ---------------------------------------------------------------------------
+// epilogue write-out: typed vector access, one compact loop per variant
+// ---------------------------------------------------------------------------
+struct NoRes {};
+template <typename T>
+struct Vec4;
+template <>
+struct Vec4<float> {
+    static __device__ __forceinline__ float4 load(const void* base, int64_t i) {
+        return __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + i));
+    }
+    static __device__ __forceinline__ void store(void* base, int64_t i, float4 v) {
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(base) + i) = v;
+    }
+};
+template <>
+struct Vec4<__nv_bfloat16> {
+    static __device__ __forceinline__ float4 load(const void* base, int64_t i) {
+        const uint2 u = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(base) + i));
+        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+        const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+        return make_float4(a.x, a.y, b.x, b.y);
+    }
+    static __device__ __forceinline__ void store(void* base, int64_t i, float4 v) {
+        const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+        *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(base) + i) =
+            make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+    }
+};
+
+// Rows lane_base .. lane_base+nrows-1 of the staged f32 tile -> global, four
+// consecutive columns per lane (cout % 4 == 0, so a lane's four columns are
+// all valid or all past `limit`).
+template <typename OutT, typename ResT, bool SILU, bool STATS>
+__device__ __forceinline__ void writeout_fast(const TcParams& p, uint32_t so_base, int ostride, int lane_base, int lane,
+                                              int64_t m0, int n0, int limit, int nrows, const float4 (&bias4)[2],
+                                              double (&s1)[2][4], double (&s2)[2][4]) {
+#pragma unroll 2
+    for (int rr = 0; rr < nrows; ++rr) {
+        const int row = lane_base + rr;
+        const int64_t r = m0 + row;
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const int lc = 128 * q + 4 * lane;
+            if (lc >= limit) continue;
+            float4 v;
+            asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+                         : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                         : "r"(so_base + (uint32_t)((row * ostride + lc) * 4)));
+            v.x += bias4[q].x;
+            v.y += bias4[q].y;
+            v.z += bias4[q].z;
+            v.w += bias4[q].w;
+            if constexpr (!std::is_same<ResT, NoRes>::value) {
+                const float4 t = Vec4<ResT>::load(p.residual, (r >> p.res_shift) * p.cout + n0 + lc);
+                v.x += t.x;
+                v.y += t.y;
+                v.z += t.z;
+                v.w += t.w;
+            }
+            if constexpr (STATS) {
+                s1[q][0] += (double)v.x;
+                s2[q][0] += (double)v.x * v.x;
+                s1[q][1] += (double)v.y;
+                s2[q][1] += (double)v.y * v.y;
+                s1[q][2] += (double)v.z;
+                s2[q][2] += (double)v.z * v.z;
+                s1[q][3] += (double)v.w;
+                s2[q][3] += (double)v.w * v.w;
+            }
+            if constexpr (SILU) {
+                v.x = silu_f(v.x);
+                v.y = silu_f(v.y);
+                v.z = silu_f(v.z);
+                v.w = silu_f(v.w);
+            }
+            Vec4<OutT>::store(p.out, r * p.cout + n0 + lc, v);
+        }
+    }
+}
+
+// Any dtype / ragged width: element-wise.
+__device__ __forceinline__ void writeout_generic(const TcParams& p, const float* stage_out, int ostride, int lane_base,
+                                              int lane, int64_t m0, int n0, int limit, int nrows,
+                                              const float4 (&bias4)[2], bool stats, double (&s1)[2][4],
+                                              double (&s2)[2][4]) {
+    for (int rr = 0; rr < nrows; ++rr) {
+        const int row = lane_base + rr;
+        const int64_t r = m0 + row;
+        for (int q = 0; q < 2; ++q) {
+            const int lc0 = 128 * q + 4 * lane;
+            for (int j = 0; j < 4; ++j) {
+                const int lc = lc0 + j;
+                if (lc >= limit) break;
+                const int col = n0 + lc;
+                const float bj = j == 0 ? bias4[q].x : j == 1 ? bias4[q].y : j == 2 ? bias4[q].z : bias4[q].w;
+                float v = stage_out[(size_t)row * ostride + lc] + bj;
+                if (p.residual) v += load1(p.residual, p.res_dtype, (r >> p.res_shift) * p.cout + col);
+                if (stats) {
+                    s1[q][j] += (double)v;
+                    s2[q][j] += (double)v * v;
+                }
+                if (p.flags & S3DSP_EPI_SILU) v = silu_f(v);
+                store1(p.out, p.out_dtype, r * p.cout + col, v);
+            }
+        }
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -184,15 +310,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int S = p.stages;
     const int bstage = p.bn * 128;
+    // layout (offsets from the 1024-aligned base): ring A | ring B | sidx |
+    // gsum | barriers | tmem holder, abort flag. The tail starts 1024-aligned,
+    // so sidx (read as int4) and gsum (f64) are 16-byte aligned.
     uint8_t* sA = smem;
     uint8_t* sB = smem + (size_t)S * kAStage;
-    uint64_t* full = reinterpret_cast<uint64_t*>(sB + (size_t)S * bstage);
+    int32_t* sidx = reinterpret_cast<int32_t*>(sB + (size_t)S * bstage);  // [kvol][128]
+    double* gsum = reinterpret_cast<double*>(sidx + kMaxKvol * 128);       // [64][2]
+    uint64_t* full = reinterpret_cast<uint64_t*>(gsum + 128);
     uint64_t* empty = full + S;
     uint64_t* accum = empty + S;
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(accum + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-    double* gsum = reinterpret_cast<double*>(tmem_holder + 4);           // [64][2]
-    int32_t* sidx = reinterpret_cast<int32_t*>(gsum + 128);              // [kvol][128]
+    float* stage_out = reinterpret_cast<float*>(smem);           // epilogue tile (reuses the ring)
+    const int ostride = p.bn + 4;                                 // padded row stride (floats)
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
@@ -209,14 +340,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- setup: barriers, TMEM, gather indices ----
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
-            mbar_init(smem_u32(full + s), 128 + 1);
+            mbar_init(smem_u32(full + s), kProdWarps * 32 + p.nb);  // cp.async threads + weight issuers
             mbar_init(smem_u32(empty + s), 1);
         }
         mbar_init(smem_u32(accum), 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 5) {
+    if (warp == kMmaWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
                      "r"(tcols)
                      : "memory");
@@ -224,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (p.gn_partials)
         for (int i = tid; i < 128; i += kThreads) gsum[i] = 0.0;
-    // gather indices of the active offsets for the tile's 128 rows
+    // gather row coordinates of the active offsets for the tile's 128 rows
     for (int i = tid; i < kMaxKvol * 128; i += kThreads) {
         const int o = i >> 7, row = i & 127;
         if (!((mask >> o) & 1u)) continue;
@@ -238,13 +369,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
 
-    if (warp < 4) {
-        // ================= A producers: gathered rows via cp.async =================
+    bool prod_ok = true;
+    if (warp < kProdWarps) {
+        // ================= A producers: cp.async gathers =================
         const int c16 = tid & 7;  // 16-byte chunk within a 128-byte row
-        const int rg = tid >> 3;  // rows rg + 16*i
+        const int rg = tid >> 3;  // rows rg and rg + 64
         uint32_t mrem = mask;
         int o = 0;
-        bool ok = true;
         for (int it = 0; it < T; ++it) {
             const int s = it % S;
             const uint32_t ph = (uint32_t)(it / S) & 1u;
@@ -254,139 +385,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mrem &= mrem - 1;
             }
             if (!mbar_wait(smem_u32(empty + s), ph ^ 1u, abort_flag, p.status)) {
-                ok = false;
+                prod_ok = false;
                 break;
             }
             const int k0 = kc * 64 + c16 * 8;
             const uint32_t a_base = smem_u32(sA + (size_t)s * kAStage);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int row = rg + 16 * i;
+            for (int i = 0; i < 2; ++i) {
+                const int row = rg + 64 * i;
                 const int32_t src = sidx[o * 128 + row];
                 const bool valid = src >= 0 && k0 < p.cin;
                 const void* g = valid ? (const void*)(p.in + (int64_t)src * p.cin + k0) : (const void*)p.in;
                 cp_async_16(a_base + row * 128 + ((c16 ^ (row & 7)) << 4), g, valid ? 16u : 0u);
             }
-            cp_async_commit();
-            if (it >= kLag) {
-                cp_async_wait<kLag>();
-                fence_proxy_async();
-                mbar_arrive(smem_u32(full + (it - kLag) % S));
-            }
+            cp_async_arrive_noinc(smem_u32(full + s));
         }
-        cp_async_wait<0>();
-        fence_proxy_async();
-        if (ok)
-            for (int it = (T > kLag ? T - kLag : 0); it < T; ++it) mbar_arrive(smem_u32(full + it % S));
-
-        // ================= epilogue =================
-        const int row = warp * 32 + lane;
-        const int64_t r = m0 + row;
-        const bool have_acc = T > 0 && ok && mbar_wait(smem_u32(accum), 0, abort_flag, p.status);
-        tc_fence_after();
-        const bool stats = p.gn_partials != nullptr;
-        const int gs = stats ? p.cout / p.gn_groups : 1;
-        const bool row_ok = r < p.n_out;
-        const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
-        for (int c0 = 0; c0 < p.bn; c0 += 16) {
-            uint32_t v[16];
-            if (have_acc) {
-                tmem_ld16(taddr + (uint32_t)c0, v);
-            } else {
-#pragma unroll
-                for (int j = 0; j < 16; ++j) v[j] = 0u;
-            }
-            float f[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int col = n0 + c0 + j;
-                float x = __uint_as_float(v[j]);
-                if (col < p.cout) {
-                    if (p.bias) x += __ldg(p.bias + col);
-                    if (p.residual && row_ok)
-                        x += load_as_f32(p.residual, p.res_dtype, (r >> p.res_shift) * p.cout + col);
-                }
-                f[j] = x;
-            }
-            if (stats) {
-                // columns are warp-uniform, so group changes are too
-                double s1 = 0.0, s2 = 0.0;
-                int g_cur = -1;
-                for (int j = 0; j <= 16; ++j) {
-                    const int col = n0 + c0 + j;
-                    const int g = (j < 16 && col < p.cout) ? col / gs : -2;
-                    if (g != g_cur) {
-                        if (g_cur >= 0) {
-#pragma unroll
-                            for (int d = 16; d > 0; d >>= 1) {
-                                s1 += __shfl_xor_sync(0xffffffffu, s1, d);
-                                s2 += __shfl_xor_sync(0xffffffffu, s2, d);
-                            }
-                            if (lane == 0) {
-                                atomicAdd(gsum + 2 * g_cur, s1);
-                                atomicAdd(gsum + 2 * g_cur + 1, s2);
-                            }
-                        }
-                        s1 = s2 = 0.0;
-                        g_cur = g;
-                    }
-                    if (g >= 0 && row_ok) {
-                        s1 += (double)f[j];
-                        s2 += (double)f[j] * (double)f[j];
-                    }
-                }
-            }
-            if (p.flags & S3DSP_EPI_SILU) {
-#pragma unroll
-                for (int j = 0; j < 16; ++j) f[j] = silu_f(f[j]);
-            }
-            if (row_ok) {
-                const int nvalid = min(16, p.cout - (n0 + c0));
-                if (p.out_dtype == S3DSP_F32) {
-                    float* dst = reinterpret_cast<float*>(p.out) + r * p.cout + n0 + c0;
-                    if (nvalid == 16 && (p.cout & 3) == 0) {
-#pragma unroll
-                        for (int q = 0; q < 4; ++q)
-                            reinterpret_cast<float4*>(dst)[q] = make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
-                    } else {
-                        for (int j = 0; j < nvalid; ++j) dst[j] = f[j];
-                    }
-                } else {
-                    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + r * p.cout + n0 + c0;
-                    if (p.out_dtype == S3DSP_BF16 && nvalid == 16 && (p.cout & 7) == 0) {
-                        uint32_t w[8];
-#pragma unroll
-                        for (int q = 0; q < 8; ++q) {
-                            const __nv_bfloat162 h2 = __floats2bfloat162_rn(f[2 * q], f[2 * q + 1]);
-                            w[q] = *reinterpret_cast<const uint32_t*>(&h2);
-                        }
-                        reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-                        reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
-                    } else if (p.out_dtype == S3DSP_BF16) {
-                        for (int j = 0; j < nvalid; ++j) dst[j] = __float2bfloat16(f[j]);
-                    } else {
-                        __half* hd = reinterpret_cast<__half*>(p.out) + r * p.cout + n0 + c0;
-                        for (int j = 0; j < nvalid; ++j) hd[j] = __float2half(f[j]);
-                    }
-                }
-            }
-        }
-        if (stats) {
-            asm volatile("bar.sync 1, 128;" ::: "memory");
-            const int g_lo = n0 / gs;
-            const int g_hi = min(p.gn_groups - 1, (min(n0 + p.bn, p.cout) - 1) / gs);
-            for (int g = g_lo + tid; g <= g_hi; g += 128) {
-                atomicAdd(p.gn_partials + ((int64_t)tile * p.gn_groups + g) * 2 + 0, gsum[2 * g]);
-                atomicAdd(p.gn_partials + ((int64_t)tile * p.gn_groups + g) * 2 + 1, gsum[2 * g + 1]);
-            }
-        }
-        tc_fence_before();
-    } else if (warp == 4) {
-        // ================= B producer: weight tiles via TMA =================
-        if (lane == 0) {
+        asm volatile("cp.async.wait_all;" ::: "memory");
+    } else if (warp < kBWarp0 + kMaxBWarps) {
+        // ================= weight TMA issuers =================
+        const int j = warp - kBWarp0;
+        if (lane == 0 && j < p.nb) {
             uint32_t mrem = mask;
             int o = 0;
-            const uint32_t bytes = (uint32_t)bstage;
+            const int rows = p.bn / p.nb;
+            const uint32_t bytes = (uint32_t)rows * 128;
             for (int it = 0; it < T; ++it) {
                 const int s = it % S;
                 const uint32_t ph = (uint32_t)(it / S) & 1u;
@@ -398,10 +420,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!mbar_wait(smem_u32(empty + s), ph ^ 1u, abort_flag, p.status)) break;
                 const uint32_t fb = smem_u32(full + s);
                 mbar_arrive_tx(fb, bytes);
-                tma_load_2d(smem_u32(sB + (size_t)s * bstage), &wmap, kc * 64, o * p.cout_pad + n0, fb);
+                tma_load_2d(smem_u32(sB + (size_t)s * bstage + (size_t)j * rows * 128), &wmap, kc * 64,
+                            o * p.cout_pad + n0 + j * rows, fb);
             }
         }
-    } else {
+    } else if (warp == kMmaWarp) {
         // ================= MMA issuer =================
         if (lane == 0) {
             bool ok = true;
@@ -425,9 +448,119 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     }
+    if (warp < 4) {
+        // ================= epilogue (warps 0-3, after their gathers) =================
+        const int lane_base = 32 * warp;  // TMEM lanes this warp may access
+        bool have_acc = T > 0 && prod_ok && mbar_wait(smem_u32(accum), 0, abort_flag, p.status);
+        have_acc = __all_sync(0xffffffffu, have_acc);
+        tc_fence_after();
+        // phase 1: TMEM -> padded smem tile, row = lane_base + lane
+        {
+            float* dst = stage_out + (size_t)(lane_base + lane) * ostride;
+            const uint32_t taddr = tmem + ((uint32_t)lane_base << 16);
+            for (int c0 = 0; c0 < p.bn; c0 += 16) {
+                float f[16];
+                if (have_acc) {
+                    tmem_ld16(taddr + (uint32_t)c0, f);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) f[j] = 0.f;
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    *reinterpret_cast<float4*>(dst + c0 + 4 * q) = make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
+            }
+        }
+        __syncwarp();
+        // phase 2: coalesced row write-out. lane owns columns 4*lane + 128*q.
+        const bool stats = p.gn_partials != nullptr;
+        const int gs = stats ? p.cout / p.gn_groups : 1;
+        constexpr int kQ = 2;  // bn <= 256 -> at most two 128-column slabs
+        const int limit = min(p.bn, p.cout - n0);  // valid columns of this tile
+        float4 bias4[kQ];
+        double s1[kQ][4], s2[kQ][4];
+#pragma unroll
+        for (int q = 0; q < kQ; ++q) {
+            const int col = n0 + 128 * q + 4 * lane;
+            bias4[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (p.bias && 128 * q + 4 * lane < limit) {
+                bias4[q].x = __ldg(p.bias + col + 0);
+                bias4[q].y = col + 1 < p.cout ? __ldg(p.bias + col + 1) : 0.f;
+                bias4[q].z = col + 2 < p.cout ? __ldg(p.bias + col + 2) : 0.f;
+                bias4[q].w = col + 3 < p.cout ? __ldg(p.bias + col + 3) : 0.f;
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) s1[q][j] = s2[q][j] = 0.0;
+        }
+        const int nrows = (int)min((int64_t)32, p.n_out - (m0 + lane_base));
+        const uint32_t so_base = smem_u32(stage_out);
+        // One compact loop body per (out dtype, residual dtype, SiLU, stats)
+        // combination: a single generic body with every variant inlined runs
+        // several times slower (instruction-cache misses).
+        const int out_k = (p.cout & 3) ? -1 : p.out_dtype == S3DSP_F32 ? 0 : p.out_dtype == S3DSP_BF16 ? 1 : -1;
+        const int res_k = !p.residual ? 0 : p.res_dtype == S3DSP_F32 ? 1 : p.res_dtype == S3DSP_BF16 ? 2 : -1;
+        const int silu_k = (p.flags & S3DSP_EPI_SILU) ? 1 : 0;
+        const int sel = (out_k < 0 || res_k < 0) ? -1 : ((out_k * 3 + res_k) * 2 + silu_k) * 2 + (stats ? 1 : 0);
+        switch (sel) {
+#define S3DSP_WO(idx, OT, RT, SL, ST)                                                                            \
+    case idx:                                                                                                \
+        writeout_fast<OT, RT, SL, ST>(p, so_base, ostride, lane_base, lane, m0, n0, limit, nrows, bias4, s1, s2); \
+        break;
+            S3DSP_WO(0, float, NoRes, false, false)
+            S3DSP_WO(1, float, NoRes, false, true)
+            S3DSP_WO(2, float, NoRes, true, false)
+            S3DSP_WO(3, float, NoRes, true, true)
+            S3DSP_WO(4, float, float, false, false)
+            S3DSP_WO(5, float, float, false, true)
+            S3DSP_WO(6, float, float, true, false)
+            S3DSP_WO(7, float, float, true, true)
+            S3DSP_WO(8, float, __nv_bfloat16, false, false)
+            S3DSP_WO(9, float, __nv_bfloat16, false, true)
+            S3DSP_WO(10, float, __nv_bfloat16, true, false)
+            S3DSP_WO(11, float, __nv_bfloat16, true, true)
+            S3DSP_WO(12, __nv_bfloat16, NoRes, false, false)
+            S3DSP_WO(13, __nv_bfloat16, NoRes, false, true)
+            S3DSP_WO(14, __nv_bfloat16, NoRes, true, false)
+            S3DSP_WO(15, __nv_bfloat16, NoRes, true, true)
+            S3DSP_WO(16, __nv_bfloat16, float, false, false)
+            S3DSP_WO(17, __nv_bfloat16, float, false, true)
+            S3DSP_WO(18, __nv_bfloat16, float, true, false)
+            S3DSP_WO(19, __nv_bfloat16, float, true, true)
+            S3DSP_WO(20, __nv_bfloat16, __nv_bfloat16, false, false)
+            S3DSP_WO(21, __nv_bfloat16, __nv_bfloat16, false, true)
+            S3DSP_WO(22, __nv_bfloat16, __nv_bfloat16, true, false)
+            S3DSP_WO(23, __nv_bfloat16, __nv_bfloat16, true, true)
+#undef S3DSP_WO
+            default:
+                writeout_generic(p, stage_out, ostride, lane_base, lane, m0, n0, limit, nrows, bias4, stats, s1, s2);
+        }
+        if (stats) {
+#pragma unroll
+            for (int q = 0; q < kQ; ++q)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int lc = 128 * q + 4 * lane + j;
+                    const int col = n0 + lc;
+                    if (lc < limit) {
+                        const int g = col / gs;
+                        atomicAdd(gsum + 2 * g, s1[q][j]);
+                        atomicAdd(gsum + 2 * g + 1, s2[q][j]);
+                    }
+                }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            const int et = tid - kEpiWarp0 * 32;
+            const int g_lo = n0 / gs;
+            const int g_hi = min(p.gn_groups - 1, (min(n0 + p.bn, p.cout) - 1) / gs);
+            for (int g = g_lo + et; g <= g_hi; g += 128) {
+                atomicAdd(p.gn_partials + ((int64_t)tile * p.gn_groups + g) * 2 + 0, gsum[2 * g]);
+                atomicAdd(p.gn_partials + ((int64_t)tile * p.gn_groups + g) * 2 + 1, gsum[2 * g + 1]);
+            }
+        }
+        tc_fence_before();
+    }
 
     __syncthreads();
-    if (warp == 5) {
+    if (warp == kMmaWarp) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tcols) : "memory");
     }
@@ -471,31 +604,36 @@ cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
                            uint32_t res_dtype, int res_shift, void* out, uint32_t out_dtype,
                            int64_t n_out, int cout, uint32_t flags, double* gn_partials,
                            int gn_groups, char* error, uint64_t error_capacity, s3d_status* st) {
-    (void)n_in;
     *st = S3D_OK;
     const int cout_pad = (cout + 15) / 16 * 16;
     const int cin_pad = (cin + 63) / 64 * 64;
     const int bn = tc_pick_bn(cout);
     int stages = (int)((200 * 1024) / (kAStage + bn * 128));
     if (stages > 8) stages = 8;
-    if (stages < kLag + 1) stages = kLag + 1;
+    // the epilogue reuses the ring for a 128 x (bn + 4) f32 tile
+    while ((size_t)stages * (kAStage + bn * 128) < (size_t)128 * (bn + 4) * 4) ++stages;
+    (void)n_in;
 
     auto encode = get_encode_fn();
     if (!encode) {
         *st = fail(error, error_capacity, S3D_INTERNAL_ERROR, "cuTensorMapEncodeTiled unavailable");
         return cudaErrorNotSupported;
     }
-    CUtensorMap map;
-    const cuuint64_t dims[2] = {(cuuint64_t)cin_pad, (cuuint64_t)kvol * (cuuint64_t)cout_pad};
-    const cuuint64_t strides[1] = {(cuuint64_t)cin_pad * 2};
-    const cuuint32_t box[2] = {64, (cuuint32_t)bn};
-    const cuuint32_t estr[2] = {1, 1};
-    CUresult cr = encode(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)w, dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (cr != CUDA_SUCCESS) {
-        *st = fail(error, error_capacity, S3D_INTERNAL_ERROR, "cuTensorMapEncodeTiled failed (%d)", (int)cr);
-        return cudaErrorInvalidValue;
+    // weight tile rows per TMA load: NB issuers, slices a multiple of 8 rows
+    const int nb = (bn % 32 == 0) ? 4 : 2;
+    CUtensorMap wmap;
+    {
+        const cuuint64_t dims[2] = {(cuuint64_t)cin_pad, (cuuint64_t)kvol * (cuuint64_t)cout_pad};
+        const cuuint64_t strides[1] = {(cuuint64_t)cin_pad * 2};
+        const cuuint32_t box[2] = {64, (cuuint32_t)(bn / nb)};
+        const cuuint32_t estr[2] = {1, 1};
+        CUresult cr = encode(&wmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)w, dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (cr != CUDA_SUCCESS) {
+            *st = fail(error, error_capacity, S3D_INTERNAL_ERROR, "weight tensor map failed (%d)", (int)cr);
+            return cudaErrorInvalidValue;
+        }
     }
     TcParams p;
     p.in = in;
@@ -506,6 +644,7 @@ cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     p.kvol = kvol;
     p.cout_pad = cout_pad;
     p.bn = bn;
+    p.nb = nb;
     p.stages = stages;
     p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
     p.bias = bias;
@@ -530,8 +669,7 @@ cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
         if (e != cudaSuccess) return e;
     }
     const dim3 grid((unsigned)tiles, (unsigned)(cout_pad / bn));
-    conv_tc_kernel<<<grid, kThreads, smem, ctx->stream>>>(p, map);
-    (void)cin_pad;
+    conv_tc_kernel<<<grid, kThreads, smem, ctx->stream>>>(p, wmap);
     return cudaGetLastError();
 }
 

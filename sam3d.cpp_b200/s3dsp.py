@@ -26,6 +26,7 @@ LAYOUT_SLAT_ROW, LAYOUT_MESH_PACKED, LAYOUT_LINEAR, LAYOUT_SPCONV_1X1, LAYOUT_TR
 SENTINEL_SLAT_N, SENTINEL_MESH_NEG1 = 0, 1
 EPI_SILU, PRO_AFFINE_SILU = 1, 2
 CONTEXT_DEFERRED_CHECKS = 1
+CONTEXT_OWN_STREAM = 2
 
 # every symbol include/s3dsp.h declares (tests check the library exports them)
 EXPORTED = [
@@ -152,7 +153,8 @@ class Hash:
 
 
 class Context:
-    """One device + one CUDA stream (default: torch's current stream)."""
+    """One device + one CUDA stream (default: torch's current stream, so the
+    library's kernels are ordered with torch's copies and events)."""
 
     def __init__(self, device: int = 0, stream: int | None = None, flags: int = 0):
         L = load()
