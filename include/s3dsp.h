@@ -150,6 +150,22 @@ S3DSP_API s3d_status s3dsp_kmap_pairs(s3dsp_context *ctx, const s3dsp_kmap *kmap
                                       int32_t *d_out, int64_t capacity, int64_t *h_offsets,
                                       char *error, uint64_t error_capacity);
 
+/* Allocation-free variant of s3dsp_kmap_pairs, for callers that may not
+ * allocate device memory once they are running: a host whose memory is a
+ * fixed, pre-reserved pool, or code that runs where cudaMalloc is not
+ * allowed. It has no counterpart in the reference (whose tables are built on
+ * the host). Same arguments and results as s3dsp_kmap_pairs; its scratch is a
+ * static device array in the library, so the map may have at most 2^21
+ * (2,097,152) output rows — larger maps fail with S3D_INVALID_ARGUMENT.
+ * The first call on each device looks up that array's device address; make
+ * it before any stream capture. All calls on a device share the array:
+ * calls whose GPU work overlaps (different streams, concurrent contexts)
+ * race and must be ordered by the caller. Synchronous, like s3dsp_kmap_pairs. */
+S3DSP_API s3d_status s3dsp_kmap_pairs_noalloc(s3dsp_context *ctx, const s3dsp_kmap *kmap,
+                                              int32_t *d_in, int32_t *d_out, int64_t capacity,
+                                              int64_t *h_offsets, char *error,
+                                              uint64_t error_capacity);
+
 /* ---------------------------------------------------------------------------
  * Weights. Converts a GGUF-layout weight (host or device `src`, f32/f16/bf16)
  * into the device layout a conv of `precision` consumes, at d_dst (size from

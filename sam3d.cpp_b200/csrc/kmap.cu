@@ -15,6 +15,8 @@
 // offsets have any neighbour (the conv skips empty offsets).
 #include "s3dsp_internal.h"
 
+#include <mutex>
+
 using namespace s3dsp;
 
 namespace {
@@ -266,6 +268,48 @@ __global__ void pair_write_kernel(const int32_t* __restrict__ nbr, int64_t n, co
         pin[pos] = v;
         pout[pos] = (int32_t)r;
     }
+}
+
+// ---------------------------------------------------------------------------
+// Scratch of s3dsp_kmap_pairs_noalloc: a file-scope device array, so the call
+// allocates nothing. Layout: int32 counts[kNoAllocMaxBlocks] (one per offset
+// and 1024-row block) | int64 starts[kNoAllocMaxBlocks + 1] (their exclusive
+// prefix sums) | int64 offsets[32] (the kvol + 1 per-offset starts). Every
+// element a call reads is written earlier in the same call, so nothing needs
+// clearing between calls. Each device that loads the library holds this
+// array (about 0.65 MiB) until the process exits.
+// ---------------------------------------------------------------------------
+constexpr int64_t kNoAllocMaxRows = 1ll << 21;  // 2,097,152 output rows
+constexpr int64_t kNoAllocMaxBlocks = 27 * (kNoAllocMaxRows / kPairBlock);
+constexpr size_t kNoAllocCountsBytes = (size_t)kNoAllocMaxBlocks * 4;
+constexpr size_t kNoAllocStartsBytes = (size_t)(kNoAllocMaxBlocks + 1) * 8;
+constexpr size_t kNoAllocBytes = kNoAllocCountsBytes + kNoAllocStartsBytes + 32 * 8;
+static __device__ __align__(256) unsigned char g_pairs_scratch[kNoAllocBytes];
+
+__global__ void pair_offsets_kernel(const int64_t* __restrict__ starts, int64_t nblk, int kvol, int64_t m,
+                                    int64_t* __restrict__ offs) {
+    const int o = threadIdx.x;
+    if (o < kvol) offs[o] = starts[o * nblk];
+    if (o == kvol) offs[kvol] = starts[m];
+}
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_scratch[64] = {};
+
+// Device address of g_pairs_scratch for `device` (the current device). The
+// host-side name of the array is only a stand-in, so the address comes from
+// cudaGetSymbolAddress, once per device, and is cached.
+cudaError_t noalloc_scratch(int device, unsigned char** out) {
+    if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_scratch[device]) {
+        void* ptr = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&ptr, g_pairs_scratch);
+        if (e != cudaSuccess) return e;
+        g_noalloc_scratch[device] = ptr;
+    }
+    *out = static_cast<unsigned char*>(g_noalloc_scratch[device]);
+    return cudaSuccess;
 }
 
 inline int grid_for(int64_t n, int threads, int sm_count) {
@@ -539,4 +583,42 @@ extern "C" S3DSP_API s3d_status s3dsp_kmap_pairs(s3dsp_context* ctx, const s3dsp
     cudaFreeAsync(counts, ctx->stream);
     cudaFreeAsync(starts, ctx->stream);
     return st;
+}
+
+extern "C" S3DSP_API s3d_status s3dsp_kmap_pairs_noalloc(s3dsp_context* ctx, const s3dsp_kmap* k, int32_t* d_in,
+                                                         int32_t* d_out, int64_t capacity, int64_t* h_offsets,
+                                                         char* error, uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx || !k || !d_in || !d_out || !h_offsets)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
+    if (k->n_out > kNoAllocMaxRows)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT,
+                    "kernel map has %lld output rows; the allocation-free pair build is limited to %lld rows "
+                    "(use s3dsp_kmap_pairs)",
+                    (long long)k->n_out, (long long)kNoAllocMaxRows);
+    S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    unsigned char* scratch = nullptr;
+    S3DSP_CUDA(noalloc_scratch(ctx->device, &scratch), "cudaGetSymbolAddress(no-alloc scratch)");
+    int32_t* counts = reinterpret_cast<int32_t*>(scratch);
+    int64_t* starts = reinterpret_cast<int64_t*>(scratch + kNoAllocCountsBytes);
+    int64_t* offs = reinterpret_cast<int64_t*>(scratch + kNoAllocCountsBytes + kNoAllocStartsBytes);
+    const int64_t nblk = (k->n_out + kPairBlock - 1) / kPairBlock;
+    const int64_t m = nblk * k->kvol;
+    if (nblk > 0)
+        pair_count_kernel<<<dim3((unsigned)nblk, k->kvol), kPairBlock, 0, ctx->stream>>>(k->nbr, k->n_out, counts, nblk);
+    pair_scan_kernel<<<1, 1024, 0, ctx->stream>>>(counts, m, starts);
+    pair_offsets_kernel<<<1, 32, 0, ctx->stream>>>(starts, nblk, k->kvol, m, offs);
+    S3DSP_LAUNCH_CHECK("pair count/scan kernels");
+    S3DSP_CUDA(cudaMemcpyAsync(h_offsets, offs, sizeof(int64_t) * (size_t)(k->kvol + 1), cudaMemcpyDeviceToHost,
+                               ctx->stream),
+               "pair offsets readback");
+    S3DSP_CUDA(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    if (h_offsets[k->kvol] > capacity)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "pair capacity %lld < %lld needed",
+                    (long long)capacity, (long long)h_offsets[k->kvol]);
+    if (nblk > 0)
+        pair_write_kernel<<<dim3((unsigned)nblk, k->kvol), kPairBlock, 0, ctx->stream>>>(k->nbr, k->n_out, starts,
+                                                                                         nblk, d_in, d_out);
+    S3DSP_LAUNCH_CHECK("pair_write_kernel");
+    return S3D_OK;
 }

@@ -33,7 +33,7 @@ EXPORTED = [
     "s3dsp_abi_version", "s3dsp_context_create", "s3dsp_context_free", "s3dsp_context_stream",
     "s3dsp_context_check", "s3dsp_hash_build", "s3dsp_hash_free", "s3dsp_hash_size",
     "s3dsp_hash_lookup", "s3dsp_kmap_build_subm3", "s3dsp_subdivide", "s3dsp_kmap_free",
-    "s3dsp_kmap_rows", "s3dsp_kmap_export_dense", "s3dsp_kmap_pairs",
+    "s3dsp_kmap_rows", "s3dsp_kmap_export_dense", "s3dsp_kmap_pairs", "s3dsp_kmap_pairs_noalloc",
     "s3dsp_weights_packed_bytes", "s3dsp_weights_pack", "s3dsp_gn_partials_count", "s3dsp_conv",
     "s3dsp_gn_stats", "s3dsp_gn_finalize", "s3dsp_channel_affine", "s3dsp_layer_norm",
     "s3dsp_convert",
@@ -81,6 +81,7 @@ def load(path: str = LIB_PATH):
         "s3dsp_kmap_rows": (_i64, [_vp]),
         "s3dsp_kmap_export_dense": (_u32, [_vp, _vp, _u32, _vp, _cp, _u64]),
         "s3dsp_kmap_pairs": (_u32, [_vp, _vp, _vp, _vp, _i64, ctypes.POINTER(_i64), _cp, _u64]),
+        "s3dsp_kmap_pairs_noalloc": (_u32, [_vp, _vp, _vp, _vp, _i64, ctypes.POINTER(_i64), _cp, _u64]),
         "s3dsp_weights_packed_bytes": (_i64, [_u32, _i32, _i64, _i64]),
         "s3dsp_weights_pack": (_u32, [_vp, _vp, _u32, _i32, _u32, _i32, _i64, _i64, _u32, _vp, _cp, _u64]),
         "s3dsp_gn_partials_count": (_i64, [_i64, _i64, _i32]),
@@ -206,6 +207,13 @@ class Context:
     def kmap_pairs(self, kmap: Kmap, pin, pout):
         offs = (ctypes.c_int64 * 28)()
         _call(load().s3dsp_kmap_pairs, self.handle, kmap.handle, ptr(pin), ptr(pout), pin.numel(), offs)
+        return list(offs)
+
+    def kmap_pairs_noalloc(self, kmap: Kmap, pin, pout):
+        """Same as kmap_pairs, but the library allocates no device memory
+        (its scratch is a static device array; maps of at most 2^21 rows)."""
+        offs = (ctypes.c_int64 * 28)()
+        _call(load().s3dsp_kmap_pairs_noalloc, self.handle, kmap.handle, ptr(pin), ptr(pout), pin.numel(), offs)
         return list(offs)
 
     # ---- weights ---------------------------------------------------------
