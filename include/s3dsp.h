@@ -45,6 +45,7 @@ typedef uint32_t s3d_status;
 typedef struct s3dsp_context s3dsp_context;
 typedef struct s3dsp_hash s3dsp_hash;
 typedef struct s3dsp_kmap s3dsp_kmap;
+typedef struct s3dsp_slat_tables s3dsp_slat_tables;
 
 /* element types */
 #define S3DSP_F32 UINT32_C(0)
@@ -241,6 +242,90 @@ S3DSP_API s3d_status s3dsp_layer_norm(s3dsp_context *ctx, const void *x, uint32_
 S3DSP_API s3d_status s3dsp_convert(s3dsp_context *ctx, const void *x, uint32_t x_dtype, void *y,
                                    uint32_t y_dtype, int64_t count, char *error,
                                    uint64_t error_capacity);
+
+/* ---------------------------------------------------------------------------
+ * SLat 2x down/up-sample tables and gathers: the coarse half of
+ * SlatTables::build (sparse_ops.cpp:53-105, conv_coarse :142) and the
+ * downsample / upsample lambdas of slat_flow_graph.cpp:159-190.
+ * Coarse rows are the sorted unique (batch, x/2, y/2, z/2) keys (C++
+ * truncating division); children are the first 8 fine rows of each coarse
+ * cell in fine-row order (sentinel nf); inv_count = 1/(count+1).
+ * ------------------------------------------------------------------------- */
+S3DSP_API s3d_status s3dsp_slat_tables_build(s3dsp_context *ctx, const s3dsp_hash *fine,
+                                             s3dsp_slat_tables **out, char *error,
+                                             uint64_t error_capacity);
+S3DSP_API void s3dsp_slat_tables_free(s3dsp_context *ctx, s3dsp_slat_tables *tables);
+S3DSP_API int64_t s3dsp_slat_tables_coarse_rows(const s3dsp_slat_tables *tables);
+/* The coarse submanifold map (conv_coarse); owned by the tables. */
+S3DSP_API const s3dsp_kmap *s3dsp_slat_tables_coarse_kmap(const s3dsp_slat_tables *tables);
+/* Copies tables to device buffers (any may be NULL): fine_to_coarse [nf],
+ * coarse_children [8*nc], coarse_inv_count [nc] f32, coarse_coords [nc, 4]. */
+S3DSP_API s3d_status s3dsp_slat_tables_export(s3dsp_context *ctx, const s3dsp_slat_tables *tables,
+                                              int32_t *d_fine_to_coarse, int32_t *d_coarse_children,
+                                              float *d_coarse_inv_count, int32_t *d_coarse_coords,
+                                              char *error, uint64_t error_capacity);
+/* y[nc, c] = mean-pool of x[nf, c] (sum of the 8 child slots * inv_count). */
+S3DSP_API s3d_status s3dsp_slat_downsample(s3dsp_context *ctx, const s3dsp_slat_tables *tables,
+                                           const void *x, uint32_t x_dtype, int64_t c, void *y,
+                                           uint32_t y_dtype, char *error, uint64_t error_capacity);
+/* y[nf, c] = x[fine_to_coarse[i]] (nearest upsample). */
+S3DSP_API s3d_status s3dsp_slat_upsample(s3dsp_context *ctx, const s3dsp_slat_tables *tables,
+                                         const void *x, uint32_t x_dtype, int64_t c, void *y,
+                                         uint32_t y_dtype, char *error, uint64_t error_capacity);
+
+/* ---------------------------------------------------------------------------
+ * Block drivers (host C++ composing the kernels; scratch from the device's
+ * stream-ordered pool). Weights are packed for `precision` by
+ * s3dsp_weights_pack. Inputs/outputs f32 [rows, channels] on the device.
+ * ------------------------------------------------------------------------- */
+/* conv3 -> GroupNorm(groups, eps, gamma, beta) -> SiLU -> conv3 -> + x
+ * (GroupNorm semantics of mesh_decoder_graph.cpp:16-30). */
+S3DSP_API s3d_status s3dsp_res_block_gn(s3dsp_context *ctx, const s3dsp_kmap *kmap,
+                                        uint32_t precision, const float *x, int64_t n, int64_t c,
+                                        const void *w1, const float *b1, const float *gamma,
+                                        const float *beta, const void *w2, const float *b2,
+                                        int32_t groups, float eps, float *out, char *error,
+                                        uint64_t error_capacity);
+/* One MeshUpsampleGraph level (mesh_decoder_graph.cpp:42-132): subdivide the
+ * parents (hash built with reject_duplicates), GN(32)+SiLU, 27-offset conv
+ * over the children reading parent rows, GN(32)+SiLU, 27-offset conv,
+ * + 1x1 skip of the parents broadcast to their children. Writes the 8*np
+ * child coords and out [8*np, cout]. conv weights MESH_PACKED (27), skip
+ * weight 1x1 (LINEAR or SPCONV_1X1), all packed for `precision`. */
+S3DSP_API s3d_status s3dsp_mesh_upsample_level(
+    s3dsp_context *ctx, const s3dsp_hash *parents, uint32_t precision, const float *x, int64_t cin,
+    int64_t cout, const float *gn1_w, const float *gn1_b, const void *conv1_w,
+    const float *conv1_b, const float *gn2_w, const float *gn2_b, const void *conv2_w,
+    const float *conv2_b, const void *skip_w, const float *skip_b, int32_t *child_coords,
+    float *out, char *error, uint64_t error_capacity);
+/* The SLat res_block (slat_flow_graph.cpp:216-275): LayerNorm(1e-6, affine)
+ * -> SiLU -> conv1 -> LayerNorm(1e-6) -> h*(1+mod_scale)+mod_shift -> SiLU ->
+ * conv2 -> + skip (identity, or the Linear skip_w/skip_b when cin != cout).
+ * mod_scale/mod_shift [cout] come from the caller's timestep embedding. */
+S3DSP_API s3d_status s3dsp_slat_res_block(s3dsp_context *ctx, const s3dsp_kmap *kmap,
+                                          uint32_t precision, const float *x, int64_t n,
+                                          int64_t cin, int64_t cout, const float *norm1_w,
+                                          const float *norm1_b, const void *conv1_w,
+                                          const float *conv1_b, const float *mod_scale,
+                                          const float *mod_shift, const void *conv2_w,
+                                          const float *conv2_b, const void *skip_w,
+                                          const float *skip_b, float *out, char *error,
+                                          uint64_t error_capacity);
+/* Host-buffer forms (what decode_object_mesh does per level with its Backend,
+ * session.cpp:927-962): upload coords + features, build the tables, run the
+ * block, read the result back. Synchronous. */
+S3DSP_API s3d_status s3dsp_res_block_gn_host(s3dsp_context *ctx, uint32_t precision,
+                                             const int32_t *h_coords, int64_t n, const float *h_x,
+                                             int64_t c, const void *w1, const float *b1,
+                                             const float *gamma, const float *beta, const void *w2,
+                                             const float *b2, int32_t groups, float eps,
+                                             float *h_out, char *error, uint64_t error_capacity);
+S3DSP_API s3d_status s3dsp_mesh_upsample_level_host(
+    s3dsp_context *ctx, uint32_t precision, const int32_t *h_parent_coords, int64_t np,
+    const float *h_x, int64_t cin, int64_t cout, const float *gn1_w, const float *gn1_b,
+    const void *conv1_w, const float *conv1_b, const float *gn2_w, const float *gn2_b,
+    const void *conv2_w, const float *conv2_b, const void *skip_w, const float *skip_b,
+    int32_t *h_child_coords, float *h_out, char *error, uint64_t error_capacity);
 
 #ifdef __cplusplus
 }

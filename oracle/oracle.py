@@ -274,3 +274,16 @@ def mesh_upsample_level(x, neighbors, p, threads=0, taps=None):
     if taps is not None:
         taps["skip"] = skip
     return h + skip
+
+
+def slat_res_block(x, nbr_slat, norm1_w, norm1_b, w1, b1, mod_scale, mod_shift, w2, b2, skip_w=None, skip_b=None,
+                   threads=0):
+    """res_block of slat_flow_graph.cpp:216-275 (no down/up): LayerNorm(1e-6,
+    affine) -> SiLU -> conv1 -> LayerNorm(1e-6) -> modulate -> SiLU -> conv2
+    -> + skip (identity, or Linear when the width changes, :266-272)."""
+    h = layer_norm(x, 1e-6, norm1_w, norm1_b, silu=True)
+    h = subm_conv_slat(h, nbr_slat, w1, b1, threads=threads)
+    h = layer_norm(h, 1e-6, None, None, mod_scale, mod_shift, silu=True)
+    h = subm_conv_slat(h, nbr_slat, w2, b2, threads=threads)
+    skip = x if skip_w is None else linear(x, skip_w, skip_b, threads=threads)
+    return h + skip

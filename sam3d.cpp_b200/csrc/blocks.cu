@@ -1,0 +1,274 @@
+// Block-level host drivers: the host C++ that replaces the reference's GGML
+// graph for one sparse block, composed from the library's kernels.
+//   s3dsp_res_block_gn        conv3 -> GroupNorm -> SiLU -> conv3 -> + x
+//                             (the BASELINE config-2 block; GroupNorm as in
+//                             mesh_decoder_graph.cpp:16-30)
+//   s3dsp_mesh_upsample_level MeshUpsampleGraph::build, mesh_decoder_graph.cpp:42-132
+//   s3dsp_slat_res_block      res_block of slat_flow_graph.cpp:216-275
+// Scratch comes from the device's stream-ordered pool on the context stream.
+#include "s3dsp_internal.h"
+
+using namespace s3dsp;
+
+namespace {
+
+// RAII list of stream-ordered scratch allocations
+struct Scratch {
+    cudaStream_t st;
+    void* ptrs[16] = {};
+    int n = 0;
+    explicit Scratch(cudaStream_t s) : st(s) {}
+    ~Scratch() {
+        for (int i = 0; i < n; ++i)
+            if (ptrs[i]) cudaFreeAsync(ptrs[i], st);
+    }
+    template <class T>
+    cudaError_t get(T** p, size_t bytes) {
+        void* q = nullptr;
+        const cudaError_t e = cudaMallocAsync(&q, bytes > 0 ? bytes : 16, st);
+        if (e != cudaSuccess) return e;
+        ptrs[n++] = q;
+        *p = static_cast<T*>(q);
+        return cudaSuccess;
+    }
+};
+
+#define S3DSP_TRY(call)                  \
+    do {                                 \
+        const s3d_status s_ = (call);    \
+        if (s_ != S3D_OK) return s_;     \
+    } while (0)
+
+}  // namespace
+
+extern "C" S3DSP_API s3d_status s3dsp_res_block_gn(s3dsp_context* ctx, const s3dsp_kmap* kmap, uint32_t precision,
+                                                   const float* x, int64_t n, int64_t c, const void* w1,
+                                                   const float* b1, const float* gamma, const float* beta,
+                                                   const void* w2, const float* b2, int32_t groups, float eps,
+                                                   float* out, char* error, uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx || !kmap || !x || !w1 || !w2 || !out) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
+    if (n != kmap->n_out) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "n != kmap rows");
+    S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    Scratch sc(ctx->stream);
+    double* part;
+    float *sub, *mul, *add, *y1;
+    S3DSP_CUDA(sc.get(&part, sizeof(double) * (size_t)s3dsp_gn_partials_count(n, c, groups)), "scratch");
+    S3DSP_CUDA(sc.get(&sub, 4 * (size_t)c), "scratch");
+    S3DSP_CUDA(sc.get(&mul, 4 * (size_t)c), "scratch");
+    S3DSP_CUDA(sc.get(&add, 4 * (size_t)c), "scratch");
+    S3DSP_CUDA(sc.get(&y1, 4 * (size_t)(n * c)), "scratch");
+    if (precision == S3DSP_PREC_F32_STRICT) {
+        S3DSP_TRY(s3dsp_conv(ctx, kmap, 27, precision, x, S3DSP_F32, n, c, 0, w1, b1, nullptr, 0, 0, y1, S3DSP_F32, n, c,
+                             0, nullptr, nullptr, nullptr, part, groups, error, error_capacity));
+        S3DSP_TRY(s3dsp_gn_finalize(ctx, part, n, c, groups, eps, gamma, beta, sub, mul, add, error, error_capacity));
+        return s3dsp_conv(ctx, kmap, 27, precision, y1, S3DSP_F32, n, c, 0, w2, b2, x, S3DSP_F32, 0, out, S3DSP_F32, n,
+                          c, S3DSP_PRO_AFFINE_SILU, sub, mul, add, nullptr, 0, error, error_capacity);
+    }
+    __nv_bfloat16 *xb, *hb;
+    S3DSP_CUDA(sc.get(&xb, 2 * (size_t)(n * c)), "scratch");
+    S3DSP_CUDA(sc.get(&hb, 2 * (size_t)(n * c)), "scratch");
+    S3DSP_TRY(s3dsp_convert(ctx, x, S3DSP_F32, xb, S3DSP_BF16, n * c, error, error_capacity));
+    S3DSP_TRY(s3dsp_conv(ctx, kmap, 27, precision, xb, S3DSP_BF16, n, c, 0, w1, b1, nullptr, 0, 0, y1, S3DSP_F32, n, c,
+                         0, nullptr, nullptr, nullptr, part, groups, error, error_capacity));
+    S3DSP_TRY(s3dsp_gn_finalize(ctx, part, n, c, groups, eps, gamma, beta, sub, mul, add, error, error_capacity));
+    S3DSP_TRY(s3dsp_channel_affine(ctx, y1, S3DSP_F32, n, c, sub, mul, add, 1, hb, S3DSP_BF16, error, error_capacity));
+    return s3dsp_conv(ctx, kmap, 27, precision, hb, S3DSP_BF16, n, c, 0, w2, b2, x, S3DSP_F32, 0, out, S3DSP_F32, n, c,
+                      0, nullptr, nullptr, nullptr, nullptr, 0, error, error_capacity);
+}
+
+extern "C" S3DSP_API s3d_status s3dsp_mesh_upsample_level(
+    s3dsp_context* ctx, const s3dsp_hash* parents, uint32_t precision, const float* x, int64_t cin, int64_t cout,
+    const float* gn1_w, const float* gn1_b, const void* conv1_w, const float* conv1_b, const float* gn2_w,
+    const float* gn2_b, const void* conv2_w, const float* conv2_b, const void* skip_w, const float* skip_b,
+    int32_t* child_coords, float* out, char* error, uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx || !parents || !x || !conv1_w || !conv2_w || !skip_w || !child_coords || !out)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
+    S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    const int64_t np = parents->n, nc = 8 * np;
+    const int groups = 32;
+    const float eps = 1e-5f;  // SparseGroupNorm32 (mesh_decoder_graph.cpp:23)
+    s3dsp_kmap* kmap = nullptr;
+    S3DSP_TRY(s3dsp_subdivide(ctx, parents, child_coords, &kmap, error, error_capacity));
+    struct KmapGuard {
+        s3dsp_context* c;
+        s3dsp_kmap* k;
+        ~KmapGuard() { s3dsp_kmap_free(c, k); }
+    } guard{ctx, kmap};
+    Scratch sc(ctx->stream);
+    const int64_t gmax = np > nc ? np : nc;
+    double* part;
+    float *sub1, *mul1, *add1, *sub2, *mul2, *add2, *y1, *skip;
+    S3DSP_CUDA(sc.get(&part, sizeof(double) * (size_t)s3dsp_gn_partials_count(gmax, 1, groups)), "scratch");
+    S3DSP_CUDA(sc.get(&sub1, 4 * (size_t)cin), "scratch");
+    S3DSP_CUDA(sc.get(&mul1, 4 * (size_t)cin), "scratch");
+    S3DSP_CUDA(sc.get(&add1, 4 * (size_t)cin), "scratch");
+    S3DSP_CUDA(sc.get(&sub2, 4 * (size_t)cout), "scratch");
+    S3DSP_CUDA(sc.get(&mul2, 4 * (size_t)cout), "scratch");
+    S3DSP_CUDA(sc.get(&add2, 4 * (size_t)cout), "scratch");
+    S3DSP_CUDA(sc.get(&y1, 4 * (size_t)(nc * cout)), "scratch");
+    S3DSP_CUDA(sc.get(&skip, 4 * (size_t)(np * cout)), "scratch");
+    // norm1 + silu1 on the parents (subdivide copies them to the 8 children)
+    S3DSP_TRY(s3dsp_gn_stats(ctx, x, S3DSP_F32, np, cin, groups, part, error, error_capacity));
+    S3DSP_TRY(s3dsp_gn_finalize(ctx, part, np, cin, groups, eps, gn1_w, gn1_b, sub1, mul1, add1, error, error_capacity));
+    if (precision == S3DSP_PREC_F32_STRICT) {
+        // conv1 over the children, gathering parent rows, GN1+SiLU in its prologue
+        S3DSP_TRY(s3dsp_conv(ctx, kmap, 27, precision, x, S3DSP_F32, np, cin, 3, conv1_w, conv1_b, nullptr, 0, 0, y1,
+                             S3DSP_F32, nc, cout, S3DSP_PRO_AFFINE_SILU, sub1, mul1, add1, part, groups, error,
+                             error_capacity));
+        S3DSP_TRY(s3dsp_gn_finalize(ctx, part, nc, cout, groups, eps, gn2_w, gn2_b, sub2, mul2, add2, error, error_capacity));
+        // skip: 1x1 conv on the parents (== on the repeated input), broadcast to children
+        S3DSP_TRY(s3dsp_conv(ctx, nullptr, 1, precision, x, S3DSP_F32, np, cin, 0, skip_w, skip_b, nullptr, 0, 0, skip,
+                             S3DSP_F32, np, cout, 0, nullptr, nullptr, nullptr, nullptr, 0, error, error_capacity));
+        return s3dsp_conv(ctx, kmap, 27, precision, y1, S3DSP_F32, nc, cout, 0, conv2_w, conv2_b, skip, S3DSP_F32, 3,
+                          out, S3DSP_F32, nc, cout, S3DSP_PRO_AFFINE_SILU, sub2, mul2, add2, nullptr, 0, error,
+                          error_capacity);
+    }
+    __nv_bfloat16 *h1, *h2, *xb;
+    S3DSP_CUDA(sc.get(&h1, 2 * (size_t)(np * cin)), "scratch");
+    S3DSP_CUDA(sc.get(&xb, 2 * (size_t)(np * cin)), "scratch");
+    S3DSP_CUDA(sc.get(&h2, 2 * (size_t)(nc * cout)), "scratch");
+    S3DSP_TRY(s3dsp_channel_affine(ctx, x, S3DSP_F32, np, cin, sub1, mul1, add1, 1, h1, S3DSP_BF16, error, error_capacity));
+    S3DSP_TRY(s3dsp_conv(ctx, kmap, 27, precision, h1, S3DSP_BF16, np, cin, 3, conv1_w, conv1_b, nullptr, 0, 0, y1,
+                         S3DSP_F32, nc, cout, 0, nullptr, nullptr, nullptr, part, groups, error, error_capacity));
+    S3DSP_TRY(s3dsp_gn_finalize(ctx, part, nc, cout, groups, eps, gn2_w, gn2_b, sub2, mul2, add2, error, error_capacity));
+    S3DSP_TRY(s3dsp_channel_affine(ctx, y1, S3DSP_F32, nc, cout, sub2, mul2, add2, 1, h2, S3DSP_BF16, error, error_capacity));
+    S3DSP_TRY(s3dsp_convert(ctx, x, S3DSP_F32, xb, S3DSP_BF16, np * cin, error, error_capacity));
+    S3DSP_TRY(s3dsp_conv(ctx, nullptr, 1, precision, xb, S3DSP_BF16, np, cin, 0, skip_w, skip_b, nullptr, 0, 0, skip,
+                         S3DSP_F32, np, cout, 0, nullptr, nullptr, nullptr, nullptr, 0, error, error_capacity));
+    return s3dsp_conv(ctx, kmap, 27, precision, h2, S3DSP_BF16, nc, cout, 0, conv2_w, conv2_b, skip, S3DSP_F32, 3, out,
+                      S3DSP_F32, nc, cout, 0, nullptr, nullptr, nullptr, nullptr, 0, error, error_capacity);
+}
+
+extern "C" S3DSP_API s3d_status s3dsp_slat_res_block(s3dsp_context* ctx, const s3dsp_kmap* kmap, uint32_t precision,
+                                                     const float* x, int64_t n, int64_t cin, int64_t cout,
+                                                     const float* norm1_w, const float* norm1_b, const void* conv1_w,
+                                                     const float* conv1_b, const float* mod_scale,
+                                                     const float* mod_shift, const void* conv2_w, const float* conv2_b,
+                                                     const void* skip_w, const float* skip_b, float* out, char* error,
+                                                     uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx || !kmap || !x || !conv1_w || !conv2_w || !out)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
+    if (n != kmap->n_out) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "n != kmap rows");
+    if (cin != cout && !skip_w)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "cin != cout needs a skip Linear (slat_flow_graph.cpp:266-272)");
+    S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    const float eps = 1e-6f;  // gb_layer_norm in res_block (slat_flow_graph.cpp:245-255)
+    const bool bf = precision == S3DSP_PREC_BF16;
+    const uint32_t hdt = bf ? S3DSP_BF16 : S3DSP_F32;
+    const size_t hsz = bf ? 2 : 4;
+    Scratch sc(ctx->stream);
+    void *h1, *h2;
+    float *y1, *skip = nullptr;
+    S3DSP_CUDA(sc.get(&h1, hsz * (size_t)(n * cin)), "scratch");
+    S3DSP_CUDA(sc.get(&h2, hsz * (size_t)(n * cout)), "scratch");
+    S3DSP_CUDA(sc.get(&y1, 4 * (size_t)(n * cout)), "scratch");
+    // norm1 (affine) -> SiLU -> conv1
+    S3DSP_TRY(s3dsp_layer_norm(ctx, x, S3DSP_F32, n, cin, eps, norm1_w, norm1_b, nullptr, nullptr, 1, h1, hdt, error,
+                               error_capacity));
+    S3DSP_TRY(s3dsp_conv(ctx, kmap, 27, precision, h1, hdt, n, cin, 0, conv1_w, conv1_b, nullptr, 0, 0, y1, S3DSP_F32,
+                         n, cout, 0, nullptr, nullptr, nullptr, nullptr, 0, error, error_capacity));
+    // norm2 (no affine) -> modulate -> SiLU
+    S3DSP_TRY(s3dsp_layer_norm(ctx, y1, S3DSP_F32, n, cout, eps, nullptr, nullptr, mod_scale, mod_shift, 1, h2, hdt,
+                               error, error_capacity));
+    // skip: identity, or Linear when the width changes
+    const float* res = x;
+    if (cin != cout) {
+        S3DSP_CUDA(sc.get(&skip, 4 * (size_t)(n * cout)), "scratch");
+        const void* xin = x;
+        if (bf) {
+            __nv_bfloat16* xb;
+            S3DSP_CUDA(sc.get(&xb, 2 * (size_t)(n * cin)), "scratch");
+            S3DSP_TRY(s3dsp_convert(ctx, x, S3DSP_F32, xb, S3DSP_BF16, n * cin, error, error_capacity));
+            xin = xb;
+        }
+        S3DSP_TRY(s3dsp_conv(ctx, nullptr, 1, precision, xin, hdt, n, cin, 0, skip_w, skip_b, nullptr, 0, 0, skip,
+                             S3DSP_F32, n, cout, 0, nullptr, nullptr, nullptr, nullptr, 0, error, error_capacity));
+        res = skip;
+    }
+    return s3dsp_conv(ctx, kmap, 27, precision, h2, hdt, n, cout, 0, conv2_w, conv2_b, res, S3DSP_F32, 0, out, S3DSP_F32,
+                      n, cout, 0, nullptr, nullptr, nullptr, nullptr, 0, error, error_capacity);
+}
+
+// ---------------------------------------------------------------------------
+// Host-buffer entry points: what the reference's per-level code does with its
+// Backend (upload coords + features, run, read back: session.cpp:927-962), as
+// one call. Weights stay device-resident (packed once at model load).
+// ---------------------------------------------------------------------------
+extern "C" S3DSP_API s3d_status s3dsp_res_block_gn_host(s3dsp_context* ctx, uint32_t precision,
+                                                        const int32_t* h_coords, int64_t n, const float* h_x, int64_t c,
+                                                        const void* w1, const float* b1, const float* gamma,
+                                                        const float* beta, const void* w2, const float* b2,
+                                                        int32_t groups, float eps, float* h_out, char* error,
+                                                        uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx || !h_coords || !h_x || !h_out || n <= 0 || c <= 0)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "bad argument");
+    S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    Scratch sc(ctx->stream);
+    int32_t* d_coords;
+    float *d_x, *d_out;
+    S3DSP_CUDA(sc.get(&d_coords, 16 * (size_t)n), "scratch");
+    S3DSP_CUDA(sc.get(&d_x, 4 * (size_t)(n * c)), "scratch");
+    S3DSP_CUDA(sc.get(&d_out, 4 * (size_t)(n * c)), "scratch");
+    S3DSP_CUDA(cudaMemcpyAsync(d_coords, h_coords, 16 * (size_t)n, cudaMemcpyHostToDevice, ctx->stream), "H2D coords");
+    S3DSP_CUDA(cudaMemcpyAsync(d_x, h_x, 4 * (size_t)(n * c), cudaMemcpyHostToDevice, ctx->stream), "H2D features");
+    s3dsp_hash* h = nullptr;
+    S3DSP_TRY(s3dsp_hash_build(ctx, d_coords, n, 0, &h, error, error_capacity));
+    s3dsp_kmap* k = nullptr;
+    s3d_status s = s3dsp_kmap_build_subm3(ctx, h, &k, error, error_capacity);
+    if (s == S3D_OK)
+        s = s3dsp_res_block_gn(ctx, k, precision, d_x, n, c, w1, b1, gamma, beta, w2, b2, groups, eps, d_out, error,
+                               error_capacity);
+    if (s == S3D_OK) {
+        const cudaError_t e = cudaMemcpyAsync(h_out, d_out, 4 * (size_t)(n * c), cudaMemcpyDeviceToHost, ctx->stream);
+        if (e != cudaSuccess) s = cuda_fail(error, error_capacity, e, "D2H output");
+    }
+    s3dsp_kmap_free(ctx, k);
+    s3dsp_hash_free(ctx, h);
+    if (s == S3D_OK) {
+        const cudaError_t e = cudaStreamSynchronize(ctx->stream);
+        if (e != cudaSuccess) s = cuda_fail(error, error_capacity, e, "cudaStreamSynchronize");
+    }
+    if (s == S3D_OK && (ctx->flags & S3DSP_CONTEXT_DEFERRED_CHECKS)) s = check_status(ctx, error, error_capacity);
+    return s;
+}
+
+extern "C" S3DSP_API s3d_status s3dsp_mesh_upsample_level_host(
+    s3dsp_context* ctx, uint32_t precision, const int32_t* h_parent_coords, int64_t np, const float* h_x, int64_t cin,
+    int64_t cout, const float* gn1_w, const float* gn1_b, const void* conv1_w, const float* conv1_b,
+    const float* gn2_w, const float* gn2_b, const void* conv2_w, const float* conv2_b, const void* skip_w,
+    const float* skip_b, int32_t* h_child_coords, float* h_out, char* error, uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx || !h_parent_coords || !h_x || !h_child_coords || !h_out || np <= 0)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "bad argument");
+    if (np > INT32_MAX / 8) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "parent count exceeds INT32_MAX/8");
+    S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    const int64_t nc = 8 * np;
+    Scratch sc(ctx->stream);
+    int32_t *d_pc, *d_cc;
+    float *d_x, *d_out;
+    S3DSP_CUDA(sc.get(&d_pc, 16 * (size_t)np), "scratch");
+    S3DSP_CUDA(sc.get(&d_cc, 16 * (size_t)nc), "scratch");
+    S3DSP_CUDA(sc.get(&d_x, 4 * (size_t)(np * cin)), "scratch");
+    S3DSP_CUDA(sc.get(&d_out, 4 * (size_t)(nc * cout)), "scratch");
+    S3DSP_CUDA(cudaMemcpyAsync(d_pc, h_parent_coords, 16 * (size_t)np, cudaMemcpyHostToDevice, ctx->stream), "H2D coords");
+    S3DSP_CUDA(cudaMemcpyAsync(d_x, h_x, 4 * (size_t)(np * cin), cudaMemcpyHostToDevice, ctx->stream), "H2D features");
+    s3dsp_hash* h = nullptr;
+    S3DSP_TRY(s3dsp_hash_build(ctx, d_pc, np, 1, &h, error, error_capacity));
+    s3d_status s = s3dsp_mesh_upsample_level(ctx, h, precision, d_x, cin, cout, gn1_w, gn1_b, conv1_w, conv1_b, gn2_w,
+                                             gn2_b, conv2_w, conv2_b, skip_w, skip_b, d_cc, d_out, error,
+                                             error_capacity);
+    if (s == S3D_OK) {
+        cudaError_t e = cudaMemcpyAsync(h_child_coords, d_cc, 16 * (size_t)nc, cudaMemcpyDeviceToHost, ctx->stream);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(h_out, d_out, 4 * (size_t)(nc * cout), cudaMemcpyDeviceToHost, ctx->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+        if (e != cudaSuccess) s = cuda_fail(error, error_capacity, e, "readback");
+    }
+    s3dsp_hash_free(ctx, h);
+    if (s == S3D_OK && (ctx->flags & S3DSP_CONTEXT_DEFERRED_CHECKS)) s = check_status(ctx, error, error_capacity);
+    return s;
+}

@@ -36,7 +36,10 @@ EXPORTED = [
     "s3dsp_kmap_rows", "s3dsp_kmap_export_dense", "s3dsp_kmap_pairs", "s3dsp_kmap_pairs_noalloc",
     "s3dsp_weights_packed_bytes", "s3dsp_weights_pack", "s3dsp_gn_partials_count", "s3dsp_conv",
     "s3dsp_gn_stats", "s3dsp_gn_finalize", "s3dsp_channel_affine", "s3dsp_layer_norm",
-    "s3dsp_convert",
+    "s3dsp_convert", "s3dsp_slat_tables_build", "s3dsp_slat_tables_free", "s3dsp_slat_tables_coarse_rows",
+    "s3dsp_slat_tables_coarse_kmap", "s3dsp_slat_tables_export", "s3dsp_slat_downsample", "s3dsp_slat_upsample",
+    "s3dsp_res_block_gn", "s3dsp_mesh_upsample_level", "s3dsp_slat_res_block", "s3dsp_res_block_gn_host",
+    "s3dsp_mesh_upsample_level_host",
 ]
 
 
@@ -93,6 +96,20 @@ def load(path: str = LIB_PATH):
         "s3dsp_layer_norm": (_u32, [_vp, _vp, _u32, _i64, _i64, _f, _vp, _vp, _vp, _vp, _i32, _vp, _u32, _cp,
                                     _u64]),
         "s3dsp_convert": (_u32, [_vp, _vp, _u32, _vp, _u32, _i64, _cp, _u64]),
+        "s3dsp_slat_tables_build": (_u32, [_vp, _vp, ctypes.POINTER(_vp), _cp, _u64]),
+        "s3dsp_slat_tables_free": (None, [_vp, _vp]),
+        "s3dsp_slat_tables_coarse_rows": (_i64, [_vp]),
+        "s3dsp_slat_tables_coarse_kmap": (_vp, [_vp]),
+        "s3dsp_slat_tables_export": (_u32, [_vp, _vp, _vp, _vp, _vp, _vp, _cp, _u64]),
+        "s3dsp_slat_downsample": (_u32, [_vp, _vp, _vp, _u32, _i64, _vp, _u32, _cp, _u64]),
+        "s3dsp_slat_upsample": (_u32, [_vp, _vp, _vp, _u32, _i64, _vp, _u32, _cp, _u64]),
+        "s3dsp_res_block_gn": (_u32, [_vp, _vp, _u32, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _f, _vp,
+                                      _cp, _u64]),
+        "s3dsp_mesh_upsample_level": (_u32, [_vp, _vp, _u32, _vp, _i64, _i64] + [_vp] * 12 + [_cp, _u64]),
+        "s3dsp_slat_res_block": (_u32, [_vp, _vp, _u32, _vp, _i64, _i64, _i64] + [_vp] * 11 + [_cp, _u64]),
+        "s3dsp_res_block_gn_host": (_u32, [_vp, _u32, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _f,
+                                           _vp, _cp, _u64]),
+        "s3dsp_mesh_upsample_level_host": (_u32, [_vp, _u32, _vp, _i64, _vp, _i64, _i64] + [_vp] * 12 + [_cp, _u64]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -144,6 +161,26 @@ class Hash:
     def free(self):
         if self.handle:
             load().s3dsp_hash_free(self.ctx.handle, self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class SlatTables:
+    def __init__(self, ctx: "Context", handle: int, nf: int):
+        self.ctx, self.handle, self.nf = ctx, handle, nf
+        self.nc = load().s3dsp_slat_tables_coarse_rows(handle)
+        self.coarse_kmap = Kmap(ctx, None, self.nc)
+        self.coarse_kmap.handle = load().s3dsp_slat_tables_coarse_kmap(handle)
+        self.coarse_kmap.free = lambda: None  # owned by the tables
+
+    def free(self):
+        if self.handle:
+            load().s3dsp_slat_tables_free(self.ctx.handle, self.handle)
             self.handle = None
 
     def __del__(self):
@@ -261,3 +298,50 @@ class Context:
 
     def convert(self, x, y):
         _call(load().s3dsp_convert, self.handle, ptr(x), dtype_code(x), ptr(y), dtype_code(y), x.numel())
+
+    # ---- SLat coarse tables / down / up ----------------------------------
+    def slat_tables(self, fine: Hash) -> SlatTables:
+        t = _vp()
+        _call(load().s3dsp_slat_tables_build, self.handle, fine.handle, ctypes.byref(t))
+        return SlatTables(self, t.value, fine.n)
+
+    def slat_tables_export(self, t: SlatTables, f2c=None, children=None, inv=None, coarse_coords=None):
+        _call(load().s3dsp_slat_tables_export, self.handle, t.handle, ptr(f2c), ptr(children), ptr(inv),
+              ptr(coarse_coords))
+
+    def slat_downsample(self, t: SlatTables, x, y):
+        _call(load().s3dsp_slat_downsample, self.handle, t.handle, ptr(x), dtype_code(x), x.shape[1], ptr(y),
+              dtype_code(y))
+
+    def slat_upsample(self, t: SlatTables, x, y):
+        _call(load().s3dsp_slat_upsample, self.handle, t.handle, ptr(x), dtype_code(x), x.shape[1], ptr(y),
+              dtype_code(y))
+
+    # ---- block drivers ---------------------------------------------------
+    def res_block_gn(self, kmap: Kmap, precision: int, x, w1, b1, gamma, beta, w2, b2, out, groups=32, eps=1e-5):
+        _call(load().s3dsp_res_block_gn, self.handle, kmap.handle, precision, ptr(x), x.shape[0], x.shape[1],
+              ptr(w1), ptr(b1), ptr(gamma), ptr(beta), ptr(w2), ptr(b2), groups, eps, ptr(out))
+
+    def res_block_gn_host(self, precision: int, coords_h, x_h, w1, b1, gamma, beta, w2, b2, out_h, groups=32,
+                          eps=1e-5):
+        _call(load().s3dsp_res_block_gn_host, self.handle, precision, ptr(coords_h), coords_h.shape[0], ptr(x_h),
+              x_h.shape[1], ptr(w1), ptr(b1), ptr(gamma), ptr(beta), ptr(w2), ptr(b2), groups, eps, ptr(out_h))
+
+    def mesh_upsample_level(self, parents: Hash, precision: int, x, cout, gn1_w, gn1_b, conv1_w, conv1_b, gn2_w,
+                            gn2_b, conv2_w, conv2_b, skip_w, skip_b, child_coords, out):
+        _call(load().s3dsp_mesh_upsample_level, self.handle, parents.handle, precision, ptr(x), x.shape[1], cout,
+              ptr(gn1_w), ptr(gn1_b), ptr(conv1_w), ptr(conv1_b), ptr(gn2_w), ptr(gn2_b), ptr(conv2_w),
+              ptr(conv2_b), ptr(skip_w), ptr(skip_b), ptr(child_coords), ptr(out))
+
+    def mesh_upsample_level_host(self, precision: int, parent_coords_h, x_h, cout, gn1_w, gn1_b, conv1_w, conv1_b,
+                                 gn2_w, gn2_b, conv2_w, conv2_b, skip_w, skip_b, child_coords_h, out_h):
+        _call(load().s3dsp_mesh_upsample_level_host, self.handle, precision, ptr(parent_coords_h),
+              parent_coords_h.shape[0], ptr(x_h), x_h.shape[1], cout, ptr(gn1_w), ptr(gn1_b), ptr(conv1_w),
+              ptr(conv1_b), ptr(gn2_w), ptr(gn2_b), ptr(conv2_w), ptr(conv2_b), ptr(skip_w), ptr(skip_b),
+              ptr(child_coords_h), ptr(out_h))
+
+    def slat_res_block(self, kmap: Kmap, precision: int, x, cout, norm1_w, norm1_b, conv1_w, conv1_b, mod_scale,
+                       mod_shift, conv2_w, conv2_b, skip_w, skip_b, out):
+        _call(load().s3dsp_slat_res_block, self.handle, kmap.handle, precision, ptr(x), x.shape[0], x.shape[1], cout,
+              ptr(norm1_w), ptr(norm1_b), ptr(conv1_w), ptr(conv1_b), ptr(mod_scale), ptr(mod_shift), ptr(conv2_w),
+              ptr(conv2_b), ptr(skip_w), ptr(skip_b), ptr(out))
