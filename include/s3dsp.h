@@ -72,6 +72,8 @@ typedef struct s3dsp_slat_tables s3dsp_slat_tables;
 /* conv epilogue / prologue flags */
 #define S3DSP_EPI_SILU UINT32_C(1)      /* apply SiLU after bias (and residual) */
 #define S3DSP_PRO_AFFINE_SILU UINT32_C(2) /* gathered x -> silu((x - sub[c]) * mul[c] + add[c]) */
+#define S3DSP_CONV_CTA_PAIR UINT32_C(4)  /* BF16: tcgen05 CTA pairs (256-row MMA over two tiles) instead of
+                                          one CTA per 128-row tile; same results, slower on B200 today */
 
 /* context flags */
 #define S3DSP_CONTEXT_DEFERRED_CHECKS UINT32_C(1) /* device-detected input errors are reported by

@@ -72,6 +72,7 @@ struct TcParams {
     void* out;
     uint32_t out_dtype;
     int64_t n_out;
+    int64_t n_tiles;            // 128-row tiles of the output
     int cout;
     uint32_t flags;
     double* gn_partials;
@@ -139,6 +140,74 @@ __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint3
 __device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
 }
+// --- CTA-pair (cluster of 2) helpers ---
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// shared::cluster address of the same smem variable in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
+    uint32_t out;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(addr), "r"(rank));
+    return out;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_cluster(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// TMA tile load into this CTA's smem whose completion is counted on `bar`,
+// which may be the pair leader's barrier (shared::cluster address)
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"((unsigned long long)map), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void mma_bf16_pair(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+// arrive on `bar` (shared::cluster address, this CTA's or the peer's) when
+// all prior pair MMAs of this thread complete
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+// bounded wait with cluster-scope acquire (arrivals released by the peer CTA)
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                                  uint32_t* status) {
+    if (mbar_try_cluster(bar, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_cluster(bar, parity)) return true;
+        if ((it & 255u) == 0) {
+            if (*abort_flag) return false;
+            if (global_ns() - t0 > kWaitNs) {
+                *abort_flag = 1;
+                atomicOr(status, kErrPipelineTimeout);
+                return false;
+            }
+        }
+    }
+}
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -303,21 +372,28 @@ __device__ __forceinline__ void writeout_generic(const TcParams& p, const float*
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
+// kPair = false: one CTA per 128-row tile (tcgen05 cta_group::1, M = 128).
+// kPair = true: CTA pairs (cluster of 2) share each MMA (cta_group::2,
+// M = 256): each CTA gathers its own 128 rows and loads HALF of the weight
+// tile, so weight traffic per output row halves. The leader (rank 0) issues
+// the MMAs; the peer's weight TMA completes on the leader's barrier and the
+// peer's gathered rows are relayed to it by a remote mbarrier arrive.
+template <bool kPair>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_tc_kernel(const TcParams p, const __grid_constant__ CUtensorMap wmap) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte aligned base for the swizzled tiles
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int S = p.stages;
-    const int bstage = p.bn * 128;
+    const int brows = kPair ? p.bn / 2 : p.bn;  // weight rows held by this CTA
+    const int bstage = brows * 128;
     // layout (offsets from the 1024-aligned base): ring A | ring B | sidx |
-    // gsum | barriers | tmem holder, abort flag. The tail starts 1024-aligned,
-    // so sidx (read as int4) and gsum (f64) are 16-byte aligned.
+    // barriers | tmem holder, abort flag. The epilogue reuses the ring for
+    // its f32 output tile followed by the f64 GroupNorm column sums.
     uint8_t* sA = smem;
     uint8_t* sB = smem + (size_t)S * kAStage;
     int32_t* sidx = reinterpret_cast<int32_t*>(sB + (size_t)S * bstage);  // [kvol][128]
-    double* gsum = reinterpret_cast<double*>(sidx + kMaxKvol * 128);       // [64][2]
-    uint64_t* full = reinterpret_cast<uint64_t*>(gsum + 128);
+    uint64_t* full = reinterpret_cast<uint64_t*>(sidx + kMaxKvol * 128);
     uint64_t* empty = full + S;
     uint64_t* accum = empty + S;
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(accum + 1);
@@ -331,7 +407,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t m0 = (int64_t)tile * 128;
     const int n0 = blockIdx.y * p.bn;
 
-    uint32_t mask = p.nbr ? (p.tile_mask ? p.tile_mask[tile] : 0x7ffffffu) : 1u;
+    const uint32_t rank = kPair ? cluster_rank() : 0u;
+    const bool leader = rank == 0;
+    // both CTAs of a pair walk the union of their tiles' active offsets
+    uint32_t mask = 1u;
+    if (p.nbr) {
+        mask = 0x7ffffffu;
+        if (p.tile_mask) {
+            mask = tile < p.n_tiles ? p.tile_mask[tile] : 0u;
+            if (kPair && (tile ^ 1) < p.n_tiles) mask |= p.tile_mask[tile ^ 1];
+        }
+    }
     mask &= (p.kvol >= 32) ? 0xffffffffu : ((1u << p.kvol) - 1u);
     const int kchunks = (p.cin + 63) / 64;
     const int T = __popc(mask) * kchunks;
@@ -340,7 +426,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- setup: barriers, TMEM, gather indices ----
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
-            mbar_init(smem_u32(full + s), kProdWarps * 32 + p.nb);  // cp.async threads + weight issuers
+            // single CTA: cp.async threads + weight issuers; pair leader: + the
+            // peer's relay arrival; pair peer: its own cp.async threads only
+            const uint32_t cnt = !kPair ? kProdWarps * 32 + p.nb : leader ? kProdWarps * 32 + p.nb + 1 : kProdWarps * 32;
+            mbar_init(smem_u32(full + s), cnt);
             mbar_init(smem_u32(empty + s), 1);
         }
         mbar_init(smem_u32(accum), 1);
@@ -348,13 +437,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == kMmaWarp) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
-                     "r"(tcols)
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        if (kPair) {
+            asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                         "r"(tcols)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+        } else {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                         "r"(tcols)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        }
     }
-    if (p.gn_partials)
-        for (int i = tid; i < 128; i += kThreads) gsum[i] = 0.0;
     // gather row coordinates of the active offsets for the tile's 128 rows
     for (int i = tid; i < kMaxKvol * 128; i += kThreads) {
         const int o = i >> 7, row = i & 127;
@@ -366,6 +460,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     tc_fence_before();
     __syncthreads();
+    if (kPair) cluster_sync();  // the peer's barriers exist before any remote arrive
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
 
@@ -407,7 +502,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0 && j < p.nb) {
             uint32_t mrem = mask;
             int o = 0;
-            const int rows = p.bn / p.nb;
+            const int rows = brows / p.nb;
             const uint32_t bytes = (uint32_t)rows * 128;
             for (int it = 0; it < T; ++it) {
                 const int s = it % S;
@@ -419,32 +514,68 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (!mbar_wait(smem_u32(empty + s), ph ^ 1u, abort_flag, p.status)) break;
                 const uint32_t fb = smem_u32(full + s);
-                mbar_arrive_tx(fb, bytes);
-                tma_load_2d(smem_u32(sB + (size_t)s * bstage + (size_t)j * rows * 128), &wmap, kc * 64,
-                            o * p.cout_pad + n0 + j * rows, fb);
+                const uint32_t dst = smem_u32(sB + (size_t)s * bstage + (size_t)j * rows * 128);
+                const int y = o * p.cout_pad + n0 + (int)rank * brows + j * rows;
+                if (!kPair) {
+                    mbar_arrive_tx(fb, bytes);
+                    tma_load_2d(dst, &wmap, kc * 64, y, fb);
+                } else {
+                    // the leader expects both CTAs' slice j; both complete on its barrier
+                    if (leader) mbar_arrive_tx(fb, 2 * bytes);
+                    tma_load_2d_pair(dst, &wmap, kc * 64, y, map_to_rank(fb, 0));
+                }
             }
         }
     } else if (warp == kMmaWarp) {
-        // ================= MMA issuer =================
-        if (lane == 0) {
+        if (lane == 0 && kPair && !leader) {
+            // ================= relay (pair peer): gathered rows landed -> leader =================
+            for (int it = 0; it < T; ++it) {
+                const int s = it % S;
+                const uint32_t ph = (uint32_t)(it / S) & 1u;
+                if (!mbar_wait(smem_u32(full + s), ph, abort_flag, p.status)) break;
+                // the rows were written through the generic proxy; the leader's
+                // tensor core reads them through the async proxy
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_arrive_remote(map_to_rank(smem_u32(full + s), 0));
+            }
+        } else if (lane == 0) {
+            // ================= MMA issuer =================
             bool ok = true;
             for (int it = 0; it < T; ++it) {
                 const int s = it % S;
                 const uint32_t ph = (uint32_t)(it / S) & 1u;
-                if (!mbar_wait(smem_u32(full + s), ph, abort_flag, p.status)) {
+                const bool got = kPair ? mbar_wait_cluster(smem_u32(full + s), ph, abort_flag, p.status)
+                                       : mbar_wait(smem_u32(full + s), ph, abort_flag, p.status);
+                if (!got) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint32_t a0 = smem_u32(sA + (size_t)s * kAStage);
                 const uint32_t b0 = smem_u32(sB + (size_t)s * bstage);
+                if (kPair) {
 #pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    mma_bf16(tmem, sw128_desc(a0 + 32 * k), sw128_desc(b0 + 32 * k), p.idesc,
-                             (it > 0 || k > 0) ? 1u : 0u);
-                mma_commit(smem_u32(empty + s));
+                    for (int k = 0; k < 4; ++k)
+                        mma_bf16_pair(tmem, sw128_desc(a0 + 32 * k), sw128_desc(b0 + 32 * k), p.idesc,
+                                      (it > 0 || k > 0) ? 1u : 0u);
+                    mma_commit_pair(smem_u32(empty + s));                       // this CTA's stage
+                    mma_commit_pair(map_to_rank(smem_u32(empty + s), 1));      // the peer's stage
+                } else {
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        mma_bf16(tmem, sw128_desc(a0 + 32 * k), sw128_desc(b0 + 32 * k), p.idesc,
+                                 (it > 0 || k > 0) ? 1u : 0u);
+                    mma_commit(smem_u32(empty + s));
+                }
             }
-            if (ok && T > 0) mma_commit(smem_u32(accum));
+            if (ok && T > 0) {
+                if (kPair) {
+                    mma_commit_pair(smem_u32(accum));
+                    mma_commit_pair(map_to_rank(smem_u32(accum), 1));
+                } else {
+                    mma_commit(smem_u32(accum));
+                }
+            }
         }
         __syncwarp();
     }
@@ -535,34 +666,49 @@ __global__ void __launch_bounds__(kThreads, 1)
                 writeout_generic(p, stage_out, ostride, lane_base, lane, m0, n0, limit, nrows, bias4, stats, s1, s2);
         }
         if (stats) {
+            // deterministic GroupNorm partials: per-warp column sums to smem,
+            // then each group summed over warps and columns in a fixed order
+            double* colp = reinterpret_cast<double*>(smem + (size_t)128 * ostride * 4);  // [4][bn][2]
 #pragma unroll
             for (int q = 0; q < kQ; ++q)
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const int lc = 128 * q + 4 * lane + j;
-                    const int col = n0 + lc;
-                    if (lc < limit) {
-                        const int g = col / gs;
-                        atomicAdd(gsum + 2 * g, s1[q][j]);
-                        atomicAdd(gsum + 2 * g + 1, s2[q][j]);
+                    if (lc < p.bn) {
+                        colp[((size_t)warp * p.bn + lc) * 2 + 0] = lc < limit ? s1[q][j] : 0.0;
+                        colp[((size_t)warp * p.bn + lc) * 2 + 1] = lc < limit ? s2[q][j] : 0.0;
                     }
                 }
             asm volatile("bar.sync 1, 128;" ::: "memory");
             const int et = tid - kEpiWarp0 * 32;
             const int g_lo = n0 / gs;
-            const int g_hi = min(p.gn_groups - 1, (min(n0 + p.bn, p.cout) - 1) / gs);
-            for (int g = g_lo + et; g <= g_hi; g += 128) {
-                atomicAdd(p.gn_partials + ((int64_t)tile * p.gn_groups + g) * 2 + 0, gsum[2 * g]);
-                atomicAdd(p.gn_partials + ((int64_t)tile * p.gn_groups + g) * 2 + 1, gsum[2 * g + 1]);
+            const int g_hi = min(p.gn_groups - 1, (n0 + limit - 1) / gs);
+            // the padding CTA of an odd pair count (tile == n_tiles) has no rows and no slot
+            for (int g = g_lo + et; tile < p.n_tiles && g <= g_hi; g += 128) {
+                const int c_lo = max(g * gs - n0, 0), c_hi = min((g + 1) * gs - n0, limit);
+                double a = 0.0, b = 0.0;
+                for (int w = 0; w < 4; ++w)
+                    for (int c = c_lo; c < c_hi; ++c) {
+                        a += colp[((size_t)w * p.bn + c) * 2 + 0];
+                        b += colp[((size_t)w * p.bn + c) * 2 + 1];
+                    }
+                // a group split across two column tiles gets exactly two adds
+                // onto a zeroed slot, which is order independent
+                atomicAdd(p.gn_partials + ((int64_t)tile * p.gn_groups + g) * 2 + 0, a);
+                atomicAdd(p.gn_partials + ((int64_t)tile * p.gn_groups + g) * 2 + 1, b);
             }
         }
         tc_fence_before();
     }
 
     __syncthreads();
+    if (kPair) cluster_sync();  // no CTA leaves while its pair may still touch its smem/TMEM
     if (warp == kMmaWarp) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tcols) : "memory");
+        if (kPair)
+            asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tcols) : "memory");
+        else
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tcols) : "memory");
     }
 }
 
@@ -583,7 +729,7 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 
 size_t smem_bytes(int stages, int bn) {
     return 1024 /*align slack*/ + (size_t)stages * (kAStage + bn * 128) + (2 * stages + 1) * 8 + 16 +
-           128 * 8 /*gsum*/ + kMaxKvol * 128 * 4 /*sidx*/;
+           kMaxKvol * 128 * 4 /*sidx*/;
 }
 
 }  // namespace
@@ -608,10 +754,14 @@ cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     const int cout_pad = (cout + 15) / 16 * 16;
     const int cin_pad = (cin + 63) / 64 * 64;
     const int bn = tc_pick_bn(cout);
-    int stages = (int)((200 * 1024) / (kAStage + bn * 128));
+    const int64_t tiles = (n_out + 127) / 128;
+    // CTA pairs need an even row-tile count (the last pair may hold one empty tile)
+    const bool pair = (flags & S3DSP_CONV_CTA_PAIR) != 0;
+    const int brows = pair ? bn / 2 : bn;
+    int stages = (int)((200 * 1024) / (kAStage + brows * 128));
     if (stages > 8) stages = 8;
-    // the epilogue reuses the ring for a 128 x (bn + 4) f32 tile
-    while ((size_t)stages * (kAStage + bn * 128) < (size_t)128 * (bn + 4) * 4) ++stages;
+    // the epilogue reuses the ring for a 128 x (bn + 4) f32 tile plus 4 x bn x 2 f64 column sums
+    while ((size_t)stages * (kAStage + brows * 128) < (size_t)128 * (bn + 4) * 4 + (size_t)4 * bn * 16) ++stages;
     (void)n_in;
 
     auto encode = get_encode_fn();
@@ -620,12 +770,12 @@ cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
         return cudaErrorNotSupported;
     }
     // weight tile rows per TMA load: NB issuers, slices a multiple of 8 rows
-    const int nb = (bn % 32 == 0) ? 4 : 2;
+    const int nb = (brows % 32 == 0) ? 4 : (brows % 16 == 0) ? 2 : 1;
     CUtensorMap wmap;
     {
         const cuuint64_t dims[2] = {(cuuint64_t)cin_pad, (cuuint64_t)kvol * (cuuint64_t)cout_pad};
         const cuuint64_t strides[1] = {(cuuint64_t)cin_pad * 2};
-        const cuuint32_t box[2] = {64, (cuuint32_t)(bn / nb)};
+        const cuuint32_t box[2] = {64, (cuuint32_t)(brows / nb)};
         const cuuint32_t estr[2] = {1, 1};
         CUresult cr = encode(&wmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)w, dims, strides, box, estr,
                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -646,7 +796,8 @@ cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     p.bn = bn;
     p.nb = nb;
     p.stages = stages;
-    p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+    const uint32_t mma_m = pair ? 256u : 128u;  // pair: M spans both CTAs' rows
+    p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(bn >> 3) << 17) | ((mma_m >> 4) << 24);
     p.bias = bias;
     p.residual = residual;
     p.res_dtype = res_dtype;
@@ -654,22 +805,40 @@ cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     p.out = out;
     p.out_dtype = out_dtype;
     p.n_out = n_out;
+    p.n_tiles = tiles;
     p.cout = cout;
     p.flags = flags;
     p.gn_partials = gn_partials;
     p.gn_groups = gn_groups;
     p.status = ctx->d_status;
 
-    const size_t smem = smem_bytes(stages, bn);
-    cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const size_t smem = smem_bytes(stages, brows);
+    cudaError_t e = pair ? cudaFuncSetAttribute(conv_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
+                         : cudaFuncSetAttribute(conv_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    const int64_t tiles = (n_out + 127) / 128;
     if (gn_partials) {
         e = cudaMemsetAsync(gn_partials, 0, sizeof(double) * 2 * (size_t)gn_groups * (size_t)tiles, ctx->stream);
         if (e != cudaSuccess) return e;
     }
-    const dim3 grid((unsigned)tiles, (unsigned)(cout_pad / bn));
-    conv_tc_kernel<<<grid, kThreads, smem, ctx->stream>>>(p, wmap);
+    if (!pair) {
+        const dim3 grid((unsigned)tiles, (unsigned)(cout_pad / bn));
+        conv_tc_kernel<false><<<grid, kThreads, smem, ctx->stream>>>(p, wmap);
+        return cudaGetLastError();
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((tiles + 1) / 2 * 2), (unsigned)(cout_pad / bn));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = ctx->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, conv_tc_kernel<true>, p, wmap);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 

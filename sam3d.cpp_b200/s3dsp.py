@@ -24,7 +24,7 @@ F32, BF16, F16 = 0, 1, 2
 PREC_F32_STRICT, PREC_BF16 = 0, 1
 LAYOUT_SLAT_ROW, LAYOUT_MESH_PACKED, LAYOUT_LINEAR, LAYOUT_SPCONV_1X1, LAYOUT_TRANSPOSED_2X2X2 = 0, 1, 2, 3, 4
 SENTINEL_SLAT_N, SENTINEL_MESH_NEG1 = 0, 1
-EPI_SILU, PRO_AFFINE_SILU = 1, 2
+EPI_SILU, PRO_AFFINE_SILU, CONV_CTA_PAIR = 1, 2, 4
 CONTEXT_DEFERRED_CHECKS = 1
 CONTEXT_OWN_STREAM = 2
 
