@@ -4,6 +4,33 @@
 
 using namespace s3dsp;
 
+namespace {
+
+// BF16 kernel choice. The 256-row stream-K kernel moves fewer bytes per MAC
+// but pays a fix-up for every split tile and a pipeline refill per tile; it
+// wins once there are a few waves of 128-row tiles (B200 sweep of 64^3..256^3
+// shells at C = 128 and 256: 267 tiles on 148 SMs favours 128-row tiles, 473
+// and more favour stream-K).
+bool use_stream_k(const s3dsp_context* ctx, int64_t n_out, uint32_t flags) {
+    if (flags & (S3DSP_CONV_TILE128 | S3DSP_CONV_CTA_PAIR)) return false;
+    if (flags & S3DSP_CONV_STREAM_K) return true;
+    const int64_t tiles = (n_out + 127) / 128;
+    return tiles * 2 >= (int64_t)ctx->sm_count * 5;
+}
+
+}  // namespace
+
+extern "C" S3DSP_API const char* s3dsp_conv_kernel(const s3dsp_context* ctx, int64_t n_out, int32_t kvol, int64_t cin,
+                                                   int64_t cout, uint32_t precision, uint32_t flags) {
+    (void)kvol;
+    (void)cin;
+    (void)cout;
+    if (!ctx) return nullptr;
+    if (precision == S3DSP_PREC_F32_STRICT) return "conv_f32_kernel";
+    if (precision != S3DSP_PREC_BF16) return nullptr;
+    return use_stream_k(ctx, n_out, flags) ? "conv_sk_kernel" : "conv_tc_kernel";
+}
+
 extern "C" S3DSP_API s3d_status s3dsp_conv(s3dsp_context* ctx, const s3dsp_kmap* kmap, int32_t kvol,
                                            uint32_t precision, const void* in, uint32_t in_dtype, int64_t n_in,
                                            int64_t cin, int32_t in_shift, const void* weight, const float* bias,
@@ -68,11 +95,17 @@ extern "C" S3DSP_API s3d_status s3dsp_conv(s3dsp_context* ctx, const s3dsp_kmap*
             return fail(error, error_capacity, S3D_INVALID_ARGUMENT,
                         "BF16 needs cin %% 8 == 0 and 16-byte aligned in/weight/out/residual");
         s3d_status st = S3D_OK;
-        e = launch_conv_tc(ctx, kmap, kvol, (const __nv_bfloat16*)in, n_in, (int)cin, in_shift,
-                           (const __nv_bfloat16*)weight, bias, residual, res_dtype, res_shift, out, out_dtype, n_out,
-                           (int)cout, flags, gn_partials, gn_groups, error, error_capacity, &st);
+        const bool tile128 = !use_stream_k(ctx, n_out, flags);
+        if (tile128)
+            e = launch_conv_tc(ctx, kmap, kvol, (const __nv_bfloat16*)in, n_in, (int)cin, in_shift,
+                               (const __nv_bfloat16*)weight, bias, residual, res_dtype, res_shift, out, out_dtype,
+                               n_out, (int)cout, flags, gn_partials, gn_groups, error, error_capacity, &st);
+        else
+            e = launch_conv_sk(ctx, kmap, kvol, (const __nv_bfloat16*)in, n_in, (int)cin, in_shift,
+                               (const __nv_bfloat16*)weight, bias, residual, res_dtype, res_shift, out, out_dtype,
+                               n_out, (int)cout, flags, gn_partials, gn_groups, error, error_capacity, &st);
         if (st != S3D_OK) return st;
-        if (e != cudaSuccess) return cuda_fail(error, error_capacity, e, "conv_tc_kernel");
+        if (e != cudaSuccess) return cuda_fail(error, error_capacity, e, tile128 ? "conv_tc_kernel" : "conv_sk_kernel");
         return S3D_OK;
     }
     return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "unknown precision %u", precision);

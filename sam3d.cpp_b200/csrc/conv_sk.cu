@@ -1,0 +1,583 @@
+// K3 (BF16) implicit-gather sparse convolution, stream-K form: the default
+// tensor-core path.
+//
+// Work tile: 256 output rows x BN output channels, held as two 128-row f32
+// accumulators in TMEM (columns [0, BN) and [H, H + BN), H = the allocation
+// half). Each weight tile that TMA brings in feeds both accumulators, so a
+// reduction step moves 32 KB of gathered rows + BN x 128 B of weights for
+// 2 x 128 x BN x 64 MACs. The per-SM copy rate, not L2 bandwidth, bounds
+// this kernel (L2 runs at about a fifth of its peak), so bytes per MAC per
+// SM is what the tile shape minimises.
+//
+// Stream-K: the iteration space (work tile, kernel offset) of U = tiles x
+// kvol units is cut into `grid` (= number of SMs, fewer for small problems)
+// contiguous ranges of equal length, one per CTA, so every SM gets the same
+// number of reduction steps whatever the tile count. A CTA walks its range
+// as segments (one work tile each). A tile covered by one CTA runs the
+// epilogue straight from TMEM. A tile split over k CTAs ("pieces") is fixed
+// up without any waiting: each piece stores its raw accumulator to a
+// workspace slot, then bumps the tile's counter; the piece that arrives
+// last sums the k slots in piece order (so the result does not depend on
+// which CTA finished last) and runs the epilogue. Nothing spins on another
+// CTA, so no co-residency is assumed.
+//
+// Warp roles (672 threads) as in the 128-row kernel: warps 0-15 gather A by
+// cp.async (4 rows x 16 B per thread per step) and then run the epilogue
+// (warp w: TMEM lanes 32*(w%4).., column chunks w/4, w/4+4, ...; write-out
+// rows 8w..8w+7), warps 16-19 issue the weight TMA loads, warp 20 owns TMEM
+// and issues 8 tcgen05.mma (M=128, N=BN, K=16) per step. Waits are bounded
+// (2 s of %globaltimer); a timeout sets kErrPipelineTimeout and the CTA
+// leaves through the common teardown.
+//
+// Replaces the same reference code as the 128-row kernel: the GGML
+// get_rows + mul_mat chains of slat_flow_graph.cpp:112-155 and
+// mesh_decoder_graph.cpp:81-103 (in_shift = 3 is repeat_children,
+// mesh_decoder_graph.cpp:32-38, without materialising it).
+#include "s3dsp_internal.h"
+#include "tc_common.cuh"
+
+using namespace s3dsp;
+using namespace s3dsp::tc;
+
+namespace {
+
+constexpr int kProdWarps = 16;        // A gather + epilogue warps (512 threads)
+constexpr int kEpiThreads = kProdWarps * 32;
+constexpr int kBWarp0 = 16;           // first weight-TMA warp
+constexpr int kMaxBWarps = 4;
+constexpr int kMmaWarp = 20;
+constexpr int kThreads = 21 * 32;
+constexpr int kRows = 256;            // output rows per work tile
+constexpr int kAStage = kRows * 128;  // bytes: 256 rows x 64 bf16
+constexpr int kAHalf = 128 * 128;     // second accumulator's rows start here
+constexpr int kMaxKvol = 27;
+constexpr int kSmemMax = kSmemOptIn;
+
+struct SkParams {
+    const __nv_bfloat16* in;
+    int cin;
+    int in_shift;
+    const int32_t* nbr;         // [kvol][n_out] or null (identity)
+    const uint32_t* tile_mask;  // [128-row tiles] or null
+    int kvol;
+    int kchunks;                // 64-channel reduction chunks per offset
+    int cout_pad;               // packed weight rows per offset
+    int bn;
+    int nb;                     // weight TMA loads per stage
+    int stages;
+    uint32_t tcols;             // TMEM columns allocated
+    uint32_t thalf;             // column of the second accumulator
+    uint32_t idesc;
+    const float* bias;
+    const void* residual;
+    uint32_t res_dtype;
+    int res_shift;
+    void* out;
+    uint32_t out_dtype;
+    int64_t n_out;
+    int64_t n_tiles;            // 128-row tiles (GroupNorm partial slots)
+    int nnb;                    // column blocks per 256-row tile
+    int64_t units;              // work tiles x kvol
+    int grid;
+    float* ws;                  // [2 * grid][2][bn / 16][4][128] float4 raw accumulators, or null
+    uint32_t* counters;         // [work tiles] pieces arrived, zeroed before launch
+    int cout;
+    uint32_t flags;
+    double* gn_partials;
+    int gn_groups;
+    uint32_t* status;
+};
+
+__device__ __forceinline__ int64_t unit_begin(const SkParams& p, int i) {
+    return (int64_t)i * p.units / p.grid;
+}
+// the CTA whose unit range holds unit u
+__device__ __forceinline__ int cta_of(const SkParams& p, int64_t u) {
+    int i = (int)(u * p.grid / p.units);
+    while (i + 1 < p.grid && unit_begin(p, i + 1) <= u) ++i;
+    while (i > 0 && unit_begin(p, i) > u) --i;
+    return i;
+}
+// workspace slot of CTA i's piece of work tile wt: a CTA is split-owner of at
+// most its first and its last tile
+__device__ __forceinline__ int64_t ws_slot(const SkParams& p, int i, int64_t wt) {
+    return 2 * (int64_t)i + ((unit_begin(p, i) / p.kvol) == wt ? 0 : 1);
+}
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
+__device__ __forceinline__ void prod_bar() { asm volatile("bar.sync 2, 512;" ::: "memory"); }
+
+__global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, const __grid_constant__ CUtensorMap wmap) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int S = p.stages;
+    const int bstage = p.bn * 128;
+    const int ostride = p.bn + 4;  // staged f32 row stride (floats)
+    // layout: region0 = max(ring A | ring B, epilogue tile | GN column sums),
+    // then sidx, barriers, tmem holder, flags
+    const size_t ring = (size_t)S * (kAStage + bstage);
+    const size_t epi = (size_t)128 * ostride * 4 + (size_t)kProdWarps * p.bn * 16;
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + (size_t)S * kAStage;
+    int32_t* sidx = reinterpret_cast<int32_t*>(smem + (ring > epi ? ring : epi));  // [kvol][256]
+    uint64_t* full = reinterpret_cast<uint64_t*>(sidx + kMaxKvol * kRows);
+    uint64_t* empty = full + S;
+    uint64_t* accum = empty + S;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(accum + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+    volatile int* owner_flag = abort_flag + 1;
+    float* stage_out = reinterpret_cast<float*>(smem);
+    double* colp = reinterpret_cast<double*>(smem + (size_t)128 * ostride * 4);  // [16][bn][2]
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int me = blockIdx.x;
+
+    if (tid == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(smem_u32(full + s), kEpiThreads + p.nb);
+            mbar_init(smem_u32(empty + s), 1);
+        }
+        mbar_init(smem_u32(accum), 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == kMmaWarp) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                     "r"(p.tcols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_holder;
+
+    uint32_t it = 0;      // pipeline step counter, identical in every role
+    uint32_t acc_ph = 0;  // accum barrier phase
+    const int64_t u_end = unit_begin(p, me + 1);
+    for (int64_t u = unit_begin(p, me); u < u_end;) {
+        const int64_t wt = u / p.kvol;
+        const int64_t seg_end = min(u_end, (wt + 1) * p.kvol);
+        const int ob = (int)(u - wt * p.kvol), oe = (int)(seg_end - wt * p.kvol);
+        u = seg_end;
+        const int64_t st = wt / p.nnb;
+        const int n0 = (int)(wt - st * p.nnb) * p.bn;
+        const int64_t m0 = st * kRows;
+
+        uint32_t mask = 1u;
+        if (p.nbr) {
+            mask = 0xffffffffu;
+            if (p.tile_mask) {
+                mask = p.tile_mask[2 * st];
+                if (2 * st + 1 < p.n_tiles) mask |= p.tile_mask[2 * st + 1];
+            }
+        }
+        mask &= (oe >= 32 ? 0xffffffffu : ((1u << oe) - 1u)) & ~((1u << ob) - 1u);
+        const int T = __popc(mask) * p.kchunks;
+
+        bool prod_ok = true;
+        if (warp < kProdWarps) {
+            // ============ A producers: indices of this segment, then cp.async gathers ============
+            for (int i = tid; i < kMaxKvol * kRows; i += kEpiThreads) {
+                const int o = i >> 8, row = i & (kRows - 1);
+                if (!((mask >> o) & 1u)) continue;
+                const int64_t r = m0 + row;
+                int32_t s = -1;
+                if (r < p.n_out) s = p.nbr ? __ldg(p.nbr + (int64_t)o * p.n_out + r) : (int32_t)r;
+                sidx[i] = s < 0 ? -1 : (s >> p.in_shift);
+            }
+            prod_bar();
+            const int c16 = tid & 7;  // 16-byte chunk of a 128-byte row
+            const int rg = tid >> 3;  // rows rg + 64 * i
+            uint32_t mrem = mask;
+            int o = 0;
+            for (int j = 0; j < T; ++j) {
+                const uint32_t pit = it + (uint32_t)j;
+                const int s = (int)(pit % (uint32_t)S);
+                const uint32_t ph = (pit / (uint32_t)S) & 1u;
+                const int kc = j % p.kchunks;
+                if (kc == 0) {
+                    o = __ffs(mrem) - 1;
+                    mrem &= mrem - 1;
+                }
+                if (!mbar_wait(smem_u32(empty + s), ph ^ 1u, abort_flag, p.status)) {
+                    prod_ok = false;
+                    break;
+                }
+                const int k0 = kc * 64 + c16 * 8;
+                const uint32_t a_base = smem_u32(sA + (size_t)s * kAStage);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int row = rg + 64 * i;
+                    const int32_t src = sidx[o * kRows + row];
+                    const bool valid = src >= 0 && k0 < p.cin;
+                    const void* g = valid ? (const void*)(p.in + (int64_t)src * p.cin + k0) : (const void*)p.in;
+                    cp_async_16(a_base + row * 128 + ((c16 ^ (row & 7)) << 4), g, valid ? 16u : 0u);
+                }
+                cp_async_arrive_noinc(smem_u32(full + s));
+            }
+        } else if (warp < kBWarp0 + kMaxBWarps) {
+            // ============ weight TMA issuers ============
+            const int jw = warp - kBWarp0;
+            if (lane == 0 && jw < p.nb) {
+                const int rows = p.bn / p.nb;
+                const uint32_t bytes = (uint32_t)rows * 128;
+                uint32_t mrem = mask;
+                int o = 0;
+                for (int j = 0; j < T; ++j) {
+                    const uint32_t pit = it + (uint32_t)j;
+                    const int s = (int)(pit % (uint32_t)S);
+                    const uint32_t ph = (pit / (uint32_t)S) & 1u;
+                    const int kc = j % p.kchunks;
+                    if (kc == 0) {
+                        o = __ffs(mrem) - 1;
+                        mrem &= mrem - 1;
+                    }
+                    if (!mbar_wait(smem_u32(empty + s), ph ^ 1u, abort_flag, p.status)) break;
+                    const uint32_t fb = smem_u32(full + s);
+                    mbar_arrive_tx(fb, bytes);
+                    tma_load_2d(smem_u32(sB + (size_t)s * bstage + (size_t)jw * rows * 128), &wmap, kc * 64,
+                                o * p.cout_pad + n0 + jw * rows, fb);
+                }
+            }
+            __syncwarp();
+        } else if (warp == kMmaWarp) {
+            // ============ MMA issuer: two M=128 accumulators per weight tile ============
+            if (lane == 0) {
+                bool ok = true;
+                for (int j = 0; j < T; ++j) {
+                    const uint32_t pit = it + (uint32_t)j;
+                    const int s = (int)(pit % (uint32_t)S);
+                    const uint32_t ph = (pit / (uint32_t)S) & 1u;
+                    if (!mbar_wait(smem_u32(full + s), ph, abort_flag, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sA + (size_t)s * kAStage);
+                    const uint32_t b0 = smem_u32(sB + (size_t)s * bstage);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const uint32_t acc = (j > 0 || k > 0) ? 1u : 0u;
+                        const uint64_t bd = sw128_desc(b0 + 32 * k);
+                        mma_bf16(tmem, sw128_desc(a0 + 32 * k), bd, p.idesc, acc);
+                        mma_bf16(tmem + p.thalf, sw128_desc(a0 + kAHalf + 32 * k), bd, p.idesc, acc);
+                    }
+                    mma_commit(smem_u32(empty + s));
+                }
+                if (ok && T > 0) mma_commit(smem_u32(accum));
+            }
+            __syncwarp();
+        }
+        it += (uint32_t)T;
+
+        if (warp < kProdWarps) {
+            // ============ epilogue (warps 0-15) ============
+            bool have_acc = false;
+            if (T > 0) {
+                have_acc = prod_ok && mbar_wait(smem_u32(accum), acc_ph, abort_flag, p.status);
+                have_acc = __all_sync(0xffffffffu, have_acc);
+            }
+            tc_fence_after();
+            const int lq = warp & 3;                  // TMEM lane quarter (rows 32*lq ..)
+            const int row = 32 * lq + lane;           // accumulator row of this thread
+            const uint32_t tl = tmem + ((uint32_t)(32 * lq) << 16);
+            const int nch = p.bn / 16;                // 16-column chunks
+            const int64_t tb = wt * p.kvol;
+            const int i_first = cta_of(p, tb), i_last = cta_of(p, tb + p.kvol - 1);
+            const int k = i_last - i_first + 1;
+            // piece pc > 0 starts inside this tile (its first tile: slot 2i); piece 0
+            // may have started in an earlier tile (then this is its last: slot 2i+1)
+            const int64_t slot0 = ws_slot(p, i_first, wt);
+            const int64_t slot_stride = (int64_t)kRows * p.bn;
+            bool owner = true;
+            if (k > 1) {
+                // store the raw accumulator as float4s [sub][16-column chunk][quad][row]:
+                // each warp access is 512 contiguous bytes
+                float* slot = p.ws + (me == i_first ? slot0 : 2 * (int64_t)me) * slot_stride;
+                for (int sub = 0; sub < 2; ++sub)
+                    for (int c = warp >> 2; c < nch; c += 4) {
+                        float f[16];
+                        if (have_acc) {
+                            tmem_ld16(tl + sub * p.thalf + 16 * c, f);
+                        } else {
+#pragma unroll
+                            for (int q = 0; q < 16; ++q) f[q] = 0.f;
+                        }
+                        float4* d = reinterpret_cast<float4*>(slot) + (size_t)(sub * nch + c) * 512 + row;
+#pragma unroll
+                        for (int q = 0; q < 4; ++q)
+                            d[q * 128] = make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
+                    }
+                __threadfence();
+                epi_bar();
+                if (tid == 0) *owner_flag = atomicAdd(p.counters + wt, 1u) == (uint32_t)(k - 1);
+                epi_bar();
+                owner = *owner_flag != 0;
+                if (owner) __threadfence();
+            }
+            if (owner) {
+                const bool stats = p.gn_partials != nullptr;
+                const int gs = stats ? p.cout / p.gn_groups : 1;
+                const int limit = min(p.bn, p.cout - n0);
+                float4 bias4[2];
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    const int col = n0 + 128 * q + 4 * lane;
+                    bias4[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (p.bias && 128 * q + 4 * lane < limit) {
+                        bias4[q].x = __ldg(p.bias + col + 0);
+                        bias4[q].y = col + 1 < p.cout ? __ldg(p.bias + col + 1) : 0.f;
+                        bias4[q].z = col + 2 < p.cout ? __ldg(p.bias + col + 2) : 0.f;
+                        bias4[q].w = col + 3 < p.cout ? __ldg(p.bias + col + 3) : 0.f;
+                    }
+                }
+                const int out_k = (p.cout & 3) ? -1 : p.out_dtype == S3DSP_F32 ? 0 : p.out_dtype == S3DSP_BF16 ? 1 : -1;
+                const int res_k = !p.residual ? 0 : p.res_dtype == S3DSP_F32 ? 1 : p.res_dtype == S3DSP_BF16 ? 2 : -1;
+                const int silu_k = (p.flags & S3DSP_EPI_SILU) ? 1 : 0;
+                const int sel = (out_k < 0 || res_k < 0) ? -1 : ((out_k * 3 + res_k) * 2 + silu_k) * 2 + (stats ? 1 : 0);
+                const uint32_t so_base = smem_u32(stage_out);
+                for (int sub = 0; sub < 2; ++sub) {
+                    const int64_t ms = m0 + 128 * sub;
+                    if (ms >= p.n_out) break;
+                    // phase 1: accumulator (TMEM, or the pieces summed in piece order) -> smem tile
+                    for (int c = warp >> 2; c < nch; c += 4) {
+                        float f[16];
+#pragma unroll
+                        for (int q = 0; q < 16; ++q) f[q] = 0.f;
+                        if (k == 1) {
+                            if (have_acc) tmem_ld16(tl + sub * p.thalf + 16 * c, f);
+                        } else {
+                            for (int pc = 0; pc < k; ++pc) {
+                                const int64_t sl = pc == 0 ? slot0 : 2 * (int64_t)(i_first + pc);
+                                const float4* s4 = reinterpret_cast<const float4*>(p.ws + sl * slot_stride) +
+                                                   (size_t)(sub * nch + c) * 512 + row;
+#pragma unroll
+                                for (int q = 0; q < 4; ++q) {
+                                    const float4 v = __ldcg(s4 + q * 128);
+                                    f[4 * q] += v.x;
+                                    f[4 * q + 1] += v.y;
+                                    f[4 * q + 2] += v.z;
+                                    f[4 * q + 3] += v.w;
+                                }
+                            }
+                        }
+                        float* dst = stage_out + (size_t)row * ostride + 16 * c;
+#pragma unroll
+                        for (int q = 0; q < 4; ++q)
+                            *reinterpret_cast<float4*>(dst + 4 * q) = make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
+                    }
+                    epi_bar();
+                    // phase 2: coalesced write-out, rows 8w .. 8w+7
+                    double* colw = colp + (size_t)warp * p.bn * 2;
+                    const int lane_base = 8 * warp;
+                    const int nrows = (int)max((int64_t)0, min((int64_t)8, p.n_out - (ms + lane_base)));
+                    switch (sel) {
+#define S3DSP_WO(idx, OT, RT, SL, ST)                                                                                \
+    case idx:                                                                                                        \
+        writeout_fast<OT, RT, SL, ST>(p, so_base, ostride, lane_base, lane, ms, n0, limit, nrows, bias4, colw); \
+        break;
+                        S3DSP_WO(0, float, NoRes, false, false)
+                        S3DSP_WO(1, float, NoRes, false, true)
+                        S3DSP_WO(2, float, NoRes, true, false)
+                        S3DSP_WO(3, float, NoRes, true, true)
+                        S3DSP_WO(4, float, float, false, false)
+                        S3DSP_WO(5, float, float, false, true)
+                        S3DSP_WO(6, float, float, true, false)
+                        S3DSP_WO(7, float, float, true, true)
+                        S3DSP_WO(8, float, __nv_bfloat16, false, false)
+                        S3DSP_WO(9, float, __nv_bfloat16, false, true)
+                        S3DSP_WO(10, float, __nv_bfloat16, true, false)
+                        S3DSP_WO(11, float, __nv_bfloat16, true, true)
+                        S3DSP_WO(12, __nv_bfloat16, NoRes, false, false)
+                        S3DSP_WO(13, __nv_bfloat16, NoRes, false, true)
+                        S3DSP_WO(14, __nv_bfloat16, NoRes, true, false)
+                        S3DSP_WO(15, __nv_bfloat16, NoRes, true, true)
+                        S3DSP_WO(16, __nv_bfloat16, float, false, false)
+                        S3DSP_WO(17, __nv_bfloat16, float, false, true)
+                        S3DSP_WO(18, __nv_bfloat16, float, true, false)
+                        S3DSP_WO(19, __nv_bfloat16, float, true, true)
+                        S3DSP_WO(20, __nv_bfloat16, __nv_bfloat16, false, false)
+                        S3DSP_WO(21, __nv_bfloat16, __nv_bfloat16, false, true)
+                        S3DSP_WO(22, __nv_bfloat16, __nv_bfloat16, true, false)
+                        S3DSP_WO(23, __nv_bfloat16, __nv_bfloat16, true, true)
+#undef S3DSP_WO
+                        default:
+                            writeout_generic(p, stage_out, ostride, lane_base, lane, ms, n0, limit, nrows, bias4,
+                                             stats ? colw : nullptr);
+                    }
+                    if (stats) {
+                        // deterministic GroupNorm partials of the 128-row tile: the write-out
+                        // left per-warp column sums; each group summed over warps, columns in order
+                        epi_bar();
+                        const int64_t t128 = 2 * st + sub;
+                        const int g_lo = n0 / gs;
+                        const int g_hi = min(p.gn_groups - 1, (n0 + limit - 1) / gs);
+                        for (int g = g_lo + tid; g <= g_hi; g += kEpiThreads) {
+                            const int c_lo = max(g * gs - n0, 0), c_hi = min((g + 1) * gs - n0, limit);
+                            double a = 0.0, b = 0.0;
+                            for (int w = 0; w < kProdWarps; ++w)
+                                for (int c = c_lo; c < c_hi; ++c) {
+                                    a += colp[((size_t)w * p.bn + c) * 2 + 0];
+                                    b += colp[((size_t)w * p.bn + c) * 2 + 1];
+                                }
+                            // a group split across two column blocks gets exactly two adds
+                            // onto a zeroed slot, which is order independent
+                            atomicAdd(p.gn_partials + (t128 * p.gn_groups + g) * 2 + 0, a);
+                            atomicAdd(p.gn_partials + (t128 * p.gn_groups + g) * 2 + 1, b);
+                        }
+                    }
+                    epi_bar();  // the tile and column sums are reused by the next subtile
+                }
+            }
+            // generic-proxy writes to the ring precede the next segment's TMA writes
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tc_fence_before();
+            if (T > 0) acc_ph ^= 1u;
+        }
+        __syncthreads();
+        tc_fence_after();
+        if (*abort_flag) break;
+    }
+    if (warp < kProdWarps) asm volatile("cp.async.wait_all;" ::: "memory");
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(p.tcols) : "memory");
+    }
+}
+
+size_t sk_smem_bytes(int stages, int bn) {
+    const size_t ring = (size_t)stages * (kAStage + bn * 128);
+    const size_t epi = (size_t)128 * (bn + 4) * 4 + (size_t)kProdWarps * bn * 16;
+    return 1024 /*align slack*/ + (ring > epi ? ring : epi) + (size_t)kMaxKvol * kRows * 4 /*sidx*/ +
+           (2 * stages + 1) * 8 + 16;
+}
+
+}  // namespace
+
+namespace s3dsp {
+
+int tc_pick_bn(int cout);
+
+cudaError_t launch_conv_sk(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol, const __nv_bfloat16* in,
+                           int64_t n_in, int cin, int in_shift, const __nv_bfloat16* w, const float* bias,
+                           const void* residual, uint32_t res_dtype, int res_shift, void* out, uint32_t out_dtype,
+                           int64_t n_out, int cout, uint32_t flags, double* gn_partials, int gn_groups, char* error,
+                           uint64_t error_capacity, s3d_status* st) {
+    *st = S3D_OK;
+    (void)n_in;
+    const int cout_pad = (cout + 15) / 16 * 16;
+    const int cin_pad = (cin + 63) / 64 * 64;
+    const int bn = tc_pick_bn(cout);
+    const int nnb = cout_pad / bn;
+    const int kchunks = cin_pad / 64;
+    const int64_t tiles = (n_out + 127) / 128;
+    const int64_t work_tiles = (n_out + kRows - 1) / kRows * nnb;
+    const int64_t units = work_tiles * kvol;
+
+    int stages = 8;
+    while (stages > 2 && sk_smem_bytes(stages, bn) > (size_t)kSmemMax) --stages;
+    const size_t smem = sk_smem_bytes(stages, bn);
+    if (smem > (size_t)kSmemMax) {
+        *st = fail(error, error_capacity, S3D_INTERNAL_ERROR, "conv tile of %d columns does not fit shared memory", bn);
+        return cudaErrorInvalidValue;
+    }
+    // at least ~16 reduction steps per CTA before splitting tiles further
+    const int64_t min_units = (16 + kchunks - 1) / kchunks;
+    int64_t g = (units + min_units - 1) / min_units;
+    if (g > ctx->sm_count) g = ctx->sm_count;
+    if (g < 1) g = 1;
+    const int grid = (int)g;
+    bool split = false;
+    for (int i = 1; i < grid && !split; ++i) split = ((int64_t)i * units / grid) % kvol != 0;
+
+    auto encode = get_encode_fn();
+    if (!encode) {
+        *st = fail(error, error_capacity, S3D_INTERNAL_ERROR, "cuTensorMapEncodeTiled unavailable");
+        return cudaErrorNotSupported;
+    }
+    const int nb = (bn % 32 == 0) ? 4 : (bn % 16 == 0) ? 2 : 1;
+    CUtensorMap wmap;
+    {
+        const cuuint64_t dims[2] = {(cuuint64_t)cin_pad, (cuuint64_t)kvol * (cuuint64_t)cout_pad};
+        const cuuint64_t strides[1] = {(cuuint64_t)cin_pad * 2};
+        const cuuint32_t box[2] = {64, (cuuint32_t)(bn / nb)};
+        const cuuint32_t estr[2] = {1, 1};
+        CUresult cr = encode(&wmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)w, dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (cr != CUDA_SUCCESS) {
+            *st = fail(error, error_capacity, S3D_INTERNAL_ERROR, "weight tensor map failed (%d)", (int)cr);
+            return cudaErrorInvalidValue;
+        }
+    }
+    uint32_t thalf = 32;
+    while ((int)thalf < bn) thalf <<= 1;
+
+    SkParams p;
+    p.in = in;
+    p.cin = cin;
+    p.in_shift = in_shift;
+    p.nbr = kmap ? kmap->nbr : nullptr;
+    p.tile_mask = kmap ? kmap->tile_mask : nullptr;
+    p.kvol = kvol;
+    p.kchunks = kchunks;
+    p.cout_pad = cout_pad;
+    p.bn = bn;
+    p.nb = nb;
+    p.stages = stages;
+    p.tcols = 2 * thalf;
+    p.thalf = thalf;
+    p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(bn >> 3) << 17) | ((128u >> 4) << 24);
+    p.bias = bias;
+    p.residual = residual;
+    p.res_dtype = res_dtype;
+    p.res_shift = res_shift;
+    p.out = out;
+    p.out_dtype = out_dtype;
+    p.n_out = n_out;
+    p.n_tiles = tiles;
+    p.nnb = nnb;
+    p.units = units;
+    p.grid = grid;
+    p.ws = nullptr;
+    p.counters = nullptr;
+    p.cout = cout;
+    p.flags = flags;
+    p.gn_partials = gn_partials;
+    p.gn_groups = gn_groups;
+    p.status = ctx->d_status;
+
+    cudaStream_t s = ctx->stream;
+    static std::atomic<uint64_t> optin{0};
+    cudaError_t e = smem_optin((const void*)conv_sk_kernel, ctx->device, optin);
+    if (e != cudaSuccess) return e;
+    if (gn_partials) {
+        e = cudaMemsetAsync(gn_partials, 0, sizeof(double) * 2 * (size_t)gn_groups * (size_t)tiles, s);
+        if (e != cudaSuccess) return e;
+    }
+    void* ws = nullptr;
+    void* counters = nullptr;
+    if (split) {
+        e = cudaMallocAsync(&ws, (size_t)2 * grid * kRows * bn * sizeof(float), s);
+        if (e == cudaSuccess) e = cudaMallocAsync(&counters, (size_t)work_tiles * sizeof(uint32_t), s);
+        if (e == cudaSuccess) e = cudaMemsetAsync(counters, 0, (size_t)work_tiles * sizeof(uint32_t), s);
+        if (e != cudaSuccess) {
+            if (ws) cudaFreeAsync(ws, s);
+            if (counters) cudaFreeAsync(counters, s);
+            *st = cuda_fail(error, error_capacity, e, "conv workspace");
+            return e;
+        }
+        p.ws = static_cast<float*>(ws);
+        p.counters = static_cast<uint32_t*>(counters);
+    }
+    conv_sk_kernel<<<grid, kThreads, smem, s>>>(p, wmap);
+    e = cudaGetLastError();
+    if (ws) cudaFreeAsync(ws, s);
+    if (counters) cudaFreeAsync(counters, s);
+    return e;
+}
+
+}  // namespace s3dsp

@@ -34,12 +34,10 @@
 // as one gather-GEMM; in_shift = 3 gathers the parent row of a child, which
 // is repeat_children (mesh_decoder_graph.cpp:32-38) without materialising it.
 #include "s3dsp_internal.h"
-
-#include <cudaTypedefs.h>
-
-#include <type_traits>
+#include "tc_common.cuh"
 
 using namespace s3dsp;
+using namespace s3dsp::tc;
 
 namespace {
 
@@ -51,7 +49,6 @@ constexpr int kThreads = 21 * 32;
 constexpr int kEpiWarp0 = 0;        // first of the 4 epilogue warps
 constexpr int kAStage = 128 * 128;  // bytes: 128 rows x 64 bf16
 constexpr int kMaxKvol = 27;
-constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s
 
 struct TcParams {
     const __nv_bfloat16* in;
@@ -80,66 +77,6 @@ struct TcParams {
     uint32_t* status;
 };
 
-// ---------------------------------------------------------------------------
-// PTX helpers
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return (uint32_t)__cvta_generic_to_shared(p);
-}
-__device__ __forceinline__ unsigned long long global_ns() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Bounded wait. Returns false (and raises the CTA abort flag) on timeout or
-// when another role already aborted.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                          uint32_t* status) {
-    if (mbar_try(bar, parity)) return true;
-    const unsigned long long t0 = global_ns();
-    for (uint32_t it = 1;; ++it) {
-        if (mbar_try(bar, parity)) return true;
-        if ((it & 255u) == 0) {
-            if (*abort_flag) return false;
-            if (global_ns() - t0 > kWaitNs) {
-                *abort_flag = 1;
-                atomicOr(status, kErrPipelineTimeout);
-                return false;
-            }
-        }
-    }
-}
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
-        "l"((unsigned long long)map), "r"(x), "r"(y), "r"(bar)
-        : "memory");
-}
-__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
-}
-// arrive on `bar` once all of this thread's prior cp.async copies have landed
-// (counts as one of the barrier's expected arrivals)
-__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
-}
 // --- CTA-pair (cluster of 2) helpers ---
 __device__ __forceinline__ uint32_t cluster_rank() {
     uint32_t r;
@@ -208,166 +145,6 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
     }
 }
 
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// K-major operand in the 128-byte swizzle canonical layout: rows of 128 B,
-// 8-row (1024 B) swizzle atoms stacked along M/N (stride byte offset 1024),
-// descriptor version 1, layout type 2 (SWIZZLE_128B).
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
-    return (uint64_t)((addr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
-__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(a), "l"(b), "r"(idesc), "r"(acc)
-        : "memory");
-}
-__device__ __forceinline__ void mma_commit(uint32_t bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
-                 : "memory");
-}
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&f)[16]) {
-    uint32_t v[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-        : "r"(taddr)
-        : "memory");
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int j = 0; j < 16; ++j) f[j] = __uint_as_float(v[j]);
-}
-
-__device__ __forceinline__ float silu_f(float v) { return v / (1.0f + __expf(-v)); }
-
-__device__ __forceinline__ float load1(const void* p, uint32_t dt, int64_t i) {
-    if (dt == S3DSP_F32) return reinterpret_cast<const float*>(p)[i];
-    if (dt == S3DSP_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
-    return __half2float(reinterpret_cast<const __half*>(p)[i]);
-}
-__device__ __forceinline__ void store1(void* p, uint32_t dt, int64_t i, float v) {
-    if (dt == S3DSP_F32)
-        reinterpret_cast<float*>(p)[i] = v;
-    else if (dt == S3DSP_BF16)
-        reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16(v);
-    else
-        reinterpret_cast<__half*>(p)[i] = __float2half(v);
-}
-
-
-// ---------------------------------------------------------------------------
-// epilogue write-out: typed vector access, one compact loop per variant
-// ---------------------------------------------------------------------------
-struct NoRes {};
-template <typename T>
-struct Vec4;
-template <>
-struct Vec4<float> {
-    static __device__ __forceinline__ float4 load(const void* base, int64_t i) {
-        return __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + i));
-    }
-    static __device__ __forceinline__ void store(void* base, int64_t i, float4 v) {
-        *reinterpret_cast<float4*>(reinterpret_cast<float*>(base) + i) = v;
-    }
-};
-template <>
-struct Vec4<__nv_bfloat16> {
-    static __device__ __forceinline__ float4 load(const void* base, int64_t i) {
-        const uint2 u = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(base) + i));
-        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
-        const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
-        return make_float4(a.x, a.y, b.x, b.y);
-    }
-    static __device__ __forceinline__ void store(void* base, int64_t i, float4 v) {
-        const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
-        *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(base) + i) =
-            make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
-    }
-};
-
-// Rows lane_base .. lane_base+nrows-1 of the staged f32 tile -> global, four
-// consecutive columns per lane (cout % 4 == 0, so a lane's four columns are
-// all valid or all past `limit`).
-template <typename OutT, typename ResT, bool SILU, bool STATS>
-__device__ __forceinline__ void writeout_fast(const TcParams& p, uint32_t so_base, int ostride, int lane_base, int lane,
-                                              int64_t m0, int n0, int limit, int nrows, const float4 (&bias4)[2],
-                                              double (&s1)[2][4], double (&s2)[2][4]) {
-#pragma unroll 2
-    for (int rr = 0; rr < nrows; ++rr) {
-        const int row = lane_base + rr;
-        const int64_t r = m0 + row;
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-            const int lc = 128 * q + 4 * lane;
-            if (lc >= limit) continue;
-            float4 v;
-            asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
-                         : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                         : "r"(so_base + (uint32_t)((row * ostride + lc) * 4)));
-            v.x += bias4[q].x;
-            v.y += bias4[q].y;
-            v.z += bias4[q].z;
-            v.w += bias4[q].w;
-            if constexpr (!std::is_same<ResT, NoRes>::value) {
-                const float4 t = Vec4<ResT>::load(p.residual, (r >> p.res_shift) * p.cout + n0 + lc);
-                v.x += t.x;
-                v.y += t.y;
-                v.z += t.z;
-                v.w += t.w;
-            }
-            if constexpr (STATS) {
-                s1[q][0] += (double)v.x;
-                s2[q][0] += (double)v.x * v.x;
-                s1[q][1] += (double)v.y;
-                s2[q][1] += (double)v.y * v.y;
-                s1[q][2] += (double)v.z;
-                s2[q][2] += (double)v.z * v.z;
-                s1[q][3] += (double)v.w;
-                s2[q][3] += (double)v.w * v.w;
-            }
-            if constexpr (SILU) {
-                v.x = silu_f(v.x);
-                v.y = silu_f(v.y);
-                v.z = silu_f(v.z);
-                v.w = silu_f(v.w);
-            }
-            Vec4<OutT>::store(p.out, r * p.cout + n0 + lc, v);
-        }
-    }
-}
-
-// Any dtype / ragged width: element-wise.
-__device__ __forceinline__ void writeout_generic(const TcParams& p, const float* stage_out, int ostride, int lane_base,
-                                              int lane, int64_t m0, int n0, int limit, int nrows,
-                                              const float4 (&bias4)[2], bool stats, double (&s1)[2][4],
-                                              double (&s2)[2][4]) {
-    for (int rr = 0; rr < nrows; ++rr) {
-        const int row = lane_base + rr;
-        const int64_t r = m0 + row;
-        for (int q = 0; q < 2; ++q) {
-            const int lc0 = 128 * q + 4 * lane;
-            for (int j = 0; j < 4; ++j) {
-                const int lc = lc0 + j;
-                if (lc >= limit) break;
-                const int col = n0 + lc;
-                const float bj = j == 0 ? bias4[q].x : j == 1 ? bias4[q].y : j == 2 ? bias4[q].z : bias4[q].w;
-                float v = stage_out[(size_t)row * ostride + lc] + bj;
-                if (p.residual) v += load1(p.residual, p.res_dtype, (r >> p.res_shift) * p.cout + col);
-                if (stats) {
-                    s1[q][j] += (double)v;
-                    s2[q][j] += (double)v * v;
-                }
-                if (p.flags & S3DSP_EPI_SILU) v = silu_f(v);
-                store1(p.out, p.out_dtype, r * p.cout + col, v);
-            }
-        }
-    }
-}
 
 // ---------------------------------------------------------------------------
 // the kernel
@@ -609,7 +386,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr int kQ = 2;  // bn <= 256 -> at most two 128-column slabs
         const int limit = min(p.bn, p.cout - n0);  // valid columns of this tile
         float4 bias4[kQ];
-        double s1[kQ][4], s2[kQ][4];
 #pragma unroll
         for (int q = 0; q < kQ; ++q) {
             const int col = n0 + 128 * q + 4 * lane;
@@ -620,11 +396,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 bias4[q].z = col + 2 < p.cout ? __ldg(p.bias + col + 2) : 0.f;
                 bias4[q].w = col + 3 < p.cout ? __ldg(p.bias + col + 3) : 0.f;
             }
-#pragma unroll
-            for (int j = 0; j < 4; ++j) s1[q][j] = s2[q][j] = 0.0;
         }
         const int nrows = (int)min((int64_t)32, p.n_out - (m0 + lane_base));
         const uint32_t so_base = smem_u32(stage_out);
+        double* colp = reinterpret_cast<double*>(smem + (size_t)128 * ostride * 4);  // [4][bn][2]
+        double* colw = colp + (size_t)warp * p.bn * 2;
         // One compact loop body per (out dtype, residual dtype, SiLU, stats)
         // combination: a single generic body with every variant inlined runs
         // several times slower (instruction-cache misses).
@@ -635,7 +411,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         switch (sel) {
 #define S3DSP_WO(idx, OT, RT, SL, ST)                                                                            \
     case idx:                                                                                                \
-        writeout_fast<OT, RT, SL, ST>(p, so_base, ostride, lane_base, lane, m0, n0, limit, nrows, bias4, s1, s2); \
+        writeout_fast<OT, RT, SL, ST>(p, so_base, ostride, lane_base, lane, m0, n0, limit, nrows, bias4, colw); \
         break;
             S3DSP_WO(0, float, NoRes, false, false)
             S3DSP_WO(1, float, NoRes, false, true)
@@ -663,22 +439,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             S3DSP_WO(23, __nv_bfloat16, __nv_bfloat16, true, true)
 #undef S3DSP_WO
             default:
-                writeout_generic(p, stage_out, ostride, lane_base, lane, m0, n0, limit, nrows, bias4, stats, s1, s2);
+                writeout_generic(p, stage_out, ostride, lane_base, lane, m0, n0, limit, nrows, bias4, stats ? colw : nullptr);
         }
         if (stats) {
             // deterministic GroupNorm partials: per-warp column sums to smem,
             // then each group summed over warps and columns in a fixed order
-            double* colp = reinterpret_cast<double*>(smem + (size_t)128 * ostride * 4);  // [4][bn][2]
-#pragma unroll
-            for (int q = 0; q < kQ; ++q)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int lc = 128 * q + 4 * lane + j;
-                    if (lc < p.bn) {
-                        colp[((size_t)warp * p.bn + lc) * 2 + 0] = lc < limit ? s1[q][j] : 0.0;
-                        colp[((size_t)warp * p.bn + lc) * 2 + 1] = lc < limit ? s2[q][j] : 0.0;
-                    }
-                }
             asm volatile("bar.sync 1, 128;" ::: "memory");
             const int et = tid - kEpiWarp0 * 32;
             const int g_lo = n0 / gs;
@@ -710,21 +475,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         else
             asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tcols) : "memory");
     }
-}
-
-// ---------------------------------------------------------------------------
-// host side
-// ---------------------------------------------------------------------------
-PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    if (!fn) {
-        void* ptr = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-    }
-    return fn;
 }
 
 size_t smem_bytes(int stages, int bn) {
@@ -813,8 +563,10 @@ cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     p.status = ctx->d_status;
 
     const size_t smem = smem_bytes(stages, brows);
-    cudaError_t e = pair ? cudaFuncSetAttribute(conv_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
-                         : cudaFuncSetAttribute(conv_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    static std::atomic<uint64_t> optin_pair{0}, optin_single{0};
+    cudaError_t e = pair ? smem_optin((const void*)conv_tc_kernel<true>, ctx->device, optin_pair)
+                         : smem_optin((const void*)conv_tc_kernel<false>, ctx->device, optin_single);
+    if (e == cudaSuccess && smem > (size_t)kSmemOptIn) e = cudaErrorInvalidValue;
     if (e != cudaSuccess) return e;
     if (gn_partials) {
         e = cudaMemsetAsync(gn_partials, 0, sizeof(double) * 2 * (size_t)gn_groups * (size_t)tiles, ctx->stream);

@@ -6,6 +6,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
@@ -55,6 +56,18 @@ struct s3dsp_kmap {
 namespace s3dsp {
 
 constexpr int kTileRows = 128;  // rows per conv tile (tcgen05 M) == tile_mask granularity
+constexpr int kSmemOptIn = 232448;  // opt-in dynamic shared memory per block (227 KB)
+
+// Opt a kernel in to the full dynamic shared memory once per device (device
+// < 64); later calls, including ones made during a stream capture, skip the
+// attribute call.
+inline cudaError_t smem_optin(const void* fn, int device, std::atomic<uint64_t>& done) {
+    const uint64_t bit = 1ull << (device & 63);
+    if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+    const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemOptIn);
+    if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_acq_rel);
+    return e;
+}
 
 // error-buffer helpers (reference convention: include/sam3d.h:32-34)
 inline void clear_error(char* error, uint64_t cap) {
@@ -101,6 +114,12 @@ cudaError_t launch_conv_f32(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol
                             uint32_t flags, const float* pro_sub, const float* pro_mul,
                             const float* pro_add, double* gn_partials, int gn_groups);
 cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
+                           const __nv_bfloat16* in, int64_t n_in, int cin, int in_shift,
+                           const __nv_bfloat16* w, const float* bias, const void* residual,
+                           uint32_t res_dtype, int res_shift, void* out, uint32_t out_dtype,
+                           int64_t n_out, int cout, uint32_t flags, double* gn_partials,
+                           int gn_groups, char* error, uint64_t error_capacity, s3d_status* st);
+cudaError_t launch_conv_sk(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
                            const __nv_bfloat16* in, int64_t n_in, int cin, int in_shift,
                            const __nv_bfloat16* w, const float* bias, const void* residual,
                            uint32_t res_dtype, int res_shift, void* out, uint32_t out_dtype,

@@ -1,0 +1,285 @@
+// Device helpers shared by the tcgen05 convolution kernels: mbarriers with
+// bounded waits, TMA and cp.async copies, tcgen05 MMA / commit / TMEM loads,
+// and the typed, vectorised epilogue write-out (bias, residual, GroupNorm
+// partial sums, SiLU).
+#pragma once
+
+#include "s3dsp_internal.h"
+
+#include <cudaTypedefs.h>
+
+#include <type_traits>
+
+namespace s3dsp {
+namespace tc {
+
+constexpr unsigned long long kWaitNs = 2000000000ull;  // bounded mbarrier wait: 2 s
+
+// ---------------------------------------------------------------------------
+// PTX helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait. Returns false (and raises the CTA abort flag) on timeout or
+// when another role already aborted.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          uint32_t* status) {
+    if (mbar_try(bar, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try(bar, parity)) return true;
+        if ((it & 255u) == 0) {
+            if (*abort_flag) return false;
+            if (global_ns() - t0 > kWaitNs) {
+                *abort_flag = 1;
+                atomicOr(status, kErrPipelineTimeout);
+                return false;
+            }
+        }
+    }
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"((unsigned long long)map), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+// arrive on `bar` once all of this thread's prior cp.async copies have landed
+// (counts as one of the barrier's expected arrivals)
+__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// K-major operand in the 128-byte swizzle canonical layout: rows of 128 B,
+// 8-row (1024 B) swizzle atoms stacked along M/N (stride byte offset 1024),
+// descriptor version 1, layout type 2 (SWIZZLE_128B).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+    return (uint64_t)((addr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&f)[16]) {
+    uint32_t v[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr)
+        : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int j = 0; j < 16; ++j) f[j] = __uint_as_float(v[j]);
+}
+
+__device__ __forceinline__ float silu_f(float v) { return v / (1.0f + __expf(-v)); }
+
+__device__ __forceinline__ float load1(const void* p, uint32_t dt, int64_t i) {
+    if (dt == S3DSP_F32) return reinterpret_cast<const float*>(p)[i];
+    if (dt == S3DSP_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+    return __half2float(reinterpret_cast<const __half*>(p)[i]);
+}
+__device__ __forceinline__ void store1(void* p, uint32_t dt, int64_t i, float v) {
+    if (dt == S3DSP_F32)
+        reinterpret_cast<float*>(p)[i] = v;
+    else if (dt == S3DSP_BF16)
+        reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16(v);
+    else
+        reinterpret_cast<__half*>(p)[i] = __float2half(v);
+}
+
+
+// ---------------------------------------------------------------------------
+// epilogue write-out: typed vector access, one compact loop per variant
+// ---------------------------------------------------------------------------
+struct NoRes {};
+template <typename T>
+struct Vec4;
+template <>
+struct Vec4<float> {
+    static __device__ __forceinline__ float4 load(const void* base, int64_t i) {
+        return __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + i));
+    }
+    static __device__ __forceinline__ void store(void* base, int64_t i, float4 v) {
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(base) + i) = v;
+    }
+};
+template <>
+struct Vec4<__nv_bfloat16> {
+    static __device__ __forceinline__ float4 load(const void* base, int64_t i) {
+        const uint2 u = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(base) + i));
+        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+        const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+        return make_float4(a.x, a.y, b.x, b.y);
+    }
+    static __device__ __forceinline__ void store(void* base, int64_t i, float4 v) {
+        const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+        *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(base) + i) =
+            make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+    }
+};
+
+// Per-warp GroupNorm column sums -> colw[lc][2] (this warp's row of the
+// column-sum table; columns past `limit` get zeros).
+__device__ __forceinline__ void store_colsums(double* colw, int bn, int lane, int limit, const double (&s1)[2][4],
+                                              const double (&s2)[2][4]) {
+#pragma unroll
+    for (int q = 0; q < 2; ++q)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int lc = 128 * q + 4 * lane + j;
+            if (lc < bn) {
+                colw[lc * 2 + 0] = lc < limit ? s1[q][j] : 0.0;
+                colw[lc * 2 + 1] = lc < limit ? s2[q][j] : 0.0;
+            }
+        }
+}
+
+// Rows lane_base .. lane_base+nrows-1 of the staged f32 tile -> global, four
+// consecutive columns per lane (cout % 4 == 0, so a lane's four columns are
+// all valid or all past `limit`). STATS: the warp's per-column sums of the
+// values before SiLU go to colw.
+template <typename OutT, typename ResT, bool SILU, bool STATS, typename P>
+__device__ __forceinline__ void writeout_fast(const P& p, uint32_t so_base, int ostride, int lane_base, int lane,
+                                              int64_t m0, int n0, int limit, int nrows, const float4 (&bias4)[2],
+                                              double* colw) {
+    double s1[2][4], s2[2][4];
+    if constexpr (STATS) {
+#pragma unroll
+        for (int q = 0; q < 2; ++q)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) s1[q][j] = s2[q][j] = 0.0;
+    }
+#pragma unroll 2
+    for (int rr = 0; rr < nrows; ++rr) {
+        const int row = lane_base + rr;
+        const int64_t r = m0 + row;
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const int lc = 128 * q + 4 * lane;
+            if (lc >= limit) continue;
+            float4 v;
+            asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+                         : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                         : "r"(so_base + (uint32_t)((row * ostride + lc) * 4)));
+            v.x += bias4[q].x;
+            v.y += bias4[q].y;
+            v.z += bias4[q].z;
+            v.w += bias4[q].w;
+            if constexpr (!std::is_same<ResT, NoRes>::value) {
+                const float4 t = Vec4<ResT>::load(p.residual, (r >> p.res_shift) * p.cout + n0 + lc);
+                v.x += t.x;
+                v.y += t.y;
+                v.z += t.z;
+                v.w += t.w;
+            }
+            if constexpr (STATS) {
+                s1[q][0] += (double)v.x;
+                s2[q][0] += (double)v.x * v.x;
+                s1[q][1] += (double)v.y;
+                s2[q][1] += (double)v.y * v.y;
+                s1[q][2] += (double)v.z;
+                s2[q][2] += (double)v.z * v.z;
+                s1[q][3] += (double)v.w;
+                s2[q][3] += (double)v.w * v.w;
+            }
+            if constexpr (SILU) {
+                v.x = silu_f(v.x);
+                v.y = silu_f(v.y);
+                v.z = silu_f(v.z);
+                v.w = silu_f(v.w);
+            }
+            Vec4<OutT>::store(p.out, r * p.cout + n0 + lc, v);
+        }
+    }
+    if constexpr (STATS) store_colsums(colw, p.bn, lane, limit, s1, s2);
+}
+
+// Any dtype / ragged width: element-wise. colw as in writeout_fast (null: no
+// statistics).
+template <typename P>
+__device__ __forceinline__ void writeout_generic(const P& p, const float* stage_out, int ostride, int lane_base,
+                                                 int lane, int64_t m0, int n0, int limit, int nrows,
+                                                 const float4 (&bias4)[2], double* colw) {
+    double s1[2][4], s2[2][4];
+    for (int q = 0; q < 2; ++q)
+        for (int j = 0; j < 4; ++j) s1[q][j] = s2[q][j] = 0.0;
+    for (int rr = 0; rr < nrows; ++rr) {
+        const int row = lane_base + rr;
+        const int64_t r = m0 + row;
+        for (int q = 0; q < 2; ++q) {
+            const int lc0 = 128 * q + 4 * lane;
+            for (int j = 0; j < 4; ++j) {
+                const int lc = lc0 + j;
+                if (lc >= limit) break;
+                const int col = n0 + lc;
+                const float bj = j == 0 ? bias4[q].x : j == 1 ? bias4[q].y : j == 2 ? bias4[q].z : bias4[q].w;
+                float v = stage_out[(size_t)row * ostride + lc] + bj;
+                if (p.residual) v += load1(p.residual, p.res_dtype, (r >> p.res_shift) * p.cout + col);
+                if (colw) {
+                    s1[q][j] += (double)v;
+                    s2[q][j] += (double)v * v;
+                }
+                if (p.flags & S3DSP_EPI_SILU) v = silu_f(v);
+                store1(p.out, p.out_dtype, r * p.cout + col, v);
+            }
+        }
+    }
+    if (colw) store_colsums(colw, p.bn, lane, limit, s1, s2);
+}
+
+// cuTensorMapEncodeTiled through the runtime (no -lcuda)
+inline PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }
+    return fn;
+}
+
+
+}  // namespace tc
+}  // namespace s3dsp

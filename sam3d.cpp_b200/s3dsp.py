@@ -24,7 +24,7 @@ F32, BF16, F16 = 0, 1, 2
 PREC_F32_STRICT, PREC_BF16 = 0, 1
 LAYOUT_SLAT_ROW, LAYOUT_MESH_PACKED, LAYOUT_LINEAR, LAYOUT_SPCONV_1X1, LAYOUT_TRANSPOSED_2X2X2 = 0, 1, 2, 3, 4
 SENTINEL_SLAT_N, SENTINEL_MESH_NEG1 = 0, 1
-EPI_SILU, PRO_AFFINE_SILU, CONV_CTA_PAIR = 1, 2, 4
+EPI_SILU, PRO_AFFINE_SILU, CONV_CTA_PAIR, CONV_TILE128, CONV_STREAM_K = 1, 2, 4, 8, 16
 CONTEXT_DEFERRED_CHECKS = 1
 CONTEXT_OWN_STREAM = 2
 
@@ -34,7 +34,7 @@ EXPORTED = [
     "s3dsp_context_check", "s3dsp_hash_build", "s3dsp_hash_free", "s3dsp_hash_size",
     "s3dsp_hash_lookup", "s3dsp_kmap_build_subm3", "s3dsp_subdivide", "s3dsp_kmap_free",
     "s3dsp_kmap_rows", "s3dsp_kmap_export_dense", "s3dsp_kmap_pairs", "s3dsp_kmap_pairs_noalloc",
-    "s3dsp_weights_packed_bytes", "s3dsp_weights_pack", "s3dsp_gn_partials_count", "s3dsp_conv",
+    "s3dsp_weights_packed_bytes", "s3dsp_weights_pack", "s3dsp_gn_partials_count", "s3dsp_conv", "s3dsp_conv_kernel",
     "s3dsp_gn_stats", "s3dsp_gn_finalize", "s3dsp_channel_affine", "s3dsp_layer_norm",
     "s3dsp_convert", "s3dsp_slat_tables_build", "s3dsp_slat_tables_free", "s3dsp_slat_tables_coarse_rows",
     "s3dsp_slat_tables_coarse_kmap", "s3dsp_slat_tables_export", "s3dsp_slat_downsample", "s3dsp_slat_upsample",
@@ -88,6 +88,7 @@ def load(path: str = LIB_PATH):
         "s3dsp_weights_packed_bytes": (_i64, [_u32, _i32, _i64, _i64]),
         "s3dsp_weights_pack": (_u32, [_vp, _vp, _u32, _i32, _u32, _i32, _i64, _i64, _u32, _vp, _cp, _u64]),
         "s3dsp_gn_partials_count": (_i64, [_i64, _i64, _i32]),
+        "s3dsp_conv_kernel": (_cp, [_vp, _i64, _i32, _i64, _i64, _u32, _u32]),
         "s3dsp_conv": (_u32, [_vp, _vp, _i32, _u32, _vp, _u32, _i64, _i64, _i32, _vp, _vp, _vp, _u32, _i32,
                               _vp, _u32, _i64, _i64, _u32, _vp, _vp, _vp, _vp, _i32, _cp, _u64]),
         "s3dsp_gn_stats": (_u32, [_vp, _vp, _u32, _i64, _i64, _i32, _vp, _cp, _u64]),
@@ -264,6 +265,11 @@ class Context:
               precision, ptr(dst))
 
     # ---- conv ------------------------------------------------------------
+    def conv_kernel(self, n_out: int, kvol: int, cin: int, cout: int, precision: int, flags: int = 0) -> str:
+        """Name of the kernel s3dsp_conv launches for this shape."""
+        name = load().s3dsp_conv_kernel(self.handle, n_out, kvol, cin, cout, precision, flags)
+        return name.decode() if name else ""
+
     def conv(self, kmap: Kmap | None, kvol: int, precision: int, x, weight, bias, out, cout: int,
              in_shift: int = 0, residual=None, res_shift: int = 0, flags: int = 0, pro=None,
              gn_partials=None, gn_groups: int = 0, n_out: int | None = None):

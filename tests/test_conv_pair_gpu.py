@@ -42,7 +42,7 @@ def run(ctx, k, kvol, x, w, b, cout, n_out, single, reps=3, **kw):
     odt = kw.get("out_dtype", torch.float32)
     for _ in range(reps):
         out = torch.empty((n_out, cout), dtype=odt, device="cuda")
-        flags = kw.get("flags", 0) | (0 if single else s3dsp.CONV_CTA_PAIR)
+        flags = kw.get("flags", 0) | (s3dsp.CONV_TILE128 if single else s3dsp.CONV_CTA_PAIR)
         part = None
         if kw.get("gn"):
             part = torch.zeros(s3dsp.Context.gn_partials_count(n_out, cout, 32), dtype=torch.float64, device="cuda")
