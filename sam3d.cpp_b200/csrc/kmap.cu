@@ -1,13 +1,13 @@
 // K1 coordinate hash and K2 kernel-map construction.
 //
 // Hash: open addressing with linear probing over a power-of-two table of
-// 64-bit packed keys (load factor <= 1/2) plus a parallel int32 value array
-// holding the FIRST row of each key (atomicMin), which reproduces the
+// 16-byte slots {64-bit packed key, first row} (load factor <= 1/4). The row
+// is the FIRST row of each key (atomicMin), which reproduces the
 // std::map::emplace "first insert wins" rule of SlatTables::build
 // (src/objects_runtime/sparse_ops.cpp:119-124). Coordinates are read as one
-// int4 per row (coalesced 16-byte loads) and probes read two adjacent slots
-// per 16-byte load, so a probe sequence s0, s0+1, ... costs one load per two
-// slots. Every probe loop is bounded by the table size.
+// int4 per row (coalesced 16-byte loads) and a probe is one 16-byte load that
+// returns key and row together. Every probe loop is bounded by the table
+// size.
 //
 // Kernel maps are stored offset-major, nbr[o * n_out + r] (-1 = none), so the
 // conv's gather loader reads 128 consecutive output rows of one offset with
@@ -46,19 +46,16 @@ __device__ __forceinline__ unsigned long long mix64(unsigned long long k) {
 }
 
 struct HashView {
-    const unsigned long long* keys;
-    const int32_t* vals;
+    const ulonglong2* slots;
     unsigned long long mask;
 
     __device__ __forceinline__ int32_t find(unsigned long long key) const {
-        unsigned long long s = mix64(key) & mask & ~1ull;
-        for (unsigned long long p = 0; p <= mask; p += 2) {
-            const ulonglong2 kk = __ldg(reinterpret_cast<const ulonglong2*>(keys + s));
-            if (kk.x == key) return __ldg(vals + s);
-            if (kk.x == kEmptyKey) return -1;
-            if (kk.y == key) return __ldg(vals + s + 1);
-            if (kk.y == kEmptyKey) return -1;
-            s = (s + 2) & mask;
+        unsigned long long s = mix64(key) & mask;
+        for (unsigned long long p = 0; p <= mask; ++p) {
+            const ulonglong2 kv = __ldg(slots + s);
+            if (kv.x == key) return (int32_t)(uint32_t)kv.y;
+            if (kv.x == kEmptyKey) return -1;
+            s = (s + 1) & mask;
         }
         return -1;
     }
@@ -69,24 +66,32 @@ struct HashView {
     }
 };
 
-__global__ void hash_insert_kernel(const int4* __restrict__ coords, int64_t n,
-                                   unsigned long long* keys, int32_t* vals,
-                                   unsigned long long mask, int32_t reject_dups,
+// every slot empty: key all-ones, row INT32_MAX (the atomicMin identity)
+__global__ void hash_init_kernel(ulonglong2* __restrict__ slots, uint64_t cap) {
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < cap; i += (uint64_t)gridDim.x * blockDim.x)
+        slots[i] = make_ulonglong2(kEmptyKey, 0x7fffffffull);
+}
+
+// inserts row i and keeps a copy of its coordinates in the hash
+__global__ void hash_insert_kernel(const int4* __restrict__ coords, int64_t n, int4* __restrict__ own,
+                                   ulonglong2* slots, unsigned long long mask, int32_t reject_dups,
                                    uint32_t* status) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
         const int4 c = coords[i];
+        own[i] = c;
         unsigned long long key;
         if (!pack_key(c.x, c.y, c.z, c.w, key)) {
             atomicOr(status, kErrCoordRange);
             continue;
         }
-        unsigned long long s = mix64(key) & mask & ~1ull;
+        unsigned long long s = mix64(key) & mask;
         bool placed = false;
         for (unsigned long long p = 0; p <= mask; ++p) {
-            const unsigned long long prev = atomicCAS(keys + s, kEmptyKey, key);
+            unsigned long long* kp = reinterpret_cast<unsigned long long*>(slots + s);
+            const unsigned long long prev = atomicCAS(kp, kEmptyKey, key);
             if (prev == kEmptyKey || prev == key) {
-                atomicMin(vals + s, (int32_t)i);
+                atomicMin(reinterpret_cast<int*>(kp + 1), (int)i);  // low half of the row word
                 if (prev == key) {
                     atomicAdd(status + 1, 1u);
                     if (reject_dups) atomicOr(status, kErrDuplicate);
@@ -100,15 +105,6 @@ __global__ void hash_insert_kernel(const int4* __restrict__ coords, int64_t n,
     }
 }
 
-__global__ void hash_self_kernel(const int4* __restrict__ coords, int64_t n, HashView h,
-                                 int32_t* __restrict__ self_row) {
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int4 c = coords[i];
-        self_row[i] = h.find_coord(c.x, c.y, c.z, c.w);
-    }
-}
-
 __global__ void hash_lookup_kernel(const int4* __restrict__ q, int64_t m, HashView h,
                                    int32_t* __restrict__ rows) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < m;
@@ -118,30 +114,53 @@ __global__ void hash_lookup_kernel(const int4* __restrict__ q, int64_t m, HashVi
     }
 }
 
-// Submanifold 3x3x3 map, offset-major. grid.y = offset. Whole warps iterate
-// together so the tile-mask ballot always sees 32 lanes.
-__global__ void kmap_subm3_kernel(const int4* __restrict__ coords, const int32_t* __restrict__ self_row,
-                                  int64_t n, HashView h, int32_t* __restrict__ nbr,
-                                  uint32_t* __restrict__ tile_mask) {
+// Submanifold 3x3x3 map, offset-major: one thread per (output row, offset),
+// block (tile, offset) = 128 rows of one offset, so the nbr stores are
+// coalesced and the block sets its tile's offset bit with one atomicOr.
+// Each thread issues two independent probes: the offset neighbour and the
+// row's own key. The own-key probe finds the first row holding this key; a
+// duplicate row (not the first) gets no neighbours, as SlatTables::build
+// iterates the unique map entries (sparse_ops.cpp:129-139).
+__device__ __forceinline__ int32_t probe_rest(const HashView& h, unsigned long long key, unsigned long long slot) {
+    for (unsigned long long p = 1; p <= h.mask; ++p) {
+        slot = (slot + 1) & h.mask;
+        const ulonglong2 q = __ldg(h.slots + slot);
+        if (q.x == key) return (int32_t)(uint32_t)q.y;
+        if (q.x == kEmptyKey) return -1;
+    }
+    return -1;
+}
+
+__global__ void __launch_bounds__(kTileRows) kmap_subm3_kernel(const int4* __restrict__ coords, int64_t n, HashView h,
+                                                               int32_t* __restrict__ nbr,
+                                                               uint32_t* __restrict__ tile_mask) {
     const int o = blockIdx.y;
     const int dx = o / 9 - 1, dy = (o / 3) % 3 - 1, dz = o % 3 - 1;
-    const int lane = threadIdx.x & 31;
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t base = blockIdx.x * (int64_t)blockDim.x + (threadIdx.x & ~31); base < n; base += stride) {
-        const int64_t r = base + lane;
-        int32_t res = -1;
-        if (r < n) {
-            // only the first row of a duplicated key gets neighbours
-            // (sparse_ops.cpp:129-139 iterates the unique map entries)
-            if (self_row[r] == (int32_t)r) {
-                const int4 c = coords[r];
-                res = h.find_coord(c.x, c.y + dx, c.z + dy, c.w + dz);
-            }
-            nbr[o * n + r] = res;
+    const int64_t r = (int64_t)blockIdx.x * kTileRows + threadIdx.x;
+    int32_t res = -1;
+    if (r < n) {
+        const int4 c = __ldg(coords + r);
+        unsigned long long kn, ks;
+        const bool okn = pack_key(c.x, c.y + dx, c.z + dy, c.w + dz, kn);
+        const bool oks = pack_key(c.x, c.y, c.z, c.w, ks);
+        const unsigned long long sn = okn ? (mix64(kn) & h.mask) : 0, ss = oks ? (mix64(ks) & h.mask) : 0;
+        const ulonglong2 qn = okn ? __ldg(h.slots + sn) : make_ulonglong2(kEmptyKey, 0);
+        const ulonglong2 qs = oks ? __ldg(h.slots + ss) : make_ulonglong2(kEmptyKey, 0);
+        int32_t self = -1;
+        if (qs.x == ks && oks) self = (int32_t)(uint32_t)qs.y;
+        else if (oks && qs.x != kEmptyKey) self = probe_rest(h, ks, ss);
+        if (self == (int32_t)r && okn) {
+            if (qn.x == kn) res = (int32_t)(uint32_t)qn.y;
+            else if (qn.x != kEmptyKey) res = probe_rest(h, kn, sn);
         }
-        const unsigned any = __ballot_sync(0xffffffffu, res >= 0);
-        if (lane == 0 && any) atomicOr(tile_mask + (base / kTileRows), 1u << o);
+        nbr[o * n + r] = res;
     }
+    __shared__ int any;
+    if (threadIdx.x == 0) any = 0;
+    __syncthreads();
+    if (__ballot_sync(0xffffffffu, res >= 0) && (threadIdx.x & 31) == 0) any = 1;
+    __syncthreads();
+    if (threadIdx.x == 0 && any) atomicOr(tile_mask + blockIdx.x, 1u << o);
 }
 
 // Child geometry of MeshSubdivideTables (sparse_ops.cpp:346-365): for child
@@ -319,7 +338,7 @@ inline int grid_for(int64_t n, int threads, int sm_count) {
     return (int)(g < 1 ? 1 : g);
 }
 
-HashView view_of(const s3dsp_hash* h) { return HashView{h->keys, h->vals, h->capacity - 1}; }
+HashView view_of(const s3dsp_hash* h) { return HashView{h->slots, h->capacity - 1}; }
 
 bool g_adj_uploaded[64] = {};
 
@@ -391,27 +410,23 @@ extern "C" S3DSP_API s3d_status s3dsp_hash_build(s3dsp_context* ctx, const int32
     if (!h) return fail(error, error_capacity, S3D_OUT_OF_MEMORY, "hash allocation");
     h->n = n;
     h->reject_duplicates = reject_duplicates;
+    // load factor <= 1/4: a warp waits for its longest probe sequence, and the
+    // expected longest of 32 linear-probe sequences grows fast with the load
     uint64_t cap = 64;
-    while (cap < 2 * (uint64_t)n) cap <<= 1;
+    while (cap < 4 * (uint64_t)n) cap <<= 1;
     h->capacity = cap;
     cudaStream_t st = ctx->stream;
-    cudaError_t e = cudaMallocAsync(&h->keys, cap * 8, st);
-    if (e == cudaSuccess) e = cudaMallocAsync(&h->vals, cap * 4, st);
+    cudaError_t e = cudaMallocAsync(&h->slots, cap * 16, st);
     if (e == cudaSuccess) e = cudaMallocAsync(&h->coords, (size_t)n * 16, st);
-    if (e == cudaSuccess) e = cudaMallocAsync(&h->self_row, (size_t)n * 4, st);
-    if (e == cudaSuccess) e = cudaMemsetAsync(h->keys, 0xff, cap * 8, st);
-    if (e == cudaSuccess) e = cudaMemsetAsync(h->vals, 0x7f, cap * 4, st);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(h->coords, d_coords, (size_t)n * 16, cudaMemcpyDeviceToDevice, st);
     if (e != cudaSuccess) {
         s3dsp_hash_free(ctx, h);
         return cuda_fail(error, error_capacity, e, "hash allocation");
     }
     const int threads = 256;
+    hash_init_kernel<<<grid_for((int64_t)cap, threads, ctx->sm_count), threads, 0, st>>>(h->slots, cap);
     hash_insert_kernel<<<grid_for(n, threads, ctx->sm_count), threads, 0, st>>>(
-        reinterpret_cast<const int4*>(h->coords), n, h->keys, h->vals, cap - 1, reject_duplicates,
-        ctx->d_status);
-    hash_self_kernel<<<grid_for(n, threads, ctx->sm_count), threads, 0, st>>>(
-        reinterpret_cast<const int4*>(h->coords), n, view_of(h), h->self_row);
+        reinterpret_cast<const int4*>(d_coords), n, reinterpret_cast<int4*>(h->coords), h->slots, cap - 1,
+        reject_duplicates, ctx->d_status);
     e = cudaGetLastError();
     if (e != cudaSuccess) {
         s3dsp_hash_free(ctx, h);
@@ -431,10 +446,8 @@ extern "C" S3DSP_API s3d_status s3dsp_hash_build(s3dsp_context* ctx, const int32
 extern "C" S3DSP_API void s3dsp_hash_free(s3dsp_context* ctx, s3dsp_hash* h) {
     if (!h) return;
     cudaStream_t st = ctx ? ctx->stream : nullptr;
-    if (h->keys) cudaFreeAsync(h->keys, st);
-    if (h->vals) cudaFreeAsync(h->vals, st);
+    if (h->slots) cudaFreeAsync(h->slots, st);
     if (h->coords) cudaFreeAsync(h->coords, st);
-    if (h->self_row) cudaFreeAsync(h->self_row, st);
     delete h;
 }
 
@@ -466,12 +479,9 @@ extern "C" S3DSP_API s3d_status s3dsp_kmap_build_subm3(s3dsp_context* ctx, const
     cudaError_t e;
     s3dsp_kmap* k = new_kmap(ctx, h->n, h->n, 27, &e);
     if (!k) return cuda_fail(error, error_capacity, e, "kmap allocation");
-    const int threads = 256;
-    int gx = (int)((h->n + threads - 1) / threads);
-    const int cap = ctx->sm_count * 8;
-    if (gx > cap) gx = cap;
-    kmap_subm3_kernel<<<dim3(gx, 27), threads, 0, ctx->stream>>>(
-        reinterpret_cast<const int4*>(h->coords), h->self_row, h->n, view_of(h), k->nbr, k->tile_mask);
+    const int64_t tiles = (h->n + kTileRows - 1) / kTileRows;
+    kmap_subm3_kernel<<<dim3((unsigned)tiles, 27), kTileRows, 0, ctx->stream>>>(
+        reinterpret_cast<const int4*>(h->coords), h->n, view_of(h), k->nbr, k->tile_mask);
     e = cudaGetLastError();
     if (e != cudaSuccess) {
         s3dsp_kmap_free(ctx, k);

@@ -108,26 +108,48 @@ __global__ void channel_affine_kernel(const void* __restrict__ x, uint32_t xd, i
 }
 
 // vectorised variant: f32 in, bf16 out, c % 8 == 0
-__global__ void channel_affine_f32_bf16_kernel(const float4* __restrict__ x, int64_t n, int c,
-                                               const float* __restrict__ sub, const float* __restrict__ mul,
-                                               const float* __restrict__ add, int silu, uint4* __restrict__ y) {
-    const int64_t total8 = n * c / 8;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total8; i += (int64_t)gridDim.x * blockDim.x) {
-        const float4 a = x[2 * i], b = x[2 * i + 1];
-        const int ch = (int)((i * 8) % c);
-        float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-        uint32_t w[4];
+// f32 -> affine (+SiLU) -> bf16, 8 channels per item, 4 items per thread per
+// iteration with all loads issued before any use (bytes in flight per SM is
+// what bounds a streaming kernel). (x - sub) * mul + add is evaluated as
+// written, with the per-channel vectors read as float4.
+__global__ void channel_affine_f32_bf16_kernel(const float4* __restrict__ x, int64_t total8, uint32_t c8,
+                                               const float4* __restrict__ sub, const float4* __restrict__ mul,
+                                               const float4* __restrict__ add, int silu, uint4* __restrict__ y) {
+    constexpr int U = 4;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < total8; i0 += stride * U) {
+        float4 a[U], b[U];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            v[q] = (v[q] - sub[ch + q]) * mul[ch + q] + add[ch + q];
-            if (silu) v[q] = silu_f(v[q]);
+        for (int u = 0; u < U; ++u) {
+            const int64_t i = i0 + u * stride;
+            if (i < total8) {
+                a[u] = __ldcs(x + 2 * i);
+                b[u] = __ldcs(x + 2 * i + 1);
+            }
         }
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * q], v[2 * q + 1]);
-            w[q] = *reinterpret_cast<const uint32_t*>(&h);
+        for (int u = 0; u < U; ++u) {
+            const int64_t i = i0 + u * stride;
+            if (i >= total8) break;
+            const uint32_t q8 = (uint32_t)((uint64_t)i % c8);  // 8-channel group within the row
+            const float4 s0 = __ldg(sub + 2 * q8), s1 = __ldg(sub + 2 * q8 + 1);
+            const float4 m0 = __ldg(mul + 2 * q8), m1 = __ldg(mul + 2 * q8 + 1);
+            const float4 d0 = __ldg(add + 2 * q8), d1 = __ldg(add + 2 * q8 + 1);
+            float v[8] = {(a[u].x - s0.x) * m0.x + d0.x, (a[u].y - s0.y) * m0.y + d0.y, (a[u].z - s0.z) * m0.z + d0.z,
+                          (a[u].w - s0.w) * m0.w + d0.w, (b[u].x - s1.x) * m1.x + d1.x, (b[u].y - s1.y) * m1.y + d1.y,
+                          (b[u].z - s1.z) * m1.z + d1.z, (b[u].w - s1.w) * m1.w + d1.w};
+            if (silu) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) v[q] = silu_f(v[q]);
+            }
+            uint32_t w[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * q], v[2 * q + 1]);
+                w[q] = *reinterpret_cast<const uint32_t*>(&h);
+            }
+            y[i] = make_uint4(w[0], w[1], w[2], w[3]);
         }
-        y[i] = make_uint4(w[0], w[1], w[2], w[3]);
     }
 }
 
@@ -169,11 +191,22 @@ __global__ void convert_kernel(const void* __restrict__ x, uint32_t xd, void* __
         st_f(y, yd, i, ld_f(x, xd, i));
 }
 
+// f32 -> bf16, 4 elements per item, 4 items per thread per iteration (loads first)
 __global__ void convert_f32_bf16_kernel(const float4* __restrict__ x, uint2* __restrict__ y, int64_t count4) {
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count4; i += (int64_t)gridDim.x * blockDim.x) {
-        const float4 v = x[i];
-        const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
-        y[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+    constexpr int U = 4;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < count4; i0 += stride * U) {
+        float4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (i0 + u * stride < count4) v[u] = __ldg(x + i0 + u * stride);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t i = i0 + u * stride;
+            if (i >= count4) break;
+            const __nv_bfloat162 a = __floats2bfloat162_rn(v[u].x, v[u].y), b = __floats2bfloat162_rn(v[u].z, v[u].w);
+            y[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+        }
     }
 }
 
@@ -276,9 +309,14 @@ extern "C" S3DSP_API s3d_status s3dsp_channel_affine(s3dsp_context* ctx, const v
         return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "bad shape/dtype");
     if (n == 0) return S3D_OK;
     S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
-    if (xd == S3DSP_F32 && yd == S3DSP_BF16 && c % 8 == 0 && !((uintptr_t)x & 15) && !((uintptr_t)y & 15)) {
-        channel_affine_f32_bf16_kernel<<<grid_for(n * c / 8, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
-            reinterpret_cast<const float4*>(x), n, (int)c, sub, mul, add, silu, reinterpret_cast<uint4*>(y));
+    const bool vec_ok = !((uintptr_t)x & 15) && !((uintptr_t)y & 15) && !((uintptr_t)sub & 15) &&
+                        !((uintptr_t)mul & 15) && !((uintptr_t)add & 15);
+    if (xd == S3DSP_F32 && yd == S3DSP_BF16 && c % 8 == 0 && vec_ok) {
+        const int64_t total8 = n * c / 8;
+        channel_affine_f32_bf16_kernel<<<grid_for((total8 + 3) / 4, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
+            reinterpret_cast<const float4*>(x), total8, (uint32_t)(c / 8), reinterpret_cast<const float4*>(sub),
+            reinterpret_cast<const float4*>(mul), reinterpret_cast<const float4*>(add), silu,
+            reinterpret_cast<uint4*>(y));
     } else {
         channel_affine_kernel<<<grid_for(n * c, 256, ctx->sm_count), 256, 0, ctx->stream>>>(x, xd, n, (int)c, sub, mul,
                                                                                           add, silu, y, yd);
@@ -313,7 +351,7 @@ extern "C" S3DSP_API s3d_status s3dsp_convert(s3dsp_context* ctx, const void* x,
     if (count == 0) return S3D_OK;
     S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
     if (xd == S3DSP_F32 && yd == S3DSP_BF16 && count % 4 == 0 && !((uintptr_t)x & 15) && !((uintptr_t)y & 7))
-        convert_f32_bf16_kernel<<<grid_for(count / 4, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
+        convert_f32_bf16_kernel<<<grid_for((count / 4 + 3) / 4, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
             reinterpret_cast<const float4*>(x), reinterpret_cast<uint2*>(y), count / 4);
     else
         convert_kernel<<<grid_for(count, 256, ctx->sm_count), 256, 0, ctx->stream>>>(x, xd, y, yd, count);

@@ -36,11 +36,9 @@ struct s3dsp_context {
 
 struct s3dsp_hash {
     int64_t n = 0;
-    uint64_t capacity = 0;               // power of two >= 2n
-    unsigned long long* keys = nullptr;  // [capacity]
-    int32_t* vals = nullptr;             // [capacity] first row per key
+    uint64_t capacity = 0;               // power of two >= 4n
+    ulonglong2* slots = nullptr;         // [capacity] {packed key, first row in the low 32 bits}
     int32_t* coords = nullptr;           // [n, 4] own copy
-    int32_t* self_row = nullptr;         // [n] first row holding the same key
     int32_t reject_duplicates = 0;
 };
 
