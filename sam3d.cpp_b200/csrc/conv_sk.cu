@@ -48,10 +48,14 @@ constexpr int kMaxBWarps = 4;
 constexpr int kMmaWarp = 20;
 constexpr int kThreads = 21 * 32;
 constexpr int kRows = 256;            // output rows per work tile
-constexpr int kAStage = kRows * 128;  // bytes: 256 rows x 64 bf16
-constexpr int kAHalf = 128 * 128;     // second accumulator's rows start here
+constexpr int kKC = 64;  // channels per pipeline stage (128-byte rows, SWIZZLE_128B; 32 measured slower)
+constexpr int kAStage = kRows * 2 * kKC;  // bytes: 256 gathered rows x kKC bf16
+constexpr int kAHalf = 128 * 2 * kKC;     // second accumulator's rows start here
 constexpr int kMaxKvol = 27;
 constexpr int kSmemMax = kSmemOptIn;
+// Each stage's "full" barrier may be split in kFullSplit barriers, one per
+// group of producer warps; splitting measured slower on B200.
+constexpr int kFullSplit = 1;
 
 struct SkParams {
     const __nv_bfloat16* in;
@@ -60,7 +64,7 @@ struct SkParams {
     const int32_t* nbr;         // [kvol][n_out] or null (identity)
     const uint32_t* tile_mask;  // [128-row tiles] or null
     int kvol;
-    int kchunks;                // 64-channel reduction chunks per offset
+    int kchunks;                // kKC-channel reduction chunks per offset
     int cout_pad;               // packed weight rows per offset
     int bn;
     int nb;                     // weight TMA loads per stage
@@ -110,7 +114,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int S = p.stages;
-    const int bstage = p.bn * 128;
+    const int bstage = p.bn * 2 * kKC;
     const int ostride = p.bn + 4;  // staged f32 row stride (floats)
     // layout: region0 = max(ring A | ring B, epilogue tile | GN column sums),
     // then sidx, barriers, tmem holder, flags
@@ -120,7 +124,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
     uint8_t* sB = smem + (size_t)S * kAStage;
     int32_t* sidx = reinterpret_cast<int32_t*>(smem + (ring > epi ? ring : epi));  // [kvol][256]
     uint64_t* full = reinterpret_cast<uint64_t*>(sidx + kMaxKvol * kRows);
-    uint64_t* empty = full + S;
+    uint64_t* empty = full + S * kFullSplit;
     uint64_t* accum = empty + S;
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(accum + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
@@ -134,7 +138,8 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
 
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
-            mbar_init(smem_u32(full + s), kEpiThreads + p.nb);
+            for (int j = 0; j < kFullSplit; ++j)
+                mbar_init(smem_u32(full + s * kFullSplit + j), kEpiThreads / kFullSplit + (j == 0 ? p.nb : 0));
             mbar_init(smem_u32(empty + s), 1);
         }
         mbar_init(smem_u32(accum), 1);
@@ -187,8 +192,10 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
                 sidx[i] = s < 0 ? -1 : (s >> p.in_shift);
             }
             prod_bar();
-            const int c16 = tid & 7;  // 16-byte chunk of a 128-byte row
-            const int rg = tid >> 3;  // rows rg + 64 * i
+            constexpr int kCpr = kKC / 8;         // 16-byte chunks per row
+            constexpr int kRowStep = 512 / kCpr;  // rows covered by one pass of the 512 threads
+            const int c16 = tid & (kCpr - 1);
+            const int rg = tid / kCpr;  // rows rg + kRowStep * i
             uint32_t mrem = mask;
             int o = 0;
             for (int j = 0; j < T; ++j) {
@@ -204,24 +211,24 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
                     prod_ok = false;
                     break;
                 }
-                const int k0 = kc * 64 + c16 * 8;
+                const int k0 = kc * kKC + c16 * 8;
                 const uint32_t a_base = smem_u32(sA + (size_t)s * kAStage);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int row = rg + 64 * i;
+                for (int i = 0; i < kRows / kRowStep; ++i) {
+                    const int row = rg + kRowStep * i;
                     const int32_t src = sidx[o * kRows + row];
                     const bool valid = src >= 0 && k0 < p.cin;
                     const void* g = valid ? (const void*)(p.in + (int64_t)src * p.cin + k0) : (const void*)p.in;
-                    cp_async_16(a_base + row * 128 + ((c16 ^ (row & 7)) << 4), g, valid ? 16u : 0u);
+                    cp_async_16(a_base + row * (2 * kKC) + ((c16 ^ kmajor_swz<kKC>(row)) << 4), g, valid ? 16u : 0u);
                 }
-                cp_async_arrive_noinc(smem_u32(full + s));
+                cp_async_arrive_noinc(smem_u32(full + s * kFullSplit + warp / (kProdWarps / kFullSplit)));
             }
         } else if (warp < kBWarp0 + kMaxBWarps) {
             // ============ weight TMA issuers ============
             const int jw = warp - kBWarp0;
             if (lane == 0 && jw < p.nb) {
                 const int rows = p.bn / p.nb;
-                const uint32_t bytes = (uint32_t)rows * 128;
+                const uint32_t bytes = (uint32_t)rows * 2 * kKC;
                 uint32_t mrem = mask;
                 int o = 0;
                 for (int j = 0; j < T; ++j) {
@@ -234,9 +241,9 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
                         mrem &= mrem - 1;
                     }
                     if (!mbar_wait(smem_u32(empty + s), ph ^ 1u, abort_flag, p.status)) break;
-                    const uint32_t fb = smem_u32(full + s);
+                    const uint32_t fb = smem_u32(full + s * kFullSplit);
                     mbar_arrive_tx(fb, bytes);
-                    tma_load_2d(smem_u32(sB + (size_t)s * bstage + (size_t)jw * rows * 128), &wmap, kc * 64,
+                    tma_load_2d(smem_u32(sB + (size_t)s * bstage + (size_t)jw * rows * 2 * kKC), &wmap, kc * kKC,
                                 o * p.cout_pad + n0 + jw * rows, fb);
                 }
             }
@@ -249,19 +256,18 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
                     const uint32_t pit = it + (uint32_t)j;
                     const int s = (int)(pit % (uint32_t)S);
                     const uint32_t ph = (pit / (uint32_t)S) & 1u;
-                    if (!mbar_wait(smem_u32(full + s), ph, abort_flag, p.status)) {
-                        ok = false;
-                        break;
-                    }
+                    for (int jf = 0; jf < kFullSplit && ok; ++jf)
+                        ok = mbar_wait(smem_u32(full + s * kFullSplit + jf), ph, abort_flag, p.status);
+                    if (!ok) break;
                     tc_fence_after();
                     const uint32_t a0 = smem_u32(sA + (size_t)s * kAStage);
                     const uint32_t b0 = smem_u32(sB + (size_t)s * bstage);
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) {
+                    for (int k = 0; k < kKC / 16; ++k) {
                         const uint32_t acc = (j > 0 || k > 0) ? 1u : 0u;
-                        const uint64_t bd = sw128_desc(b0 + 32 * k);
-                        mma_bf16(tmem, sw128_desc(a0 + 32 * k), bd, p.idesc, acc);
-                        mma_bf16(tmem + p.thalf, sw128_desc(a0 + kAHalf + 32 * k), bd, p.idesc, acc);
+                        const uint64_t bd = kmajor_desc<kKC>(b0 + 32 * k);
+                        mma_bf16(tmem, kmajor_desc<kKC>(a0 + 32 * k), bd, p.idesc, acc);
+                        mma_bf16(tmem + p.thalf, kmajor_desc<kKC>(a0 + kAHalf + 32 * k), bd, p.idesc, acc);
                     }
                     mma_commit(smem_u32(empty + s));
                 }
@@ -449,10 +455,10 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
 }
 
 size_t sk_smem_bytes(int stages, int bn) {
-    const size_t ring = (size_t)stages * (kAStage + bn * 128);
+    const size_t ring = (size_t)stages * (kAStage + bn * 2 * kKC);
     const size_t epi = (size_t)128 * (bn + 4) * 4 + (size_t)kProdWarps * bn * 16;
     return 1024 /*align slack*/ + (ring > epi ? ring : epi) + (size_t)kMaxKvol * kRows * 4 /*sidx*/ +
-           (2 * stages + 1) * 8 + 16;
+           ((kFullSplit + 1) * stages + 1) * 8 + 16;
 }
 
 }  // namespace
@@ -472,20 +478,20 @@ cudaError_t launch_conv_sk(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     const int cin_pad = (cin + 63) / 64 * 64;
     const int bn = tc_pick_bn(cout);
     const int nnb = cout_pad / bn;
-    const int kchunks = cin_pad / 64;
+    const int kchunks = cin_pad / kKC;
     const int64_t tiles = (n_out + 127) / 128;
     const int64_t work_tiles = (n_out + kRows - 1) / kRows * nnb;
     const int64_t units = work_tiles * kvol;
 
-    int stages = 8;
+    int stages = 16;
     while (stages > 2 && sk_smem_bytes(stages, bn) > (size_t)kSmemMax) --stages;
     const size_t smem = sk_smem_bytes(stages, bn);
     if (smem > (size_t)kSmemMax) {
         *st = fail(error, error_capacity, S3D_INTERNAL_ERROR, "conv tile of %d columns does not fit shared memory", bn);
         return cudaErrorInvalidValue;
     }
-    // at least ~16 reduction steps per CTA before splitting tiles further
-    const int64_t min_units = (16 + kchunks - 1) / kchunks;
+    // at least ~32 reduction steps (of kKC channels) per CTA before splitting tiles further
+    const int64_t min_units = (32 + kchunks - 1) / kchunks;
     int64_t g = (units + min_units - 1) / min_units;
     if (g > ctx->sm_count) g = ctx->sm_count;
     if (g < 1) g = 1;
@@ -503,10 +509,11 @@ cudaError_t launch_conv_sk(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     {
         const cuuint64_t dims[2] = {(cuuint64_t)cin_pad, (cuuint64_t)kvol * (cuuint64_t)cout_pad};
         const cuuint64_t strides[1] = {(cuuint64_t)cin_pad * 2};
-        const cuuint32_t box[2] = {64, (cuuint32_t)(bn / nb)};
+        const cuuint32_t box[2] = {(cuuint32_t)kKC, (cuuint32_t)(bn / nb)};
         const cuuint32_t estr[2] = {1, 1};
         CUresult cr = encode(&wmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)w, dims, strides, box, estr,
-                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             kKC == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (cr != CUDA_SUCCESS) {
             *st = fail(error, error_capacity, S3D_INTERNAL_ERROR, "weight tensor map failed (%d)", (int)cr);

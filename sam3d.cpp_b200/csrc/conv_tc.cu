@@ -47,8 +47,11 @@ constexpr int kMaxBWarps = 4;
 constexpr int kMmaWarp = 20;
 constexpr int kThreads = 21 * 32;
 constexpr int kEpiWarp0 = 0;        // first of the 4 epilogue warps
-constexpr int kAStage = 128 * 128;  // bytes: 128 rows x 64 bf16
 constexpr int kMaxKvol = 27;
+// Each stage's "full" barrier may be split in kFullSplit barriers, one per
+// group of producer warps. Measured on B200 (config-2 conv, 85 us with one
+// barrier): 4 barriers 115 us, 16 barriers 469 us; one barrier per stage.
+constexpr int kFullSplit = 1;
 
 struct TcParams {
     const __nv_bfloat16* in;
@@ -155,7 +158,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
 // tile, so weight traffic per output row halves. The leader (rank 0) issues
 // the MMAs; the peer's weight TMA completes on the leader's barrier and the
 // peer's gathered rows are relayed to it by a remote mbarrier arrive.
-template <bool kPair>
+template <bool kPair, int KC>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_tc_kernel(const TcParams p, const __grid_constant__ CUtensorMap wmap) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -163,7 +166,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int S = p.stages;
     const int brows = kPair ? p.bn / 2 : p.bn;  // weight rows held by this CTA
-    const int bstage = brows * 128;
+    constexpr int kAStage = 128 * 2 * KC;  // bytes: 128 rows x KC bf16
+    const int bstage = brows * 2 * KC;
     // layout (offsets from the 1024-aligned base): ring A | ring B | sidx |
     // barriers | tmem holder, abort flag. The epilogue reuses the ring for
     // its f32 output tile followed by the f64 GroupNorm column sums.
@@ -171,7 +175,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* sB = smem + (size_t)S * kAStage;
     int32_t* sidx = reinterpret_cast<int32_t*>(sB + (size_t)S * bstage);  // [kvol][128]
     uint64_t* full = reinterpret_cast<uint64_t*>(sidx + kMaxKvol * 128);
-    uint64_t* empty = full + S;
+    constexpr int kFS = kPair ? 1 : kFullSplit;  // the pair relay arrives on one barrier
+    uint64_t* empty = full + S * kFS;
     uint64_t* accum = empty + S;
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(accum + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
@@ -196,7 +201,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
     mask &= (p.kvol >= 32) ? 0xffffffffu : ((1u << p.kvol) - 1u);
-    const int kchunks = (p.cin + 63) / 64;
+    const int kchunks = (p.cin + 63) / 64 * (64 / KC);  // KC-channel reduction chunks per offset
     const int T = __popc(mask) * kchunks;
     const uint32_t tcols = p.bn <= 32 ? 32u : (p.bn <= 64 ? 64u : (p.bn <= 128 ? 128u : 256u));
 
@@ -205,8 +210,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s = 0; s < S; ++s) {
             // single CTA: cp.async threads + weight issuers; pair leader: + the
             // peer's relay arrival; pair peer: its own cp.async threads only
-            const uint32_t cnt = !kPair ? kProdWarps * 32 + p.nb : leader ? kProdWarps * 32 + p.nb + 1 : kProdWarps * 32;
-            mbar_init(smem_u32(full + s), cnt);
+            for (int j = 0; j < kFS; ++j) {
+                uint32_t cnt = kProdWarps * 32 / kFS;
+                if (j == 0) cnt += !kPair ? p.nb : leader ? p.nb + 1 : 0;
+                mbar_init(smem_u32(full + s * kFS + j), cnt);
+            }
             mbar_init(smem_u32(empty + s), 1);
         }
         mbar_init(smem_u32(accum), 1);
@@ -244,8 +252,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool prod_ok = true;
     if (warp < kProdWarps) {
         // ================= A producers: cp.async gathers =================
-        const int c16 = tid & 7;  // 16-byte chunk within a 128-byte row
-        const int rg = tid >> 3;  // rows rg and rg + 64
+        constexpr int kCpr = KC / 8;          // 16-byte chunks per row
+        constexpr int kRowStep = 512 / kCpr;  // rows covered by one pass of the 512 threads
+        const int c16 = tid & (kCpr - 1);
+        const int rg = tid / kCpr;  // rows rg, rg + kRowStep, ...
         uint32_t mrem = mask;
         int o = 0;
         for (int it = 0; it < T; ++it) {
@@ -260,17 +270,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 prod_ok = false;
                 break;
             }
-            const int k0 = kc * 64 + c16 * 8;
+            const int k0 = kc * KC + c16 * 8;
             const uint32_t a_base = smem_u32(sA + (size_t)s * kAStage);
 #pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const int row = rg + 64 * i;
+            for (int i = 0; i < 128 / kRowStep; ++i) {
+                const int row = rg + kRowStep * i;
                 const int32_t src = sidx[o * 128 + row];
                 const bool valid = src >= 0 && k0 < p.cin;
                 const void* g = valid ? (const void*)(p.in + (int64_t)src * p.cin + k0) : (const void*)p.in;
-                cp_async_16(a_base + row * 128 + ((c16 ^ (row & 7)) << 4), g, valid ? 16u : 0u);
+                cp_async_16(a_base + row * (2 * KC) + ((c16 ^ kmajor_swz<KC>(row)) << 4), g, valid ? 16u : 0u);
             }
-            cp_async_arrive_noinc(smem_u32(full + s));
+            cp_async_arrive_noinc(smem_u32(full + s * kFS + warp / (kProdWarps / kFS)));
         }
         asm volatile("cp.async.wait_all;" ::: "memory");
     } else if (warp < kBWarp0 + kMaxBWarps) {
@@ -280,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t mrem = mask;
             int o = 0;
             const int rows = brows / p.nb;
-            const uint32_t bytes = (uint32_t)rows * 128;
+            const uint32_t bytes = (uint32_t)rows * 2 * KC;
             for (int it = 0; it < T; ++it) {
                 const int s = it % S;
                 const uint32_t ph = (uint32_t)(it / S) & 1u;
@@ -290,16 +300,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mrem &= mrem - 1;
                 }
                 if (!mbar_wait(smem_u32(empty + s), ph ^ 1u, abort_flag, p.status)) break;
-                const uint32_t fb = smem_u32(full + s);
-                const uint32_t dst = smem_u32(sB + (size_t)s * bstage + (size_t)j * rows * 128);
+                const uint32_t fb = smem_u32(full + s * kFS);
+                const uint32_t dst = smem_u32(sB + (size_t)s * bstage + (size_t)j * rows * 2 * KC);
                 const int y = o * p.cout_pad + n0 + (int)rank * brows + j * rows;
                 if (!kPair) {
                     mbar_arrive_tx(fb, bytes);
-                    tma_load_2d(dst, &wmap, kc * 64, y, fb);
+                    tma_load_2d(dst, &wmap, kc * KC, y, fb);
                 } else {
                     // the leader expects both CTAs' slice j; both complete on its barrier
                     if (leader) mbar_arrive_tx(fb, 2 * bytes);
-                    tma_load_2d_pair(dst, &wmap, kc * 64, y, map_to_rank(fb, 0));
+                    tma_load_2d_pair(dst, &wmap, kc * KC, y, map_to_rank(fb, 0));
                 }
             }
         }
@@ -309,11 +319,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int it = 0; it < T; ++it) {
                 const int s = it % S;
                 const uint32_t ph = (uint32_t)(it / S) & 1u;
-                if (!mbar_wait(smem_u32(full + s), ph, abort_flag, p.status)) break;
+                if (!mbar_wait(smem_u32(full + s * kFS), ph, abort_flag, p.status)) break;
                 // the rows were written through the generic proxy; the leader's
                 // tensor core reads them through the async proxy
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                mbar_arrive_remote(map_to_rank(smem_u32(full + s), 0));
+                mbar_arrive_remote(map_to_rank(smem_u32(full + s * kFS), 0));
             }
         } else if (lane == 0) {
             // ================= MMA issuer =================
@@ -321,8 +331,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int it = 0; it < T; ++it) {
                 const int s = it % S;
                 const uint32_t ph = (uint32_t)(it / S) & 1u;
-                const bool got = kPair ? mbar_wait_cluster(smem_u32(full + s), ph, abort_flag, p.status)
-                                       : mbar_wait(smem_u32(full + s), ph, abort_flag, p.status);
+                bool got = true;
+                for (int j = 0; j < kFS && got; ++j)
+                    got = kPair ? mbar_wait_cluster(smem_u32(full + s * kFS + j), ph, abort_flag, p.status)
+                                : mbar_wait(smem_u32(full + s * kFS + j), ph, abort_flag, p.status);
                 if (!got) {
                     ok = false;
                     break;
@@ -332,15 +344,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t b0 = smem_u32(sB + (size_t)s * bstage);
                 if (kPair) {
 #pragma unroll
-                    for (int k = 0; k < 4; ++k)
-                        mma_bf16_pair(tmem, sw128_desc(a0 + 32 * k), sw128_desc(b0 + 32 * k), p.idesc,
+                    for (int k = 0; k < KC / 16; ++k)
+                        mma_bf16_pair(tmem, kmajor_desc<KC>(a0 + 32 * k), kmajor_desc<KC>(b0 + 32 * k), p.idesc,
                                       (it > 0 || k > 0) ? 1u : 0u);
                     mma_commit_pair(smem_u32(empty + s));                       // this CTA's stage
                     mma_commit_pair(map_to_rank(smem_u32(empty + s), 1));      // the peer's stage
                 } else {
 #pragma unroll
-                    for (int k = 0; k < 4; ++k)
-                        mma_bf16(tmem, sw128_desc(a0 + 32 * k), sw128_desc(b0 + 32 * k), p.idesc,
+                    for (int k = 0; k < KC / 16; ++k)
+                        mma_bf16(tmem, kmajor_desc<KC>(a0 + 32 * k), kmajor_desc<KC>(b0 + 32 * k), p.idesc,
                                  (it > 0 || k > 0) ? 1u : 0u);
                     mma_commit(smem_u32(empty + s));
                 }
@@ -477,8 +489,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-size_t smem_bytes(int stages, int bn) {
-    return 1024 /*align slack*/ + (size_t)stages * (kAStage + bn * 128) + (2 * stages + 1) * 8 + 16 +
+// stage = 128 gathered rows + brows weight rows, KC bf16 each
+size_t stage_bytes(int brows, int kc) { return (size_t)(128 + brows) * 2 * kc; }
+size_t smem_bytes(int stages, int brows, int kc) {
+    return 1024 /*align slack*/ + (size_t)stages * stage_bytes(brows, kc) + ((kFullSplit + 1) * stages + 1) * 8 + 16 +
            kMaxKvol * 128 * 4 /*sidx*/;
 }
 
@@ -508,10 +522,14 @@ cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     // CTA pairs need an even row-tile count (the last pair may hold one empty tile)
     const bool pair = (flags & S3DSP_CONV_CTA_PAIR) != 0;
     const int brows = pair ? bn / 2 : bn;
-    int stages = (int)((200 * 1024) / (kAStage + brows * 128));
-    if (stages > 8) stages = 8;
+    // 64-channel stages: 32-channel stages (twice as many for the same shared
+    // memory) measured slower on B200 (config-2 conv 119-123 us vs 81-85 us):
+    // a stage has a fixed cost beyond its bytes
+    const int kc = 64;
+    int stages = (int)((200 * 1024) / stage_bytes(brows, kc));
+    if (stages > 16) stages = 16;
     // the epilogue reuses the ring for a 128 x (bn + 4) f32 tile plus 4 x bn x 2 f64 column sums
-    while ((size_t)stages * (kAStage + brows * 128) < (size_t)128 * (bn + 4) * 4 + (size_t)4 * bn * 16) ++stages;
+    while ((size_t)stages * stage_bytes(brows, kc) < (size_t)128 * (bn + 4) * 4 + (size_t)4 * bn * 16) ++stages;
     (void)n_in;
 
     auto encode = get_encode_fn();
@@ -525,10 +543,10 @@ cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     {
         const cuuint64_t dims[2] = {(cuuint64_t)cin_pad, (cuuint64_t)kvol * (cuuint64_t)cout_pad};
         const cuuint64_t strides[1] = {(cuuint64_t)cin_pad * 2};
-        const cuuint32_t box[2] = {64, (cuuint32_t)(brows / nb)};
+        const cuuint32_t box[2] = {(cuuint32_t)kc, (cuuint32_t)(brows / nb)};
         const cuuint32_t estr[2] = {1, 1};
         CUresult cr = encode(&wmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)w, dims, strides, box, estr,
-                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, kc == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (cr != CUDA_SUCCESS) {
             *st = fail(error, error_capacity, S3D_INTERNAL_ERROR, "weight tensor map failed (%d)", (int)cr);
@@ -562,10 +580,10 @@ cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     p.gn_groups = gn_groups;
     p.status = ctx->d_status;
 
-    const size_t smem = smem_bytes(stages, brows);
+    const size_t smem = smem_bytes(stages, brows, kc);
     static std::atomic<uint64_t> optin_pair{0}, optin_single{0};
-    cudaError_t e = pair ? smem_optin((const void*)conv_tc_kernel<true>, ctx->device, optin_pair)
-                         : smem_optin((const void*)conv_tc_kernel<false>, ctx->device, optin_single);
+    cudaError_t e = pair ? smem_optin((const void*)conv_tc_kernel<true, 64>, ctx->device, optin_pair)
+                         : smem_optin((const void*)conv_tc_kernel<false, 64>, ctx->device, optin_single);
     if (e == cudaSuccess && smem > (size_t)kSmemOptIn) e = cudaErrorInvalidValue;
     if (e != cudaSuccess) return e;
     if (gn_partials) {
@@ -574,7 +592,7 @@ cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     }
     if (!pair) {
         const dim3 grid((unsigned)tiles, (unsigned)(cout_pad / bn));
-        conv_tc_kernel<false><<<grid, kThreads, smem, ctx->stream>>>(p, wmap);
+        conv_tc_kernel<false, 64><<<grid, kThreads, smem, ctx->stream>>>(p, wmap);
         return cudaGetLastError();
     }
     cudaLaunchConfig_t cfg = {};
@@ -589,7 +607,7 @@ cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, conv_tc_kernel<true>, p, wmap);
+    e = cudaLaunchKernelEx(&cfg, conv_tc_kernel<true, 64>, p, wmap);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }

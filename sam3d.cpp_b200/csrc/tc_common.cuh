@@ -86,6 +86,26 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
     return (uint64_t)((addr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
+// K-major operand tile of KC bf16 per row (KC = 64: 128-byte rows, SWIZZLE_128B;
+// KC = 32: 64-byte rows, SWIZZLE_64B, 8-row groups 512 bytes apart). A K=16
+// step advances the start address by 32 bytes in either layout.
+template <int KC>
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t addr) {
+    static_assert(KC == 32 || KC == 64, "KC");
+    if constexpr (KC == 64) {
+        return sw128_desc(addr);
+    } else {
+        return (uint64_t)((addr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(512 >> 4) << 32) |
+               ((uint64_t)1 << 46) | ((uint64_t)4 << 61);
+    }
+}
+// 16-byte chunk index XOR of the matching swizzle for row `row`
+template <int KC>
+__device__ __forceinline__ int kmajor_swz(int row) {
+    if constexpr (KC == 64) return row & 7;
+    else return (row >> 1) & 3;
+}
+
 __device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
