@@ -176,8 +176,9 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     cfg = workloads.config2(seed=0)
-    if rank > 0:  # every rank its own object (independent objects, weak scaling)
-        cfg["coords"] = workloads.ellipsoid_shell(64, rank)
+    if rank > 0:
+        # every rank its own object of the config-2 shape (its own features):
+        # independent objects, fixed work per GPU (weak scaling)
         cfg["feats"] = workloads.normal((len(cfg["coords"]), cfg["channels"]), 1000 + rank)
     # one non-default stream for everything: the library context, torch's
     # copies and the L2 flush, and the CUDA-graph capture of a step
@@ -202,7 +203,8 @@ def run_ours(args, rank, world, local_rank):
     stream.synchronize()
     marks = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(7)]
     graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
+    # thread-local capture: NCCL's watchdog thread may query events meanwhile
+    with torch.cuda.graph(graph, stream=stream, capture_error_mode="thread_local"):
         path.step(marks)
     for _ in range(args.warmup):
         graph.replay()
@@ -301,6 +303,107 @@ def run_ours(args, rank, world, local_rank):
 
 
 # ---------------------------------------------------------------------------
+# config 5b: one large volume split in Morton slabs, NCCL halo exchange
+# ---------------------------------------------------------------------------
+VOLUME_RES, VOLUME_THICKNESS, VOLUME_C, VOLUME_LAYERS = 512, 4.0, 128, 8  # ~2.5M voxels
+
+
+def run_volume(args, rank, world, local_rank):
+    """Config 5b: a 512^3 ellipsoid shell (thickness 4 voxels, ~2.5M active
+    voxels), C = 128, 8 bf16 subm conv layers (+SiLU). Each rank owns a
+    Morton slab; before every layer the one-voxel halo is swapped with one
+    all-to-all (NCCL), then the rank convolves its own rows. Strong scaling:
+    the volume is fixed, ranks split it."""
+    import torch
+    import s3dsp
+    import shard
+    import workloads
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    stream = torch.cuda.Stream(device)
+    torch.cuda.set_stream(stream)
+    ctx = s3dsp.Context(local_rank, stream=stream.cuda_stream, flags=s3dsp.CONTEXT_DEFERRED_CHECKS)
+    coords = workloads.ellipsoid_shell(VOLUME_RES, 0, thickness=VOLUME_THICKNESS)
+    n, c = len(coords), VOLUME_C
+    plan = shard.plan_halos(coords, world)[rank]
+    h = ctx.hash_build(torch.from_numpy(plan.shard_coords(coords)).to(device))
+    k = ctx.kmap_subm3_rows(h, plan.n_own)
+    P = s3dsp.PREC_BF16
+    ws, bs = [], []
+    for i in range(VOLUME_LAYERS):
+        w = torch.empty(s3dsp.Context.packed_bytes(P, 27, c, c), dtype=torch.uint8, device=device)
+        ctx.weights_pack(torch.from_numpy(workloads.conv_weight_slat(c, c, 100 + i)), s3dsp.LAYOUT_SLAT_ROW, 27, c, c,
+                         P, w)
+        ws.append(w)
+        bs.append(torch.from_numpy(workloads.normal((c,), 200 + i, 0.1)).to(device))
+    rows = plan.n_own + plan.n_ghost
+    gen = torch.Generator(device=device).manual_seed(1000 + rank)
+    xa = torch.randn((rows, c), generator=gen, device=device).to(torch.bfloat16)
+    xb = torch.zeros_like(xa)
+    kernel = ctx.conv_kernel(plan.n_own, 27, c, c, P)
+
+    def step(times=None):
+        cur, nxt = xa, xb
+        for li in range(VOLUME_LAYERS):
+            e = [torch.cuda.Event(enable_timing=True) for _ in range(3)] if times is not None else None
+            if e:
+                e[0].record(stream)
+            shard.exchange_halo(cur, plan)
+            if e:
+                e[1].record(stream)
+            ctx.conv(k, 27, P, cur, ws[li], bs[li], nxt[:plan.n_own], c, flags=s3dsp.EPI_SILU)
+            if e:
+                e[2].record(stream)
+                times.append(e)
+            cur, nxt = nxt, cur
+
+    for _ in range(args.warmup):
+        step()
+    stream.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.3)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    per_layer = []
+    for i in range(args.steps):
+        starts[i].record(stream)
+        step(per_layer)
+        ends[i].record(stream)
+    stream.synchronize()
+    clocks = sampler.stop()
+    dev_ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends))
+    halo_ms = float(np.mean([e[0].elapsed_time(e[1]) for e in per_layer]))
+    conv_ms = float(np.mean([e[1].elapsed_time(e[2]) for e in per_layer]))
+    ctx.check()
+    vals = torch.tensor([dev_ms, halo_ms, conv_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX)
+    dev_ms, halo_ms, conv_ms = vals.tolist()
+    if rank != 0:
+        return None
+    units = float(n) * VOLUME_LAYERS * args.steps
+    hbm, tflops, tflops_sus, peak_src = load_peaks()
+    return {
+        "metric": "active-voxel outputs/s (C=128 subm conv, one volume split in Morton slabs)",
+        "value": units / (dev_ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded 512^3 ellipsoid shell, random features and weights)",
+        "config": {"workload": f"config5b: {VOLUME_RES}^3 shell (thickness {VOLUME_THICKNESS}) {n} voxels, C={c}, "
+                               f"{VOLUME_LAYERS} subm conv layers, Morton slabs + NCCL halo all-to-all",
+                   "voxels": n, "own_rows_rank0": plan.n_own, "ghost_rows_rank0": plan.n_ghost,
+                   "parallelism": f"morton-slabs{world}", "conv_kernel": kernel},
+        "breakdown_ms_per_layer": {"halo_exchange_max_rank": halo_ms, "conv_max_rank": conv_ms},
+        "gpu_launches": VOLUME_LAYERS * args.steps * (2 if world > 1 else 1),
+        "clocks": clocks,
+    }
+
+
+# ---------------------------------------------------------------------------
 # CPU path (reference arm and cpu_baseline)
 # ---------------------------------------------------------------------------
 def cpu_step(cfg, threads):
@@ -357,6 +460,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="config2", choices=["config2", "volume"],
+                    help="config2: the headline (default); volume: config 5b, one volume split across ranks")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -370,7 +475,7 @@ def main():
             torch.cuda.set_device(local_rank)
             torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                                  device_id=torch.device("cuda", local_rank))
-        line = run_ours(args, rank, world, local_rank)
+        line = (run_volume if args.workload == "volume" else run_ours)(args, rank, world, local_rank)
         if world > 1:
             import torch
             torch.distributed.barrier()

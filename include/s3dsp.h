@@ -132,6 +132,13 @@ S3DSP_API s3d_status s3dsp_hash_lookup(s3dsp_context *ctx, const s3dsp_hash *has
 S3DSP_API s3d_status s3dsp_kmap_build_subm3(s3dsp_context *ctx, const s3dsp_hash *hash,
                                             s3dsp_kmap **out, char *error,
                                             uint64_t error_capacity);
+/* The same map for the hash's first n_out rows only, gathering from all of
+ * its rows (inputs: the n rows of the hash). Used by a volume split across
+ * GPUs: a shard's own voxels come first, its halo (ghost) voxels after them.
+ * No reference counterpart. */
+S3DSP_API s3d_status s3dsp_kmap_build_subm3_rows(s3dsp_context *ctx, const s3dsp_hash *hash,
+                                                 int64_t n_out, s3dsp_kmap **out, char *error,
+                                                 uint64_t error_capacity);
 /* Stride-2 subdivide of a parent set: MeshSubdivideTables::build
  * (sparse_ops.cpp:272-404). Writes the 8*n child coords (child row =
  * parent*8 + xb*4 + yb*2 + zb, coords 2p + bits) to d_child_coords [8n, 4]

@@ -6,29 +6,36 @@ using namespace s3dsp;
 
 namespace {
 
-// BF16 kernel choice. The 256-row stream-K kernel moves fewer bytes per MAC
-// but pays a fix-up for every split tile and a pipeline refill per tile; it
-// wins once there are a few waves of 128-row tiles (B200 sweep of 64^3..256^3
-// shells at C = 128 and 256: 267 tiles on 148 SMs favours 128-row tiles, 473
-// and more favour stream-K).
-bool use_stream_k(const s3dsp_context* ctx, int64_t n_out, uint32_t flags) {
+// BF16 kernel choice by estimated time, in units of one wave of 128-row
+// tiles (every SM running one full tile). 128-row tiles: ceil(tiles / SMs)
+// waves. Stream-K (256-row tiles split evenly over the SMs): a fixed ~0.55
+// wave for the split-tile fix-up and pipeline refills, plus 1.525 / kvol of a
+// wave per (256-row tile, offset) unit and SM. Fitted to a B200 sweep of
+// 64^3..256^3 shells at C = 128 and 256 (15k-242k rows); a quarter-empty
+// second wave is where stream-K wins most (155 tiles: 2 waves vs ~1.35).
+// Maps with few offsets (linear layers) always use 128-row tiles.
+bool use_stream_k(const s3dsp_context* ctx, int64_t n_out, int32_t kvol, uint32_t flags) {
     if (flags & (S3DSP_CONV_TILE128 | S3DSP_CONV_CTA_PAIR)) return false;
     if (flags & S3DSP_CONV_STREAM_K) return true;
+    if (kvol < 8) return false;
+    const double sms = (double)ctx->sm_count;
     const int64_t tiles = (n_out + 127) / 128;
-    return tiles * 2 >= (int64_t)ctx->sm_count * 5;
+    const double waves128 = (double)((tiles + ctx->sm_count - 1) / ctx->sm_count);
+    const double units = (double)((n_out + 255) / 256) * kvol;
+    const double est_sk = 0.55 + (units / sms) * 1.525 / kvol;
+    return est_sk < 0.95 * waves128;
 }
 
 }  // namespace
 
 extern "C" S3DSP_API const char* s3dsp_conv_kernel(const s3dsp_context* ctx, int64_t n_out, int32_t kvol, int64_t cin,
                                                    int64_t cout, uint32_t precision, uint32_t flags) {
-    (void)kvol;
     (void)cin;
     (void)cout;
     if (!ctx) return nullptr;
     if (precision == S3DSP_PREC_F32_STRICT) return "conv_f32_kernel";
     if (precision != S3DSP_PREC_BF16) return nullptr;
-    return use_stream_k(ctx, n_out, flags) ? "conv_sk_kernel" : "conv_tc_kernel";
+    return use_stream_k(ctx, n_out, kvol, flags) ? "conv_sk_kernel" : "conv_tc_kernel";
 }
 
 extern "C" S3DSP_API s3d_status s3dsp_conv(s3dsp_context* ctx, const s3dsp_kmap* kmap, int32_t kvol,
@@ -95,7 +102,7 @@ extern "C" S3DSP_API s3d_status s3dsp_conv(s3dsp_context* ctx, const s3dsp_kmap*
             return fail(error, error_capacity, S3D_INVALID_ARGUMENT,
                         "BF16 needs cin %% 8 == 0 and 16-byte aligned in/weight/out/residual");
         s3d_status st = S3D_OK;
-        const bool tile128 = !use_stream_k(ctx, n_out, flags);
+        const bool tile128 = !use_stream_k(ctx, n_out, kvol, flags);
         if (tile128)
             e = launch_conv_tc(ctx, kmap, kvol, (const __nv_bfloat16*)in, n_in, (int)cin, in_shift,
                                (const __nv_bfloat16*)weight, bias, residual, res_dtype, res_shift, out, out_dtype,

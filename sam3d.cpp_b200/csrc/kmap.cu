@@ -469,19 +469,22 @@ extern "C" S3DSP_API s3d_status s3dsp_hash_lookup(s3dsp_context* ctx, const s3ds
     return S3D_OK;
 }
 
-extern "C" S3DSP_API s3d_status s3dsp_kmap_build_subm3(s3dsp_context* ctx, const s3dsp_hash* h,
-                                                       s3dsp_kmap** out, char* error,
-                                                       uint64_t error_capacity) {
+extern "C" S3DSP_API s3d_status s3dsp_kmap_build_subm3_rows(s3dsp_context* ctx, const s3dsp_hash* h, int64_t n_out,
+                                                            s3dsp_kmap** out, char* error, uint64_t error_capacity) {
     clear_error(error, error_capacity);
     if (!ctx || !h || !out) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
     *out = nullptr;
+    if (n_out <= 0 || n_out > h->n)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "n_out %lld outside 1..%lld", (long long)n_out,
+                    (long long)h->n);
     S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
     cudaError_t e;
-    s3dsp_kmap* k = new_kmap(ctx, h->n, h->n, 27, &e);
+    s3dsp_kmap* k = new_kmap(ctx, n_out, h->n, 27, &e);
     if (!k) return cuda_fail(error, error_capacity, e, "kmap allocation");
-    const int64_t tiles = (h->n + kTileRows - 1) / kTileRows;
+    const int64_t tiles = (n_out + kTileRows - 1) / kTileRows;
+    // output rows are the hash's first n_out rows; inputs are all its rows
     kmap_subm3_kernel<<<dim3((unsigned)tiles, 27), kTileRows, 0, ctx->stream>>>(
-        reinterpret_cast<const int4*>(h->coords), h->n, view_of(h), k->nbr, k->tile_mask);
+        reinterpret_cast<const int4*>(h->coords), n_out, view_of(h), k->nbr, k->tile_mask);
     e = cudaGetLastError();
     if (e != cudaSuccess) {
         s3dsp_kmap_free(ctx, k);
@@ -489,6 +492,16 @@ extern "C" S3DSP_API s3d_status s3dsp_kmap_build_subm3(s3dsp_context* ctx, const
     }
     *out = k;
     return S3D_OK;
+}
+
+extern "C" S3DSP_API s3d_status s3dsp_kmap_build_subm3(s3dsp_context* ctx, const s3dsp_hash* h,
+                                                       s3dsp_kmap** out, char* error,
+                                                       uint64_t error_capacity) {
+    if (!h) {
+        clear_error(error, error_capacity);
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
+    }
+    return s3dsp_kmap_build_subm3_rows(ctx, h, h->n, out, error, error_capacity);
 }
 
 extern "C" S3DSP_API s3d_status s3dsp_subdivide(s3dsp_context* ctx, const s3dsp_hash* parents,

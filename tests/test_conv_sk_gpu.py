@@ -151,8 +151,10 @@ def test_sk_identity_linear(ctx, n):
 def test_kernel_choice(ctx):
     P = s3dsp.PREC_BF16
     sms = torch.cuda.get_device_properties(0).multi_processor_count
-    assert ctx.conv_kernel(1000, 27, 256, 256, P) == "conv_tc_kernel"
-    assert ctx.conv_kernel(128 * 3 * sms, 27, 256, 256, P) == "conv_sk_kernel"
+    assert ctx.conv_kernel(128 * sms - 5, 27, 256, 256, P) == "conv_tc_kernel"   # one full wave
+    assert ctx.conv_kernel(128 * sms + 900, 27, 256, 256, P) == "conv_sk_kernel"  # a thin second wave
+    assert ctx.conv_kernel(128 * 8 * sms, 27, 256, 256, P) == "conv_sk_kernel"
+    assert ctx.conv_kernel(128 * 8 * sms, 1, 256, 256, P) == "conv_tc_kernel"     # linear layers
     assert ctx.conv_kernel(1000, 27, 256, 256, P, s3dsp.CONV_STREAM_K) == "conv_sk_kernel"
     assert ctx.conv_kernel(128 * 3 * sms, 27, 256, 256, P, s3dsp.CONV_TILE128) == "conv_tc_kernel"
     assert ctx.conv_kernel(1000, 27, 256, 256, s3dsp.PREC_F32_STRICT) == "conv_f32_kernel"
