@@ -404,6 +404,83 @@ def run_volume(args, rank, world, local_rank):
 
 
 # ---------------------------------------------------------------------------
+# config 5a: a batch of independent objects through config 4, sharded by object
+# ---------------------------------------------------------------------------
+OBJECTS, OBJECT_RES = 64, 64
+
+
+def run_objects(args, rank, world, local_rank):
+    """Config 5a: 64 ellipsoid shells at 64^3 (random axes, seeds 0..63), each
+    through the config-4 stack (bf16). Objects are dealt to ranks largest
+    first (no collective on the data path). Strong scaling: the batch is
+    fixed; a step is one pass over the whole batch."""
+    import torch
+    import s3dsp
+    import shard
+    import stack
+    import workloads
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    stream = torch.cuda.Stream(device)
+    torch.cuda.set_stream(stream)
+    ctx = s3dsp.Context(local_rank, stream=stream.cuda_stream, flags=s3dsp.CONTEXT_DEFERRED_CHECKS)
+    sizes = [len(workloads.ellipsoid_shell(OBJECT_RES, i)) for i in range(OBJECTS)]
+    mine = shard.assign_objects(sizes, world)[rank]
+    st = stack.Config4Stack(s3dsp, ctx, stack.config4_params(0), s3dsp.PREC_BF16, device)
+    objs = []
+    for i in mine:
+        co = workloads.ellipsoid_shell(OBJECT_RES, i)
+        lat = workloads.normal((len(co), stack.LATENT), 5000 + i)
+        objs.append((torch.from_numpy(co).to(device), torch.from_numpy(lat).to(device)))
+    units_rank = sum(stack.units(sizes[i]) for i in mine)
+
+    def step():
+        for co, lat in objs:
+            st.forward(co, lat)
+
+    for _ in range(args.warmup):
+        step()
+    stream.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.3)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for i in range(args.steps):
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    stream.synchronize()
+    clocks = sampler.stop()
+    dev_ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends))
+    ctx.check()
+    vals = torch.tensor([dev_ms], dtype=torch.float64, device=device)
+    units = torch.tensor([float(units_rank) * args.steps], dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX)
+        torch.distributed.all_reduce(units, op=torch.distributed.ReduceOp.SUM)
+    dev_ms = vals.item()
+    total_units = units.item()
+    if rank != 0:
+        return None
+    return {
+        "metric": "active-voxel outputs/s (config-4 stack over a batch of 64 objects, sharded by object)",
+        "value": total_units / (dev_ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (64 seeded 64^3 ellipsoid shells with random axes, random latents and weights)",
+        "config": {"workload": "config5a: 64 objects x config 4 (Linear 8->256, 4 GN res blocks @256, subdivide "
+                               "->128 + 2 blocks, subdivide ->64 + 2 blocks, Linear ->32)",
+                   "objects": OBJECTS, "voxels_total": int(sum(sizes)), "objects_rank0": len(mine),
+                   "parallelism": f"objects-dp{world} (largest-first assignment)"},
+        "clocks": clocks,
+    }
+
+
+# ---------------------------------------------------------------------------
 # CPU path (reference arm and cpu_baseline)
 # ---------------------------------------------------------------------------
 def cpu_step(cfg, threads):
@@ -460,8 +537,9 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="config2", choices=["config2", "volume"],
-                    help="config2: the headline (default); volume: config 5b, one volume split across ranks")
+    ap.add_argument("--workload", default="config2", choices=["config2", "volume", "objects"],
+                    help="config2: the headline (default); volume: config 5b, one volume split across ranks; "
+                         "objects: config 5a, 64 objects through config 4 sharded by object")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -475,7 +553,8 @@ def main():
             torch.cuda.set_device(local_rank)
             torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                                  device_id=torch.device("cuda", local_rank))
-        line = (run_volume if args.workload == "volume" else run_ours)(args, rank, world, local_rank)
+        runner = {"config2": run_ours, "volume": run_volume, "objects": run_objects}[args.workload]
+        line = runner(args, rank, world, local_rank)
         if world > 1:
             import torch
             torch.distributed.barrier()

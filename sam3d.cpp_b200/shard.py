@@ -1,4 +1,10 @@
-"""One large voxel volume split across GPUs (Morton-ordered slabs + halo).
+"""Splitting work across GPUs: independent objects, and one large volume.
+
+Objects (`assign_objects`): whole objects are dealt to ranks, largest first,
+each to the rank with the least voxels so far (longest-processing-time
+first); objects never talk to each other, so there is no collective.
+
+One large volume (Morton-ordered slabs + halo):
 
 The volume's active voxels are sorted by their 3D Morton code and cut into
 `world` contiguous ranges of (nearly) equal voxel count; rank r owns range r.
@@ -21,6 +27,18 @@ from __future__ import annotations
 from dataclasses import dataclass
 
 import numpy as np
+
+def assign_objects(sizes, world: int) -> list[list[int]]:
+    """Object indices per rank: largest first, each to the least-loaded rank
+    (ties: lowest rank). Deterministic, so every rank computes the same split."""
+    load = [0] * world
+    out = [[] for _ in range(world)]
+    for i in sorted(range(len(sizes)), key=lambda j: (-int(sizes[j]), j)):
+        r = min(range(world), key=lambda q: (load[q], q))
+        out[r].append(i)
+        load[r] += int(sizes[i])
+    return out
+
 
 _OFFSETS = np.array([(dx, dy, dz) for dx in (-1, 0, 1) for dy in (-1, 0, 1) for dz in (-1, 0, 1)
                      if (dx, dy, dz) != (0, 0, 0)], dtype=np.int64)

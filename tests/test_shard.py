@@ -22,6 +22,21 @@ def test_morton_interleave():
     assert code[4] == 0b011101110
 
 
+def test_assign_objects_lpt():
+    sizes = [5, 9, 1, 7, 3, 8, 2, 6]
+    parts = shard.assign_objects(sizes, 3)
+    assert sorted(i for p in parts for i in p) == list(range(len(sizes)))
+    loads = [sum(sizes[i] for i in p) for p in parts]
+    assert max(loads) - min(loads) <= max(sizes)
+    assert parts == shard.assign_objects(sizes, 3)  # deterministic
+    assert shard.assign_objects(sizes, 1) == [sorted(range(8), key=lambda j: -sizes[j])]
+    # 64 shells over 8 ranks: within a few percent of perfect balance
+    import workloads
+    sz = [len(workloads.ellipsoid_shell(32, s)) for s in range(64)]
+    loads = [sum(sz[i] for i in p) for p in shard.assign_objects(sz, 8)]
+    assert max(loads) / (sum(sz) / 8) < 1.05
+
+
 def test_slab_bounds():
     assert shard.slab_bounds(10, 3).tolist() == [0, 3, 6, 10]
     b = shard.slab_bounds(1001, 8)
