@@ -1,0 +1,61 @@
+"""Small, self-contained invocations of single kernels, for ncu captures.
+
+  python sam3d.cpp_b200/profile_case.py conv2      # config-2 conv (C=256, 15,159 voxels), 128-row kernel
+  python sam3d.cpp_b200/profile_case.py conv_sk    # 256^3 shell (241,978 voxels), C=256, stream-K kernel
+  python sam3d.cpp_b200/profile_case.py tables     # hash + submanifold kmap of the 2.58M-voxel 512^3 shell
+
+Each case warms up once, then runs the kernel(s) under test `--reps` times on
+one stream, synchronising at the end; the process exits 0 on success. The
+inputs are larger than L2 where the case allows it (conv_sk: 124 MB of bf16
+features; tables: 41 MB of coordinates, 168 MB of table, 279 MB of map).
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+
+import numpy as np
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case", choices=["conv2", "conv_sk", "tables"])
+    ap.add_argument("--reps", type=int, default=3)
+    a = ap.parse_args()
+    import torch
+    import s3dsp
+    import workloads
+
+    ctx = s3dsp.Context(0)
+    P = s3dsp.PREC_BF16
+    if a.case in ("conv2", "conv_sk"):
+        coords = workloads.ellipsoid_shell(64 if a.case == "conv2" else 256, 0)
+        n, c = len(coords), 256
+        h = ctx.hash_build(torch.from_numpy(coords).cuda())
+        k = ctx.kmap_subm3(h)
+        w = torch.empty(s3dsp.Context.packed_bytes(P, 27, c, c), dtype=torch.uint8, device="cuda")
+        ctx.weights_pack(torch.from_numpy(workloads.kaiming_normal_slat(c, c, 2)), s3dsp.LAYOUT_SLAT_ROW, 27, c, c, P, w)
+        x = torch.from_numpy(workloads.normal((n, c), 1)).cuda().to(torch.bfloat16)
+        b = torch.from_numpy(workloads.normal((c,), 3, 0.1)).cuda()
+        out = torch.empty((n, c), device="cuda")
+        flags = s3dsp.CONV_TILE128 if a.case == "conv2" else s3dsp.CONV_STREAM_K
+        for _ in range(1 + a.reps):
+            ctx.conv(k, 27, P, x, w, b, out, c, flags=flags)
+    else:
+        coords = workloads.ellipsoid_shell(512, 0, thickness=4.0)  # the config-5b volume
+        d = torch.from_numpy(coords).cuda()
+        for _ in range(1 + a.reps):
+            h = ctx.hash_build(d)
+            k = ctx.kmap_subm3(h)
+            k.free()
+            h.free()
+    torch.cuda.synchronize()
+    ctx.check()
+    print(f"{a.case}: ok", flush=True)
+
+
+if __name__ == "__main__":
+    main()
