@@ -105,6 +105,16 @@ __global__ void hash_insert_kernel(const int4* __restrict__ coords, int64_t n, i
     }
 }
 
+// first row holding each row's key (a duplicate row is not its own first row)
+__global__ void hash_self_kernel(const int4* __restrict__ coords, int64_t n, HashView h,
+                                 int32_t* __restrict__ self_row) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int4 c = coords[i];
+        self_row[i] = h.find_coord(c.x, c.y, c.z, c.w);
+    }
+}
+
 __global__ void hash_lookup_kernel(const int4* __restrict__ q, int64_t m, HashView h,
                                    int32_t* __restrict__ rows) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < m;
@@ -116,11 +126,12 @@ __global__ void hash_lookup_kernel(const int4* __restrict__ q, int64_t m, HashVi
 
 // Submanifold 3x3x3 map, offset-major: one thread per (output row, offset),
 // block (tile, offset) = 128 rows of one offset, so the nbr stores are
-// coalesced and the block sets its tile's offset bit with one atomicOr.
-// Each thread issues two independent probes: the offset neighbour and the
-// row's own key. The own-key probe finds the first row holding this key; a
-// duplicate row (not the first) gets no neighbours, as SlatTables::build
-// iterates the unique map entries (sparse_ops.cpp:129-139).
+// coalesced and the block sets its tile's offset bit with one atomicOr. A
+// duplicate row (not the first holding its key) gets no neighbours, as
+// SlatTables::build iterates the unique map entries (sparse_ops.cpp:
+// 129-139). The first row comes from the hash's self-row array when the
+// table is larger than L2 can serve (one probe per row, done once), else
+// from a second probe issued next to the neighbour probe (no extra pass).
 __device__ __forceinline__ int32_t probe_rest(const HashView& h, unsigned long long key, unsigned long long slot) {
     for (unsigned long long p = 1; p <= h.mask; ++p) {
         slot = (slot + 1) & h.mask;
@@ -132,6 +143,7 @@ __device__ __forceinline__ int32_t probe_rest(const HashView& h, unsigned long l
 }
 
 __global__ void __launch_bounds__(kTileRows) kmap_subm3_kernel(const int4* __restrict__ coords, int64_t n, HashView h,
+                                                               const int32_t* __restrict__ self_row,
                                                                int32_t* __restrict__ nbr,
                                                                uint32_t* __restrict__ tile_mask) {
     const int o = blockIdx.y;
@@ -142,13 +154,18 @@ __global__ void __launch_bounds__(kTileRows) kmap_subm3_kernel(const int4* __res
         const int4 c = __ldg(coords + r);
         unsigned long long kn, ks;
         const bool okn = pack_key(c.x, c.y + dx, c.z + dy, c.w + dz, kn);
-        const bool oks = pack_key(c.x, c.y, c.z, c.w, ks);
-        const unsigned long long sn = okn ? (mix64(kn) & h.mask) : 0, ss = oks ? (mix64(ks) & h.mask) : 0;
+        const unsigned long long sn = okn ? (mix64(kn) & h.mask) : 0;
         const ulonglong2 qn = okn ? __ldg(h.slots + sn) : make_ulonglong2(kEmptyKey, 0);
-        const ulonglong2 qs = oks ? __ldg(h.slots + ss) : make_ulonglong2(kEmptyKey, 0);
         int32_t self = -1;
-        if (qs.x == ks && oks) self = (int32_t)(uint32_t)qs.y;
-        else if (oks && qs.x != kEmptyKey) self = probe_rest(h, ks, ss);
+        if (self_row) {
+            self = __ldg(self_row + r);
+        } else {
+            const bool oks = pack_key(c.x, c.y, c.z, c.w, ks);
+            const unsigned long long ss = oks ? (mix64(ks) & h.mask) : 0;
+            const ulonglong2 qs = oks ? __ldg(h.slots + ss) : make_ulonglong2(kEmptyKey, 0);
+            if (qs.x == ks && oks) self = (int32_t)(uint32_t)qs.y;
+            else if (oks && qs.x != kEmptyKey) self = probe_rest(h, ks, ss);
+        }
         if (self == (int32_t)r && okn) {
             if (qn.x == kn) res = (int32_t)(uint32_t)qn.y;
             else if (qn.x != kEmptyKey) res = probe_rest(h, kn, sn);
@@ -416,8 +433,12 @@ extern "C" S3DSP_API s3d_status s3dsp_hash_build(s3dsp_context* ctx, const int32
     while (cap < 4 * (uint64_t)n) cap <<= 1;
     h->capacity = cap;
     cudaStream_t st = ctx->stream;
+    // above 16 MB of table, probes mostly miss L2: map builders then read each
+    // row's first row from a one-probe-per-row pass instead of probing again
+    const bool self_pass = cap * 16 > (16ull << 20);
     cudaError_t e = cudaMallocAsync(&h->slots, cap * 16, st);
     if (e == cudaSuccess) e = cudaMallocAsync(&h->coords, (size_t)n * 16, st);
+    if (e == cudaSuccess && self_pass) e = cudaMallocAsync(&h->self_row, (size_t)n * 4, st);
     if (e != cudaSuccess) {
         s3dsp_hash_free(ctx, h);
         return cuda_fail(error, error_capacity, e, "hash allocation");
@@ -427,6 +448,9 @@ extern "C" S3DSP_API s3d_status s3dsp_hash_build(s3dsp_context* ctx, const int32
     hash_insert_kernel<<<grid_for(n, threads, ctx->sm_count), threads, 0, st>>>(
         reinterpret_cast<const int4*>(d_coords), n, reinterpret_cast<int4*>(h->coords), h->slots, cap - 1,
         reject_duplicates, ctx->d_status);
+    if (self_pass)
+        hash_self_kernel<<<grid_for(n, threads, ctx->sm_count), threads, 0, st>>>(
+            reinterpret_cast<const int4*>(h->coords), n, view_of(h), h->self_row);
     e = cudaGetLastError();
     if (e != cudaSuccess) {
         s3dsp_hash_free(ctx, h);
@@ -447,6 +471,7 @@ extern "C" S3DSP_API void s3dsp_hash_free(s3dsp_context* ctx, s3dsp_hash* h) {
     if (!h) return;
     cudaStream_t st = ctx ? ctx->stream : nullptr;
     if (h->slots) cudaFreeAsync(h->slots, st);
+    if (h->self_row) cudaFreeAsync(h->self_row, st);
     if (h->coords) cudaFreeAsync(h->coords, st);
     delete h;
 }
@@ -484,7 +509,7 @@ extern "C" S3DSP_API s3d_status s3dsp_kmap_build_subm3_rows(s3dsp_context* ctx, 
     const int64_t tiles = (n_out + kTileRows - 1) / kTileRows;
     // output rows are the hash's first n_out rows; inputs are all its rows
     kmap_subm3_kernel<<<dim3((unsigned)tiles, 27), kTileRows, 0, ctx->stream>>>(
-        reinterpret_cast<const int4*>(h->coords), n_out, view_of(h), k->nbr, k->tile_mask);
+        reinterpret_cast<const int4*>(h->coords), n_out, view_of(h), h->self_row, k->nbr, k->tile_mask);
     e = cudaGetLastError();
     if (e != cudaSuccess) {
         s3dsp_kmap_free(ctx, k);

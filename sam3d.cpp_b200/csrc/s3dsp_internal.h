@@ -39,6 +39,7 @@ struct s3dsp_hash {
     uint64_t capacity = 0;               // power of two >= 4n
     ulonglong2* slots = nullptr;         // [capacity] {packed key, first row in the low 32 bits}
     int32_t* coords = nullptr;           // [n, 4] own copy
+    int32_t* self_row = nullptr;         // [n] first row holding each row's key, or null (small tables)
     int32_t reject_duplicates = 0;
 };
 

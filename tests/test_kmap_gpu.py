@@ -65,6 +65,19 @@ def test_subm_kmap_bit_exact(ctx, seed, res):
     assert np.array_equal(mesh, np.where(exp >= len(coords), -1, exp))
 
 
+def test_subm_kmap_large_table_with_duplicates(ctx):
+    """Above 16 MB of hash table (> 262k rows) the map reads each row's first
+    row from the hash's self-row pass: 968k shell voxels plus 5,000 repeated
+    rows, shuffled, must still match the reference table builder's rules."""
+    base = workloads.ellipsoid_shell(512, 0)
+    rng = np.random.default_rng(9)
+    coords = np.concatenate([base, base[rng.choice(len(base), 5000, replace=False)]])
+    coords = np.ascontiguousarray(coords[rng.permutation(len(coords))])
+    slat, _, _, _ = gpu_subm_tables(ctx, coords)
+    exp = oracle.slat_tables(coords)["conv_fine"].reshape(-1, 27)
+    assert np.array_equal(slat, exp)
+
+
 def test_subm_kmap_golden_digest(ctx, golden_dir):
     with open(os.path.join(golden_dir, "digests.json")) as f:
         e = json.load(f)["config1_shell"]
