@@ -37,6 +37,9 @@ for sub in ("sam3d.cpp_b200", "oracle"):
 METRIC = "active-voxel outputs/s per GPU (C=256 subm conv)"
 UNIT = "voxel-outputs/s"
 L2_FLUSH_BYTES = 512 << 20  # > 126 MB L2
+# DRAM bytes (read + write) per launch of the config-2 conv kernel, from one ncu
+# capture of `python sam3d.cpp_b200/profile_case.py conv2` (profiles/conv_tc_kernel_config2.md)
+CONV_TRAFFIC_BYTES = {"conv_tc_kernel": 13.02e6}
 
 
 def load_peaks():
@@ -287,7 +290,8 @@ def run_ours(args, rank, world, local_rank):
                    "timing": "device steps replayed as a CUDA graph of the library calls; e2e = "
                              "s3dsp_res_block_gn_host (host buffers in/out) per step"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": tflops, "unit": "TFLOP/s",
-                     "frac": achieved / tflops, "traffic": None,
+                     "frac": achieved / tflops, "traffic": CONV_TRAFFIC_BYTES.get(path.conv_kernel),
+                     "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
                      "kernel": path.conv_kernel, "flops_per_launch": flops, "avg_launch_ms": conv_avg_ms,
                      "peak_source": f"{peak_src} bf16_tflops (burst)"},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
