@@ -485,6 +485,131 @@ def run_objects(args, rank, world, local_rank):
 
 
 # ---------------------------------------------------------------------------
+# configs 1 and 3: single layers (F32-strict or BF16)
+# ---------------------------------------------------------------------------
+def run_layers(args, rank, world, local_rank):
+    """Config 1: one subm conv on the 64^3 shell, C = 64 (seed 0).
+    Config 3: the learned stride-2 subdivide of that shell (2x2x2 transposed
+    conv 128 -> 64, one GEMM onto the child-major [Np, 8*64] layout) followed
+    by one subm conv at C = 64 over the 8*Np children. Tables are built once
+    (outside the timed region); a step is the layer(s) alone. Replicas only:
+    at N > 1 each rank runs the same layer on its own GPU."""
+    import torch
+    import s3dsp
+    import workloads
+    import oracle
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    stream = torch.cuda.Stream(device)
+    torch.cuda.set_stream(stream)
+    ctx = s3dsp.Context(local_rank, stream=stream.cuda_stream, flags=s3dsp.CONTEXT_DEFERRED_CHECKS)
+    prec = s3dsp.PREC_F32_STRICT if args.precision == "f32" else s3dsp.PREC_BF16
+    xdt = torch.float32 if prec == s3dsp.PREC_F32_STRICT else torch.bfloat16
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+
+    def dev(a):
+        return torch.from_numpy(np.ascontiguousarray(a)).to(device)
+
+    def pack(w, layout, kvol, cin, cout):
+        dst = torch.empty(s3dsp.Context.packed_bytes(prec, kvol, cin, cout), dtype=torch.uint8, device=device)
+        ctx.weights_pack(torch.from_numpy(np.ascontiguousarray(w)), layout, kvol, cin, cout, prec, dst)
+        return dst
+
+    if args.workload == "config1":
+        cfg = workloads.config1(0)
+        coords, n, c = cfg["coords"], len(cfg["coords"]), 64
+        h = ctx.hash_build(dev(coords))
+        k = ctx.kmap_subm3(h)
+        w = pack(cfg["weight"], s3dsp.LAYOUT_SLAT_ROW, 27, c, c)
+        b = dev(cfg["bias"])
+        x = dev(cfg["feats"]).to(xdt)
+        out = torch.empty((n, c), dtype=torch.float32, device=device)
+
+        def step():
+            ctx.conv(k, 27, prec, x, w, b, out, c)
+        units = n
+        nbr = oracle.slat_tables(coords)["conv_fine"].reshape(n, 27)
+        cpu = lambda: oracle.subm_conv_slat(cfg["feats"], nbr, cfg["weight"], cfg["bias"])  # noqa: E731
+        P = int(ctx.kmap_pairs(k, torch.empty(27 * n, dtype=torch.int32, device=device),
+                               torch.empty(27 * n, dtype=torch.int32, device=device))[27])
+        flops = 2.0 * c * c * P
+        desc = f"config1: one subm conv, 64^3 shell {n} voxels, C=64 ({args.precision})"
+    else:
+        cfg = workloads.config3(1)
+        parents, np_, cin, cout = cfg["coords"], len(cfg["coords"]), cfg["cin"], cfg["cout"]
+        hp = ctx.hash_build(dev(parents), reject_duplicates=True)
+        cc = torch.empty((8 * np_, 4), dtype=torch.int32, device=device)
+        ks = ctx.subdivide(hp, cc)  # child coords + child submanifold map
+        w_up = pack(cfg["w_up"].reshape(8 * cout, cin), s3dsp.LAYOUT_LINEAR, 1, cin, 8 * cout)
+        b_up = dev(np.tile(cfg["b_up"], 8))
+        w = pack(workloads.slat_to_mesh_packed(cfg["w"], cout, cout), s3dsp.LAYOUT_MESH_PACKED, 27, cout, cout)
+        b = dev(cfg["b"])
+        x = dev(cfg["feats"]).to(xdt)
+        up = torch.empty((np_, 8 * cout), dtype=xdt, device=device)  # == [8 Np, cout] child-major
+        out = torch.empty((8 * np_, cout), dtype=torch.float32, device=device)
+
+        def step():
+            ctx.conv(None, 1, prec, x, w_up, b_up, up, 8 * cout)
+            ctx.conv(ks, 27, prec, up.view(8 * np_, cout), w, b, out, cout)
+        units = np_ + 8 * np_
+        cc_h, nb = oracle.mesh_subdivide(parents)
+        wl = cfg["w_up"].reshape(8 * cout, cin)
+
+        def cpu():
+            u = oracle.linear(cfg["feats"], wl, np.tile(cfg["b_up"], 8)).reshape(8 * np_, cout)
+            return oracle.subm_conv_mesh(u, nb, workloads.slat_to_mesh_packed(cfg["w"], cout, cout), cfg["b"], cout)
+        P = int(ctx.kmap_pairs(ks, torch.empty(27 * 8 * np_, dtype=torch.int32, device=device),
+                               torch.empty(27 * 8 * np_, dtype=torch.int32, device=device))[27])
+        flops = 2.0 * cin * 8 * cout * np_ + 2.0 * cout * cout * P
+        desc = (f"config3: 2x2x2 transposed subdivide {np_} -> {8 * np_} voxels (128 -> 64) + subm conv C=64 "
+                f"({args.precision})")
+    for _ in range(args.warmup):
+        step()
+        flush.fill_(1.0)
+    stream.synchronize()
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.3)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for i in range(args.steps):
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+        flush.fill_(1.0)
+    stream.synchronize()
+    clocks = sampler.stop()
+    dev_ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends))
+    ctx.check()
+    vals = torch.tensor([dev_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX)
+    dev_ms = vals.item()
+    if rank != 0:
+        return None
+    t0 = time.perf_counter()
+    cpu()
+    cpu_s = time.perf_counter() - t0
+    hbm, tflops, tflops_sus, peak_src = load_peaks()
+    ms = dev_ms / args.steps
+    peak = tflops if prec == s3dsp.PREC_BF16 else None
+    return {
+        "metric": "active-voxel outputs/s", "value": units * world / (ms / 1e3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": args.precision,
+        "data": "synthetic (seeded 64^3 ellipsoid shell, random features and weights)",
+        "config": {"workload": desc, "pairs": P, "l2": "flushed between steps (512 MiB write)",
+                   "parallelism": f"replicas{world}"},
+        "achieved_tflops": flops / (ms / 1e3) / 1e12,
+        "roofline_frac": (flops / (ms / 1e3) / 1e12) / peak if peak else None,
+        "cpu_baseline": {"value": units / cpu_s, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                         "sample": "the same layer(s) once through the oracle's f32 restatement"},
+        "clocks": clocks,
+    }
+
+
+# ---------------------------------------------------------------------------
 # CPU path (reference arm and cpu_baseline)
 # ---------------------------------------------------------------------------
 def cpu_step(cfg, threads):
@@ -541,9 +666,11 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="config2", choices=["config2", "volume", "objects"],
+    ap.add_argument("--workload", default="config2", choices=["config2", "config1", "config3", "volume", "objects"],
                     help="config2: the headline (default); volume: config 5b, one volume split across ranks; "
-                         "objects: config 5a, 64 objects through config 4 sharded by object")
+                         "objects: config 5a, 64 objects through config 4 sharded by object; "
+                         "config1 / config3: single layers")
+    ap.add_argument("--precision", default="f32", choices=["f32", "bf16"], help="config1 / config3 only")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -557,7 +684,8 @@ def main():
             torch.cuda.set_device(local_rank)
             torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                                  device_id=torch.device("cuda", local_rank))
-        runner = {"config2": run_ours, "volume": run_volume, "objects": run_objects}[args.workload]
+        runner = {"config2": run_ours, "volume": run_volume, "objects": run_objects, "config1": run_layers,
+                  "config3": run_layers}[args.workload]
         line = runner(args, rank, world, local_rank)
         if world > 1:
             import torch
