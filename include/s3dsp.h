@@ -74,7 +74,8 @@ typedef struct s3dsp_slat_tables s3dsp_slat_tables;
 #define S3DSP_PRO_AFFINE_SILU UINT32_C(2) /* gathered x -> silu((x - sub[c]) * mul[c] + add[c]) */
 #define S3DSP_CONV_TILE128 UINT32_C(8)   /* BF16: force one CTA per 128-row tile */
 #define S3DSP_CONV_STREAM_K UINT32_C(16) /* BF16: force 256-row tiles split evenly over all SMs
-                                          (stream-K). Neither flag: chosen by size, see s3dsp_conv_kernel */
+                                          (stream-K). No kernel flag: chosen by size, see s3dsp_conv_kernel */
+#define S3DSP_CONV_STREAM_K128 UINT32_C(32) /* BF16: force 128-row tiles split evenly over all SMs */
 #define S3DSP_CONV_CTA_PAIR UINT32_C(4)  /* BF16: tcgen05 CTA pairs (256-row MMA over two tiles) instead of
                                           one CTA per 128-row tile; same results, slower on B200 today */
 
@@ -222,9 +223,10 @@ S3DSP_API s3d_status s3dsp_conv(s3dsp_context *ctx, const s3dsp_kmap *kmap, int3
                                 int32_t gn_groups, char *error, uint64_t error_capacity);
 
 /* Name of the kernel s3dsp_conv launches for this shape on ctx's device
- * ("conv_f32_kernel", "conv_tc_kernel" = 128-row tiles, "conv_sk_kernel" =
- * 256-row stream-K tiles), or NULL for a NULL ctx / unknown precision. No
- * reference counterpart: a query for profiling and tests. */
+ * ("conv_f32_kernel", "conv_tc_kernel" = 128-row tiles, "conv_sk_kernel<256>"
+ * / "conv_sk_kernel<128>" = stream-K over 256- / 128-row tiles), or NULL for
+ * a NULL ctx / unknown precision. No reference counterpart: a query for
+ * profiling and tests. */
 S3DSP_API const char *s3dsp_conv_kernel(const s3dsp_context *ctx, int64_t n_out, int32_t kvol, int64_t cin,
                                         int64_t cout, uint32_t precision, uint32_t flags);
 

@@ -14,16 +14,24 @@ namespace {
 // 64^3..256^3 shells at C = 128 and 256 (15k-242k rows); a quarter-empty
 // second wave is where stream-K wins most (155 tiles: 2 waves vs ~1.35).
 // Maps with few offsets (linear layers) always use 128-row tiles.
-bool use_stream_k(const s3dsp_context* ctx, int64_t n_out, int32_t kvol, uint32_t flags) {
-    if (flags & (S3DSP_CONV_TILE128 | S3DSP_CONV_CTA_PAIR)) return false;
-    if (flags & S3DSP_CONV_STREAM_K) return true;
-    if (kvol < 8) return false;
+enum class Bf16Kernel { kTile128, kStreamK128, kStreamK256 };
+
+Bf16Kernel pick_bf16_kernel(const s3dsp_context* ctx, int64_t n_out, int32_t kvol, uint32_t flags) {
+    if (flags & (S3DSP_CONV_TILE128 | S3DSP_CONV_CTA_PAIR)) return Bf16Kernel::kTile128;
+    if (flags & S3DSP_CONV_STREAM_K128) return Bf16Kernel::kStreamK128;
+    if (flags & S3DSP_CONV_STREAM_K) return Bf16Kernel::kStreamK256;
+    if (kvol < 8) return Bf16Kernel::kTile128;
     const double sms = (double)ctx->sm_count;
     const int64_t tiles = (n_out + 127) / 128;
     const double waves128 = (double)((tiles + ctx->sm_count - 1) / ctx->sm_count);
     const double units = (double)((n_out + 255) / 256) * kvol;
     const double est_sk = 0.55 + (units / sms) * 1.525 / kvol;
-    return est_sk < 0.95 * waves128;
+    return est_sk < 0.95 * waves128 ? Bf16Kernel::kStreamK256 : Bf16Kernel::kTile128;
+}
+
+const char* bf16_kernel_name(Bf16Kernel k) {
+    return k == Bf16Kernel::kTile128 ? "conv_tc_kernel" : k == Bf16Kernel::kStreamK128 ? "conv_sk_kernel<128>"
+                                                                                        : "conv_sk_kernel<256>";
 }
 
 }  // namespace
@@ -35,7 +43,7 @@ extern "C" S3DSP_API const char* s3dsp_conv_kernel(const s3dsp_context* ctx, int
     if (!ctx) return nullptr;
     if (precision == S3DSP_PREC_F32_STRICT) return "conv_f32_kernel";
     if (precision != S3DSP_PREC_BF16) return nullptr;
-    return use_stream_k(ctx, n_out, kvol, flags) ? "conv_sk_kernel" : "conv_tc_kernel";
+    return bf16_kernel_name(pick_bf16_kernel(ctx, n_out, kvol, flags));
 }
 
 extern "C" S3DSP_API s3d_status s3dsp_conv(s3dsp_context* ctx, const s3dsp_kmap* kmap, int32_t kvol,
@@ -102,17 +110,18 @@ extern "C" S3DSP_API s3d_status s3dsp_conv(s3dsp_context* ctx, const s3dsp_kmap*
             return fail(error, error_capacity, S3D_INVALID_ARGUMENT,
                         "BF16 needs cin %% 8 == 0 and 16-byte aligned in/weight/out/residual");
         s3d_status st = S3D_OK;
-        const bool tile128 = !use_stream_k(ctx, n_out, kvol, flags);
-        if (tile128)
+        const Bf16Kernel kern = pick_bf16_kernel(ctx, n_out, kvol, flags);
+        if (kern == Bf16Kernel::kTile128)
             e = launch_conv_tc(ctx, kmap, kvol, (const __nv_bfloat16*)in, n_in, (int)cin, in_shift,
                                (const __nv_bfloat16*)weight, bias, residual, res_dtype, res_shift, out, out_dtype,
                                n_out, (int)cout, flags, gn_partials, gn_groups, error, error_capacity, &st);
         else
             e = launch_conv_sk(ctx, kmap, kvol, (const __nv_bfloat16*)in, n_in, (int)cin, in_shift,
                                (const __nv_bfloat16*)weight, bias, residual, res_dtype, res_shift, out, out_dtype,
-                               n_out, (int)cout, flags, gn_partials, gn_groups, error, error_capacity, &st);
+                               n_out, (int)cout, flags, gn_partials, gn_groups,
+                               kern == Bf16Kernel::kStreamK128 ? 128 : 256, error, error_capacity, &st);
         if (st != S3D_OK) return st;
-        if (e != cudaSuccess) return cuda_fail(error, error_capacity, e, tile128 ? "conv_tc_kernel" : "conv_sk_kernel");
+        if (e != cudaSuccess) return cuda_fail(error, error_capacity, e, bf16_kernel_name(kern));
         return S3D_OK;
     }
     return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "unknown precision %u", precision);

@@ -47,15 +47,10 @@ constexpr int kBWarp0 = 16;           // first weight-TMA warp
 constexpr int kMaxBWarps = 4;
 constexpr int kMmaWarp = 20;
 constexpr int kThreads = 21 * 32;
-constexpr int kRows = 256;            // output rows per work tile
 constexpr int kKC = 64;  // channels per pipeline stage (128-byte rows, SWIZZLE_128B; 32 measured slower)
-constexpr int kAStage = kRows * 2 * kKC;  // bytes: 256 gathered rows x kKC bf16
-constexpr int kAHalf = 128 * 2 * kKC;     // second accumulator's rows start here
+constexpr int kAHalf = 128 * 2 * kKC;  // the second accumulator's rows start here in an A stage
 constexpr int kMaxKvol = 27;
 constexpr int kSmemMax = kSmemOptIn;
-// Each stage's "full" barrier may be split in kFullSplit barriers, one per
-// group of producer warps; splitting measured slower on B200.
-constexpr int kFullSplit = 1;
 
 struct SkParams {
     const __nv_bfloat16* in;
@@ -83,7 +78,7 @@ struct SkParams {
     int nnb;                    // column blocks per 256-row tile
     int64_t units;              // work tiles x kvol
     int grid;
-    float* ws;                  // [2 * grid][2][bn / 16][4][128] float4 raw accumulators, or null
+    float* ws;                  // [2 * grid][rows / 128][bn / 16][4][128] float4 raw accumulators, or null
     uint32_t* counters;         // [work tiles] pieces arrived, zeroed before launch
     int cout;
     uint32_t flags;
@@ -110,7 +105,11 @@ __device__ __forceinline__ int64_t ws_slot(const SkParams& p, int i, int64_t wt)
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
 __device__ __forceinline__ void prod_bar() { asm volatile("bar.sync 2, 512;" ::: "memory"); }
 
+// kRows = 256: two 128-row accumulators per work tile; 128: one.
+template <int kRows>
 __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, const __grid_constant__ CUtensorMap wmap) {
+    constexpr int kSub = kRows / 128;              // 128-row accumulators per work tile
+    constexpr int kAStage = kRows * 2 * kKC;       // bytes: kRows gathered rows x kKC bf16
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int S = p.stages;
@@ -124,7 +123,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
     uint8_t* sB = smem + (size_t)S * kAStage;
     int32_t* sidx = reinterpret_cast<int32_t*>(smem + (ring > epi ? ring : epi));  // [kvol][256]
     uint64_t* full = reinterpret_cast<uint64_t*>(sidx + kMaxKvol * kRows);
-    uint64_t* empty = full + S * kFullSplit;
+    uint64_t* empty = full + S;
     uint64_t* accum = empty + S;
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(accum + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
@@ -138,8 +137,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
 
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
-            for (int j = 0; j < kFullSplit; ++j)
-                mbar_init(smem_u32(full + s * kFullSplit + j), kEpiThreads / kFullSplit + (j == 0 ? p.nb : 0));
+            mbar_init(smem_u32(full + s), kEpiThreads + p.nb);
             mbar_init(smem_u32(empty + s), 1);
         }
         mbar_init(smem_u32(accum), 1);
@@ -173,8 +171,10 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
         if (p.nbr) {
             mask = 0xffffffffu;
             if (p.tile_mask) {
-                mask = p.tile_mask[2 * st];
-                if (2 * st + 1 < p.n_tiles) mask |= p.tile_mask[2 * st + 1];
+                mask = 0u;
+#pragma unroll
+                for (int j = 0; j < kSub; ++j)
+                    if (kSub * st + j < p.n_tiles) mask |= p.tile_mask[kSub * st + j];
             }
         }
         mask &= (oe >= 32 ? 0xffffffffu : ((1u << oe) - 1u)) & ~((1u << ob) - 1u);
@@ -184,7 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
         if (warp < kProdWarps) {
             // ============ A producers: indices of this segment, then cp.async gathers ============
             for (int i = tid; i < kMaxKvol * kRows; i += kEpiThreads) {
-                const int o = i >> 8, row = i & (kRows - 1);
+                const int o = i / kRows, row = i & (kRows - 1);
                 if (!((mask >> o) & 1u)) continue;
                 const int64_t r = m0 + row;
                 int32_t s = -1;
@@ -221,7 +221,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
                     const void* g = valid ? (const void*)(p.in + (int64_t)src * p.cin + k0) : (const void*)p.in;
                     cp_async_16(a_base + row * (2 * kKC) + ((c16 ^ kmajor_swz<kKC>(row)) << 4), g, valid ? 16u : 0u);
                 }
-                cp_async_arrive_noinc(smem_u32(full + s * kFullSplit + warp / (kProdWarps / kFullSplit)));
+                cp_async_arrive_noinc(smem_u32(full + s));
             }
         } else if (warp < kBWarp0 + kMaxBWarps) {
             // ============ weight TMA issuers ============
@@ -241,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
                         mrem &= mrem - 1;
                     }
                     if (!mbar_wait(smem_u32(empty + s), ph ^ 1u, abort_flag, p.status)) break;
-                    const uint32_t fb = smem_u32(full + s * kFullSplit);
+                    const uint32_t fb = smem_u32(full + s);
                     mbar_arrive_tx(fb, bytes);
                     tma_load_2d(smem_u32(sB + (size_t)s * bstage + (size_t)jw * rows * 2 * kKC), &wmap, kc * kKC,
                                 o * p.cout_pad + n0 + jw * rows, fb);
@@ -256,9 +256,10 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
                     const uint32_t pit = it + (uint32_t)j;
                     const int s = (int)(pit % (uint32_t)S);
                     const uint32_t ph = (pit / (uint32_t)S) & 1u;
-                    for (int jf = 0; jf < kFullSplit && ok; ++jf)
-                        ok = mbar_wait(smem_u32(full + s * kFullSplit + jf), ph, abort_flag, p.status);
-                    if (!ok) break;
+                    if (!mbar_wait(smem_u32(full + s), ph, abort_flag, p.status)) {
+                        ok = false;
+                        break;
+                    }
                     tc_fence_after();
                     const uint32_t a0 = smem_u32(sA + (size_t)s * kAStage);
                     const uint32_t b0 = smem_u32(sB + (size_t)s * bstage);
@@ -267,7 +268,8 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
                         const uint32_t acc = (j > 0 || k > 0) ? 1u : 0u;
                         const uint64_t bd = kmajor_desc<kKC>(b0 + 32 * k);
                         mma_bf16(tmem, kmajor_desc<kKC>(a0 + 32 * k), bd, p.idesc, acc);
-                        mma_bf16(tmem + p.thalf, kmajor_desc<kKC>(a0 + kAHalf + 32 * k), bd, p.idesc, acc);
+                        if constexpr (kSub == 2)
+                            mma_bf16(tmem + p.thalf, kmajor_desc<kKC>(a0 + kAHalf + 32 * k), bd, p.idesc, acc);
                     }
                     mma_commit(smem_u32(empty + s));
                 }
@@ -301,7 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
                 // store the raw accumulator as float4s [sub][16-column chunk][quad][row]:
                 // each warp access is 512 contiguous bytes
                 float* slot = p.ws + (me == i_first ? slot0 : 2 * (int64_t)me) * slot_stride;
-                for (int sub = 0; sub < 2; ++sub)
+                for (int sub = 0; sub < kSub; ++sub)
                     for (int c = warp >> 2; c < nch; c += 4) {
                         float f[16];
                         if (have_acc) {
@@ -343,7 +345,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
                 const int silu_k = (p.flags & S3DSP_EPI_SILU) ? 1 : 0;
                 const int sel = (out_k < 0 || res_k < 0) ? -1 : ((out_k * 3 + res_k) * 2 + silu_k) * 2 + (stats ? 1 : 0);
                 const uint32_t so_base = smem_u32(stage_out);
-                for (int sub = 0; sub < 2; ++sub) {
+                for (int sub = 0; sub < kSub; ++sub) {
                     const int64_t ms = m0 + 128 * sub;
                     if (ms >= p.n_out) break;
                     // phase 1: accumulator (TMEM, or the pieces summed in piece order) -> smem tile
@@ -416,7 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
                         // deterministic GroupNorm partials of the 128-row tile: the write-out
                         // left per-warp column sums; each group summed over warps, columns in order
                         epi_bar();
-                        const int64_t t128 = 2 * st + sub;
+                        const int64_t t128 = kSub * st + sub;
                         const int g_lo = n0 / gs;
                         const int g_hi = min(p.gn_groups - 1, (n0 + limit - 1) / gs);
                         for (int g = g_lo + tid; g <= g_hi; g += kEpiThreads) {
@@ -454,11 +456,11 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
     }
 }
 
-size_t sk_smem_bytes(int stages, int bn) {
-    const size_t ring = (size_t)stages * (kAStage + bn * 2 * kKC);
+size_t sk_smem_bytes(int stages, int bn, int rows) {
+    const size_t ring = (size_t)stages * ((size_t)rows * 2 * kKC + (size_t)bn * 2 * kKC);
     const size_t epi = (size_t)128 * (bn + 4) * 4 + (size_t)kProdWarps * bn * 16;
-    return 1024 /*align slack*/ + (ring > epi ? ring : epi) + (size_t)kMaxKvol * kRows * 4 /*sidx*/ +
-           ((kFullSplit + 1) * stages + 1) * 8 + 16;
+    return 1024 /*align slack*/ + (ring > epi ? ring : epi) + (size_t)kMaxKvol * rows * 4 /*sidx*/ +
+           (2 * stages + 1) * 8 + 16;
 }
 
 }  // namespace
@@ -470,22 +472,26 @@ int tc_pick_bn(int cout);
 cudaError_t launch_conv_sk(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol, const __nv_bfloat16* in,
                            int64_t n_in, int cin, int in_shift, const __nv_bfloat16* w, const float* bias,
                            const void* residual, uint32_t res_dtype, int res_shift, void* out, uint32_t out_dtype,
-                           int64_t n_out, int cout, uint32_t flags, double* gn_partials, int gn_groups, char* error,
-                           uint64_t error_capacity, s3d_status* st) {
+                           int64_t n_out, int cout, uint32_t flags, double* gn_partials, int gn_groups, int rows,
+                           char* error, uint64_t error_capacity, s3d_status* st) {
     *st = S3D_OK;
     (void)n_in;
+    if (rows != 128 && rows != 256) {
+        *st = fail(error, error_capacity, S3D_INTERNAL_ERROR, "stream-K tile rows %d", rows);
+        return cudaErrorInvalidValue;
+    }
     const int cout_pad = (cout + 15) / 16 * 16;
     const int cin_pad = (cin + 63) / 64 * 64;
     const int bn = tc_pick_bn(cout);
     const int nnb = cout_pad / bn;
     const int kchunks = cin_pad / kKC;
     const int64_t tiles = (n_out + 127) / 128;
-    const int64_t work_tiles = (n_out + kRows - 1) / kRows * nnb;
+    const int64_t work_tiles = (n_out + rows - 1) / rows * nnb;
     const int64_t units = work_tiles * kvol;
 
     int stages = 16;
-    while (stages > 2 && sk_smem_bytes(stages, bn) > (size_t)kSmemMax) --stages;
-    const size_t smem = sk_smem_bytes(stages, bn);
+    while (stages > 2 && sk_smem_bytes(stages, bn, rows) > (size_t)kSmemMax) --stages;
+    const size_t smem = sk_smem_bytes(stages, bn, rows);
     if (smem > (size_t)kSmemMax) {
         *st = fail(error, error_capacity, S3D_INTERNAL_ERROR, "conv tile of %d columns does not fit shared memory", bn);
         return cudaErrorInvalidValue;
@@ -535,7 +541,7 @@ cudaError_t launch_conv_sk(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     p.bn = bn;
     p.nb = nb;
     p.stages = stages;
-    p.tcols = 2 * thalf;
+    p.tcols = (uint32_t)(rows / 128) * thalf;
     p.thalf = thalf;
     p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(bn >> 3) << 17) | ((128u >> 4) << 24);
     p.bias = bias;
@@ -558,8 +564,9 @@ cudaError_t launch_conv_sk(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     p.status = ctx->d_status;
 
     cudaStream_t s = ctx->stream;
-    static std::atomic<uint64_t> optin{0};
-    cudaError_t e = smem_optin((const void*)conv_sk_kernel, ctx->device, optin);
+    static std::atomic<uint64_t> optin128{0}, optin256{0};
+    cudaError_t e = rows == 256 ? smem_optin((const void*)conv_sk_kernel<256>, ctx->device, optin256)
+                                : smem_optin((const void*)conv_sk_kernel<128>, ctx->device, optin128);
     if (e != cudaSuccess) return e;
     if (gn_partials) {
         e = cudaMemsetAsync(gn_partials, 0, sizeof(double) * 2 * (size_t)gn_groups * (size_t)tiles, s);
@@ -568,7 +575,7 @@ cudaError_t launch_conv_sk(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     void* ws = nullptr;
     void* counters = nullptr;
     if (split) {
-        e = cudaMallocAsync(&ws, (size_t)2 * grid * kRows * bn * sizeof(float), s);
+        e = cudaMallocAsync(&ws, (size_t)2 * grid * rows * bn * sizeof(float), s);
         if (e == cudaSuccess) e = cudaMallocAsync(&counters, (size_t)work_tiles * sizeof(uint32_t), s);
         if (e == cudaSuccess) e = cudaMemsetAsync(counters, 0, (size_t)work_tiles * sizeof(uint32_t), s);
         if (e != cudaSuccess) {
@@ -580,7 +587,10 @@ cudaError_t launch_conv_sk(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
         p.ws = static_cast<float*>(ws);
         p.counters = static_cast<uint32_t*>(counters);
     }
-    conv_sk_kernel<<<grid, kThreads, smem, s>>>(p, wmap);
+    if (rows == 256)
+        conv_sk_kernel<256><<<grid, kThreads, smem, s>>>(p, wmap);
+    else
+        conv_sk_kernel<128><<<grid, kThreads, smem, s>>>(p, wmap);
     e = cudaGetLastError();
     if (ws) cudaFreeAsync(ws, s);
     if (counters) cudaFreeAsync(counters, s);

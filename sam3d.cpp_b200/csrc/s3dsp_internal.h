@@ -118,11 +118,12 @@ cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
                            uint32_t res_dtype, int res_shift, void* out, uint32_t out_dtype,
                            int64_t n_out, int cout, uint32_t flags, double* gn_partials,
                            int gn_groups, char* error, uint64_t error_capacity, s3d_status* st);
+// rows: 128 or 256 output rows per stream-K work tile
 cudaError_t launch_conv_sk(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
                            const __nv_bfloat16* in, int64_t n_in, int cin, int in_shift,
                            const __nv_bfloat16* w, const float* bias, const void* residual,
                            uint32_t res_dtype, int res_shift, void* out, uint32_t out_dtype,
                            int64_t n_out, int cout, uint32_t flags, double* gn_partials,
-                           int gn_groups, char* error, uint64_t error_capacity, s3d_status* st);
+                           int gn_groups, int rows, char* error, uint64_t error_capacity, s3d_status* st);
 
 }  // namespace s3dsp

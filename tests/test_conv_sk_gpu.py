@@ -66,6 +66,10 @@ def same(a, b):
     return np.array_equal(a, b)
 
 
+SK_FLAGS = [s3dsp.CONV_STREAM_K, s3dsp.CONV_STREAM_K128]  # 256- and 128-row work tiles
+
+
+@pytest.mark.parametrize("skflag", SK_FLAGS)
 @pytest.mark.parametrize("cin,cout,res,seed", [
     (256, 256, 64, 0),   # config 2 shape: 60 tiles over all SMs, most tiles split
     (64, 64, 64, 1),     # config 1 shape
@@ -75,7 +79,7 @@ def same(a, b):
     (64, 16, 8, 5),      # a handful of rows: many pieces per tile
     (256, 512, 20, 6),   # two 256-column blocks
 ])
-def test_sk_matches_tile128_and_oracle(ctx, cin, cout, res, seed):
+def test_sk_matches_tile128_and_oracle(ctx, cin, cout, res, seed, skflag):
     coords = workloads.ellipsoid_shell(res, seed) if res >= 16 else workloads.ellipsoid_shell(16, seed)[:37]
     n = len(coords)
     h = ctx.hash_build(dev(coords))
@@ -85,7 +89,7 @@ def test_sk_matches_tile128_and_oracle(ctx, cin, cout, res, seed):
     b = workloads.normal((cout,), 30 + seed, 0.1)
     wp = pack(ctx, w, s3dsp.LAYOUT_SLAT_ROW, 27, cin, cout)
     xb = dev(x).to(torch.bfloat16)
-    sk = run(ctx, k, 27, xb, wp, dev(b), cout, n)
+    sk = run(ctx, k, 27, xb, wp, dev(b), cout, n, flags=skflag)
     t128 = run(ctx, k, 27, xb, wp, dev(b), cout, n, flags=s3dsp.CONV_TILE128, reps=1)
     for o in sk[1:]:
         assert np.array_equal(o, sk[0]), "stream-K kernel not deterministic"
@@ -94,10 +98,11 @@ def test_sk_matches_tile128_and_oracle(ctx, cin, cout, res, seed):
     assert rel_l2(sk[0], oracle.subm_conv_slat(x, nbr, w, b, accum64=True)) < 1e-2
 
 
+@pytest.mark.parametrize("skflag", SK_FLAGS)
 @pytest.mark.parametrize("out_dtype,res_dtype,silu", [(torch.float32, torch.float32, True),
                                                       (torch.bfloat16, torch.bfloat16, False),
                                                       (torch.float32, torch.bfloat16, False)])
-def test_sk_epilogue_gn_and_subdivide(ctx, out_dtype, res_dtype, silu):
+def test_sk_epilogue_gn_and_subdivide(ctx, out_dtype, res_dtype, silu, skflag):
     parents = workloads.ellipsoid_shell(24, 7)
     hp = ctx.hash_build(dev(parents), reject_duplicates=True)
     cc = torch.empty((8 * len(parents), 4), dtype=torch.int32, device="cuda")
@@ -111,7 +116,7 @@ def test_sk_epilogue_gn_and_subdivide(ctx, out_dtype, res_dtype, silu):
     wp = pack(ctx, w, s3dsp.LAYOUT_MESH_PACKED, 27, cin, cout)
     xb = dev(x).to(torch.bfloat16)
     kw = dict(in_shift=3, residual=res, res_shift=3, epi=s3dsp.EPI_SILU if silu else 0, gn=True, out_dtype=out_dtype)
-    sk = run(ctx, k, 27, xb, wp, dev(b), cout, n_out, **kw)
+    sk = run(ctx, k, 27, xb, wp, dev(b), cout, n_out, flags=skflag, **kw)
     t128 = run(ctx, k, 27, xb, wp, dev(b), cout, n_out, flags=s3dsp.CONV_TILE128, reps=1, **kw)
     for o in sk[1:]:
         assert same(o, sk[0]), "stream-K kernel not deterministic"
@@ -152,9 +157,10 @@ def test_kernel_choice(ctx):
     P = s3dsp.PREC_BF16
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     assert ctx.conv_kernel(128 * sms - 5, 27, 256, 256, P) == "conv_tc_kernel"   # one full wave
-    assert ctx.conv_kernel(128 * sms + 900, 27, 256, 256, P) == "conv_sk_kernel"  # a thin second wave
-    assert ctx.conv_kernel(128 * 8 * sms, 27, 256, 256, P) == "conv_sk_kernel"
+    assert ctx.conv_kernel(128 * sms + 900, 27, 256, 256, P) == "conv_sk_kernel<256>"  # a thin second wave
+    assert ctx.conv_kernel(128 * 8 * sms, 27, 256, 256, P) == "conv_sk_kernel<256>"
     assert ctx.conv_kernel(128 * 8 * sms, 1, 256, 256, P) == "conv_tc_kernel"     # linear layers
-    assert ctx.conv_kernel(1000, 27, 256, 256, P, s3dsp.CONV_STREAM_K) == "conv_sk_kernel"
+    assert ctx.conv_kernel(1000, 27, 256, 256, P, s3dsp.CONV_STREAM_K) == "conv_sk_kernel<256>"
+    assert ctx.conv_kernel(1000, 27, 256, 256, P, s3dsp.CONV_STREAM_K128) == "conv_sk_kernel<128>"
     assert ctx.conv_kernel(128 * 3 * sms, 27, 256, 256, P, s3dsp.CONV_TILE128) == "conv_tc_kernel"
     assert ctx.conv_kernel(1000, 27, 256, 256, s3dsp.PREC_F32_STRICT) == "conv_f32_kernel"
