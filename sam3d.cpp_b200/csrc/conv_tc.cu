@@ -16,14 +16,15 @@
 // the stage with tcgen05.commit.
 //
 // Epilogue: the accumulator is read back with tcgen05.ld into a padded
-// shared-memory tile (each warp its 32 TMEM lanes = rows), then written out
-// row by row with coalesced vector loads/stores: bias, residual, GroupNorm
+// shared-memory tile (warp w: TMEM lanes 32*(w%4).., i.e. its rows, column
+// chunks w/4, w/4+4, ...), then written out row by row (warp w: rows
+// 8w..8w+7) with coalesced vector loads/stores: bias, residual, GroupNorm
 // partial sums (f64) and SiLU are applied on the way. Outputs are written
 // once; nothing accumulates through atomics.
 //
-// Warp roles (672 threads): warps 0-15 gather A, and warps 0-3 then run the
-// epilogue (warp w reads TMEM lanes 32*w .. +31); warps 16-19 issue the
-// weight TMA loads (lane 0 each); warp 20 owns TMEM and issues the MMAs.
+// Warp roles (672 threads): warps 0-15 gather A and then run the epilogue;
+// warps 16-19 issue the weight TMA loads (lane 0 each); warp 20 owns TMEM and
+// issues the MMAs.
 //
 // Every mbarrier wait is bounded (about two seconds of %globaltimer); on
 // timeout the CTA records kErrPipelineTimeout, stops issuing work and exits
@@ -46,7 +47,6 @@ constexpr int kBWarp0 = 16;         // first weight-TMA warp
 constexpr int kMaxBWarps = 4;
 constexpr int kMmaWarp = 20;
 constexpr int kThreads = 21 * 32;
-constexpr int kEpiWarp0 = 0;        // first of the 4 epilogue warps
 constexpr int kMaxKvol = 27;
 // Each stage's "full" barrier may be split in kFullSplit barriers, one per
 // group of producer warps. Measured on B200 (config-2 conv, 85 us with one
@@ -79,6 +79,9 @@ struct TcParams {
     int gn_groups;
     uint32_t* status;
 };
+
+// named barrier of the 16 gather/epilogue warps
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
 
 // --- CTA-pair (cluster of 2) helpers ---
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -368,17 +371,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     }
-    if (warp < 4) {
-        // ================= epilogue (warps 0-3, after their gathers) =================
-        const int lane_base = 32 * warp;  // TMEM lanes this warp may access
+    if (warp < kProdWarps) {
+        // ================= epilogue (all 16 gather warps, after their gathers) =================
         bool have_acc = T > 0 && prod_ok && mbar_wait(smem_u32(accum), 0, abort_flag, p.status);
         have_acc = __all_sync(0xffffffffu, have_acc);
         tc_fence_after();
-        // phase 1: TMEM -> padded smem tile, row = lane_base + lane
+        // phase 1: TMEM -> padded smem tile. Warp w reads TMEM lanes 32*(w%4)..
+        // (its rows), 16-column chunks w/4, w/4 + 4, ...
         {
-            float* dst = stage_out + (size_t)(lane_base + lane) * ostride;
-            const uint32_t taddr = tmem + ((uint32_t)lane_base << 16);
-            for (int c0 = 0; c0 < p.bn; c0 += 16) {
+            const int lq = warp & 3;
+            float* dst = stage_out + (size_t)(32 * lq + lane) * ostride;
+            const uint32_t taddr = tmem + ((uint32_t)(32 * lq) << 16);
+            for (int c0 = 16 * (warp >> 2); c0 < p.bn; c0 += 64) {
                 float f[16];
                 if (have_acc) {
                     tmem_ld16(taddr + (uint32_t)c0, f);
@@ -391,8 +395,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     *reinterpret_cast<float4*>(dst + c0 + 4 * q) = make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
             }
         }
-        __syncwarp();
-        // phase 2: coalesced row write-out. lane owns columns 4*lane + 128*q.
+        epi_bar();
+        // phase 2: coalesced row write-out, rows 8w .. 8w+7; lane owns columns 4*lane + 128*q.
         const bool stats = p.gn_partials != nullptr;
         const int gs = stats ? p.cout / p.gn_groups : 1;
         constexpr int kQ = 2;  // bn <= 256 -> at most two 128-column slabs
@@ -409,9 +413,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 bias4[q].w = col + 3 < p.cout ? __ldg(p.bias + col + 3) : 0.f;
             }
         }
-        const int nrows = (int)min((int64_t)32, p.n_out - (m0 + lane_base));
+        const int lane_base = 8 * warp;
+        const int nrows = (int)max((int64_t)0, min((int64_t)8, p.n_out - (m0 + lane_base)));
         const uint32_t so_base = smem_u32(stage_out);
-        double* colp = reinterpret_cast<double*>(smem + (size_t)128 * ostride * 4);  // [4][bn][2]
+        // [16][bn][2]: may run past the rings into the gather indices, unused by now
+        double* colp = reinterpret_cast<double*>(smem + (size_t)128 * ostride * 4);
         double* colw = colp + (size_t)warp * p.bn * 2;
         // One compact loop body per (out dtype, residual dtype, SiLU, stats)
         // combination: a single generic body with every variant inlined runs
@@ -456,15 +462,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (stats) {
             // deterministic GroupNorm partials: per-warp column sums to smem,
             // then each group summed over warps and columns in a fixed order
-            asm volatile("bar.sync 1, 128;" ::: "memory");
-            const int et = tid - kEpiWarp0 * 32;
+            epi_bar();
+            const int et = tid;
             const int g_lo = n0 / gs;
             const int g_hi = min(p.gn_groups - 1, (n0 + limit - 1) / gs);
             // the padding CTA of an odd pair count (tile == n_tiles) has no rows and no slot
-            for (int g = g_lo + et; tile < p.n_tiles && g <= g_hi; g += 128) {
+            for (int g = g_lo + et; tile < p.n_tiles && g <= g_hi; g += kProdWarps * 32) {
                 const int c_lo = max(g * gs - n0, 0), c_hi = min((g + 1) * gs - n0, limit);
                 double a = 0.0, b = 0.0;
-                for (int w = 0; w < 4; ++w)
+                for (int w = 0; w < kProdWarps; ++w)
                     for (int c = c_lo; c < c_hi; ++c) {
                         a += colp[((size_t)w * p.bn + c) * 2 + 0];
                         b += colp[((size_t)w * p.bn + c) * 2 + 1];
@@ -528,8 +534,11 @@ cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     const int kc = 64;
     int stages = (int)((200 * 1024) / stage_bytes(brows, kc));
     if (stages > 16) stages = 16;
-    // the epilogue reuses the ring for a 128 x (bn + 4) f32 tile plus 4 x bn x 2 f64 column sums
-    while ((size_t)stages * stage_bytes(brows, kc) < (size_t)128 * (bn + 4) * 4 + (size_t)4 * bn * 16) ++stages;
+    // the epilogue reuses the ring and the gather indices after it for a
+    // 128 x (bn + 4) f32 tile plus 16 x bn x 2 f64 column sums
+    while ((size_t)stages * stage_bytes(brows, kc) + kMaxKvol * 128 * 4 <
+           (size_t)128 * (bn + 4) * 4 + (size_t)kProdWarps * bn * 16)
+        ++stages;
     (void)n_in;
 
     auto encode = get_encode_fn();
