@@ -140,6 +140,13 @@ S3DSP_API s3d_status s3dsp_kmap_build_subm3(s3dsp_context *ctx, const s3dsp_hash
 S3DSP_API s3d_status s3dsp_kmap_build_subm3_rows(s3dsp_context *ctx, const s3dsp_hash *hash,
                                                  int64_t n_out, s3dsp_kmap **out, char *error,
                                                  uint64_t error_capacity);
+/* The same for hash rows [row_begin, row_end): output row r of the map is hash
+ * row row_begin + r (a shard's interior and boundary rows as two maps, so the
+ * interior can be convolved while the halo is in flight). No reference
+ * counterpart. */
+S3DSP_API s3d_status s3dsp_kmap_build_subm3_range(s3dsp_context *ctx, const s3dsp_hash *hash,
+                                                  int64_t row_begin, int64_t row_end, s3dsp_kmap **out,
+                                                  char *error, uint64_t error_capacity);
 /* Stride-2 subdivide of a parent set: MeshSubdivideTables::build
  * (sparse_ops.cpp:272-404). Writes the 8*n child coords (child row =
  * parent*8 + xb*4 + yb*2 + zb, coords 2p + bits) to d_child_coords [8n, 4]

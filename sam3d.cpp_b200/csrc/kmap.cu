@@ -142,8 +142,9 @@ __device__ __forceinline__ int32_t probe_rest(const HashView& h, unsigned long l
     return -1;
 }
 
-__global__ void __launch_bounds__(kTileRows) kmap_subm3_kernel(const int4* __restrict__ coords, int64_t n, HashView h,
-                                                               const int32_t* __restrict__ self_row,
+// Output row r is hash row row0 + r (r < n).
+__global__ void __launch_bounds__(kTileRows) kmap_subm3_kernel(const int4* __restrict__ coords, int64_t row0, int64_t n,
+                                                               HashView h, const int32_t* __restrict__ self_row,
                                                                int32_t* __restrict__ nbr,
                                                                uint32_t* __restrict__ tile_mask) {
     const int o = blockIdx.y;
@@ -151,14 +152,15 @@ __global__ void __launch_bounds__(kTileRows) kmap_subm3_kernel(const int4* __res
     const int64_t r = (int64_t)blockIdx.x * kTileRows + threadIdx.x;
     int32_t res = -1;
     if (r < n) {
-        const int4 c = __ldg(coords + r);
+        const int64_t hr = row0 + r;  // the row in the hash
+        const int4 c = __ldg(coords + hr);
         unsigned long long kn, ks;
         const bool okn = pack_key(c.x, c.y + dx, c.z + dy, c.w + dz, kn);
         const unsigned long long sn = okn ? (mix64(kn) & h.mask) : 0;
         const ulonglong2 qn = okn ? __ldg(h.slots + sn) : make_ulonglong2(kEmptyKey, 0);
         int32_t self = -1;
         if (self_row) {
-            self = __ldg(self_row + r);
+            self = __ldg(self_row + hr);
         } else {
             const bool oks = pack_key(c.x, c.y, c.z, c.w, ks);
             const unsigned long long ss = oks ? (mix64(ks) & h.mask) : 0;
@@ -166,7 +168,7 @@ __global__ void __launch_bounds__(kTileRows) kmap_subm3_kernel(const int4* __res
             if (qs.x == ks && oks) self = (int32_t)(uint32_t)qs.y;
             else if (oks && qs.x != kEmptyKey) self = probe_rest(h, ks, ss);
         }
-        if (self == (int32_t)r && okn) {
+        if (self == (int32_t)hr && okn) {
             if (qn.x == kn) res = (int32_t)(uint32_t)qn.y;
             else if (qn.x != kEmptyKey) res = probe_rest(h, kn, sn);
         }
@@ -494,22 +496,24 @@ extern "C" S3DSP_API s3d_status s3dsp_hash_lookup(s3dsp_context* ctx, const s3ds
     return S3D_OK;
 }
 
-extern "C" S3DSP_API s3d_status s3dsp_kmap_build_subm3_rows(s3dsp_context* ctx, const s3dsp_hash* h, int64_t n_out,
-                                                            s3dsp_kmap** out, char* error, uint64_t error_capacity) {
+extern "C" S3DSP_API s3d_status s3dsp_kmap_build_subm3_range(s3dsp_context* ctx, const s3dsp_hash* h,
+                                                             int64_t row_begin, int64_t row_end, s3dsp_kmap** out,
+                                                             char* error, uint64_t error_capacity) {
     clear_error(error, error_capacity);
     if (!ctx || !h || !out) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
     *out = nullptr;
-    if (n_out <= 0 || n_out > h->n)
-        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "n_out %lld outside 1..%lld", (long long)n_out,
-                    (long long)h->n);
+    if (row_begin < 0 || row_end <= row_begin || row_end > h->n)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "rows [%lld, %lld) outside [0, %lld)",
+                    (long long)row_begin, (long long)row_end, (long long)h->n);
     S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
     cudaError_t e;
+    const int64_t n_out = row_end - row_begin;
     s3dsp_kmap* k = new_kmap(ctx, n_out, h->n, 27, &e);
     if (!k) return cuda_fail(error, error_capacity, e, "kmap allocation");
     const int64_t tiles = (n_out + kTileRows - 1) / kTileRows;
-    // output rows are the hash's first n_out rows; inputs are all its rows
+    // output rows are hash rows row_begin ..; inputs are all its rows
     kmap_subm3_kernel<<<dim3((unsigned)tiles, 27), kTileRows, 0, ctx->stream>>>(
-        reinterpret_cast<const int4*>(h->coords), n_out, view_of(h), h->self_row, k->nbr, k->tile_mask);
+        reinterpret_cast<const int4*>(h->coords), row_begin, n_out, view_of(h), h->self_row, k->nbr, k->tile_mask);
     e = cudaGetLastError();
     if (e != cudaSuccess) {
         s3dsp_kmap_free(ctx, k);
@@ -519,6 +523,11 @@ extern "C" S3DSP_API s3d_status s3dsp_kmap_build_subm3_rows(s3dsp_context* ctx, 
     return S3D_OK;
 }
 
+extern "C" S3DSP_API s3d_status s3dsp_kmap_build_subm3_rows(s3dsp_context* ctx, const s3dsp_hash* h, int64_t n_out,
+                                                            s3dsp_kmap** out, char* error, uint64_t error_capacity) {
+    return s3dsp_kmap_build_subm3_range(ctx, h, 0, n_out, out, error, error_capacity);
+}
+
 extern "C" S3DSP_API s3d_status s3dsp_kmap_build_subm3(s3dsp_context* ctx, const s3dsp_hash* h,
                                                        s3dsp_kmap** out, char* error,
                                                        uint64_t error_capacity) {
@@ -526,7 +535,7 @@ extern "C" S3DSP_API s3d_status s3dsp_kmap_build_subm3(s3dsp_context* ctx, const
         clear_error(error, error_capacity);
         return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
     }
-    return s3dsp_kmap_build_subm3_rows(ctx, h, h->n, out, error, error_capacity);
+    return s3dsp_kmap_build_subm3_range(ctx, h, 0, h->n, out, error, error_capacity);
 }
 
 extern "C" S3DSP_API s3d_status s3dsp_subdivide(s3dsp_context* ctx, const s3dsp_hash* parents,

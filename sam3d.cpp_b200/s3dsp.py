@@ -32,7 +32,7 @@ CONTEXT_OWN_STREAM = 2
 EXPORTED = [
     "s3dsp_abi_version", "s3dsp_context_create", "s3dsp_context_free", "s3dsp_context_stream",
     "s3dsp_context_check", "s3dsp_hash_build", "s3dsp_hash_free", "s3dsp_hash_size",
-    "s3dsp_hash_lookup", "s3dsp_kmap_build_subm3", "s3dsp_kmap_build_subm3_rows", "s3dsp_subdivide", "s3dsp_kmap_free",
+    "s3dsp_hash_lookup", "s3dsp_kmap_build_subm3", "s3dsp_kmap_build_subm3_rows", "s3dsp_kmap_build_subm3_range", "s3dsp_subdivide", "s3dsp_kmap_free",
     "s3dsp_kmap_rows", "s3dsp_kmap_export_dense", "s3dsp_kmap_pairs", "s3dsp_kmap_pairs_noalloc",
     "s3dsp_weights_packed_bytes", "s3dsp_weights_pack", "s3dsp_gn_partials_count", "s3dsp_conv", "s3dsp_conv_kernel",
     "s3dsp_gn_stats", "s3dsp_gn_finalize", "s3dsp_channel_affine", "s3dsp_layer_norm",
@@ -80,6 +80,7 @@ def load(path: str = LIB_PATH):
         "s3dsp_hash_lookup": (_u32, [_vp, _vp, _vp, _i64, _vp, _cp, _u64]),
         "s3dsp_kmap_build_subm3": (_u32, [_vp, _vp, ctypes.POINTER(_vp), _cp, _u64]),
         "s3dsp_kmap_build_subm3_rows": (_u32, [_vp, _vp, _i64, ctypes.POINTER(_vp), _cp, _u64]),
+        "s3dsp_kmap_build_subm3_range": (_u32, [_vp, _vp, _i64, _i64, ctypes.POINTER(_vp), _cp, _u64]),
         "s3dsp_subdivide": (_u32, [_vp, _vp, _vp, ctypes.POINTER(_vp), _cp, _u64]),
         "s3dsp_kmap_free": (None, [_vp, _vp]),
         "s3dsp_kmap_rows": (_i64, [_vp]),
@@ -240,6 +241,12 @@ class Context:
         k = _vp()
         _call(load().s3dsp_kmap_build_subm3_rows, self.handle, hsh.handle, n_out, ctypes.byref(k))
         return Kmap(self, k.value, n_out)
+
+    def kmap_subm3_range(self, hsh: Hash, row_begin: int, row_end: int) -> Kmap:
+        """Submanifold map of hash rows [row_begin, row_end), gathering from all rows."""
+        k = _vp()
+        _call(load().s3dsp_kmap_build_subm3_range, self.handle, hsh.handle, row_begin, row_end, ctypes.byref(k))
+        return Kmap(self, k.value, row_end - row_begin)
 
     def subdivide(self, parents: Hash, child_coords_out) -> Kmap:
         k = _vp()

@@ -4,7 +4,9 @@ Objects (`assign_objects`): whole objects are dealt to ranks, largest first,
 each to the rank with the least voxels so far (longest-processing-time
 first); objects never talk to each other, so there is no collective.
 
-One large volume (Morton-ordered slabs + halo):
+One large volume (Morton-ordered slabs + halo; each rank's own rows are
+ordered interior first, so the interior rows' conv can run while the halo
+is exchanged):
 
 The volume's active voxels are sorted by their 3D Morton code and cut into
 `world` contiguous ranges of (nearly) equal voxel count; rank r owns range r.
@@ -86,11 +88,12 @@ def _packed_keys(c: np.ndarray) -> np.ndarray:
 class HaloPlan:
     rank: int
     world: int
-    own: np.ndarray          # global row ids of this rank's voxels, Morton order
+    own: np.ndarray          # global row ids of this rank's voxels: interior, then boundary (Morton order in each)
     ghost: np.ndarray        # global row ids of the halo, grouped by owner rank, Morton order within
     recv_counts: np.ndarray  # [world] ghost rows received from each rank
     send_rows: np.ndarray    # local row indices (into `own`) sent, grouped by destination rank
     send_counts: np.ndarray  # [world]
+    n_interior: int = 0      # own rows [0, n_interior) have no neighbour on another rank
 
     @property
     def n_own(self) -> int:
@@ -139,6 +142,11 @@ def plan_halos(coords: np.ndarray, world: int) -> list[HaloPlan]:
     plans = []
     for r in range(world):
         own = order[bounds[r]:bounds[r + 1]]
+        # interior rows first: their conv needs no halo, so it can run while the halo is in flight
+        nb = nb_owner[own]
+        boundary = ((nb >= 0) & (nb != r)).any(axis=1)
+        own = np.concatenate([own[~boundary], own[boundary]])
+        n_interior = int((~boundary).sum())
         # ghosts: voxels of other ranks adjacent to some voxel of r
         # == voxels v with owner != r having a neighbour owned by r
         touches_r = (nb_owner == r).any(axis=1)
@@ -156,7 +164,7 @@ def plan_halos(coords: np.ndarray, world: int) -> list[HaloPlan]:
             send.append(sel)
             send_counts[p] = sel.shape[0]
         send_rows = np.concatenate(send) if send else np.zeros(0, dtype=np.int64)
-        plans.append(HaloPlan(r, world, own, g, recv_counts, send_rows, send_counts))
+        plans.append(HaloPlan(r, world, own, g, recv_counts, send_rows, send_counts, n_interior))
     return plans
 
 

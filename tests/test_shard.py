@@ -63,6 +63,12 @@ def test_plan_matches_bruteforce(world):
                 j = index.get((x + dx, y + dy, z + dz))
                 if j is not None and owner[j] != p.rank:
                     want.add(j)
+        # own rows: interior (no neighbour on another rank) first, then boundary
+        for pos_, i in enumerate(p.own):
+            x, y, z = coords[i][1:]
+            remote = any((j := index.get((x + dx, y + dy, z + dz))) is not None and owner[j] != p.rank
+                         for dx, dy, dz in offs)
+            assert remote == (pos_ >= p.n_interior)
         assert set(p.ghost.tolist()) == want
         assert len(p.ghost) == len(want)
         assert p.recv_counts.sum() == p.n_ghost

@@ -90,3 +90,37 @@ def test_sharded_default_dispatch(ctx):
     # different kernels / split-tile sums on the two sides: bf16 output rounding
     rel = np.sqrt(((got.astype(np.float64) - ref) ** 2).sum() / (ref.astype(np.float64) ** 2).sum())
     assert rel < 1e-2
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_interior_then_boundary_maps(ctx, world):
+    """A shard's own rows as two maps (interior rows, which need no halo, and
+    boundary rows) over the same [own | ghost] input: what a rank computes
+    while its halo is in flight, then after it lands."""
+    coords = workloads.ellipsoid_shell(40, 3)
+    c = 64
+    x = dev(workloads.normal((len(coords), c), 4)).to(torch.bfloat16)
+    ws, bs = layers(ctx, c, 2)
+    ref = run_global(ctx, coords, x, ws, bs, s3dsp.CONV_TILE128)
+    plans = shard.plan_halos(coords, world)
+    glob = x.clone()
+    maps = []
+    for p in plans:
+        h = ctx.hash_build(dev(p.shard_coords(coords)))
+        ki = ctx.kmap_subm3_range(h, 0, p.n_interior) if p.n_interior > 0 else None
+        kb = ctx.kmap_subm3_range(h, p.n_interior, p.n_own)
+        maps.append((h, ki, kb))
+    assert any(p.n_interior > 0 for p in plans)
+    for w, b in zip(ws, bs):
+        nxt = torch.empty_like(glob)
+        for p, (h, ki, kb) in zip(plans, maps):
+            rows = torch.as_tensor(np.concatenate([p.own, p.ghost]), device="cuda")
+            xs = glob.index_select(0, rows)
+            out = torch.empty((p.n_own, c), dtype=x.dtype, device="cuda")
+            f = s3dsp.CONV_TILE128 | s3dsp.EPI_SILU
+            if ki is not None:
+                ctx.conv(ki, 27, s3dsp.PREC_BF16, xs, w, b, out[:p.n_interior], c, flags=f)
+            ctx.conv(kb, 27, s3dsp.PREC_BF16, xs, w, b, out[p.n_interior:], c, flags=f)
+            nxt[torch.as_tensor(p.own, device="cuda")] = out
+        glob = nxt
+    assert np.array_equal(glob.float().cpu().numpy(), ref)
