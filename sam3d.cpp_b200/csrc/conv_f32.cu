@@ -62,7 +62,7 @@ __global__ void __launch_bounds__(NT) conv_f32_kernel(const F32ConvParams p) {
     constexpr int TN = BN / 16;
     __shared__ __align__(16) float As[2][BK][BM];
     __shared__ __align__(16) float Bs[2][BK][BN];
-    __shared__ double gsum[64][2];
+    __shared__ double colsum[16][BN][2];  // per row group ty: column sums, summed in a fixed order
 
     const int tid = threadIdx.x;
     const int64_t m0 = (int64_t)blockIdx.x * BM;
@@ -166,10 +166,6 @@ __global__ void __launch_bounds__(NT) conv_f32_kernel(const F32ConvParams p) {
     // epilogue
     const bool stats = p.gn_partials != nullptr;
     const int gs = stats ? p.cout / p.gn_groups : 1;
-    if (stats) {
-        for (int i = tid; i < 64 * 2; i += NT) (&gsum[0][0])[i] = 0.0;
-        __syncthreads();
-    }
     double csum[TN], csq[TN];
 #pragma unroll
     for (int j = 0; j < TN; ++j) csum[j] = csq[j] = 0.0;
@@ -197,20 +193,29 @@ __global__ void __launch_bounds__(NT) conv_f32_kernel(const F32ConvParams p) {
         }
     }
     if (stats) {
+        // deterministic: every thread's column sums to smem, then each group
+        // summed over row groups and columns in a fixed order
 #pragma unroll
         for (int j = 0; j < TN; ++j) {
-            const int col = n0 + tx * TN + j;
-            if (col >= p.cout) continue;
-            const int g = col / gs;
-            atomicAdd(&gsum[g][0], csum[j]);
-            atomicAdd(&gsum[g][1], csq[j]);
+            colsum[ty][tx * TN + j][0] = csum[j];
+            colsum[ty][tx * TN + j][1] = csq[j];
         }
         __syncthreads();
+        const int limit = min(BN, p.cout - n0);
         const int g_lo = n0 / gs;
-        const int g_hi = min(p.gn_groups - 1, (min(n0 + BN, p.cout) - 1) / gs);
+        const int g_hi = min(p.gn_groups - 1, (n0 + limit - 1) / gs);
         for (int g = g_lo + tid; g <= g_hi; g += NT) {
-            atomicAdd(p.gn_partials + ((int64_t)tile * p.gn_groups + g) * 2 + 0, gsum[g][0]);
-            atomicAdd(p.gn_partials + ((int64_t)tile * p.gn_groups + g) * 2 + 1, gsum[g][1]);
+            const int c_lo = max(g * gs - n0, 0), c_hi = min((g + 1) * gs - n0, limit);
+            double a = 0.0, b = 0.0;
+            for (int y = 0; y < 16; ++y)
+                for (int c = c_lo; c < c_hi; ++c) {
+                    a += colsum[y][c][0];
+                    b += colsum[y][c][1];
+                }
+            // a group split across two column tiles gets exactly two adds onto a
+            // zeroed slot, which is order independent
+            atomicAdd(p.gn_partials + ((int64_t)tile * p.gn_groups + g) * 2 + 0, a);
+            atomicAdd(p.gn_partials + ((int64_t)tile * p.gn_groups + g) * 2 + 1, b);
         }
     }
 }
