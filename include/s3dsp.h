@@ -122,6 +122,35 @@ S3DSP_API s3d_status s3dsp_hash_lookup(s3dsp_context *ctx, const s3dsp_hash *has
                                        char *error, uint64_t error_capacity);
 
 /* ---------------------------------------------------------------------------
+ * The coordinate pipeline in front of the path (src/objects_runtime/
+ * session.cpp). Each call returns the row count in *count (host) and so
+ * synchronises the context's stream; rows are written only when the count
+ * fits `capacity` (else S3D_INVALID_ARGUMENT, *count still set). Input order
+ * is kept. Coordinates must lie in the hash domain (0 <= b < 32768,
+ * |x|,|y|,|z| < 32768).
+ * ------------------------------------------------------------------------- */
+/* SS occupancy argwhere (session.cpp:1436-1441): d_occ is a C-order f32
+ * [nx, ny, nz] grid; every cell > 0 gives a row (batch, x, y, z), x-major. */
+S3DSP_API s3d_status s3dsp_occupancy_coords(s3dsp_context *ctx, const float *d_occ, int32_t nx,
+                                            int32_t ny, int32_t nz, int32_t batch, int32_t *d_coords,
+                                            int64_t capacity, int64_t *count, char *error,
+                                            uint64_t error_capacity);
+/* prune_surface_coords (session.cpp:129-166): keep the rows with some cell of
+ * their (2*max_axis_dist+1)^3 neighbourhood unoccupied. */
+S3DSP_API s3d_status s3dsp_prune_surface(s3dsp_context *ctx, const int32_t *d_coords, int64_t n,
+                                         int32_t max_axis_dist, int32_t *d_out, int64_t capacity,
+                                         int64_t *count, char *error, uint64_t error_capacity);
+/* downsample_coords (session.cpp:168-236): n <= max_coords rows are copied
+ * unchanged; otherwise every axis is rescaled by 1/factor about the box
+ * centre (double arithmetic, round half up, clamped), first occurrences kept,
+ * and above max_coords again max_coords rows are drawn by std::shuffle with
+ * std::mt19937(seed) (on the host). */
+S3DSP_API s3d_status s3dsp_downsample_coords(s3dsp_context *ctx, const int32_t *d_coords, int64_t n,
+                                             int64_t max_coords, int32_t factor, uint32_t seed,
+                                             int32_t *d_out, int64_t capacity, int64_t *count,
+                                             char *error, uint64_t error_capacity);
+
+/* ---------------------------------------------------------------------------
  * K2 kernel maps. A kmap holds, per kernel offset o (o = kd*9 + kh*3 + kw with
  * (dx,dy,dz) = (kd-1, kh-1, kw-1), sparse_ops.cpp:132), the input row feeding
  * every output row (offset-major [kvol][n_out], -1 = none) plus a per-tile

@@ -70,6 +70,12 @@ def lib():
         L.oracle_downsample_mean.argtypes = [_f32p, _c_i64, _c_i64, _i32p, _f32p, _c_i64, _f32p]
         L.oracle_upsample_nearest.restype = None
         L.oracle_upsample_nearest.argtypes = [_f32p, _c_i64, _c_i64, _i32p, _c_i64, _f32p]
+        L.oracle_occupancy_coords.restype = _c_i64
+        L.oracle_occupancy_coords.argtypes = [_f32p, _c_i32, _c_i32, _c_i32, _c_i32, _i32p]
+        L.oracle_prune_surface.restype = _c_i64
+        L.oracle_prune_surface.argtypes = [_i32p, _c_i64, _c_i32, _i32p]
+        L.oracle_downsample_coords.restype = _c_i64
+        L.oracle_downsample_coords.argtypes = [_i32p, _c_i64, _c_i64, _c_i32, ctypes.c_uint32, _i32p]
         _lib = L
     return _lib
 
@@ -141,6 +147,34 @@ def mesh_subdivide(parents: np.ndarray, use_ref: bool = False):
     if not ok:
         return None
     return cc[:32 * n].reshape(8 * n, 4), nb[:8 * 27 * n].reshape(8 * n, 27)
+
+
+def occupancy_coords(occ: np.ndarray, batch: int = 0) -> np.ndarray:
+    """SS occupancy argwhere (session.cpp:1436-1441): occ [X, Y, Z] > 0 ->
+    int32 rows (batch, x, y, z), x-major."""
+    occ = _c(occ, np.float32)
+    nx, ny, nz = occ.shape
+    out = np.zeros((max(occ.size, 1), 4), np.int32)
+    n = lib().oracle_occupancy_coords(occ.reshape(-1), nx, ny, nz, batch, out.reshape(-1))
+    return out[:n]
+
+
+def prune_surface(coords: np.ndarray, dist: int = 1) -> np.ndarray:
+    """prune_surface_coords (session.cpp:129-166)."""
+    coords = _c(coords, np.int32).reshape(-1, 4)
+    out = np.zeros((max(len(coords), 1), 4), np.int32)
+    n = lib().oracle_prune_surface(coords.reshape(-1) if len(coords) else out.reshape(-1), len(coords), dist,
+                                   out.reshape(-1))
+    return out[:n]
+
+
+def downsample_coords(coords: np.ndarray, max_coords: int = 42000, factor: int = 2, seed: int = 42) -> np.ndarray:
+    """downsample_coords (session.cpp:168-236)."""
+    coords = _c(coords, np.int32).reshape(-1, 4)
+    out = np.zeros((max(len(coords), 1), 4), np.int32)
+    n = lib().oracle_downsample_coords(coords.reshape(-1) if len(coords) else out.reshape(-1), len(coords),
+                                       max_coords, factor, seed, out.reshape(-1))
+    return out[:n]
 
 
 # ---------------------------------------------------------------------------

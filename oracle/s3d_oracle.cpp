@@ -26,6 +26,13 @@
 //     PARITY UNPINNED against GGML (its CPU kernels cannot be built here); the
 //     conv/norm semantics are instead cross-checked in tests against an
 //     independent dense torch.conv3d / group_norm / layer_norm in float64.
+//   * the coordinate pipeline before the path (src/objects_runtime/session.cpp)
+//       - SS occupancy argwhere        session.cpp:1436-1441
+//       - prune_surface_coords         session.cpp:122-166
+//       - downsample_coords            session.cpp:168-236
+//     PARITY UNPINNED against the reference: session.cpp needs GGML and cannot
+//     be built here; the argwhere + prune restatement reproduces the occupancy
+//     counts recorded for the reference's shipped SS fixture (69,537 -> 67,783).
 //
 // Layouts follow GGML's ne order with channels fastest: a feature matrix of
 // (C, N) in GGML is stored here as N rows of C floats.
@@ -35,7 +42,9 @@
 #include <cstdint>
 #include <cstring>
 #include <numeric>
+#include <random>
 #include <thread>
+#include <unordered_set>
 #include <vector>
 
 namespace {
@@ -523,6 +532,115 @@ void oracle_upsample_nearest(const float* x, int64_t nc, int64_t ch, const int32
         for (int64_t k = 0; k < ch; ++k)
             out[i * ch + k] = (c >= 0 && c < nc) ? x[(int64_t)c * ch + k] : 0.0f;
     }
+}
+
+// ---------------------------------------------------------------------------
+// coordinate pipeline (src/objects_runtime/session.cpp)
+// ---------------------------------------------------------------------------
+static inline uint64_t coord_key(int32_t b, int32_t x, int32_t y, int32_t z) {
+    // the reference's coordinate_key (session.cpp:122-127)
+    return ((uint64_t)(uint32_t)b << 48) | ((uint64_t)(uint32_t)x << 32) | ((uint64_t)(uint32_t)y << 16) |
+           ((uint64_t)(uint32_t)z & 0xffffu);
+}
+
+// occupancy argwhere (session.cpp:1436-1441): occ[(x*ny + y)*nz + z] > 0 ->
+// row (batch, x, y, z), x-major. Returns the row count.
+int64_t oracle_occupancy_coords(const float* occ, int32_t nx, int32_t ny, int32_t nz, int32_t batch,
+                                int32_t* out) {
+    int64_t n = 0;
+    for (int32_t x = 0; x < nx; ++x)
+        for (int32_t y = 0; y < ny; ++y)
+            for (int32_t z = 0; z < nz; ++z)
+                if (occ[((int64_t)x * ny + y) * nz + z] > 0.0f) {
+                    out[4 * n + 0] = batch;
+                    out[4 * n + 1] = x;
+                    out[4 * n + 2] = y;
+                    out[4 * n + 3] = z;
+                    ++n;
+                }
+    return n;
+}
+
+// prune_surface_coords (session.cpp:129-166): keep a row iff some cell of its
+// (2d+1)^3 neighbourhood is unoccupied, input order kept. Returns the count.
+int64_t oracle_prune_surface(const int32_t* coords, int64_t n, int32_t d, int32_t* out) {
+    std::unordered_set<uint64_t> occ;
+    occ.reserve((size_t)n * 2);
+    for (int64_t i = 0; i < n; ++i) occ.insert(coord_key(coords[4 * i], coords[4 * i + 1], coords[4 * i + 2], coords[4 * i + 3]));
+    int64_t m = 0;
+    for (int64_t i = 0; i < n; ++i) {
+        const int32_t* c = coords + 4 * i;
+        bool surface = false;
+        for (int dx = -d; dx <= d && !surface; ++dx)
+            for (int dy = -d; dy <= d && !surface; ++dy)
+                for (int dz = -d; dz <= d && !surface; ++dz)
+                    surface = occ.find(coord_key(c[0], c[1] + dx, c[2] + dy, c[3] + dz)) == occ.end();
+        if (surface) {
+            std::memcpy(out + 4 * m, c, 16);
+            ++m;
+        }
+    }
+    return m;
+}
+
+// downsample_coords (session.cpp:168-236): above max_coords rows, rescale each
+// axis by 1/factor about the box centre (double arithmetic, round half up,
+// clamped), keep first occurrences, and above max_coords again keep
+// max_coords rows chosen by std::shuffle with std::mt19937(seed). Returns the
+// count; out holds n rows at most. Unfused multiply-add, as the reference is
+// built (-ffp-contract=off, CMakeLists.txt:65).
+__attribute__((optimize("fp-contract=off")))
+int64_t oracle_downsample_coords(const int32_t* coords, int64_t n, int64_t max_coords, int32_t factor,
+                                 uint32_t seed, int32_t* out) {
+    if (n <= max_coords) {
+        std::memcpy(out, coords, (size_t)n * 16);
+        return n;
+    }
+    int32_t lo[3] = {coords[1], coords[2], coords[3]}, hi[3] = {coords[1], coords[2], coords[3]};
+    for (int64_t i = 1; i < n; ++i)
+        for (int c = 0; c < 3; ++c) {
+            lo[c] = std::min(lo[c], coords[4 * i + c + 1]);
+            hi[c] = std::max(hi[c], coords[4 * i + c + 1]);
+        }
+    double target[3], tmin[3];
+    int32_t tmin_i[3], tmax_i[3];
+    for (int c = 0; c < 3; ++c) {
+        const double original = (double)(hi[c] - lo[c] + 1);
+        target[c] = original / (double)factor;
+        const double offset = (original - target[c]) * 0.5;
+        tmin[c] = (double)lo[c] + offset;
+        const double tmax = tmin[c] + target[c] - 1.0;
+        tmin_i[c] = (int32_t)tmin[c];  // truncation toward zero, as torch .int()
+        tmax_i[c] = (int32_t)tmax;
+    }
+    std::vector<int32_t> uniq;
+    std::unordered_set<uint64_t> seen;
+    seen.reserve((size_t)n * 2);
+    for (int64_t i = 0; i < n; ++i) {
+        const int32_t* p = coords + 4 * i;
+        int32_t o[4] = {p[0], 0, 0, 0};
+        for (int c = 0; c < 3; ++c) {
+            const double denom = (double)(hi[c] - lo[c]);
+            const double normalized = denom > 0.0 ? ((double)p[c + 1] - lo[c]) / denom : 0.0;
+            const double value = normalized * (target[c] - 1.0) + tmin[c];
+            int64_t r = (int64_t)std::floor(value + 0.5);
+            r = std::max<int64_t>(r, tmin_i[c]);
+            r = std::min<int64_t>(r, tmax_i[c]);
+            o[c + 1] = (int32_t)r;
+        }
+        if (seen.insert(coord_key(o[0], o[1], o[2], o[3])).second) uniq.insert(uniq.end(), o, o + 4);
+    }
+    const int64_t un = (int64_t)uniq.size() / 4;
+    if (un > max_coords) {
+        std::mt19937 rng(seed);
+        std::vector<size_t> order((size_t)un);
+        std::iota(order.begin(), order.end(), 0);
+        std::shuffle(order.begin(), order.end(), rng);
+        for (int64_t j = 0; j < max_coords; ++j) std::memcpy(out + 4 * j, &uniq[order[(size_t)j] * 4], 16);
+        return max_coords;
+    }
+    std::memcpy(out, uniq.data(), (size_t)un * 16);
+    return un;
 }
 
 }  // extern "C"

@@ -33,12 +33,6 @@ struct Scratch {
     }
 };
 
-#define S3DSP_TRY(call)                  \
-    do {                                 \
-        const s3d_status s_ = (call);    \
-        if (s_ != S3D_OK) return s_;     \
-    } while (0)
-
 }  // namespace
 
 extern "C" S3DSP_API s3d_status s3dsp_res_block_gn(s3dsp_context* ctx, const s3dsp_kmap* kmap, uint32_t precision,

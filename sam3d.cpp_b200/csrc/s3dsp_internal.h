@@ -103,6 +103,13 @@ inline size_t dtype_size(uint32_t dt) { return dt == S3DSP_F32 ? 4 : 2; }
 inline bool dtype_ok(uint32_t dt) { return dt == S3DSP_F32 || dt == S3DSP_BF16 || dt == S3DSP_F16; }
 
 // Reads back the device status words and turns them into a status.
+// return a C-ABI call's status when it is not S3D_OK
+#define S3DSP_TRY(call)               \
+    do {                              \
+        const s3d_status s_ = (call); \
+        if (s_ != S3D_OK) return s_;  \
+    } while (0)
+
 s3d_status check_status(s3dsp_context* ctx, char* error, uint64_t error_capacity);
 
 // launch helpers implemented in the .cu files

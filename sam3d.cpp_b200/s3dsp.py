@@ -32,7 +32,8 @@ CONTEXT_OWN_STREAM = 2
 EXPORTED = [
     "s3dsp_abi_version", "s3dsp_context_create", "s3dsp_context_free", "s3dsp_context_stream",
     "s3dsp_context_check", "s3dsp_hash_build", "s3dsp_hash_free", "s3dsp_hash_size",
-    "s3dsp_hash_lookup", "s3dsp_kmap_build_subm3", "s3dsp_kmap_build_subm3_rows", "s3dsp_kmap_build_subm3_range", "s3dsp_subdivide", "s3dsp_kmap_free",
+    "s3dsp_hash_lookup", "s3dsp_occupancy_coords", "s3dsp_prune_surface", "s3dsp_downsample_coords",
+    "s3dsp_kmap_build_subm3", "s3dsp_kmap_build_subm3_rows", "s3dsp_kmap_build_subm3_range", "s3dsp_subdivide", "s3dsp_kmap_free",
     "s3dsp_kmap_rows", "s3dsp_kmap_export_dense", "s3dsp_kmap_pairs", "s3dsp_kmap_pairs_noalloc",
     "s3dsp_weights_packed_bytes", "s3dsp_weights_pack", "s3dsp_gn_partials_count", "s3dsp_conv", "s3dsp_conv_kernel",
     "s3dsp_gn_stats", "s3dsp_gn_finalize", "s3dsp_channel_affine", "s3dsp_layer_norm",
@@ -78,6 +79,11 @@ def load(path: str = LIB_PATH):
         "s3dsp_hash_free": (None, [_vp, _vp]),
         "s3dsp_hash_size": (_i64, [_vp]),
         "s3dsp_hash_lookup": (_u32, [_vp, _vp, _vp, _i64, _vp, _cp, _u64]),
+        "s3dsp_occupancy_coords": (_u32, [_vp, _vp, _i32, _i32, _i32, _i32, _vp, _i64, ctypes.POINTER(_i64), _cp,
+                                          _u64]),
+        "s3dsp_prune_surface": (_u32, [_vp, _vp, _i64, _i32, _vp, _i64, ctypes.POINTER(_i64), _cp, _u64]),
+        "s3dsp_downsample_coords": (_u32, [_vp, _vp, _i64, _i64, _i32, ctypes.c_uint32, _vp, _i64,
+                                           ctypes.POINTER(_i64), _cp, _u64]),
         "s3dsp_kmap_build_subm3": (_u32, [_vp, _vp, ctypes.POINTER(_vp), _cp, _u64]),
         "s3dsp_kmap_build_subm3_rows": (_u32, [_vp, _vp, _i64, ctypes.POINTER(_vp), _cp, _u64]),
         "s3dsp_kmap_build_subm3_range": (_u32, [_vp, _vp, _i64, _i64, ctypes.POINTER(_vp), _cp, _u64]),
@@ -230,6 +236,27 @@ class Context:
 
     def hash_lookup(self, hsh: Hash, query, rows_out):
         _call(load().s3dsp_hash_lookup, self.handle, hsh.handle, ptr(query), query.shape[0], ptr(rows_out))
+
+    # ---- coordinate pipeline -----------------------------------------------
+    def occupancy_coords(self, occ, out, batch: int = 0) -> int:
+        """Rows (batch, x, y, z) of the cells of occ [X, Y, Z] > 0 into out [cap, 4]; returns the count."""
+        n = ctypes.c_int64()
+        nx, ny, nz = occ.shape
+        _call(load().s3dsp_occupancy_coords, self.handle, ptr(occ), nx, ny, nz, batch, ptr(out), out.shape[0],
+              ctypes.byref(n))
+        return n.value
+
+    def prune_surface(self, coords, out, max_axis_dist: int = 1) -> int:
+        n = ctypes.c_int64()
+        _call(load().s3dsp_prune_surface, self.handle, ptr(coords), coords.shape[0], max_axis_dist, ptr(out),
+              out.shape[0], ctypes.byref(n))
+        return n.value
+
+    def downsample_coords(self, coords, out, max_coords: int = 42000, factor: int = 2, seed: int = 42) -> int:
+        n = ctypes.c_int64()
+        _call(load().s3dsp_downsample_coords, self.handle, ptr(coords), coords.shape[0], max_coords, factor, seed,
+              ptr(out), out.shape[0], ctypes.byref(n))
+        return n.value
 
     def kmap_subm3(self, hsh: Hash) -> Kmap:
         k = _vp()
