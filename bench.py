@@ -639,6 +639,77 @@ def run_layers(args, rank, world, local_rank):
 
 
 # ---------------------------------------------------------------------------
+# the coordinate pipeline in front of the path (session.cpp argwhere, prune, downsample)
+# ---------------------------------------------------------------------------
+def run_coords(args, rank, world, local_rank):
+    """SS occupancy -> coordinates as the reference runs it before the SLat
+    stage: argwhere of the 64^3 occupancy grid, surface pruning, downsample to
+    at most 42,000 rows (identity below). Input: the reference's shipped SS
+    decoder occupancy fixture (69,537 occupied -> 67,783 surface voxels),
+    resident on the device. A step = the three calls (each returns its count
+    to the host). Unit: one input occupancy cell. Replicas only at N > 1."""
+    import torch
+    import s3dsp
+    import oracle
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    stream = torch.cuda.Stream(device)
+    torch.cuda.set_stream(stream)
+    ctx = s3dsp.Context(local_rank, stream=stream.cuda_stream)
+    bits = np.load(os.path.join(ROOT, "tests", "golden", "ss_occ_mask.npz"))["bits"]
+    grid_h = np.unpackbits(bits)[: 64 ** 3].astype(np.float32).reshape(64, 64, 64)
+    grid = torch.from_numpy(grid_h).to(device)
+    a = torch.empty((grid.numel(), 4), dtype=torch.int32, device=device)
+    b = torch.empty_like(a)
+    c = torch.empty_like(a)
+    counts = []
+
+    def step():
+        n = ctx.occupancy_coords(grid, a)
+        m = ctx.prune_surface(a[:n], b)
+        k = ctx.downsample_coords(b[:m], c, 42000, 2, 42)
+        counts[:] = [n, m, k]
+
+    for _ in range(args.warmup):
+        step()
+    stream.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for i in range(args.steps):
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    stream.synchronize()
+    ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends)) / args.steps
+    vals = torch.tensor([ms], dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX)
+    ms = vals.item()
+    if rank != 0:
+        return None
+    t0 = time.perf_counter()
+    reps = 5
+    for _ in range(reps):
+        oc = oracle.occupancy_coords(grid_h)
+        pr = oracle.prune_surface(oc)
+        oracle.downsample_coords(pr, 42000, 2, 42)
+    cpu_s = (time.perf_counter() - t0) / reps
+    cells = grid_h.size
+    return {
+        "metric": "occupancy cells/s (argwhere + surface prune + downsample)", "value": cells * world / (ms / 1e3),
+        "unit": "cells/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int32",
+        "data": "the reference's shipped 64^3 SS occupancy fixture (tests/golden/ss_occ_mask.npz)",
+        "config": {"workload": "coordinate pipeline: 64^3 occupancy -> coords -> surface prune -> downsample "
+                               "(max 42,000)", "counts": counts, "parallelism": f"replicas{world}",
+                   "note": "each call returns its row count to the host (a stream synchronisation per call)"},
+        "cpu_baseline": {"value": cells / cpu_s, "unit": "cells/s", "cores": 1, "kind": "port",
+                         "sample": "the same three steps through the oracle's single-threaded restatement"},
+    }
+
+
+# ---------------------------------------------------------------------------
 # CPU path (reference arm and cpu_baseline)
 # ---------------------------------------------------------------------------
 def cpu_step(cfg, threads):
@@ -695,10 +766,11 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="config2", choices=["config2", "config1", "config3", "volume", "objects"],
+    ap.add_argument("--workload", default="config2",
+                    choices=["config2", "config1", "config3", "volume", "objects", "coords"],
                     help="config2: the headline (default); volume: config 5b, one volume split across ranks; "
                          "objects: config 5a, 64 objects through config 4 sharded by object; "
-                         "config1 / config3: single layers")
+                         "config1 / config3: single layers; coords: the coordinate pipeline before the path")
     ap.add_argument("--precision", default="f32", choices=["f32", "bf16"], help="config1 / config3 only")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -714,7 +786,7 @@ def main():
             torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                                  device_id=torch.device("cuda", local_rank))
         runner = {"config2": run_ours, "volume": run_volume, "objects": run_objects, "config1": run_layers,
-                  "config3": run_layers}[args.workload]
+                  "config3": run_layers, "coords": run_coords}[args.workload]
         line = runner(args, rank, world, local_rank)
         if world > 1:
             import torch
