@@ -710,6 +710,74 @@ def run_coords(args, rank, world, local_rank):
 
 
 # ---------------------------------------------------------------------------
+# GS decoder Swin window tables (GsTables::build)
+# ---------------------------------------------------------------------------
+def run_gs_tables(args, rank, world, local_rank):
+    """The GS decoder's per-object tables (sparse_ops.cpp:182-270): window
+    buckets for shift (0,0,0) and (4,4,4) plus the 768-channel absolute
+    position embedding, over the config-2 coordinates resident on the device.
+    A step = both window tables and the embedding (each table call returns its
+    bucket list to the host). Unit: one voxel. Replicas only at N > 1."""
+    import torch
+    import s3dsp
+    import oracle
+    import workloads
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    stream = torch.cuda.Stream(device)
+    torch.cuda.set_stream(stream)
+    ctx = s3dsp.Context(local_rank, stream=stream.cuda_stream)
+    coords_h = workloads.config2(seed=0)["coords"]
+    n = len(coords_h)
+    coords = torch.from_numpy(coords_h).to(device)
+    bkt = [torch.empty(n, dtype=torch.int32, device=device) for _ in range(2)]
+    bwd = [torch.empty(n, dtype=torch.int32, device=device) for _ in range(2)]
+    ape = torch.empty((n, 768), dtype=torch.float32, device=device)
+    nbk = []
+
+    def step():
+        nbk[:] = [len(ctx.gs_window_tables(coords, 4 * si, bkt[si], bwd[si])) for si in (0, 1)]
+        ctx.ape(coords, ape)
+
+    for _ in range(args.warmup):
+        step()
+    stream.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for i in range(args.steps):
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    stream.synchronize()
+    ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends)) / args.steps
+    vals = torch.tensor([ms], dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX)
+    ms = vals.item()
+    if rank != 0:
+        return None
+    t0 = time.perf_counter()
+    reps = 5
+    for _ in range(reps):
+        for si in (0, 1):
+            oracle.gs_window_tables(coords_h, si)
+        oracle.ape(coords_h)
+    cpu_s = (time.perf_counter() - t0) / reps
+    return {
+        "metric": "voxels/s (GS window tables, both shifts, + APE)", "value": n * world / (ms / 1e3),
+        "unit": "voxels/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int32+f32",
+        "data": "synthetic: the config-2 64^3 ellipsoid shell coordinates",
+        "config": {"workload": "GS decoder tables: Swin windows (8^3, shifts 0 and 4) + 768-ch APE",
+                   "voxels": n, "buckets": nbk, "parallelism": f"replicas{world}",
+                   "note": "each table call returns its bucket list to the host (a stream synchronisation)"},
+        "cpu_baseline": {"value": n / cpu_s, "unit": "voxels/s", "cores": 1, "kind": "port",
+                         "sample": "the same tables through the oracle's single-threaded restatement"},
+    }
+
+
+# ---------------------------------------------------------------------------
 # CPU path (reference arm and cpu_baseline)
 # ---------------------------------------------------------------------------
 def cpu_step(cfg, threads):
@@ -767,10 +835,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="config2",
-                    choices=["config2", "config1", "config3", "volume", "objects", "coords"],
+                    choices=["config2", "config1", "config3", "volume", "objects", "coords", "gs_tables"],
                     help="config2: the headline (default); volume: config 5b, one volume split across ranks; "
                          "objects: config 5a, 64 objects through config 4 sharded by object; "
-                         "config1 / config3: single layers; coords: the coordinate pipeline before the path")
+                         "config1 / config3: single layers; coords: the coordinate pipeline before the path; "
+                         "gs_tables: the GS decoder's Swin window tables and APE")
     ap.add_argument("--precision", default="f32", choices=["f32", "bf16"], help="config1 / config3 only")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -786,7 +855,7 @@ def main():
             torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                                  device_id=torch.device("cuda", local_rank))
         runner = {"config2": run_ours, "volume": run_volume, "objects": run_objects, "config1": run_layers,
-                  "config3": run_layers, "coords": run_coords}[args.workload]
+                  "config3": run_layers, "coords": run_coords, "gs_tables": run_gs_tables}[args.workload]
         line = runner(args, rank, world, local_rank)
         if world > 1:
             import torch

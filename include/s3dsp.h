@@ -151,6 +151,28 @@ S3DSP_API s3d_status s3dsp_downsample_coords(s3dsp_context *ctx, const int32_t *
                                              char *error, uint64_t error_capacity);
 
 /* ---------------------------------------------------------------------------
+ * GS decoder Swin window tables and position embedding (GsTables::build,
+ * src/objects_runtime/sparse_ops.cpp:182-270).
+ * ------------------------------------------------------------------------- */
+/* Windows of side `window` (8 in the reference) over the coordinates shifted
+ * by `shift` (0 or 4): a window's id is the order of its first token; tokens
+ * are grouped by window (table order inside) and windows laid out by token
+ * count ascending (id order inside a count). d_bkt_idx[row] = token,
+ * d_bwd_idx[token] = row (device, [n] each); h_buckets[3k..3k+2] = {tokens per
+ * window, first row, windows} per distinct count (host). Synchronises the
+ * context's stream; *n_buckets is set even when it exceeds bucket_capacity
+ * (then S3D_INVALID_ARGUMENT). */
+S3DSP_API s3d_status s3dsp_gs_window_tables(s3dsp_context *ctx, const int32_t *d_coords, int64_t n,
+                                            int32_t shift, int32_t window, int32_t *d_bkt_idx,
+                                            int32_t *d_bwd_idx, int32_t *h_buckets,
+                                            int64_t bucket_capacity, int64_t *n_buckets, char *error,
+                                            uint64_t error_capacity);
+/* AbsolutePositionEmbedder: d_out [n, channels] f32, per axis channels/6 sines
+ * then channels/6 cosines of coordinate * 10000^(-i/(channels/6)). */
+S3DSP_API s3d_status s3dsp_ape(s3dsp_context *ctx, const int32_t *d_coords, int64_t n, int32_t channels,
+                               float *d_out, char *error, uint64_t error_capacity);
+
+/* ---------------------------------------------------------------------------
  * K2 kernel maps. A kmap holds, per kernel offset o (o = kd*9 + kh*3 + kw with
  * (dx,dy,dz) = (kd-1, kh-1, kw-1), sparse_ops.cpp:132), the input row feeding
  * every output row (offset-major [kvol][n_out], -1 = none) plus a per-tile

@@ -76,6 +76,10 @@ def lib():
         L.oracle_prune_surface.argtypes = [_i32p, _c_i64, _c_i32, _i32p]
         L.oracle_downsample_coords.restype = _c_i64
         L.oracle_downsample_coords.argtypes = [_i32p, _c_i64, _c_i64, _c_i32, ctypes.c_uint32, _i32p]
+        L.oracle_gs_window_tables.restype = _c_i64
+        L.oracle_gs_window_tables.argtypes = [_i32p, _c_i64, _c_i32, _c_i32, _i32p, _i32p, _i32p]
+        L.oracle_ape.restype = None
+        L.oracle_ape.argtypes = [_i32p, _c_i64, _c_i32, _f32p]
         _lib = L
     return _lib
 
@@ -94,6 +98,8 @@ def ref_lib():
         L.ref_slat_tables.argtypes = [_i32p, _c_i64, _c_i32, _i32p, _i32p, _f32p, _i32p, _i32p]
         L.ref_mesh_subdivide.restype = _c_i32
         L.ref_mesh_subdivide.argtypes = [_i32p, _c_i64, _i32p, _i32p]
+        L.ref_gs_tables.restype = _c_i64
+        L.ref_gs_tables.argtypes = [_i32p, _c_i64, _c_i32, _i32p, _i32p, _i32p, _vp]
         _ref = L
     return _ref
 
@@ -147,6 +153,39 @@ def mesh_subdivide(parents: np.ndarray, use_ref: bool = False):
     if not ok:
         return None
     return cc[:32 * n].reshape(8 * n, 4), nb[:8 * 27 * n].reshape(8 * n, 27)
+
+
+def gs_window_tables(coords: np.ndarray, shift_index: int, use_ref: bool = False):
+    """GsTables::build (sparse_ops.cpp:182-270), shift (0,0,0) or (4,4,4):
+    (bkt_idx [n], bwd_idx [n], buckets [k, 3] = {len, off, n_win})."""
+    coords = _c(coords, np.int32).reshape(-1, 4)
+    n = len(coords)
+    bkt = np.zeros(max(n, 1), np.int32)
+    bwd = np.zeros(max(n, 1), np.int32)
+    bk = np.zeros((max(n, 1), 3), np.int32)
+    if use_ref:
+        k = ref_lib().ref_gs_tables(coords.reshape(-1), n, shift_index, bkt, bwd, bk.reshape(-1), None)
+    else:
+        k = lib().oracle_gs_window_tables(coords.reshape(-1), n, 4 * shift_index, 8, bkt, bwd, bk.reshape(-1))
+    if k < 0:
+        return None
+    return bkt[:n], bwd[:n], bk[:k]
+
+
+def ape(coords: np.ndarray, channels: int = 768, use_ref: bool = False) -> np.ndarray:
+    """AbsolutePositionEmbedder of GsTables::build: [n, channels] f32."""
+    coords = _c(coords, np.int32).reshape(-1, 4)
+    n = len(coords)
+    out = np.zeros((n, channels), np.float32)
+    if use_ref:
+        assert channels == 768
+        d = np.zeros(max(n, 1), np.int32)
+        b = np.zeros((max(n, 1), 3), np.int32)
+        ref_lib().ref_gs_tables(coords.reshape(-1), n, 0, d, d.copy(), b.reshape(-1),
+                                out.ctypes.data_as(ctypes.c_void_p))
+    else:
+        lib().oracle_ape(coords.reshape(-1), n, channels, out.reshape(-1))
+    return out
 
 
 def occupancy_coords(occ: np.ndarray, batch: int = 0) -> np.ndarray:

@@ -8,6 +8,7 @@
 // Wrapped entry points (reference file:line):
 //   sam3d::SlatTables::build           src/objects_runtime/sparse_ops.cpp:49-173
 //   sam3d::MeshSubdivideTables::build  src/objects_runtime/sparse_ops.cpp:272-404
+//   sam3d::GsTables::build             src/objects_runtime/sparse_ops.cpp:182-270
 #include "sparse_ops.hpp"
 
 #include <cstdint>
@@ -43,6 +44,26 @@ int32_t ref_mesh_subdivide(const int32_t* parent_coords, int64_t count,
     std::memcpy(child_coords, t.child_coords.data(), t.child_coords.size() * 4);
     std::memcpy(neighbors, t.neighbors.data(), t.neighbors.size() * 4);
     return 1;
+}
+
+// Runs GsTables::build and copies out shift `si`'s tables (bkt_idx, bwd_idx,
+// buckets as {len, off, n_win} triples) and, when ape is not NULL, the
+// (n, 768) position embedding. Returns the bucket count, or -1 when the
+// reference builder returns false.
+int64_t ref_gs_tables(const int32_t* coords, int64_t n, int32_t si, int32_t* bkt_idx, int32_t* bwd_idx,
+                      int32_t* buckets, float* ape) {
+    sam3d::GsTables t;
+    if (!t.build(coords, n)) return -1;
+    const sam3d::GsWindowTables& w = t.shifts[si];
+    std::memcpy(bkt_idx, w.bkt_idx.data(), w.bkt_idx.size() * 4);
+    std::memcpy(bwd_idx, w.bwd_idx.data(), w.bwd_idx.size() * 4);
+    for (size_t k = 0; k < w.buckets.size(); ++k) {
+        buckets[3 * k + 0] = w.buckets[k].len;
+        buckets[3 * k + 1] = w.buckets[k].off;
+        buckets[3 * k + 2] = w.buckets[k].n_win;
+    }
+    if (ape) std::memcpy(ape, t.ape.data(), t.ape.size() * 4);
+    return (int64_t)w.buckets.size();
 }
 
 }  // extern "C"

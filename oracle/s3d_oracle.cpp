@@ -8,6 +8,8 @@
 //   * integer tables
 //       - SlatTables::build            src/objects_runtime/sparse_ops.cpp:49-173
 //       - MeshSubdivideTables::build   src/objects_runtime/sparse_ops.cpp:272-404
+//       - GsTables::build (Swin window buckets + APE)
+//                                      src/objects_runtime/sparse_ops.cpp:182-270
 //     PINNED: tests compare these bit-exactly with the reference's own
 //     sparse_ops.cpp compiled into oracle/_ref, and with committed goldens.
 //   * float ops, in GGML graph order (GGML itself is an un-vendored submodule,
@@ -44,6 +46,7 @@
 #include <numeric>
 #include <random>
 #include <thread>
+#include <unordered_map>
 #include <unordered_set>
 #include <vector>
 
@@ -641,6 +644,85 @@ int64_t oracle_downsample_coords(const int32_t* coords, int64_t n, int64_t max_c
     }
     std::memcpy(out, uniq.data(), (size_t)un * 16);
     return un;
+}
+
+// ---------------------------------------------------------------------------
+// GS decoder Swin window tables (sparse_ops.cpp:182-270)
+// ---------------------------------------------------------------------------
+// Windows of side `window` over coords shifted by `shift` (C division); a
+// window's id is the order of its first token; tokens are grouped by window
+// (window-id order, table order inside), and windows are laid out by token
+// count ascending, window-id order within a count. bkt_idx[row] = original
+// token, bwd_idx[token] = row; buckets[3*k] = {len, first row, windows}.
+// Returns the bucket count, or -1 for n <= 0.
+int64_t oracle_gs_window_tables(const int32_t* coords, int64_t n, int32_t shift, int32_t window, int32_t* bkt_idx,
+                                int32_t* bwd_idx, int32_t* buckets) {
+    if (n <= 0) return -1;
+    struct K {
+        int32_t b, x, y, z;
+        bool operator==(const K& o) const { return b == o.b && x == o.x && y == o.y && z == o.z; }
+    };
+    struct H {
+        size_t operator()(const K& k) const {
+            return std::hash<uint64_t>()(((uint64_t)(uint32_t)k.b << 32) ^ ((uint64_t)(uint32_t)k.x << 21) ^
+                                         ((uint64_t)(uint32_t)k.y << 10) ^ (uint64_t)(uint32_t)k.z);
+        }
+    };
+    std::unordered_map<K, int32_t, H> ids;
+    std::vector<int32_t> wid((size_t)n);
+    for (int64_t i = 0; i < n; ++i) {
+        const K k{coords[4 * i], (coords[4 * i + 1] + shift) / window, (coords[4 * i + 2] + shift) / window,
+                  (coords[4 * i + 3] + shift) / window};
+        wid[(size_t)i] = ids.emplace(k, (int32_t)ids.size()).first->second;
+    }
+    const int32_t nw = (int32_t)ids.size();
+    // tokens per window and each window's tokens in table order (counting sort)
+    std::vector<int32_t> cnt((size_t)nw, 0), start((size_t)nw + 1, 0), tokens((size_t)n);
+    for (int64_t i = 0; i < n; ++i) ++cnt[(size_t)wid[(size_t)i]];
+    for (int32_t w = 0; w < nw; ++w) start[(size_t)w + 1] = start[(size_t)w] + cnt[(size_t)w];
+    std::vector<int32_t> fill(start.begin(), start.end() - 1);
+    for (int64_t i = 0; i < n; ++i) tokens[(size_t)fill[(size_t)wid[(size_t)i]]++] = (int32_t)i;
+    // windows by (token count, id)
+    std::vector<int32_t> wins((size_t)nw);
+    std::iota(wins.begin(), wins.end(), 0);
+    std::stable_sort(wins.begin(), wins.end(), [&](int32_t a, int32_t b) { return cnt[(size_t)a] < cnt[(size_t)b]; });
+    int32_t row = 0;
+    int64_t nb = 0;
+    for (size_t k = 0; k < wins.size(); ++k) {
+        const int32_t w = wins[k];
+        const int32_t len = cnt[(size_t)w];
+        if (k == 0 || len != cnt[(size_t)wins[k - 1]]) {
+            buckets[3 * nb + 0] = len;
+            buckets[3 * nb + 1] = row;
+            buckets[3 * nb + 2] = 0;
+            ++nb;
+        }
+        ++buckets[3 * (nb - 1) + 2];
+        for (int32_t j = 0; j < len; ++j) {
+            const int32_t t = tokens[(size_t)(start[(size_t)w] + j)];
+            bkt_idx[row] = t;
+            bwd_idx[t] = row;
+            ++row;
+        }
+    }
+    return nb;
+}
+
+// AbsolutePositionEmbedder (sparse_ops.cpp:242-262): per token and axis,
+// channels/6 sines then channels/6 cosines of coordinate * 10000^(-i/(channels/6)).
+void oracle_ape(const int32_t* coords, int64_t n, int32_t channels, float* out) {
+    const int f = channels / 6;
+    std::vector<float> freq((size_t)f);
+    for (int i = 0; i < f; ++i) freq[(size_t)i] = 1.0f / powf(10000.0f, (float)i / (float)f);
+    for (int64_t t = 0; t < n; ++t)
+        for (int a = 0; a < 3; ++a) {
+            const float v = (float)coords[4 * t + 1 + a];
+            float* o = out + (size_t)t * channels + (size_t)a * 2 * f;
+            for (int i = 0; i < f; ++i) {
+                o[i] = sinf(v * freq[(size_t)i]);
+                o[f + i] = cosf(v * freq[(size_t)i]);
+            }
+        }
 }
 
 }  // extern "C"

@@ -32,7 +32,7 @@ CONTEXT_OWN_STREAM = 2
 EXPORTED = [
     "s3dsp_abi_version", "s3dsp_context_create", "s3dsp_context_free", "s3dsp_context_stream",
     "s3dsp_context_check", "s3dsp_hash_build", "s3dsp_hash_free", "s3dsp_hash_size",
-    "s3dsp_hash_lookup", "s3dsp_occupancy_coords", "s3dsp_prune_surface", "s3dsp_downsample_coords",
+    "s3dsp_hash_lookup", "s3dsp_gs_window_tables", "s3dsp_ape", "s3dsp_occupancy_coords", "s3dsp_prune_surface", "s3dsp_downsample_coords",
     "s3dsp_kmap_build_subm3", "s3dsp_kmap_build_subm3_rows", "s3dsp_kmap_build_subm3_range", "s3dsp_subdivide", "s3dsp_kmap_free",
     "s3dsp_kmap_rows", "s3dsp_kmap_export_dense", "s3dsp_kmap_pairs", "s3dsp_kmap_pairs_noalloc",
     "s3dsp_weights_packed_bytes", "s3dsp_weights_pack", "s3dsp_gn_partials_count", "s3dsp_conv", "s3dsp_conv_kernel",
@@ -79,6 +79,9 @@ def load(path: str = LIB_PATH):
         "s3dsp_hash_free": (None, [_vp, _vp]),
         "s3dsp_hash_size": (_i64, [_vp]),
         "s3dsp_hash_lookup": (_u32, [_vp, _vp, _vp, _i64, _vp, _cp, _u64]),
+        "s3dsp_gs_window_tables": (_u32, [_vp, _vp, _i64, _i32, _i32, _vp, _vp, _vp, _i64, ctypes.POINTER(_i64), _cp,
+                                          _u64]),
+        "s3dsp_ape": (_u32, [_vp, _vp, _i64, _i32, _vp, _cp, _u64]),
         "s3dsp_occupancy_coords": (_u32, [_vp, _vp, _i32, _i32, _i32, _i32, _vp, _i64, ctypes.POINTER(_i64), _cp,
                                           _u64]),
         "s3dsp_prune_surface": (_u32, [_vp, _vp, _i64, _i32, _vp, _i64, ctypes.POINTER(_i64), _cp, _u64]),
@@ -236,6 +239,22 @@ class Context:
 
     def hash_lookup(self, hsh: Hash, query, rows_out):
         _call(load().s3dsp_hash_lookup, self.handle, hsh.handle, ptr(query), query.shape[0], ptr(rows_out))
+
+    # ---- GS decoder window tables ---------------------------------------------
+    def gs_window_tables(self, coords, shift: int, bkt_idx, bwd_idx, window: int = 8):
+        """Fills bkt_idx / bwd_idx (device int32 [n]); returns the buckets as a
+        numpy [k, 3] array of {tokens per window, first row, windows}."""
+        import numpy as np
+        n = coords.shape[0]
+        cap = max(n, 1)
+        bk = np.zeros((cap, 3), np.int32)
+        nb = ctypes.c_int64()
+        _call(load().s3dsp_gs_window_tables, self.handle, ptr(coords), n, shift, window, ptr(bkt_idx), ptr(bwd_idx),
+              bk.ctypes.data, cap, ctypes.byref(nb))
+        return bk[:nb.value]
+
+    def ape(self, coords, out):
+        _call(load().s3dsp_ape, self.handle, ptr(coords), coords.shape[0], out.shape[1], ptr(out))
 
     # ---- coordinate pipeline -----------------------------------------------
     def occupancy_coords(self, occ, out, batch: int = 0) -> int:

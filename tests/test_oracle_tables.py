@@ -144,3 +144,27 @@ def test_oracle_matches_compiled_reference(seed):
         assert np.array_equal(a[k], b[k]), k
     ma, mb = oracle.mesh_subdivide(coords), oracle.mesh_subdivide(coords, use_ref=True)
     assert np.array_equal(ma[0], mb[0]) and np.array_equal(ma[1], mb[1])
+
+
+def gs_cases():
+    rng = np.random.default_rng(3)
+    shell = workloads.ellipsoid_shell(64, 0)
+    multi = np.concatenate([workloads.ellipsoid_shell(32, 1, batch=0), workloads.ellipsoid_shell(32, 2, batch=1)])
+    neg = np.array([[0, x, y, z] for x in range(-9, 3) for y in range(-5, 7) for z in range(-12, 1)], np.int32)
+    return {"shell64": shell, "shell64_shuffled": shell[rng.permutation(len(shell))],
+            "multi_batch_shuffled": multi[rng.permutation(len(multi))], "negative": neg,
+            "one": np.array([[0, 5, 6, 7]], np.int32)}
+
+
+@pytest.mark.skipif(not oracle.ref_available(), reason="reference table builder not built")
+@pytest.mark.parametrize("name", list(gs_cases()))
+def test_oracle_gs_tables_match_reference(name):
+    """The restated GsTables::build (window buckets for both shifts, APE) equals
+    the reference's own, compiled from sparse_ops.cpp."""
+    coords = gs_cases()[name]
+    for si in (0, 1):
+        mine = oracle.gs_window_tables(coords, si)
+        ref = oracle.gs_window_tables(coords, si, use_ref=True)
+        for a, b in zip(mine, ref):
+            assert np.array_equal(a, b), (name, si)
+    assert np.array_equal(oracle.ape(coords), oracle.ape(coords, use_ref=True))
