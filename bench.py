@@ -778,6 +778,109 @@ def run_gs_tables(args, rank, world, local_rank):
 
 
 # ---------------------------------------------------------------------------
+# FlexiCubes extraction (the step after the path)
+# ---------------------------------------------------------------------------
+def run_flexicubes(args, rank, world, local_rank):
+    """extract_object_mesh (mesh_extractor.cpp:95-377) on the mesh decoder's
+    256^3 output for the config-1 shell after two subdivisions (970,176 cubes,
+    raw [N, 101] f32). A step = one s3dsp_flexicubes_extract (two host
+    synchronisations inside) + freeing its mesh. Unit: one input cube.
+    Replicas only at N > 1."""
+    import torch
+    import s3dsp
+    import oracle
+    import workloads
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    stream = torch.cuda.Stream(device)
+    torch.cuda.set_stream(stream)
+    ctx = s3dsp.Context(local_rank, stream=stream.cuda_stream)
+    t = np.load(os.path.join(ROOT, "tests", "golden", "flexicubes_tables.npz"))
+    tab = ctx.flexicubes_tables(t["dmc"], t["num_dual"], t["check"])
+    coords_h, raw_h = workloads.flexicubes_input(64, 0)
+    n = len(coords_h)
+    coords = torch.from_numpy(coords_h).to(device)
+    raw = torch.from_numpy(raw_h).to(device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    counts = {}
+
+    def step():
+        m = ctx.flexicubes(tab, raw, coords)
+        counts.update(vertices=m.n_vertices, faces=m.n_faces, surface=m.n_surface, edges=m.n_edges)
+        m.free()
+
+    for _ in range(args.warmup):
+        step()
+    stream.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush.fill_(i & 255)
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    stream.synchronize()
+    ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends)) / args.steps
+    # end to end: host raw + coords in (pinned), mesh out (vertices, attributes, faces)
+    raw_p, coords_p = torch.from_numpy(raw_h).pin_memory(), torch.from_numpy(coords_h).pin_memory()
+    e_s, e_e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(1, min(args.steps, 5))
+    d2h = 0
+    e_s.record(stream)
+    for _ in range(e2e_steps):
+        r_d = raw_p.to(device, non_blocking=True)
+        c_d = coords_p.to(device, non_blocking=True)
+        m = ctx.flexicubes(tab, r_d, c_d)
+        out = m.host()
+        d2h = out["vertices"].nbytes + out["attrs"].nbytes + out["faces"].nbytes
+        m.free()
+    e_e.record(stream)
+    stream.synchronize()
+    e2e_ms = e_s.elapsed_time(e_e) / e2e_steps
+    vals = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX)
+    ms, e2e_ms = vals.tolist()
+    if rank != 0:
+        return None
+    use_ref = oracle.ref_available()
+    reps = 3
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        if use_ref:
+            oracle.flexicubes(raw_h, coords_h, use_ref=True)
+        else:
+            oracle.flexicubes(raw_h, coords_h, dict(dmc=t["dmc"], num_dual=t["num_dual"], check=t["check"]))
+    cpu_s = (time.perf_counter() - t0) / reps
+    in_bytes = raw_h.nbytes + coords_h.nbytes
+    out_bytes = counts["vertices"] * 36 + counts["faces"] * 12 + counts["surface"] * 8 + counts["edges"] * 8
+    hbm, _, _, peak_src = load_peaks()
+    achieved = (in_bytes + out_bytes) / (ms / 1e3) / 1e9
+    return {
+        "metric": "cubes/s (FlexiCubes extraction at 256^3)", "value": n * world / (ms / 1e3), "unit": "cubes/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: config-1 shell subdivided twice (mesh decoder row order), SDF = signed distance "
+                "+ noise, other channels normal",
+        "config": {"workload": "FlexiCubes extraction: raw [970176, 101] f32 at 256^3 -> dual-vertex mesh",
+                   "cubes": n, **counts, "parallelism": f"replicas{world}",
+                   "l2": "flushed between steps (256 MiB write)",
+                   "note": "the call synchronises twice (surface/edge counts, dual-vertex count)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "traffic": None, "algorithmic_bytes": in_bytes + out_bytes, "peak_source": peak_src,
+                     "scope": "whole call (all kernels and both synchronisations)"},
+        "e2e": {"value": n / (e2e_ms / 1e3), "unit": "cubes/s", "h2d_bytes_per_step": in_bytes,
+                "d2h_bytes_per_step": d2h},
+        "cpu_baseline": {"value": n / cpu_s, "unit": "cubes/s", "cores": 1,
+                         "kind": "reference" if use_ref else "port",
+                         "sample": f"{reps} full extractions through "
+                                   + ("the reference's extract_object_mesh (oracle/_ref)" if use_ref
+                                      else "the oracle restatement")},
+    }
+
+
+# ---------------------------------------------------------------------------
 # CPU path (reference arm and cpu_baseline)
 # ---------------------------------------------------------------------------
 def cpu_step(cfg, threads):
@@ -835,11 +938,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="config2",
-                    choices=["config2", "config1", "config3", "volume", "objects", "coords", "gs_tables"],
+                    choices=["config2", "config1", "config3", "volume", "objects", "coords", "gs_tables",
+                             "flexicubes"],
                     help="config2: the headline (default); volume: config 5b, one volume split across ranks; "
                          "objects: config 5a, 64 objects through config 4 sharded by object; "
                          "config1 / config3: single layers; coords: the coordinate pipeline before the path; "
-                         "gs_tables: the GS decoder's Swin window tables and APE")
+                         "gs_tables: the GS decoder's Swin window tables and APE; flexicubes: the mesh extraction after "
+                         "the path")
     ap.add_argument("--precision", default="f32", choices=["f32", "bf16"], help="config1 / config3 only")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -855,7 +960,8 @@ def main():
             torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                                  device_id=torch.device("cuda", local_rank))
         runner = {"config2": run_ours, "volume": run_volume, "objects": run_objects, "config1": run_layers,
-                  "config3": run_layers, "coords": run_coords, "gs_tables": run_gs_tables}[args.workload]
+                  "config3": run_layers, "coords": run_coords, "gs_tables": run_gs_tables,
+                  "flexicubes": run_flexicubes}[args.workload]
         line = runner(args, rank, world, local_rank)
         if world > 1:
             import torch

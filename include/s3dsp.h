@@ -46,6 +46,8 @@ typedef struct s3dsp_context s3dsp_context;
 typedef struct s3dsp_hash s3dsp_hash;
 typedef struct s3dsp_kmap s3dsp_kmap;
 typedef struct s3dsp_slat_tables s3dsp_slat_tables;
+typedef struct s3dsp_fc_tables s3dsp_fc_tables;
+typedef struct s3dsp_mesh s3dsp_mesh;
 
 /* element types */
 #define S3DSP_F32 UINT32_C(0)
@@ -171,6 +173,48 @@ S3DSP_API s3d_status s3dsp_gs_window_tables(s3dsp_context *ctx, const int32_t *d
  * then channels/6 cosines of coordinate * 10000^(-i/(channels/6)). */
 S3DSP_API s3d_status s3dsp_ape(s3dsp_context *ctx, const int32_t *d_coords, int64_t n, int32_t channels,
                                float *d_out, char *error, uint64_t error_capacity);
+
+/* ---------------------------------------------------------------------------
+ * FlexiCubes extraction at resolution 256 (extract_object_mesh,
+ * src/objects_runtime/mesh_extractor.cpp:95-377: SparseFeatures2Mesh followed
+ * by inference-mode FlexiCubes), on the device.
+ * ------------------------------------------------------------------------- */
+/* Copies the dual-marching-cubes tables to the device: dmc [256][4][7] (edge
+ * lists of each case's dual vertices, -1 padded), num_dual [256], check
+ * [256][5] ({ambiguous, dx, dy, dz, replacement case}) -- the arrays of the
+ * reference's generated src/objects_runtime/flexicubes_tables.hpp. */
+S3DSP_API s3d_status s3dsp_flexicubes_tables_create(s3dsp_context *ctx, const int8_t *h_dmc,
+                                                    const int8_t *h_num_dual, const int16_t *h_check,
+                                                    s3dsp_fc_tables **out, char *error,
+                                                    uint64_t error_capacity);
+S3DSP_API void s3dsp_flexicubes_tables_free(s3dsp_context *ctx, s3dsp_fc_tables *tables);
+/* d_raw [n, 101] f32 (row-major, channels: 0-7 corner SDF, 8-31 corner
+ * deformation, 32-52 FlexiCubes weights, 53-100 corner colours), d_coords
+ * [n, 4] int32 (batch 0, x, y, z in [0, 256)). Errors as the reference: batch
+ * != 0, coordinate outside [0, 256), duplicate coordinate (the first bad row
+ * decides the message). Synchronises the context's stream twice. The mesh
+ * owns its device outputs: dual vertices [V, 3], their six attributes [V, 6],
+ * triangles [F, 3] and the surface cubes (dense ids, x-major), their resolved
+ * case ids and the surface edges [E, 2] (dense vertex ids). */
+S3DSP_API s3d_status s3dsp_flexicubes_extract(s3dsp_context *ctx, const s3dsp_fc_tables *tables,
+                                              const float *d_raw, const int32_t *d_coords, int64_t n,
+                                              s3dsp_mesh **out, char *error, uint64_t error_capacity);
+/* Counts of a mesh; any pointer may be NULL. */
+S3DSP_API s3d_status s3dsp_mesh_info(const s3dsp_mesh *mesh, int64_t *n_vertices, int64_t *n_faces,
+                                     int64_t *n_surface, int64_t *n_edges);
+/* Device pointers owned by the mesh (valid until s3dsp_mesh_free); any output
+ * pointer may be NULL. */
+S3DSP_API s3d_status s3dsp_mesh_device(const s3dsp_mesh *mesh, const float **vertices,
+                                       const float **attributes, const int32_t **faces,
+                                       const int32_t **surface, const int32_t **cases,
+                                       const int32_t **edges);
+/* Copies the mesh to host memory (ObjectMesh + the topology taps) and
+ * synchronises; any pointer may be NULL. */
+S3DSP_API s3d_status s3dsp_mesh_copy(s3dsp_context *ctx, const s3dsp_mesh *mesh, float *h_vertices,
+                                     float *h_attributes, int32_t *h_faces, int32_t *h_surface,
+                                     int32_t *h_cases, int32_t *h_edges, char *error,
+                                     uint64_t error_capacity);
+S3DSP_API void s3dsp_mesh_free(s3dsp_context *ctx, s3dsp_mesh *mesh);
 
 /* ---------------------------------------------------------------------------
  * K2 kernel maps. A kmap holds, per kernel offset o (o = kd*9 + kh*3 + kw with

@@ -80,6 +80,10 @@ def lib():
         L.oracle_gs_window_tables.argtypes = [_i32p, _c_i64, _c_i32, _c_i32, _i32p, _i32p, _i32p]
         L.oracle_ape.restype = None
         L.oracle_ape.argtypes = [_i32p, _c_i64, _c_i32, _f32p]
+        L.oracle_flexicubes.restype = _c_i32
+        L.oracle_flexicubes.argtypes = [_f32p, _i32p, _c_i64, _vp, _vp, _vp, _vp]
+        L.oracle_flexicubes_fetch.restype = None
+        L.oracle_flexicubes_fetch.argtypes = [_vp] * 6
         _lib = L
     return _lib
 
@@ -100,6 +104,12 @@ def ref_lib():
         L.ref_mesh_subdivide.argtypes = [_i32p, _c_i64, _i32p, _i32p]
         L.ref_gs_tables.restype = _c_i64
         L.ref_gs_tables.argtypes = [_i32p, _c_i64, _c_i32, _i32p, _i32p, _i32p, _vp]
+        L.ref_flexicubes_tables.restype = None
+        L.ref_flexicubes_tables.argtypes = [_vp, _vp, _vp]
+        L.ref_flexicubes.restype = _c_i32
+        L.ref_flexicubes.argtypes = [_f32p, _i32p, _c_i64, _vp, ctypes.c_char_p, _c_i64]
+        L.ref_flexicubes_fetch.restype = None
+        L.ref_flexicubes_fetch.argtypes = [_vp] * 6
         _ref = L
     return _ref
 
@@ -360,3 +370,52 @@ def slat_res_block(x, nbr_slat, norm1_w, norm1_b, w1, b1, mod_scale, mod_shift, 
     h = subm_conv_slat(h, nbr_slat, w2, b2, threads=threads)
     skip = x if skip_w is None else linear(x, skip_w, skip_b, threads=threads)
     return h + skip
+
+
+# ---------------------------------------------------------------------------
+# FlexiCubes extraction (src/objects_runtime/mesh_extractor.cpp:95-377)
+# ---------------------------------------------------------------------------
+FLEXICUBES_ERRORS = {-1: "invalid mesh decoder tensor", -2: "mesh extraction currently requires batch one",
+                     -3: "mesh cube coordinate outside resolution 256", -4: "duplicate mesh cube coordinate"}
+
+
+def ref_flexicubes_tables():
+    """The reference's DMC tables, read from its compiled extractor:
+    dict(dmc int8 [256, 4, 7], num_dual int8 [256], check int16 [256, 5])."""
+    dmc = np.zeros((256, 4, 7), np.int8)
+    nd = np.zeros(256, np.int8)
+    ck = np.zeros((256, 5), np.int16)
+    ref_lib().ref_flexicubes_tables(_ptr(dmc), _ptr(nd), _ptr(ck))
+    return dict(dmc=dmc, num_dual=nd, check=ck)
+
+
+def flexicubes(raw: np.ndarray, coords: np.ndarray, tables=None, use_ref: bool = False):
+    """extract_object_mesh with taps: dict(vertices [D, 3], attrs [D, 6],
+    faces [F, 3], surface [S] dense cube ids, cases [S], edges [E, 2]); raises
+    ValueError with the reference's message on its input errors. `tables`
+    (dmc, num_dual, check) is needed by the restatement only."""
+    raw = _c(raw, np.float32).reshape(-1, 101)
+    coords = _c(coords, np.int32).reshape(-1, 4)
+    n = len(coords)
+    counts = np.zeros(4, np.int64)
+    if use_ref:
+        err = ctypes.create_string_buffer(256)
+        rc = ref_lib().ref_flexicubes(raw.reshape(-1), coords.reshape(-1), n, _ptr(counts), err, 256)
+        if rc != 0:
+            raise ValueError(err.value.decode())
+        fetch = ref_lib().ref_flexicubes_fetch
+    else:
+        dmc = _c(tables["dmc"], np.int8)
+        nd = _c(tables["num_dual"], np.int8)
+        ck = _c(tables["check"], np.int16)
+        rc = lib().oracle_flexicubes(raw.reshape(-1), coords.reshape(-1), n, _ptr(dmc), _ptr(nd), _ptr(ck),
+                                     _ptr(counts))
+        if rc != 0:
+            raise ValueError(FLEXICUBES_ERRORS[rc])
+        fetch = lib().oracle_flexicubes_fetch
+    d, f, ns, ne = (int(v) for v in counts)
+    out = dict(vertices=np.zeros((d, 3), np.float32), attrs=np.zeros((d, 6), np.float32),
+               faces=np.zeros((f, 3), np.int32), surface=np.zeros(ns, np.int32), cases=np.zeros(ns, np.int32),
+               edges=np.zeros((ne, 2), np.int32))
+    fetch(*(_ptr(out[k]) for k in ("vertices", "attrs", "faces", "surface", "cases", "edges")))
+    return out

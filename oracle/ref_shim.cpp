@@ -9,7 +9,15 @@
 //   sam3d::SlatTables::build           src/objects_runtime/sparse_ops.cpp:49-173
 //   sam3d::MeshSubdivideTables::build  src/objects_runtime/sparse_ops.cpp:272-404
 //   sam3d::GsTables::build             src/objects_runtime/sparse_ops.cpp:182-270
+//   sam3d::extract_object_mesh         src/objects_runtime/mesh_extractor.cpp:95-377
+//     (compiled unchanged from mesh_extractor.cpp, with its generated
+//     flexicubes_tables.hpp, which ref_flexicubes_tables copies out)
+#include "flexicubes_tables.hpp"
+#include "mesh_extractor.hpp"
 #include "sparse_ops.hpp"
+
+#include <string>
+#include <vector>
 
 #include <cstdint>
 #include <cstring>
@@ -64,6 +72,52 @@ int64_t ref_gs_tables(const int32_t* coords, int64_t n, int32_t si, int32_t* bkt
     }
     if (ape) std::memcpy(ape, t.ape.data(), t.ape.size() * 4);
     return (int64_t)w.buckets.size();
+}
+
+// Copies the reference's DMC tables: dmc [256][4][7], num_dual [256],
+// check [256][5].
+void ref_flexicubes_tables(int8_t* dmc, int8_t* num_dual, int16_t* check) {
+    namespace t = sam3d::flexicubes_tables;
+    std::memcpy(dmc, t::dmc, sizeof t::dmc);
+    std::memcpy(num_dual, t::num_dual, sizeof t::num_dual);
+    std::memcpy(check, t::check, sizeof t::check);
+}
+
+static sam3d::ObjectMesh g_mesh;
+static sam3d::MeshExtractionTaps g_taps;
+
+// Runs extract_object_mesh with taps. Returns 0, or -1 when the reference
+// returns false (the message goes to `error`). counts: {dual vertices,
+// triangles, surface cubes, surface edges}.
+int32_t ref_flexicubes(const float* raw, const int32_t* coords, int64_t n, int64_t* counts, char* error,
+                       int64_t error_capacity) {
+    std::string msg;
+    if (!sam3d::extract_object_mesh(raw, coords, n, g_mesh, &g_taps, &msg)) {
+        if (error && error_capacity > 0) {
+            std::strncpy(error, msg.c_str(), (size_t)error_capacity - 1);
+            error[error_capacity - 1] = '\0';
+        }
+        return -1;
+    }
+    counts[0] = (int64_t)g_mesh.vertices.size() / 3;
+    counts[1] = (int64_t)g_mesh.faces.size() / 3;
+    counts[2] = (int64_t)g_taps.surface_cube_indices.size();
+    counts[3] = (int64_t)g_taps.surface_edges.size() / 2;
+    return 0;
+}
+
+// Copies the last ref_flexicubes result; any pointer may be NULL.
+void ref_flexicubes_fetch(float* vertices, float* attrs, int32_t* faces, int32_t* surface, int32_t* cases,
+                          int32_t* edges) {
+    const auto put = [](auto* dst, const auto& v) {
+        if (dst && !v.empty()) std::memcpy(dst, v.data(), v.size() * sizeof(v[0]));
+    };
+    put(vertices, g_mesh.vertices);
+    put(attrs, g_mesh.vertex_attributes);
+    put(faces, g_mesh.faces);
+    put(surface, g_taps.surface_cube_indices);
+    put(cases, g_taps.case_ids);
+    put(edges, g_taps.surface_edges);
 }
 
 }  // extern "C"

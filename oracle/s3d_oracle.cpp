@@ -725,4 +725,255 @@ void oracle_ape(const int32_t* coords, int64_t n, int32_t channels, float* out) 
         }
 }
 
+// ---------------------------------------------------------------------------
+// FlexiCubes extraction at 256^3: SparseFeatures2Mesh + inference FlexiCubes
+// (src/objects_runtime/mesh_extractor.cpp:95-377), restated over dense grids
+// (cube -> row, vertex -> SDF, vertex -> attribute slot) in the arithmetic
+// order of the reference: a vertex's sums run over its cubes in ascending row
+// order; the dual-vertex, quad and face orders are the reference's. The DMC
+// tables (dmc [256][4][7], num_dual [256], check [256][5]) are inputs.
+// Results stay in a process-wide buffer until the next call
+// (oracle_flexicubes_fetch copies them out).
+// ---------------------------------------------------------------------------
+namespace fcx {
+constexpr int R = 256, RV = 257, RAW = 101;
+// corner c = (c & 1, c >> 1 & 1, c >> 2 & 1); edge e joins kEdge[e][0] -> kEdge[e][1]
+constexpr int kCorner[8][3] = {{0, 0, 0}, {1, 0, 0}, {0, 1, 0}, {1, 1, 0}, {0, 0, 1}, {1, 0, 1}, {0, 1, 1}, {1, 1, 1}};
+constexpr int kEdge[12][2] = {{0, 1}, {1, 5}, {4, 5}, {0, 4}, {2, 3}, {3, 7}, {6, 7}, {2, 6}, {2, 0}, {3, 1}, {7, 5}, {6, 4}};
+inline int64_t vid(int x, int y, int z) { return ((int64_t)x * RV + y) * RV + z; }
+inline int64_t cid(int x, int y, int z) { return ((int64_t)x * R + y) * R + z; }
+struct Mesh {
+    std::vector<float> vertices, attrs;
+    std::vector<int32_t> faces, surface, cases, edges;
+};
+Mesh g_mesh;
+}  // namespace fcx
+
+// Returns 0, or -1 bad arguments, -2 batch != 0, -3 coordinate outside
+// [0, 256), -4 duplicate coordinate (the reference's three input errors).
+// counts: {dual vertices, triangles, surface cubes, surface edges}.
+__attribute__((optimize("fp-contract=off")))
+int32_t oracle_flexicubes(const float* raw, const int32_t* coords, int64_t n, const int8_t* dmc,
+                          const int8_t* num_dual, const int16_t* check, int64_t* counts) {
+    using namespace fcx;
+    g_mesh = Mesh{};
+    if (!raw || !coords || n <= 0 || n > INT32_MAX || !dmc || !num_dual || !check) return -1;
+    std::vector<int32_t> cube_row((size_t)R * R * R, -1);
+    for (int64_t r = 0; r < n; ++r) {
+        const int32_t* c = coords + 4 * r;
+        if (c[0] != 0) return -2;
+        if (c[1] < 0 || c[2] < 0 || c[3] < 0 || c[1] >= R || c[2] >= R || c[3] >= R) return -3;
+        int32_t& slot = cube_row[(size_t)cid(c[1], c[2], c[3])];
+        if (slot >= 0) return -4;
+        slot = (int32_t)r;
+    }
+    // per-vertex means, computed once by the lowest-row cube holding the vertex
+    const size_t nv = (size_t)RV * RV * RV;
+    std::vector<float> sdf(nv, 1.0f);
+    std::vector<int32_t> vslot(nv, -1);
+    std::vector<float> vattr((size_t)n * 8 * 9);
+    for (int64_t r = 0; r < n; ++r)
+        for (int corner = 0; corner < 8; ++corner) {
+            const int x = coords[4 * r + 1] + kCorner[corner][0], y = coords[4 * r + 2] + kCorner[corner][1],
+                      z = coords[4 * r + 3] + kCorner[corner][2];
+            int32_t rows[8], ks[8], m = 0;
+            for (int k = 0; k < 8; ++k) {
+                const int cx = x - kCorner[k][0], cy = y - kCorner[k][1], cz = z - kCorner[k][2];
+                if (cx < 0 || cy < 0 || cz < 0 || cx >= R || cy >= R || cz >= R) continue;
+                const int32_t row = cube_row[(size_t)cid(cx, cy, cz)];
+                if (row < 0) continue;
+                int j = m++;
+                for (; j > 0 && rows[j - 1] > row; --j) rows[j] = rows[j - 1], ks[j] = ks[j - 1];
+                rows[j] = row, ks[j] = k;
+            }
+            if (rows[0] != r) continue;  // owned by a lower row
+            float sum[10] = {};
+            for (int j = 0; j < m; ++j) {
+                const float* f = raw + (size_t)rows[j] * RAW;
+                const int k = ks[j];
+                sum[0] += f[k] - 1.0f / R;
+                for (int a = 0; a < 3; ++a) sum[1 + a] += f[8 + 3 * k + a];
+                for (int ch = 0; ch < 6; ++ch) sum[4 + ch] += f[53 + 6 * k + ch];
+            }
+            float mean[10];
+            for (int ch = 0; ch < 10; ++ch) mean[ch] = sum[ch] / (float)m;
+            const int64_t v = vid(x, y, z);
+            sdf[(size_t)v] = mean[0];
+            const int64_t slot = r * 8 + corner;
+            float* o = vattr.data() + slot * 9;
+            const int p[3] = {x, y, z};
+            for (int a = 0; a < 3; ++a)
+                o[a] = (float)p[a] / R - 0.5f + (1.0f / (R * 2.0f)) * std::tanh(mean[1 + a]);
+            for (int ch = 0; ch < 6; ++ch) o[3 + ch] = 1.0f / (1.0f + std::exp(-mean[4 + ch]));
+            vslot[(size_t)v] = (int32_t)slot;
+        }
+    const auto vertex_attr = [&](int64_t v, float out[9]) {
+        const int32_t s = vslot[(size_t)v];
+        if (s >= 0) {
+            std::memcpy(out, vattr.data() + (size_t)s * 9, 9 * sizeof(float));
+            return;
+        }
+        const int p[3] = {(int)(v / ((int64_t)RV * RV)), (int)(v / RV % RV), (int)(v % RV)};
+        for (int a = 0; a < 3; ++a) out[a] = (float)p[a] / R - 0.5f;
+        for (int ch = 0; ch < 6; ++ch) out[3 + ch] = 0.5f;
+    };
+    // surface cubes in dense (x, y, z) order
+    std::vector<uint8_t> occ((size_t)R * R * R);
+    std::vector<int32_t> sidx((size_t)R * R * R, -1);
+    std::vector<int32_t>& surf = g_mesh.surface;
+    for (int x = 0; x < R; ++x)
+        for (int y = 0; y < R; ++y)
+            for (int z = 0; z < R; ++z) {
+                unsigned bits = 0;
+                for (int k = 0; k < 8; ++k)
+                    if (sdf[(size_t)vid(x + kCorner[k][0], y + kCorner[k][1], z + kCorner[k][2])] < 0.0f) bits |= 1u << k;
+                const int64_t c = cid(x, y, z);
+                occ[(size_t)c] = (uint8_t)bits;
+                if (bits != 0 && bits != 255) {
+                    sidx[(size_t)c] = (int32_t)surf.size();
+                    surf.push_back((int32_t)c);
+                }
+            }
+    // ambiguous configurations resolved against the face neighbour's raw case
+    const int64_t ns = (int64_t)surf.size();
+    std::vector<int32_t>& cases = g_mesh.cases;
+    cases.resize((size_t)ns);
+    for (int64_t i = 0; i < ns; ++i) {
+        const int32_t c = surf[(size_t)i];
+        int32_t cs = occ[(size_t)c];
+        const int16_t* ck = check + 5 * cs;
+        if (ck[0] == 1) {
+            const int nx = c / (R * R) + ck[1], ny = c / R % R + ck[2], nz = c % R + ck[3];
+            if (nx >= 0 && ny >= 0 && nz >= 0 && nx < R && ny < R && nz < R) {
+                const int nb = occ[(size_t)cid(nx, ny, nz)];
+                if (nb != 0 && nb != 255 && check[5 * nb] == 1) cs = ck[4];
+            }
+        }
+        cases[(size_t)i] = cs;
+    }
+    // sign-changing grid edges in (first vertex, second vertex) order: for a
+    // first vertex u the -y edge, then +z, then +x
+    std::vector<int32_t>& edges = g_mesh.edges;
+    for (int x = 0; x < RV; ++x)
+        for (int y = 0; y < RV; ++y)
+            for (int z = 0; z < RV; ++z) {
+                const int64_t u = vid(x, y, z);
+                const bool s = sdf[(size_t)u] < 0.0f;
+                if (y >= 1 && s != (sdf[(size_t)vid(x, y - 1, z)] < 0.0f)) edges.insert(edges.end(), {(int32_t)u, (int32_t)vid(x, y - 1, z)});
+                if (z < R && s != (sdf[(size_t)(u + 1)] < 0.0f)) edges.insert(edges.end(), {(int32_t)u, (int32_t)(u + 1)});
+                if (x < R && s != (sdf[(size_t)vid(x + 1, y, z)] < 0.0f)) edges.insert(edges.end(), {(int32_t)u, (int32_t)vid(x + 1, y, z)});
+            }
+    // dual vertices: grouped by dual count, then surface order, then local index
+    int64_t per_count[5] = {0, 0, 0, 0, 0};
+    for (int64_t i = 0; i < ns; ++i) ++per_count[num_dual[cases[(size_t)i]]];
+    int64_t base[5] = {0, 0, 0, 0, 0};
+    for (int k = 1; k < 5; ++k) base[k] = base[k - 1] + per_count[k - 1] * (k - 1);
+    const int64_t nd_total = base[4] + per_count[4] * 4;
+    g_mesh.vertices.assign((size_t)nd_total * 3, 0.0f);
+    g_mesh.attrs.assign((size_t)nd_total * 6, 0.0f);
+    std::vector<float> dual_gamma((size_t)nd_total);
+    std::vector<int32_t> dmap((size_t)ns * 12, 0);
+    int64_t rank[5] = {0, 0, 0, 0, 0};
+    for (int64_t i = 0; i < ns; ++i) {
+        const int32_t c = surf[(size_t)i];
+        const int cs = cases[(size_t)i];
+        const int nd = num_dual[cs];
+        const int cx = c / (R * R), cy = c / R % R, cz = c % R;
+        int64_t vtx[8];
+        for (int k = 0; k < 8; ++k) vtx[k] = vid(cx + kCorner[k][0], cy + kCorner[k][1], cz + kCorner[k][2]);
+        const int32_t row = cube_row[(size_t)c];
+        const auto w = [&](int ch) { return row < 0 ? 0.0f : raw[(size_t)row * RAW + 32 + ch]; };
+        float beta[12], alpha[8];
+        for (int e = 0; e < 12; ++e) beta[e] = std::tanh(w(e)) * 0.99f + 1.0f;
+        for (int k = 0; k < 8; ++k) alpha[k] = std::tanh(w(12 + k)) * 0.99f + 1.0f;
+        const float gamma = 1.0f / (1.0f + std::exp(-w(20))) * 0.99f + 0.005f;
+        const int64_t first_id = base[nd] + rank[nd]++ * nd;
+        for (int j = 0; j < nd; ++j) {
+            const int64_t id = first_id + j;
+            float pos[3] = {0, 0, 0}, col[6] = {0, 0, 0, 0, 0, 0}, beta_sum = 0.0f;
+            for (int t = 0; t < 7; ++t) {
+                const int e = dmc[(cs * 4 + j) * 7 + t];
+                if (e < 0) continue;
+                const int ka = kEdge[e][0], kb = kEdge[e][1];
+                const float wa = sdf[(size_t)vtx[ka]] * alpha[ka];
+                const float wb = sdf[(size_t)vtx[kb]] * alpha[kb];
+                const float den = wb - wa;
+                float va[9], vb[9];
+                vertex_attr(vtx[ka], va);
+                vertex_attr(vtx[kb], vb);
+                beta_sum += beta[e];
+                for (int a = 0; a < 3; ++a) pos[a] += ((va[a] * wb - vb[a] * wa) / den) * beta[e];
+                for (int ch = 0; ch < 6; ++ch) col[ch] += ((va[3 + ch] * wb - vb[3 + ch] * wa) / den) * beta[e];
+                dmap[(size_t)i * 12 + e] = (int32_t)id;
+            }
+            for (int a = 0; a < 3; ++a) g_mesh.vertices[(size_t)id * 3 + a] = pos[a] / beta_sum;
+            for (int ch = 0; ch < 6; ++ch) g_mesh.attrs[(size_t)id * 6 + ch] = col[ch] / beta_sum;
+            dual_gamma[(size_t)id] = gamma;
+        }
+    }
+    // one quad per surface edge with four incident cubes; flipped quads first
+    std::vector<int32_t> flipped, straight;
+    const int64_t ne = (int64_t)edges.size() / 2;
+    for (int64_t s = 0; s < ne; ++s) {
+        const int64_t u = edges[(size_t)s * 2], v = edges[(size_t)s * 2 + 1];
+        const int ux = (int)(u / ((int64_t)RV * RV)), uy = (int)(u / RV % RV), uz = (int)(u % RV);
+        int64_t cubes[4];
+        int m = 0;
+        for (int d0 = 0; d0 < 2; ++d0)
+            for (int d1 = 0; d1 < 2; ++d1) {
+                int x = ux, y = uy, z = uz;
+                if (v == u + (int64_t)RV * RV) y -= d0, z -= d1;       // +x edge
+                else if (v == u + 1) x -= d0, y -= d1;                 // +z edge
+                else x -= d0, y -= 1, z -= d1;                         // -y edge
+                if (x < 0 || y < 0 || z < 0 || x >= R || y >= R || z >= R) continue;
+                cubes[m++] = cid(x, y, z);
+            }
+        if (m != 4) continue;
+        std::sort(cubes, cubes + 4);
+        int32_t q[4];
+        for (int j = 0; j < 4; ++j) {
+            const int64_t c = cubes[j];
+            const int cx = (int)(c / (R * R)), cy = (int)(c / R % R), cz = (int)(c % R);
+            int e = 0;
+            for (; e < 12; ++e) {
+                const int ka = kEdge[e][0], kb = kEdge[e][1];
+                if (vid(cx + kCorner[ka][0], cy + kCorner[ka][1], cz + kCorner[ka][2]) == u &&
+                    vid(cx + kCorner[kb][0], cy + kCorner[kb][1], cz + kCorner[kb][2]) == v)
+                    break;
+            }
+            q[j] = dmap[(size_t)sidx[(size_t)c] * 12 + e];
+        }
+        const bool flip = sdf[(size_t)u] > 0.0f;
+        const int32_t o[4] = {flip ? q[0] : q[2], flip ? q[1] : q[3], flip ? q[3] : q[1], flip ? q[2] : q[0]};
+        const bool split1 = dual_gamma[(size_t)o[0]] * dual_gamma[(size_t)o[2]] > dual_gamma[(size_t)o[1]] * dual_gamma[(size_t)o[3]];
+        std::vector<int32_t>& dst = flip ? flipped : straight;
+        if (split1) dst.insert(dst.end(), {o[0], o[1], o[2], o[0], o[2], o[3]});
+        else dst.insert(dst.end(), {o[0], o[1], o[3], o[3], o[1], o[2]});
+    }
+    g_mesh.faces = std::move(flipped);
+    g_mesh.faces.insert(g_mesh.faces.end(), straight.begin(), straight.end());
+    if (counts) {
+        counts[0] = nd_total;
+        counts[1] = (int64_t)g_mesh.faces.size() / 3;
+        counts[2] = ns;
+        counts[3] = ne;
+    }
+    return 0;
+}
+
+// Copies the last oracle_flexicubes result; any pointer may be NULL.
+void oracle_flexicubes_fetch(float* vertices, float* attrs, int32_t* faces, int32_t* surface, int32_t* cases,
+                             int32_t* edges) {
+    using fcx::g_mesh;
+    const auto put = [](auto* dst, const auto& v) {
+        if (dst && !v.empty()) std::memcpy(dst, v.data(), v.size() * sizeof(v[0]));
+    };
+    put(vertices, g_mesh.vertices);
+    put(attrs, g_mesh.attrs);
+    put(faces, g_mesh.faces);
+    put(surface, g_mesh.surface);
+    put(cases, g_mesh.cases);
+    put(edges, g_mesh.edges);
+}
+
 }  // extern "C"

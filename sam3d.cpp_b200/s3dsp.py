@@ -32,7 +32,9 @@ CONTEXT_OWN_STREAM = 2
 EXPORTED = [
     "s3dsp_abi_version", "s3dsp_context_create", "s3dsp_context_free", "s3dsp_context_stream",
     "s3dsp_context_check", "s3dsp_hash_build", "s3dsp_hash_free", "s3dsp_hash_size",
-    "s3dsp_hash_lookup", "s3dsp_gs_window_tables", "s3dsp_ape", "s3dsp_occupancy_coords", "s3dsp_prune_surface", "s3dsp_downsample_coords",
+    "s3dsp_hash_lookup", "s3dsp_gs_window_tables", "s3dsp_ape", "s3dsp_flexicubes_tables_create",
+    "s3dsp_flexicubes_tables_free", "s3dsp_flexicubes_extract", "s3dsp_mesh_info", "s3dsp_mesh_device", "s3dsp_mesh_copy",
+    "s3dsp_mesh_free", "s3dsp_occupancy_coords", "s3dsp_prune_surface", "s3dsp_downsample_coords",
     "s3dsp_kmap_build_subm3", "s3dsp_kmap_build_subm3_rows", "s3dsp_kmap_build_subm3_range", "s3dsp_subdivide", "s3dsp_kmap_free",
     "s3dsp_kmap_rows", "s3dsp_kmap_export_dense", "s3dsp_kmap_pairs", "s3dsp_kmap_pairs_noalloc",
     "s3dsp_weights_packed_bytes", "s3dsp_weights_pack", "s3dsp_gn_partials_count", "s3dsp_conv", "s3dsp_conv_kernel",
@@ -82,6 +84,13 @@ def load(path: str = LIB_PATH):
         "s3dsp_gs_window_tables": (_u32, [_vp, _vp, _i64, _i32, _i32, _vp, _vp, _vp, _i64, ctypes.POINTER(_i64), _cp,
                                           _u64]),
         "s3dsp_ape": (_u32, [_vp, _vp, _i64, _i32, _vp, _cp, _u64]),
+        "s3dsp_flexicubes_tables_create": (_u32, [_vp, _vp, _vp, _vp, ctypes.POINTER(_vp), _cp, _u64]),
+        "s3dsp_flexicubes_tables_free": (None, [_vp, _vp]),
+        "s3dsp_flexicubes_extract": (_u32, [_vp, _vp, _vp, _vp, _i64, ctypes.POINTER(_vp), _cp, _u64]),
+        "s3dsp_mesh_info": (_u32, [_vp] + [ctypes.POINTER(_i64)] * 4),
+        "s3dsp_mesh_device": (_u32, [_vp] + [ctypes.POINTER(_vp)] * 6),
+        "s3dsp_mesh_copy": (_u32, [_vp, _vp] + [_vp] * 6 + [_cp, _u64]),
+        "s3dsp_mesh_free": (None, [_vp, _vp]),
         "s3dsp_occupancy_coords": (_u32, [_vp, _vp, _i32, _i32, _i32, _i32, _vp, _i64, ctypes.POINTER(_i64), _cp,
                                           _u64]),
         "s3dsp_prune_surface": (_u32, [_vp, _vp, _i64, _i32, _vp, _i64, ctypes.POINTER(_i64), _cp, _u64]),
@@ -202,6 +211,57 @@ class SlatTables:
             pass
 
 
+class FlexiCubesTables:
+    def __init__(self, ctx: "Context", handle: int):
+        self.ctx, self.handle = ctx, handle
+
+    def free(self):
+        if self.handle:
+            load().s3dsp_flexicubes_tables_free(self.ctx.handle, self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class Mesh:
+    """A device mesh from s3dsp_flexicubes_extract (counts + host copies)."""
+
+    def __init__(self, ctx: "Context", handle: int):
+        self.ctx, self.handle = ctx, handle
+        c = [_i64() for _ in range(4)]
+        st = load().s3dsp_mesh_info(handle, *(ctypes.byref(v) for v in c))
+        if st != S3D_OK:
+            raise S3dError(st, "s3dsp_mesh_info")
+        self.n_vertices, self.n_faces, self.n_surface, self.n_edges = (v.value for v in c)
+
+    def host(self) -> dict:
+        """dict(vertices [V, 3], attrs [V, 6], faces [F, 3], surface [S],
+        cases [S], edges [E, 2]) as numpy arrays."""
+        import numpy as np
+        out = dict(vertices=np.zeros((self.n_vertices, 3), np.float32),
+                   attrs=np.zeros((self.n_vertices, 6), np.float32),
+                   faces=np.zeros((self.n_faces, 3), np.int32), surface=np.zeros(self.n_surface, np.int32),
+                   cases=np.zeros(self.n_surface, np.int32), edges=np.zeros((self.n_edges, 2), np.int32))
+        _call(load().s3dsp_mesh_copy, self.ctx.handle, self.handle,
+              *(out[k].ctypes.data for k in ("vertices", "attrs", "faces", "surface", "cases", "edges")))
+        return out
+
+    def free(self):
+        if self.handle:
+            load().s3dsp_mesh_free(self.ctx.handle, self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
 class Context:
     """One device + one CUDA stream (default: torch's current stream, so the
     library's kernels are ordered with torch's copies and events)."""
@@ -255,6 +315,26 @@ class Context:
 
     def ape(self, coords, out):
         _call(load().s3dsp_ape, self.handle, ptr(coords), coords.shape[0], out.shape[1], ptr(out))
+
+    # ---- FlexiCubes extraction ---------------------------------------------
+    def flexicubes_tables(self, dmc, num_dual, check) -> FlexiCubesTables:
+        """DMC tables (numpy int8 [256, 4, 7], int8 [256], int16 [256, 5])."""
+        import numpy as np
+        dmc = np.ascontiguousarray(dmc, np.int8)
+        num_dual = np.ascontiguousarray(num_dual, np.int8)
+        check = np.ascontiguousarray(check, np.int16)
+        assert dmc.size == 256 * 28 and num_dual.size == 256 and check.size == 256 * 5
+        h = _vp()
+        _call(load().s3dsp_flexicubes_tables_create, self.handle, dmc.ctypes.data, num_dual.ctypes.data,
+              check.ctypes.data, ctypes.byref(h))
+        return FlexiCubesTables(self, h.value)
+
+    def flexicubes(self, tables: FlexiCubesTables, raw, coords) -> Mesh:
+        """extract_object_mesh over device raw [n, 101] f32 and coords [n, 4] int32."""
+        h = _vp()
+        _call(load().s3dsp_flexicubes_extract, self.handle, tables.handle, ptr(raw), ptr(coords), coords.shape[0],
+              ctypes.byref(h))
+        return Mesh(self, h.value)
 
     # ---- coordinate pipeline -----------------------------------------------
     def occupancy_coords(self, occ, out, batch: int = 0) -> int:

@@ -111,3 +111,61 @@ def config3(seed: int = 1, cin: int = 128, cout: int = 64):
                 b_up=normal((cout,), seed + 3, std=0.1),
                 w=conv_weight_slat(cout, cout, seed + 4), b=normal((cout,), seed + 5, std=0.1),
                 cin=cin, cout=cout)
+
+
+def ellipsoid_params(res: int = 64, seed: int = 0, axes_range=(16.0, 30.0), centre_jitter: float = 4.0):
+    """The semi-axes and centre `ellipsoid_shell(res, seed)` draws."""
+    rng = np.random.default_rng(seed)
+    scale = res / 64.0
+    a = rng.uniform(axes_range[0], axes_range[1], size=3) * scale
+    c = res / 2.0 + rng.uniform(-centre_jitter, centre_jitter, size=3) * scale
+    return a, c
+
+
+MESH_RES = 256
+MESH_RAW = 101
+
+
+def subdivide_order(parents: np.ndarray, levels: int = 2) -> np.ndarray:
+    """Children of `parents` after `levels` stride-2 subdivisions, in the
+    mesh decoder's row order (parent-major, child j = xb*4 + yb*2 + zb)."""
+    c = np.asarray(parents, np.int32)
+    off = np.array([[0, (j >> 2) & 1, (j >> 1) & 1, j & 1] for j in range(8)], np.int32)
+    scale = np.array([1, 2, 2, 2], np.int32)
+    for _ in range(levels):
+        c = (c[:, None, :] * scale + off[None]).reshape(-1, 4)
+    return np.ascontiguousarray(c)
+
+
+def flexicubes_input(parent_res: int = 64, seed: int = 0, sdf_noise: float = 0.3, thickness: float = 1.5):
+    """Stand-in for the mesh decoder's final output at 256^3: the cubes of the
+    config-1-style shell at `parent_res` after two subdivisions (x4 per axis,
+    mesh decoder row order) and raw [N, 101] features in the extractor's
+    channel layout: 0-7 corner SDFs, 8-31 corner deformations, 32-52
+    FlexiCubes weights, 53-100 corner colours.
+
+    The corner SDFs are the signed radial distance of the corner to the
+    ellipsoid surface in grid units of 1/256, plus the extractor's 1/256
+    offset, plus N(0, sdf_noise/256) noise so that ambiguous cube
+    configurations occur; the other channels are N(0, 0.5^2) / N(0, 1)."""
+    assert parent_res * 4 <= MESH_RES
+    parents = ellipsoid_shell(parent_res, seed, thickness=thickness)
+    cubes = subdivide_order(parents, 2)
+    n = len(cubes)
+    a, c = ellipsoid_params(parent_res, seed)
+    a, c = a * 4.0, c * 4.0
+    corners = np.array([[0, 0, 0], [1, 0, 0], [0, 1, 0], [1, 1, 0], [0, 0, 1], [1, 0, 1], [0, 1, 1], [1, 1, 1]],
+                       np.float64)
+    p = cubes[:, None, 1:].astype(np.float64) + corners[None]  # [n, 8, 3]
+    d = p - c
+    r = np.sqrt((d * d).sum(-1))
+    q = np.sqrt(((d / a) ** 2).sum(-1))
+    with np.errstate(divide="ignore", invalid="ignore"):
+        dist = np.where(q > 0, r * (1.0 - 1.0 / q), -1.0)
+    rng = np.random.default_rng(seed + 17)
+    raw = np.empty((n, MESH_RAW), np.float32)
+    raw[:, 0:8] = (dist + 1.0 + rng.normal(0.0, sdf_noise, size=(n, 8))) / MESH_RES
+    raw[:, 8:32] = rng.normal(0.0, 0.5, size=(n, 24))
+    raw[:, 32:53] = rng.normal(0.0, 1.0, size=(n, 21))
+    raw[:, 53:101] = rng.normal(0.0, 1.0, size=(n, 48))
+    return cubes, raw

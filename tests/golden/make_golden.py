@@ -20,7 +20,20 @@ oracle/_ref/libsparse_ops_ref.so), never from our restatement. Outputs:
                      tests/objects_runtime/fixtures/ss_occ_f32.samt (a real 64^3
                      SS-decoder output), packed with np.packbits;
 * digests.json     - sha256 of the reference tables for the larger sets
-                     (config-1 shell, its subdivide, the pruned ss_occ set).
+                     (config-1 shell, its subdivide, the pruned ss_occ set)
+                     and of the reference's FlexiCubes topology for the
+                     full-size extraction inputs;
+* flexicubes_tables.npz - the DMC tables (dmc, num_dual, check) read out of
+                     the reference's compiled extractor
+                     (src/objects_runtime/flexicubes_tables.hpp, used by
+                     mesh_extractor.cpp); the device extractor takes them as
+                     an input;
+* flexicubes_small.npz - extract_object_mesh output (with taps) for
+                     workloads.flexicubes_input(8, 0), the input regenerated
+                     from its seed.
+
+`python tests/golden/make_golden.py --flexicubes` regenerates only the
+FlexiCubes fixtures (and their digests entries).
 """
 from __future__ import annotations
 
@@ -99,10 +112,37 @@ def prune_surface(coords):
     return coords[keep]
 
 
+FLEXICUBES_DIGEST_CASES = {"flexicubes_full64": dict(parent_res=64, seed=0),
+                           "flexicubes_noisy16": dict(parent_res=16, seed=1, sdf_noise=3.0)}
+
+
+def make_flexicubes():
+    t = oracle.ref_flexicubes_tables()
+    np.savez_compressed(os.path.join(HERE, "flexicubes_tables.npz"), **t)
+    c, r = workloads.flexicubes_input(8, 0)
+    m = oracle.flexicubes(r, c, use_ref=True)
+    np.savez_compressed(os.path.join(HERE, "flexicubes_small.npz"), parent_res=8, seed=0, n=len(c), **m)
+    out = {}
+    for name, kw in FLEXICUBES_DIGEST_CASES.items():
+        c, r = workloads.flexicubes_input(**kw)
+        m = oracle.flexicubes(r, c, use_ref=True)
+        out[name] = dict(kw, n=len(c), **{k: sha(m[k]) for k in ("faces", "surface", "cases", "edges")},
+                         **{"n_" + k: len(m[k]) for k in ("vertices", "faces", "surface", "edges")})
+    return out
+
+
 def main():
-    ref_root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("S3D_REFERENCE_ROOT", "")
     if not oracle.ref_available():
         raise SystemExit("build oracle/_ref first: make -C oracle ref")
+    if "--flexicubes" in sys.argv[1:]:
+        path = os.path.join(HERE, "digests.json")
+        with open(path) as f:
+            digests = json.load(f)
+        digests.update(make_flexicubes())
+        with open(path, "w") as f:
+            json.dump(digests, f, indent=1, sort_keys=True)
+        return
+    ref_root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("S3D_REFERENCE_ROOT", "")
 
     save_full("kat_block3.npz", block3())
     save_full("shell16.npz", workloads.ellipsoid_shell(16, seed=3))
@@ -155,6 +195,7 @@ def main():
                                         coarse_children=sha(t["coarse_children"]),
                                         coarse_inv_count=sha_f(t["coarse_inv_count"]),
                                         child_coords=sha(m[0]), neighbors=sha(m[1]))
+    digests.update(make_flexicubes())
     with open(os.path.join(HERE, "digests.json"), "w") as f:
         json.dump(digests, f, indent=1, sort_keys=True)
     print(json.dumps({k: v.get("n") for k, v in digests.items()}))
