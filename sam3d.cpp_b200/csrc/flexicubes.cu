@@ -8,10 +8,12 @@
 //
 //  1. cube_row[cube] = lowest input row (atomicMin); per-row checks of batch,
 //     range and duplicates record the first offending row of each kind.
-//  2. Every vertex is aggregated once, by the lowest-row cube holding it: it
-//     gathers the (<= 8) holding cubes, sorts them by row and sums in that
-//     order -- the reference's accumulation order, so the means are
-//     bit-identical to the host's. Slot = row * 8 + corner.
+//  2. A warp per (x, y) row of 257 vertices writes every vertex's SDF (1 where
+//     no cube holds it) and attribute slot: a vertex's (<= 8) holding cubes
+//     are read coalesced along z, sorted by row in registers (a 19-comparator
+//     network on row << 3 | corner) and summed in that order -- the
+//     reference's accumulation order, so the means are bit-identical to the
+//     host's. Slot = lowest row * 8 + its corner.
 //  3. A warp per (x, y) row of 256 cubes computes the occupancy bytes and
 //     counts the surface cubes (ballot); a warp per (x, y) row of 257
 //     vertices counts the sign-changing edges starting there (the -y, +z, +x
@@ -22,9 +24,10 @@
 //  4. Per surface cube: the ambiguous-case check against the neighbour's raw
 //     case, then the dual vertices, numbered by (dual count, surface index,
 //     local index) through an int4 scan of one-hot dual counts.
-//  5. Per surface edge with four cubes: the quad over the four cubes' dual
-//     vertices in dense cube order, flipped quads first, split by the gamma
-//     products, written straight to its face slot.
+//  5. The edge pass records each quad (a surface edge with four cubes in the
+//     grid) at its slot, flipped quads first; a thread per quad then joins
+//     the four cubes' dual vertices in dense cube order and writes the two
+//     triangles, split by the gamma products.
 //
 // Arithmetic follows the reference's order with no contraction (explicit
 // _rn intrinsics); tanhf / expf are CUDA's, so positions and attributes match
@@ -83,13 +86,6 @@ struct Int4Add {
     }
 };
 
-__global__ void fc_fill_kernel(float* __restrict__ sdf, int32_t* __restrict__ vslot, int64_t n) {
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        sdf[i] = 1.0f;
-        vslot[i] = -1;
-    }
-}
-
 __global__ void fc_scatter_kernel(const int4* __restrict__ coords, int64_t n, int32_t* __restrict__ cube_row,
                                   int32_t* __restrict__ err_row) {
     const int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
@@ -116,65 +112,88 @@ __global__ void fc_dup_kernel(const int4* __restrict__ coords, int64_t n, const 
     if (cube_row[cid(c.y, c.z, c.w)] != (int32_t)r) atomicMin(err_row + kErrDup, (int32_t)r);
 }
 
-// One thread per (row, corner): the owner (lowest row holding the vertex)
-// sums the vertex's contributions in ascending row order.
-__global__ void fc_aggregate_kernel(const float* __restrict__ raw, const int4* __restrict__ coords, int64_t n,
-                                    const int32_t* __restrict__ cube_row, float* __restrict__ sdf,
-                                    int32_t* __restrict__ vslot, float* __restrict__ vattr) {
-    const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    if (t >= n * 8) return;
-    const int32_t r = (int32_t)(t >> 3);
-    const int corner = (int)(t & 7);
-    const int4 c = coords[r];
-    if (c.x != 0 || !in_grid(c.y, c.z, c.w)) return;
-    const int x = c.y + (corner & 1), y = c.z + (corner >> 1 & 1), z = c.w + (corner >> 2 & 1);
-    int32_t rows[8];
-    int ks[8];
-    int m = 0;
+__device__ __forceinline__ void cswap(int32_t& a, int32_t& b) {
+    const int32_t lo = min(a, b), hi = max(a, b);
+    a = lo;
+    b = hi;
+}
+
+constexpr int kVChunks = (RV + 31) / 32;  // 32-vertex chunks per (x, y) row
+
+// Warp per 32 vertices of an (x, y) row (lane = z offset). Vertex (x, y, z)
+// is corner k of cube (x - (k & 1), y - (k >> 1 & 1), z - (k >> 2 & 1)).
+__global__ void fc_vertex_kernel(const float* __restrict__ raw, const int32_t* __restrict__ cube_row,
+                                 float* __restrict__ sdf, int32_t* __restrict__ vslot, float* __restrict__ vattr) {
+    const int w = (int)((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5);
+    const int lane = threadIdx.x & 31;
+    if (w >= RV * RV * kVChunks) return;
+    const int row = w / kVChunks;
+    const int x = row / RV, y = row % RV;
+    const int z = (w % kVChunks) * 32 + lane;
+    if (z < RV) {
+        int32_t rk[8];  // row << 3 | corner, INT_MAX when the cube is absent
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        const int cx = x - (k & 1), cy = y - (k >> 1 & 1), cz = z - (k >> 2 & 1);
-        if (!in_grid(cx, cy, cz)) continue;
-        const int32_t row = cube_row[cid(cx, cy, cz)];
-        if (row == kNoRow) continue;
-        int j = m++;
-        for (; j > 0 && rows[j - 1] > row; --j) {
-            rows[j] = rows[j - 1];
-            ks[j] = ks[j - 1];
+        for (int k = 0; k < 8; ++k) {
+            const int cx = x - (k & 1), cy = y - (k >> 1 & 1), cz = z - (k >> 2 & 1);
+            const int32_t r = in_grid(cx, cy, cz) ? cube_row[cid(cx, cy, cz)] : kNoRow;
+            rk[k] = r == kNoRow ? INT_MAX : (r << 3 | k);
         }
-        rows[j] = row;
-        ks[j] = k;
+        const int32_t v = vid(x, y, z);
+        if ((rk[0] & rk[1] & rk[2] & rk[3] & rk[4] & rk[5] & rk[6] & rk[7]) == INT_MAX) {
+            sdf[v] = 1.0f;
+            vslot[v] = -1;
+            return;
+        }
+        cswap(rk[0], rk[2]), cswap(rk[1], rk[3]), cswap(rk[4], rk[6]), cswap(rk[5], rk[7]);
+        cswap(rk[0], rk[4]), cswap(rk[1], rk[5]), cswap(rk[2], rk[6]), cswap(rk[3], rk[7]);
+        cswap(rk[0], rk[1]), cswap(rk[2], rk[3]), cswap(rk[4], rk[5]), cswap(rk[6], rk[7]);
+        cswap(rk[2], rk[4]), cswap(rk[3], rk[5]);
+        cswap(rk[1], rk[4]), cswap(rk[3], rk[6]);
+        cswap(rk[1], rk[2]), cswap(rk[3], rk[4]), cswap(rk[5], rk[6]);
+        float sum[10];
+#pragma unroll
+        for (int ch = 0; ch < 10; ++ch) sum[ch] = 0.0f;
+        // Absent cubes (sorted last) read the first cube's row and add +0,
+        // which leaves a sum that starts at +0 unchanged, so every load can be
+        // in flight at once.
+        int m = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const bool ok = rk[i] != INT_MAX;
+            m += ok;
+            const int32_t e = ok ? rk[i] : rk[0];
+            const float* f = raw + (int64_t)(e >> 3) * RAW;
+            const int k = e & 7;
+            const float t0 = __fsub_rn(__ldg(f + k), 1.0f / R);
+            sum[0] = __fadd_rn(sum[0], ok ? t0 : 0.0f);
+#pragma unroll
+            for (int a = 0; a < 3; ++a) {
+                const float t = __ldg(f + 8 + 3 * k + a);
+                sum[1 + a] = __fadd_rn(sum[1 + a], ok ? t : 0.0f);
+            }
+#pragma unroll
+            for (int ch = 0; ch < 6; ++ch) {
+                const float t = __ldg(f + 53 + 6 * k + ch);
+                sum[4 + ch] = __fadd_rn(sum[4 + ch], ok ? t : 0.0f);
+            }
+        }
+        const float fm = (float)m;
+        const int32_t slot = rk[0];  // lowest row * 8 + its corner
+        float* o = vattr + (int64_t)slot * 9;
+        const int p[3] = {x, y, z};
+#pragma unroll
+        for (int a = 0; a < 3; ++a) {
+            const float mean = __fdiv_rn(sum[1 + a], fm);
+            o[a] = __fadd_rn(__fsub_rn(__fdiv_rn((float)p[a], (float)R), 0.5f), __fmul_rn(1.0f / (R * 2.0f), tanhf(mean)));
+        }
+#pragma unroll
+        for (int ch = 0; ch < 6; ++ch) {
+            const float mean = __fdiv_rn(sum[4 + ch], fm);
+            o[3 + ch] = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-mean)));
+        }
+        sdf[v] = __fdiv_rn(sum[0], fm);
+        vslot[v] = slot;
     }
-    if (m == 0 || rows[0] != r) return;
-    float sum[10];
-#pragma unroll
-    for (int ch = 0; ch < 10; ++ch) sum[ch] = 0.0f;
-    for (int j = 0; j < m; ++j) {
-        const float* f = raw + (int64_t)rows[j] * RAW;
-        const int k = ks[j];
-        sum[0] = __fadd_rn(sum[0], __fsub_rn(__ldg(f + k), 1.0f / R));
-#pragma unroll
-        for (int a = 0; a < 3; ++a) sum[1 + a] = __fadd_rn(sum[1 + a], __ldg(f + 8 + 3 * k + a));
-#pragma unroll
-        for (int ch = 0; ch < 6; ++ch) sum[4 + ch] = __fadd_rn(sum[4 + ch], __ldg(f + 53 + 6 * k + ch));
-    }
-    const float fm = (float)m;
-    const int32_t v = vid(x, y, z);
-    const int32_t slot = (int32_t)t;  // row * 8 + corner
-    float* o = vattr + (int64_t)slot * 9;
-    const int p[3] = {x, y, z};
-#pragma unroll
-    for (int a = 0; a < 3; ++a) {
-        const float mean = __fdiv_rn(sum[1 + a], fm);
-        o[a] = __fadd_rn(__fsub_rn(__fdiv_rn((float)p[a], (float)R), 0.5f), __fmul_rn(1.0f / (R * 2.0f), tanhf(mean)));
-    }
-#pragma unroll
-    for (int ch = 0; ch < 6; ++ch) {
-        const float mean = __fdiv_rn(sum[4 + ch], fm);
-        o[3 + ch] = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-mean)));
-    }
-    sdf[v] = __fdiv_rn(sum[0], fm);
-    vslot[v] = slot;
 }
 
 // Warp per (x, y) row of 256 cubes: occupancy bytes + surface count.
@@ -446,11 +465,10 @@ __device__ void emit_quad(int x, int y, int z, int d, int32_t u, int32_t v, bool
 }
 
 // Warp per (x, y) row of vertices: writes the surface edges in key order and
-// each quad's two triangles at its slot (flipped quads first).
+// a record {u, direction, flip} for each quad at its slot (flipped first).
 __global__ void fc_edge_write_kernel(const float* __restrict__ sdf, const int4* __restrict__ row_off,
-                                     const int64_t* __restrict__ totals, const int32_t* __restrict__ sidx,
-                                     const int32_t* __restrict__ dmap, const float* __restrict__ dual_gamma,
-                                     int32_t* __restrict__ edges, int32_t* __restrict__ faces) {
+                                     const int64_t* __restrict__ totals, int32_t* __restrict__ edges,
+                                     int32_t* __restrict__ quads) {
     const int row = (int)((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= RV * RV) return;
@@ -482,10 +500,7 @@ __global__ void fc_edge_write_kernel(const float* __restrict__ sdf, const int4* 
                 edges[(int64_t)ep * 2] = u;
                 edges[(int64_t)ep * 2 + 1] = second[d];
                 ++ep;
-                if (q >> d & 1u) {
-                    emit_quad(x, y, z, d, u, second[d], flip, sidx, dmap, dual_gamma, faces + qp * 6);
-                    ++qp;
-                }
+                if (q >> d & 1u) quads[qp++] = u | d << 25 | (int32_t)flip << 27;
             }
         }
         const int total = __shfl_sync(0xffffffffu, incl, 31);
@@ -493,6 +508,21 @@ __global__ void fc_edge_write_kernel(const float* __restrict__ sdf, const int4* 
         off.y += total >> 10 & 1023;
         off.z += total >> 20 & 1023;
     }
+}
+
+// Thread per quad record (u < 2^25 vertices, direction in bits 25-26, flip in bit 27).
+__global__ void fc_quad_kernel(const int32_t* __restrict__ quads, int64_t nq, const int32_t* __restrict__ sidx,
+                               const int32_t* __restrict__ dmap, const float* __restrict__ dual_gamma,
+                               int32_t* __restrict__ faces) {
+    const int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (q >= nq) return;
+    const int32_t rec = quads[q];
+    const int32_t u = rec & ((1 << 25) - 1);
+    const int d = rec >> 25 & 3;
+    const bool flip = rec >> 27 & 1;
+    const int x = u / (RV * RV), y = u / RV % RV, z = u % RV;
+    const int32_t v = d == 0 ? u - RV : d == 1 ? u + 1 : u + RV * RV;
+    emit_quad(x, y, z, d, u, v, flip, sidx, dmap, dual_gamma, faces + q * 6);
 }
 
 int grid_for(int64_t n, int threads) {
@@ -612,10 +642,9 @@ extern "C" S3DSP_API s3d_status s3dsp_flexicubes_extract(s3dsp_context* ctx, con
     if (e != cudaSuccess) return cuda_fail(error, error_capacity, e, "flexicubes scratch");
     S3DSP_CUDA(cudaMemsetAsync(cube_row, 0x7F, 4 * kCubes, st), "memset");
     S3DSP_CUDA(cudaMemsetAsync(err_row, 0x7F, 16, st), "memset");
-    fc_fill_kernel<<<ctx->sm_count * 8, 256, 0, st>>>(sdf, vslot, kVerts);
     fc_scatter_kernel<<<grid_for(n, 256), 256, 0, st>>>(coords, n, cube_row, err_row);
     fc_dup_kernel<<<grid_for(n, 256), 256, 0, st>>>(coords, n, cube_row, err_row);
-    fc_aggregate_kernel<<<grid_for(n * 8, 256), 256, 0, st>>>(d_raw, coords, n, cube_row, sdf, vslot, vattr);
+    fc_vertex_kernel<<<(RV * RV * kVChunks + 7) / 8, 256, 0, st>>>(d_raw, cube_row, sdf, vslot, vattr);
     fc_surface_count_kernel<<<R * R / 8, 256, 0, st>>>(sdf, occ, srow_count);
     fc_edge_count_kernel<<<(RV * RV + 7) / 8, 256, 0, st>>>(sdf, erow_count);
     S3DSP_LAUNCH_CHECK("flexicubes count kernels");
@@ -666,11 +695,12 @@ extern "C" S3DSP_API s3d_status s3dsp_flexicubes_extract(s3dsp_context* ctx, con
     if (e == cudaSuccess) e = alloc(&m->edges, 8 * (size_t)ne);
     int4 *onehot = nullptr, *rank = nullptr;
     float* dual_gamma = nullptr;
-    int32_t* dmap = nullptr;
+    int32_t *dmap = nullptr, *quads = nullptr;
     if (e == cudaSuccess) e = sc.get(&onehot, 16 * (size_t)ns);
     if (e == cudaSuccess) e = sc.get(&rank, 16 * (size_t)ns);
     if (e == cudaSuccess) e = sc.get(&dual_gamma, 4 * vcap);
     if (e == cudaSuccess) e = sc.get(&dmap, 48 * (size_t)ns);
+    if (e == cudaSuccess) e = sc.get(&quads, 4 * (size_t)nq);
     if (e == cudaSuccess && ns > 0) {
         fc_surface_write_kernel<<<R * R / 8, 256, 0, st>>>(occ, srow_off, m->surface, sidx);
         fc_case_kernel<<<grid_for(ns, 256), 256, 0, st>>>(m->surface, ns, occ, tables->num_dual, tables->check,
@@ -693,8 +723,9 @@ extern "C" S3DSP_API s3d_status s3dsp_flexicubes_extract(s3dsp_context* ctx, con
         e = cudaMemsetAsync(totals + 7, 0, 8, st);
     }
     if (e == cudaSuccess && ne > 0) {
-        fc_edge_write_kernel<<<(RV * RV + 7) / 8, 256, 0, st>>>(sdf, erow_off, totals, sidx, dmap, dual_gamma,
-                                                                 m->edges, m->faces);
+        fc_edge_write_kernel<<<(RV * RV + 7) / 8, 256, 0, st>>>(sdf, erow_off, totals, m->edges, quads);
+        if (nq > 0)
+            fc_quad_kernel<<<grid_for(nq, 128), 128, 0, st>>>(quads, nq, sidx, dmap, dual_gamma, m->faces);
         e = cudaGetLastError();
     }
     int64_t nv = 0;

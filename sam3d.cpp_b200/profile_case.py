@@ -3,11 +3,13 @@
   python sam3d.cpp_b200/profile_case.py conv2      # config-2 conv (C=256, 15,159 voxels), 128-row kernel
   python sam3d.cpp_b200/profile_case.py conv_sk    # 256^3 shell (241,978 voxels), C=256, stream-K kernel
   python sam3d.cpp_b200/profile_case.py tables     # hash + submanifold kmap of the 2.58M-voxel 512^3 shell
+  python sam3d.cpp_b200/profile_case.py flexicubes # FlexiCubes extraction of 970,176 cubes at 256^3
 
 Each case warms up once, then runs the kernel(s) under test `--reps` times on
 one stream, synchronising at the end; the process exits 0 on success. The
 inputs are larger than L2 where the case allows it (conv_sk: 124 MB of bf16
-features; tables: 41 MB of coordinates, 168 MB of table, 279 MB of map).
+features; tables: 41 MB of coordinates, 168 MB of table, 279 MB of map;
+flexicubes: 392 MB of raw features, about 0.9 GB of dense grids and slots).
 """
 from __future__ import annotations
 
@@ -22,7 +24,7 @@ sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["conv2", "conv_sk", "tables"])
+    ap.add_argument("case", choices=["conv2", "conv_sk", "tables", "flexicubes"])
     ap.add_argument("--reps", type=int, default=3)
     a = ap.parse_args()
     import torch
@@ -44,6 +46,14 @@ def main():
         flags = s3dsp.CONV_TILE128 if a.case == "conv2" else s3dsp.CONV_STREAM_K
         for _ in range(1 + a.reps):
             ctx.conv(k, 27, P, x, w, b, out, c, flags=flags)
+    elif a.case == "flexicubes":
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        t = np.load(os.path.join(root, "tests", "golden", "flexicubes_tables.npz"))
+        tab = ctx.flexicubes_tables(t["dmc"], t["num_dual"], t["check"])
+        coords, raw = workloads.flexicubes_input(64, 0)
+        dc, dr = torch.from_numpy(coords).cuda(), torch.from_numpy(raw).cuda()
+        for _ in range(1 + a.reps):
+            ctx.flexicubes(tab, dr, dc).free()
     else:
         coords = workloads.ellipsoid_shell(512, 0, thickness=4.0)  # the config-5b volume
         d = torch.from_numpy(coords).cuda()
