@@ -48,6 +48,7 @@ typedef struct s3dsp_kmap s3dsp_kmap;
 typedef struct s3dsp_slat_tables s3dsp_slat_tables;
 typedef struct s3dsp_fc_tables s3dsp_fc_tables;
 typedef struct s3dsp_mesh s3dsp_mesh;
+typedef struct s3dsp_gguf s3dsp_gguf;
 
 /* element types */
 #define S3DSP_F32 UINT32_C(0)
@@ -173,6 +174,68 @@ S3DSP_API s3d_status s3dsp_gs_window_tables(s3dsp_context *ctx, const int32_t *d
  * then channels/6 cosines of coordinate * 10000^(-i/(channels/6)). */
 S3DSP_API s3d_status s3dsp_ape(s3dsp_context *ctx, const int32_t *d_coords, int64_t n, int32_t channels,
                                float *d_out, char *error, uint64_t error_capacity);
+
+/* ---------------------------------------------------------------------------
+ * On-disk formats. GGUF weight files (GGUFModel::load / get / u32 / i32 / f32
+ * / str / str_array / i32_array, src/objects_runtime/gguf_loader.hpp:14-46):
+ * header, metadata and tensor directory parsed on the host at open, tensor
+ * bytes read on demand. SAMT raw tensors (save_raw_tensor / load_raw_tensor,
+ * src/objects_runtime/common.hpp:34-48, common.cpp:59-119). ggml type ids:
+ * F32 0, F16 1, Q4_0 2, Q4_1 3, Q8_0 8, Q4_K 12, I32 26, BF16 30.
+ * ------------------------------------------------------------------------- */
+S3DSP_API s3d_status s3dsp_gguf_open(const char *path, s3dsp_gguf **out, char *error,
+                                     uint64_t error_capacity);
+S3DSP_API void s3dsp_gguf_close(s3dsp_gguf *gguf);
+S3DSP_API int64_t s3dsp_gguf_n_tensors(const s3dsp_gguf *gguf);
+/* index of a tensor by name, -1 when absent (GGUFModel::get / has) */
+S3DSP_API int64_t s3dsp_gguf_find(const s3dsp_gguf *gguf, const char *name);
+/* ne[4] in ggml order (ne[0] fastest); nbytes of the stored data */
+S3DSP_API s3d_status s3dsp_gguf_tensor_info(const s3dsp_gguf *gguf, int64_t index, const char **name,
+                                            int32_t *ggml_type, int32_t *n_dims, int64_t *ne,
+                                            uint64_t *nbytes);
+/* metadata with defaults, GGUFModel semantics: u32/i32 accept the 32- and
+ * 64-bit integer types; str / str_array copy a NUL-terminated string and
+ * return its length (-1 when missing or of another type); i32_array and
+ * array_len return the element count (-1 likewise). */
+S3DSP_API uint32_t s3dsp_gguf_u32(const s3dsp_gguf *gguf, const char *key, uint32_t def);
+S3DSP_API int32_t s3dsp_gguf_i32(const s3dsp_gguf *gguf, const char *key, int32_t def);
+S3DSP_API float s3dsp_gguf_f32(const s3dsp_gguf *gguf, const char *key, float def);
+S3DSP_API int64_t s3dsp_gguf_str(const s3dsp_gguf *gguf, const char *key, char *buf, uint64_t cap);
+S3DSP_API int64_t s3dsp_gguf_array_len(const s3dsp_gguf *gguf, const char *key);
+S3DSP_API int64_t s3dsp_gguf_str_array(const s3dsp_gguf *gguf, const char *key, int64_t i, char *buf,
+                                       uint64_t cap);
+S3DSP_API int64_t s3dsp_gguf_i32_array(const s3dsp_gguf *gguf, const char *key, int32_t *out,
+                                       int64_t cap);
+/* raw stored bytes of a tensor into host memory */
+S3DSP_API s3d_status s3dsp_gguf_read(const s3dsp_gguf *gguf, int64_t index, void *h_dst,
+                                     uint64_t capacity, char *error, uint64_t error_capacity);
+/* a float tensor (F32, F16, BF16, Q8_0, Q4_0, Q4_1, Q4_K) to the device as
+ * dtype (S3DSP_F32 or S3DSP_BF16), dequantised with GGML's block formulas;
+ * synchronises the context's stream. */
+S3DSP_API s3d_status s3dsp_gguf_load(s3dsp_context *ctx, const s3dsp_gguf *gguf, int64_t index,
+                                     uint32_t dtype, void *d_out, int64_t capacity, char *error,
+                                     uint64_t error_capacity);
+/* a conv / linear weight by name straight into s3dsp_weights_pack's device
+ * layout, after checking the stored shape: MESH_PACKED ne = {cout*cin,
+ * kvol} (1x1 skips included, already transposed by the converter), SLAT_ROW
+ * ne = {27*cin, cout}, LINEAR ne = {cin, cout}. */
+S3DSP_API s3d_status s3dsp_gguf_load_weights(s3dsp_context *ctx, const s3dsp_gguf *gguf,
+                                             const char *name, uint32_t layout, int32_t kvol,
+                                             int64_t cin, int64_t cout, uint32_t precision,
+                                             void *d_dst, char *error, uint64_t error_capacity);
+/* device-to-device dequantisation of n elements stored as ggml_type */
+S3DSP_API s3d_status s3dsp_dequantize(s3dsp_context *ctx, int32_t ggml_type, const void *d_src,
+                                      int64_t n, uint32_t dtype, void *d_out, char *error,
+                                      uint64_t error_capacity);
+/* SAMT: "SAMT" | int32 ndims (1..8) | int64 ne[ndims] | int32 ggml type |
+ * data; type 30 reads as I32 (26), as the reference's reader normalises it. */
+S3DSP_API s3d_status s3dsp_samt_info(const char *path, int32_t *n_dims, int64_t *ne, int32_t *ggml_type,
+                                     uint64_t *nbytes, char *error, uint64_t error_capacity);
+S3DSP_API s3d_status s3dsp_samt_read(const char *path, void *h_dst, uint64_t capacity, char *error,
+                                     uint64_t error_capacity);
+S3DSP_API s3d_status s3dsp_samt_write(const char *path, int32_t n_dims, const int64_t *ne,
+                                      int32_t ggml_type, const void *data, uint64_t nbytes,
+                                      char *error, uint64_t error_capacity);
 
 /* ---------------------------------------------------------------------------
  * FlexiCubes extraction at resolution 256 (extract_object_mesh,

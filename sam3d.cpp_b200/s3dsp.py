@@ -34,7 +34,10 @@ EXPORTED = [
     "s3dsp_context_check", "s3dsp_hash_build", "s3dsp_hash_free", "s3dsp_hash_size",
     "s3dsp_hash_lookup", "s3dsp_gs_window_tables", "s3dsp_ape", "s3dsp_flexicubes_tables_create",
     "s3dsp_flexicubes_tables_free", "s3dsp_flexicubes_extract", "s3dsp_mesh_info", "s3dsp_mesh_device", "s3dsp_mesh_copy",
-    "s3dsp_mesh_free", "s3dsp_occupancy_coords", "s3dsp_prune_surface", "s3dsp_downsample_coords",
+    "s3dsp_mesh_free", "s3dsp_gguf_open", "s3dsp_gguf_close", "s3dsp_gguf_n_tensors", "s3dsp_gguf_find",
+    "s3dsp_gguf_tensor_info", "s3dsp_gguf_u32", "s3dsp_gguf_i32", "s3dsp_gguf_f32", "s3dsp_gguf_str",
+    "s3dsp_gguf_array_len", "s3dsp_gguf_str_array", "s3dsp_gguf_i32_array", "s3dsp_gguf_read", "s3dsp_gguf_load",
+    "s3dsp_gguf_load_weights", "s3dsp_dequantize", "s3dsp_samt_info", "s3dsp_samt_read", "s3dsp_samt_write", "s3dsp_occupancy_coords", "s3dsp_prune_surface", "s3dsp_downsample_coords",
     "s3dsp_kmap_build_subm3", "s3dsp_kmap_build_subm3_rows", "s3dsp_kmap_build_subm3_range", "s3dsp_subdivide", "s3dsp_kmap_free",
     "s3dsp_kmap_rows", "s3dsp_kmap_export_dense", "s3dsp_kmap_pairs", "s3dsp_kmap_pairs_noalloc",
     "s3dsp_weights_packed_bytes", "s3dsp_weights_pack", "s3dsp_gn_partials_count", "s3dsp_conv", "s3dsp_conv_kernel",
@@ -91,6 +94,27 @@ def load(path: str = LIB_PATH):
         "s3dsp_mesh_device": (_u32, [_vp] + [ctypes.POINTER(_vp)] * 6),
         "s3dsp_mesh_copy": (_u32, [_vp, _vp] + [_vp] * 6 + [_cp, _u64]),
         "s3dsp_mesh_free": (None, [_vp, _vp]),
+        "s3dsp_gguf_open": (_u32, [ctypes.c_char_p, ctypes.POINTER(_vp), _cp, _u64]),
+        "s3dsp_gguf_close": (None, [_vp]),
+        "s3dsp_gguf_n_tensors": (_i64, [_vp]),
+        "s3dsp_gguf_find": (_i64, [_vp, ctypes.c_char_p]),
+        "s3dsp_gguf_tensor_info": (_u32, [_vp, _i64, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(_i32),
+                                          ctypes.POINTER(_i32), ctypes.POINTER(_i64), ctypes.POINTER(_u64)]),
+        "s3dsp_gguf_u32": (ctypes.c_uint32, [_vp, ctypes.c_char_p, ctypes.c_uint32]),
+        "s3dsp_gguf_i32": (_i32, [_vp, ctypes.c_char_p, _i32]),
+        "s3dsp_gguf_f32": (ctypes.c_float, [_vp, ctypes.c_char_p, ctypes.c_float]),
+        "s3dsp_gguf_str": (_i64, [_vp, ctypes.c_char_p, _cp, _u64]),
+        "s3dsp_gguf_array_len": (_i64, [_vp, ctypes.c_char_p]),
+        "s3dsp_gguf_str_array": (_i64, [_vp, ctypes.c_char_p, _i64, _cp, _u64]),
+        "s3dsp_gguf_i32_array": (_i64, [_vp, ctypes.c_char_p, _vp, _i64]),
+        "s3dsp_gguf_read": (_u32, [_vp, _i64, _vp, _u64, _cp, _u64]),
+        "s3dsp_gguf_load": (_u32, [_vp, _vp, _i64, _u32, _vp, _i64, _cp, _u64]),
+        "s3dsp_gguf_load_weights": (_u32, [_vp, _vp, ctypes.c_char_p, _u32, _i32, _i64, _i64, _u32, _vp, _cp, _u64]),
+        "s3dsp_dequantize": (_u32, [_vp, _i32, _vp, _i64, _u32, _vp, _cp, _u64]),
+        "s3dsp_samt_info": (_u32, [ctypes.c_char_p, ctypes.POINTER(_i32), ctypes.POINTER(_i64), ctypes.POINTER(_i32),
+                                   ctypes.POINTER(_u64), _cp, _u64]),
+        "s3dsp_samt_read": (_u32, [ctypes.c_char_p, _vp, _u64, _cp, _u64]),
+        "s3dsp_samt_write": (_u32, [ctypes.c_char_p, _i32, _vp, _i32, _vp, _u64, _cp, _u64]),
         "s3dsp_occupancy_coords": (_u32, [_vp, _vp, _i32, _i32, _i32, _i32, _vp, _i64, ctypes.POINTER(_i64), _cp,
                                           _u64]),
         "s3dsp_prune_surface": (_u32, [_vp, _vp, _i64, _i32, _vp, _i64, ctypes.POINTER(_i64), _cp, _u64]),
@@ -260,6 +284,152 @@ class Mesh:
             self.free()
         except Exception:
             pass
+
+
+GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q4_1, GGML_Q8_0, GGML_Q4_K, GGML_I32, GGML_BF16 = 0, 1, 2, 3, 8, 12, 26, 30
+
+
+class Gguf:
+    """A GGUF weight file (s3dsp_gguf_*): metadata and tensor directory on the
+    host; tensors read raw or loaded to the device (dequantised / packed).
+    Shapes are numpy order (ne reversed)."""
+
+    def __init__(self, path: str):
+        h = _vp()
+        _call(load().s3dsp_gguf_open, path.encode(), ctypes.byref(h))
+        self.handle = h.value
+        self.path = path
+
+    def close(self):
+        if getattr(self, "handle", None):
+            load().s3dsp_gguf_close(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def names(self) -> list:
+        L = load()
+        out = []
+        for i in range(L.s3dsp_gguf_n_tensors(self.handle)):
+            nm = ctypes.c_char_p()
+            L.s3dsp_gguf_tensor_info(self.handle, i, ctypes.byref(nm), None, None, None, None)
+            out.append(nm.value.decode())
+        return out
+
+    def index(self, name: str) -> int:
+        i = load().s3dsp_gguf_find(self.handle, name.encode())
+        if i < 0:
+            raise KeyError(name)
+        return i
+
+    def info(self, name: str) -> dict:
+        t, nd, nb = _i32(), _i32(), _u64()
+        ne = (_i64 * 4)()
+        st = load().s3dsp_gguf_tensor_info(self.handle, self.index(name), None, ctypes.byref(t), ctypes.byref(nd), ne,
+                                           ctypes.byref(nb))
+        if st != S3D_OK:
+            raise S3dError(st, "s3dsp_gguf_tensor_info")
+        return dict(type=t.value, shape=tuple(reversed(ne[:nd.value])), nbytes=nb.value)
+
+    def u32(self, key, default=0):
+        return load().s3dsp_gguf_u32(self.handle, key.encode(), default)
+
+    def i32(self, key, default=0):
+        return load().s3dsp_gguf_i32(self.handle, key.encode(), default)
+
+    def f32(self, key, default=0.0):
+        return load().s3dsp_gguf_f32(self.handle, key.encode(), default)
+
+    def str(self, key, default=""):
+        n = load().s3dsp_gguf_str(self.handle, key.encode(), None, 0)
+        if n < 0:
+            return default
+        buf = ctypes.create_string_buffer(n + 1)
+        load().s3dsp_gguf_str(self.handle, key.encode(), buf, n + 1)
+        return buf.raw[:n].decode()
+
+    def str_array(self, key) -> list:
+        L = load()
+        n = L.s3dsp_gguf_array_len(self.handle, key.encode())
+        out = []
+        for i in range(max(n, 0)):
+            m = L.s3dsp_gguf_str_array(self.handle, key.encode(), i, None, 0)
+            if m < 0:
+                return []
+            buf = ctypes.create_string_buffer(m + 1)
+            L.s3dsp_gguf_str_array(self.handle, key.encode(), i, buf, m + 1)
+            out.append(buf.raw[:m].decode())
+        return out
+
+    def i32_array(self, key) -> list:
+        import numpy as np
+        n = load().s3dsp_gguf_i32_array(self.handle, key.encode(), None, 0)
+        if n < 0:
+            return []
+        a = np.zeros(n, np.int32)
+        load().s3dsp_gguf_i32_array(self.handle, key.encode(), a.ctypes.data, n)
+        return a.tolist()
+
+    def read(self, name: str):
+        """Raw stored bytes (numpy uint8)."""
+        import numpy as np
+        a = np.zeros(self.info(name)["nbytes"], np.uint8)
+        _call(load().s3dsp_gguf_read, self.handle, self.index(name), a.ctypes.data, a.nbytes)
+        return a
+
+    def load(self, ctx: "Context", name: str, bf16: bool = False):
+        """A float tensor on ctx's device as f32 (or bf16), numpy-order shape."""
+        import torch
+        shape = self.info(name)["shape"]
+        out = torch.empty(shape, dtype=torch.bfloat16 if bf16 else torch.float32, device=f"cuda:{ctx.device}")
+        _call(load().s3dsp_gguf_load, ctx.handle, self.handle, self.index(name), BF16 if bf16 else F32, ptr(out),
+              out.numel())
+        return out
+
+    def load_weights(self, ctx: "Context", name: str, layout: int, kvol: int, cin: int, cout: int, precision: int):
+        """A conv / linear weight packed for `precision` (uint8 device buffer)."""
+        import torch
+        dst = torch.empty(Context.packed_bytes(precision, kvol, cin, cout), dtype=torch.uint8,
+                          device=f"cuda:{ctx.device}")
+        _call(load().s3dsp_gguf_load_weights, ctx.handle, self.handle, name.encode(), layout, kvol, cin, cout,
+              precision, ptr(dst))
+        return dst
+
+
+def samt_info(path: str) -> dict:
+    nd, t, nb = _i32(), _i32(), _u64()
+    ne = (_i64 * 8)()
+    _call(load().s3dsp_samt_info, path.encode(), ctypes.byref(nd), ne, ctypes.byref(t), ctypes.byref(nb))
+    return dict(shape=tuple(reversed(ne[:nd.value])), type=t.value, nbytes=nb.value)
+
+
+def samt_read(path: str):
+    """(raw bytes as numpy uint8, info dict); F32 / I32 tensors come back typed."""
+    import numpy as np
+    inf = samt_info(path)
+    a = np.zeros(inf["nbytes"], np.uint8)
+    _call(load().s3dsp_samt_read, path.encode(), a.ctypes.data, a.nbytes)
+    if inf["type"] == GGML_F32:
+        return a.view(np.float32).reshape(inf["shape"]), inf
+    if inf["type"] == GGML_I32:
+        return a.view(np.int32).reshape(inf["shape"]), inf
+    return a, inf
+
+
+def samt_write(path: str, array, ggml_type: int | None = None, shape=None):
+    """Writes a numpy array (F32 / I32 inferred) or raw bytes with an explicit
+    type and numpy-order shape."""
+    import numpy as np
+    a = np.ascontiguousarray(array)
+    if ggml_type is None:
+        ggml_type = {np.dtype(np.float32): GGML_F32, np.dtype(np.int32): GGML_I32}[a.dtype]
+    shape = a.shape if shape is None else shape
+    ne = (_i64 * len(shape))(*reversed(shape))
+    _call(load().s3dsp_samt_write, path.encode(), len(shape), ne, ggml_type, a.ctypes.data, a.nbytes)
 
 
 class Context:
