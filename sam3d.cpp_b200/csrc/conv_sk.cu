@@ -22,7 +22,9 @@
 // CTA, so no co-residency is assumed.
 //
 // Warp roles (672 threads) as in the 128-row kernel: warps 0-15 gather A by
-// cp.async (4 rows x 16 B per thread per step) and then run the epilogue
+// cp.async (4 rows x 16 B per thread per step; each thread reads the map
+// entries of its own rows from global memory one kernel offset ahead, so a
+// segment starts gathering at once) and then run the epilogue
 // (warp w: TMEM lanes 32*(w%4).., column chunks w/4, w/4+4, ...; write-out
 // rows 8w..8w+7), warps 16-19 issue the weight TMA loads, warp 20 owns TMEM
 // and issues 8 tcgen05.mma (M=128, N=BN, K=16) per step. Waits are bounded
@@ -49,7 +51,6 @@ constexpr int kMmaWarp = 20;
 constexpr int kThreads = 21 * 32;
 constexpr int kKC = 64;  // channels per pipeline stage (128-byte rows, SWIZZLE_128B; 32 measured slower)
 constexpr int kAHalf = 128 * 2 * kKC;  // the second accumulator's rows start here in an A stage
-constexpr int kMaxKvol = 27;
 constexpr int kSmemMax = kSmemOptIn;
 
 struct SkParams {
@@ -103,7 +104,8 @@ __device__ __forceinline__ int64_t ws_slot(const SkParams& p, int i, int64_t wt)
     return 2 * (int64_t)i + ((unit_begin(p, i) / p.kvol) == wt ? 0 : 1);
 }
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
-__device__ __forceinline__ void prod_bar() { asm volatile("bar.sync 2, 512;" ::: "memory"); }
+
+
 
 // kRows = 256: two 128-row accumulators per work tile; 128: one.
 template <int kRows>
@@ -116,13 +118,12 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
     const int bstage = p.bn * 2 * kKC;
     const int ostride = p.bn + 4;  // staged f32 row stride (floats)
     // layout: region0 = max(ring A | ring B, epilogue tile | GN column sums),
-    // then sidx, barriers, tmem holder, flags
+    // then barriers, tmem holder, flags
     const size_t ring = (size_t)S * (kAStage + bstage);
     const size_t epi = (size_t)128 * ostride * 4 + (size_t)kProdWarps * p.bn * 16;
     uint8_t* sA = smem;
     uint8_t* sB = smem + (size_t)S * kAStage;
-    int32_t* sidx = reinterpret_cast<int32_t*>(smem + (ring > epi ? ring : epi));  // [kvol][256]
-    uint64_t* full = reinterpret_cast<uint64_t*>(sidx + kMaxKvol * kRows);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + (ring > epi ? ring : epi));
     uint64_t* empty = full + S;
     uint64_t* accum = empty + S;
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(accum + 1);
@@ -182,30 +183,40 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
 
         bool prod_ok = true;
         if (warp < kProdWarps) {
-            // ============ A producers: indices of this segment, then cp.async gathers ============
-            for (int i = tid; i < kMaxKvol * kRows; i += kEpiThreads) {
-                const int o = i / kRows, row = i & (kRows - 1);
-                if (!((mask >> o) & 1u)) continue;
-                const int64_t r = m0 + row;
-                int32_t s = -1;
-                if (r < p.n_out) s = p.nbr ? __ldg(p.nbr + (int64_t)o * p.n_out + r) : (int32_t)r;
-                sidx[i] = s < 0 ? -1 : (s >> p.in_shift);
-            }
-            prod_bar();
+            // ============ A producers: cp.async gathers ============
             constexpr int kCpr = kKC / 8;         // 16-byte chunks per row
             constexpr int kRowStep = 512 / kCpr;  // rows covered by one pass of the 512 threads
+            constexpr int kMine = kRows / kRowStep;  // rows of this thread: rg + kRowStep * i
             const int c16 = tid & (kCpr - 1);
-            const int rg = tid / kCpr;  // rows rg + kRowStep * i
+            const int rg = tid / kCpr;
+            // the map entries of this thread's rows for kernel offset o (source row, or -1)
+            auto load_idx = [&](int o, int32_t (&dst)[kMine]) {
+#pragma unroll
+                for (int i = 0; i < kMine; ++i) {
+                    const int64_t r = m0 + rg + kRowStep * i;
+                    int32_t src = -1;
+                    if (r < p.n_out) src = p.nbr ? __ldg(p.nbr + (int64_t)o * p.n_out + r) : (int32_t)r;
+                    dst[i] = src < 0 ? -1 : (src >> p.in_shift);
+                }
+            };
             uint32_t mrem = mask;
-            int o = 0;
+            int32_t cur[kMine], nxt[kMine];
+            if (mrem) {
+                load_idx(__ffs(mrem) - 1, nxt);
+                mrem &= mrem - 1;
+            }
             for (int j = 0; j < T; ++j) {
                 const uint32_t pit = it + (uint32_t)j;
                 const int s = (int)(pit % (uint32_t)S);
                 const uint32_t ph = (pit / (uint32_t)S) & 1u;
                 const int kc = j % p.kchunks;
-                if (kc == 0) {
-                    o = __ffs(mrem) - 1;
-                    mrem &= mrem - 1;
+                if (kc == 0) {  // next kernel offset: its entries were loaded one offset ago
+#pragma unroll
+                    for (int i = 0; i < kMine; ++i) cur[i] = nxt[i];
+                    if (mrem) {
+                        load_idx(__ffs(mrem) - 1, nxt);
+                        mrem &= mrem - 1;
+                    }
                 }
                 if (!mbar_wait(smem_u32(empty + s), ph ^ 1u, abort_flag, p.status)) {
                     prod_ok = false;
@@ -214,9 +225,9 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
                 const int k0 = kc * kKC + c16 * 8;
                 const uint32_t a_base = smem_u32(sA + (size_t)s * kAStage);
 #pragma unroll
-                for (int i = 0; i < kRows / kRowStep; ++i) {
+                for (int i = 0; i < kMine; ++i) {
                     const int row = rg + kRowStep * i;
-                    const int32_t src = sidx[o * kRows + row];
+                    const int32_t src = cur[i];
                     const bool valid = src >= 0 && k0 < p.cin;
                     const void* g = valid ? (const void*)(p.in + (int64_t)src * p.cin + k0) : (const void*)p.in;
                     cp_async_16(a_base + row * (2 * kKC) + ((c16 ^ kmajor_swz<kKC>(row)) << 4), g, valid ? 16u : 0u);
@@ -356,7 +367,18 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
                         if (k == 1) {
                             if (have_acc) tmem_ld16(tl + sub * p.thalf + 16 * c, f);
                         } else {
+                            // pieces in piece order; this CTA's own piece comes from TMEM (the
+                            // workspace holds the same f32 values)
                             for (int pc = 0; pc < k; ++pc) {
+                                if (i_first + pc == me) {
+                                    float g[16];
+                                    if (have_acc) {
+                                        tmem_ld16(tl + sub * p.thalf + 16 * c, g);
+#pragma unroll
+                                        for (int q = 0; q < 16; ++q) f[q] += g[q];
+                                    }
+                                    continue;
+                                }
                                 const int64_t sl = pc == 0 ? slot0 : 2 * (int64_t)(i_first + pc);
                                 const float4* s4 = reinterpret_cast<const float4*>(p.ws + sl * slot_stride) +
                                                    (size_t)(sub * nch + c) * 512 + row;
@@ -459,8 +481,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
 size_t sk_smem_bytes(int stages, int bn, int rows) {
     const size_t ring = (size_t)stages * ((size_t)rows * 2 * kKC + (size_t)bn * 2 * kKC);
     const size_t epi = (size_t)128 * (bn + 4) * 4 + (size_t)kProdWarps * bn * 16;
-    return 1024 /*align slack*/ + (ring > epi ? ring : epi) + (size_t)kMaxKvol * rows * 4 /*sidx*/ +
-           (2 * stages + 1) * 8 + 16;
+    return 1024 /*align slack*/ + (ring > epi ? ring : epi) + (2 * stages + 1) * 8 + 16;
 }
 
 }  // namespace

@@ -47,7 +47,6 @@ constexpr int kBWarp0 = 16;         // first weight-TMA warp
 constexpr int kMaxBWarps = 4;
 constexpr int kMmaWarp = 20;
 constexpr int kThreads = 21 * 32;
-constexpr int kMaxKvol = 27;
 // Each stage's "full" barrier may be split in kFullSplit barriers, one per
 // group of producer warps. Measured on B200 (config-2 conv, 85 us with one
 // barrier): 4 barriers 115 us, 16 barriers 469 us; one barrier per stage.
@@ -171,13 +170,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int brows = kPair ? p.bn / 2 : p.bn;  // weight rows held by this CTA
     constexpr int kAStage = 128 * 2 * KC;  // bytes: 128 rows x KC bf16
     const int bstage = brows * 2 * KC;
-    // layout (offsets from the 1024-aligned base): ring A | ring B | sidx |
-    // barriers | tmem holder, abort flag. The epilogue reuses the ring for
-    // its f32 output tile followed by the f64 GroupNorm column sums.
+    // layout (offsets from the 1024-aligned base): region0 = max(ring A |
+    // ring B, epilogue f32 output tile | f64 GroupNorm column sums), then
+    // barriers, tmem holder, abort flag.
     uint8_t* sA = smem;
     uint8_t* sB = smem + (size_t)S * kAStage;
-    int32_t* sidx = reinterpret_cast<int32_t*>(sB + (size_t)S * bstage);  // [kvol][128]
-    uint64_t* full = reinterpret_cast<uint64_t*>(sidx + kMaxKvol * 128);
+    const size_t ring_bytes = (size_t)S * (kAStage + bstage);
+    const size_t epi_bytes = (size_t)128 * (p.bn + 4) * 4 + (size_t)kProdWarps * p.bn * 16;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + (ring_bytes > epi_bytes ? ring_bytes : epi_bytes));
     constexpr int kFS = kPair ? 1 : kFullSplit;  // the pair relay arrives on one barrier
     uint64_t* empty = full + S * kFS;
     uint64_t* accum = empty + S;
@@ -208,7 +208,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int T = __popc(mask) * kchunks;
     const uint32_t tcols = p.bn <= 32 ? 32u : (p.bn <= 64 ? 64u : (p.bn <= 128 ? 128u : 256u));
 
-    // ---- setup: barriers, TMEM, gather indices ----
+    // ---- setup: barriers, TMEM ----
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
             // single CTA: cp.async threads + weight issuers; pair leader: + the
@@ -237,15 +237,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
         }
     }
-    // gather row coordinates of the active offsets for the tile's 128 rows
-    for (int i = tid; i < kMaxKvol * 128; i += kThreads) {
-        const int o = i >> 7, row = i & 127;
-        if (!((mask >> o) & 1u)) continue;
-        const int64_t r = m0 + row;
-        int32_t s = -1;
-        if (r < p.n_out) s = p.nbr ? __ldg(p.nbr + (int64_t)o * p.n_out + r) : (int32_t)r;
-        sidx[i] = s < 0 ? -1 : (s >> p.in_shift);
-    }
     tc_fence_before();
     __syncthreads();
     if (kPair) cluster_sync();  // the peer's barriers exist before any remote arrive
@@ -255,19 +246,39 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool prod_ok = true;
     if (warp < kProdWarps) {
         // ================= A producers: cp.async gathers =================
+        // Each thread gathers fixed rows (rg + kRowStep * i) and reads their map
+        // entries itself, one kernel offset ahead of the gathers that use them.
         constexpr int kCpr = KC / 8;          // 16-byte chunks per row
         constexpr int kRowStep = 512 / kCpr;  // rows covered by one pass of the 512 threads
+        constexpr int kMine = 128 / kRowStep;
         const int c16 = tid & (kCpr - 1);
         const int rg = tid / kCpr;  // rows rg, rg + kRowStep, ...
+        auto load_idx = [&](int o, int32_t (&dst)[kMine]) {
+#pragma unroll
+            for (int i = 0; i < kMine; ++i) {
+                const int64_t r = m0 + rg + kRowStep * i;
+                int32_t src = -1;
+                if (r < p.n_out) src = p.nbr ? __ldg(p.nbr + (int64_t)o * p.n_out + r) : (int32_t)r;
+                dst[i] = src < 0 ? -1 : (src >> p.in_shift);
+            }
+        };
         uint32_t mrem = mask;
-        int o = 0;
+        int32_t cur[kMine], nxt[kMine];
+        if (mrem) {
+            load_idx(__ffs(mrem) - 1, nxt);
+            mrem &= mrem - 1;
+        }
         for (int it = 0; it < T; ++it) {
             const int s = it % S;
             const uint32_t ph = (uint32_t)(it / S) & 1u;
             const int kc = it % kchunks;
             if (kc == 0) {
-                o = __ffs(mrem) - 1;
-                mrem &= mrem - 1;
+#pragma unroll
+                for (int i = 0; i < kMine; ++i) cur[i] = nxt[i];
+                if (mrem) {
+                    load_idx(__ffs(mrem) - 1, nxt);
+                    mrem &= mrem - 1;
+                }
             }
             if (!mbar_wait(smem_u32(empty + s), ph ^ 1u, abort_flag, p.status)) {
                 prod_ok = false;
@@ -276,9 +287,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int k0 = kc * KC + c16 * 8;
             const uint32_t a_base = smem_u32(sA + (size_t)s * kAStage);
 #pragma unroll
-            for (int i = 0; i < 128 / kRowStep; ++i) {
+            for (int i = 0; i < kMine; ++i) {
                 const int row = rg + kRowStep * i;
-                const int32_t src = sidx[o * 128 + row];
+                const int32_t src = cur[i];
                 const bool valid = src >= 0 && k0 < p.cin;
                 const void* g = valid ? (const void*)(p.in + (int64_t)src * p.cin + k0) : (const void*)p.in;
                 cp_async_16(a_base + row * (2 * KC) + ((c16 ^ kmajor_swz<KC>(row)) << 4), g, valid ? 16u : 0u);
@@ -497,9 +508,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // stage = 128 gathered rows + brows weight rows, KC bf16 each
 size_t stage_bytes(int brows, int kc) { return (size_t)(128 + brows) * 2 * kc; }
-size_t smem_bytes(int stages, int brows, int kc) {
-    return 1024 /*align slack*/ + (size_t)stages * stage_bytes(brows, kc) + ((kFullSplit + 1) * stages + 1) * 8 + 16 +
-           kMaxKvol * 128 * 4 /*sidx*/;
+size_t smem_bytes(int stages, int brows, int kc, int bn) {
+    const size_t ring = (size_t)stages * stage_bytes(brows, kc);
+    const size_t epi = (size_t)128 * (bn + 4) * 4 + (size_t)kProdWarps * bn * 16;
+    return 1024 /*align slack*/ + (ring > epi ? ring : epi) + ((kFullSplit + 1) * stages + 1) * 8 + 16;
 }
 
 }  // namespace
@@ -534,11 +546,6 @@ cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     const int kc = 64;
     int stages = (int)((200 * 1024) / stage_bytes(brows, kc));
     if (stages > 16) stages = 16;
-    // the epilogue reuses the ring and the gather indices after it for a
-    // 128 x (bn + 4) f32 tile plus 16 x bn x 2 f64 column sums
-    while ((size_t)stages * stage_bytes(brows, kc) + kMaxKvol * 128 * 4 <
-           (size_t)128 * (bn + 4) * 4 + (size_t)kProdWarps * bn * 16)
-        ++stages;
     (void)n_in;
 
     auto encode = get_encode_fn();
@@ -589,7 +596,7 @@ cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     p.gn_groups = gn_groups;
     p.status = ctx->d_status;
 
-    const size_t smem = smem_bytes(stages, brows, kc);
+    const size_t smem = smem_bytes(stages, brows, kc, bn);
     static std::atomic<uint64_t> optin_pair{0}, optin_single{0};
     cudaError_t e = pair ? smem_optin((const void*)conv_tc_kernel<true, 64>, ctx->device, optin_pair)
                          : smem_optin((const void*)conv_tc_kernel<false, 64>, ctx->device, optin_single);
