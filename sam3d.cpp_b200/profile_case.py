@@ -4,6 +4,8 @@
   python sam3d.cpp_b200/profile_case.py conv_sk    # 256^3 shell (241,978 voxels), C=256, stream-K kernel
   python sam3d.cpp_b200/profile_case.py tables     # hash + submanifold kmap of the 2.58M-voxel 512^3 shell
   python sam3d.cpp_b200/profile_case.py flexicubes # FlexiCubes extraction of 970,176 cubes at 256^3
+  python sam3d.cpp_b200/profile_case.py coords     # SS occupancy -> coords -> surface prune -> downsample (64^3 fixture)
+  python sam3d.cpp_b200/profile_case.py gs_tables  # GS window tables (both shifts) + APE, config-2 coordinates
 
 Each case warms up once, then runs the kernel(s) under test `--reps` times on
 one stream, synchronising at the end; the process exits 0 on success. The
@@ -24,7 +26,7 @@ sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["conv2", "conv_sk", "tables", "flexicubes"])
+    ap.add_argument("case", choices=["conv2", "conv_sk", "tables", "flexicubes", "coords", "gs_tables"])
     ap.add_argument("--reps", type=int, default=3)
     a = ap.parse_args()
     import torch
@@ -46,6 +48,25 @@ def main():
         flags = s3dsp.CONV_TILE128 if a.case == "conv2" else s3dsp.CONV_STREAM_K
         for _ in range(1 + a.reps):
             ctx.conv(k, 27, P, x, w, b, out, c, flags=flags)
+    elif a.case == "coords":
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        bits = np.load(os.path.join(root, "tests", "golden", "ss_occ_mask.npz"))["bits"]
+        grid = torch.from_numpy(np.unpackbits(bits)[: 64 ** 3].astype(np.float32).reshape(64, 64, 64)).cuda()
+        bufs = [torch.empty((grid.numel(), 4), dtype=torch.int32, device="cuda") for _ in range(3)]
+        for _ in range(1 + a.reps):
+            m1 = ctx.occupancy_coords(grid, bufs[0])
+            m2 = ctx.prune_surface(bufs[0][:m1], bufs[1])
+            ctx.downsample_coords(bufs[1][:m2], bufs[2], 42000, 2, 42)
+    elif a.case == "gs_tables":
+        coords = torch.from_numpy(workloads.config2(seed=0)["coords"]).cuda()
+        n = coords.shape[0]
+        bkt = torch.empty(n, dtype=torch.int32, device="cuda")
+        bwd = torch.empty(n, dtype=torch.int32, device="cuda")
+        ape = torch.empty((n, 768), device="cuda")
+        for _ in range(1 + a.reps):
+            for si in (0, 1):
+                ctx.gs_window_tables(coords, 4 * si, bkt, bwd)
+            ctx.ape(coords, ape)
     elif a.case == "flexicubes":
         root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
         t = np.load(os.path.join(root, "tests", "golden", "flexicubes_tables.npz"))
