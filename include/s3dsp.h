@@ -58,6 +58,10 @@ typedef struct s3dsp_gguf s3dsp_gguf;
 /* arithmetic of a convolution */
 #define S3DSP_PREC_F32_STRICT UINT32_C(0) /* f32 FMA, f32 accumulation */
 #define S3DSP_PREC_BF16 UINT32_C(1)       /* bf16 tcgen05 MMA, f32 accumulation in TMEM */
+#define S3DSP_PREC_F32_3XTF32 UINT32_C(2) /* f32 in / out on the tensor cores: operands split into a TF32
+                                             high part and its remainder, lo*hi + hi*lo + hi*hi
+                                             tcgen05 MMAs (kind::tf32) into an f32 TMEM accumulator.
+                                             s3dsp_conv only (no prologue, no CTA pairs) */
 
 /* weight layouts accepted by s3dsp_weights_pack (all row-major as stored in GGUF) */
 #define S3DSP_LAYOUT_SLAT_ROW UINT32_C(0)    /* (Cout, 27, Cin): scripts/objects/gguf_schema.py:326-334 */

@@ -42,6 +42,7 @@ extern "C" S3DSP_API const char* s3dsp_conv_kernel(const s3dsp_context* ctx, int
     (void)cout;
     if (!ctx) return nullptr;
     if (precision == S3DSP_PREC_F32_STRICT) return "conv_f32_kernel";
+    if (precision == S3DSP_PREC_F32_3XTF32) return "conv_tc_kernel<tf32x3>";
     if (precision != S3DSP_PREC_BF16) return nullptr;
     return bf16_kernel_name(pick_bf16_kernel(ctx, n_out, kvol, flags));
 }
@@ -122,6 +123,31 @@ extern "C" S3DSP_API s3d_status s3dsp_conv(s3dsp_context* ctx, const s3dsp_kmap*
                                kern == Bf16Kernel::kStreamK128 ? 128 : 256, error, error_capacity, &st);
         if (st != S3D_OK) return st;
         if (e != cudaSuccess) return cuda_fail(error, error_capacity, e, bf16_kernel_name(kern));
+        return S3D_OK;
+    }
+    if (precision == S3DSP_PREC_F32_3XTF32) {
+        if (in_dtype != S3DSP_F32)
+            return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "3XTF32 precision needs f32 input");
+        if (flags & (S3DSP_PRO_AFFINE_SILU | S3DSP_CONV_CTA_PAIR))
+            return fail(error, error_capacity, S3D_INVALID_ARGUMENT,
+                        "3XTF32 conv takes pre-normalised input and runs without CTA pairs");
+        if (cin % 4 || ((uintptr_t)in & 15) || ((uintptr_t)weight & 15) || ((uintptr_t)out & 15) ||
+            ((uintptr_t)residual & 15))
+            return fail(error, error_capacity, S3D_INVALID_ARGUMENT,
+                        "3XTF32 needs cin %% 4 == 0 and 16-byte aligned in/weight/out/residual");
+        // the input split once into TF32 high parts and remainders (stream-ordered scratch)
+        const size_t nel = (size_t)n_in * (size_t)cin;
+        float* split = nullptr;
+        S3DSP_CUDA(cudaMallocAsync(&split, 8 * (nel > 0 ? nel : 1), ctx->stream), "3xTF32 split buffer");
+        e = split_tf32(ctx, (const float*)in, (int64_t)nel, split, split + nel);
+        s3d_status st = S3D_OK;
+        if (e == cudaSuccess)
+            e = launch_conv_tf32x3(ctx, kmap, kvol, split, split + nel, (int)cin, in_shift, (const float*)weight, bias,
+                                   residual, res_dtype, res_shift, out, out_dtype, n_out, (int)cout, flags,
+                                   gn_partials, gn_groups, error, error_capacity, &st);
+        cudaFreeAsync(split, ctx->stream);
+        if (st != S3D_OK) return st;
+        if (e != cudaSuccess) return cuda_fail(error, error_capacity, e, "conv_tc_kernel<tf32x3>");
         return S3D_OK;
     }
     return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "unknown precision %u", precision);

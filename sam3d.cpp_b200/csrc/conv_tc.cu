@@ -53,7 +53,10 @@ constexpr int kThreads = 21 * 32;
 constexpr int kFullSplit = 1;
 
 struct TcParams {
-    const __nv_bfloat16* in;
+    const __nv_bfloat16* in;    // BF16 input [n_in, cin]
+    const float* in_hi;         // 3xTF32: input split into TF32 high parts ...
+    const float* in_lo;         // ... and the f32 remainders, [n_in, cin] each
+    int lo_rows;                // 3xTF32: row of the low weight block in the weight tensor map
     int cin;
     int in_shift;
     const int32_t* nbr;         // [kvol][n_out] or null (identity)
@@ -160,7 +163,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
 // tile, so weight traffic per output row halves. The leader (rank 0) issues
 // the MMAs; the peer's weight TMA completes on the leader's barrier and the
 // peer's gathered rows are relayed to it by a remote mbarrier arrive.
-template <bool kPair, int KC>
+template <bool kPair, int KC, bool kTF32 = false>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_tc_kernel(const TcParams p, const __grid_constant__ CUtensorMap wmap) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -168,8 +171,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int S = p.stages;
     const int brows = kPair ? p.bn / 2 : p.bn;  // weight rows held by this CTA
-    constexpr int kAStage = 128 * 2 * KC;  // bytes: 128 rows x KC bf16
-    const int bstage = brows * 2 * KC;
+    // A row chunk: KC elements = 128 bytes (64 bf16, or 32 f32 read as TF32);
+    // 3xTF32 stages hold a high and a low half of each operand
+    constexpr int kEs = kTF32 ? 4 : 2;        // bytes per element
+    constexpr int kRowB = KC * kEs;           // bytes per row chunk
+    constexpr int KCB = kRowB / 2;            // the same row in bf16 units (swizzle / descriptors)
+    constexpr int kParts = kTF32 ? 2 : 1;
+    constexpr int kAHalf = 128 * kRowB;       // bytes of one A half
+    constexpr int kAStage = kAHalf * kParts;
+    const int bhalf = brows * kRowB;
+    const int bstage = bhalf * kParts;
     // layout (offsets from the 1024-aligned base): region0 = max(ring A |
     // ring B, epilogue f32 output tile | f64 GroupNorm column sums), then
     // barriers, tmem holder, abort flag.
@@ -204,9 +215,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
     mask &= (p.kvol >= 32) ? 0xffffffffu : ((1u << p.kvol) - 1u);
-    const int kchunks = (p.cin + 63) / 64 * (64 / KC);  // KC-channel reduction chunks per offset
+    // KC-channel reduction chunks per offset
+    const int kchunks = kTF32 ? (p.cin + KC - 1) / KC : (p.cin + 63) / 64 * (64 / KC);
     const int T = __popc(mask) * kchunks;
-    const uint32_t tcols = p.bn <= 32 ? 32u : (p.bn <= 64 ? 64u : (p.bn <= 128 ? 128u : 256u));
+    // 3xTF32 keeps kTfAcc accumulators (one per K step of a stage, summed in the
+    // epilogue): the tensor core's f32 accumulation truncates, and a quarter of
+    // the reduction per accumulator keeps the error inside the F32 gate
+    constexpr int kTfAcc = kTF32 ? kRowB / 32 : 1;
+    const int tneed = kTfAcc * p.bn;
+    const uint32_t tcols = tneed <= 32 ? 32u : (tneed <= 64 ? 64u : (tneed <= 128 ? 128u : (tneed <= 256 ? 256u : 512u)));
 
     // ---- setup: barriers, TMEM ----
     if (tid == 0) {
@@ -248,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ================= A producers: cp.async gathers =================
         // Each thread gathers fixed rows (rg + kRowStep * i) and reads their map
         // entries itself, one kernel offset ahead of the gathers that use them.
-        constexpr int kCpr = KC / 8;          // 16-byte chunks per row
+        constexpr int kCpr = kRowB / 16;      // 16-byte chunks per row
         constexpr int kRowStep = 512 / kCpr;  // rows covered by one pass of the 512 threads
         constexpr int kMine = 128 / kRowStep;
         const int c16 = tid & (kCpr - 1);
@@ -284,15 +301,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                 prod_ok = false;
                 break;
             }
-            const int k0 = kc * KC + c16 * 8;
+            const int k0 = kc * KC + c16 * (16 / kEs);
             const uint32_t a_base = smem_u32(sA + (size_t)s * kAStage);
 #pragma unroll
             for (int i = 0; i < kMine; ++i) {
                 const int row = rg + kRowStep * i;
                 const int32_t src = cur[i];
                 const bool valid = src >= 0 && k0 < p.cin;
-                const void* g = valid ? (const void*)(p.in + (int64_t)src * p.cin + k0) : (const void*)p.in;
-                cp_async_16(a_base + row * (2 * KC) + ((c16 ^ kmajor_swz<KC>(row)) << 4), g, valid ? 16u : 0u);
+                const uint32_t d = a_base + row * kRowB + ((c16 ^ kmajor_swz<KCB>(row)) << 4);
+                if constexpr (kTF32) {
+                    const int64_t off = valid ? (int64_t)src * p.cin + k0 : 0;
+                    cp_async_16(d, p.in_hi + off, valid ? 16u : 0u);
+                    cp_async_16(d + kAHalf, p.in_lo + off, valid ? 16u : 0u);
+                } else {
+                    const void* g = valid ? (const void*)(p.in + (int64_t)src * p.cin + k0) : (const void*)p.in;
+                    cp_async_16(d, g, valid ? 16u : 0u);
+                }
             }
             cp_async_arrive_noinc(smem_u32(full + s * kFS + warp / (kProdWarps / kFS)));
         }
@@ -304,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t mrem = mask;
             int o = 0;
             const int rows = brows / p.nb;
-            const uint32_t bytes = (uint32_t)rows * 2 * KC;
+            const uint32_t bytes = (uint32_t)rows * kRowB;
             for (int it = 0; it < T; ++it) {
                 const int s = it % S;
                 const uint32_t ph = (uint32_t)(it / S) & 1u;
@@ -315,11 +339,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (!mbar_wait(smem_u32(empty + s), ph ^ 1u, abort_flag, p.status)) break;
                 const uint32_t fb = smem_u32(full + s * kFS);
-                const uint32_t dst = smem_u32(sB + (size_t)s * bstage + (size_t)j * rows * 2 * KC);
+                const uint32_t dst = smem_u32(sB + (size_t)s * bstage + (size_t)j * rows * kRowB);
                 const int y = o * p.cout_pad + n0 + (int)rank * brows + j * rows;
                 if (!kPair) {
-                    mbar_arrive_tx(fb, bytes);
+                    mbar_arrive_tx(fb, bytes * kParts);
                     tma_load_2d(dst, &wmap, kc * KC, y, fb);
+                    if (kTF32) tma_load_2d(dst + bhalf, &wmap, kc * KC, y + p.lo_rows, fb);
                 } else {
                     // the leader expects both CTAs' slice j; both complete on its barrier
                     if (leader) mbar_arrive_tx(fb, 2 * bytes);
@@ -358,16 +383,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t b0 = smem_u32(sB + (size_t)s * bstage);
                 if (kPair) {
 #pragma unroll
-                    for (int k = 0; k < KC / 16; ++k)
-                        mma_bf16_pair(tmem, kmajor_desc<KC>(a0 + 32 * k), kmajor_desc<KC>(b0 + 32 * k), p.idesc,
+                    for (int k = 0; k < kRowB / 32; ++k)
+                        mma_bf16_pair(tmem, kmajor_desc<KCB>(a0 + 32 * k), kmajor_desc<KCB>(b0 + 32 * k), p.idesc,
                                       (it > 0 || k > 0) ? 1u : 0u);
                     mma_commit_pair(smem_u32(empty + s));                       // this CTA's stage
                     mma_commit_pair(map_to_rank(smem_u32(empty + s), 1));      // the peer's stage
                 } else {
 #pragma unroll
-                    for (int k = 0; k < KC / 16; ++k)
-                        mma_bf16(tmem, kmajor_desc<KC>(a0 + 32 * k), kmajor_desc<KC>(b0 + 32 * k), p.idesc,
-                                 (it > 0 || k > 0) ? 1u : 0u);
+                    for (int k = 0; k < kRowB / 32; ++k) {
+                        if constexpr (kTF32) {
+                            // 3xTF32: lo*hi + hi*lo + hi*hi (small products first) into the
+                            // accumulator of K step k
+                            const uint64_t ah = kmajor_desc<KCB>(a0 + 32 * k), al = kmajor_desc<KCB>(a0 + kAHalf + 32 * k);
+                            const uint64_t bh = kmajor_desc<KCB>(b0 + 32 * k), bl = kmajor_desc<KCB>(b0 + bhalf + 32 * k);
+                            const uint32_t dk = tmem + (uint32_t)(k * p.bn);
+                            mma_tf32(dk, al, bh, p.idesc, it > 0 ? 1u : 0u);
+                            mma_tf32(dk, ah, bl, p.idesc, 1u);
+                            mma_tf32(dk, ah, bh, p.idesc, 1u);
+                        } else {
+                            mma_bf16(tmem, kmajor_desc<KCB>(a0 + 32 * k), kmajor_desc<KCB>(b0 + 32 * k), p.idesc,
+                                     (it > 0 || k > 0) ? 1u : 0u);
+                        }
+                    }
                     mma_commit(smem_u32(empty + s));
                 }
             }
@@ -397,6 +434,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float f[16];
                 if (have_acc) {
                     tmem_ld16(taddr + (uint32_t)c0, f);
+                    // 3xTF32: the other accumulators, summed in order in f32
+                    for (int a = 1; a < kTfAcc; ++a) {
+                        float g[16];
+                        tmem_ld16(taddr + (uint32_t)(a * p.bn + c0), g);
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) f[j] += g[j];
+                    }
                 } else {
 #pragma unroll
                     for (int j = 0; j < 16; ++j) f[j] = 0.f;
@@ -506,10 +550,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-// stage = 128 gathered rows + brows weight rows, KC bf16 each
-size_t stage_bytes(int brows, int kc) { return (size_t)(128 + brows) * 2 * kc; }
-size_t smem_bytes(int stages, int brows, int kc, int bn) {
-    const size_t ring = (size_t)stages * stage_bytes(brows, kc);
+// stage = 128 gathered rows + brows weight rows, 128 bytes each, per part
+// (3xTF32: a high and a low part)
+size_t stage_bytes(int brows, int parts) { return (size_t)(128 + brows) * 128 * parts; }
+size_t smem_bytes(int stages, int brows, int parts, int bn) {
+    const size_t ring = (size_t)stages * stage_bytes(brows, parts);
     const size_t epi = (size_t)128 * (bn + 4) * 4 + (size_t)kProdWarps * bn * 16;
     return 1024 /*align slack*/ + (ring > epi ? ring : epi) + ((kFullSplit + 1) * stages + 1) * 8 + 16;
 }
@@ -526,27 +571,38 @@ int tc_pick_bn(int cout) {
     return 16;
 }
 
-cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
-                           const __nv_bfloat16* in, int64_t n_in, int cin, int in_shift,
-                           const __nv_bfloat16* w, const float* bias, const void* residual,
-                           uint32_t res_dtype, int res_shift, void* out, uint32_t out_dtype,
-                           int64_t n_out, int cout, uint32_t flags, double* gn_partials,
-                           int gn_groups, char* error, uint64_t error_capacity, s3d_status* st) {
+// One launcher for both tensor-core modes: BF16 (in = bf16 rows) and 3xTF32
+// (in = high parts, in_lo = remainders, both f32; weights packed as a high
+// block followed by a low block).
+static cudaError_t launch_tc_impl(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol, const void* in, const float* in_lo,
+                           int cin, int in_shift, const void* w, const float* bias, const void* residual,
+                           uint32_t res_dtype, int res_shift, void* out, uint32_t out_dtype, int64_t n_out, int cout,
+                           uint32_t flags, double* gn_partials, int gn_groups, char* error, uint64_t error_capacity,
+                           s3d_status* st) {
     *st = S3D_OK;
+    const bool tf32 = in_lo != nullptr;
     const int cout_pad = (cout + 15) / 16 * 16;
-    const int cin_pad = (cin + 63) / 64 * 64;
-    const int bn = tc_pick_bn(cout);
+    const int cin_pad = tf32 ? (cin + 31) / 32 * 32 : (cin + 63) / 64 * 64;
+    int bn = tc_pick_bn(cout);
+    if (tf32 && bn > 128) {  // two-part stages: keep three of them in shared memory
+        bn = 16;
+        for (int c = 128; c >= 16; c -= 16)
+            if (cout_pad % c == 0) {
+                bn = c;
+                break;
+            }
+    }
     const int64_t tiles = (n_out + 127) / 128;
     // CTA pairs need an even row-tile count (the last pair may hold one empty tile)
-    const bool pair = (flags & S3DSP_CONV_CTA_PAIR) != 0;
+    const bool pair = !tf32 && (flags & S3DSP_CONV_CTA_PAIR) != 0;
     const int brows = pair ? bn / 2 : bn;
-    // 64-channel stages: 32-channel stages (twice as many for the same shared
-    // memory) measured slower on B200 (config-2 conv 119-123 us vs 81-85 us):
-    // a stage has a fixed cost beyond its bytes
-    const int kc = 64;
-    int stages = (int)((200 * 1024) / stage_bytes(brows, kc));
+    const int parts = tf32 ? 2 : 1;
+    // 128-byte row chunks per stage (64 bf16 / 32 f32): 64-byte bf16 stages
+    // (twice as many for the same shared memory) measured slower on B200
+    // (config-2 conv 119-123 us vs 81-85 us): a stage has a fixed cost beyond its bytes
+    const int kc = tf32 ? 32 : 64;
+    int stages = (int)((200 * 1024) / stage_bytes(brows, parts));
     if (stages > 16) stages = 16;
-    (void)n_in;
 
     auto encode = get_encode_fn();
     if (!encode) {
@@ -557,20 +613,25 @@ cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     const int nb = (brows % 32 == 0) ? 4 : (brows % 16 == 0) ? 2 : 1;
     CUtensorMap wmap;
     {
-        const cuuint64_t dims[2] = {(cuuint64_t)cin_pad, (cuuint64_t)kvol * (cuuint64_t)cout_pad};
-        const cuuint64_t strides[1] = {(cuuint64_t)cin_pad * 2};
+        const int es = tf32 ? 4 : 2;
+        const cuuint64_t dims[2] = {(cuuint64_t)cin_pad, (cuuint64_t)parts * kvol * (cuuint64_t)cout_pad};
+        const cuuint64_t strides[1] = {(cuuint64_t)cin_pad * es};
         const cuuint32_t box[2] = {(cuuint32_t)kc, (cuuint32_t)(brows / nb)};
         const cuuint32_t estr[2] = {1, 1};
-        CUresult cr = encode(&wmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)w, dims, strides, box, estr,
-                             CU_TENSOR_MAP_INTERLEAVE_NONE, kc == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
-                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        CUresult cr = encode(&wmap, tf32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                             const_cast<void*>(w), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (cr != CUDA_SUCCESS) {
             *st = fail(error, error_capacity, S3D_INTERNAL_ERROR, "weight tensor map failed (%d)", (int)cr);
             return cudaErrorInvalidValue;
         }
     }
     TcParams p;
-    p.in = in;
+    p.in = tf32 ? nullptr : static_cast<const __nv_bfloat16*>(in);
+    p.in_hi = tf32 ? static_cast<const float*>(in) : nullptr;
+    p.in_lo = in_lo;
+    p.lo_rows = kvol * cout_pad;
     p.cin = cin;
     p.in_shift = in_shift;
     p.nbr = kmap ? kmap->nbr : nullptr;
@@ -581,7 +642,9 @@ cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     p.nb = nb;
     p.stages = stages;
     const uint32_t mma_m = pair ? 256u : 128u;  // pair: M spans both CTAs' rows
-    p.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(bn >> 3) << 17) | ((mma_m >> 4) << 24);
+    // instruction descriptor: f32 accumulator; A, B = BF16 (1) or TF32 (2), both K-major
+    const uint32_t fmt = tf32 ? 2u : 1u;
+    p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(bn >> 3) << 17) | ((mma_m >> 4) << 24);
     p.bias = bias;
     p.residual = residual;
     p.res_dtype = res_dtype;
@@ -596,10 +659,11 @@ cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     p.gn_groups = gn_groups;
     p.status = ctx->d_status;
 
-    const size_t smem = smem_bytes(stages, brows, kc, bn);
-    static std::atomic<uint64_t> optin_pair{0}, optin_single{0};
-    cudaError_t e = pair ? smem_optin((const void*)conv_tc_kernel<true, 64>, ctx->device, optin_pair)
-                         : smem_optin((const void*)conv_tc_kernel<false, 64>, ctx->device, optin_single);
+    const size_t smem = smem_bytes(stages, brows, parts, bn);
+    static std::atomic<uint64_t> optin_pair{0}, optin_single{0}, optin_tf32{0};
+    cudaError_t e = tf32   ? smem_optin((const void*)conv_tc_kernel<false, 32, true>, ctx->device, optin_tf32)
+                    : pair ? smem_optin((const void*)conv_tc_kernel<true, 64>, ctx->device, optin_pair)
+                           : smem_optin((const void*)conv_tc_kernel<false, 64>, ctx->device, optin_single);
     if (e == cudaSuccess && smem > (size_t)kSmemOptIn) e = cudaErrorInvalidValue;
     if (e != cudaSuccess) return e;
     if (gn_partials) {
@@ -608,7 +672,10 @@ cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     }
     if (!pair) {
         const dim3 grid((unsigned)tiles, (unsigned)(cout_pad / bn));
-        conv_tc_kernel<false, 64><<<grid, kThreads, smem, ctx->stream>>>(p, wmap);
+        if (tf32)
+            conv_tc_kernel<false, 32, true><<<grid, kThreads, smem, ctx->stream>>>(p, wmap);
+        else
+            conv_tc_kernel<false, 64><<<grid, kThreads, smem, ctx->stream>>>(p, wmap);
         return cudaGetLastError();
     }
     cudaLaunchConfig_t cfg = {};
@@ -626,6 +693,26 @@ cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     e = cudaLaunchKernelEx(&cfg, conv_tc_kernel<true, 64>, p, wmap);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
+}
+
+cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
+                           const __nv_bfloat16* in, int64_t n_in, int cin, int in_shift,
+                           const __nv_bfloat16* w, const float* bias, const void* residual,
+                           uint32_t res_dtype, int res_shift, void* out, uint32_t out_dtype,
+                           int64_t n_out, int cout, uint32_t flags, double* gn_partials,
+                           int gn_groups, char* error, uint64_t error_capacity, s3d_status* st) {
+    (void)n_in;
+    return launch_tc_impl(ctx, kmap, kvol, in, nullptr, cin, in_shift, w, bias, residual, res_dtype, res_shift, out,
+                          out_dtype, n_out, cout, flags, gn_partials, gn_groups, error, error_capacity, st);
+}
+
+cudaError_t launch_conv_tf32x3(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol, const float* in_hi,
+                               const float* in_lo, int cin, int in_shift, const float* w, const float* bias,
+                               const void* residual, uint32_t res_dtype, int res_shift, void* out, uint32_t out_dtype,
+                               int64_t n_out, int cout, uint32_t flags, double* gn_partials, int gn_groups,
+                               char* error, uint64_t error_capacity, s3d_status* st) {
+    return launch_tc_impl(ctx, kmap, kvol, in_hi, in_lo, cin, in_shift, w, bias, residual, res_dtype, res_shift, out,
+                          out_dtype, n_out, cout, flags, gn_partials, gn_groups, error, error_capacity, st);
 }
 
 }  // namespace s3dsp

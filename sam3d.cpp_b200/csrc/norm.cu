@@ -218,6 +218,15 @@ __global__ void convert_f32_bf16_kernel(const float4* __restrict__ x, uint2* __r
 //   TRANSPOSED_2X2X2 (8, Cout, Cin) == MESH_PACKED with kvol 8
 // Destinations: F32_STRICT -> [kvol][cin_pad16][cout_pad64] f32 (zero padded)
 //               BF16       -> [kvol][cout_pad16][cin_pad64] bf16 (K-major)
+// x = hi + lo: hi = x rounded to TF32 (10 explicit mantissa bits, ties away
+// from zero), lo = x - hi exactly in f32 (zero for non-finite x)
+__device__ __forceinline__ void tf32_split(float x, float& hi, float& lo) {
+    uint32_t h;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
+    hi = __uint_as_float(h);
+    lo = isfinite(x) ? __fsub_rn(x, hi) : 0.0f;
+}
+
 __global__ void pack_kernel(const void* __restrict__ src, uint32_t sd, uint32_t layout, int kvol, int cin,
                             int cout, uint32_t prec, int cin_pad, int cout_pad, void* __restrict__ dst) {
     const int64_t total = (int64_t)kvol * cin_pad * cout_pad;
@@ -243,10 +252,27 @@ __global__ void pack_kernel(const void* __restrict__ src, uint32_t sd, uint32_t 
             }
             v = ld_f(src, sd, s);
         }
-        if (prec == S3DSP_PREC_F32_STRICT)
+        if (prec == S3DSP_PREC_F32_STRICT) {
             reinterpret_cast<float*>(dst)[i] = v;
-        else
+        } else if (prec == S3DSP_PREC_F32_3XTF32) {
+            // high block [kvol][cout_pad][cin_pad] then the low block of remainders
+            float hi, lo;
+            tf32_split(v, hi, lo);
+            reinterpret_cast<float*>(dst)[i] = hi;
+            reinterpret_cast<float*>(dst)[i + total] = lo;
+        } else {
             reinterpret_cast<__nv_bfloat16*>(dst)[i] = __float2bfloat16(v);
+        }
+    }
+}
+
+__global__ void split_tf32_kernel(const float* __restrict__ x, int64_t n, float* __restrict__ hi,
+                                  float* __restrict__ lo) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        float h, l;
+        tf32_split(__ldg(x + i), h, l);
+        hi[i] = h;
+        lo[i] = l;
     }
 }
 
@@ -364,6 +390,9 @@ void packed_dims(uint32_t prec, int64_t cin, int64_t cout, int64_t& cin_pad, int
     if (prec == S3DSP_PREC_F32_STRICT) {
         cin_pad = (cin + 15) / 16 * 16;
         cout_pad = (cout + 63) / 64 * 64;
+    } else if (prec == S3DSP_PREC_F32_3XTF32) {
+        cin_pad = (cin + 31) / 32 * 32;
+        cout_pad = (cout + 15) / 16 * 16;
     } else {
         cin_pad = (cin + 63) / 64 * 64;
         cout_pad = (cout + 15) / 16 * 16;
@@ -374,7 +403,7 @@ void packed_dims(uint32_t prec, int64_t cin, int64_t cout, int64_t& cin_pad, int
 extern "C" S3DSP_API int64_t s3dsp_weights_packed_bytes(uint32_t prec, int32_t kvol, int64_t cin, int64_t cout) {
     int64_t cp, op;
     packed_dims(prec, cin, cout, cp, op);
-    return (int64_t)kvol * cp * op * (prec == S3DSP_PREC_F32_STRICT ? 4 : 2);
+    return (int64_t)kvol * cp * op * (prec == S3DSP_PREC_F32_STRICT ? 4 : prec == S3DSP_PREC_F32_3XTF32 ? 8 : 2);
 }
 
 extern "C" S3DSP_API s3d_status s3dsp_weights_pack(s3dsp_context* ctx, const void* src, uint32_t sd, int32_t on_host,
@@ -383,7 +412,7 @@ extern "C" S3DSP_API s3d_status s3dsp_weights_pack(s3dsp_context* ctx, const voi
     clear_error(error, error_capacity);
     if (!ctx || !src || !dst) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
     if (!dtype_ok(sd)) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "bad source dtype");
-    if (prec != S3DSP_PREC_F32_STRICT && prec != S3DSP_PREC_BF16)
+    if (prec != S3DSP_PREC_F32_STRICT && prec != S3DSP_PREC_BF16 && prec != S3DSP_PREC_F32_3XTF32)
         return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "unknown precision %u", prec);
     if (layout > S3DSP_LAYOUT_TRANSPOSED_2X2X2) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "unknown layout");
     if (cin <= 0 || cout <= 0 || (kvol != 1 && kvol != 8 && kvol != 27))
@@ -418,3 +447,11 @@ extern "C" S3DSP_API s3d_status s3dsp_weights_pack(s3dsp_context* ctx, const voi
     if (on_host) S3DSP_CUDA(cudaStreamSynchronize(ctx->stream), "weight upload sync");
     return S3D_OK;
 }
+
+namespace s3dsp {
+cudaError_t split_tf32(s3dsp_context* ctx, const float* x, int64_t n, float* hi, float* lo) {
+    if (n <= 0) return cudaSuccess;
+    split_tf32_kernel<<<grid_for(n, 256, ctx->sm_count), 256, 0, ctx->stream>>>(x, n, hi, lo);
+    return cudaGetLastError();
+}
+}  // namespace s3dsp

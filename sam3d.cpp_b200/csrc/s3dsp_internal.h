@@ -125,6 +125,15 @@ cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
                            uint32_t res_dtype, int res_shift, void* out, uint32_t out_dtype,
                            int64_t n_out, int cout, uint32_t flags, double* gn_partials,
                            int gn_groups, char* error, uint64_t error_capacity, s3d_status* st);
+// 3xTF32 on the 128-row tensor-core kernel: in_hi / in_lo are the input split
+// by s3dsp::split_tf32, w a weight packed for S3DSP_PREC_F32_3XTF32
+cudaError_t launch_conv_tf32x3(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol, const float* in_hi,
+                               const float* in_lo, int cin, int in_shift, const float* w, const float* bias,
+                               const void* residual, uint32_t res_dtype, int res_shift, void* out, uint32_t out_dtype,
+                               int64_t n_out, int cout, uint32_t flags, double* gn_partials, int gn_groups,
+                               char* error, uint64_t error_capacity, s3d_status* st);
+// x -> (TF32 high part, f32 remainder), n elements, on ctx's stream
+cudaError_t split_tf32(s3dsp_context* ctx, const float* x, int64_t n, float* hi, float* lo);
 // rows: 128 or 256 output rows per stream-K work tile
 cudaError_t launch_conv_sk(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
                            const __nv_bfloat16* in, int64_t n_in, int cin, int in_shift,

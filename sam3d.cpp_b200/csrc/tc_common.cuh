@@ -114,6 +114,15 @@ __device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b
         "l"(a), "l"(b), "r"(idesc), "r"(acc)
         : "memory");
 }
+// D (f32, TMEM) += A * B with A, B read as TF32 (the top 19 bits of f32 words)
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                  : "memory");

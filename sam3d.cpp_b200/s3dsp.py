@@ -21,7 +21,7 @@ LIB_PATH = os.path.join(HERE, "libs3dsp.so")
 
 S3D_OK, S3D_INVALID_ARGUMENT, S3D_OUT_OF_MEMORY, S3D_INTERNAL_ERROR = 0, 1, 2, 3
 F32, BF16, F16 = 0, 1, 2
-PREC_F32_STRICT, PREC_BF16 = 0, 1
+PREC_F32_STRICT, PREC_BF16, PREC_F32_3XTF32 = 0, 1, 2
 LAYOUT_SLAT_ROW, LAYOUT_MESH_PACKED, LAYOUT_LINEAR, LAYOUT_SPCONV_1X1, LAYOUT_TRANSPOSED_2X2X2 = 0, 1, 2, 3, 4
 SENTINEL_SLAT_N, SENTINEL_MESH_NEG1 = 0, 1
 EPI_SILU, PRO_AFFINE_SILU, CONV_CTA_PAIR, CONV_TILE128, CONV_STREAM_K, CONV_STREAM_K128 = 1, 2, 4, 8, 16, 32
