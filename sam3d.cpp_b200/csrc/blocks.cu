@@ -59,16 +59,25 @@ extern "C" S3DSP_API s3d_status s3dsp_res_block_gn(s3dsp_context* ctx, const s3d
         return s3dsp_conv(ctx, kmap, 27, precision, y1, S3DSP_F32, n, c, 0, w2, b2, x, S3DSP_F32, 0, out, S3DSP_F32, n,
                           c, S3DSP_PRO_AFFINE_SILU, sub, mul, add, nullptr, 0, error, error_capacity);
     }
-    __nv_bfloat16 *xb, *hb;
-    S3DSP_CUDA(sc.get(&xb, 2 * (size_t)(n * c)), "scratch");
-    S3DSP_CUDA(sc.get(&hb, 2 * (size_t)(n * c)), "scratch");
-    S3DSP_TRY(s3dsp_convert(ctx, x, S3DSP_F32, xb, S3DSP_BF16, n * c, error, error_capacity));
-    S3DSP_TRY(s3dsp_conv(ctx, kmap, 27, precision, xb, S3DSP_BF16, n, c, 0, w1, b1, nullptr, 0, 0, y1, S3DSP_F32, n, c,
-                         0, nullptr, nullptr, nullptr, part, groups, error, error_capacity));
+    // tensor-core precisions read their activations materialised: bf16 for BF16,
+    // f32 for 3xTF32 (GN + SiLU applied by s3dsp_channel_affine, not a prologue)
+    const bool bf = precision == S3DSP_PREC_BF16;
+    const uint32_t adt = bf ? S3DSP_BF16 : S3DSP_F32;
+    const void* xin = x;
+    void* hb;
+    if (bf) {
+        __nv_bfloat16* xb;
+        S3DSP_CUDA(sc.get(&xb, 2 * (size_t)(n * c)), "scratch");
+        S3DSP_TRY(s3dsp_convert(ctx, x, S3DSP_F32, xb, S3DSP_BF16, n * c, error, error_capacity));
+        xin = xb;
+    }
+    S3DSP_CUDA(sc.get(&hb, dtype_size(adt) * (size_t)(n * c)), "scratch");
+    S3DSP_TRY(s3dsp_conv(ctx, kmap, 27, precision, xin, adt, n, c, 0, w1, b1, nullptr, 0, 0, y1, S3DSP_F32, n, c, 0,
+                         nullptr, nullptr, nullptr, part, groups, error, error_capacity));
     S3DSP_TRY(s3dsp_gn_finalize(ctx, part, n, c, groups, eps, gamma, beta, sub, mul, add, error, error_capacity));
-    S3DSP_TRY(s3dsp_channel_affine(ctx, y1, S3DSP_F32, n, c, sub, mul, add, 1, hb, S3DSP_BF16, error, error_capacity));
-    return s3dsp_conv(ctx, kmap, 27, precision, hb, S3DSP_BF16, n, c, 0, w2, b2, x, S3DSP_F32, 0, out, S3DSP_F32, n, c,
-                      0, nullptr, nullptr, nullptr, nullptr, 0, error, error_capacity);
+    S3DSP_TRY(s3dsp_channel_affine(ctx, y1, S3DSP_F32, n, c, sub, mul, add, 1, hb, adt, error, error_capacity));
+    return s3dsp_conv(ctx, kmap, 27, precision, hb, adt, n, c, 0, w2, b2, x, S3DSP_F32, 0, out, S3DSP_F32, n, c, 0,
+                      nullptr, nullptr, nullptr, nullptr, 0, error, error_capacity);
 }
 
 extern "C" S3DSP_API s3d_status s3dsp_mesh_upsample_level(
@@ -119,19 +128,28 @@ extern "C" S3DSP_API s3d_status s3dsp_mesh_upsample_level(
                           out, S3DSP_F32, nc, cout, S3DSP_PRO_AFFINE_SILU, sub2, mul2, add2, nullptr, 0, error,
                           error_capacity);
     }
-    __nv_bfloat16 *h1, *h2, *xb;
-    S3DSP_CUDA(sc.get(&h1, 2 * (size_t)(np * cin)), "scratch");
-    S3DSP_CUDA(sc.get(&xb, 2 * (size_t)(np * cin)), "scratch");
-    S3DSP_CUDA(sc.get(&h2, 2 * (size_t)(nc * cout)), "scratch");
-    S3DSP_TRY(s3dsp_channel_affine(ctx, x, S3DSP_F32, np, cin, sub1, mul1, add1, 1, h1, S3DSP_BF16, error, error_capacity));
-    S3DSP_TRY(s3dsp_conv(ctx, kmap, 27, precision, h1, S3DSP_BF16, np, cin, 3, conv1_w, conv1_b, nullptr, 0, 0, y1,
-                         S3DSP_F32, nc, cout, 0, nullptr, nullptr, nullptr, part, groups, error, error_capacity));
+    // tensor-core precisions: activations materialised as bf16 (BF16) or f32 (3xTF32)
+    const bool bf = precision == S3DSP_PREC_BF16;
+    const uint32_t adt = bf ? S3DSP_BF16 : S3DSP_F32;
+    const size_t asz = dtype_size(adt);
+    void *h1, *h2;
+    const void* xin = x;
+    S3DSP_CUDA(sc.get(&h1, asz * (size_t)(np * cin)), "scratch");
+    S3DSP_CUDA(sc.get(&h2, asz * (size_t)(nc * cout)), "scratch");
+    if (bf) {
+        __nv_bfloat16* xb;
+        S3DSP_CUDA(sc.get(&xb, 2 * (size_t)(np * cin)), "scratch");
+        S3DSP_TRY(s3dsp_convert(ctx, x, S3DSP_F32, xb, S3DSP_BF16, np * cin, error, error_capacity));
+        xin = xb;
+    }
+    S3DSP_TRY(s3dsp_channel_affine(ctx, x, S3DSP_F32, np, cin, sub1, mul1, add1, 1, h1, adt, error, error_capacity));
+    S3DSP_TRY(s3dsp_conv(ctx, kmap, 27, precision, h1, adt, np, cin, 3, conv1_w, conv1_b, nullptr, 0, 0, y1, S3DSP_F32,
+                         nc, cout, 0, nullptr, nullptr, nullptr, part, groups, error, error_capacity));
     S3DSP_TRY(s3dsp_gn_finalize(ctx, part, nc, cout, groups, eps, gn2_w, gn2_b, sub2, mul2, add2, error, error_capacity));
-    S3DSP_TRY(s3dsp_channel_affine(ctx, y1, S3DSP_F32, nc, cout, sub2, mul2, add2, 1, h2, S3DSP_BF16, error, error_capacity));
-    S3DSP_TRY(s3dsp_convert(ctx, x, S3DSP_F32, xb, S3DSP_BF16, np * cin, error, error_capacity));
-    S3DSP_TRY(s3dsp_conv(ctx, nullptr, 1, precision, xb, S3DSP_BF16, np, cin, 0, skip_w, skip_b, nullptr, 0, 0, skip,
+    S3DSP_TRY(s3dsp_channel_affine(ctx, y1, S3DSP_F32, nc, cout, sub2, mul2, add2, 1, h2, adt, error, error_capacity));
+    S3DSP_TRY(s3dsp_conv(ctx, nullptr, 1, precision, xin, adt, np, cin, 0, skip_w, skip_b, nullptr, 0, 0, skip,
                          S3DSP_F32, np, cout, 0, nullptr, nullptr, nullptr, nullptr, 0, error, error_capacity));
-    return s3dsp_conv(ctx, kmap, 27, precision, h2, S3DSP_BF16, nc, cout, 0, conv2_w, conv2_b, skip, S3DSP_F32, 3, out,
+    return s3dsp_conv(ctx, kmap, 27, precision, h2, adt, nc, cout, 0, conv2_w, conv2_b, skip, S3DSP_F32, 3, out,
                       S3DSP_F32, nc, cout, 0, nullptr, nullptr, nullptr, nullptr, 0, error, error_capacity);
 }
 

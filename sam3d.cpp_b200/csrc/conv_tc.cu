@@ -57,6 +57,7 @@ struct TcParams {
     const float* in_hi;         // 3xTF32: input split into TF32 high parts ...
     const float* in_lo;         // ... and the f32 remainders, [n_in, cin] each
     int lo_rows;                // 3xTF32: row of the low weight block in the weight tensor map
+    int tf_groups;              // 3xTF32: groups of four TMEM accumulators (1, or 2 alternating by stage)
     int cin;
     int in_shift;
     const int32_t* nbr;         // [kvol][n_out] or null (identity)
@@ -218,11 +219,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // KC-channel reduction chunks per offset
     const int kchunks = kTF32 ? (p.cin + KC - 1) / KC : (p.cin + 63) / 64 * (64 / KC);
     const int T = __popc(mask) * kchunks;
-    // 3xTF32 keeps kTfAcc accumulators (one per K step of a stage, summed in the
-    // epilogue): the tensor core's f32 accumulation truncates, and a quarter of
-    // the reduction per accumulator keeps the error inside the F32 gate
-    constexpr int kTfAcc = kTF32 ? kRowB / 32 : 1;
-    const int tneed = kTfAcc * p.bn;
+    // 3xTF32 keeps one TMEM accumulator per K step of a stage (and, for tiles of
+    // at most 64 columns, a second group used by every other stage), summed in
+    // f32 in the epilogue: the tensor core's f32 accumulation truncates, and a
+    // fraction of the reduction per accumulator keeps the error inside the F32 gate
+    constexpr int kTfStep = kTF32 ? kRowB / 32 : 1;  // accumulators per group: one per K step
+    const int tf_groups = kTF32 ? p.tf_groups : 1;
+    const int tneed = kTfStep * tf_groups * p.bn;
     const uint32_t tcols = tneed <= 32 ? 32u : (tneed <= 64 ? 64u : (tneed <= 128 ? 128u : (tneed <= 256 ? 256u : 512u)));
 
     // ---- setup: barriers, TMEM ----
@@ -396,8 +399,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                             // accumulator of K step k
                             const uint64_t ah = kmajor_desc<KCB>(a0 + 32 * k), al = kmajor_desc<KCB>(a0 + kAHalf + 32 * k);
                             const uint64_t bh = kmajor_desc<KCB>(b0 + 32 * k), bl = kmajor_desc<KCB>(b0 + bhalf + 32 * k);
-                            const uint32_t dk = tmem + (uint32_t)(k * p.bn);
-                            mma_tf32(dk, al, bh, p.idesc, it > 0 ? 1u : 0u);
+                            const int grp = tf_groups > 1 ? (it & 1) : 0;
+                            const uint32_t dk = tmem + (uint32_t)((grp * kTfStep + k) * p.bn);
+                            mma_tf32(dk, al, bh, p.idesc, it >= tf_groups ? 1u : 0u);
                             mma_tf32(dk, ah, bl, p.idesc, 1u);
                             mma_tf32(dk, ah, bh, p.idesc, 1u);
                         } else {
@@ -434,8 +438,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float f[16];
                 if (have_acc) {
                     tmem_ld16(taddr + (uint32_t)c0, f);
-                    // 3xTF32: the other accumulators, summed in order in f32
-                    for (int a = 1; a < kTfAcc; ++a) {
+                    // 3xTF32: the other accumulators that were written, summed in order in f32
+                    const int n_acc = kTfStep * (T < tf_groups ? T : tf_groups);
+                    for (int a = 1; a < n_acc; ++a) {
                         float g[16];
                         tmem_ld16(taddr + (uint32_t)(a * p.bn + c0), g);
 #pragma unroll
@@ -584,9 +589,14 @@ static cudaError_t launch_tc_impl(s3dsp_context* ctx, const s3dsp_kmap* kmap, in
     const int cout_pad = (cout + 15) / 16 * 16;
     const int cin_pad = tf32 ? (cin + 31) / 32 * 32 : (cin + 63) / 64 * 64;
     int bn = tc_pick_bn(cout);
-    if (tf32 && bn > 128) {  // two-part stages: keep three of them in shared memory
+    // 3xTF32: two-part stages (at most 128 columns keeps three stages), and
+    // TMEM for 4 accumulators per group; long reductions take 64-column tiles
+    // so that 8 accumulators fit (the tensor core's f32 accumulation truncates)
+    const int64_t kred = (int64_t)cin * kvol;
+    const int tf_cap = kred > 4096 ? 64 : 128;
+    if (tf32 && bn > tf_cap) {
         bn = 16;
-        for (int c = 128; c >= 16; c -= 16)
+        for (int c = tf_cap; c >= 16; c -= 16)
             if (cout_pad % c == 0) {
                 bn = c;
                 break;
@@ -632,6 +642,7 @@ static cudaError_t launch_tc_impl(s3dsp_context* ctx, const s3dsp_kmap* kmap, in
     p.in_hi = tf32 ? static_cast<const float*>(in) : nullptr;
     p.in_lo = in_lo;
     p.lo_rows = kvol * cout_pad;
+    p.tf_groups = tf32 && bn <= 64 ? 2 : 1;
     p.cin = cin;
     p.in_shift = in_shift;
     p.nbr = kmap ? kmap->nbr : nullptr;

@@ -13,7 +13,7 @@ import workloads
 pytestmark = pytest.mark.gpu
 
 F32_TOL, BF16_TOL = 1e-5, 1e-2
-PRECS = [(s3dsp.PREC_F32_STRICT, F32_TOL), (s3dsp.PREC_BF16, BF16_TOL)]
+PRECS = [(s3dsp.PREC_F32_STRICT, F32_TOL), (s3dsp.PREC_F32_3XTF32, F32_TOL), (s3dsp.PREC_BF16, BF16_TOL)]
 
 
 def rel_l2(a, e):

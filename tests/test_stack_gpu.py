@@ -45,7 +45,7 @@ def case():
     return coords, latent, p, cur, ref
 
 
-@pytest.mark.parametrize("prec,tol", [(s3dsp.PREC_F32_STRICT, 1e-5), (s3dsp.PREC_BF16, 1e-2)])
+@pytest.mark.parametrize("prec,tol", [(s3dsp.PREC_F32_STRICT, 1e-5), (s3dsp.PREC_F32_3XTF32, 1e-5), (s3dsp.PREC_BF16, 1e-2)])
 def test_config4_end_to_end(ctx, case, prec, tol):
     coords, latent, p, ref_coords, ref = case
     st = stack.Config4Stack(s3dsp, ctx, p, prec, torch.device("cuda"))
