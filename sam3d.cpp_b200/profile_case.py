@@ -4,6 +4,7 @@
   python sam3d.cpp_b200/profile_case.py conv_sk    # 256^3 shell (241,978 voxels), C=256, stream-K kernel
   python sam3d.cpp_b200/profile_case.py tables     # hash + submanifold kmap of the 2.58M-voxel 512^3 shell
   python sam3d.cpp_b200/profile_case.py flexicubes # FlexiCubes extraction of 970,176 cubes at 256^3
+  python sam3d.cpp_b200/profile_case.py conv1_tf32 # config-1 subm conv (C=64, 15,159 voxels) in 3xTF32
   python sam3d.cpp_b200/profile_case.py coords     # SS occupancy -> coords -> surface prune -> downsample (64^3 fixture)
   python sam3d.cpp_b200/profile_case.py gs_tables  # GS window tables (both shifts) + APE, config-2 coordinates
 
@@ -26,7 +27,7 @@ sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["conv2", "conv_sk", "tables", "flexicubes", "coords", "gs_tables"])
+    ap.add_argument("case", choices=["conv2", "conv_sk", "tables", "flexicubes", "coords", "gs_tables", "conv1_tf32"])
     ap.add_argument("--reps", type=int, default=3)
     a = ap.parse_args()
     import torch
@@ -48,6 +49,18 @@ def main():
         flags = s3dsp.CONV_TILE128 if a.case == "conv2" else s3dsp.CONV_STREAM_K
         for _ in range(1 + a.reps):
             ctx.conv(k, 27, P, x, w, b, out, c, flags=flags)
+    elif a.case == "conv1_tf32":
+        cfg = workloads.config1(0)
+        coords, n, c = cfg["coords"], len(cfg["coords"]), 64
+        k = ctx.kmap_subm3(ctx.hash_build(torch.from_numpy(coords).cuda()))
+        P3 = s3dsp.PREC_F32_3XTF32
+        w = torch.empty(s3dsp.Context.packed_bytes(P3, 27, c, c), dtype=torch.uint8, device="cuda")
+        ctx.weights_pack(torch.from_numpy(cfg["weight"]), s3dsp.LAYOUT_SLAT_ROW, 27, c, c, P3, w)
+        x = torch.from_numpy(cfg["feats"]).cuda()
+        b = torch.from_numpy(cfg["bias"]).cuda()
+        out = torch.empty((n, c), device="cuda")
+        for _ in range(1 + a.reps):
+            ctx.conv(k, 27, P3, x, w, b, out, c)
     elif a.case == "coords":
         root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
         bits = np.load(os.path.join(root, "tests", "golden", "ss_occ_mask.npz"))["bits"]
