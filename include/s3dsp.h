@@ -49,6 +49,7 @@ typedef struct s3dsp_slat_tables s3dsp_slat_tables;
 typedef struct s3dsp_fc_tables s3dsp_fc_tables;
 typedef struct s3dsp_mesh s3dsp_mesh;
 typedef struct s3dsp_gguf s3dsp_gguf;
+typedef struct s3dsp_shard s3dsp_shard;
 
 /* element types */
 #define S3DSP_F32 UINT32_C(0)
@@ -178,6 +179,43 @@ S3DSP_API s3d_status s3dsp_gs_window_tables(s3dsp_context *ctx, const int32_t *d
  * then channels/6 cosines of coordinate * 10000^(-i/(channels/6)). */
 S3DSP_API s3d_status s3dsp_ape(s3dsp_context *ctx, const int32_t *d_coords, int64_t n, int32_t channels,
                                float *d_out, char *error, uint64_t error_capacity);
+
+/* ---------------------------------------------------------------------------
+ * One volume over several GPUs (one process per GPU; no reference
+ * counterpart: the reference runs one object on one device). Morton-ordered
+ * slabs of (nearly) equal voxel count; each rank's own rows interior first
+ * (no 26-neighbour on another rank), then boundary; ghost rows = other ranks'
+ * voxels adjacent to the rank, grouped by owner, Morton order within; send
+ * lists in the matching order. The plan is computed on the host from the
+ * global coordinate list, identically on every rank, without communication.
+ * ------------------------------------------------------------------------- */
+S3DSP_API s3d_status s3dsp_shard_plan_morton(const int32_t *h_coords, int64_t n, int32_t world,
+                                             int32_t rank, s3dsp_shard **out, char *error,
+                                             uint64_t error_capacity);
+S3DSP_API s3d_status s3dsp_shard_info(const s3dsp_shard *plan, int64_t *n_own, int64_t *n_interior,
+                                      int64_t *n_ghost, int64_t *n_send);
+/* host copies: own / ghost global row ids, per-peer recv / send counts
+ * [world], send rows (indices into the own rows, grouped by destination);
+ * any pointer may be NULL */
+S3DSP_API s3d_status s3dsp_shard_lists(const s3dsp_shard *plan, int64_t *h_own, int64_t *h_ghost,
+                                       int64_t *h_recv_counts, int64_t *h_send_counts,
+                                       int64_t *h_send_rows);
+S3DSP_API void s3dsp_shard_free(s3dsp_context *ctx, s3dsp_shard *plan);
+/* NCCL is bound at run time (an already loaded libnccl.so.2, else the
+ * system one); communicators passed to s3dsp_halo_exchange must come from
+ * that NCCL, e.g. from s3dsp_nccl_comm_create with an id (128 bytes) made by
+ * one rank with s3dsp_nccl_unique_id and shared by the host. */
+S3DSP_API s3d_status s3dsp_nccl_unique_id(uint8_t *id, char *error, uint64_t error_capacity);
+S3DSP_API s3d_status s3dsp_nccl_comm_create(s3dsp_context *ctx, int32_t world, int32_t rank,
+                                            const uint8_t *id, void **comm, char *error,
+                                            uint64_t error_capacity);
+S3DSP_API void s3dsp_nccl_comm_free(void *comm);
+/* Fills the ghost rows [n_own, n_own + n_ghost) of d_x ([n_own + n_ghost, c]
+ * of dtype, device) with the peers' rows: the send rows are gathered, then
+ * one NCCL group of send / recv per peer on the context's stream. */
+S3DSP_API s3d_status s3dsp_halo_exchange(s3dsp_context *ctx, s3dsp_shard *plan, void *comm, void *d_x,
+                                         int64_t c, uint32_t dtype, char *error,
+                                         uint64_t error_capacity);
 
 /* ---------------------------------------------------------------------------
  * On-disk formats. GGUF weight files (GGUFModel::load / get / u32 / i32 / f32

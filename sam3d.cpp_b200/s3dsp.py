@@ -37,7 +37,9 @@ EXPORTED = [
     "s3dsp_mesh_free", "s3dsp_gguf_open", "s3dsp_gguf_close", "s3dsp_gguf_n_tensors", "s3dsp_gguf_find",
     "s3dsp_gguf_tensor_info", "s3dsp_gguf_u32", "s3dsp_gguf_i32", "s3dsp_gguf_f32", "s3dsp_gguf_str",
     "s3dsp_gguf_array_len", "s3dsp_gguf_str_array", "s3dsp_gguf_i32_array", "s3dsp_gguf_read", "s3dsp_gguf_load",
-    "s3dsp_gguf_load_weights", "s3dsp_dequantize", "s3dsp_samt_info", "s3dsp_samt_read", "s3dsp_samt_write", "s3dsp_occupancy_coords", "s3dsp_prune_surface", "s3dsp_downsample_coords",
+    "s3dsp_gguf_load_weights", "s3dsp_dequantize", "s3dsp_samt_info", "s3dsp_samt_read", "s3dsp_samt_write",
+    "s3dsp_shard_plan_morton", "s3dsp_shard_info", "s3dsp_shard_lists", "s3dsp_shard_free", "s3dsp_nccl_unique_id",
+    "s3dsp_nccl_comm_create", "s3dsp_nccl_comm_free", "s3dsp_halo_exchange", "s3dsp_occupancy_coords", "s3dsp_prune_surface", "s3dsp_downsample_coords",
     "s3dsp_kmap_build_subm3", "s3dsp_kmap_build_subm3_rows", "s3dsp_kmap_build_subm3_range", "s3dsp_subdivide", "s3dsp_kmap_free",
     "s3dsp_kmap_rows", "s3dsp_kmap_export_dense", "s3dsp_kmap_pairs", "s3dsp_kmap_pairs_noalloc",
     "s3dsp_weights_packed_bytes", "s3dsp_weights_pack", "s3dsp_gn_partials_count", "s3dsp_conv", "s3dsp_conv_kernel",
@@ -115,6 +117,14 @@ def load(path: str = LIB_PATH):
                                    ctypes.POINTER(_u64), _cp, _u64]),
         "s3dsp_samt_read": (_u32, [ctypes.c_char_p, _vp, _u64, _cp, _u64]),
         "s3dsp_samt_write": (_u32, [ctypes.c_char_p, _i32, _vp, _i32, _vp, _u64, _cp, _u64]),
+        "s3dsp_shard_plan_morton": (_u32, [_vp, _i64, _i32, _i32, ctypes.POINTER(_vp), _cp, _u64]),
+        "s3dsp_shard_info": (_u32, [_vp] + [ctypes.POINTER(_i64)] * 4),
+        "s3dsp_shard_lists": (_u32, [_vp] + [_vp] * 5),
+        "s3dsp_shard_free": (None, [_vp, _vp]),
+        "s3dsp_nccl_unique_id": (_u32, [_vp, _cp, _u64]),
+        "s3dsp_nccl_comm_create": (_u32, [_vp, _i32, _i32, _vp, ctypes.POINTER(_vp), _cp, _u64]),
+        "s3dsp_nccl_comm_free": (None, [_vp]),
+        "s3dsp_halo_exchange": (_u32, [_vp, _vp, _vp, _vp, _i64, _u32, _cp, _u64]),
         "s3dsp_occupancy_coords": (_u32, [_vp, _vp, _i32, _i32, _i32, _i32, _vp, _i64, ctypes.POINTER(_i64), _cp,
                                           _u64]),
         "s3dsp_prune_surface": (_u32, [_vp, _vp, _i64, _i32, _vp, _i64, ctypes.POINTER(_i64), _cp, _u64]),
@@ -400,6 +410,45 @@ class Gguf:
         return dst
 
 
+class ShardPlan:
+    """s3dsp_shard_plan_morton: the Morton-slab plan of one rank, with its
+    lists as numpy arrays (own, ghost, recv_counts, send_counts, send_rows)."""
+
+    def __init__(self, coords, world: int, rank: int):
+        import numpy as np
+        c = np.ascontiguousarray(coords, dtype=np.int32).reshape(-1, 4)
+        h = _vp()
+        _call(load().s3dsp_shard_plan_morton, c.ctypes.data, c.shape[0], world, rank, ctypes.byref(h))
+        self.handle, self.world, self.rank = h.value, world, rank
+        no, ni, ng, ns = (_i64() for _ in range(4))
+        load().s3dsp_shard_info(self.handle, ctypes.byref(no), ctypes.byref(ni), ctypes.byref(ng), ctypes.byref(ns))
+        self.n_own, self.n_interior, self.n_ghost = no.value, ni.value, ng.value
+        self.own = np.zeros(no.value, np.int64)
+        self.ghost = np.zeros(ng.value, np.int64)
+        self.recv_counts = np.zeros(world, np.int64)
+        self.send_counts = np.zeros(world, np.int64)
+        self.send_rows = np.zeros(ns.value, np.int64)
+        load().s3dsp_shard_lists(self.handle, *(a.ctypes.data for a in (self.own, self.ghost, self.recv_counts,
+                                                                         self.send_counts, self.send_rows)))
+
+    def free(self, ctx: "Context | None" = None):
+        if getattr(self, "handle", None):
+            load().s3dsp_shard_free(ctx.handle if ctx else None, self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def nccl_unique_id() -> bytes:
+    buf = ctypes.create_string_buffer(128)
+    _call(load().s3dsp_nccl_unique_id, ctypes.cast(buf, ctypes.c_void_p))
+    return buf.raw
+
+
 def samt_info(path: str) -> dict:
     nd, t, nb = _i32(), _i32(), _u64()
     ne = (_i64 * 8)()
@@ -485,6 +534,18 @@ class Context:
 
     def ape(self, coords, out):
         _call(load().s3dsp_ape, self.handle, ptr(coords), coords.shape[0], out.shape[1], ptr(out))
+
+    # ---- several GPUs --------------------------------------------------------
+    def nccl_comm(self, world: int, rank: int, uid: bytes) -> int:
+        c = _vp()
+        buf = ctypes.create_string_buffer(uid, 128)
+        _call(load().s3dsp_nccl_comm_create, self.handle, world, rank, ctypes.cast(buf, ctypes.c_void_p),
+              ctypes.byref(c))
+        return c.value
+
+    def halo_exchange(self, plan: ShardPlan, comm: int, x):
+        """Fill x's ghost rows [n_own, n_own + n_ghost) from the peers (x on this device)."""
+        _call(load().s3dsp_halo_exchange, self.handle, plan.handle, comm, ptr(x), x.shape[1], dtype_code(x))
 
     # ---- FlexiCubes extraction ---------------------------------------------
     def flexicubes_tables(self, dmc, num_dual, check) -> FlexiCubesTables:
