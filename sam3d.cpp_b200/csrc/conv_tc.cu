@@ -1,5 +1,6 @@
-// K3 (BF16) implicit-gather sparse convolution on the 5th-generation tensor
-// cores: tcgen05.mma with the f32 accumulator in TMEM.
+// K3 implicit-gather sparse convolution on the 5th-generation tensor cores:
+// tcgen05.mma with the f32 accumulator in TMEM; BF16 operands, or f32
+// operands as 3xTF32 (kTF32, described at the end of this comment).
 //
 // Tile: 128 output rows x BN output channels per CTA (BN = a multiple of 16,
 // <= 256). The reduction walks (active offset, 64-channel chunk) steps. Per
@@ -8,6 +9,8 @@
 //      512 producer threads (8 threads per row, 16 B each, zero-filled for a
 //      missing neighbour); each thread's copies complete onto the stage's
 //      mbarrier (cp.async.mbarrier.arrive.noinc), so producers run ahead;
+//      a thread reads the kernel-map entries of its own rows itself, one
+//      kernel offset ahead of the gathers that use them (no setup pass);
 //   B: the BN x 64 weight tile W[o][n0:n0+BN][k0:k0+64] as NB TMA tile loads
 //      of BN/NB rows, issued by NB different warps: one thread's TMA ops are
 //      serialised (a few hundred cycles each), separate issuers overlap.
@@ -29,6 +32,15 @@
 // Every mbarrier wait is bounded (about two seconds of %globaltimer); on
 // timeout the CTA records kErrPipelineTimeout, stops issuing work and exits
 // through the common teardown, which frees its TMEM.
+//
+// 3xTF32 (kTF32): f32 operands split into a TF32 high part and its f32
+// remainder (input split once per conv, weights at pack time). A 32-channel
+// f32 row chunk is the same 128 bytes as a 64-channel bf16 one, so the layout,
+// descriptors and TMA boxes are the bf16 ones; a stage holds a high and a low
+// half of each operand, and each K step issues lo*hi, hi*lo, hi*hi
+// (kind::tf32). The tensor core's f32 accumulation truncates, so each K step
+// of a stage has its own TMEM accumulator (two alternating groups for tiles of
+// at most 64 columns), summed in f32 by the epilogue.
 //
 // Replaces the GGML get_rows + mul_mat chains of slat_flow_graph.cpp:112-155
 // (SLat conv) and mesh_decoder_graph.cpp:81-103 (mesh conv, per-offset form)
@@ -476,7 +488,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int lane_base = 8 * warp;
         const int nrows = (int)max((int64_t)0, min((int64_t)8, p.n_out - (m0 + lane_base)));
         const uint32_t so_base = smem_u32(stage_out);
-        // [16][bn][2]: may run past the rings into the gather indices, unused by now
+        // [16][bn][2]: may run past the rings (region0 is sized for it)
         double* colp = reinterpret_cast<double*>(smem + (size_t)128 * ostride * 4);
         double* colw = colp + (size_t)warp * p.bn * 2;
         // One compact loop body per (out dtype, residual dtype, SiLU, stats)
