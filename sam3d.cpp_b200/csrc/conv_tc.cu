@@ -91,6 +91,7 @@ struct TcParams {
     int cout;
     uint32_t flags;
     double* gn_partials;
+    int gn_store;  // one column tile covers every channel: each slot has one writer
     int gn_groups;
     uint32_t* status;
 };
@@ -547,10 +548,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                         a += colp[((size_t)w * p.bn + c) * 2 + 0];
                         b += colp[((size_t)w * p.bn + c) * 2 + 1];
                     }
-                // a group split across two column tiles gets exactly two adds
-                // onto a zeroed slot, which is order independent
-                atomicAdd(p.gn_partials + ((int64_t)tile * p.gn_groups + g) * 2 + 0, a);
-                atomicAdd(p.gn_partials + ((int64_t)tile * p.gn_groups + g) * 2 + 1, b);
+                double* slot = p.gn_partials + ((int64_t)tile * p.gn_groups + g) * 2;
+                if (p.gn_store) {
+                    slot[0] = a;
+                    slot[1] = b;
+                } else {
+                    // a group split across two column tiles gets exactly two
+                    // adds onto a zeroed slot, which is order independent
+                    atomicAdd(slot + 0, a);
+                    atomicAdd(slot + 1, b);
+                }
             }
         }
         tc_fence_before();
@@ -680,6 +687,7 @@ static cudaError_t launch_tc_impl(s3dsp_context* ctx, const s3dsp_kmap* kmap, in
     p.flags = flags;
     p.gn_partials = gn_partials;
     p.gn_groups = gn_groups;
+    p.gn_store = cout_pad == bn;
     p.status = ctx->d_status;
 
     const size_t smem = smem_bytes(stages, brows, parts, bn);
@@ -689,7 +697,7 @@ static cudaError_t launch_tc_impl(s3dsp_context* ctx, const s3dsp_kmap* kmap, in
                            : smem_optin((const void*)conv_tc_kernel<false, 64>, ctx->device, optin_single);
     if (e == cudaSuccess && smem > (size_t)kSmemOptIn) e = cudaErrorInvalidValue;
     if (e != cudaSuccess) return e;
-    if (gn_partials) {
+    if (gn_partials && !p.gn_store) {
         e = cudaMemsetAsync(gn_partials, 0, sizeof(double) * 2 * (size_t)gn_groups * (size_t)tiles, ctx->stream);
         if (e != cudaSuccess) return e;
     }

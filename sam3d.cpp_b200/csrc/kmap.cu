@@ -81,14 +81,17 @@ __global__ void hash_lookup_kernel(const int4* __restrict__ q, int64_t m, HashVi
     }
 }
 
-// Submanifold 3x3x3 map, offset-major: one thread per (output row, offset),
-// block (tile, offset) = 128 rows of one offset, so the nbr stores are
-// coalesced and the block sets its tile's offset bit with one atomicOr. A
-// duplicate row (not the first holding its key) gets no neighbours, as
-// SlatTables::build iterates the unique map entries (sparse_ops.cpp:
-// 129-139). The first row comes from the hash's self-row array when the
-// table is larger than L2 can serve (one probe per row, done once), else
-// from a second probe issued next to the neighbour probe (no extra pass).
+// Submanifold 3x3x3 map, offset-major. One block per 128-row tile; thread
+// (slab s, row r), s = threadIdx.x / 128, owns the nine offsets with
+// dx = s - 1 (o = 9 s .. 9 s + 8, o = kd * 9 + kh * 3 + kw as in
+// sparse_ops.cpp:132) of row r. Its nine probes are issued back to back, a
+// warp's stores nbr[o * n + r] are coalesced, and the block writes its
+// tile's 27-bit offset mask with one plain store (no zeroing pass, no global
+// atomics). A duplicate row (not the first holding its key) gets no
+// neighbours, as SlatTables::build iterates the unique map entries
+// (sparse_ops.cpp:129-139). The first row comes from the hash's self-row
+// array when the table is larger than L2 can serve (one probe per row, done
+// once), else from a probe of the row's own key.
 __device__ __forceinline__ int32_t probe_rest(const HashView& h, unsigned long long key, unsigned long long slot) {
     for (unsigned long long p = 1; p <= h.mask; ++p) {
         slot = (slot + 1) & h.mask;
@@ -99,44 +102,61 @@ __device__ __forceinline__ int32_t probe_rest(const HashView& h, unsigned long l
     return -1;
 }
 
+constexpr int kSlabs = 3;  // dx = -1, 0, +1
+
 // Output row r is hash row row0 + r (r < n).
-__global__ void __launch_bounds__(kTileRows) kmap_subm3_kernel(const int4* __restrict__ coords, int64_t row0, int64_t n,
-                                                               HashView h, const int32_t* __restrict__ self_row,
-                                                               int32_t* __restrict__ nbr,
-                                                               uint32_t* __restrict__ tile_mask) {
-    const int o = blockIdx.y;
-    const int dx = o / 9 - 1, dy = (o / 3) % 3 - 1, dz = o % 3 - 1;
-    const int64_t r = (int64_t)blockIdx.x * kTileRows + threadIdx.x;
-    int32_t res = -1;
+__global__ void __launch_bounds__(kTileRows * kSlabs) kmap_subm3_kernel(const int4* __restrict__ coords, int64_t row0,
+                                                                        int64_t n, HashView h,
+                                                                        const int32_t* __restrict__ self_row,
+                                                                        int32_t* __restrict__ nbr,
+                                                                        uint32_t* __restrict__ tile_mask) {
+    const int s = threadIdx.x / kTileRows;
+    const int dx = s - 1;
+    const int64_t r = (int64_t)blockIdx.x * kTileRows + threadIdx.x % kTileRows;
+    __shared__ uint32_t block_bits;
+    if (threadIdx.x == 0) block_bits = 0;
+    __syncthreads();
+    uint32_t bits = 0;
     if (r < n) {
         const int64_t hr = row0 + r;  // the row in the hash
         const int4 c = __ldg(coords + hr);
-        unsigned long long kn, ks;
-        const bool okn = pack_key(c.x, c.y + dx, c.z + dy, c.w + dz, kn);
-        const unsigned long long sn = okn ? (mix64(kn) & h.mask) : 0;
-        const ulonglong2 qn = okn ? __ldg(h.slots + sn) : make_ulonglong2(kEmptyKey, 0);
         int32_t self = -1;
         if (self_row) {
             self = __ldg(self_row + hr);
         } else {
-            const bool oks = pack_key(c.x, c.y, c.z, c.w, ks);
-            const unsigned long long ss = oks ? (mix64(ks) & h.mask) : 0;
-            const ulonglong2 qs = oks ? __ldg(h.slots + ss) : make_ulonglong2(kEmptyKey, 0);
-            if (qs.x == ks && oks) self = (int32_t)(uint32_t)qs.y;
-            else if (oks && qs.x != kEmptyKey) self = probe_rest(h, ks, ss);
+            unsigned long long ks;
+            if (pack_key(c.x, c.y, c.z, c.w, ks)) {
+                const unsigned long long ss = mix64(ks) & h.mask;
+                const ulonglong2 qs = __ldg(h.slots + ss);
+                if (qs.x == ks) self = (int32_t)(uint32_t)qs.y;
+                else if (qs.x != kEmptyKey) self = probe_rest(h, ks, ss);
+            }
         }
-        if (self == (int32_t)hr && okn) {
-            if (qn.x == kn) res = (int32_t)(uint32_t)qn.y;
-            else if (qn.x != kEmptyKey) res = probe_rest(h, kn, sn);
+        const bool first = self == (int32_t)hr;
+        unsigned long long key[9], slot[9];
+        ulonglong2 q[9];
+        bool ok[9];
+#pragma unroll
+        for (int j = 0; j < 9; ++j) {
+            ok[j] = first && pack_key(c.x, c.y + dx, c.z + j / 3 - 1, c.w + j % 3 - 1, key[j]);
+            slot[j] = ok[j] ? (mix64(key[j]) & h.mask) : 0;
+            q[j] = ok[j] ? __ldg(h.slots + slot[j]) : make_ulonglong2(kEmptyKey, 0);
         }
-        nbr[o * n + r] = res;
+#pragma unroll
+        for (int j = 0; j < 9; ++j) {
+            int32_t res = -1;
+            if (ok[j]) {
+                if (q[j].x == key[j]) res = (int32_t)(uint32_t)q[j].y;
+                else if (q[j].x != kEmptyKey) res = probe_rest(h, key[j], slot[j]);
+            }
+            nbr[(int64_t)(9 * s + j) * n + r] = res;
+            if (res >= 0) bits |= 1u << (9 * s + j);
+        }
     }
-    __shared__ int any;
-    if (threadIdx.x == 0) any = 0;
+    bits = __reduce_or_sync(0xffffffffu, bits);
+    if ((threadIdx.x & 31) == 0 && bits) atomicOr(&block_bits, bits);
     __syncthreads();
-    if (__ballot_sync(0xffffffffu, res >= 0) && (threadIdx.x & 31) == 0) any = 1;
-    __syncthreads();
-    if (threadIdx.x == 0 && any) atomicOr(tile_mask + blockIdx.x, 1u << o);
+    if (threadIdx.x == 0) tile_mask[blockIdx.x] = block_bits;
 }
 
 // Child geometry of MeshSubdivideTables (sparse_ops.cpp:346-365): for child
@@ -340,7 +360,9 @@ cudaError_t upload_adjacency(int device) {
     return e;
 }
 
-s3dsp_kmap* new_kmap(s3dsp_context* ctx, int64_t n_out, int64_t n_in, int kvol, cudaError_t* err) {
+// zero_mask: the builder ORs tile bits across blocks (a builder that stores
+// every tile's mask whole passes false)
+s3dsp_kmap* new_kmap(s3dsp_context* ctx, int64_t n_out, int64_t n_in, int kvol, bool zero_mask, cudaError_t* err) {
     auto* k = new (std::nothrow) s3dsp_kmap();
     if (!k) {
         *err = cudaErrorMemoryAllocation;
@@ -353,7 +375,7 @@ s3dsp_kmap* new_kmap(s3dsp_context* ctx, int64_t n_out, int64_t n_in, int kvol, 
     *err = cudaMallocAsync(&k->nbr, sizeof(int32_t) * (size_t)kvol * (size_t)(n_out > 0 ? n_out : 1), ctx->stream);
     if (*err == cudaSuccess)
         *err = cudaMallocAsync(&k->tile_mask, sizeof(uint32_t) * (size_t)(k->n_tiles > 0 ? k->n_tiles : 1), ctx->stream);
-    if (*err == cudaSuccess && k->n_tiles > 0)
+    if (*err == cudaSuccess && zero_mask && k->n_tiles > 0)
         *err = cudaMemsetAsync(k->tile_mask, 0, sizeof(uint32_t) * (size_t)k->n_tiles, ctx->stream);
     if (*err != cudaSuccess) {
         if (k->nbr) cudaFreeAsync(k->nbr, ctx->stream);
@@ -464,11 +486,11 @@ extern "C" S3DSP_API s3d_status s3dsp_kmap_build_subm3_range(s3dsp_context* ctx,
     S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
     cudaError_t e;
     const int64_t n_out = row_end - row_begin;
-    s3dsp_kmap* k = new_kmap(ctx, n_out, h->n, 27, &e);
+    s3dsp_kmap* k = new_kmap(ctx, n_out, h->n, 27, false, &e);
     if (!k) return cuda_fail(error, error_capacity, e, "kmap allocation");
     const int64_t tiles = (n_out + kTileRows - 1) / kTileRows;
     // output rows are hash rows row_begin ..; inputs are all its rows
-    kmap_subm3_kernel<<<dim3((unsigned)tiles, 27), kTileRows, 0, ctx->stream>>>(
+    kmap_subm3_kernel<<<(unsigned)tiles, kTileRows * kSlabs, 0, ctx->stream>>>(
         reinterpret_cast<const int4*>(h->coords), row_begin, n_out, view_of(h), h->self_row, k->nbr, k->tile_mask);
     e = cudaGetLastError();
     if (e != cudaSuccess) {
@@ -512,7 +534,7 @@ extern "C" S3DSP_API s3d_status s3dsp_subdivide(s3dsp_context* ctx, const s3dsp_
     S3DSP_CUDA(upload_adjacency(ctx->device), "adjacency tables");
     cudaError_t e;
     const int64_t np = parents->n;
-    s3dsp_kmap* k = new_kmap(ctx, np * 8, np * 8, 27, &e);
+    s3dsp_kmap* k = new_kmap(ctx, np * 8, np * 8, 27, true, &e);
     if (!k) return cuda_fail(error, error_capacity, e, "kmap allocation");
     const int64_t blocks = (np + 31) / 32;
     subdivide_kernel<<<(unsigned)blocks, 256, 0, ctx->stream>>>(
