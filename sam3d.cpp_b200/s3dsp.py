@@ -494,6 +494,7 @@ class Context:
         _call(L.s3dsp_context_create, device, stream, flags, ctypes.byref(h))
         self.handle = h.value
         self.device = device
+        self.flags = flags
 
     def close(self):
         if getattr(self, "handle", None):
