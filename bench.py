@@ -1,4 +1,4 @@
-"""Benchmark of the sparse-convolution hot path.
+"""Benchmark of the sparse-convolution hot path (config 2: the residual block on a 64^3 shell at C = 256).
 
 Workload (one "step" = one pass of the whole path over one object): the
 64^3 ellipsoid-shell active set (seed 0), C = 256:

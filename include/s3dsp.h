@@ -110,7 +110,7 @@ S3DSP_API void *s3dsp_context_stream(const s3dsp_context *ctx);
 S3DSP_API s3d_status s3dsp_context_check(s3dsp_context *ctx, char *error, uint64_t error_capacity);
 
 /* ---------------------------------------------------------------------------
- * K1 coordinate hash. Replaces the std::map / unordered_map indexes of
+ * Coordinate hash. Replaces the std::map / unordered_map indexes of
  * SlatTables::build (sparse_ops.cpp:119-124) and MeshSubdivideTables::build
  * (sparse_ops.cpp:299-333; FNV key hash :32-45).
  * d_coords: device int32 [n, 4] rows (batch, x, y, z); the hash keeps its own
@@ -322,7 +322,7 @@ S3DSP_API s3d_status s3dsp_mesh_copy(s3dsp_context *ctx, const s3dsp_mesh *mesh,
 S3DSP_API void s3dsp_mesh_free(s3dsp_context *ctx, s3dsp_mesh *mesh);
 
 /* ---------------------------------------------------------------------------
- * K2 kernel maps. A kmap holds, per kernel offset o (o = kd*9 + kh*3 + kw with
+ * Kernel maps. A kmap holds, per kernel offset o (o = kd*9 + kh*3 + kw with
  * (dx,dy,dz) = (kd-1, kh-1, kw-1), sparse_ops.cpp:132), the input row feeding
  * every output row (offset-major [kvol][n_out], -1 = none) plus a per-tile
  * bitmask of offsets that have any neighbour.
@@ -402,7 +402,7 @@ S3DSP_API s3d_status s3dsp_weights_pack(s3dsp_context *ctx, const void *src, uin
                                         void *d_dst, char *error, uint64_t error_capacity);
 
 /* ---------------------------------------------------------------------------
- * K3+K4 sparse convolution (implicit gather GEMM, no atomics on outputs):
+ * Sparse convolution (implicit gather GEMM, no atomics on outputs):
  *   out[r] = epi( sum_o W_o * pro(in[nbr_o(r) >> in_shift]) + bias
  *                 + residual[r >> res_shift] )
  * kmap == NULL means the identity map with kvol 1 (a Linear / 1x1 conv,
@@ -438,7 +438,7 @@ S3DSP_API const char *s3dsp_conv_kernel(const s3dsp_context *ctx, int64_t n_out,
                                         int64_t cout, uint32_t precision, uint32_t flags);
 
 /* ---------------------------------------------------------------------------
- * K4 normalisations (sparse_group_norm mesh_decoder_graph.cpp:16-30;
+ * Normalisations (sparse_group_norm mesh_decoder_graph.cpp:16-30;
  * gb_layer_norm graph_builder.cpp:56-62; modulate slat_flow_graph.cpp:55-59).
  * ------------------------------------------------------------------------- */
 /* GroupNorm statistics of x [n, c] into f64 partials (same buffer format the
@@ -507,7 +507,7 @@ S3DSP_API s3d_status s3dsp_slat_upsample(s3dsp_context *ctx, const s3dsp_slat_ta
  * s3dsp_weights_pack. Inputs/outputs f32 [rows, channels] on the device.
  * ------------------------------------------------------------------------- */
 /* conv3 -> GroupNorm(groups, eps, gamma, beta) -> SiLU -> conv3 -> + x
- * (GroupNorm semantics of mesh_decoder_graph.cpp:16-30). */
+ * (the config-2 benchmark block; GroupNorm semantics of mesh_decoder_graph.cpp:16-30). */
 S3DSP_API s3d_status s3dsp_res_block_gn(s3dsp_context *ctx, const s3dsp_kmap *kmap,
                                         uint32_t precision, const float *x, int64_t n, int64_t c,
                                         const void *w1, const float *b1, const float *gamma,

@@ -1,7 +1,7 @@
 // Block-level host drivers: the host C++ that replaces the reference's GGML
 // graph for one sparse block, composed from the library's kernels.
 //   s3dsp_res_block_gn        conv3 -> GroupNorm -> SiLU -> conv3 -> + x
-//                             (the BASELINE config-2 block; GroupNorm as in
+//                             (the config-2 benchmark block; GroupNorm as in
 //                             mesh_decoder_graph.cpp:16-30)
 //   s3dsp_mesh_upsample_level MeshUpsampleGraph::build, mesh_decoder_graph.cpp:42-132
 //   s3dsp_slat_res_block      res_block of slat_flow_graph.cpp:216-275

@@ -1,4 +1,4 @@
-// K3 (F32-strict) implicit-gather sparse convolution on the FP32 pipes.
+// F32-strict implicit-gather sparse convolution on the FP32 pipes.
 //
 // out[r, :] = sum_{o active} sum_ci pro(in[nbr_o(r) >> in_shift, ci]) * W[o, ci, :]
 //             + bias (+ residual) (-> SiLU)

@@ -1,4 +1,4 @@
-// K3 (BF16) implicit-gather sparse convolution, stream-K form: the default
+// BF16 implicit-gather sparse convolution, stream-K form: the default
 // tensor-core path.
 //
 // Work tile: 256 output rows x BN output channels, held as two 128-row f32

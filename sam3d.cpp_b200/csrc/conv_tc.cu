@@ -1,4 +1,4 @@
-// K3 implicit-gather sparse convolution on the 5th-generation tensor cores:
+// Implicit-gather sparse convolution on the 5th-generation tensor cores:
 // tcgen05.mma with the f32 accumulator in TMEM; BF16 operands, or f32
 // operands as 3xTF32 (kTF32, described at the end of this comment).
 //

@@ -1,4 +1,4 @@
-// K1 coordinate hash and K2 kernel-map construction.
+// Coordinate hash and kernel-map construction.
 //
 // Hash: open addressing with linear probing over a power-of-two table of
 // 16-byte slots {64-bit packed key, first row} (load factor <= 1/4). The row

@@ -1,4 +1,4 @@
-// K4 normalisation kernels (GroupNorm statistics / finalize / apply, LayerNorm
+// Normalisation kernels (GroupNorm statistics / finalize / apply, LayerNorm
 // with modulate and SiLU), dtype conversion and weight packing.
 //
 // GroupNorm follows sparse_group_norm (src/objects_runtime/mesh_decoder_graph.cpp

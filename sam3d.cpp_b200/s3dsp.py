@@ -510,7 +510,7 @@ class Context:
     def check(self):
         _call(load().s3dsp_context_check, self.handle)
 
-    # ---- K1 / K2 --------------------------------------------------------
+    # ---- coordinate hash / kernel maps --------------------------------------------------------
     def hash_build(self, coords, reject_duplicates: bool = False) -> Hash:
         h = _vp()
         _call(load().s3dsp_hash_build, self.handle, ptr(coords), coords.shape[0], int(reject_duplicates),

@@ -1,6 +1,6 @@
-"""K3/K4 sparse convolutions on the GPU against the CPU oracle.
+"""Sparse convolutions and normalisations on the GPU against the CPU oracle.
 
-Gates: F32-strict within rel-L2 1e-5, BF16 within
+Parity gates: F32-strict within rel-L2 1e-5, BF16 within
 rel-L2 1e-2, both against the oracle's float64-accumulated restatement of the
 reference op order. rel-L2 = ||a - e||_2 / max(||e||_2, DBL_MIN) in float64,
 max_abs and sign agreement as tests/test_objects_mesh_decoder_parity.cpp:84-110

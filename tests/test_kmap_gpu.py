@@ -1,4 +1,4 @@
-"""K1 hash + K2 kernel maps on the GPU, bit-exact against the reference tables.
+"""Coordinate hash and kernel maps on the GPU, bit-exact against the reference tables.
 
 Expected tables: the oracle restatement (itself pinned to the reference's
 sparse_ops.cpp by test_oracle_tables.py) and the committed golden digests made

@@ -1,7 +1,7 @@
 """Config 4 (mesh-decoder-shaped stack: Linear, 4 GN residual blocks at 256,
 subdivide to 128 + 2 blocks, subdivide to 64 + 2 blocks, Linear) through the
 C-ABI, end to end against the oracle chain: F32-strict within rel-L2 1e-5,
-BF16 within rel-L2 1e-2 (BASELINE's end-to-end gates)."""
+BF16 within rel-L2 1e-2 (the end-to-end parity gates)."""
 import numpy as np
 import pytest
 import torch
