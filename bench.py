@@ -275,13 +275,22 @@ def run_ours(args, rank, world, local_rank):
     # ---- device-resident steps, replayed as one CUDA graph per step ----
     path.step()  # eager first pass: one-time library initialisation stays out of the graph
     stream.synchronize()
+    ref_out = path.out.clone()  # the eager pass's output: every replay must reproduce it bit for bit
+    # two captures of the same step: `graph` is timed for the value; `marked`
+    # records events between the phases (for the breakdown and the conv time
+    # of the roofline), which also cuts the programmatic-launch overlap
+    # between the kernels at each mark
     marks = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(7)]
-    graph = torch.cuda.CUDAGraph()
+    graph, marked = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
     # thread-local capture: NCCL's watchdog thread may query events meanwhile
     with torch.cuda.graph(graph, stream=stream, capture_error_mode="thread_local"):
+        path.step()
+    with torch.cuda.graph(marked, stream=stream, capture_error_mode="thread_local"):
         path.step(marks)
     for _ in range(args.warmup):
         graph.replay()
+        flush_l2()
+        marked.replay()
         flush_l2()
     stream.synchronize()
     if world > 1:
@@ -292,21 +301,27 @@ def run_ours(args, rank, world, local_rank):
     time.sleep(0.3)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    phase_ms = []
     t0 = time.perf_counter()
     for i in range(args.steps):
         starts[i].record(stream)
         graph.replay()
         ends[i].record(stream)
         flush_l2()
-        ends[i].synchronize()  # the phase events are re-recorded by the next replay
-        phase_ms.append([marks[j].elapsed_time(marks[j + 1]) for j in range(6)])
     stream.synchronize()
     wall = time.perf_counter() - t0
     dev_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    if not torch.equal(path.out, ref_out):
+        raise RuntimeError("the graph-replayed step's output differs from the eager step's")
+    phase_ms = []
+    for i in range(args.steps):
+        marked.replay()
+        flush_l2()
+        stream.synchronize()  # the phase events are re-recorded by the next replay
+        phase_ms.append([marks[j].elapsed_time(marks[j + 1]) for j in range(6)])
     phase_ms = np.array(phase_ms)
     conv_ms = np.concatenate([phase_ms[:, 3], phase_ms[:, 5]])
     breakdown = {name: float(v) for name, v in zip(ResBlockPath.PHASES, phase_ms.mean(0))}
+    breakdown["step_with_marks"] = float(phase_ms.sum(1).mean())
 
     # ---- e2e: the C-ABI block call with host buffers (H2D, tables, block, D2H, sync) ----
     coords_h = torch.from_numpy(cfg["coords"]).pin_memory()
@@ -348,7 +363,7 @@ def run_ours(args, rank, world, local_rank):
     dev_ms, serial_ms, pipe_ms = vals.tolist()
     total_units, pipe_units = units.tolist()
     if rank != 0:
-        del graph
+        del graph, marked
         return None
 
     value = total_units / (dev_ms / 1e3)
@@ -367,7 +382,8 @@ def run_ours(args, rank, world, local_rank):
                                "+skip), hash + kmap rebuilt every step",
                    "voxels": n, "pairs": P, "channels": c, "objects_per_gpu": 1, "parallelism": f"objects-dp{world}",
                    "l2": "flushed between steps (512 MiB write, then 256 MiB read of another buffer)",
-                   "timing": "device steps replayed as a CUDA graph of the library calls; e2e = "
+                   "timing": "device steps replayed as a CUDA graph of the library calls (the breakdown and "
+                             "the roofline's conv time from a second capture with events between the phases); e2e = "
                              "s3dsp_res_block_gn_host (host buffers in/out) per step, called by "
                              f"{E2E_WORKERS} concurrent host threads (serial figure beside it)"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": tflops, "unit": "TFLOP/s",
@@ -382,13 +398,13 @@ def run_ours(args, rank, world, local_rank):
                         "call (inside the timed region); device-timed from one start event to the last call's end",
                 "steps": pipe_steps, "serial_value": total_units / (serial_ms / 1e3),
                 "serial_ms_per_step": serial_ms / args.steps},
-        # inside the timed regions: graph replays, serial host calls, worker calls
-        "gpu_launches": path.launches_per_step * (2 * args.steps + pipe_steps),
+        # inside the timed regions: both graphs' replays, serial host calls, worker calls
+        "gpu_launches": path.launches_per_step * (3 * args.steps + pipe_steps),
         "clocks": clocks,
         "wall_s": wall,
         "breakdown_ms": breakdown,
     }
-    del graph
+    del graph, marked
     if world == 1:
         line["cpu_baseline"] = cpu_baseline(cfg, sample_only=True)
     return line

@@ -219,19 +219,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const uint32_t rank = kPair ? cluster_rank() : 0u;
     const bool leader = rank == 0;
-    // both CTAs of a pair walk the union of their tiles' active offsets
-    uint32_t mask = 1u;
-    if (p.nbr) {
-        mask = 0x7ffffffu;
-        if (p.tile_mask) {
-            mask = tile < p.n_tiles ? p.tile_mask[tile] : 0u;
-            if (kPair && (tile ^ 1) < p.n_tiles) mask |= p.tile_mask[tile ^ 1];
-        }
-    }
-    mask &= (p.kvol >= 32) ? 0xffffffffu : ((1u << p.kvol) - 1u);
-    // KC-channel reduction chunks per offset
-    const int kchunks = kTF32 ? (p.cin + KC - 1) / KC : (p.cin + 63) / 64 * (64 / KC);
-    const int T = __popc(mask) * kchunks;
     // 3xTF32 keeps one TMEM accumulator per K step of a stage (and, for tiles of
     // at most 64 columns, a second group used by every other stage), summed in
     // f32 in the epilogue: the tensor core's f32 accumulation truncates, and a
@@ -275,6 +262,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (kPair) cluster_sync();  // the peer's barriers exist before any remote arrive
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
+
+    // everything above touched shared memory, TMEM and parameters only
+    pdl_wait();
+    pdl_trigger();
+    // both CTAs of a pair walk the union of their tiles' active offsets
+    uint32_t mask = 1u;
+    if (p.nbr) {
+        mask = 0x7ffffffu;
+        if (p.tile_mask) {
+            mask = tile < p.n_tiles ? p.tile_mask[tile] : 0u;
+            if (kPair && (tile ^ 1) < p.n_tiles) mask |= p.tile_mask[tile ^ 1];
+        }
+    }
+    mask &= (p.kvol >= 32) ? 0xffffffffu : ((1u << p.kvol) - 1u);
+    // KC-channel reduction chunks per offset
+    const int kchunks = kTF32 ? (p.cin + KC - 1) / KC : (p.cin + 63) / 64 * (64 / KC);
+    const int T = __popc(mask) * kchunks;
 
     bool prod_ok = true;
     if (warp < kProdWarps) {
@@ -703,10 +707,9 @@ static cudaError_t launch_tc_impl(s3dsp_context* ctx, const s3dsp_kmap* kmap, in
     }
     if (!pair) {
         const dim3 grid((unsigned)tiles, (unsigned)(cout_pad / bn));
-        if (tf32)
-            conv_tc_kernel<false, 32, true><<<grid, kThreads, smem, ctx->stream>>>(p, wmap);
-        else
-            conv_tc_kernel<false, 64><<<grid, kThreads, smem, ctx->stream>>>(p, wmap);
+        e = tf32 ? launch_pdl(conv_tc_kernel<false, 32, true>, grid, dim3(kThreads), smem, ctx->stream, p, wmap)
+                 : launch_pdl(conv_tc_kernel<false, 64>, grid, dim3(kThreads), smem, ctx->stream, p, wmap);
+        if (e != cudaSuccess) return e;
         return cudaGetLastError();
     }
     cudaLaunchConfig_t cfg = {};

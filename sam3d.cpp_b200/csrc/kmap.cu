@@ -25,6 +25,8 @@ namespace {
 
 // every slot empty: key all-ones, row INT32_MAX (the atomicMin identity)
 __global__ void hash_init_kernel(ulonglong2* __restrict__ slots, uint64_t cap) {
+    pdl_wait();
+    pdl_trigger();
     for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < cap; i += (uint64_t)gridDim.x * blockDim.x)
         slots[i] = make_ulonglong2(kEmptyKey, 0x7fffffffull);
 }
@@ -33,6 +35,8 @@ __global__ void hash_init_kernel(ulonglong2* __restrict__ slots, uint64_t cap) {
 __global__ void hash_insert_kernel(const int4* __restrict__ coords, int64_t n, int4* __restrict__ own,
                                    ulonglong2* slots, unsigned long long mask, int32_t reject_dups,
                                    uint32_t* status) {
+    pdl_wait();
+    pdl_trigger();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
         const int4 c = coords[i];
@@ -65,6 +69,8 @@ __global__ void hash_insert_kernel(const int4* __restrict__ coords, int64_t n, i
 // first row holding each row's key (a duplicate row is not its own first row)
 __global__ void hash_self_kernel(const int4* __restrict__ coords, int64_t n, HashView h,
                                  int32_t* __restrict__ self_row) {
+    pdl_wait();
+    pdl_trigger();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
         const int4 c = coords[i];
@@ -110,6 +116,8 @@ __global__ void __launch_bounds__(kTileRows * kSlabs) kmap_subm3_kernel(const in
                                                                         const int32_t* __restrict__ self_row,
                                                                         int32_t* __restrict__ nbr,
                                                                         uint32_t* __restrict__ tile_mask) {
+    pdl_wait();
+    pdl_trigger();
     const int s = threadIdx.x / kTileRows;
     const int dx = s - 1;
     const int64_t r = (int64_t)blockIdx.x * kTileRows + threadIdx.x % kTileRows;
@@ -424,14 +432,16 @@ extern "C" S3DSP_API s3d_status s3dsp_hash_build(s3dsp_context* ctx, const int32
         return cuda_fail(error, error_capacity, e, "hash allocation");
     }
     const int threads = 256;
-    hash_init_kernel<<<grid_for((int64_t)cap, threads, ctx->sm_count), threads, 0, st>>>(h->slots, cap);
-    hash_insert_kernel<<<grid_for(n, threads, ctx->sm_count), threads, 0, st>>>(
-        reinterpret_cast<const int4*>(d_coords), n, reinterpret_cast<int4*>(h->coords), h->slots, cap - 1,
-        reject_duplicates, ctx->d_status);
-    if (self_pass)
-        hash_self_kernel<<<grid_for(n, threads, ctx->sm_count), threads, 0, st>>>(
-            reinterpret_cast<const int4*>(h->coords), n, view_of(h), h->self_row);
-    e = cudaGetLastError();
+    e = launch_pdl(hash_init_kernel, dim3(grid_for((int64_t)cap, threads, ctx->sm_count)), dim3(threads), 0, st,
+                   h->slots, cap);
+    if (e == cudaSuccess)
+        e = launch_pdl(hash_insert_kernel, dim3(grid_for(n, threads, ctx->sm_count)), dim3(threads), 0, st,
+                       reinterpret_cast<const int4*>(d_coords), n, reinterpret_cast<int4*>(h->coords), h->slots,
+                       (unsigned long long)(cap - 1), reject_duplicates, ctx->d_status);
+    if (e == cudaSuccess && self_pass)
+        e = launch_pdl(hash_self_kernel, dim3(grid_for(n, threads, ctx->sm_count)), dim3(threads), 0, st,
+                       reinterpret_cast<const int4*>(h->coords), n, view_of(h), h->self_row);
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) {
         s3dsp_hash_free(ctx, h);
         return cuda_fail(error, error_capacity, e, "hash kernels");
@@ -490,9 +500,10 @@ extern "C" S3DSP_API s3d_status s3dsp_kmap_build_subm3_range(s3dsp_context* ctx,
     if (!k) return cuda_fail(error, error_capacity, e, "kmap allocation");
     const int64_t tiles = (n_out + kTileRows - 1) / kTileRows;
     // output rows are hash rows row_begin ..; inputs are all its rows
-    kmap_subm3_kernel<<<(unsigned)tiles, kTileRows * kSlabs, 0, ctx->stream>>>(
-        reinterpret_cast<const int4*>(h->coords), row_begin, n_out, view_of(h), h->self_row, k->nbr, k->tile_mask);
-    e = cudaGetLastError();
+    e = launch_pdl(kmap_subm3_kernel, dim3((unsigned)tiles), dim3(kTileRows * kSlabs), 0, ctx->stream,
+                   reinterpret_cast<const int4*>(h->coords), row_begin, n_out, view_of(h),
+                   static_cast<const int32_t*>(h->self_row), k->nbr, k->tile_mask);
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) {
         s3dsp_kmap_free(ctx, k);
         return cuda_fail(error, error_capacity, e, "kmap_subm3_kernel");

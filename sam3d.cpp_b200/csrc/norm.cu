@@ -63,6 +63,8 @@ __global__ void gn_finalize_kernel(const double* __restrict__ partials, int64_t 
                                    int groups, float eps, const float* __restrict__ gamma,
                                    const float* __restrict__ beta, float* __restrict__ sub, float* __restrict__ mul,
                                    float* __restrict__ add) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ double s1s[256], s2s[256];
     const int g = blockIdx.x;
     double s1 = 0.0, s2 = 0.0;
@@ -115,6 +117,8 @@ __global__ void channel_affine_kernel(const void* __restrict__ x, uint32_t xd, i
 __global__ void channel_affine_f32_bf16_kernel(const float4* __restrict__ x, int64_t total8, uint32_t c8,
                                                const float4* __restrict__ sub, const float4* __restrict__ mul,
                                                const float4* __restrict__ add, int silu, uint4* __restrict__ y) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int U = 4;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < total8; i0 += stride * U) {
@@ -193,6 +197,8 @@ __global__ void convert_kernel(const void* __restrict__ x, uint32_t xd, void* __
 
 // f32 -> bf16, 4 elements per item, 4 items per thread per iteration (loads first)
 __global__ void convert_f32_bf16_kernel(const float4* __restrict__ x, uint2* __restrict__ y, int64_t count4) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int U = 4;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < count4; i0 += stride * U) {
@@ -318,8 +324,9 @@ extern "C" S3DSP_API s3d_status s3dsp_gn_finalize(s3dsp_context* ctx, const doub
     if (n_rows <= 0 || c <= 0 || groups <= 0 || groups > 64 || c % groups || c / groups > 256)
         return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "bad GroupNorm shape");
     S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
-    gn_finalize_kernel<<<groups, 256, 0, ctx->stream>>>(partials, (n_rows + 127) / 128, n_rows, (int)c, groups, eps,
-                                                        gamma, beta, sub, mul, add);
+    S3DSP_CUDA(launch_pdl(gn_finalize_kernel, dim3(groups), dim3(256), 0, ctx->stream, partials,
+                          (int64_t)((n_rows + 127) / 128), n_rows, (int)c, (int)groups, eps, gamma, beta, sub, mul, add),
+               "gn_finalize_kernel");
     S3DSP_LAUNCH_CHECK("gn_finalize_kernel");
     return S3D_OK;
 }
@@ -339,10 +346,11 @@ extern "C" S3DSP_API s3d_status s3dsp_channel_affine(s3dsp_context* ctx, const v
                         !((uintptr_t)mul & 15) && !((uintptr_t)add & 15);
     if (xd == S3DSP_F32 && yd == S3DSP_BF16 && c % 8 == 0 && vec_ok) {
         const int64_t total8 = n * c / 8;
-        channel_affine_f32_bf16_kernel<<<grid_for((total8 + 3) / 4, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
-            reinterpret_cast<const float4*>(x), total8, (uint32_t)(c / 8), reinterpret_cast<const float4*>(sub),
-            reinterpret_cast<const float4*>(mul), reinterpret_cast<const float4*>(add), silu,
-            reinterpret_cast<uint4*>(y));
+        S3DSP_CUDA(launch_pdl(channel_affine_f32_bf16_kernel, dim3(grid_for((total8 + 3) / 4, 256, ctx->sm_count)),
+                              dim3(256), 0, ctx->stream, reinterpret_cast<const float4*>(x), total8, (uint32_t)(c / 8),
+                              reinterpret_cast<const float4*>(sub), reinterpret_cast<const float4*>(mul),
+                              reinterpret_cast<const float4*>(add), (int)silu, reinterpret_cast<uint4*>(y)),
+                   "channel_affine_f32_bf16_kernel");
     } else {
         channel_affine_kernel<<<grid_for(n * c, 256, ctx->sm_count), 256, 0, ctx->stream>>>(x, xd, n, (int)c, sub, mul,
                                                                                           add, silu, y, yd);
@@ -377,8 +385,10 @@ extern "C" S3DSP_API s3d_status s3dsp_convert(s3dsp_context* ctx, const void* x,
     if (count == 0) return S3D_OK;
     S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
     if (xd == S3DSP_F32 && yd == S3DSP_BF16 && count % 4 == 0 && !((uintptr_t)x & 15) && !((uintptr_t)y & 7))
-        convert_f32_bf16_kernel<<<grid_for((count / 4 + 3) / 4, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
-            reinterpret_cast<const float4*>(x), reinterpret_cast<uint2*>(y), count / 4);
+        S3DSP_CUDA(launch_pdl(convert_f32_bf16_kernel, dim3(grid_for((count / 4 + 3) / 4, 256, ctx->sm_count)),
+                              dim3(256), 0, ctx->stream, reinterpret_cast<const float4*>(x), reinterpret_cast<uint2*>(y),
+                              (int64_t)(count / 4)),
+                   "convert_f32_bf16_kernel");
     else
         convert_kernel<<<grid_for(count, 256, ctx->sm_count), 256, 0, ctx->stream>>>(x, xd, y, yd, count);
     S3DSP_LAUNCH_CHECK("convert_kernel");

@@ -12,6 +12,7 @@
 #include <cstdio>
 #include <cstring>
 #include <new>
+#include <utility>
 
 #include "s3dsp.h"
 
@@ -66,6 +67,31 @@ inline cudaError_t smem_optin(const void* fn, int device, std::atomic<uint64_t>&
     const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemOptIn);
     if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_acq_rel);
     return e;
+}
+
+// Programmatic dependent launch. A kernel launched by launch_pdl may start
+// while the kernel before it on the stream is still finishing; it calls
+// pdl_wait() before its first global-memory access (read or write), which
+// returns once that kernel has completed and its writes are visible, and then
+// pdl_trigger() so that the next launch_pdl kernel may be scheduled. Work
+// before pdl_wait() touches shared memory, TMEM and kernel parameters only.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // error-buffer helpers (reference convention: include/sam3d.h:32-34)

@@ -1,0 +1,87 @@
+"""Independent contexts used concurrently from several host threads.
+
+The C ABI promises that separate contexts (each on its own stream) may run at
+the same time, as the reference's handles may. Every thread here runs whole
+host-buffer residual blocks (upload, hash, kernel map, two convolutions,
+GroupNorm, download) on its own object; each output must equal, bit for bit,
+the same call made alone on one context. The kernels are deterministic (no
+float atomics on outputs, fixed-order GroupNorm partials), so any sharing of
+scratch or state between contexts would show up as a difference."""
+import threading
+
+import numpy as np
+import pytest
+import torch
+
+import s3dsp
+import workloads
+
+pytestmark = pytest.mark.gpu
+
+THREADS, CALLS, C = 4, 3, 64
+
+
+def pinned(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).pin_memory()
+
+
+@pytest.fixture(scope="module")
+def setup():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    ctx = s3dsp.Context(0)
+    P = s3dsp.PREC_BF16
+    w = workloads.config2(seed=0, channels=C)
+    packs = []
+    for key in ("w1", "w2"):
+        dst = torch.empty(s3dsp.Context.packed_bytes(P, 27, C, C), dtype=torch.uint8, device="cuda")
+        ctx.weights_pack(torch.from_numpy(w[key]), s3dsp.LAYOUT_SLAT_ROW, 27, C, C, P, dst)
+        packs.append(dst)
+    params = dict(w1=packs[0], w2=packs[1], b1=torch.from_numpy(w["b1"]).cuda(), b2=torch.from_numpy(w["b2"]).cuda(),
+                  gamma=torch.from_numpy(w["gamma"]).cuda(), beta=torch.from_numpy(w["beta"]).cuda())
+    # one object per thread: different shells and features
+    objs = []
+    for t in range(THREADS):
+        coords = workloads.ellipsoid_shell(32 + 8 * t, t)
+        objs.append((pinned(coords), pinned(workloads.normal((len(coords), C), 100 + t))))
+    torch.cuda.synchronize()
+    expected = []
+    for coords, x in objs:
+        out = torch.empty((coords.shape[0], C), dtype=torch.float32).pin_memory()
+        ctx.res_block_gn_host(P, coords, x, params["w1"], params["b1"], params["gamma"], params["beta"],
+                              params["w2"], params["b2"], out)
+        expected.append(out.clone())
+    return params, objs, expected
+
+
+@pytest.mark.parametrize("flags", [0, s3dsp.CONTEXT_DEFERRED_CHECKS])
+def test_concurrent_host_blocks_bit_exact(setup, flags):
+    params, objs, expected = setup
+    errors, results = [], [None] * THREADS
+    start = threading.Barrier(THREADS)
+
+    def body(t):
+        try:
+            torch.cuda.set_device(0)
+            st = torch.cuda.Stream()
+            cx = s3dsp.Context(0, stream=st.cuda_stream, flags=flags)
+            coords, x = objs[t]
+            outs = [torch.empty((coords.shape[0], C), dtype=torch.float32).pin_memory() for _ in range(CALLS)]
+            start.wait()
+            for o in outs:
+                cx.res_block_gn_host(s3dsp.PREC_BF16, coords, x, params["w1"], params["b1"], params["gamma"],
+                                     params["beta"], params["w2"], params["b2"], o)
+            cx.check()
+            results[t] = outs
+        except Exception as e:  # reported below
+            errors.append(e)
+            start.abort()
+
+    threads = [threading.Thread(target=body, args=(t,)) for t in range(THREADS)]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join()
+    assert not errors, errors
+    for t in range(THREADS):
+        for o in results[t]:
+            assert torch.equal(o, expected[t]), f"thread {t}: output differs from the call made alone"
