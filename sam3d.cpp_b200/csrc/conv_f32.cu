@@ -59,6 +59,8 @@ __device__ __forceinline__ float load_as_f32(const void* p, uint32_t dt, int64_t
 
 template <int BN>
 __global__ void __launch_bounds__(NT) conv_f32_kernel(const F32ConvParams p) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int TN = BN / 16;
     __shared__ __align__(16) float As[2][BK][BM];
     __shared__ __align__(16) float Bs[2][BK][BN];
@@ -264,9 +266,9 @@ cudaError_t launch_conv_f32(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol
     }
     const dim3 grid((unsigned)tiles, (unsigned)((cout + bn - 1) / bn));
     if (bn == 64)
-        conv_f32_kernel<64><<<grid, NT, 0, ctx->stream>>>(p);
+        launch_pdl(conv_f32_kernel<64>, dim3(grid), dim3(NT), 0, ctx->stream, p);
     else
-        conv_f32_kernel<32><<<grid, NT, 0, ctx->stream>>>(p);
+        launch_pdl(conv_f32_kernel<32>, dim3(grid), dim3(NT), 0, ctx->stream, p);
     return cudaGetLastError();
 }
 

@@ -110,6 +110,8 @@ __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 512;" ::: 
 // kRows = 256: two 128-row accumulators per work tile; 128: one.
 template <int kRows>
 __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, const __grid_constant__ CUtensorMap wmap) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int kSub = kRows / 128;              // 128-row accumulators per work tile
     constexpr int kAStage = kRows * 2 * kKC;       // bytes: kRows gathered rows x kKC bf16
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -609,9 +611,9 @@ cudaError_t launch_conv_sk(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
         p.counters = static_cast<uint32_t*>(counters);
     }
     if (rows == 256)
-        conv_sk_kernel<256><<<grid, kThreads, smem, s>>>(p, wmap);
+        launch_pdl(conv_sk_kernel<256>, dim3(grid), dim3(kThreads), smem, s, p, wmap);
     else
-        conv_sk_kernel<128><<<grid, kThreads, smem, s>>>(p, wmap);
+        launch_pdl(conv_sk_kernel<128>, dim3(grid), dim3(kThreads), smem, s, p, wmap);
     e = cudaGetLastError();
     if (ws) cudaFreeAsync(ws, s);
     if (counters) cudaFreeAsync(counters, s);

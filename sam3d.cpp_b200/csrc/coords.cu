@@ -34,12 +34,16 @@ inline int grid_for(int64_t n, int threads, int sm_count) {
 }
 
 __global__ void occ_flag_kernel(const float* __restrict__ occ, int64_t total, int32_t* __restrict__ flag) {
+    pdl_wait();
+    pdl_trigger();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x)
         flag[i] = occ[i] > 0.0f ? 1 : 0;
 }
 
 __global__ void occ_scatter_kernel(const int32_t* __restrict__ flag, const int32_t* __restrict__ pos, int64_t total,
                                    int32_t ny, int32_t nz, int32_t batch, int4* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x)
         if (flag[i]) {
             const int32_t z = (int32_t)(i % nz);
@@ -51,6 +55,8 @@ __global__ void occ_scatter_kernel(const int32_t* __restrict__ flag, const int32
 // surface: some cell of the (2d+1)^3 neighbourhood is not in the set
 __global__ void prune_flag_kernel(const int4* __restrict__ coords, int64_t n, HashView h, int32_t d,
                                   int32_t* __restrict__ flag) {
+    pdl_wait();
+    pdl_trigger();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         const int4 c = coords[i];
         int32_t surface = 0;
@@ -64,11 +70,15 @@ __global__ void prune_flag_kernel(const int4* __restrict__ coords, int64_t n, Ha
 
 __global__ void select_scatter_kernel(const int4* __restrict__ in, const int32_t* __restrict__ flag,
                                       const int32_t* __restrict__ pos, int64_t n, int4* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         if (flag[i]) out[pos[i]] = in[i];
 }
 
 __global__ void bounds_kernel(const int4* __restrict__ coords, int64_t n, int32_t* __restrict__ lohi) {
+    pdl_wait();
+    pdl_trigger();
     int32_t lo[3] = {INT32_MAX, INT32_MAX, INT32_MAX}, hi[3] = {INT32_MIN, INT32_MIN, INT32_MIN};
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         const int4 c = coords[i];
@@ -94,6 +104,8 @@ struct DownsampleAxes {
 // separately (no fused multiply-add)
 __global__ void downsample_map_kernel(const int4* __restrict__ coords, int64_t n, DownsampleAxes ax,
                                       int4* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         const int4 c = coords[i];
         const int32_t v[3] = {c.y, c.z, c.w};
@@ -114,6 +126,8 @@ __global__ void downsample_map_kernel(const int4* __restrict__ coords, int64_t n
 
 // first occurrence of each coordinate: the row the hash kept for its key
 __global__ void first_flag_kernel(const int4* __restrict__ coords, int64_t n, HashView h, int32_t* __restrict__ flag) {
+    pdl_wait();
+    pdl_trigger();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         const int4 c = coords[i];
         flag[i] = h.find_coord(c.x, c.y, c.z, c.w) == (int32_t)i;
@@ -174,7 +188,7 @@ extern "C" S3DSP_API s3d_status s3dsp_occupancy_coords(s3dsp_context* ctx, const
     Scratch sc(st);
     int32_t *flag, *pos;
     S3DSP_CUDA(sc.get(&flag, sizeof(int32_t) * (size_t)total), "scratch");
-    occ_flag_kernel<<<grid_for(total, 256, ctx->sm_count), 256, 0, st>>>(d_occ, total, flag);
+    launch_pdl(occ_flag_kernel, dim3(grid_for(total, 256, ctx->sm_count)), dim3(256), 0, st, d_occ, total, flag);
     S3DSP_LAUNCH_CHECK("occ_flag_kernel");
     int64_t n = 0;
     S3DSP_CUDA(scan_flags(ctx, sc, flag, total, &pos, &n), "occupancy scan");
@@ -182,8 +196,8 @@ extern "C" S3DSP_API s3d_status s3dsp_occupancy_coords(s3dsp_context* ctx, const
     if (n > capacity)
         return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "%lld occupied cells > capacity %lld", (long long)n,
                     (long long)capacity);
-    occ_scatter_kernel<<<grid_for(total, 256, ctx->sm_count), 256, 0, st>>>(flag, pos, total, ny, nz, batch,
-                                                                           reinterpret_cast<int4*>(d_coords));
+    launch_pdl(occ_scatter_kernel, dim3(grid_for(total, 256, ctx->sm_count)), dim3(256), 0, st, flag, pos, total, ny,
+               nz, batch, reinterpret_cast<int4*>(d_coords));
     S3DSP_LAUNCH_CHECK("occ_scatter_kernel");
     return S3D_OK;
 }
@@ -209,8 +223,8 @@ extern "C" S3DSP_API s3d_status s3dsp_prune_surface(s3dsp_context* ctx, const in
         int32_t *flag = nullptr, *pos = nullptr;
         cudaError_t e = sc.get(&flag, sizeof(int32_t) * (size_t)n);
         if (e == cudaSuccess) {
-            prune_flag_kernel<<<grid_for(n, 256, ctx->sm_count), 256, 0, st>>>(
-                reinterpret_cast<const int4*>(h->coords), n, view_of(h), max_axis_dist, flag);
+            launch_pdl(prune_flag_kernel, dim3(grid_for(n, 256, ctx->sm_count)), dim3(256), 0, st,
+                       reinterpret_cast<const int4*>(h->coords), n, view_of(h), max_axis_dist, flag);
             e = cudaGetLastError();
         }
         int64_t m = 0;
@@ -223,8 +237,8 @@ extern "C" S3DSP_API s3d_status s3dsp_prune_surface(s3dsp_context* ctx, const in
                 status = fail(error, error_capacity, S3D_INVALID_ARGUMENT, "%lld surface rows > capacity %lld",
                               (long long)m, (long long)capacity);
             } else {
-                select_scatter_kernel<<<grid_for(n, 256, ctx->sm_count), 256, 0, st>>>(
-                    reinterpret_cast<const int4*>(h->coords), flag, pos, n, reinterpret_cast<int4*>(d_out));
+                launch_pdl(select_scatter_kernel, dim3(grid_for(n, 256, ctx->sm_count)), dim3(256), 0, st,
+                           reinterpret_cast<const int4*>(h->coords), flag, pos, n, reinterpret_cast<int4*>(d_out));
                 e = cudaGetLastError();
                 if (e != cudaSuccess) status = cuda_fail(error, error_capacity, e, "select_scatter_kernel");
             }
@@ -263,7 +277,8 @@ extern "C" S3DSP_API s3d_status s3dsp_downsample_coords(s3dsp_context* ctx, cons
     S3DSP_CUDA(sc.get(&lohi, 6 * sizeof(int32_t)), "scratch");
     const int32_t init[6] = {INT32_MAX, INT32_MAX, INT32_MAX, INT32_MIN, INT32_MIN, INT32_MIN};
     S3DSP_CUDA(cudaMemcpyAsync(lohi, init, sizeof init, cudaMemcpyHostToDevice, st), "bounds init");
-    bounds_kernel<<<grid_for(n, 256, ctx->sm_count), 256, 0, st>>>(reinterpret_cast<const int4*>(d_coords), n, lohi);
+    launch_pdl(bounds_kernel, dim3(grid_for(n, 256, ctx->sm_count)), dim3(256), 0, st,
+               reinterpret_cast<const int4*>(d_coords), n, lohi);
     S3DSP_LAUNCH_CHECK("bounds_kernel");
     int32_t hb[6];
     S3DSP_CUDA(cudaMemcpyAsync(hb, lohi, sizeof hb, cudaMemcpyDeviceToHost, st), "bounds");
@@ -286,8 +301,8 @@ extern "C" S3DSP_API s3d_status s3dsp_downsample_coords(s3dsp_context* ctx, cons
     }
     int32_t* mapped;
     S3DSP_CUDA(sc.get(&mapped, (size_t)n * 16), "scratch");
-    downsample_map_kernel<<<grid_for(n, 256, ctx->sm_count), 256, 0, st>>>(reinterpret_cast<const int4*>(d_coords), n,
-                                                                          ax, reinterpret_cast<int4*>(mapped));
+    launch_pdl(downsample_map_kernel, dim3(grid_for(n, 256, ctx->sm_count)), dim3(256), 0, st,
+               reinterpret_cast<const int4*>(d_coords), n, ax, reinterpret_cast<int4*>(mapped));
     S3DSP_LAUNCH_CHECK("downsample_map_kernel");
     // first occurrences, in input order
     s3dsp_hash* h = nullptr;
@@ -295,16 +310,16 @@ extern "C" S3DSP_API s3d_status s3dsp_downsample_coords(s3dsp_context* ctx, cons
     int32_t *flag = nullptr, *pos = nullptr, *uniq = nullptr;
     cudaError_t e = sc.get(&flag, sizeof(int32_t) * (size_t)n);
     if (e == cudaSuccess) {
-        first_flag_kernel<<<grid_for(n, 256, ctx->sm_count), 256, 0, st>>>(reinterpret_cast<const int4*>(mapped), n,
-                                                                          view_of(h), flag);
+        launch_pdl(first_flag_kernel, dim3(grid_for(n, 256, ctx->sm_count)), dim3(256), 0, st,
+                   reinterpret_cast<const int4*>(mapped), n, view_of(h), flag);
         e = cudaGetLastError();
     }
     int64_t un = 0;
     if (e == cudaSuccess) e = scan_flags(ctx, sc, flag, n, &pos, &un);
     if (e == cudaSuccess) e = sc.get(&uniq, (size_t)un * 16);
     if (e == cudaSuccess) {
-        select_scatter_kernel<<<grid_for(n, 256, ctx->sm_count), 256, 0, st>>>(
-            reinterpret_cast<const int4*>(mapped), flag, pos, n, reinterpret_cast<int4*>(uniq));
+        launch_pdl(select_scatter_kernel, dim3(grid_for(n, 256, ctx->sm_count)), dim3(256), 0, st,
+                   reinterpret_cast<const int4*>(mapped), flag, pos, n, reinterpret_cast<int4*>(uniq));
         e = cudaGetLastError();
     }
     s3dsp_hash_free(ctx, h);

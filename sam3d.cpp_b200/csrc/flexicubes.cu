@@ -88,6 +88,8 @@ struct Int4Add {
 
 __global__ void fc_scatter_kernel(const int4* __restrict__ coords, int64_t n, int32_t* __restrict__ cube_row,
                                   int32_t* __restrict__ err_row) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (r >= n) return;
     const int4 c = coords[r];
@@ -105,6 +107,8 @@ __global__ void fc_scatter_kernel(const int4* __restrict__ coords, int64_t n, in
 // A row whose cube already holds a lower row is the reference's duplicate.
 __global__ void fc_dup_kernel(const int4* __restrict__ coords, int64_t n, const int32_t* __restrict__ cube_row,
                               int32_t* __restrict__ err_row) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (r >= n) return;
     const int4 c = coords[r];
@@ -124,6 +128,8 @@ constexpr int kVChunks = (RV + 31) / 32;  // 32-vertex chunks per (x, y) row
 // is corner k of cube (x - (k & 1), y - (k >> 1 & 1), z - (k >> 2 & 1)).
 __global__ void fc_vertex_kernel(const float* __restrict__ raw, const int32_t* __restrict__ cube_row,
                                  float* __restrict__ sdf, int32_t* __restrict__ vslot, float* __restrict__ vattr) {
+    pdl_wait();
+    pdl_trigger();
     const int w = (int)((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5);
     const int lane = threadIdx.x & 31;
     if (w >= RV * RV * kVChunks) return;
@@ -199,6 +205,8 @@ __global__ void fc_vertex_kernel(const float* __restrict__ raw, const int32_t* _
 // Warp per (x, y) row of 256 cubes: occupancy bytes + surface count.
 __global__ void fc_surface_count_kernel(const float* __restrict__ sdf, uint8_t* __restrict__ occ,
                                         int32_t* __restrict__ row_count) {
+    pdl_wait();
+    pdl_trigger();
     const int row = (int)((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= R * R) return;
@@ -240,6 +248,8 @@ __device__ __forceinline__ void vertex_edges(const float* __restrict__ sdf, int 
 
 // Warp per (x, y) row of 257 vertices: {edges, flipped quads, other quads}.
 __global__ void fc_edge_count_kernel(const float* __restrict__ sdf, int4* __restrict__ row_count) {
+    pdl_wait();
+    pdl_trigger();
     const int row = (int)((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= RV * RV) return;
@@ -266,6 +276,8 @@ __global__ void fc_edge_count_kernel(const float* __restrict__ sdf, int4* __rest
 __global__ void fc_totals_kernel(const int32_t* __restrict__ srow_count, const int32_t* __restrict__ srow_off,
                                  const int4* __restrict__ erow_count, const int4* __restrict__ erow_off,
                                  const int32_t* __restrict__ err_row, int64_t* __restrict__ totals) {
+    pdl_wait();
+    pdl_trigger();
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
     totals[0] = (int64_t)srow_off[R * R - 1] + srow_count[R * R - 1];
     const int4 a = erow_off[RV * RV - 1], b = erow_count[RV * RV - 1];
@@ -278,6 +290,8 @@ __global__ void fc_totals_kernel(const int32_t* __restrict__ srow_count, const i
 // Warp per (x, y) row of cubes: the surface list in dense order.
 __global__ void fc_surface_write_kernel(const uint8_t* __restrict__ occ, const int32_t* __restrict__ row_off,
                                         int32_t* __restrict__ surf, int32_t* __restrict__ sidx) {
+    pdl_wait();
+    pdl_trigger();
     const int row = (int)((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= R * R) return;
@@ -302,6 +316,8 @@ __global__ void fc_surface_write_kernel(const uint8_t* __restrict__ occ, const i
 __global__ void fc_case_kernel(const int32_t* __restrict__ surf, int64_t ns, const uint8_t* __restrict__ occ,
                                const int8_t* __restrict__ num_dual, const int16_t* __restrict__ check,
                                int32_t* __restrict__ cases, int4* __restrict__ onehot) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (i >= ns) return;
     const int32_t c = surf[i];
@@ -347,6 +363,8 @@ __global__ void fc_dual_kernel(const int32_t* __restrict__ surf, int64_t ns, con
                                const int8_t* __restrict__ num_dual, float* __restrict__ out_v,
                                float* __restrict__ out_a, float* __restrict__ dual_gamma,
                                int32_t* __restrict__ dmap, int64_t* __restrict__ n_dual) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     // dual vertices of each count: totals = last exclusive rank + last one-hot
     const int4 tot = Int4Add()(rank[ns - 1], onehot[ns - 1]);
@@ -469,6 +487,8 @@ __device__ void emit_quad(int x, int y, int z, int d, int32_t u, int32_t v, bool
 __global__ void fc_edge_write_kernel(const float* __restrict__ sdf, const int4* __restrict__ row_off,
                                      const int64_t* __restrict__ totals, int32_t* __restrict__ edges,
                                      int32_t* __restrict__ quads) {
+    pdl_wait();
+    pdl_trigger();
     const int row = (int)((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= RV * RV) return;
@@ -514,6 +534,8 @@ __global__ void fc_edge_write_kernel(const float* __restrict__ sdf, const int4* 
 __global__ void fc_quad_kernel(const int32_t* __restrict__ quads, int64_t nq, const int32_t* __restrict__ sidx,
                                const int32_t* __restrict__ dmap, const float* __restrict__ dual_gamma,
                                int32_t* __restrict__ faces) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (q >= nq) return;
     const int32_t rec = quads[q];
@@ -642,11 +664,12 @@ extern "C" S3DSP_API s3d_status s3dsp_flexicubes_extract(s3dsp_context* ctx, con
     if (e != cudaSuccess) return cuda_fail(error, error_capacity, e, "flexicubes scratch");
     S3DSP_CUDA(cudaMemsetAsync(cube_row, 0x7F, 4 * kCubes, st), "memset");
     S3DSP_CUDA(cudaMemsetAsync(err_row, 0x7F, 16, st), "memset");
-    fc_scatter_kernel<<<grid_for(n, 256), 256, 0, st>>>(coords, n, cube_row, err_row);
-    fc_dup_kernel<<<grid_for(n, 256), 256, 0, st>>>(coords, n, cube_row, err_row);
-    fc_vertex_kernel<<<(RV * RV * kVChunks + 7) / 8, 256, 0, st>>>(d_raw, cube_row, sdf, vslot, vattr);
-    fc_surface_count_kernel<<<R * R / 8, 256, 0, st>>>(sdf, occ, srow_count);
-    fc_edge_count_kernel<<<(RV * RV + 7) / 8, 256, 0, st>>>(sdf, erow_count);
+    launch_pdl(fc_scatter_kernel, dim3(grid_for(n, 256)), dim3(256), 0, st, coords, n, cube_row, err_row);
+    launch_pdl(fc_dup_kernel, dim3(grid_for(n, 256)), dim3(256), 0, st, coords, n, cube_row, err_row);
+    launch_pdl(fc_vertex_kernel, dim3((RV * RV * kVChunks + 7) / 8), dim3(256), 0, st, d_raw, cube_row, sdf, vslot,
+               vattr);
+    launch_pdl(fc_surface_count_kernel, dim3(R * R / 8), dim3(256), 0, st, sdf, occ, srow_count);
+    launch_pdl(fc_edge_count_kernel, dim3((RV * RV + 7) / 8), dim3(256), 0, st, sdf, erow_count);
     S3DSP_LAUNCH_CHECK("flexicubes count kernels");
     size_t tb1 = 0, tb2 = 0;
     void *t1 = nullptr, *t2 = nullptr;
@@ -659,7 +682,7 @@ extern "C" S3DSP_API s3d_status s3dsp_flexicubes_extract(s3dsp_context* ctx, con
     if (e == cudaSuccess)
         e = cub::DeviceScan::ExclusiveScan(t2, tb2, erow_count, erow_off, Int4Add(), make_int4(0, 0, 0, 0), RV * RV, st);
     if (e != cudaSuccess) return cuda_fail(error, error_capacity, e, "flexicubes row scans");
-    fc_totals_kernel<<<1, 32, 0, st>>>(srow_count, srow_off, erow_count, erow_off, err_row, totals);
+    launch_pdl(fc_totals_kernel, dim3(1), dim3(32), 0, st, srow_count, srow_off, erow_count, erow_off, err_row, totals);
     S3DSP_LAUNCH_CHECK("fc_totals_kernel");
     int64_t h_tot[8];
     S3DSP_CUDA(cudaMemcpyAsync(h_tot, totals, 7 * 8, cudaMemcpyDeviceToHost, st), "D2H");
@@ -702,9 +725,9 @@ extern "C" S3DSP_API s3d_status s3dsp_flexicubes_extract(s3dsp_context* ctx, con
     if (e == cudaSuccess) e = sc.get(&dmap, 48 * (size_t)ns);
     if (e == cudaSuccess) e = sc.get(&quads, 4 * (size_t)nq);
     if (e == cudaSuccess && ns > 0) {
-        fc_surface_write_kernel<<<R * R / 8, 256, 0, st>>>(occ, srow_off, m->surface, sidx);
-        fc_case_kernel<<<grid_for(ns, 256), 256, 0, st>>>(m->surface, ns, occ, tables->num_dual, tables->check,
-                                                           m->cases, onehot);
+        launch_pdl(fc_surface_write_kernel, dim3(R * R / 8), dim3(256), 0, st, occ, srow_off, m->surface, sidx);
+        launch_pdl(fc_case_kernel, dim3(grid_for(ns, 256)), dim3(256), 0, st, m->surface, ns, occ, tables->num_dual,
+                   tables->check, m->cases, onehot);
         e = cudaGetLastError();
         size_t tb3 = 0;
         void* t3 = nullptr;
@@ -714,18 +737,20 @@ extern "C" S3DSP_API s3d_status s3dsp_flexicubes_extract(s3dsp_context* ctx, con
         if (e == cudaSuccess)
             e = cub::DeviceScan::ExclusiveScan(t3, tb3, onehot, rank, Int4Add(), make_int4(0, 0, 0, 0), (int)ns, st);
         if (e == cudaSuccess) {
-            fc_dual_kernel<<<grid_for(ns, 128), 128, 0, st>>>(m->surface, ns, m->cases, onehot, rank, cube_row, d_raw,
-                                                               sdf, vslot, vattr, tables->dmc, tables->num_dual,
-                                                               m->vertices, m->attrs, dual_gamma, dmap, totals + 7);
+            launch_pdl(fc_dual_kernel, dim3(grid_for(ns, 128)), dim3(128), 0, st, m->surface, ns, m->cases, onehot,
+                       rank, cube_row, d_raw, sdf, vslot, vattr, tables->dmc, tables->num_dual, m->vertices, m->attrs,
+                       dual_gamma, dmap, totals + 7);
             e = cudaGetLastError();
         }
     } else if (e == cudaSuccess) {
         e = cudaMemsetAsync(totals + 7, 0, 8, st);
     }
     if (e == cudaSuccess && ne > 0) {
-        fc_edge_write_kernel<<<(RV * RV + 7) / 8, 256, 0, st>>>(sdf, erow_off, totals, m->edges, quads);
+        launch_pdl(fc_edge_write_kernel, dim3((RV * RV + 7) / 8), dim3(256), 0, st, sdf, erow_off, totals, m->edges,
+                   quads);
         if (nq > 0)
-            fc_quad_kernel<<<grid_for(nq, 128), 128, 0, st>>>(quads, nq, sidx, dmap, dual_gamma, m->faces);
+            launch_pdl(fc_quad_kernel, dim3(grid_for(nq, 128)), dim3(128), 0, st, quads, nq, sidx, dmap, dual_gamma,
+                       m->faces);
         e = cudaGetLastError();
     }
     int64_t nv = 0;

@@ -80,6 +80,8 @@ __device__ __forceinline__ void put<__nv_bfloat16>(__nv_bfloat16* out, int64_t i
 
 template <typename OutT>
 __global__ void dequant_kernel(const uint8_t* __restrict__ src, int32_t type, int64_t n, OutT* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         float v;
         switch (type) {
@@ -316,9 +318,11 @@ s3d_status dequantize_device(s3dsp_context* ctx, int32_t type, const void* d_src
     const int grid = (int)(g < ctx->sm_count * 16 ? g : ctx->sm_count * 16);
     const uint8_t* src = static_cast<const uint8_t*>(d_src);
     if (dtype == S3DSP_F32)
-        dequant_kernel<float><<<grid, 256, 0, ctx->stream>>>(src, type, n, static_cast<float*>(d_out));
+        launch_pdl(dequant_kernel<float>, dim3(grid), dim3(256), 0, ctx->stream, src, type, n,
+                   static_cast<float*>(d_out));
     else
-        dequant_kernel<__nv_bfloat16><<<grid, 256, 0, ctx->stream>>>(src, type, n, static_cast<__nv_bfloat16*>(d_out));
+        launch_pdl(dequant_kernel<__nv_bfloat16>, dim3(grid), dim3(256), 0, ctx->stream, src, type, n,
+                   static_cast<__nv_bfloat16*>(d_out));
     S3DSP_LAUNCH_CHECK("dequant_kernel");
     return S3D_OK;
 }

@@ -36,6 +36,8 @@ inline int grid_for(int64_t n, int threads, int sm_count) {
 
 __global__ void window_key_kernel(const int4* __restrict__ coords, int64_t n, int32_t shift, int32_t window,
                                   int4* __restrict__ wc) {
+    pdl_wait();
+    pdl_trigger();
     GRID_LOOP(i, n) {
         const int4 c = coords[i];
         wc[i] = make_int4(c.x, (c.y + shift) / window, (c.z + shift) / window, (c.w + shift) / window);
@@ -44,6 +46,8 @@ __global__ void window_key_kernel(const int4* __restrict__ coords, int64_t n, in
 
 __global__ void first_of_window_kernel(const int4* __restrict__ wc, int64_t n, HashView h, int32_t* __restrict__ fr,
                                        int32_t* __restrict__ is_first) {
+    pdl_wait();
+    pdl_trigger();
     GRID_LOOP(i, n) {
         const int4 k = wc[i];
         const int32_t f = h.find_coord(k.x, k.y, k.z, k.w);
@@ -54,6 +58,8 @@ __global__ void first_of_window_kernel(const int4* __restrict__ wc, int64_t n, H
 
 __global__ void window_id_kernel(const int32_t* __restrict__ fr, const int32_t* __restrict__ first_rank, int64_t n,
                                  int32_t* __restrict__ wid, int32_t* __restrict__ rows, int32_t* __restrict__ cnt) {
+    pdl_wait();
+    pdl_trigger();
     GRID_LOOP(i, n) {
         const int32_t w = first_rank[fr[i]];
         wid[i] = w;
@@ -63,18 +69,24 @@ __global__ void window_id_kernel(const int32_t* __restrict__ fr, const int32_t* 
 }
 
 __global__ void iota_kernel(int32_t* __restrict__ v, int64_t n) {
+    pdl_wait();
+    pdl_trigger();
     GRID_LOOP(i, n) v[i] = (int32_t)i;
 }
 
 __global__ void window_offset_scatter_kernel(const int32_t* __restrict__ win_by_len,
                                              const int32_t* __restrict__ off_by_len, int64_t nw,
                                              int32_t* __restrict__ win_off) {
+    pdl_wait();
+    pdl_trigger();
     GRID_LOOP(k, nw) win_off[win_by_len[k]] = off_by_len[k];
 }
 
 __global__ void bucket_rows_kernel(const int32_t* __restrict__ swid, const int32_t* __restrict__ srow, int64_t n,
                                    const int32_t* __restrict__ seg_start, const int32_t* __restrict__ win_off,
                                    int32_t* __restrict__ bkt_idx, int32_t* __restrict__ bwd_idx) {
+    pdl_wait();
+    pdl_trigger();
     GRID_LOOP(p, n) {
         const int32_t w = swid[p], r = srow[p];
         const int32_t out = win_off[w] + ((int32_t)p - seg_start[w]);
@@ -85,6 +97,8 @@ __global__ void bucket_rows_kernel(const int32_t* __restrict__ swid, const int32
 
 __global__ void ape_kernel(const int4* __restrict__ coords, int64_t n, int32_t f, const float* __restrict__ freq,
                            float* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t total = n * 3 * f;
     GRID_LOOP(j, total) {
         const int32_t i = (int32_t)(j % f);
@@ -144,7 +158,7 @@ extern "C" S3DSP_API s3d_status s3dsp_gs_window_tables(s3dsp_context* ctx, const
     Scratch sc(st);
     int32_t* wc;
     S3DSP_CUDA(sc.get(&wc, (size_t)n * 16), "scratch");
-    window_key_kernel<<<g, 256, 0, st>>>(reinterpret_cast<const int4*>(d_coords), n, shift, window,
+    launch_pdl(window_key_kernel, dim3(g), dim3(256), 0, st, reinterpret_cast<const int4*>(d_coords), n, shift, window,
                                          reinterpret_cast<int4*>(wc));
     S3DSP_LAUNCH_CHECK("window_key_kernel");
     s3dsp_hash* h = nullptr;
@@ -158,7 +172,8 @@ extern "C" S3DSP_API s3d_status s3dsp_gs_window_tables(s3dsp_context* ctx, const
     if (e == cudaSuccess) e = sc.get(&swid, 4 * (size_t)n);
     if (e == cudaSuccess) e = sc.get(&srow, 4 * (size_t)n);
     if (e == cudaSuccess) {
-        first_of_window_kernel<<<g, 256, 0, st>>>(reinterpret_cast<const int4*>(wc), n, view_of(h), fr, is_first);
+        launch_pdl(first_of_window_kernel, dim3(g), dim3(256), 0, st, reinterpret_cast<const int4*>(wc), n,
+                   view_of(h), fr, is_first);
         e = cudaGetLastError();
     }
     // window ids in first-appearance order
@@ -183,7 +198,7 @@ extern "C" S3DSP_API s3d_status s3dsp_gs_window_tables(s3dsp_context* ctx, const
     if (e == cudaSuccess) e = sc.get(&win_off, 4 * (size_t)nw);
     if (e == cudaSuccess) e = cudaMemsetAsync(cnt, 0, 4 * (size_t)nw, st);
     if (e == cudaSuccess) {
-        window_id_kernel<<<g, 256, 0, st>>>(fr, rank, n, wid, rows, cnt);
+        launch_pdl(window_id_kernel, dim3(g), dim3(256), 0, st, fr, rank, n, wid, rows, cnt);
         e = cudaGetLastError();
     }
     // tokens grouped by window (stable: table order inside a window)
@@ -201,7 +216,7 @@ extern "C" S3DSP_API s3d_status s3dsp_gs_window_tables(s3dsp_context* ctx, const
     if (e == cudaSuccess) e = cub::DeviceScan::ExclusiveSum(temp3, tb3, cnt, seg_start, (int)nw, st);
     // windows by token count (stable: id order inside a count)
     if (e == cudaSuccess) {
-        iota_kernel<<<grid_for(nw, 256, ctx->sm_count), 256, 0, st>>>(win, nw);
+        launch_pdl(iota_kernel, dim3(grid_for(nw, 256, ctx->sm_count)), dim3(256), 0, st, win, nw);
         e = cudaGetLastError();
     }
     const int lbits = bits_for(n);
@@ -216,11 +231,13 @@ extern "C" S3DSP_API s3d_status s3dsp_gs_window_tables(s3dsp_context* ctx, const
     if (e == cudaSuccess) e = sc.get(&temp5, tb5);
     if (e == cudaSuccess) e = cub::DeviceScan::ExclusiveSum(temp5, tb5, slen, off_by_len, (int)nw, st);
     if (e == cudaSuccess) {
-        window_offset_scatter_kernel<<<grid_for(nw, 256, ctx->sm_count), 256, 0, st>>>(swin, off_by_len, nw, win_off);
+        launch_pdl(window_offset_scatter_kernel, dim3(grid_for(nw, 256, ctx->sm_count)), dim3(256), 0, st, swin,
+                   off_by_len, nw, win_off);
         e = cudaGetLastError();
     }
     if (e == cudaSuccess) {
-        bucket_rows_kernel<<<g, 256, 0, st>>>(swid, srow, n, seg_start, win_off, d_bkt_idx, d_bwd_idx);
+        launch_pdl(bucket_rows_kernel, dim3(g), dim3(256), 0, st, swid, srow, n, seg_start, win_off, d_bkt_idx,
+                   d_bwd_idx);
         e = cudaGetLastError();
     }
     // bucket list on the host: one entry per distinct token count
@@ -267,8 +284,8 @@ extern "C" S3DSP_API s3d_status s3dsp_ape(s3dsp_context* ctx, const int32_t* d_c
     float* dfreq;
     S3DSP_CUDA(sc.get(&dfreq, 4 * (size_t)f), "scratch");
     S3DSP_CUDA(cudaMemcpyAsync(dfreq, freq.data(), 4 * (size_t)f, cudaMemcpyHostToDevice, st), "H2D");
-    ape_kernel<<<grid_for(n * 3 * f, 256, ctx->sm_count), 256, 0, st>>>(reinterpret_cast<const int4*>(d_coords), n, f,
-                                                                       dfreq, d_out);
+    launch_pdl(ape_kernel, dim3(grid_for(n * 3 * f, 256, ctx->sm_count)), dim3(256), 0, st,
+               reinterpret_cast<const int4*>(d_coords), n, f, dfreq, d_out);
     S3DSP_LAUNCH_CHECK("ape_kernel");
     return S3D_OK;  // a copy from pageable memory has been staged when cudaMemcpyAsync returns
 }

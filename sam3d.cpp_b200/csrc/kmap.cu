@@ -80,6 +80,8 @@ __global__ void hash_self_kernel(const int4* __restrict__ coords, int64_t n, Has
 
 __global__ void hash_lookup_kernel(const int4* __restrict__ q, int64_t m, HashView h,
                                    int32_t* __restrict__ rows) {
+    pdl_wait();
+    pdl_trigger();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < m;
          i += (int64_t)gridDim.x * blockDim.x) {
         const int4 c = q[i];
@@ -180,6 +182,8 @@ __global__ void __launch_bounds__(256) subdivide_kernel(const int4* __restrict__
                                                         HashView h, int4* __restrict__ child_coords,
                                                         int32_t* __restrict__ nbr,
                                                         uint32_t* __restrict__ tile_mask) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ int32_t padj[32][28];
     const int64_t p0 = (int64_t)blockIdx.x * 32;
     for (int t = threadIdx.x; t < 32 * 27; t += blockDim.x) {
@@ -216,6 +220,8 @@ __global__ void __launch_bounds__(256) subdivide_kernel(const int4* __restrict__
 
 __global__ void export_dense_kernel(const int32_t* __restrict__ nbr, int64_t n, int32_t kvol,
                                     int32_t sentinel, int32_t* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n * 27;
          i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = i / 27;
@@ -230,6 +236,8 @@ constexpr int kPairBlock = 1024;
 
 __global__ void pair_count_kernel(const int32_t* __restrict__ nbr, int64_t n, int32_t* counts,
                                   int64_t nblk) {
+    pdl_wait();
+    pdl_trigger();
     const int o = blockIdx.y;
     const int64_t r = blockIdx.x * (int64_t)kPairBlock + threadIdx.x;
     const int valid = (r < n) && nbr[o * n + r] >= 0;
@@ -240,6 +248,8 @@ __global__ void pair_count_kernel(const int32_t* __restrict__ nbr, int64_t n, in
 // single-block exclusive scan of m ints into int64 starts (m is small:
 // 27 * ceil(n / 1024))
 __global__ void pair_scan_kernel(const int32_t* counts, int64_t m, int64_t* starts) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ int64_t carry;
     __shared__ int64_t warp_sums[32];
     if (threadIdx.x == 0) carry = 0;
@@ -276,6 +286,8 @@ __global__ void pair_scan_kernel(const int32_t* counts, int64_t m, int64_t* star
 
 __global__ void pair_write_kernel(const int32_t* __restrict__ nbr, int64_t n, const int64_t* starts,
                                   int64_t nblk, int32_t* __restrict__ pin, int32_t* __restrict__ pout) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ int warp_cnt[kPairBlock / 32];
     const int o = blockIdx.y;
     const int64_t r = blockIdx.x * (int64_t)kPairBlock + threadIdx.x;
@@ -311,6 +323,8 @@ static __device__ __align__(256) unsigned char g_pairs_scratch[kNoAllocBytes];
 
 __global__ void pair_offsets_kernel(const int64_t* __restrict__ starts, int64_t nblk, int kvol, int64_t m,
                                     int64_t* __restrict__ offs) {
+    pdl_wait();
+    pdl_trigger();
     const int o = threadIdx.x;
     if (o < kvol) offs[o] = starts[o * nblk];
     if (o == kvol) offs[kvol] = starts[m];
@@ -478,8 +492,8 @@ extern "C" S3DSP_API s3d_status s3dsp_hash_lookup(s3dsp_context* ctx, const s3ds
     if (!d_query || ((uintptr_t)d_query & 15) || !d_rows)
         return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "query/rows pointers invalid");
     S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
-    hash_lookup_kernel<<<grid_for(m, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
-        reinterpret_cast<const int4*>(d_query), m, view_of(h), d_rows);
+    launch_pdl(hash_lookup_kernel, dim3(grid_for(m, 256, ctx->sm_count)), dim3(256), 0, ctx->stream,
+               reinterpret_cast<const int4*>(d_query), m, view_of(h), d_rows);
     S3DSP_LAUNCH_CHECK("hash_lookup_kernel");
     return S3D_OK;
 }
@@ -548,9 +562,9 @@ extern "C" S3DSP_API s3d_status s3dsp_subdivide(s3dsp_context* ctx, const s3dsp_
     s3dsp_kmap* k = new_kmap(ctx, np * 8, np * 8, 27, true, &e);
     if (!k) return cuda_fail(error, error_capacity, e, "kmap allocation");
     const int64_t blocks = (np + 31) / 32;
-    subdivide_kernel<<<(unsigned)blocks, 256, 0, ctx->stream>>>(
-        reinterpret_cast<const int4*>(parents->coords), np, view_of(parents),
-        reinterpret_cast<int4*>(d_child_coords), k->nbr, k->tile_mask);
+    launch_pdl(subdivide_kernel, dim3((unsigned)blocks), dim3(256), 0, ctx->stream,
+               reinterpret_cast<const int4*>(parents->coords), np, view_of(parents),
+               reinterpret_cast<int4*>(d_child_coords), k->nbr, k->tile_mask);
     e = cudaGetLastError();
     if (e != cudaSuccess) {
         s3dsp_kmap_free(ctx, k);
@@ -579,8 +593,8 @@ extern "C" S3DSP_API s3d_status s3dsp_kmap_export_dense(s3dsp_context* ctx, cons
         return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "unknown sentinel mode %u", sentinel_mode);
     S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
     const int32_t sentinel = sentinel_mode == S3DSP_SENTINEL_SLAT_N ? (int32_t)k->n_in : -1;
-    export_dense_kernel<<<grid_for(k->n_out * 27, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
-        k->nbr, k->n_out, k->kvol, sentinel, d_out);
+    launch_pdl(export_dense_kernel, dim3(grid_for(k->n_out * 27, 256, ctx->sm_count)), dim3(256), 0, ctx->stream,
+               k->nbr, k->n_out, k->kvol, sentinel, d_out);
     S3DSP_LAUNCH_CHECK("export_dense_kernel");
     return S3D_OK;
 }
@@ -604,8 +618,9 @@ extern "C" S3DSP_API s3d_status s3dsp_kmap_pairs(s3dsp_context* ctx, const s3dsp
         return cuda_fail(error, error_capacity, e, "pairs scratch");
     }
     if (nblk > 0)
-        pair_count_kernel<<<dim3((unsigned)nblk, k->kvol), kPairBlock, 0, ctx->stream>>>(k->nbr, k->n_out, counts, nblk);
-    pair_scan_kernel<<<1, 1024, 0, ctx->stream>>>(counts, m, starts);
+        launch_pdl(pair_count_kernel, dim3((unsigned)nblk, k->kvol), dim3(kPairBlock), 0, ctx->stream, k->nbr,
+                   k->n_out, counts, nblk);
+    launch_pdl(pair_scan_kernel, dim3(1), dim3(1024), 0, ctx->stream, counts, m, starts);
     // per-offset starts = starts[o * nblk]
     int64_t* host_starts = new int64_t[(size_t)m + 1];
     e = cudaMemcpyAsync(host_starts, starts, sizeof(int64_t) * (size_t)(m + 1), cudaMemcpyDeviceToHost, ctx->stream);
@@ -620,8 +635,8 @@ extern "C" S3DSP_API s3d_status s3dsp_kmap_pairs(s3dsp_context* ctx, const s3dsp
         for (int o = 0; o < k->kvol; ++o) h_offsets[o] = host_starts[o * nblk];
         h_offsets[k->kvol] = host_starts[m];
         if (nblk > 0)
-            pair_write_kernel<<<dim3((unsigned)nblk, k->kvol), kPairBlock, 0, ctx->stream>>>(
-                k->nbr, k->n_out, starts, nblk, d_in, d_out);
+            launch_pdl(pair_write_kernel, dim3((unsigned)nblk, k->kvol), dim3(kPairBlock), 0, ctx->stream,
+                       k->nbr, k->n_out, starts, nblk, d_in, d_out);
         e = cudaGetLastError();
         if (e != cudaSuccess) st = cuda_fail(error, error_capacity, e, "pair_write_kernel");
     }
@@ -651,9 +666,10 @@ extern "C" S3DSP_API s3d_status s3dsp_kmap_pairs_noalloc(s3dsp_context* ctx, con
     const int64_t nblk = (k->n_out + kPairBlock - 1) / kPairBlock;
     const int64_t m = nblk * k->kvol;
     if (nblk > 0)
-        pair_count_kernel<<<dim3((unsigned)nblk, k->kvol), kPairBlock, 0, ctx->stream>>>(k->nbr, k->n_out, counts, nblk);
-    pair_scan_kernel<<<1, 1024, 0, ctx->stream>>>(counts, m, starts);
-    pair_offsets_kernel<<<1, 32, 0, ctx->stream>>>(starts, nblk, k->kvol, m, offs);
+        launch_pdl(pair_count_kernel, dim3((unsigned)nblk, k->kvol), dim3(kPairBlock), 0, ctx->stream, k->nbr,
+                   k->n_out, counts, nblk);
+    launch_pdl(pair_scan_kernel, dim3(1), dim3(1024), 0, ctx->stream, counts, m, starts);
+    launch_pdl(pair_offsets_kernel, dim3(1), dim3(32), 0, ctx->stream, starts, nblk, k->kvol, m, offs);
     S3DSP_LAUNCH_CHECK("pair count/scan kernels");
     S3DSP_CUDA(cudaMemcpyAsync(h_offsets, offs, sizeof(int64_t) * (size_t)(k->kvol + 1), cudaMemcpyDeviceToHost,
                                ctx->stream),
@@ -663,8 +679,8 @@ extern "C" S3DSP_API s3d_status s3dsp_kmap_pairs_noalloc(s3dsp_context* ctx, con
         return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "pair capacity %lld < %lld needed",
                     (long long)capacity, (long long)h_offsets[k->kvol]);
     if (nblk > 0)
-        pair_write_kernel<<<dim3((unsigned)nblk, k->kvol), kPairBlock, 0, ctx->stream>>>(k->nbr, k->n_out, starts,
-                                                                                         nblk, d_in, d_out);
+        launch_pdl(pair_write_kernel, dim3((unsigned)nblk, k->kvol), dim3(kPairBlock), 0, ctx->stream, k->nbr,
+                   k->n_out, starts, nblk, d_in, d_out);
     S3DSP_LAUNCH_CHECK("pair_write_kernel");
     return S3D_OK;
 }

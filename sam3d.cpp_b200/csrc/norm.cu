@@ -34,6 +34,8 @@ __device__ __forceinline__ float silu_f(float v) { return v / (1.0f + __expf(-v)
 // group written (not accumulated) to partials[tile][g][2]
 __global__ void gn_stats_kernel(const void* __restrict__ x, uint32_t dt, int64_t n, int c, int groups,
                                 double* __restrict__ partials) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ double acc[64][2];
     for (int i = threadIdx.x; i < 128; i += blockDim.x) (&acc[0][0])[i] = 0.0;
     __syncthreads();
@@ -100,6 +102,8 @@ __global__ void gn_finalize_kernel(const double* __restrict__ partials, int64_t 
 __global__ void channel_affine_kernel(const void* __restrict__ x, uint32_t xd, int64_t n, int c,
                                       const float* __restrict__ sub, const float* __restrict__ mul,
                                       const float* __restrict__ add, int silu, void* __restrict__ y, uint32_t yd) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t total = n * c;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         const int ch = (int)(i % c);
@@ -163,6 +167,8 @@ __global__ void layer_norm_kernel(const void* __restrict__ x, uint32_t xd, int64
                                   const float* __restrict__ gamma, const float* __restrict__ beta,
                                   const float* __restrict__ ms, const float* __restrict__ msh, int silu,
                                   void* __restrict__ y, uint32_t yd) {
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int64_t row = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= n) return;
@@ -191,6 +197,8 @@ __global__ void layer_norm_kernel(const void* __restrict__ x, uint32_t xd, int64
 
 __global__ void convert_kernel(const void* __restrict__ x, uint32_t xd, void* __restrict__ y, uint32_t yd,
                                int64_t count) {
+    pdl_wait();
+    pdl_trigger();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x)
         st_f(y, yd, i, ld_f(x, xd, i));
 }
@@ -235,6 +243,8 @@ __device__ __forceinline__ void tf32_split(float x, float& hi, float& lo) {
 
 __global__ void pack_kernel(const void* __restrict__ src, uint32_t sd, uint32_t layout, int kvol, int cin,
                             int cout, uint32_t prec, int cin_pad, int cout_pad, void* __restrict__ dst) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t total = (int64_t)kvol * cin_pad * cout_pad;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         int o, ci, co;
@@ -274,6 +284,8 @@ __global__ void pack_kernel(const void* __restrict__ src, uint32_t sd, uint32_t 
 
 __global__ void split_tf32_kernel(const float* __restrict__ x, int64_t n, float* __restrict__ hi,
                                   float* __restrict__ lo) {
+    pdl_wait();
+    pdl_trigger();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         float h, l;
         tf32_split(__ldg(x + i), h, l);
@@ -309,7 +321,8 @@ extern "C" S3DSP_API s3d_status s3dsp_gn_stats(s3dsp_context* ctx, const void* x
                     (long long)n, (long long)c, groups);
     S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
     const int64_t tiles = (n + 127) / 128;
-    gn_stats_kernel<<<(unsigned)tiles, 256, 0, ctx->stream>>>(x, dtype, n, (int)c, groups, partials);
+    launch_pdl(gn_stats_kernel, dim3((unsigned)tiles), dim3(256), 0, ctx->stream, x, dtype, n, (int)c, groups,
+               partials);
     S3DSP_LAUNCH_CHECK("gn_stats_kernel");
     return S3D_OK;
 }
@@ -352,8 +365,8 @@ extern "C" S3DSP_API s3d_status s3dsp_channel_affine(s3dsp_context* ctx, const v
                               reinterpret_cast<const float4*>(add), (int)silu, reinterpret_cast<uint4*>(y)),
                    "channel_affine_f32_bf16_kernel");
     } else {
-        channel_affine_kernel<<<grid_for(n * c, 256, ctx->sm_count), 256, 0, ctx->stream>>>(x, xd, n, (int)c, sub, mul,
-                                                                                          add, silu, y, yd);
+        launch_pdl(channel_affine_kernel, dim3(grid_for(n * c, 256, ctx->sm_count)), dim3(256), 0, ctx->stream, x, xd,
+                   n, (int)c, sub, mul, add, silu, y, yd);
     }
     S3DSP_LAUNCH_CHECK("channel_affine_kernel");
     return S3D_OK;
@@ -370,8 +383,8 @@ extern "C" S3DSP_API s3d_status s3dsp_layer_norm(s3dsp_context* ctx, const void*
     if (n == 0) return S3D_OK;
     S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
     const int64_t blocks = (n + 7) / 8;
-    layer_norm_kernel<<<(unsigned)blocks, 256, 0, ctx->stream>>>(x, xd, n, (int)c, eps, gamma, beta, ms, msh, silu, y,
-                                                                 yd);
+    launch_pdl(layer_norm_kernel, dim3((unsigned)blocks), dim3(256), 0, ctx->stream, x, xd, n, (int)c, eps, gamma,
+               beta, ms, msh, silu, y, yd);
     S3DSP_LAUNCH_CHECK("layer_norm_kernel");
     return S3D_OK;
 }
@@ -390,7 +403,8 @@ extern "C" S3DSP_API s3d_status s3dsp_convert(s3dsp_context* ctx, const void* x,
                               (int64_t)(count / 4)),
                    "convert_f32_bf16_kernel");
     else
-        convert_kernel<<<grid_for(count, 256, ctx->sm_count), 256, 0, ctx->stream>>>(x, xd, y, yd, count);
+        launch_pdl(convert_kernel, dim3(grid_for(count, 256, ctx->sm_count)), dim3(256), 0, ctx->stream, x, xd, y, yd,
+                   count);
     S3DSP_LAUNCH_CHECK("convert_kernel");
     return S3D_OK;
 }
@@ -449,8 +463,8 @@ extern "C" S3DSP_API s3d_status s3dsp_weights_pack(s3dsp_context* ctx, const voi
         dsrc = staged;
     }
     const int64_t total = (int64_t)kvol * cp * op;
-    pack_kernel<<<grid_for(total, 256, ctx->sm_count), 256, 0, ctx->stream>>>(dsrc, sd, layout, kvol, (int)cin,
-                                                                             (int)cout, prec, (int)cp, (int)op, dst);
+    launch_pdl(pack_kernel, dim3(grid_for(total, 256, ctx->sm_count)), dim3(256), 0, ctx->stream, dsrc, sd, layout,
+               kvol, (int)cin, (int)cout, prec, (int)cp, (int)op, dst);
     cudaError_t e = cudaGetLastError();
     if (staged) cudaFreeAsync(staged, ctx->stream);
     if (e != cudaSuccess) return cuda_fail(error, error_capacity, e, "pack_kernel");
@@ -461,7 +475,7 @@ extern "C" S3DSP_API s3d_status s3dsp_weights_pack(s3dsp_context* ctx, const voi
 namespace s3dsp {
 cudaError_t split_tf32(s3dsp_context* ctx, const float* x, int64_t n, float* hi, float* lo) {
     if (n <= 0) return cudaSuccess;
-    split_tf32_kernel<<<grid_for(n, 256, ctx->sm_count), 256, 0, ctx->stream>>>(x, n, hi, lo);
+    launch_pdl(split_tf32_kernel, dim3(grid_for(n, 256, ctx->sm_count)), dim3(256), 0, ctx->stream, x, n, hi, lo);
     return cudaGetLastError();
 }
 }  // namespace s3dsp

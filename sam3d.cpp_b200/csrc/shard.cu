@@ -134,6 +134,8 @@ const NcclApi& nccl_api() {
 
 __global__ void gather_rows_kernel(const uint8_t* __restrict__ x, const int32_t* __restrict__ rows, int64_t n_rows,
                                    int64_t row_bytes, uint8_t* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     // 16-byte words when rows allow it, else bytes
     if ((row_bytes & 15) == 0) {
         const int64_t words = row_bytes >> 4;
@@ -343,7 +345,8 @@ S3DSP_API s3d_status s3dsp_halo_exchange(s3dsp_context* ctx, s3dsp_shard* p, voi
         const int64_t work = (row_bytes & 15) == 0 ? n_send * (row_bytes >> 4) : n_send * row_bytes;
         int64_t g = (work + 255) / 256;
         if (g > ctx->sm_count * 8) g = ctx->sm_count * 8;
-        gather_rows_kernel<<<(int)(g < 1 ? 1 : g), 256, 0, st>>>(x, p->d_send, n_send, row_bytes, send);
+        launch_pdl(gather_rows_kernel, dim3((int)(g < 1 ? 1 : g)), dim3(256), 0, st, x, p->d_send, n_send, row_bytes,
+                   send);
         const cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) {
             cudaFreeAsync(send, st);

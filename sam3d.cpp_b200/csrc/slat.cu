@@ -35,6 +35,8 @@ __device__ __forceinline__ bool pack_key(int32_t b, int32_t x, int32_t y, int32_
 
 __global__ void coarse_key_kernel(const int4* __restrict__ coords, int64_t n, unsigned long long* __restrict__ keys,
                                   int32_t* __restrict__ rows, uint32_t* status) {
+    pdl_wait();
+    pdl_trigger();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         const int4 c = coords[i];
         unsigned long long k;
@@ -50,6 +52,8 @@ __global__ void coarse_key_kernel(const int4* __restrict__ coords, int64_t n, un
 
 // head[i] = 1 where a new coarse key starts in the sorted order
 __global__ void run_head_kernel(const unsigned long long* __restrict__ skeys, int64_t n, int32_t* __restrict__ head) {
+    pdl_wait();
+    pdl_trigger();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         head[i] = (i == 0 || skeys[i] != skeys[i - 1]) ? 1 : 0;
 }
@@ -59,6 +63,8 @@ __global__ void run_scatter_kernel(const unsigned long long* __restrict__ skeys,
                                    const int32_t* __restrict__ head, const int32_t* __restrict__ incl, int64_t n,
                                    int32_t* __restrict__ run_start, int4* __restrict__ ccoords,
                                    int32_t* __restrict__ f2c) {
+    pdl_wait();
+    pdl_trigger();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         const int32_t c = incl[i] - 1;
         f2c[srows[i]] = c;
@@ -75,6 +81,8 @@ __global__ void run_scatter_kernel(const unsigned long long* __restrict__ skeys,
 // stable and rows entered in ascending order) and 1/(count+1)
 __global__ void children_kernel(const int32_t* __restrict__ srows, const int32_t* __restrict__ run_start, int64_t nc,
                                 int64_t nf, int32_t* __restrict__ children, float* __restrict__ inv) {
+    pdl_wait();
+    pdl_trigger();
     for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < nc; c += (int64_t)gridDim.x * blockDim.x) {
         const int32_t b = run_start[c];
         const int32_t e = c + 1 < nc ? run_start[c + 1] : (int32_t)nf;
@@ -103,6 +111,8 @@ __device__ __forceinline__ void stf(void* p, uint32_t dt, int64_t i, float v) {
 // (slat_flow_graph.cpp:159-183); sentinel slots read zeros
 __global__ void downsample_kernel(const void* __restrict__ x, uint32_t xd, int64_t nf, int c, const int32_t* __restrict__ ch,
                                   const float* __restrict__ inv, int64_t nc, void* __restrict__ y, uint32_t yd) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t total = nc * c;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = i / c;
@@ -121,6 +131,8 @@ __global__ void downsample_kernel(const void* __restrict__ x, uint32_t xd, int64
 // out[i] = x[f2c[i]] (slat_flow_graph.cpp:186-190)
 __global__ void upsample_kernel(const void* __restrict__ x, uint32_t xd, int64_t nc, int c, const int32_t* __restrict__ f2c,
                                 int64_t nf, void* __restrict__ y, uint32_t yd) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t total = nf * c;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = i / c;
@@ -184,16 +196,17 @@ extern "C" S3DSP_API s3d_status s3dsp_slat_tables_build(s3dsp_context* ctx, cons
     int32_t nc = 0;
     if (e == cudaSuccess) {
         const int g = grid_for(n, 256, ctx->sm_count);
-        coarse_key_kernel<<<g, 256, 0, st>>>(reinterpret_cast<const int4*>(fine->coords), n, keys, rows, ctx->d_status);
+        launch_pdl(coarse_key_kernel, dim3(g), dim3(256), 0, st, reinterpret_cast<const int4*>(fine->coords), n, keys,
+                   rows, ctx->d_status);
         size_t tb = temp_bytes;
         e = cub::DeviceRadixSort::SortPairs(temp, tb, keys, skeys, rows, srows, (int)n, 0, 64, st);
         if (e == cudaSuccess) {
-            run_head_kernel<<<g, 256, 0, st>>>(skeys, n, head);
+            launch_pdl(run_head_kernel, dim3(g), dim3(256), 0, st, skeys, n, head);
             tb = temp_bytes;
             e = cub::DeviceScan::InclusiveSum(temp, tb, head, incl, (int)n, st);
         }
         if (e == cudaSuccess) {
-            run_scatter_kernel<<<g, 256, 0, st>>>(skeys, srows, head, incl, n, run_start,
+            launch_pdl(run_scatter_kernel, dim3(g), dim3(256), 0, st, skeys, srows, head, incl, n, run_start,
                                                   reinterpret_cast<int4*>(t->coarse_coords), t->fine_to_coarse);
             e = cudaMemcpyAsync(&nc, incl + (n - 1), 4, cudaMemcpyDeviceToHost, st);
         }
@@ -207,8 +220,8 @@ extern "C" S3DSP_API s3d_status s3dsp_slat_tables_build(s3dsp_context* ctx, cons
         e = cudaMallocAsync(&t->coarse_children, (size_t)nc * 8 * 4, st);
         if (e == cudaSuccess) e = cudaMallocAsync(&t->coarse_inv_count, (size_t)nc * 4, st);
         if (e == cudaSuccess) {
-            children_kernel<<<grid_for(nc, 256, ctx->sm_count), 256, 0, st>>>(srows, run_start, nc, n,
-                                                                             t->coarse_children, t->coarse_inv_count);
+            launch_pdl(children_kernel, dim3(grid_for(nc, 256, ctx->sm_count)), dim3(256), 0, st, srows, run_start,
+                       nc, n, t->coarse_children, t->coarse_inv_count);
             e = cudaGetLastError();
         }
     }
@@ -261,8 +274,8 @@ extern "C" S3DSP_API s3d_status s3dsp_slat_downsample(s3dsp_context* ctx, const 
     if (!ctx || !t || !x || !y) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
     if (!dtype_ok(x_dtype) || !dtype_ok(y_dtype) || c <= 0) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "bad dtype/channels");
     S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
-    downsample_kernel<<<grid_for(t->nc * c, 256, ctx->sm_count), 256, 0, ctx->stream>>>(
-        x, x_dtype, t->nf, (int)c, t->coarse_children, t->coarse_inv_count, t->nc, y, y_dtype);
+    launch_pdl(downsample_kernel, dim3(grid_for(t->nc * c, 256, ctx->sm_count)), dim3(256), 0, ctx->stream, x,
+               x_dtype, t->nf, (int)c, t->coarse_children, t->coarse_inv_count, t->nc, y, y_dtype);
     S3DSP_LAUNCH_CHECK("downsample_kernel");
     return S3D_OK;
 }
@@ -274,8 +287,8 @@ extern "C" S3DSP_API s3d_status s3dsp_slat_upsample(s3dsp_context* ctx, const s3
     if (!ctx || !t || !x || !y) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
     if (!dtype_ok(x_dtype) || !dtype_ok(y_dtype) || c <= 0) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "bad dtype/channels");
     S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
-    upsample_kernel<<<grid_for(t->nf * c, 256, ctx->sm_count), 256, 0, ctx->stream>>>(x, x_dtype, t->nc, (int)c,
-                                                                                    t->fine_to_coarse, t->nf, y, y_dtype);
+    launch_pdl(upsample_kernel, dim3(grid_for(t->nf * c, 256, ctx->sm_count)), dim3(256), 0, ctx->stream, x, x_dtype,
+               t->nc, (int)c, t->fine_to_coarse, t->nf, y, y_dtype);
     S3DSP_LAUNCH_CHECK("upsample_kernel");
     return S3D_OK;
 }
