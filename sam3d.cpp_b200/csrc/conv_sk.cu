@@ -445,18 +445,31 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
                         const int64_t t128 = kSub * st + sub;
                         const int g_lo = n0 / gs;
                         const int g_hi = min(p.gn_groups - 1, (n0 + limit - 1) / gs);
-                        for (int g = g_lo + tid; g <= g_hi; g += kEpiThreads) {
-                            const int c_lo = max(g * gs - n0, 0), c_hi = min((g + 1) * gs - n0, limit);
+                        // 16 lanes per group (lane w: warp w's columns), fixed shuffle tree
+                        const int items = (g_hi - g_lo + 1) * kProdWarps;
+                        for (int base = 0; base < items; base += kEpiThreads) {  // warp-uniform
+                            const int idx = base + tid;
+                            const int g = g_lo + idx / kProdWarps, w = idx % kProdWarps;
+                            const bool act = idx < items;
                             double a = 0.0, b = 0.0;
-                            for (int w = 0; w < kProdWarps; ++w)
+                            if (act) {
+                                const int c_lo = max(g * gs - n0, 0), c_hi = min((g + 1) * gs - n0, limit);
                                 for (int c = c_lo; c < c_hi; ++c) {
                                     a += colp[((size_t)w * p.bn + c) * 2 + 0];
                                     b += colp[((size_t)w * p.bn + c) * 2 + 1];
                                 }
+                            }
+#pragma unroll
+                            for (int off = kProdWarps / 2; off > 0; off >>= 1) {
+                                a += __shfl_down_sync(0xffffffffu, a, off, kProdWarps);
+                                b += __shfl_down_sync(0xffffffffu, b, off, kProdWarps);
+                            }
                             // a group split across two column blocks gets exactly two adds
                             // onto a zeroed slot, which is order independent
-                            atomicAdd(p.gn_partials + (t128 * p.gn_groups + g) * 2 + 0, a);
-                            atomicAdd(p.gn_partials + (t128 * p.gn_groups + g) * 2 + 1, b);
+                            if (act && w == 0) {
+                                atomicAdd(p.gn_partials + (t128 * p.gn_groups + g) * 2 + 0, a);
+                                atomicAdd(p.gn_partials + (t128 * p.gn_groups + g) * 2 + 1, b);
+                            }
                         }
                     }
                     epi_bar();  // the tile and column sums are reused by the next subtile

@@ -340,6 +340,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             cp_async_arrive_noinc(smem_u32(full + s * kFS + warp / (kProdWarps / kFS)));
         }
+        if (p.residual && tile < p.n_tiles) {
+            // the epilogue reads this tile's residual rows: start bringing them
+            // into L2 now, while the last stages are still in flight
+            const int esz = p.res_dtype == S3DSP_F32 ? 4 : 2;
+            const int64_t r = m0 + (tid >> 2);
+            const int len = min(p.bn, p.cout - n0) * esz;
+            if (r < p.n_out) {
+                const char* row = static_cast<const char*>(p.residual) +
+                                  (((r >> p.res_shift) * p.cout + n0) * (int64_t)esz);
+                for (int b = (tid & 3) * 128; b < len; b += 4 * 128)
+                    asm volatile("prefetch.global.L2 [%0];" ::"l"(row + b));
+            }
+        }
         asm volatile("cp.async.wait_all;" ::: "memory");
     } else if (warp < kBWarp0 + kMaxBWarps) {
         // ================= weight TMA issuers =================
@@ -537,30 +550,43 @@ __global__ void __launch_bounds__(kThreads, 1)
                 writeout_generic(p, stage_out, ostride, lane_base, lane, m0, n0, limit, nrows, bias4, stats ? colw : nullptr);
         }
         if (stats) {
-            // deterministic GroupNorm partials: per-warp column sums to smem,
-            // then each group summed over warps and columns in a fixed order
+            // deterministic GroupNorm partials: per-warp column sums to smem;
+            // 16 lanes per group, lane w summing warp w's columns of the group,
+            // then a fixed shuffle tree over the 16 warps
             epi_bar();
-            const int et = tid;
             const int g_lo = n0 / gs;
             const int g_hi = min(p.gn_groups - 1, (n0 + limit - 1) / gs);
-            // the padding CTA of an odd pair count (tile == n_tiles) has no rows and no slot
-            for (int g = g_lo + et; tile < p.n_tiles && g <= g_hi; g += kProdWarps * 32) {
-                const int c_lo = max(g * gs - n0, 0), c_hi = min((g + 1) * gs - n0, limit);
+            const int items = (g_hi - g_lo + 1) * kProdWarps;
+            // warp-uniform trip count: every lane of a warp takes part in the shuffles
+            for (int base = 0; base < items; base += kProdWarps * 32) {
+                const int idx = base + tid;
+                const int g = g_lo + idx / kProdWarps, w = idx % kProdWarps;
+                // the padding CTA of an odd pair count (tile == n_tiles) has no rows and no slot
+                const bool act = tile < p.n_tiles && idx < items;
                 double a = 0.0, b = 0.0;
-                for (int w = 0; w < kProdWarps; ++w)
+                if (act) {
+                    const int c_lo = max(g * gs - n0, 0), c_hi = min((g + 1) * gs - n0, limit);
                     for (int c = c_lo; c < c_hi; ++c) {
                         a += colp[((size_t)w * p.bn + c) * 2 + 0];
                         b += colp[((size_t)w * p.bn + c) * 2 + 1];
                     }
-                double* slot = p.gn_partials + ((int64_t)tile * p.gn_groups + g) * 2;
-                if (p.gn_store) {
-                    slot[0] = a;
-                    slot[1] = b;
-                } else {
-                    // a group split across two column tiles gets exactly two
-                    // adds onto a zeroed slot, which is order independent
-                    atomicAdd(slot + 0, a);
-                    atomicAdd(slot + 1, b);
+                }
+#pragma unroll
+                for (int off = kProdWarps / 2; off > 0; off >>= 1) {
+                    a += __shfl_down_sync(0xffffffffu, a, off, kProdWarps);
+                    b += __shfl_down_sync(0xffffffffu, b, off, kProdWarps);
+                }
+                if (act && w == 0) {
+                    double* slot = p.gn_partials + ((int64_t)tile * p.gn_groups + g) * 2;
+                    if (p.gn_store) {
+                        slot[0] = a;
+                        slot[1] = b;
+                    } else {
+                        // a group split across two column tiles gets exactly two
+                        // adds onto a zeroed slot, which is order independent
+                        atomicAdd(slot + 0, a);
+                        atomicAdd(slot + 1, b);
+                    }
                 }
             }
         }
