@@ -292,6 +292,21 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
         }
         it += (uint32_t)T;
 
+        if (warp < kProdWarps && p.residual) {
+            // the epilogue reads this work tile's residual rows: start bringing
+            // them into L2 while the last MMAs finish
+            const int esz = p.res_dtype == S3DSP_F32 ? 4 : 2;
+            constexpr int kTpr = kEpiThreads / kRows;  // threads per row
+            const int64_t r = m0 + tid / kTpr;
+            const int len = min(p.bn, p.cout - n0) * esz;
+            if (r < p.n_out) {
+                const char* row = static_cast<const char*>(p.residual) +
+                                  (((r >> p.res_shift) * p.cout + n0) * (int64_t)esz);
+                for (int b = (tid % kTpr) * 128; b < len; b += kTpr * 128)
+                    asm volatile("prefetch.global.L2 [%0];" ::"l"(row + b));
+            }
+        }
+
         if (warp < kProdWarps) {
             // ============ epilogue (warps 0-15) ============
             bool have_acc = false;
