@@ -29,6 +29,9 @@ __device__ __forceinline__ void st_f(void* p, uint32_t dt, int64_t i, float v) {
         reinterpret_cast<__half*>(p)[i] = __float2half(v);
 }
 __device__ __forceinline__ float silu_f(float v) { return v / (1.0f + __expf(-v)); }
+// for a bf16 result: the approximate divide's error is far below bf16 rounding
+// (1 + exp(-v) is >= 1, and +inf for v < -88, where the quotient is 0)
+__device__ __forceinline__ float silu_fast(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
 
 // stats of x [n, c]: one block per 128-row tile; block-local double sums per
 // group written (not accumulated) to partials[tile][g][2]
@@ -125,6 +128,7 @@ __global__ void channel_affine_f32_bf16_kernel(const float4* __restrict__ x, int
     pdl_trigger();
     constexpr int U = 4;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const bool narrow = total8 <= 0xffffffffll;
     for (int64_t i0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < total8; i0 += stride * U) {
         float4 a[U], b[U];
 #pragma unroll
@@ -139,7 +143,8 @@ __global__ void channel_affine_f32_bf16_kernel(const float4* __restrict__ x, int
         for (int u = 0; u < U; ++u) {
             const int64_t i = i0 + u * stride;
             if (i >= total8) break;
-            const uint32_t q8 = (uint32_t)((uint64_t)i % c8);  // 8-channel group within the row
+            // 8-channel group within the row (32-bit remainder when the index fits)
+            const uint32_t q8 = narrow ? (uint32_t)i % c8 : (uint32_t)((uint64_t)i % c8);
             const float4 s0 = __ldg(sub + 2 * q8), s1 = __ldg(sub + 2 * q8 + 1);
             const float4 m0 = __ldg(mul + 2 * q8), m1 = __ldg(mul + 2 * q8 + 1);
             const float4 d0 = __ldg(add + 2 * q8), d1 = __ldg(add + 2 * q8 + 1);
@@ -148,7 +153,7 @@ __global__ void channel_affine_f32_bf16_kernel(const float4* __restrict__ x, int
                           (b[u].z - s1.z) * m1.z + d1.z, (b[u].w - s1.w) * m1.w + d1.w};
             if (silu) {
 #pragma unroll
-                for (int q = 0; q < 8; ++q) v[q] = silu_f(v[q]);
+                for (int q = 0; q < 8; ++q) v[q] = silu_fast(v[q]);
             }
             uint32_t w[4];
 #pragma unroll
