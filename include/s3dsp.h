@@ -109,6 +109,19 @@ S3DSP_API void *s3dsp_context_stream(const s3dsp_context *ctx);
  * error recorded since the last check. */
 S3DSP_API s3d_status s3dsp_context_check(s3dsp_context *ctx, char *error, uint64_t error_capacity);
 
+/* Device memory the library holds on `device`. Every table, map and scratch
+ * buffer the library allocates comes from its own stream-ordered pool (made
+ * by the first s3dsp_context_create on the device; memory freed by the
+ * library stays in that pool for reuse). The device's default pool, which
+ * the host process may use, is left as it was. Reports the pool's reserved
+ * bytes, bytes in use and the high-water mark of bytes in use (any pointer
+ * may be NULL); reset_high != 0 then resets that mark to the current use.
+ * The reference reserves graph memory through GGML's allocator per stage
+ * (backend.cpp:44-118); this is the counterpart for accounting. */
+S3DSP_API s3d_status s3dsp_memory_stats(int32_t device, uint64_t *reserved, uint64_t *used,
+                                        uint64_t *used_high, int32_t reset_high, char *error,
+                                        uint64_t error_capacity);
+
 /* ---------------------------------------------------------------------------
  * Coordinate hash. Replaces the std::map / unordered_map indexes of
  * SlatTables::build (sparse_ops.cpp:119-124) and MeshSubdivideTables::build
@@ -366,7 +379,8 @@ S3DSP_API s3d_status s3dsp_kmap_export_dense(s3dsp_context *ctx, const s3dsp_kma
 /* Offset-sorted (in, out) pair lists: for each offset o in order, the pairs
  * with a neighbour, sorted by output row. d_in/d_out hold capacity int32
  * each (27*n_out always suffices); h_offsets receives kvol+1 host int64
- * start offsets. Synchronous. */
+ * start offsets. Synchronous: the call waits for the context's stream, so the
+ * lists are complete when it returns. */
 S3DSP_API s3d_status s3dsp_kmap_pairs(s3dsp_context *ctx, const s3dsp_kmap *kmap, int32_t *d_in,
                                       int32_t *d_out, int64_t capacity, int64_t *h_offsets,
                                       char *error, uint64_t error_capacity);
@@ -378,10 +392,13 @@ S3DSP_API s3d_status s3dsp_kmap_pairs(s3dsp_context *ctx, const s3dsp_kmap *kmap
  * the host). Same arguments and results as s3dsp_kmap_pairs; its scratch is a
  * static device array in the library, so the map may have at most 2^21
  * (2,097,152) output rows — larger maps fail with S3D_INVALID_ARGUMENT.
- * The first call on each device looks up that array's device address; make
- * it before any stream capture. All calls on a device share the array:
+ * The kernel map may have at most 27 offsets. Every call looks up that
+ * array's device address (cudaGetSymbolAddress); make the first call on a
+ * device before any stream capture. All calls on a device share the array:
  * calls whose GPU work overlaps (different streams, concurrent contexts)
- * race and must be ordered by the caller. Synchronous, like s3dsp_kmap_pairs. */
+ * race and must be ordered by the caller. Synchronous, like s3dsp_kmap_pairs:
+ * the call waits for its last kernel on the context's stream, so two calls
+ * the host has ordered never overlap on the GPU. */
 S3DSP_API s3d_status s3dsp_kmap_pairs_noalloc(s3dsp_context *ctx, const s3dsp_kmap *kmap,
                                               int32_t *d_in, int32_t *d_out, int64_t capacity,
                                               int64_t *h_offsets, char *error,

@@ -1,7 +1,40 @@
 // Context management and status reporting for the s3dsp C ABI.
+#include <mutex>
+
 #include "s3dsp_internal.h"
 
 using namespace s3dsp;
+
+namespace s3dsp {
+namespace {
+std::mutex g_pool_mu;
+cudaMemPool_t g_pools[64] = {};
+}  // namespace
+
+cudaError_t lib_pool(int device, cudaMemPool_t* out) {
+    if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(g_pool_mu);
+    if (!g_pools[device]) {
+        cudaMemPoolProps props = {};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.handleTypes = cudaMemHandleTypeNone;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = device;
+        cudaMemPool_t pool;
+        cudaError_t e = cudaMemPoolCreate(&pool, &props);
+        if (e != cudaSuccess) return e;
+        uint64_t keep = ~0ull;
+        e = cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+        if (e != cudaSuccess) {
+            cudaMemPoolDestroy(pool);
+            return e;
+        }
+        g_pools[device] = pool;
+    }
+    *out = g_pools[device];
+    return cudaSuccess;
+}
+}  // namespace s3dsp
 
 extern "C" S3DSP_API uint32_t s3dsp_abi_version(void) { return 1u; }
 
@@ -38,15 +71,14 @@ extern "C" S3DSP_API s3d_status s3dsp_context_create(int32_t device, void* strea
         }
         ctx->owns_stream = true;
     }
-    // Keep memory freed by cudaFreeAsync in the device pool instead of
-    // returning it at every synchronisation: hash tables and kernel maps are
-    // rebuilt per object, and re-mapping pool memory costs milliseconds.
+    // the library's private pool (the host's default pool keeps its policy)
     cudaMemPool_t pool;
-    if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess) {
-        uint64_t keep = ~0ull;
-        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    cudaError_t e = lib_pool(device, &pool);
+    if (e != cudaSuccess) {
+        s3dsp_context_free(ctx);
+        return cuda_fail(error, error_capacity, e, "library memory pool");
     }
-    cudaError_t e = cudaMalloc(&ctx->d_status, 4 * sizeof(uint32_t));
+    e = cudaMalloc(&ctx->d_status, 4 * sizeof(uint32_t));
     if (e == cudaSuccess) e = cudaMemsetAsync(ctx->d_status, 0, 4 * sizeof(uint32_t), ctx->stream);
     if (e != cudaSuccess) {
         s3dsp_context_free(ctx);
@@ -99,4 +131,34 @@ extern "C" S3DSP_API s3d_status s3dsp_context_check(s3dsp_context* ctx, char* er
     if (!ctx) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "ctx is NULL");
     S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
     return check_status(ctx, error, error_capacity);
+}
+
+extern "C" S3DSP_API s3d_status s3dsp_memory_stats(int32_t device, uint64_t* reserved, uint64_t* used,
+                                                  uint64_t* used_high, int32_t reset_high, char* error,
+                                                  uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    int count = 0;
+    S3DSP_CUDA(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
+    if (device < 0 || device >= count || device >= 64)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "device %d out of range [0,%d)", device, count);
+    cudaMemPool_t pool;
+    S3DSP_CUDA(lib_pool(device, &pool), "library memory pool");
+    cuuint64_t v = 0;
+    if (reserved) {
+        S3DSP_CUDA(cudaMemPoolGetAttribute(pool, cudaMemPoolAttrReservedMemCurrent, &v), "pool attribute");
+        *reserved = v;
+    }
+    if (used) {
+        S3DSP_CUDA(cudaMemPoolGetAttribute(pool, cudaMemPoolAttrUsedMemCurrent, &v), "pool attribute");
+        *used = v;
+    }
+    if (used_high) {
+        S3DSP_CUDA(cudaMemPoolGetAttribute(pool, cudaMemPoolAttrUsedMemHigh, &v), "pool attribute");
+        *used_high = v;
+    }
+    if (reset_high) {
+        v = 0;  // resets the high-water mark to the current use
+        S3DSP_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrUsedMemHigh, &v), "pool attribute");
+    }
+    return S3D_OK;
 }

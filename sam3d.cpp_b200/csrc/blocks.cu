@@ -25,7 +25,7 @@ struct Scratch {
     template <class T>
     cudaError_t get(T** p, size_t bytes) {
         void* q = nullptr;
-        const cudaError_t e = cudaMallocAsync(&q, bytes > 0 ? bytes : 16, st);
+        const cudaError_t e = s3dsp::malloc_async(&q, bytes > 0 ? bytes : 16, st);
         if (e != cudaSuccess) return e;
         ptrs[n++] = q;
         *p = static_cast<T*>(q);

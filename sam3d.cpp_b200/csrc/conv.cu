@@ -138,7 +138,7 @@ extern "C" S3DSP_API s3d_status s3dsp_conv(s3dsp_context* ctx, const s3dsp_kmap*
         // the input split once into TF32 high parts and remainders (stream-ordered scratch)
         const size_t nel = (size_t)n_in * (size_t)cin;
         float* split = nullptr;
-        S3DSP_CUDA(cudaMallocAsync(&split, 8 * (nel > 0 ? nel : 1), ctx->stream), "3xTF32 split buffer");
+        S3DSP_CUDA(s3dsp::malloc_async(&split, 8 * (nel > 0 ? nel : 1), ctx->stream), "3xTF32 split buffer");
         e = split_tf32(ctx, (const float*)in, (int64_t)nel, split, split + nel);
         s3d_status st = S3D_OK;
         if (e == cudaSuccess)

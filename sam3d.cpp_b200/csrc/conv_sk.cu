@@ -626,8 +626,8 @@ cudaError_t launch_conv_sk(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     void* ws = nullptr;
     void* counters = nullptr;
     if (split) {
-        e = cudaMallocAsync(&ws, (size_t)2 * grid * rows * bn * sizeof(float), s);
-        if (e == cudaSuccess) e = cudaMallocAsync(&counters, (size_t)work_tiles * sizeof(uint32_t), s);
+        e = s3dsp::malloc_async(&ws, (size_t)2 * grid * rows * bn * sizeof(float), s);
+        if (e == cudaSuccess) e = s3dsp::malloc_async(&counters, (size_t)work_tiles * sizeof(uint32_t), s);
         if (e == cudaSuccess) e = cudaMemsetAsync(counters, 0, (size_t)work_tiles * sizeof(uint32_t), s);
         if (e != cudaSuccess) {
             if (ws) cudaFreeAsync(ws, s);

@@ -145,7 +145,7 @@ struct Scratch {
     template <typename T>
     cudaError_t get(T** p, size_t bytes) {
         void* q = nullptr;
-        const cudaError_t e = cudaMallocAsync(&q, bytes > 0 ? bytes : 16, s);
+        const cudaError_t e = s3dsp::malloc_async(&q, bytes > 0 ? bytes : 16, s);
         if (e == cudaSuccess) ptrs.push_back(q);
         *p = static_cast<T*>(q);
         return e;

@@ -563,7 +563,7 @@ struct Scratch {
     template <typename T>
     cudaError_t get(T** p, size_t bytes) {
         void* q = nullptr;
-        const cudaError_t e = count < 32 ? cudaMallocAsync(&q, bytes > 0 ? bytes : 16, s) : cudaErrorMemoryAllocation;
+        const cudaError_t e = count < 32 ? s3dsp::malloc_async(&q, bytes > 0 ? bytes : 16, s) : cudaErrorMemoryAllocation;
         if (e == cudaSuccess) ptrs[count++] = q;
         *p = static_cast<T*>(q);
         return e;
@@ -705,7 +705,7 @@ extern "C" S3DSP_API s3d_status s3dsp_flexicubes_extract(s3dsp_context* ctx, con
     m->n_faces = 2 * nq;
     const auto alloc = [&](auto** p, size_t bytes) {
         void* q = nullptr;
-        const cudaError_t r = cudaMallocAsync(&q, bytes > 0 ? bytes : 16, st);
+        const cudaError_t r = s3dsp::malloc_async(&q, bytes > 0 ? bytes : 16, st);
         *p = static_cast<std::remove_reference_t<decltype(**p)>*>(q);
         return r;
     };

@@ -490,7 +490,7 @@ S3DSP_API s3d_status s3dsp_gguf_load(s3dsp_context* ctx, const s3dsp_gguf* g, in
     S3DSP_TRY(read_bytes(g->path, g->data_offset + t.offset, host.data(), t.nbytes, error, error_capacity));
     S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
     void* staged = nullptr;
-    S3DSP_CUDA(cudaMallocAsync(&staged, t.nbytes > 0 ? t.nbytes : 16, ctx->stream), "cudaMallocAsync");
+    S3DSP_CUDA(s3dsp::malloc_async(&staged, t.nbytes > 0 ? t.nbytes : 16, ctx->stream), "cudaMallocAsync");
     cudaError_t e = cudaMemcpyAsync(staged, host.data(), t.nbytes, cudaMemcpyHostToDevice, ctx->stream);
     s3d_status st = S3D_OK;
     if (e == cudaSuccess) st = dequantize_device(ctx, t.type, staged, n, dtype, d_out, error, error_capacity);
@@ -524,7 +524,7 @@ S3DSP_API s3d_status s3dsp_gguf_load_weights(s3dsp_context* ctx, const s3dsp_ggu
     const int64_t n = want0 * want1;
     S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
     float* f32 = nullptr;
-    S3DSP_CUDA(cudaMallocAsync(&f32, 4 * (size_t)n, ctx->stream), "cudaMallocAsync");
+    S3DSP_CUDA(s3dsp::malloc_async(&f32, 4 * (size_t)n, ctx->stream), "cudaMallocAsync");
     s3d_status st = s3dsp_gguf_load(ctx, g, index, S3DSP_F32, f32, n, error, error_capacity);
     if (st == S3D_OK)
         st = s3dsp_weights_pack(ctx, f32, S3DSP_F32, 0, layout, kvol, cin, cout, precision, d_dst, error,

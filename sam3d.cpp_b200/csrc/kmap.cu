@@ -172,8 +172,33 @@ __global__ void __launch_bounds__(kTileRows * kSlabs) kmap_subm3_kernel(const in
 // Child geometry of MeshSubdivideTables (sparse_ops.cpp:346-365): for child
 // bits j and offset o, which of the parent's 27 neighbours holds the target
 // child, and which of its 8 children it is.
-__constant__ uint8_t c_adj_parent[8][27];
-__constant__ uint8_t c_adj_child[8][27];
+// Child-adjacency tables of the subdivide map, fixed at compile time: for child
+// j (bits xb,yb,zb) and offset o (d = (o/9-1, (o/3)%3-1, o%3-1)), t = bit + d
+// per axis in [-1, 2]; the neighbour's parent is offset floor(t/2) from the
+// child's parent (par) and the neighbour is that parent's child t mod 2 (chl).
+struct AdjTables {
+    uint8_t par[8][27];
+    uint8_t chl[8][27];
+};
+constexpr AdjTables make_adjacency() {
+    AdjTables t{};
+    for (int j = 0; j < 8; ++j) {
+        const int bits[3] = {j >> 2, (j >> 1) & 1, j & 1};
+        for (int o = 0; o < 27; ++o) {
+            const int d[3] = {o / 9 - 1, (o / 3) % 3 - 1, o % 3 - 1};
+            int pd[3] = {0, 0, 0}, tb[3] = {0, 0, 0};
+            for (int a = 0; a < 3; ++a) {
+                const int v = bits[a] + d[a];
+                pd[a] = v < 0 ? -1 : (v > 1 ? 1 : 0);
+                tb[a] = v - 2 * pd[a];
+            }
+            t.par[j][o] = (uint8_t)((pd[0] + 1) * 9 + (pd[1] + 1) * 3 + (pd[2] + 1));
+            t.chl[j][o] = (uint8_t)(tb[0] * 4 + tb[1] * 2 + tb[2]);
+        }
+    }
+    return t;
+}
+__constant__ AdjTables c_adj = make_adjacency();
 
 // One block = 32 parents = 256 children. Phase 1: 27 probes per parent into
 // shared memory. Phase 2: 27 x 256 child entries written offset-major
@@ -209,8 +234,8 @@ __global__ void __launch_bounds__(256) subdivide_kernel(const int4* __restrict__
     for (int o = 0; o < 27; ++o) {
         int32_t v = -1;
         if (p < np) {
-            const int32_t tp = padj[pl][c_adj_parent[j][o]];
-            if (tp >= 0) v = tp * 8 + c_adj_child[j][o];
+            const int32_t tp = padj[pl][c_adj.par[j][o]];
+            if (tp >= 0) v = tp * 8 + c_adj.chl[j][o];
             nbr[o * nc + child] = v;
         }
         const unsigned any = __ballot_sync(0xffffffffu, v >= 0);
@@ -330,22 +355,16 @@ __global__ void pair_offsets_kernel(const int64_t* __restrict__ starts, int64_t 
     if (o == kvol) offs[kvol] = starts[m];
 }
 
-std::mutex g_noalloc_mu;
-void* g_noalloc_scratch[64] = {};
-
-// Device address of g_pairs_scratch for `device` (the current device). The
-// host-side name of the array is only a stand-in, so the address comes from
-// cudaGetSymbolAddress, once per device, and is cached.
-cudaError_t noalloc_scratch(int device, unsigned char** out) {
-    if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
-    std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (!g_noalloc_scratch[device]) {
-        void* ptr = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&ptr, g_pairs_scratch);
-        if (e != cudaSuccess) return e;
-        g_noalloc_scratch[device] = ptr;
-    }
-    *out = static_cast<unsigned char*>(g_noalloc_scratch[device]);
+// Device address of g_pairs_scratch on the current device. The host-side name
+// of the array is only a stand-in, so the address comes from
+// cudaGetSymbolAddress; it is looked up on every call (cheap after the first),
+// so a module reloaded after cudaDeviceReset is never addressed through a
+// stale pointer.
+cudaError_t noalloc_scratch(unsigned char** out) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_pairs_scratch);
+    if (e != cudaSuccess) return e;
+    *out = static_cast<unsigned char*>(ptr);
     return cudaSuccess;
 }
 
@@ -356,31 +375,6 @@ inline int grid_for(int64_t n, int threads, int sm_count) {
     return (int)(g < 1 ? 1 : g);
 }
 
-
-bool g_adj_uploaded[64] = {};
-
-cudaError_t upload_adjacency(int device) {
-    if (device >= 0 && device < 64 && g_adj_uploaded[device]) return cudaSuccess;
-    uint8_t par[8][27], chl[8][27];
-    for (int j = 0; j < 8; ++j) {
-        const int bits[3] = {j >> 2, (j >> 1) & 1, j & 1};
-        for (int o = 0; o < 27; ++o) {
-            const int d[3] = {o / 9 - 1, (o / 3) % 3 - 1, o % 3 - 1};
-            int pd[3], tb[3];
-            for (int a = 0; a < 3; ++a) {
-                const int t = bits[a] + d[a];            // in [-1, 2]
-                pd[a] = t < 0 ? -1 : (t > 1 ? 1 : 0);    // floor(t / 2)
-                tb[a] = t - 2 * pd[a];                   // t mod 2
-            }
-            par[j][o] = (uint8_t)((pd[0] + 1) * 9 + (pd[1] + 1) * 3 + (pd[2] + 1));
-            chl[j][o] = (uint8_t)(tb[0] * 4 + tb[1] * 2 + tb[2]);
-        }
-    }
-    cudaError_t e = cudaMemcpyToSymbol(c_adj_parent, par, sizeof(par));
-    if (e == cudaSuccess) e = cudaMemcpyToSymbol(c_adj_child, chl, sizeof(chl));
-    if (e == cudaSuccess && device >= 0 && device < 64) g_adj_uploaded[device] = true;
-    return e;
-}
 
 // zero_mask: the builder ORs tile bits across blocks (a builder that stores
 // every tile's mask whole passes false)
@@ -394,9 +388,9 @@ s3dsp_kmap* new_kmap(s3dsp_context* ctx, int64_t n_out, int64_t n_in, int kvol, 
     k->n_in = n_in;
     k->kvol = kvol;
     k->n_tiles = (n_out + kTileRows - 1) / kTileRows;
-    *err = cudaMallocAsync(&k->nbr, sizeof(int32_t) * (size_t)kvol * (size_t)(n_out > 0 ? n_out : 1), ctx->stream);
+    *err = s3dsp::malloc_async(&k->nbr, sizeof(int32_t) * (size_t)kvol * (size_t)(n_out > 0 ? n_out : 1), ctx->stream);
     if (*err == cudaSuccess)
-        *err = cudaMallocAsync(&k->tile_mask, sizeof(uint32_t) * (size_t)(k->n_tiles > 0 ? k->n_tiles : 1), ctx->stream);
+        *err = s3dsp::malloc_async(&k->tile_mask, sizeof(uint32_t) * (size_t)(k->n_tiles > 0 ? k->n_tiles : 1), ctx->stream);
     if (*err == cudaSuccess && zero_mask && k->n_tiles > 0)
         *err = cudaMemsetAsync(k->tile_mask, 0, sizeof(uint32_t) * (size_t)k->n_tiles, ctx->stream);
     if (*err != cudaSuccess) {
@@ -438,9 +432,9 @@ extern "C" S3DSP_API s3d_status s3dsp_hash_build(s3dsp_context* ctx, const int32
     // above 16 MB of table, probes mostly miss L2: map builders then read each
     // row's first row from a one-probe-per-row pass instead of probing again
     const bool self_pass = cap * 16 > (16ull << 20);
-    cudaError_t e = cudaMallocAsync(&h->slots, cap * 16, st);
-    if (e == cudaSuccess) e = cudaMallocAsync(&h->coords, (size_t)n * 16, st);
-    if (e == cudaSuccess && self_pass) e = cudaMallocAsync(&h->self_row, (size_t)n * 4, st);
+    cudaError_t e = s3dsp::malloc_async(&h->slots, cap * 16, st);
+    if (e == cudaSuccess) e = s3dsp::malloc_async(&h->coords, (size_t)n * 16, st);
+    if (e == cudaSuccess && self_pass) e = s3dsp::malloc_async(&h->self_row, (size_t)n * 4, st);
     if (e != cudaSuccess) {
         s3dsp_hash_free(ctx, h);
         return cuda_fail(error, error_capacity, e, "hash allocation");
@@ -556,7 +550,6 @@ extern "C" S3DSP_API s3d_status s3dsp_subdivide(s3dsp_context* ctx, const s3dsp_
     if (parents->n > INT32_MAX / 8)
         return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "parent count exceeds INT32_MAX/8");
     S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
-    S3DSP_CUDA(upload_adjacency(ctx->device), "adjacency tables");
     cudaError_t e;
     const int64_t np = parents->n;
     s3dsp_kmap* k = new_kmap(ctx, np * 8, np * 8, 27, true, &e);
@@ -611,8 +604,8 @@ extern "C" S3DSP_API s3d_status s3dsp_kmap_pairs(s3dsp_context* ctx, const s3dsp
     const int64_t m = nblk * k->kvol;
     int32_t* counts = nullptr;
     int64_t* starts = nullptr;
-    S3DSP_CUDA(cudaMallocAsync(&counts, sizeof(int32_t) * (size_t)(m > 0 ? m : 1), ctx->stream), "pairs scratch");
-    cudaError_t e = cudaMallocAsync(&starts, sizeof(int64_t) * (size_t)(m + 1), ctx->stream);
+    S3DSP_CUDA(s3dsp::malloc_async(&counts, sizeof(int32_t) * (size_t)(m > 0 ? m : 1), ctx->stream), "pairs scratch");
+    cudaError_t e = s3dsp::malloc_async(&starts, sizeof(int64_t) * (size_t)(m + 1), ctx->stream);
     if (e != cudaSuccess) {
         cudaFreeAsync(counts, ctx->stream);
         return cuda_fail(error, error_capacity, e, "pairs scratch");
@@ -643,6 +636,9 @@ extern "C" S3DSP_API s3d_status s3dsp_kmap_pairs(s3dsp_context* ctx, const s3dsp
     delete[] host_starts;
     cudaFreeAsync(counts, ctx->stream);
     cudaFreeAsync(starts, ctx->stream);
+    // synchronous: the pair lists are complete when the call returns
+    e = cudaStreamSynchronize(ctx->stream);
+    if (st == S3D_OK && e != cudaSuccess) st = cuda_fail(error, error_capacity, e, "cudaStreamSynchronize");
     return st;
 }
 
@@ -657,9 +653,13 @@ extern "C" S3DSP_API s3d_status s3dsp_kmap_pairs_noalloc(s3dsp_context* ctx, con
                     "kernel map has %lld output rows; the allocation-free pair build is limited to %lld rows "
                     "(use s3dsp_kmap_pairs)",
                     (long long)k->n_out, (long long)kNoAllocMaxRows);
+    // the scratch is laid out for at most 27 offsets (counts, starts, offs[32])
+    if (k->kvol < 1 || k->kvol > 27)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT,
+                    "kernel map has %d offsets; the allocation-free pair build supports at most 27", (int)k->kvol);
     S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
     unsigned char* scratch = nullptr;
-    S3DSP_CUDA(noalloc_scratch(ctx->device, &scratch), "cudaGetSymbolAddress(no-alloc scratch)");
+    S3DSP_CUDA(noalloc_scratch(&scratch), "cudaGetSymbolAddress(no-alloc scratch)");
     int32_t* counts = reinterpret_cast<int32_t*>(scratch);
     int64_t* starts = reinterpret_cast<int64_t*>(scratch + kNoAllocCountsBytes);
     int64_t* offs = reinterpret_cast<int64_t*>(scratch + kNoAllocCountsBytes + kNoAllocStartsBytes);
@@ -682,5 +682,8 @@ extern "C" S3DSP_API s3d_status s3dsp_kmap_pairs_noalloc(s3dsp_context* ctx, con
         launch_pdl(pair_write_kernel, dim3((unsigned)nblk, k->kvol), dim3(kPairBlock), 0, ctx->stream, k->nbr,
                    k->n_out, starts, nblk, d_in, d_out);
     S3DSP_LAUNCH_CHECK("pair_write_kernel");
+    // the write kernel reads the shared scratch: return only once it is done,
+    // so that calls the host has ordered never overlap on the GPU
+    S3DSP_CUDA(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
     return S3D_OK;
 }

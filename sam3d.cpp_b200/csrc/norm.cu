@@ -459,7 +459,7 @@ extern "C" S3DSP_API s3d_status s3dsp_weights_pack(s3dsp_context* ctx, const voi
     void* staged = nullptr;
     if (on_host) {
         const size_t bytes = (size_t)kvol * cin * cout * dtype_size(sd);
-        S3DSP_CUDA(cudaMallocAsync(&staged, bytes, ctx->stream), "weight staging");
+        S3DSP_CUDA(s3dsp::malloc_async(&staged, bytes, ctx->stream), "weight staging");
         cudaError_t e = cudaMemcpyAsync(staged, src, bytes, cudaMemcpyHostToDevice, ctx->stream);
         if (e != cudaSuccess) {
             cudaFreeAsync(staged, ctx->stream);

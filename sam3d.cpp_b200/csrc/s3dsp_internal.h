@@ -125,6 +125,27 @@ inline s3d_status cuda_fail(char* error, uint64_t cap, cudaError_t e, const char
         if (e_ != cudaSuccess) return ::s3dsp::cuda_fail(error, error_capacity, e_, what); \
     } while (0)
 
+// The library's own stream-ordered memory pool on `device` (< 64), created on
+// first use with an unlimited release threshold: hash tables, kernel maps and
+// scratch are rebuilt per object, and returning pool memory to the driver at
+// every synchronisation would cost milliseconds of re-mapping. A private pool
+// leaves the allocator policy of the host process (the device's default pool)
+// untouched. s3dsp_context_create makes it, so no later call (inside a stream
+// capture, say) has to.
+cudaError_t lib_pool(int device, cudaMemPool_t* out);
+
+// cudaMallocAsync from the library pool of the current device.
+template <typename T>
+inline cudaError_t malloc_async(T** p, size_t bytes, cudaStream_t stream) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    cudaMemPool_t pool;
+    e = lib_pool(dev, &pool);
+    if (e != cudaSuccess) return e;
+    return cudaMallocFromPoolAsync(reinterpret_cast<void**>(p), bytes, pool, stream);
+}
+
 inline size_t dtype_size(uint32_t dt) { return dt == S3DSP_F32 ? 4 : 2; }
 inline bool dtype_ok(uint32_t dt) { return dt == S3DSP_F32 || dt == S3DSP_BF16 || dt == S3DSP_F16; }
 

@@ -341,7 +341,7 @@ S3DSP_API s3d_status s3dsp_halo_exchange(s3dsp_context* ctx, s3dsp_shard* p, voi
     uint8_t* x = static_cast<uint8_t*>(d_x);
     uint8_t* send = nullptr;
     if (n_send > 0) {
-        S3DSP_CUDA(cudaMallocAsync(&send, (size_t)(n_send * row_bytes), st), "send buffer");
+        S3DSP_CUDA(s3dsp::malloc_async(&send, (size_t)(n_send * row_bytes), st), "send buffer");
         const int64_t work = (row_bytes & 15) == 0 ? n_send * (row_bytes >> 4) : n_send * row_bytes;
         int64_t g = (work + 255) / 256;
         if (g > ctx->sm_count * 8) g = ctx->sm_count * 8;

@@ -182,16 +182,16 @@ extern "C" S3DSP_API s3d_status s3dsp_slat_tables_build(s3dsp_context* ctx, cons
     cudaError_t e = cub::DeviceRadixSort::SortPairs(nullptr, temp_sort, keys, skeys, rows, srows, (int)n, 0, 64, st);
     if (e == cudaSuccess) e = cub::DeviceScan::InclusiveSum(nullptr, temp_scan, head, incl, (int)n, st);
     const size_t temp_bytes = temp_sort > temp_scan ? temp_sort : temp_scan;
-    if (e == cudaSuccess) e = cudaMallocAsync(&keys, (size_t)n * 8, st);
-    if (e == cudaSuccess) e = cudaMallocAsync(&skeys, (size_t)n * 8, st);
-    if (e == cudaSuccess) e = cudaMallocAsync(&rows, (size_t)n * 4, st);
-    if (e == cudaSuccess) e = cudaMallocAsync(&srows, (size_t)n * 4, st);
-    if (e == cudaSuccess) e = cudaMallocAsync(&head, (size_t)n * 4, st);
-    if (e == cudaSuccess) e = cudaMallocAsync(&incl, (size_t)n * 4, st);
-    if (e == cudaSuccess) e = cudaMallocAsync(&run_start, (size_t)n * 4, st);
-    if (e == cudaSuccess) e = cudaMallocAsync(&temp, temp_bytes > 0 ? temp_bytes : 16, st);
-    if (e == cudaSuccess) e = cudaMallocAsync(&t->fine_to_coarse, (size_t)n * 4, st);
-    if (e == cudaSuccess) e = cudaMallocAsync(&t->coarse_coords, (size_t)n * 16, st);  // nc <= nf
+    if (e == cudaSuccess) e = s3dsp::malloc_async(&keys, (size_t)n * 8, st);
+    if (e == cudaSuccess) e = s3dsp::malloc_async(&skeys, (size_t)n * 8, st);
+    if (e == cudaSuccess) e = s3dsp::malloc_async(&rows, (size_t)n * 4, st);
+    if (e == cudaSuccess) e = s3dsp::malloc_async(&srows, (size_t)n * 4, st);
+    if (e == cudaSuccess) e = s3dsp::malloc_async(&head, (size_t)n * 4, st);
+    if (e == cudaSuccess) e = s3dsp::malloc_async(&incl, (size_t)n * 4, st);
+    if (e == cudaSuccess) e = s3dsp::malloc_async(&run_start, (size_t)n * 4, st);
+    if (e == cudaSuccess) e = s3dsp::malloc_async(&temp, temp_bytes > 0 ? temp_bytes : 16, st);
+    if (e == cudaSuccess) e = s3dsp::malloc_async(&t->fine_to_coarse, (size_t)n * 4, st);
+    if (e == cudaSuccess) e = s3dsp::malloc_async(&t->coarse_coords, (size_t)n * 16, st);  // nc <= nf
     s3d_status status = S3D_OK;
     int32_t nc = 0;
     if (e == cudaSuccess) {
@@ -217,8 +217,8 @@ extern "C" S3DSP_API s3d_status s3dsp_slat_tables_build(s3dsp_context* ctx, cons
         }
     }
     if (e == cudaSuccess && status == S3D_OK) {
-        e = cudaMallocAsync(&t->coarse_children, (size_t)nc * 8 * 4, st);
-        if (e == cudaSuccess) e = cudaMallocAsync(&t->coarse_inv_count, (size_t)nc * 4, st);
+        e = s3dsp::malloc_async(&t->coarse_children, (size_t)nc * 8 * 4, st);
+        if (e == cudaSuccess) e = s3dsp::malloc_async(&t->coarse_inv_count, (size_t)nc * 4, st);
         if (e == cudaSuccess) {
             launch_pdl(children_kernel, dim3(grid_for(nc, 256, ctx->sm_count)), dim3(256), 0, st, srows, run_start,
                        nc, n, t->coarse_children, t->coarse_inv_count);

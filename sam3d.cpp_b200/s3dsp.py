@@ -31,7 +31,7 @@ CONTEXT_OWN_STREAM = 2
 # every symbol include/s3dsp.h declares (tests check the library exports them)
 EXPORTED = [
     "s3dsp_abi_version", "s3dsp_context_create", "s3dsp_context_free", "s3dsp_context_stream",
-    "s3dsp_context_check", "s3dsp_hash_build", "s3dsp_hash_free", "s3dsp_hash_size",
+    "s3dsp_context_check", "s3dsp_memory_stats", "s3dsp_hash_build", "s3dsp_hash_free", "s3dsp_hash_size",
     "s3dsp_hash_lookup", "s3dsp_gs_window_tables", "s3dsp_ape", "s3dsp_flexicubes_tables_create",
     "s3dsp_flexicubes_tables_free", "s3dsp_flexicubes_extract", "s3dsp_mesh_info", "s3dsp_mesh_device", "s3dsp_mesh_copy",
     "s3dsp_mesh_free", "s3dsp_gguf_open", "s3dsp_gguf_close", "s3dsp_gguf_n_tensors", "s3dsp_gguf_find",
@@ -82,6 +82,8 @@ def load(path: str = LIB_PATH):
         "s3dsp_context_free": (None, [_vp]),
         "s3dsp_context_stream": (_vp, [_vp]),
         "s3dsp_context_check": (_u32, [_vp, _cp, _u64]),
+        "s3dsp_memory_stats": (_u32, [_i32, ctypes.POINTER(_u64), ctypes.POINTER(_u64), ctypes.POINTER(_u64), _i32,
+                                      _cp, _u64]),
         "s3dsp_hash_build": (_u32, [_vp, _vp, _i64, _i32, ctypes.POINTER(_vp), _cp, _u64]),
         "s3dsp_hash_free": (None, [_vp, _vp]),
         "s3dsp_hash_size": (_i64, [_vp]),
@@ -447,6 +449,15 @@ def nccl_unique_id() -> bytes:
     buf = ctypes.create_string_buffer(128)
     _call(load().s3dsp_nccl_unique_id, ctypes.cast(buf, ctypes.c_void_p))
     return buf.raw
+
+
+def memory_stats(device: int = 0, reset_high: bool = False) -> dict:
+    """Bytes the library's own device pool holds on `device`: reserved, in use
+    and the high-water mark of use (reset to the current use afterwards when
+    reset_high)."""
+    r, u, h = _u64(), _u64(), _u64()
+    _call(load().s3dsp_memory_stats, device, ctypes.byref(r), ctypes.byref(u), ctypes.byref(h), int(reset_high))
+    return {"reserved": r.value, "used": u.value, "used_high": h.value}
 
 
 def samt_info(path: str) -> dict:

@@ -7,7 +7,9 @@ break its contract. For them the library offers a variant of
 s3dsp_kmap_pairs whose scratch is a static device array (maps of at most
 2^21 output rows). These tests call it through the C ABI and check that it
 returns exactly what the allocating entry point returns, on two calls in a
-row (the second call reuses the shared static scratch left by the first).
+row (the second call reuses the shared static scratch left by the first),
+that it takes no memory from the library's pool (the allocating call does),
+and that the largest accepted map works.
 
 This file is named so that pytest collects it last.
 """
@@ -49,6 +51,12 @@ def pairs_with(fn, ctx, kmap, n):
     return list(offs), pin[:total].cpu().numpy(), pout[:total].cpu().numpy()
 
 
+def dense_block(side):
+    g = np.arange(side, dtype=np.int32)
+    x, y, z = np.meshgrid(g, g, g, indexing="ij")
+    return np.stack([np.zeros_like(x), x, y, z], -1).reshape(-1, 4).astype(np.int32)
+
+
 def test_noalloc_pairs_equal_allocating_pairs_twice_in_a_row(ctx):
     lib = s3dsp.load()
     shells = [workloads.ellipsoid_shell(64, 1), workloads.ellipsoid_shell(48, 2)]
@@ -63,13 +71,41 @@ def test_noalloc_pairs_equal_allocating_pairs_twice_in_a_row(ctx):
         assert np.array_equal(got_out, ref_out)
 
 
+def test_noalloc_takes_no_pool_memory(ctx):
+    lib = s3dsp.load()
+    coords = workloads.ellipsoid_shell(64, 3)
+    _, k = build_kmap(ctx, coords)
+    torch.cuda.synchronize()
+    before = s3dsp.memory_stats(0, reset_high=True)
+    pairs_with(lib.s3dsp_kmap_pairs_noalloc, ctx, k, len(coords))
+    after = s3dsp.memory_stats(0)
+    assert after["used_high"] == before["used"], (before, after)
+    # the check is sensitive: the allocating call does take pool memory
+    s3dsp.memory_stats(0, reset_high=True)
+    pairs_with(lib.s3dsp_kmap_pairs, ctx, k, len(coords))
+    assert s3dsp.memory_stats(0)["used_high"] > before["used"]
+
+
+def test_noalloc_at_exactly_its_limit(ctx):
+    # a dense 128^3 block has exactly 2^21 rows, the largest accepted map
+    lib = s3dsp.load()
+    coords = dense_block(128)
+    assert len(coords) == NOALLOC_MAX_ROWS
+    _, k = build_kmap(ctx, coords)
+    ref_offs, ref_in, ref_out = pairs_with(lib.s3dsp_kmap_pairs, ctx, k, len(coords))
+    got_offs, got_in, got_out = pairs_with(lib.s3dsp_kmap_pairs_noalloc, ctx, k, len(coords))
+    assert got_offs == ref_offs
+    # every interior voxel of the block has all 27 neighbours: 27 * 126^3 of them
+    # plus the faces; the centre offset pairs every row with itself
+    assert ref_offs[14] - ref_offs[13] == NOALLOC_MAX_ROWS
+    assert np.array_equal(got_in, ref_in)
+    assert np.array_equal(got_out, ref_out)
+
+
 def test_noalloc_rejects_maps_above_its_limit(ctx):
-    # a dense 128^3 block is exactly the limit; eight more voxels exceed it
-    g = np.arange(128, dtype=np.int32)
-    x, y, z = np.meshgrid(g, g, g, indexing="ij")
-    dense = np.stack([np.zeros_like(x), x, y, z], -1).reshape(-1, 4)
+    # eight voxels more than the dense 128^3 block
     extra = np.array([[0, 200, 0, j] for j in range(8)], np.int32)
-    coords = np.concatenate([dense, extra]).astype(np.int32)
+    coords = np.concatenate([dense_block(128), extra]).astype(np.int32)
     assert len(coords) == NOALLOC_MAX_ROWS + 8
     _, k = build_kmap(ctx, coords)
     pin = torch.empty(16, dtype=torch.int32, device="cuda")
