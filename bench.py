@@ -5,17 +5,28 @@ Workload (one "step" = one pass of the whole path over one object): the
   coordinate hash -> submanifold kernel map -> subm conv3 (+ GroupNorm partial
   sums) -> GroupNorm(32) finalize -> SiLU -> subm conv3 -> + skip,
 bf16 tcgen05 MMAs with f32 accumulation. Metric: active-voxel outputs/s, one
-unit = one output voxel of one conv layer (2 * N per step).
+unit = one output voxel of one conv layer (2 * N per step); `value` is the
+whole job's rate (all GPUs), `value_per_gpu` divides it by the GPU count.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload ...] [--no-sub] [--profile-case CASE]
 
 Multi-GPU (torchrun, one rank per GPU): objects are independent, so each rank
 runs its own object (seed = rank) with no data-path collective ("weak"
 scaling); timing is the max over ranks.
 
+The default run also measures, at every N, three sub-records on the same
+ranks: `f32` (the config-2 step in the reference's own f32 arithmetic: F32
+strict FFMA and 3xTF32 on the tensor cores), `objects_5a` (64 objects through
+the config-4 stack, dealt to the ranks) and `volume_5b` (one 2.58M-voxel
+volume in Morton slabs with the C-ABI NCCL halo exchange, checked bit for bit
+against the whole-volume conv on every rank). `--no-sub` skips them.
+
 `--impl reference` times the reference path on the host cores instead: the
 reference's own table builder (oracle/_ref, when it was built) plus the CPU
 restatement of its GGML op order, all host threads.
+
+`--profile-case CASE` runs one small kernel case for an ncu capture and exits.
 """
 from __future__ import annotations
 
@@ -34,12 +45,15 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 for sub in ("sam3d.cpp_b200", "oracle"):
     sys.path.insert(0, os.path.join(ROOT, sub))
 
-METRIC = "active-voxel outputs/s per GPU (C=256 subm conv)"
+METRIC = "active-voxel outputs/s, all GPUs (C=256 subm conv residual block)"
 UNIT = "voxel-outputs/s"
 L2_FLUSH_BYTES = 512 << 20  # > 126 MB L2
-# DRAM bytes (read + write) per launch of the config-2 conv kernel, from one ncu
-# capture of `python sam3d.cpp_b200/profile_case.py conv2` (profiles/conv_tc_kernel_config2.md)
-CONV_TRAFFIC_BYTES = {"conv_tc_kernel": 13.02e6}
+# DRAM bytes (read + write) per launch, from one ncu capture of
+# `python bench.py --profile-case conv2`, keyed by (kernel, output rows,
+# channels): it holds only for that kernel on that shape; other shapes report
+# null until captured.
+CONV_TRAFFIC_BYTES = {("conv_tc_kernel", 15159, 256): 13.02e6}
+FFMA_PEAK_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12  # nominal FP32 FMA peak of B200 (148 SMs x 128 lanes x 2 x 1.965 GHz)
 
 
 def load_peaks():
@@ -103,24 +117,91 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def gpu_cpus(local_rank: int, local_world: int):
+    """Host CPUs for this rank: the NUMA node of its GPU (from sysfs), shared
+    evenly among the ranks of this host on that node (by local rank). None
+    when the node cannot be found."""
+    import torch
+    try:
+        pr = torch.cuda.get_device_properties(local_rank)
+        bus = f"{pr.pci_domain_id:04x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        with open(f"/sys/bus/pci/devices/{bus}/numa_node") as f:
+            node = int(f.read().strip())
+        if node < 0:
+            return None
+
+        def node_of(i):
+            q = torch.cuda.get_device_properties(i)
+            b = f"{q.pci_domain_id:04x}:{q.pci_bus_id:02x}:{q.pci_device_id:02x}.0"
+            with open(f"/sys/bus/pci/devices/{b}/numa_node") as g:
+                return int(g.read().strip())
+
+        peers = [i for i in range(local_world) if node_of(i) == node]
+        with open(f"/sys/devices/system/node/node{node}/cpulist") as f:
+            cpus = []
+            for part in f.read().strip().split(","):
+                lo, _, hi = part.partition("-")
+                cpus.extend(range(int(lo), int(hi or lo) + 1))
+        cpus = [c for c in cpus if c in os.sched_getaffinity(0)]
+        share = len(cpus) // max(1, len(peers))
+        if share < 1:
+            return None
+        i = peers.index(local_rank)
+        return cpus[i * share:(i + 1) * share]
+    except Exception:
+        return None
+
+
+def conv_roofline(kernel, n, c, P, conv_ms, out_bytes, res_bytes, tflops, hbm, peak_src):
+    """North_star's roofline for one conv launch: the slower of the dense MMA
+    time (2 C^2 P at the measured bf16 peak) and the gathered bytes at HBM
+    bandwidth (P gathered rows of C bf16 + N output rows + the residual rows
+    read + 8 bytes of pair indices per pair + the 27 C^2 bf16 weights).
+    `achieved` follows the binding side; the other side is reported beside it."""
+    flops = 2.0 * c * c * P
+    gbytes = P * c * 2 + n * c * out_bytes + n * c * res_bytes + 8 * P + 27 * c * c * 2
+    t_mma, t_hbm = flops / (tflops * 1e12), gbytes / (hbm * 1e9)
+    s = conv_ms / 1e3
+    tensor = {"achieved": flops / s / 1e12, "peak": tflops, "unit": "TFLOP/s", "frac": flops / s / 1e12 / tflops}
+    hbm_v = {"achieved": gbytes / s / 1e9, "peak": hbm, "unit": "GB/s", "frac": gbytes / s / 1e9 / hbm}
+    bound = "tensor" if t_mma >= t_hbm else "hbm"
+    main, other = (tensor, hbm_v) if bound == "tensor" else (hbm_v, tensor)
+    key = (kernel, n, c)
+    return {"bound": bound, **main, "traffic": CONV_TRAFFIC_BYTES.get(key),
+            "traffic_unit": "DRAM bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum), measured for "
+                            "this (kernel, rows, channels) only",
+            "kernel": kernel, "flops_per_launch": flops, "gathered_bytes_per_launch": gbytes,
+            "avg_launch_ms": conv_ms, "roofline_ms": max(t_mma, t_hbm) * 1e3,
+            ("tensor_view" if bound == "hbm" else "hbm_view"): other,
+            "peak_source": f"{peak_src} MEASURED_PEAKS.json (bf16_tflops burst, hbm_gbs)"}
+
+
 # ---------------------------------------------------------------------------
 # our path
 # ---------------------------------------------------------------------------
 class ResBlockPath:
-    """Config-2 residual block through the s3dsp C-ABI (device-resident)."""
+    """Config-2 residual block through the s3dsp C-ABI (device-resident).
 
-    PHASES = ("hash", "kmap", "convert", "conv1", "gn_finalize+affine", "conv2")
+    BF16: x is converted to bf16 on a side stream (its own context) while the
+    hash and kernel map are built; conv1 writes y1 in bf16 with the GroupNorm
+    partial sums taken from its f32 accumulators; GN + SiLU read y1 and write
+    the bf16 input of conv2, which adds the f32 skip. F32 precisions (strict
+    FFMA, 3xTF32) keep every activation in f32, the reference's arithmetic."""
 
-    def __init__(self, s3dsp, ctx, cfg, torch, device):
+    PHASES = ("hash+kmap", "conv1", "gn_finalize+affine", "conv2")
+
+    def __init__(self, s3dsp, ctx, cfg, torch, device, precision=None, side=None):
         self.s, self.ctx, self.torch = s3dsp, ctx, torch
         t = torch
+        P = s3dsp.PREC_BF16 if precision is None else precision
+        self.prec = P
+        self.bf = P == s3dsp.PREC_BF16
         c = cfg["channels"]
         n = len(cfg["coords"])
         self.n, self.c = n, c
         dev = lambda a: t.from_numpy(np.ascontiguousarray(a)).to(device)  # noqa: E731
         self.coords = dev(cfg["coords"])
         self.x = dev(cfg["feats"])
-        P = s3dsp.PREC_BF16
         self.w1 = t.empty(s3dsp.Context.packed_bytes(P, 27, c, c), dtype=t.uint8, device=device)
         self.w2 = t.empty_like(self.w1)
         ctx.weights_pack(t.from_numpy(cfg["w1"]), s3dsp.LAYOUT_SLAT_ROW, 27, c, c, P, self.w1)
@@ -129,88 +210,159 @@ class ResBlockPath:
         self.gamma, self.beta = dev(cfg["gamma"]), dev(cfg["beta"])
         self.part = t.empty(s3dsp.Context.gn_partials_count(n, c, 32), dtype=t.float64, device=device)
         self.sub, self.mul, self.add = (t.empty(c, device=device) for _ in range(3))
-        self.xb = t.empty((n, c), dtype=t.bfloat16, device=device)
-        self.y1 = t.empty((n, c), dtype=t.float32, device=device)
-        self.hb = t.empty((n, c), dtype=t.bfloat16, device=device)
+        adt = t.bfloat16 if self.bf else t.float32
+        self.xb = t.empty((n, c), dtype=t.bfloat16, device=device) if self.bf else self.x
+        self.y1 = t.empty((n, c), dtype=adt, device=device)
+        self.hb = t.empty((n, c), dtype=adt, device=device)
         self.out = t.empty((n, c), dtype=t.float32, device=device)
-        # our kernels per step: hash init + insert, kmap, convert, conv1, finalize, affine, conv2
-        self.launches_per_step = 8
+        # (side context, side stream): the bf16 convert runs there, beside the tables
+        self.side = side if self.bf else None
+        # our kernels per step: hash init + insert, kmap, [convert], conv1, finalize, affine, conv2
+        # (3xTF32: + the TF32 split of each conv's input)
+        self.launches_per_step = 7 + (1 if self.bf else 0) + (2 if P == s3dsp.PREC_F32_3XTF32 else 0)
         self.conv_kernel = ctx.conv_kernel(n, 27, c, c, P)
 
     def step(self, marks=None):
-        """One pass of the path. `marks`: 7 events recorded between the phases.
-        The hash and kernel map are freed inside the step, so a captured graph
-        owns (and releases) their memory."""
-        s, ctx = self.s, self.ctx
+        """One pass of the path. `marks`: 5 events recorded between the phases
+        on the main stream. The hash and kernel map are freed inside the step,
+        so a captured graph owns (and releases) their memory."""
+        s, ctx, t = self.s, self.ctx, self.torch
         mark = (lambda i: marks[i].record()) if marks else (lambda i: None)
         mark(0)
+        join = None
+        if self.bf:
+            if self.side is not None:
+                sctx, sst = self.side
+                fork = t.cuda.Event()
+                fork.record()
+                sst.wait_event(fork)
+                with t.cuda.stream(sst):
+                    sctx.convert(self.x, self.xb)
+                    join = t.cuda.Event()
+                    join.record(sst)
+            else:
+                ctx.convert(self.x, self.xb)
         h = ctx.hash_build(self.coords)
-        mark(1)
         k = ctx.kmap_subm3(h)
+        if join is not None:
+            t.cuda.current_stream().wait_event(join)
+        mark(1)
+        ctx.conv(k, 27, self.prec, self.xb, self.w1, self.b1, self.y1, self.c, gn_partials=self.part, gn_groups=32)
         mark(2)
-        ctx.convert(self.x, self.xb)
-        mark(3)
-        ctx.conv(k, 27, s.PREC_BF16, self.xb, self.w1, self.b1, self.y1, self.c, gn_partials=self.part, gn_groups=32)
-        mark(4)
         ctx.gn_finalize(self.part, self.n, self.c, 32, 1e-5, self.gamma, self.beta, self.sub, self.mul, self.add)
         ctx.channel_affine(self.y1, self.sub, self.mul, self.add, True, self.hb)
-        mark(5)
-        ctx.conv(k, 27, s.PREC_BF16, self.hb, self.w2, self.b2, self.out, self.c, residual=self.x)
-        mark(6)
+        mark(3)
+        ctx.conv(k, 27, self.prec, self.hb, self.w2, self.b2, self.out, self.c, residual=self.x)
+        mark(4)
         k.free()
         h.free()
 
 
-def pairs_of(ctx, path, torch):
+def pairs_of(ctx, coords, torch):
     """Valid (in, out) pairs of the kernel map, counted by the library itself."""
-    h = ctx.hash_build(path.coords)
+    h = ctx.hash_build(coords)
     k = ctx.kmap_subm3(h)
-    cap = 27 * path.n
-    pin = torch.empty(cap, dtype=torch.int32, device=path.coords.device)
+    n = coords.shape[0]
+    pin = torch.empty(27 * n, dtype=torch.int32, device=coords.device)
     pout = torch.empty_like(pin)
     return int(ctx.kmap_pairs(k, pin, pout)[27])
 
 
-E2E_WORKERS = 4  # concurrent host callers in the e2e measurement
+class L2Flush:
+    """Write more than L2 (evicts everything a step touched), then read a
+    second buffer, so the L2 holds clean lines: the next step neither hits its
+    own data nor pays for the flush's write-backs."""
+
+    def __init__(self, torch, device):
+        self.t = torch
+        self.w = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+        self.r = torch.ones(L2_FLUSH_BYTES // 8, dtype=torch.float32, device=device)
+        self.acc = torch.empty((), dtype=torch.float32, device=device)
+
+    def __call__(self):
+        self.w.fill_(1.0)
+        self.t.sum(self.r, dim=0, out=self.acc)
 
 
-def e2e_workers(s3dsp, torch, device, main_stream, host_call, ref_out, steps, warmup):
+def time_graphs(torch, stream, path, flush, steps, warmup, n_marks):
+    """Captures `path.step` twice (plain, and with events between its phases),
+    replays warm-up rounds, then times `steps` plain replays (the L2 flushed
+    between them, outside the events) and `steps` marked replays. Every replay
+    must reproduce the eager pass's output bit for bit. Returns (device ms of
+    the plain steps, per-step phase ms [steps, n_marks - 1])."""
+    path.step()  # eager first pass: one-time library initialisation stays out of the graph
+    stream.synchronize()
+    ref_out = path.out.clone()
+    marks = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(n_marks)]
+    graph, marked = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    # thread-local capture: NCCL's watchdog thread may query events meanwhile
+    with torch.cuda.graph(graph, stream=stream, capture_error_mode="thread_local"):
+        path.step()
+    with torch.cuda.graph(marked, stream=stream, capture_error_mode="thread_local"):
+        path.step(marks)
+    for _ in range(warmup):
+        graph.replay()
+        flush()
+        marked.replay()
+        flush()
+    stream.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for i in range(steps):
+        starts[i].record(stream)
+        graph.replay()
+        ends[i].record(stream)
+        flush()
+    stream.synchronize()
+    dev_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    if not torch.equal(path.out, ref_out):
+        raise RuntimeError("the graph-replayed step's output differs from the eager step's")
+    phase_ms = []
+    for i in range(steps):
+        marked.replay()
+        flush()
+        stream.synchronize()  # the phase events are re-recorded by the next replay
+        phase_ms.append([marks[j].elapsed_time(marks[j + 1]) for j in range(n_marks - 1)])
+    if not torch.equal(path.out, ref_out):
+        raise RuntimeError("the marked replay's output differs from the eager step's")
+    del graph, marked
+    return dev_ms, np.array(phase_ms)
+
+
+def e2e_workers(s3dsp, torch, device, main_stream, host_call, ref_out, steps, warmup, workers_n, flush):
     """Device time of `steps` host-buffer calls (rounded up to a multiple of
-    E2E_WORKERS) made by E2E_WORKERS threads, each with its own context, stream
-    and pinned output. Each call is preceded, on its stream, by a write of
-    more than L2 and a read of another buffer (the L2 flush), inside the timed
-    region. The span runs from one event that every worker stream waits on to
-    the last worker's end event. Every worker's last output must equal
-    `ref_out` bit for bit. Returns (ms, calls timed)."""
-    per = max(1, -(-steps // E2E_WORKERS))
-    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
-    flush_rd = torch.ones(L2_FLUSH_BYTES // 8, dtype=torch.float32, device=device)
+    workers_n) made by workers_n threads, each with its own context, stream
+    and pinned output. Each call is preceded, on its stream, by the L2 flush,
+    inside the timed region. The span runs from one event that every worker
+    stream waits on to the last worker's end event. Every worker's last output
+    must equal `ref_out` bit for bit. Returns (ms, calls timed)."""
+    per = max(1, -(-steps // workers_n))
     workers = []
-    for _ in range(E2E_WORKERS):
+    for _ in range(workers_n):
         st = torch.cuda.Stream(device)
         workers.append((st, s3dsp.Context(device.index, stream=st.cuda_stream, flags=s3dsp.CONTEXT_DEFERRED_CHECKS),
-                        torch.empty_like(ref_out).pin_memory(),
-                        torch.empty((), dtype=torch.float32, device=device)))
+                        torch.empty_like(ref_out).pin_memory()))
     start = torch.cuda.Event(enable_timing=True)
     final = torch.cuda.Event(enable_timing=True)
     ends = [torch.cuda.Event() for _ in workers]
-    ready, go = threading.Barrier(E2E_WORKERS + 1), threading.Barrier(E2E_WORKERS + 1)
+    ready, go = threading.Barrier(workers_n + 1), threading.Barrier(workers_n + 1)
     errors = []
+    flush_lock = threading.Lock()
 
     def body(i):
-        st, cx, out, acc = workers[i]
+        st, cx, out = workers[i]
         try:
             torch.cuda.set_device(device)
             with torch.cuda.stream(st):
-                for _ in range(max(2, warmup // E2E_WORKERS)):
+                for _ in range(max(2, warmup // workers_n)):
                     host_call(cx, out)
                 st.synchronize()
                 ready.wait()
                 go.wait()
                 st.wait_event(start)
                 for _ in range(per):
-                    flush.fill_(1.0)
-                    torch.sum(flush_rd, dim=0, out=acc)
+                    with flush_lock:  # one flush buffer, queued on this worker's stream
+                        flush()
                     host_call(cx, out)
                 ends[i].record(st)
         except Exception as e:  # surfaced after the join
@@ -218,7 +370,7 @@ def e2e_workers(s3dsp, torch, device, main_stream, host_call, ref_out, steps, wa
             ready.abort()
             go.abort()
 
-    threads = [threading.Thread(target=body, args=(i,)) for i in range(E2E_WORKERS)]
+    threads = [threading.Thread(target=body, args=(i,)) for i in range(workers_n)]
     for t in threads:
         t.start()
     try:
@@ -235,11 +387,21 @@ def e2e_workers(s3dsp, torch, device, main_stream, host_call, ref_out, steps, wa
         main_stream.wait_event(e)
     final.record(main_stream)
     main_stream.synchronize()
-    for _, cx, out, _ in workers:
+    for _, cx, out in workers:
         cx.check()
         if not torch.equal(out, ref_out):
             raise RuntimeError("a concurrent host call's output differs from the serial call's")
-    return start.elapsed_time(final), per * E2E_WORKERS
+    return start.elapsed_time(final), per * workers_n
+
+
+def gather_rows(torch, world, values):
+    """Every rank's list of floats, on every rank ([world][len])."""
+    t = torch.tensor(values, dtype=torch.float64, device="cuda")
+    if world == 1:
+        return [values]
+    out = [torch.empty_like(t) for _ in range(world)]
+    torch.distributed.all_gather(out, t)
+    return [o.tolist() for o in out]
 
 
 def run_ours(args, rank, world, local_rank):
@@ -247,8 +409,15 @@ def run_ours(args, rank, world, local_rank):
     import s3dsp
     import workloads
 
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
+    # host threads of this rank on its GPU's NUMA node, shared with the node's other ranks
+    cpus = gpu_cpus(local_rank, local_world)
+    all_cpus = os.sched_getaffinity(0)
+    if cpus:
+        os.sched_setaffinity(0, cpus)
+    n_cpus = len(os.sched_getaffinity(0))
     cfg = workloads.config2(seed=0)
     if rank > 0:
         # every rank its own object of the config-2 shape (its own features):
@@ -259,69 +428,26 @@ def run_ours(args, rank, world, local_rank):
     stream = torch.cuda.Stream(device)
     torch.cuda.set_stream(stream)
     ctx = s3dsp.Context(local_rank, stream=stream.cuda_stream, flags=s3dsp.CONTEXT_DEFERRED_CHECKS)
-    path = ResBlockPath(s3dsp, ctx, cfg, torch, device)
+    side_stream = torch.cuda.Stream(device)
+    side = (s3dsp.Context(local_rank, stream=side_stream.cuda_stream, flags=s3dsp.CONTEXT_DEFERRED_CHECKS),
+            side_stream)
+    path = ResBlockPath(s3dsp, ctx, cfg, torch, device, side=side)
     n, c = path.n, path.c
-    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
-    flush_rd = torch.ones(L2_FLUSH_BYTES // 8, dtype=torch.float32, device=device)
-    flush_acc = torch.empty((), dtype=torch.float32, device=device)
-
-    def flush_l2():
-        # write more than L2 (evicts everything the step touched), then read a
-        # second buffer so the L2 holds clean lines: the next step neither
-        # hits its own data nor pays for the flush's write-backs
-        flush.fill_(1.0)
-        torch.sum(flush_rd, dim=0, out=flush_acc)
+    flush = L2Flush(torch, device)
 
     # ---- device-resident steps, replayed as one CUDA graph per step ----
-    path.step()  # eager first pass: one-time library initialisation stays out of the graph
-    stream.synchronize()
-    ref_out = path.out.clone()  # the eager pass's output: every replay must reproduce it bit for bit
-    # two captures of the same step: `graph` is timed for the value; `marked`
-    # records events between the phases (for the breakdown and the conv time
-    # of the roofline), which also cuts the programmatic-launch overlap
-    # between the kernels at each mark
-    marks = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(7)]
-    graph, marked = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
-    # thread-local capture: NCCL's watchdog thread may query events meanwhile
-    with torch.cuda.graph(graph, stream=stream, capture_error_mode="thread_local"):
-        path.step()
-    with torch.cuda.graph(marked, stream=stream, capture_error_mode="thread_local"):
-        path.step(marks)
-    for _ in range(args.warmup):
-        graph.replay()
-        flush_l2()
-        marked.replay()
-        flush_l2()
-    stream.synchronize()
     if world > 1:
         torch.distributed.barrier()
-
     sampler = ClockSampler(local_rank)
     sampler.start()
     time.sleep(0.3)
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     t0 = time.perf_counter()
-    for i in range(args.steps):
-        starts[i].record(stream)
-        graph.replay()
-        ends[i].record(stream)
-        flush_l2()
-    stream.synchronize()
+    dev_ms, phase_ms = time_graphs(torch, stream, path, flush, args.steps, args.warmup, 5)
     wall = time.perf_counter() - t0
-    dev_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
-    if not torch.equal(path.out, ref_out):
-        raise RuntimeError("the graph-replayed step's output differs from the eager step's")
-    phase_ms = []
-    for i in range(args.steps):
-        marked.replay()
-        flush_l2()
-        stream.synchronize()  # the phase events are re-recorded by the next replay
-        phase_ms.append([marks[j].elapsed_time(marks[j + 1]) for j in range(6)])
-    phase_ms = np.array(phase_ms)
-    conv_ms = np.concatenate([phase_ms[:, 3], phase_ms[:, 5]])
+    conv_ms = np.concatenate([phase_ms[:, 1], phase_ms[:, 3]])
     breakdown = {name: float(v) for name, v in zip(ResBlockPath.PHASES, phase_ms.mean(0))}
     breakdown["step_with_marks"] = float(phase_ms.sum(1).mean())
+    breakdown["note"] = "the bf16 convert of x runs on a side stream beside hash+kmap"
 
     # ---- e2e: the C-ABI block call with host buffers (H2D, tables, block, D2H, sync) ----
     coords_h = torch.from_numpy(cfg["coords"]).pin_memory()
@@ -337,7 +463,7 @@ def run_ours(args, rank, world, local_rank):
     e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     for i in range(args.steps + args.warmup):
         j = i - args.warmup
-        flush_l2()
+        flush()
         if j >= 0:
             e_starts[j].record(stream)
         host_call(ctx, out_h)
@@ -345,14 +471,34 @@ def run_ours(args, rank, world, local_rank):
             e_ends[j].record(stream)
     stream.synchronize()
     serial_ms = sum(s.elapsed_time(e) for s, e in zip(e_starts, e_ends))
-    # serving: E2E_WORKERS host threads, each with its own context, stream and
-    # output buffer, call the same entry point concurrently, so one call's
-    # copies overlap another's kernels
-    pipe_ms, pipe_steps = e2e_workers(s3dsp, torch, device, stream, host_call, out_h, args.steps, args.warmup)
+    # the copies alone: the same bytes in (coords + features) and out, one step at a time
+    d_in_c = torch.empty_like(coords_h, device=device)
+    d_in_x = torch.empty_like(x_h, device=device)
+    d_out = torch.empty_like(out_h, device=device)
+    cs, ce = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    cs.record(stream)
+    for _ in range(args.steps):
+        d_in_c.copy_(coords_h, non_blocking=True)
+        d_in_x.copy_(x_h, non_blocking=True)
+        out_h.copy_(d_out, non_blocking=True)
+    ce.record(stream)
+    stream.synchronize()
+    copy_ms = cs.elapsed_time(ce) / args.steps
+    host_call(ctx, out_h)  # the reference output of the concurrent callers
+    stream.synchronize()
+    # serving: host threads of this rank, each with its own context, stream
+    # and output buffer, call the same entry point concurrently, so one call's
+    # copies overlap another's kernels; one thread per spare host CPU of the
+    # rank (at most 4)
+    workers_n = max(1, min(4, n_cpus - 1))
+    pipe_ms, pipe_steps = e2e_workers(s3dsp, torch, device, stream, host_call, out_h, args.steps, args.warmup,
+                                      workers_n, flush)
     clocks = sampler.stop()
     h2d = coords_h.numel() * 4 + x_h.numel() * 4
     d2h = out_h.numel() * 4
     ctx.check()
+    per_rank = gather_rows(torch, world, [dev_ms / args.steps, copy_ms, serial_ms / args.steps,
+                                          pipe_ms / pipe_steps, float(workers_n), float(n_cpus)])
 
     # max over ranks
     vals = torch.tensor([dev_ms, serial_ms, pipe_ms], dtype=torch.float64, device=device)
@@ -362,86 +508,184 @@ def run_ours(args, rank, world, local_rank):
         torch.distributed.all_reduce(units, op=torch.distributed.ReduceOp.SUM)
     dev_ms, serial_ms, pipe_ms = vals.tolist()
     total_units, pipe_units = units.tolist()
-    if rank != 0:
-        del graph, marked
-        return None
 
-    value = total_units / (dev_ms / 1e3)
-    e2e_value = pipe_units / (pipe_ms / 1e3)
-    hbm, tflops, tflops_sus, peak_src = load_peaks()
-    P = pairs_of(ctx, path, torch)
-    flops = 2.0 * c * c * P  # algorithmic: valid (in, out) pairs only
-    conv_avg_ms = float(conv_ms.mean())
-    achieved = flops / (conv_avg_ms / 1e3) / 1e12
-    line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded ellipsoid shells, random-init weights)",
-        "config": {"workload": "config2: 64^3 shell res block C=256 (subm conv3 -> GN32 -> SiLU -> subm conv3 -> "
-                               "+skip), hash + kmap rebuilt every step",
-                   "voxels": n, "pairs": P, "channels": c, "objects_per_gpu": 1, "parallelism": f"objects-dp{world}",
-                   "l2": "flushed between steps (512 MiB write, then 256 MiB read of another buffer)",
-                   "timing": "device steps replayed as a CUDA graph of the library calls (the breakdown and "
-                             "the roofline's conv time from a second capture with events between the phases); e2e = "
-                             "s3dsp_res_block_gn_host (host buffers in/out) per step, called by "
-                             f"{E2E_WORKERS} concurrent host threads (serial figure beside it)"},
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": tflops, "unit": "TFLOP/s",
-                     "frac": achieved / tflops, "traffic": CONV_TRAFFIC_BYTES.get(path.conv_kernel),
-                     "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
-                     "kernel": path.conv_kernel, "flops_per_launch": flops, "avg_launch_ms": conv_avg_ms,
-                     "peak_source": f"{peak_src} bf16_tflops (burst)"},
-        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "ms_per_step": pipe_ms / pipe_steps,
-                "mode": f"{E2E_WORKERS} host threads, each its own context and stream, calling "
-                        "s3dsp_res_block_gn_host concurrently; L2 flushed on the calling stream before every "
-                        "call (inside the timed region); device-timed from one start event to the last call's end",
-                "steps": pipe_steps, "serial_value": total_units / (serial_ms / 1e3),
-                "serial_ms_per_step": serial_ms / args.steps},
-        # inside the timed regions: both graphs' replays, serial host calls, worker calls
-        "gpu_launches": path.launches_per_step * (3 * args.steps + pipe_steps),
-        "clocks": clocks,
-        "wall_s": wall,
-        "breakdown_ms": breakdown,
-    }
-    del graph, marked
-    if world == 1:
-        line["cpu_baseline"] = cpu_baseline(cfg, sample_only=True)
+    line = None
+    if rank == 0:
+        value = total_units / (dev_ms / 1e3)
+        e2e_value = pipe_units / (pipe_ms / 1e3)
+        hbm, tflops, tflops_sus, peak_src = load_peaks()
+        P = pairs_of(ctx, path.coords, torch)
+        conv_avg_ms = float(conv_ms.mean())
+        # conv1 writes bf16 (2 B); conv2 writes f32 and reads the f32 skip (4 + 4 B): their mean
+        roof = conv_roofline(path.conv_kernel, n, c, P, conv_avg_ms, 3.0, 2.0, tflops, hbm, peak_src)
+        roof["per_conv_ms"] = {"conv1": float(phase_ms[:, 1].mean()), "conv2": float(phase_ms[:, 3].mean())}
+        line = {
+            "metric": METRIC, "value": value, "value_per_gpu": value / world, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded ellipsoid shells, random-init weights)",
+            "config": {"workload": "config2: 64^3 shell res block C=256 (subm conv3 -> GN32 -> SiLU -> subm conv3 -> "
+                                   "+skip), hash + kmap rebuilt every step",
+                       "voxels": n, "pairs": P, "channels": c, "objects_per_gpu": 1,
+                       "parallelism": f"objects-dp{world}",
+                       "l2": "flushed between steps (512 MiB write, then 256 MiB read of another buffer)",
+                       "timing": "device steps replayed as a CUDA graph of the library calls (the breakdown and "
+                                 "the roofline's conv time from a second capture with events between the phases); "
+                                 "e2e = s3dsp_res_block_gn_host (host buffers in/out) per step, called by concurrent "
+                                 "host threads of each rank (serial figure beside it)"},
+            "roofline": roof,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": pipe_ms / pipe_steps,
+                    "mode": "per rank: host threads (one per spare CPU of the rank's share of its GPU's NUMA node, "
+                            "at most 4), each its own context and stream, calling s3dsp_res_block_gn_host "
+                            "concurrently; L2 flushed on the calling stream before every call (inside the timed "
+                            "region); device-timed from one start event to the last call's end; max over ranks",
+                    "steps": pipe_steps, "serial_value": total_units / (serial_ms / 1e3),
+                    "serial_ms_per_step": serial_ms / args.steps,
+                    "per_rank_ms": [{"rank": r, "device_step": v[0], "copies_only": v[1], "call_serial": v[2],
+                                     "call_concurrent": v[3], "workers": int(v[4]), "cpus": int(v[5])}
+                                    for r, v in enumerate(per_rank)]},
+            # inside the timed regions: both graphs' replays, serial host calls, worker calls
+            "gpu_launches": path.launches_per_step * (3 * args.steps + pipe_steps),
+            "clocks": clocks,
+            "wall_s": wall,
+            "breakdown_ms": breakdown,
+        }
+        if world == 1:
+            os.sched_setaffinity(0, all_cpus)  # the CPU baseline uses every host core
+            line["cpu_baseline"] = cpu_baseline(cfg, sample_only=True)
+    del path
+    if not args.no_sub:
+        sub = {}
+        for name, fn in (("f32", sub_f32), ("objects_5a", sub_objects), ("volume_5b", sub_volume)):
+            try:
+                sub[name] = fn(args, rank, world, local_rank, stream, flush)
+            except Exception as e:  # a sub-record's failure is reported, not fatal to the headline
+                sub[name] = {"error": repr(e)[:400]}
+                if world > 1:
+                    raise
+        if line is not None:
+            line.update(sub)
+            for name in ("f32", "objects_5a", "volume_5b"):
+                if isinstance(sub.get(name), dict) and "gpu_launches" in sub[name]:
+                    line["gpu_launches"] += sub[name]["gpu_launches"]
     return line
+
+
+# ---------------------------------------------------------------------------
+# sub-record: config 2 in the reference's f32 arithmetic
+# ---------------------------------------------------------------------------
+def sub_f32(args, rank, world, local_rank, stream, flush):
+    """The config-2 step with every activation in f32: PREC_F32_STRICT (FFMA,
+    f32 accumulation: the reference's own arithmetic) and PREC_F32_3XTF32
+    (the tensor cores, within the F32 gate). Same timing as the headline
+    (graph replays, L2 flushed between steps)."""
+    import torch
+    import s3dsp
+    import workloads
+
+    device = torch.device("cuda", local_rank)
+    ctx = s3dsp.Context(local_rank, stream=stream.cuda_stream, flags=s3dsp.CONTEXT_DEFERRED_CHECKS)
+    cfg = workloads.config2(seed=0)
+    if rank > 0:
+        cfg["feats"] = workloads.normal((len(cfg["coords"]), cfg["channels"]), 1000 + rank)
+    steps, warmup = max(1, min(args.steps, 10)), max(3, min(args.warmup, 5))
+    hbm, tflops, _, peak_src = load_peaks()
+    res, outs, launches = {}, {}, 0
+    for name, prec in (("f32_strict", s3dsp.PREC_F32_STRICT), ("f32_3xtf32", s3dsp.PREC_F32_3XTF32)):
+        path = ResBlockPath(s3dsp, ctx, cfg, torch, device, precision=prec)
+        dev_ms, phase_ms = time_graphs(torch, stream, path, flush, steps, warmup, 5)
+        conv_ms = float(np.concatenate([phase_ms[:, 1], phase_ms[:, 3]]).mean())
+        vals = torch.tensor([dev_ms, conv_ms], dtype=torch.float64, device=device)
+        if world > 1:
+            torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX)
+        dev_ms, conv_ms = vals.tolist()
+        outs[name] = path.out.clone()
+        launches += path.launches_per_step * 2 * steps
+        n, c = path.n, path.c
+        P = pairs_of(ctx, path.coords, torch)
+        flops = 2.0 * c * c * P
+        achieved = flops / (conv_ms / 1e3) / 1e12
+        if prec == s3dsp.PREC_F32_STRICT:
+            peak, peak_note = FFMA_PEAK_TFLOPS, "nominal FP32 FFMA peak (148 SMs x 128 lanes x 2 x 1.965 GHz)"
+        else:
+            peak = tflops / 2.0 / 3.0
+            peak_note = (f"3xTF32 effective peak = {peak_src} bf16_tflops / 2 (TF32 runs at half the bf16 rate) / 3 "
+                         "(three MMAs per product)")
+        res[name] = {"value": 2.0 * n * steps * world / (dev_ms / 1e3), "unit": UNIT,
+                     "ms_per_step": dev_ms / steps, "steps": steps, "warmup": warmup, "dtype": "f32",
+                     "kernel": path.conv_kernel,
+                     "breakdown_ms": {k: float(v) for k, v in zip(ResBlockPath.PHASES, phase_ms.mean(0))},
+                     "roofline": {"bound": "fp32" if prec == s3dsp.PREC_F32_STRICT else "tensor",
+                                  "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                                  "flops_per_launch": flops, "avg_launch_ms": conv_ms, "peak_source": peak_note}}
+        del path
+    a, b = outs["f32_3xtf32"].double(), outs["f32_strict"].double()
+    rel = float(torch.linalg.norm(a - b) / torch.linalg.norm(b))
+    ctx.check()
+    if rank != 0:
+        return None
+    res["rel_l2_3xtf32_vs_strict"] = rel
+    res["gpu_launches"] = launches
+    res["note"] = ("same config-2 step as the headline with f32 activations; value = all ranks' outputs / max-rank "
+                   "time; the reference arm computes in f32")
+    return res
 
 
 # ---------------------------------------------------------------------------
 # config 5b: one large volume split in Morton slabs, NCCL halo exchange
 # ---------------------------------------------------------------------------
 VOLUME_RES, VOLUME_THICKNESS, VOLUME_C, VOLUME_LAYERS = 512, 4.0, 128, 8  # ~2.5M voxels
+EXCHANGE_SM_RESERVE = 8  # SMs the interior conv leaves to the halo exchange's NCCL kernel
 
 
-def run_volume(args, rank, world, local_rank):
-    """Config 5b: a 512^3 ellipsoid shell (thickness 4 voxels, ~2.5M active
-    voxels), C = 128, 8 bf16 subm conv layers (+SiLU). Each rank owns a
-    Morton slab; before every layer the one-voxel halo is swapped with one
-    all-to-all (NCCL), then the rank convolves its own rows. Strong scaling:
-    the volume is fixed, ranks split it. Each rank's own rows are ordered
-    interior first: the interior rows' conv runs while the halo is in flight
-    (second stream), the boundary rows' conv after it lands."""
+def sub_volume(args, rank, world, local_rank, stream, flush, steps=None, warmup=None):
+    """Config 5b: a 512^3 ellipsoid shell (thickness 4 voxels, 2,580,824
+    active voxels), C = 128, 8 bf16 subm conv layers (+SiLU), through the
+    C ABI only. Every rank computes its Morton slab and halo lists
+    (s3dsp_shard_plan_morton); before every layer the one-voxel halo is
+    swapped by s3dsp_halo_exchange (one NCCL group of send / receive per
+    peer, on a second context and stream), while the rank's interior rows
+    (no halo needed) are convolved on a context that leaves
+    EXCHANGE_SM_RESERVE SMs to the exchange; the boundary rows' conv waits
+    for the halo. Strong scaling: the volume is fixed, ranks split it.
+
+    On-box parity: after timing, layer 0 is recomputed from features that
+    every rank can generate (a seeded global tensor), through the exchange,
+    with the 128-row kernel on both sides, and each rank compares its own
+    rows against its own whole-volume conv, bit for bit; the mismatch counts
+    are summed over ranks."""
     import torch
     import s3dsp
-    import shard
     import workloads
 
-    torch.cuda.set_device(local_rank)
+    steps = steps or max(1, min(args.steps, 5))
+    warmup = warmup or max(3, min(args.warmup, 3))
     device = torch.device("cuda", local_rank)
-    stream = torch.cuda.Stream(device)
-    torch.cuda.set_stream(stream)
-    ctx = s3dsp.Context(local_rank, stream=stream.cuda_stream, flags=s3dsp.CONTEXT_DEFERRED_CHECKS)
-    coords = workloads.ellipsoid_shell(VOLUME_RES, 0, thickness=VOLUME_THICKNESS)
+    flags = s3dsp.CONTEXT_DEFERRED_CHECKS
+    ctx = s3dsp.Context(local_rank, stream=stream.cuda_stream, flags=flags)       # boundary conv
+    ctx_int = s3dsp.Context(local_rank, stream=stream.cuda_stream, flags=flags)   # interior conv
+    xstream = torch.cuda.Stream(device)
+    ctx_x = s3dsp.Context(local_rank, stream=xstream.cuda_stream, flags=flags)    # halo exchange
+    t_setup = time.perf_counter()
+    coords = workloads.ellipsoid_shell_device(VOLUME_RES, 0, thickness=VOLUME_THICKNESS, device=device)
     n, c = len(coords), VOLUME_C
-    plan = shard.plan_halos(coords, world)[rank]
-    h = ctx.hash_build(torch.from_numpy(plan.shard_coords(coords)).to(device))
-    ni = plan.n_interior
-    # interior rows (no halo needed) and boundary rows as two maps over [own | ghost]
+    plan = s3dsp.ShardPlan(coords, world, rank)
+    n_own, ni, n_ghost = plan.n_own, plan.n_interior, plan.n_ghost
+    rows_global = np.concatenate([plan.own, plan.ghost])
+    shard_coords = torch.from_numpy(np.ascontiguousarray(coords[rows_global])).to(device)
+    comm = None
+    if world > 1:
+        uid = torch.zeros(128, dtype=torch.uint8, device=device)
+        if rank == 0:
+            uid.copy_(torch.frombuffer(bytearray(s3dsp.nccl_unique_id()), dtype=torch.uint8))
+        torch.distributed.broadcast(uid, 0)
+        comm = ctx_x.nccl_comm(world, rank, bytes(uid.cpu().numpy().tobytes()))
+        ctx_int.set_sm_limit(max(1, torch.cuda.get_device_properties(local_rank).multi_processor_count
+                                 - EXCHANGE_SM_RESERVE))
+    h = ctx.hash_build(shard_coords)
     k_int = ctx.kmap_subm3_range(h, 0, ni) if ni > 0 else None
-    k_bnd = ctx.kmap_subm3_range(h, ni, plan.n_own) if plan.n_own > ni else None
+    k_bnd = ctx.kmap_subm3_range(h, ni, n_own) if n_own > ni else None
     P = s3dsp.PREC_BF16
     ws, bs = [], []
     for i in range(VOLUME_LAYERS):
@@ -450,94 +694,157 @@ def run_volume(args, rank, world, local_rank):
                          P, w)
         ws.append(w)
         bs.append(torch.from_numpy(workloads.normal((c,), 200 + i, 0.1)).to(device))
-    rows = plan.n_own + plan.n_ghost
+    rows = n_own + n_ghost
     gen = torch.Generator(device=device).manual_seed(1000 + rank)
     xa = torch.randn((rows, c), generator=gen, device=device).to(torch.bfloat16)
     xb = torch.zeros_like(xa)
-    kernel = ctx.conv_kernel(max(ni, plan.n_own - ni), 27, c, c, P)
-    xstream = torch.cuda.Stream(device)  # the halo exchange runs beside the interior conv
+    kernel = ctx_int.conv_kernel(max(ni, 1), 27, c, c, P)
+    stream.synchronize()
+    setup_s = time.perf_counter() - t_setup
+
+    def layer(cur, nxt, li, e=None, conv_flags=0):
+        ready = torch.cuda.Event()
+        ready.record(stream)  # this layer's input rows are complete
+        done = None
+        if comm is not None:
+            xstream.wait_event(ready)
+            if e:
+                e[3].record(xstream)
+            ctx_x.halo_exchange(plan, comm, cur)
+            done = torch.cuda.Event()
+            done.record(xstream)
+            if e:
+                e[4].record(xstream)
+        if e:
+            e[0].record(stream)
+        if k_int is not None:
+            ctx_int.conv(k_int, 27, P, cur, ws[li], bs[li], nxt[:ni], c, flags=s3dsp.EPI_SILU | conv_flags)
+        if e:
+            e[1].record(stream)
+        if done is not None:
+            stream.wait_event(done)
+        if k_bnd is not None:
+            ctx.conv(k_bnd, 27, P, cur, ws[li], bs[li], nxt[ni:n_own], c, flags=s3dsp.EPI_SILU | conv_flags)
+        if e:
+            e[2].record(stream)
 
     def step(times=None):
         cur, nxt = xa, xb
         for li in range(VOLUME_LAYERS):
             e = [torch.cuda.Event(enable_timing=True) for _ in range(5)] if times is not None else None
-            ready = torch.cuda.Event()
-            ready.record(stream)  # this layer's input rows are complete
-            done = None
-            if world > 1:
-                with torch.cuda.stream(xstream):
-                    xstream.wait_event(ready)
-                    if e:
-                        e[3].record(xstream)
-                    shard.exchange_halo(cur, plan)
-                    done = torch.cuda.Event()
-                    done.record(xstream)
-                    if e:
-                        e[4].record(xstream)
+            layer(cur, nxt, li, e)
             if e:
-                e[0].record(stream)
-            if k_int is not None:
-                ctx.conv(k_int, 27, P, cur, ws[li], bs[li], nxt[:ni], c, flags=s3dsp.EPI_SILU)
-            if e:
-                e[1].record(stream)
-            if done is not None:
-                stream.wait_event(done)
-            if k_bnd is not None:
-                ctx.conv(k_bnd, 27, P, cur, ws[li], bs[li], nxt[ni:plan.n_own], c, flags=s3dsp.EPI_SILU)
-            if e:
-                e[2].record(stream)
                 times.append(e)
             cur, nxt = nxt, cur
 
-    for _ in range(args.warmup):
+    # the exchange alone (nothing else on the GPU)
+    alone_ms = 0.0
+    if comm is not None:
+        for _ in range(3):
+            ctx_x.halo_exchange(plan, comm, xa)
+        xstream.synchronize()
+        torch.distributed.barrier()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(xstream)
+        for _ in range(20):
+            ctx_x.halo_exchange(plan, comm, xa)
+        a1.record(xstream)
+        xstream.synchronize()
+        alone_ms = a0.elapsed_time(a1) / 20
+    for _ in range(warmup):
         step()
     stream.synchronize()
+    xstream.synchronize()
     if world > 1:
         torch.distributed.barrier()
-    sampler = ClockSampler(local_rank)
-    sampler.start()
-    time.sleep(0.3)
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     per_layer = []
-    for i in range(args.steps):
+    for i in range(steps):
         starts[i].record(stream)
         step(per_layer)
         ends[i].record(stream)
     stream.synchronize()
-    clocks = sampler.stop()
+    xstream.synchronize()
     dev_ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends))
-    halo_ms = float(np.mean([e[3].elapsed_time(e[4]) for e in per_layer])) if world > 1 else 0.0
+    halo_ms = float(np.mean([e[3].elapsed_time(e[4]) for e in per_layer])) if comm is not None else 0.0
     int_ms = float(np.mean([e[0].elapsed_time(e[1]) for e in per_layer]))
     layer_ms = float(np.mean([e[0].elapsed_time(e[2]) for e in per_layer]))
+
+    # ---- on-box parity of layer 0: sharded (with the exchange) vs whole volume ----
+    g = torch.Generator(device=device).manual_seed(77)
+    G = torch.randn((n, c), generator=g, device=device).to(torch.bfloat16)
+    own_idx = torch.from_numpy(plan.own).to(device)
+    ghost_idx = torch.from_numpy(plan.ghost).to(device)
+    xs = torch.zeros((rows, c), dtype=torch.bfloat16, device=device)
+    xs[:n_own] = G[own_idx]
+    ys = torch.empty((rows, c), dtype=torch.bfloat16, device=device)
+    layer(xs, ys, 0, conv_flags=s3dsp.CONV_TILE128)
+    stream.synchronize()
+    xstream.synchronize()
+    ghost_ok = bool(torch.equal(xs[n_own:], G[ghost_idx]))
+    hf = ctx.hash_build(torch.from_numpy(coords).to(device))
+    kf = ctx.kmap_subm3(hf)
+    yf = torch.empty((n, c), dtype=torch.bfloat16, device=device)
+    ctx.conv(kf, 27, P, G, ws[0], bs[0], yf, c, flags=s3dsp.EPI_SILU | s3dsp.CONV_TILE128)
+    mism = (ys[:n_own] != yf[own_idx]).any(dim=1).sum().to(torch.float64)
+    kf.free()
+    hf.free()
+    del G, yf, xs, ys
     ctx.check()
-    vals = torch.tensor([dev_ms, halo_ms, int_ms, layer_ms], dtype=torch.float64, device=device)
+    ctx_x.check()
+    vals = torch.tensor([dev_ms, halo_ms, int_ms, layer_ms, alone_ms], dtype=torch.float64, device=device)
+    cnt = torch.tensor([mism.item(), 0.0 if ghost_ok else 1.0, float(n_own)], dtype=torch.float64, device=device)
     if world > 1:
         torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX)
-    dev_ms, halo_ms, int_ms, layer_ms = vals.tolist()
+        torch.distributed.all_reduce(cnt, op=torch.distributed.ReduceOp.SUM)
+    per_rank = gather_rows(torch, world, [float(n_own), float(ni), float(n_ghost)])
+    if comm is not None:
+        torch.cuda.synchronize()
+        s3dsp.load().s3dsp_nccl_comm_free(comm)
+    plan.free(ctx)
+    dev_ms, halo_ms, int_ms, layer_ms, alone_ms = vals.tolist()
+    mismatched, ghost_bad, rows_checked = cnt.tolist()
     if rank != 0:
         return None
-    units = float(n) * VOLUME_LAYERS * args.steps
-    hbm, tflops, tflops_sus, peak_src = load_peaks()
+    units = float(n) * VOLUME_LAYERS * steps
     return {
-        "metric": "active-voxel outputs/s (C=128 subm conv, one volume split in Morton slabs)",
-        "value": units / (dev_ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded 512^3 ellipsoid shell, random features and weights)",
+        "metric": "active-voxel outputs/s (C=128 subm conv, one volume split in Morton slabs), all GPUs",
+        "value": units / (dev_ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": steps, "warmup": warmup,
+        "ms_per_step": dev_ms / steps, "scaling": "strong", "dtype": "bf16",
         "config": {"workload": f"config5b: {VOLUME_RES}^3 shell (thickness {VOLUME_THICKNESS}) {n} voxels, C={c}, "
-                               f"{VOLUME_LAYERS} subm conv layers, Morton slabs + NCCL halo all-to-all",
-                   "voxels": n, "own_rows_rank0": plan.n_own, "interior_rows_rank0": ni,
-                   "ghost_rows_rank0": plan.n_ghost,
-                   "parallelism": f"morton-slabs{world}", "conv_kernel": kernel},
-        "breakdown_ms_per_layer": {"halo_exchange_max_rank": halo_ms, "interior_conv_max_rank": int_ms,
-                                   "layer_max_rank": layer_ms,
-                                   "overlap": "the halo all-to-all runs on a second stream during the interior "
-                                              "rows' conv; the boundary rows' conv waits for it"},
-        "gpu_launches": VOLUME_LAYERS * args.steps * ((k_int is not None) + (k_bnd is not None) +
-                                                      (1 if world > 1 else 0)),
-        "clocks": clocks,
+                               f"{VOLUME_LAYERS} subm conv layers (+SiLU), Morton slabs + C-ABI NCCL halo exchange",
+                   "voxels": n, "parallelism": f"morton-slabs{world}", "conv_kernel_interior": kernel,
+                   "interior_conv_sms": "all" if comm is None else f"SMs - {EXCHANGE_SM_RESERVE}",
+                   "rows_per_rank": [{"own": int(v[0]), "interior": int(v[1]), "ghost": int(v[2])}
+                                     for v in per_rank]},
+        "ms_per_layer_max_rank": {"layer": layer_ms, "interior_conv": int_ms,
+                                  "halo_exchange_under_overlap": halo_ms, "halo_exchange_alone": alone_ms},
+        "parity": {"check": "layer 0 from a seeded global feature tensor: sharded conv over [own | ghost] rows "
+                            "after s3dsp_halo_exchange vs each rank's whole-volume conv (128-row kernel on both "
+                            "sides), compared bit for bit",
+                   "rows_checked": int(rows_checked), "mismatched_rows": int(mismatched),
+                   "ghost_rows_exact": ghost_bad == 0, "bit_exact": mismatched == 0 and ghost_bad == 0},
+        "setup_s_rank0": setup_s,
+        "gpu_launches": VOLUME_LAYERS * steps * ((k_int is not None) + (k_bnd is not None) +
+                                                 (2 if comm is not None else 0)),
     }
+
+
+def run_volume(args, rank, world, local_rank):
+    import torch
+    torch.cuda.set_device(local_rank)
+    stream = torch.cuda.Stream(torch.device("cuda", local_rank))
+    torch.cuda.set_stream(stream)
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    rec = sub_volume(args, rank, world, local_rank, stream, None, steps=args.steps, warmup=args.warmup)
+    clocks = sampler.stop()
+    if rec is None:
+        return None
+    rec.update({"higher_is_better": True, "vs_baseline": None,
+                "data": "synthetic (seeded 512^3 ellipsoid shell, random features and weights)", "clocks": clocks})
+    return rec
 
 
 # ---------------------------------------------------------------------------
@@ -546,7 +853,7 @@ def run_volume(args, rank, world, local_rank):
 OBJECTS, OBJECT_RES = 64, 64
 
 
-def run_objects(args, rank, world, local_rank):
+def sub_objects(args, rank, world, local_rank, stream, flush, steps=None, warmup=None):
     """Config 5a: 64 ellipsoid shells at 64^3 (random axes, seeds 0..63), each
     through the config-4 stack (bf16). Objects are dealt to ranks largest
     first (no collective on the data path). Strong scaling: the batch is
@@ -557,45 +864,42 @@ def run_objects(args, rank, world, local_rank):
     import stack
     import workloads
 
-    torch.cuda.set_device(local_rank)
+    steps = steps or max(1, min(args.steps, 3))
+    warmup = warmup or max(3, min(args.warmup, 3))
     device = torch.device("cuda", local_rank)
-    stream = torch.cuda.Stream(device)
-    torch.cuda.set_stream(stream)
     ctx = s3dsp.Context(local_rank, stream=stream.cuda_stream, flags=s3dsp.CONTEXT_DEFERRED_CHECKS)
-    sizes = [len(workloads.ellipsoid_shell(OBJECT_RES, i)) for i in range(OBJECTS)]
+    shells = [workloads.ellipsoid_shell(OBJECT_RES, i) for i in range(OBJECTS)]
+    sizes = [len(s_) for s_ in shells]
     mine = shard.assign_objects(sizes, world)[rank]
     st = stack.Config4Stack(s3dsp, ctx, stack.config4_params(0), s3dsp.PREC_BF16, device)
     objs = []
     for i in mine:
-        co = workloads.ellipsoid_shell(OBJECT_RES, i)
-        lat = workloads.normal((len(co), stack.LATENT), 5000 + i)
-        objs.append((torch.from_numpy(co).to(device), torch.from_numpy(lat).to(device)))
+        lat = workloads.normal((sizes[i], stack.LATENT), 5000 + i)
+        objs.append((torch.from_numpy(shells[i]).to(device), torch.from_numpy(lat).to(device)))
     units_rank = sum(stack.units(sizes[i]) for i in mine)
 
     def step():
         for co, lat in objs:
             st.forward(co, lat)
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
     stream.synchronize()
     if world > 1:
         torch.distributed.barrier()
-    sampler = ClockSampler(local_rank)
-    sampler.start()
-    time.sleep(0.3)
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    for i in range(args.steps):
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for i in range(steps):
         starts[i].record(stream)
         step()
         ends[i].record(stream)
     stream.synchronize()
-    clocks = sampler.stop()
     dev_ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends))
     ctx.check()
+    per_rank = gather_rows(torch, world, [dev_ms / steps, float(len(mine)), float(sum(sizes[i] for i in mine)),
+                                          float(units_rank)])
     vals = torch.tensor([dev_ms], dtype=torch.float64, device=device)
-    units = torch.tensor([float(units_rank) * args.steps], dtype=torch.float64, device=device)
+    units = torch.tensor([float(units_rank) * steps], dtype=torch.float64, device=device)
     if world > 1:
         torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX)
         torch.distributed.all_reduce(units, op=torch.distributed.ReduceOp.SUM)
@@ -604,17 +908,33 @@ def run_objects(args, rank, world, local_rank):
     if rank != 0:
         return None
     return {
-        "metric": "active-voxel outputs/s (config-4 stack over a batch of 64 objects, sharded by object)",
-        "value": total_units / (dev_ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (64 seeded 64^3 ellipsoid shells with random axes, random latents and weights)",
+        "metric": "active-voxel outputs/s (config-4 stack over a batch of 64 objects, sharded by object), all GPUs",
+        "value": total_units / (dev_ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": steps, "warmup": warmup,
+        "ms_per_step": dev_ms / steps, "scaling": "strong", "dtype": "bf16",
         "config": {"workload": "config5a: 64 objects x config 4 (Linear 8->256, 4 GN res blocks @256, subdivide "
                                "->128 + 2 blocks, subdivide ->64 + 2 blocks, Linear ->32)",
-                   "objects": OBJECTS, "voxels_total": int(sum(sizes)), "objects_rank0": len(mine),
-                   "parallelism": f"objects-dp{world} (largest-first assignment)"},
-        "clocks": clocks,
+                   "objects": OBJECTS, "voxels_total": int(sum(sizes)),
+                   "parallelism": f"objects-dp{world} (largest-first assignment)",
+                   "per_rank": [{"rank": r, "objects": int(v[1]), "voxels": int(v[2]), "units": int(v[3]),
+                                 "ms_per_step": v[0]} for r, v in enumerate(per_rank)]},
     }
+
+
+def run_objects(args, rank, world, local_rank):
+    import torch
+    torch.cuda.set_device(local_rank)
+    stream = torch.cuda.Stream(torch.device("cuda", local_rank))
+    torch.cuda.set_stream(stream)
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    rec = sub_objects(args, rank, world, local_rank, stream, None, steps=args.steps, warmup=args.warmup)
+    clocks = sampler.stop()
+    if rec is None:
+        return None
+    rec.update({"higher_is_better": True, "vs_baseline": None,
+                "data": "synthetic (64 seeded 64^3 ellipsoid shells with random axes, random latents and weights)",
+                "clocks": clocks})
+    return rec
 
 
 # ---------------------------------------------------------------------------
@@ -740,6 +1060,88 @@ def run_layers(args, rank, world, local_rank):
         "frac_of_ffma_peak": None if peak else (flops / (ms / 1e3) / 1e12) / ffma_peak,
         "cpu_baseline": {"value": units / cpu_s, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
                          "sample": "the same layer(s) once through the oracle's f32 restatement"},
+        "clocks": clocks,
+    }
+
+
+# ---------------------------------------------------------------------------
+# the SLat generator's sparse stages (input layer + blocks, out blocks, head)
+# ---------------------------------------------------------------------------
+def run_slat(args, rank, world, local_rank):
+    """One sparse pass of the SLat flow generator (slat_flow_graph.cpp:278-296,
+    :463-531) on the config-1 shell (64^3, seed 0): input Linear 8 -> 128,
+    input_blocks.0 (128), mean-pool + input_blocks.1 (128 -> 1024 coarse),
+    [transformer torso: identity, dense and out of scope], out_blocks.0
+    (2048-concat -> upsample -> 128), out_blocks.1 (256-concat -> 128),
+    LayerNorm + Linear 128 -> 8. Per-object tables are built once (they are
+    reused by all 50 flow steps); a step is one pass with the L2 flushed
+    between steps. Unit: one output voxel of one conv / linear layer.
+    Replicas only at N > 1."""
+    import torch
+    import s3dsp
+    import oracle
+    import slat
+    import workloads
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    stream = torch.cuda.Stream(device)
+    torch.cuda.set_stream(stream)
+    ctx = s3dsp.Context(local_rank, stream=stream.cuda_stream, flags=s3dsp.CONTEXT_DEFERRED_CHECKS)
+    prec = {"f32": s3dsp.PREC_F32_STRICT, "tf32": s3dsp.PREC_F32_3XTF32, "bf16": s3dsp.PREC_BF16}[args.precision]
+    coords = workloads.ellipsoid_shell(64, 0)
+    params, mods_h = slat.slat_params(0), slat.slat_mods(0)
+    x_h = workloads.normal((len(coords), slat.IN_CH), 3)
+    st = slat.SlatSparse(s3dsp, ctx, params, prec, device)
+    tb = slat.SlatTablesDev(s3dsp, ctx, torch.from_numpy(coords).to(device), torch)
+    mods = st.mods_to_device(mods_h)
+    x = torch.from_numpy(x_h).to(device)
+    flush = L2Flush(torch, device)
+    out = None
+    for _ in range(args.warmup):
+        out = st.forward(tb, x, mods)
+        flush()
+    stream.synchronize()
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.3)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for i in range(args.steps):
+        starts[i].record(stream)
+        out = st.forward(tb, x, mods)
+        ends[i].record(stream)
+        flush()
+    stream.synchronize()
+    clocks = sampler.stop()
+    ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends)) / args.steps
+    ctx.check()
+    vals = torch.tensor([ms], dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX)
+    ms = vals.item()
+    if rank != 0:
+        return None
+    u = slat.units(tb.nf, tb.nc)
+    t0 = time.perf_counter()
+    exp = oracle.slat_sparse_forward(coords, x_h, params, mods_h)
+    cpu_s = time.perf_counter() - t0
+    got = out.double().cpu().numpy()
+    rel = float(np.sqrt(((got - exp) ** 2).sum() / (exp.astype(np.float64) ** 2).sum()))
+    return {
+        "metric": "active-voxel outputs/s (SLat generator sparse stages, one pass)", "value": u * world / (ms / 1e3),
+        "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": args.precision,
+        "data": "synthetic (seeded 64^3 ellipsoid shell, random latent, weights and adaLN vectors)",
+        "config": {"workload": "SLat sparse pass: Linear 8->128, res blocks 128 (fine), 128->1024 (coarse), "
+                               "2048-concat->128 (upsampled), 256-concat->128, LayerNorm + Linear 128->8; the "
+                               "transformer torso between them is the identity here",
+                   "fine_voxels": tb.nf, "coarse_voxels": tb.nc, "units_per_step": u,
+                   "l2": "flushed between steps (512 MiB write + 256 MiB read)",
+                   "parallelism": f"replicas{world}"},
+        "rel_l2_vs_oracle": rel,
+        "cpu_baseline": {"value": u / cpu_s, "unit": UNIT, "cores": len(os.sched_getaffinity(0)), "kind": "port",
+                         "sample": "one full pass through the oracle's f32 restatement (all host threads)"},
         "clocks": clocks,
     }
 
@@ -989,6 +1391,9 @@ def run_flexicubes(args, rank, world, local_rank):
 # ---------------------------------------------------------------------------
 # CPU path (reference arm and cpu_baseline)
 # ---------------------------------------------------------------------------
+# ---------------------------------------------------------------------------
+# CPU path (reference arm and cpu_baseline)
+# ---------------------------------------------------------------------------
 def cpu_step(cfg, threads):
     import oracle
     coords = cfg["coords"]
@@ -1002,7 +1407,7 @@ def cpu_step(cfg, threads):
 
 
 def cpu_baseline(cfg, sample_only=False, steps=1, warmup=0):
-    threads = os.cpu_count() or 1
+    threads = len(os.sched_getaffinity(0)) or 1
     for _ in range(warmup):
         cpu_step(cfg, threads)
     t0 = time.perf_counter()
@@ -1025,22 +1430,123 @@ def cpu_baseline(cfg, sample_only=False, steps=1, warmup=0):
 
 
 def run_reference(args, rank, world):
+    """The reference arm: rank 0 alone runs the reference path on all host
+    cores, --warmup untimed and --steps timed full config-2 steps; the other
+    ranks exit without work."""
     if rank != 0:
         return None
     import workloads
     cfg = workloads.config2(seed=0)
-    steps = max(1, min(args.steps, 3))
-    cb = cpu_baseline(cfg, steps=steps, warmup=min(args.warmup, 1))
+    cb = cpu_baseline(cfg, steps=args.steps, warmup=args.warmup)
     return {
-        "metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": world, "steps": steps,
-        "warmup": min(args.warmup, 1), "ms_per_step": cb["s_per_step"] * 1e3, "higher_is_better": True,
+        "metric": METRIC, "value": cb["value"], "value_per_gpu": cb["value"], "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["s_per_step"] * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config2: 64^3 shell res block C=256, hash/tables + block per step",
+        "config": {"workload": "config2: 64^3 shell res block C=256 (subm conv3 -> GN32 -> SiLU -> subm conv3 -> "
+                               "+skip), hash + kmap rebuilt every step",
                    "voxels": len(cfg["coords"]), "channels": cfg["channels"]},
         "impl": "reference",
         "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample", "at_8_threads") if k in cb},
         "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+
+
+# ---------------------------------------------------------------------------
+# single-kernel cases for ncu captures (--profile-case)
+# ---------------------------------------------------------------------------
+PROFILE_CASES = {
+    "conv2": "config-2 conv (C=256, 15,159 voxels), 128-row kernel",
+    "conv_sk": "256^3 shell (241,978 voxels), C=256, stream-K kernel",
+    "tables": "hash + submanifold kmap of the 2.58M-voxel 512^3 shell",
+    "flexicubes": "FlexiCubes extraction of 970,176 cubes at 256^3",
+    "conv1_tf32": "config-1 subm conv (C=64, 15,159 voxels) in 3xTF32",
+    "coords": "SS occupancy -> coords -> surface prune -> downsample (64^3 fixture)",
+    "gs_tables": "GS window tables (both shifts) + APE, config-2 coordinates",
+    "step2": "the config-2 step (hash, kmap, convert, conv1, GN, conv2), eager",
+}
+
+
+def profile_case(case, reps):
+    """Warms up once, then runs the kernel(s) of `case` `reps` times on one
+    stream and synchronises. Inputs are larger than L2 where the case allows
+    it (conv_sk: 124 MB of bf16 features; tables: 41 MB of coordinates, 168 MB
+    of table, 279 MB of map; flexicubes: 392 MB of raw features)."""
+    import torch
+    import s3dsp
+    import workloads
+
+    ctx = s3dsp.Context(0)
+    P = s3dsp.PREC_BF16
+    if case in ("conv2", "conv_sk"):
+        coords = workloads.ellipsoid_shell(64 if case == "conv2" else 256, 0)
+        n, c = len(coords), 256
+        h = ctx.hash_build(torch.from_numpy(coords).cuda())
+        k = ctx.kmap_subm3(h)
+        w = torch.empty(s3dsp.Context.packed_bytes(P, 27, c, c), dtype=torch.uint8, device="cuda")
+        ctx.weights_pack(torch.from_numpy(workloads.kaiming_normal_slat(c, c, 2)), s3dsp.LAYOUT_SLAT_ROW, 27, c, c, P, w)
+        x = torch.from_numpy(workloads.normal((n, c), 1)).cuda().to(torch.bfloat16)
+        b = torch.from_numpy(workloads.normal((c,), 3, 0.1)).cuda()
+        out = torch.empty((n, c), device="cuda")
+        flags = s3dsp.CONV_TILE128 if case == "conv2" else s3dsp.CONV_STREAM_K
+        for _ in range(1 + reps):
+            ctx.conv(k, 27, P, x, w, b, out, c, flags=flags)
+    elif case == "step2":
+        stream = torch.cuda.current_stream()
+        ctx2 = s3dsp.Context(0, stream=stream.cuda_stream, flags=s3dsp.CONTEXT_DEFERRED_CHECKS)
+        path = ResBlockPath(s3dsp, ctx2, workloads.config2(seed=0), torch, torch.device("cuda", 0))
+        for _ in range(1 + reps):
+            path.step()
+        ctx = ctx2
+    elif case == "conv1_tf32":
+        cfg = workloads.config1(0)
+        coords, n, c = cfg["coords"], len(cfg["coords"]), 64
+        k = ctx.kmap_subm3(ctx.hash_build(torch.from_numpy(coords).cuda()))
+        P3 = s3dsp.PREC_F32_3XTF32
+        w = torch.empty(s3dsp.Context.packed_bytes(P3, 27, c, c), dtype=torch.uint8, device="cuda")
+        ctx.weights_pack(torch.from_numpy(cfg["weight"]), s3dsp.LAYOUT_SLAT_ROW, 27, c, c, P3, w)
+        x = torch.from_numpy(cfg["feats"]).cuda()
+        b = torch.from_numpy(cfg["bias"]).cuda()
+        out = torch.empty((n, c), device="cuda")
+        for _ in range(1 + reps):
+            ctx.conv(k, 27, P3, x, w, b, out, c)
+    elif case == "coords":
+        bits = np.load(os.path.join(ROOT, "tests", "golden", "ss_occ_mask.npz"))["bits"]
+        grid = torch.from_numpy(np.unpackbits(bits)[: 64 ** 3].astype(np.float32).reshape(64, 64, 64)).cuda()
+        bufs = [torch.empty((grid.numel(), 4), dtype=torch.int32, device="cuda") for _ in range(3)]
+        for _ in range(1 + reps):
+            m1 = ctx.occupancy_coords(grid, bufs[0])
+            m2 = ctx.prune_surface(bufs[0][:m1], bufs[1])
+            ctx.downsample_coords(bufs[1][:m2], bufs[2], 42000, 2, 42)
+    elif case == "gs_tables":
+        coords = torch.from_numpy(workloads.config2(seed=0)["coords"]).cuda()
+        n = coords.shape[0]
+        bkt = torch.empty(n, dtype=torch.int32, device="cuda")
+        bwd = torch.empty(n, dtype=torch.int32, device="cuda")
+        ape = torch.empty((n, 768), device="cuda")
+        for _ in range(1 + reps):
+            for si in (0, 1):
+                ctx.gs_window_tables(coords, 4 * si, bkt, bwd)
+            ctx.ape(coords, ape)
+    elif case == "flexicubes":
+        t = np.load(os.path.join(ROOT, "tests", "golden", "flexicubes_tables.npz"))
+        tab = ctx.flexicubes_tables(t["dmc"], t["num_dual"], t["check"])
+        coords, raw = workloads.flexicubes_input(64, 0)
+        dc, dr = torch.from_numpy(coords).cuda(), torch.from_numpy(raw).cuda()
+        for _ in range(1 + reps):
+            ctx.flexicubes(tab, dr, dc).free()
+    elif case == "tables":
+        coords = workloads.ellipsoid_shell_device(512, 0, thickness=4.0)  # the config-5b volume
+        d = torch.from_numpy(coords).cuda()
+        for _ in range(1 + reps):
+            h = ctx.hash_build(d)
+            k = ctx.kmap_subm3(h)
+            k.free()
+            h.free()
+    else:
+        raise SystemExit(f"unknown profile case {case!r}; one of {sorted(PROFILE_CASES)}")
+    torch.cuda.synchronize()
+    ctx.check()
+    print(f"{case}: ok", flush=True)
 
 
 def main():
@@ -1050,16 +1556,27 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="config2",
-                    choices=["config2", "config1", "config3", "volume", "objects", "coords", "gs_tables",
+                    choices=["config2", "config1", "config3", "volume", "objects", "slat", "coords", "gs_tables",
                              "flexicubes"],
                     help="config2: the headline (default); volume: config 5b, one volume split across ranks; "
                          "objects: config 5a, 64 objects through config 4 sharded by object; "
-                         "config1 / config3: single layers; coords: the coordinate pipeline before the path; "
+                         "config1 / config3: single layers; slat: the SLat generator's sparse stages; coords: the coordinate pipeline before the path; "
                          "gs_tables: the GS decoder's Swin window tables and APE; flexicubes: the mesh extraction after "
                          "the path")
-    ap.add_argument("--precision", default="f32", choices=["f32", "tf32", "bf16"],
-                    help="config1 / config3 only: f32 = F32-strict FFMA, tf32 = 3xTF32 tensor cores, bf16")
+    ap.add_argument("--precision", default=None, choices=["f32", "tf32", "bf16"],
+                    help="config1 / config3 (default f32) and slat (default bf16): f32 = F32-strict FFMA, "
+                         "tf32 = 3xTF32 tensor cores, bf16")
+    ap.add_argument("--no-sub", action="store_true", help="config2: skip the f32 / 5a / 5b sub-records")
+    ap.add_argument("--profile-case", choices=sorted(PROFILE_CASES),
+                    help="run one small kernel case (for ncu) and exit: " +
+                         "; ".join(f"{k}: {v}" for k, v in PROFILE_CASES.items()))
+    ap.add_argument("--reps", type=int, default=3, help="--profile-case repetitions after one warm-up")
     args = ap.parse_args()
+    if args.precision is None:
+        args.precision = "bf16" if args.workload == "slat" else "f32"
+    if args.profile_case:
+        profile_case(args.profile_case, args.reps)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -1072,7 +1589,8 @@ def main():
             torch.cuda.set_device(local_rank)
             torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                                  device_id=torch.device("cuda", local_rank))
-        runner = {"config2": run_ours, "volume": run_volume, "objects": run_objects, "config1": run_layers,
+        runner = {"config2": run_ours, "volume": run_volume, "objects": run_objects, "slat": run_slat,
+                  "config1": run_layers,
                   "config3": run_layers, "coords": run_coords, "gs_tables": run_gs_tables,
                   "flexicubes": run_flexicubes}[args.workload]
         line = runner(args, rank, world, local_rank)

@@ -105,9 +105,34 @@ S3DSP_API s3d_status s3dsp_context_create(int32_t device, void *stream, uint32_t
                                           uint64_t error_capacity);
 S3DSP_API void s3dsp_context_free(s3dsp_context *ctx);
 S3DSP_API void *s3dsp_context_stream(const s3dsp_context *ctx);
+/* Size this context's persistent and SM-proportional grids (the stream-K
+ * conv, the streaming kernels) for `sms` SMs instead of all of the device's,
+ * so that work on another stream -- a halo exchange's NCCL kernel beside an
+ * interior conv, say -- finds SMs free. 0 restores the device's count. The
+ * kernel choice of s3dsp_conv follows the same count. No counterpart in the
+ * reference (one stream per Backend). */
+S3DSP_API s3d_status s3dsp_context_set_sm_limit(s3dsp_context *ctx, int32_t sms, char *error,
+                                                uint64_t error_capacity);
 /* Waits for the stream and reports (then clears) any device-detected input
  * error recorded since the last check. */
 S3DSP_API s3d_status s3dsp_context_check(s3dsp_context *ctx, char *error, uint64_t error_capacity);
+
+/* Device buffers for a host that links only this library (the counterpart of
+ * the reference's Backend::alloc / set_input_f32 / set_input_i32 /
+ * get_tensor_f32, backend.hpp:16-92): s3dsp_device_alloc returns `bytes` of
+ * device memory on the context's device (cudaMalloc; freed by
+ * s3dsp_device_free, which first waits for the context's stream);
+ * s3dsp_copy_to_device queues a host -> device copy on the context's stream
+ * (the host buffer must stay valid until the stream reaches it: pageable
+ * memory is staged before the call returns); s3dsp_copy_to_host copies
+ * device -> host and waits for it (synchronous). */
+S3DSP_API s3d_status s3dsp_device_alloc(s3dsp_context *ctx, uint64_t bytes, void **out, char *error,
+                                        uint64_t error_capacity);
+S3DSP_API void s3dsp_device_free(s3dsp_context *ctx, void *d_ptr);
+S3DSP_API s3d_status s3dsp_copy_to_device(s3dsp_context *ctx, void *d_dst, const void *h_src, uint64_t bytes,
+                                          char *error, uint64_t error_capacity);
+S3DSP_API s3d_status s3dsp_copy_to_host(s3dsp_context *ctx, void *h_dst, const void *d_src, uint64_t bytes,
+                                        char *error, uint64_t error_capacity);
 
 /* Device memory the library holds on `device`. Every table, map and scratch
  * buffer the library allocates comes from its own stream-ordered pool (made
@@ -376,6 +401,15 @@ S3DSP_API int64_t s3dsp_kmap_rows(const s3dsp_kmap *kmap);
 S3DSP_API s3d_status s3dsp_kmap_export_dense(s3dsp_context *ctx, const s3dsp_kmap *kmap,
                                              uint32_t sentinel_mode, int32_t *d_out, char *error,
                                              uint64_t error_capacity);
+/* A new map reading through a row table: entry (o, r) = d_rows[kmap(o, r)]
+ * (none stays none). d_rows int32 [kmap input rows], values in
+ * [0, n_rows_in); an out-of-range value becomes "none" and is reported by the
+ * next status check. Used to gather coarse rows for a fine map (nearest
+ * upsampling without building the upsampled rows). No reference counterpart:
+ * the reference materialises the upsampled tensor (slat_flow_graph.cpp:185-190). */
+S3DSP_API s3d_status s3dsp_kmap_compose(s3dsp_context *ctx, const s3dsp_kmap *kmap, const int32_t *d_rows,
+                                        int64_t n_rows_in, s3dsp_kmap **out, char *error,
+                                        uint64_t error_capacity);
 /* Offset-sorted (in, out) pair lists: for each offset o in order, the pairs
  * with a neighbour, sorted by output row. d_in/d_out hold capacity int32
  * each (27*n_out always suffices); h_offsets receives kvol+1 host int64
@@ -446,6 +480,23 @@ S3DSP_API s3d_status s3dsp_conv(s3dsp_context *ctx, const s3dsp_kmap *kmap, int3
                                 const float *pro_mul, const float *pro_add, double *gn_partials,
                                 int32_t gn_groups, char *error, uint64_t error_capacity);
 
+/* s3dsp_conv over the channel concat of two tensors, ggml_concat(a, b, 0) of
+ * the out_blocks (slat_flow_graph.cpp:466, :497): channels [0, cin_a) of a
+ * gathered row come from in_a [n_in, cin_a], channels [cin_a, cin_a + cin_b)
+ * from in_b [n_in, cin_b] (the same row of both). The concat is never built:
+ * the gather picks the source per channel chunk. weight is packed for
+ * cin = cin_a + cin_b; pro_* arrays (F32 strict) index the concat channels.
+ * Each width must meet the precision's alignment (BF16: % 8, f32: % 4). */
+S3DSP_API s3d_status s3dsp_conv_concat(s3dsp_context *ctx, const s3dsp_kmap *kmap, int32_t kvol,
+                                       uint32_t precision, const void *in_a, int64_t cin_a,
+                                       const void *in_b, int64_t cin_b, uint32_t in_dtype, int64_t n_in,
+                                       int32_t in_shift, const void *weight, const float *bias,
+                                       const void *residual, uint32_t res_dtype, int32_t res_shift, void *out,
+                                       uint32_t out_dtype, int64_t n_out, int64_t cout, uint32_t flags,
+                                       const float *pro_sub, const float *pro_mul, const float *pro_add,
+                                       double *gn_partials, int32_t gn_groups, char *error,
+                                       uint64_t error_capacity);
+
 /* Name of the kernel s3dsp_conv launches for this shape on ctx's device
  * ("conv_f32_kernel", "conv_tc_kernel" = 128-row tiles, "conv_sk_kernel<256>"
  * / "conv_sk_kernel<128>" = stream-K over 256- / 128-row tiles), or NULL for
@@ -483,6 +534,15 @@ S3DSP_API s3d_status s3dsp_layer_norm(s3dsp_context *ctx, const void *x, uint32_
                                       const float *beta, const float *mod_scale,
                                       const float *mod_shift, int32_t silu, void *y,
                                       uint32_t y_dtype, char *error, uint64_t error_capacity);
+/* s3dsp_layer_norm of the channel concat of xa [n, ca] and xb [n, cb] (the
+ * out_blocks' norm1 over ggml_concat, slat_flow_graph.cpp:466-477): y
+ * [n, ca + cb]; gamma / beta / mod arrays index the concat channels. */
+S3DSP_API s3d_status s3dsp_layer_norm_concat(s3dsp_context *ctx, const void *xa, int64_t ca,
+                                             const void *xb, int64_t cb, uint32_t x_dtype, int64_t n,
+                                             float eps, const float *gamma, const float *beta,
+                                             const float *mod_scale, const float *mod_shift, int32_t silu,
+                                             void *y, uint32_t y_dtype, char *error,
+                                             uint64_t error_capacity);
 /* Element type conversion of count elements. */
 S3DSP_API s3d_status s3dsp_convert(s3dsp_context *ctx, const void *x, uint32_t x_dtype, void *y,
                                    uint32_t y_dtype, int64_t count, char *error,
@@ -556,6 +616,27 @@ S3DSP_API s3d_status s3dsp_slat_res_block(s3dsp_context *ctx, const s3dsp_kmap *
                                           const float *conv2_b, const void *skip_w,
                                           const float *skip_b, float *out, char *error,
                                           uint64_t error_capacity);
+/* The generator's res_block in every form the SLat forward uses
+ * (slat_flow_graph.cpp:216-275 for input_blocks.0/1, :463-524 for out_blocks.0/1):
+ *   - input: x_a [n_in, cin_a], or the channel concat of x_a and x_b
+ *     [n_in, cin_b] (x_b NULL, cin_b 0 for one source), f32;
+ *   - up_rows NULL: n_in == kmap rows (input_blocks, out_blocks.1);
+ *     up_rows int32 [kmap rows]: the block runs at the fine resolution of
+ *     `kmap` on the nearest upsample of its coarse input (out_blocks.0,
+ *     upsample at :467 = get_rows by fine_to_coarse, :185-190); the
+ *     upsampled tensor is never built -- norm1 and the skip Linear run on
+ *     the coarse rows (both are row-wise) and conv1 gathers coarse rows
+ *     through the kernel map composed with up_rows;
+ *   - skip: identity when one source, no upsample and cin == cout; otherwise
+ *     the Linear skip_w/skip_b (packed LINEAR for cin_a + cin_b -> cout).
+ * out [kmap rows, cout] f32. Entries of up_rows outside [0, n_in) are read
+ * as "no row" and reported by the next status check. */
+S3DSP_API s3d_status s3dsp_slat_res_block_concat(
+    s3dsp_context *ctx, const s3dsp_kmap *kmap, const int32_t *up_rows, uint32_t precision, const float *x_a,
+    int64_t cin_a, const float *x_b, int64_t cin_b, int64_t n_in, int64_t cout, const float *norm1_w,
+    const float *norm1_b, const void *conv1_w, const float *conv1_b, const float *mod_scale,
+    const float *mod_shift, const void *conv2_w, const float *conv2_b, const void *skip_w, const float *skip_b,
+    float *out, char *error, uint64_t error_capacity);
 /* Host-buffer forms (what decode_object_mesh does per level with its Backend,
  * session.cpp:927-962): upload coords + features, build the tables, run the
  * block, read the result back. Synchronous. */

@@ -360,16 +360,59 @@ def mesh_upsample_level(x, neighbors, p, threads=0, taps=None):
 
 
 def slat_res_block(x, nbr_slat, norm1_w, norm1_b, w1, b1, mod_scale, mod_shift, w2, b2, skip_w=None, skip_b=None,
-                   threads=0):
+                   threads=0, accum64=False):
     """res_block of slat_flow_graph.cpp:216-275 (no down/up): LayerNorm(1e-6,
     affine) -> SiLU -> conv1 -> LayerNorm(1e-6) -> modulate -> SiLU -> conv2
-    -> + skip (identity, or Linear when the width changes, :266-272)."""
+    -> + skip (identity, or Linear when the width changes, :266-272).
+    accum64: the convs' dot products in float64 (a second check)."""
     h = layer_norm(x, 1e-6, norm1_w, norm1_b, silu=True)
-    h = subm_conv_slat(h, nbr_slat, w1, b1, threads=threads)
+    h = subm_conv_slat(h, nbr_slat, w1, b1, accum64=accum64, threads=threads)
     h = layer_norm(h, 1e-6, None, None, mod_scale, mod_shift, silu=True)
-    h = subm_conv_slat(h, nbr_slat, w2, b2, threads=threads)
+    h = subm_conv_slat(h, nbr_slat, w2, b2, accum64=accum64, threads=threads)
     skip = x if skip_w is None else linear(x, skip_w, skip_b, threads=threads)
     return h + skip
+
+
+def slat_sparse_forward(coords, x, p, mods, mid=None, threads=0, accum64=False, taps=None):
+    """The SLat flow generator's sparse stages, in the reference's op order
+    (slat_flow_graph.cpp): input_layer Linear (:283-285); input_blocks.0
+    res_block on the fine map (:290-291); 2x mean-pool down (:159-183) +
+    input_blocks.1 res_block on the coarse map with a Linear skip (:294-296);
+    `mid` (the dense APE + transformer torso, :298-460; identity when None);
+    out_blocks.0: ggml_concat(h, skip1) -> nearest upsample (:185-190) ->
+    res_block with a Linear skip (:463-495); out_blocks.1: ggml_concat(h,
+    skip0) -> res_block with a Linear skip (:496-524); LayerNorm(1e-6, no
+    affine) -> out_layer Linear (:527-531). Tables by SlatTables::build
+    (sparse_ops.cpp:49-173). p / mods as sam3d.cpp_b200/slat.py makes them.
+    Returns [nf, out_ch] f32; `taps` (a dict) receives the intermediates."""
+    t = slat_tables(coords)
+    nf = len(coords)
+    nc = len(t["coarse_inv_count"])
+    fine = t["conv_fine"].reshape(nf, 27)
+    coarse = t["conv_coarse"].reshape(nc, 27)
+
+    def block(name, xin, nbr):
+        b = p[name]
+        sc, sh = mods[name]
+        return slat_res_block(xin, nbr, b["norm1_w"], b["norm1_b"], b["conv1_w"], b["conv1_b"], sc, sh, b["conv2_w"],
+                              b["conv2_b"], b.get("skip_w"), b.get("skip_b"), threads=threads, accum64=accum64)
+
+    h = linear(x, p["input_layer"]["w"], p["input_layer"]["b"], threads=threads)
+    skip0 = block("input_blocks.0", h, fine)
+    d = downsample_mean(skip0, t["coarse_children"], t["coarse_inv_count"])
+    skip1 = block("input_blocks.1", d, coarse)
+    h = skip1 if mid is None else mid(skip1)
+    xin = upsample_nearest(np.concatenate([h, skip1], axis=1), t["fine_to_coarse"])
+    h = block("out_blocks.0", xin, fine)
+    ob0 = h
+    xin = np.concatenate([h, skip0], axis=1)
+    h = block("out_blocks.1", xin, fine)
+    ob1 = h
+    h = layer_norm(h, 1e-6)
+    out = linear(h, p["out_layer"]["w"], p["out_layer"]["b"], threads=threads)
+    if taps is not None:
+        taps.update(skip0=skip0, skip1=skip1, out_blocks0=ob0, out_blocks1=ob1, out=out)
+    return out
 
 
 # ---------------------------------------------------------------------------

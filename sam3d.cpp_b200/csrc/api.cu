@@ -61,6 +61,7 @@ extern "C" S3DSP_API s3d_status s3dsp_context_create(int32_t device, void* strea
     ctx->device = device;
     ctx->flags = flags;
     ctx->sm_count = prop.multiProcessorCount;
+    ctx->sm_device = prop.multiProcessorCount;
     if (!(flags & S3DSP_CONTEXT_OWN_STREAM)) {
         ctx->stream = (cudaStream_t)stream;  // NULL = the legacy default stream
     } else {
@@ -101,6 +102,15 @@ extern "C" S3DSP_API void* s3dsp_context_stream(const s3dsp_context* ctx) {
     return ctx ? (void*)ctx->stream : nullptr;
 }
 
+extern "C" S3DSP_API s3d_status s3dsp_context_set_sm_limit(s3dsp_context* ctx, int32_t sms, char* error,
+                                                          uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "ctx is NULL");
+    if (sms < 0) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "negative SM limit %d", sms);
+    ctx->sm_count = (sms == 0 || sms > ctx->sm_device) ? ctx->sm_device : sms;
+    return S3D_OK;
+}
+
 namespace s3dsp {
 s3d_status check_status(s3dsp_context* ctx, char* error, uint64_t error_capacity) {
     uint32_t st[4] = {0, 0, 0, 0};
@@ -118,6 +128,9 @@ s3d_status check_status(s3dsp_context* ctx, char* error, uint64_t error_capacity
                     "duplicate coordinate (%u rows repeat an earlier row)", st[1]);
     if (st[0] & kErrHashFull)
         return fail(error, error_capacity, S3D_INTERNAL_ERROR, "coordinate hash probe bound exceeded");
+    if (st[0] & kErrRowRange)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT,
+                    "a row index passed in (upsample / composition rows) is outside its input table");
     if (st[0] & kErrPipelineTimeout)
         return fail(error, error_capacity, S3D_INTERNAL_ERROR,
                     "a device pipeline wait timed out (kernel aborted)");
@@ -160,5 +173,49 @@ extern "C" S3DSP_API s3d_status s3dsp_memory_stats(int32_t device, uint64_t* res
         v = 0;  // resets the high-water mark to the current use
         S3DSP_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrUsedMemHigh, &v), "pool attribute");
     }
+    return S3D_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Device buffers for hosts that link only this library (the counterpart of
+// Backend::alloc / set_input_* / get_tensor_f32, backend.hpp:16-92)
+// ---------------------------------------------------------------------------
+extern "C" S3DSP_API s3d_status s3dsp_device_alloc(s3dsp_context* ctx, uint64_t bytes, void** out, char* error,
+                                                  uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx || !out) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
+    *out = nullptr;
+    S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    S3DSP_CUDA(cudaMalloc(out, bytes > 0 ? bytes : 16), "cudaMalloc");
+    return S3D_OK;
+}
+
+extern "C" S3DSP_API void s3dsp_device_free(s3dsp_context* ctx, void* p) {
+    if (!p) return;
+    if (ctx) {
+        cudaSetDevice(ctx->device);
+        if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    }
+    cudaFree(p);
+}
+
+extern "C" S3DSP_API s3d_status s3dsp_copy_to_device(s3dsp_context* ctx, void* d_dst, const void* h_src,
+                                                    uint64_t bytes, char* error, uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx || (bytes && (!d_dst || !h_src))) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
+    if (!bytes) return S3D_OK;
+    S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    S3DSP_CUDA(cudaMemcpyAsync(d_dst, h_src, bytes, cudaMemcpyHostToDevice, ctx->stream), "host to device copy");
+    return S3D_OK;
+}
+
+extern "C" S3DSP_API s3d_status s3dsp_copy_to_host(s3dsp_context* ctx, void* h_dst, const void* d_src, uint64_t bytes,
+                                                  char* error, uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx || (bytes && (!d_src || !h_dst))) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
+    S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    if (bytes)
+        S3DSP_CUDA(cudaMemcpyAsync(h_dst, d_src, bytes, cudaMemcpyDeviceToHost, ctx->stream), "device to host copy");
+    S3DSP_CUDA(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
     return S3D_OK;
 }

@@ -61,6 +61,9 @@ extern "C" S3DSP_API s3d_status s3dsp_res_block_gn(s3dsp_context* ctx, const s3d
     }
     // tensor-core precisions read their activations materialised: bf16 for BF16,
     // f32 for 3xTF32 (GN + SiLU applied by s3dsp_channel_affine, not a prologue)
+    // BF16: conv1's output is stored in bf16 (its GroupNorm partial sums come
+    // from the f32 accumulators before rounding) and GN + SiLU read it back
+    // in bf16, halving that round trip
     const bool bf = precision == S3DSP_PREC_BF16;
     const uint32_t adt = bf ? S3DSP_BF16 : S3DSP_F32;
     const void* xin = x;
@@ -72,10 +75,10 @@ extern "C" S3DSP_API s3d_status s3dsp_res_block_gn(s3dsp_context* ctx, const s3d
         xin = xb;
     }
     S3DSP_CUDA(sc.get(&hb, dtype_size(adt) * (size_t)(n * c)), "scratch");
-    S3DSP_TRY(s3dsp_conv(ctx, kmap, 27, precision, xin, adt, n, c, 0, w1, b1, nullptr, 0, 0, y1, S3DSP_F32, n, c, 0,
+    S3DSP_TRY(s3dsp_conv(ctx, kmap, 27, precision, xin, adt, n, c, 0, w1, b1, nullptr, 0, 0, y1, adt, n, c, 0,
                          nullptr, nullptr, nullptr, part, groups, error, error_capacity));
     S3DSP_TRY(s3dsp_gn_finalize(ctx, part, n, c, groups, eps, gamma, beta, sub, mul, add, error, error_capacity));
-    S3DSP_TRY(s3dsp_channel_affine(ctx, y1, S3DSP_F32, n, c, sub, mul, add, 1, hb, adt, error, error_capacity));
+    S3DSP_TRY(s3dsp_channel_affine(ctx, y1, adt, n, c, sub, mul, add, 1, hb, adt, error, error_capacity));
     return s3dsp_conv(ctx, kmap, 27, precision, hb, adt, n, c, 0, w2, b2, x, S3DSP_F32, 0, out, S3DSP_F32, n, c, 0,
                       nullptr, nullptr, nullptr, nullptr, 0, error, error_capacity);
 }
@@ -143,10 +146,12 @@ extern "C" S3DSP_API s3d_status s3dsp_mesh_upsample_level(
         xin = xb;
     }
     S3DSP_TRY(s3dsp_channel_affine(ctx, x, S3DSP_F32, np, cin, sub1, mul1, add1, 1, h1, adt, error, error_capacity));
-    S3DSP_TRY(s3dsp_conv(ctx, kmap, 27, precision, h1, adt, np, cin, 3, conv1_w, conv1_b, nullptr, 0, 0, y1, S3DSP_F32,
+    // conv1's output in the activation dtype (bf16 for BF16: GN2 partials come
+    // from the f32 accumulators, the bf16 copy is only what GN2 + SiLU read)
+    S3DSP_TRY(s3dsp_conv(ctx, kmap, 27, precision, h1, adt, np, cin, 3, conv1_w, conv1_b, nullptr, 0, 0, y1, adt,
                          nc, cout, 0, nullptr, nullptr, nullptr, part, groups, error, error_capacity));
     S3DSP_TRY(s3dsp_gn_finalize(ctx, part, nc, cout, groups, eps, gn2_w, gn2_b, sub2, mul2, add2, error, error_capacity));
-    S3DSP_TRY(s3dsp_channel_affine(ctx, y1, S3DSP_F32, nc, cout, sub2, mul2, add2, 1, h2, adt, error, error_capacity));
+    S3DSP_TRY(s3dsp_channel_affine(ctx, y1, adt, nc, cout, sub2, mul2, add2, 1, h2, adt, error, error_capacity));
     S3DSP_TRY(s3dsp_conv(ctx, nullptr, 1, precision, xin, adt, np, cin, 0, skip_w, skip_b, nullptr, 0, 0, skip,
                          S3DSP_F32, np, cout, 0, nullptr, nullptr, nullptr, nullptr, 0, error, error_capacity));
     return s3dsp_conv(ctx, kmap, 27, precision, h2, adt, nc, cout, 0, conv2_w, conv2_b, skip, S3DSP_F32, 3, out,
@@ -202,6 +207,129 @@ extern "C" S3DSP_API s3d_status s3dsp_slat_res_block(s3dsp_context* ctx, const s
     }
     return s3dsp_conv(ctx, kmap, 27, precision, h2, hdt, n, cout, 0, conv2_w, conv2_b, res, S3DSP_F32, 0, out, S3DSP_F32,
                       n, cout, 0, nullptr, nullptr, nullptr, nullptr, 0, error, error_capacity);
+}
+
+namespace {
+// y[r] = x[rows[r]] for f32 rows of c channels (c % 4 == 0, 16-byte rows); a
+// row index outside [0, n_in) gives a zero row and sets kErrRowRange
+__global__ void gather_rows_f32_kernel(const float4* __restrict__ x, int64_t n_in, int c4,
+                                       const int32_t* __restrict__ rows, int64_t n_out, float4* __restrict__ y,
+                                       uint32_t* __restrict__ status) {
+    pdl_wait();
+    pdl_trigger();
+    const int64_t total = n_out * c4;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / c4, q = i - r * c4;
+        const int32_t s = __ldg(rows + r);
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (s >= 0 && s < n_in)
+            v = x[(int64_t)s * c4 + q];
+        else if (q == 0)
+            atomicOr(status, kErrRowRange);
+        y[i] = v;
+    }
+}
+}  // namespace
+
+extern "C" S3DSP_API s3d_status s3dsp_slat_res_block_concat(
+    s3dsp_context* ctx, const s3dsp_kmap* kmap, const int32_t* up_rows, uint32_t precision, const float* x_a,
+    int64_t cin_a, const float* x_b, int64_t cin_b, int64_t n_in, int64_t cout, const float* norm1_w,
+    const float* norm1_b, const void* conv1_w, const float* conv1_b, const float* mod_scale, const float* mod_shift,
+    const void* conv2_w, const float* conv2_b, const void* skip_w, const float* skip_b, float* out, char* error,
+    uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx || !kmap || !x_a || !conv1_w || !conv2_w || !out)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
+    if (x_b ? cin_b <= 0 : cin_b != 0)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "second source and its width disagree");
+    const int64_t n = kmap->n_out;
+    const int64_t cin = cin_a + cin_b;
+    if (cin_a <= 0 || cout <= 0 || n_in <= 0) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "bad shape");
+    if (!up_rows && n_in != n) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "n_in != kmap rows");
+    if (up_rows && kmap->n_in != n)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "an upsampling block needs the fine rows' own map");
+    const bool identity_skip = cin == cout && !x_b && !up_rows;
+    if (!identity_skip && !skip_w)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT,
+                    "a width change, a concat or an upsample needs the skip Linear (slat_flow_graph.cpp:266-272)");
+    if (up_rows && cout % 4)
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "upsampled skip rows need cout %% 4 == 0");
+    S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    const float eps = 1e-6f;  // gb_layer_norm in res_block (slat_flow_graph.cpp:245-255)
+    const bool bf = precision == S3DSP_PREC_BF16;
+    const uint32_t hdt = bf ? S3DSP_BF16 : S3DSP_F32;
+    const size_t hsz = bf ? 2 : 4;
+    Scratch sc(ctx->stream);
+    void *h1, *h2;
+    float *y1, *skip = nullptr;
+    S3DSP_CUDA(sc.get(&h1, hsz * (size_t)(n_in * cin)), "scratch");
+    S3DSP_CUDA(sc.get(&h2, hsz * (size_t)(n * cout)), "scratch");
+    S3DSP_CUDA(sc.get(&y1, 4 * (size_t)(n * cout)), "scratch");
+    // norm1 (affine) -> SiLU over the input rows (coarse rows when upsampling:
+    // nearest upsampling repeats rows, so it commutes with the row-wise norm)
+    if (x_b)
+        S3DSP_TRY(s3dsp_layer_norm_concat(ctx, x_a, cin_a, x_b, cin_b, S3DSP_F32, n_in, eps, norm1_w, norm1_b, nullptr,
+                                          nullptr, 1, h1, hdt, error, error_capacity));
+    else
+        S3DSP_TRY(s3dsp_layer_norm(ctx, x_a, S3DSP_F32, n_in, cin, eps, norm1_w, norm1_b, nullptr, nullptr, 1, h1, hdt,
+                                   error, error_capacity));
+    // conv1 over the fine map; upsampling reads the coarse rows through the
+    // map composed with up_rows (the upsampled tensor is never built)
+    s3dsp_kmap* k1 = nullptr;
+    if (up_rows) S3DSP_TRY(s3dsp_kmap_compose(ctx, kmap, up_rows, n_in, &k1, error, error_capacity));
+    struct KmapGuard {
+        s3dsp_context* c;
+        s3dsp_kmap* k;
+        ~KmapGuard() {
+            if (k) s3dsp_kmap_free(c, k);
+        }
+    } guard{ctx, k1};
+    S3DSP_TRY(s3dsp_conv(ctx, k1 ? k1 : kmap, 27, precision, h1, hdt, n_in, cin, 0, conv1_w, conv1_b, nullptr, 0, 0,
+                         y1, S3DSP_F32, n, cout, 0, nullptr, nullptr, nullptr, nullptr, 0, error, error_capacity));
+    // norm2 (no affine) -> modulate -> SiLU
+    S3DSP_TRY(s3dsp_layer_norm(ctx, y1, S3DSP_F32, n, cout, eps, nullptr, nullptr, mod_scale, mod_shift, 1, h2, hdt,
+                               error, error_capacity));
+    // skip: identity, or the Linear of the (concatenated) input rows, computed
+    // on the input rows and then upsampled (the Linear is row-wise too)
+    const float* res = x_a;
+    if (!identity_skip) {
+        const void *sa = x_a, *sb = x_b;
+        if (bf) {
+            __nv_bfloat16 *xa16, *xb16 = nullptr;
+            S3DSP_CUDA(sc.get(&xa16, 2 * (size_t)(n_in * cin_a)), "scratch");
+            S3DSP_TRY(s3dsp_convert(ctx, x_a, S3DSP_F32, xa16, S3DSP_BF16, n_in * cin_a, error, error_capacity));
+            if (x_b) {
+                S3DSP_CUDA(sc.get(&xb16, 2 * (size_t)(n_in * cin_b)), "scratch");
+                S3DSP_TRY(s3dsp_convert(ctx, x_b, S3DSP_F32, xb16, S3DSP_BF16, n_in * cin_b, error, error_capacity));
+            }
+            sa = xa16;
+            sb = xb16;
+        }
+        float* skip_in;
+        S3DSP_CUDA(sc.get(&skip_in, 4 * (size_t)(n_in * cout)), "scratch");
+        if (x_b)
+            S3DSP_TRY(s3dsp_conv_concat(ctx, nullptr, 1, precision, sa, cin_a, sb, cin_b, hdt, n_in, 0, skip_w, skip_b,
+                                        nullptr, 0, 0, skip_in, S3DSP_F32, n_in, cout, 0, nullptr, nullptr, nullptr,
+                                        nullptr, 0, error, error_capacity));
+        else
+            S3DSP_TRY(s3dsp_conv(ctx, nullptr, 1, precision, sa, hdt, n_in, cin, 0, skip_w, skip_b, nullptr, 0, 0,
+                                 skip_in, S3DSP_F32, n_in, cout, 0, nullptr, nullptr, nullptr, nullptr, 0, error,
+                                 error_capacity));
+        skip = skip_in;
+        if (up_rows) {
+            S3DSP_CUDA(sc.get(&skip, 4 * (size_t)(n * cout)), "scratch");
+            const int c4 = (int)(cout / 4);
+            int64_t g = (n * c4 + 255) / 256;
+            if (g > (int64_t)ctx->sm_count * 16) g = (int64_t)ctx->sm_count * 16;
+            S3DSP_CUDA(launch_pdl(gather_rows_f32_kernel, dim3((unsigned)(g < 1 ? 1 : g)), dim3(256), 0, ctx->stream,
+                                  reinterpret_cast<const float4*>(skip_in), n_in, c4, up_rows, n,
+                                  reinterpret_cast<float4*>(skip), ctx->d_status),
+                       "gather_rows_f32_kernel");
+        }
+        res = skip;
+    }
+    return s3dsp_conv(ctx, kmap, 27, precision, h2, hdt, n, cout, 0, conv2_w, conv2_b, res, S3DSP_F32, 0, out,
+                      S3DSP_F32, n, cout, 0, nullptr, nullptr, nullptr, nullptr, 0, error, error_capacity);
 }
 
 // ---------------------------------------------------------------------------

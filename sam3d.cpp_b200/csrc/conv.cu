@@ -47,15 +47,15 @@ extern "C" S3DSP_API const char* s3dsp_conv_kernel(const s3dsp_context* ctx, int
     return bf16_kernel_name(pick_bf16_kernel(ctx, n_out, kvol, flags));
 }
 
-extern "C" S3DSP_API s3d_status s3dsp_conv(s3dsp_context* ctx, const s3dsp_kmap* kmap, int32_t kvol,
-                                           uint32_t precision, const void* in, uint32_t in_dtype, int64_t n_in,
-                                           int64_t cin, int32_t in_shift, const void* weight, const float* bias,
-                                           const void* residual, uint32_t res_dtype, int32_t res_shift, void* out,
-                                           uint32_t out_dtype, int64_t n_out, int64_t cout, uint32_t flags,
-                                           const float* pro_sub, const float* pro_mul, const float* pro_add,
-                                           double* gn_partials, int32_t gn_groups, char* error,
-                                           uint64_t error_capacity) {
-    clear_error(error, error_capacity);
+namespace {
+
+// s3dsp_conv and s3dsp_conv_concat: in_b == nullptr is one source (cin_a == cin)
+s3d_status conv_impl(s3dsp_context* ctx, const s3dsp_kmap* kmap, int32_t kvol, uint32_t precision, const void* in,
+                     const void* in_b, int64_t cin_a, uint32_t in_dtype, int64_t n_in, int64_t cin, int32_t in_shift,
+                     const void* weight, const float* bias, const void* residual, uint32_t res_dtype,
+                     int32_t res_shift, void* out, uint32_t out_dtype, int64_t n_out, int64_t cout, uint32_t flags,
+                     const float* pro_sub, const float* pro_mul, const float* pro_add, double* gn_partials,
+                     int32_t gn_groups, char* error, uint64_t error_capacity) {
     if (!ctx || !in || !weight || !out) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
     if (kmap) {
         if (kvol != kmap->kvol)
@@ -68,6 +68,9 @@ extern "C" S3DSP_API s3d_status s3dsp_conv(s3dsp_context* ctx, const s3dsp_kmap*
     }
     if (n_out < 0 || n_in < 0 || cin <= 0 || cout <= 0 || cin > 65536 || cout > 65536)
         return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "bad shape");
+    if (in_b && (cin_a <= 0 || cin_a >= cin))
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "concat split %lld outside (0, %lld)",
+                    (long long)cin_a, (long long)cin);
     if (n_out == 0) return S3D_OK;
     if (n_out > (1ll << 31) - 128) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "n_out too large");
     if (in_shift < 0 || in_shift > 8 || res_shift < 0 || res_shift > 8)
@@ -86,17 +89,19 @@ extern "C" S3DSP_API s3d_status s3dsp_conv(s3dsp_context* ctx, const s3dsp_kmap*
                     gn_groups, (long long)cout);
     if ((flags & S3DSP_PRO_AFFINE_SILU) && (!pro_sub || !pro_mul || !pro_add))
         return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "prologue arrays missing");
+    const int ca = (int)(in_b ? cin_a : cin);
     S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
 
     cudaError_t e;
     if (precision == S3DSP_PREC_F32_STRICT) {
         if (in_dtype != S3DSP_F32)
             return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "F32_STRICT needs f32 input");
-        if (cin % 4 || ((uintptr_t)in & 15))
-            return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "F32_STRICT needs cin %% 4 == 0 and 16-byte rows");
-        e = launch_conv_f32(ctx, kmap, kvol, (const float*)in, n_in, (int)cin, in_shift, (const float*)weight, bias,
-                            residual, res_dtype, res_shift, out, out_dtype, n_out, (int)cout, flags, pro_sub, pro_mul,
-                            pro_add, gn_partials, gn_groups);
+        if (cin % 4 || ca % 4 || ((uintptr_t)in & 15) || ((uintptr_t)in_b & 15))
+            return fail(error, error_capacity, S3D_INVALID_ARGUMENT,
+                        "F32_STRICT needs cin %% 4 == 0 (each source) and 16-byte rows");
+        e = launch_conv_f32(ctx, kmap, kvol, (const float*)in, (const float*)in_b, ca, n_in, (int)cin, in_shift,
+                            (const float*)weight, bias, residual, res_dtype, res_shift, out, out_dtype, n_out,
+                            (int)cout, flags, pro_sub, pro_mul, pro_add, gn_partials, gn_groups);
         if (e != cudaSuccess) return cuda_fail(error, error_capacity, e, "conv_f32_kernel");
         return S3D_OK;
     }
@@ -106,20 +111,21 @@ extern "C" S3DSP_API s3d_status s3dsp_conv(s3dsp_context* ctx, const s3dsp_kmap*
         if (flags & S3DSP_PRO_AFFINE_SILU)
             return fail(error, error_capacity, S3D_INVALID_ARGUMENT,
                         "BF16 conv takes pre-normalised input (use s3dsp_channel_affine)");
-        if (cin % 8 || ((uintptr_t)in & 15) || ((uintptr_t)weight & 15) || ((uintptr_t)out & 15) ||
-            ((uintptr_t)residual & 15))
+        if (cin % 8 || ca % 8 || ((uintptr_t)in & 15) || ((uintptr_t)in_b & 15) || ((uintptr_t)weight & 15) ||
+            ((uintptr_t)out & 15) || ((uintptr_t)residual & 15))
             return fail(error, error_capacity, S3D_INVALID_ARGUMENT,
-                        "BF16 needs cin %% 8 == 0 and 16-byte aligned in/weight/out/residual");
+                        "BF16 needs cin %% 8 == 0 (each source) and 16-byte aligned in/weight/out/residual");
         s3d_status st = S3D_OK;
         const Bf16Kernel kern = pick_bf16_kernel(ctx, n_out, kvol, flags);
         if (kern == Bf16Kernel::kTile128)
-            e = launch_conv_tc(ctx, kmap, kvol, (const __nv_bfloat16*)in, n_in, (int)cin, in_shift,
-                               (const __nv_bfloat16*)weight, bias, residual, res_dtype, res_shift, out, out_dtype,
-                               n_out, (int)cout, flags, gn_partials, gn_groups, error, error_capacity, &st);
+            e = launch_conv_tc(ctx, kmap, kvol, (const __nv_bfloat16*)in, (const __nv_bfloat16*)in_b, ca, n_in,
+                               (int)cin, in_shift, (const __nv_bfloat16*)weight, bias, residual, res_dtype, res_shift,
+                               out, out_dtype, n_out, (int)cout, flags, gn_partials, gn_groups, error,
+                               error_capacity, &st);
         else
-            e = launch_conv_sk(ctx, kmap, kvol, (const __nv_bfloat16*)in, n_in, (int)cin, in_shift,
-                               (const __nv_bfloat16*)weight, bias, residual, res_dtype, res_shift, out, out_dtype,
-                               n_out, (int)cout, flags, gn_partials, gn_groups,
+            e = launch_conv_sk(ctx, kmap, kvol, (const __nv_bfloat16*)in, (const __nv_bfloat16*)in_b, ca, n_in,
+                               (int)cin, in_shift, (const __nv_bfloat16*)weight, bias, residual, res_dtype, res_shift,
+                               out, out_dtype, n_out, (int)cout, flags, gn_partials, gn_groups,
                                kern == Bf16Kernel::kStreamK128 ? 128 : 256, error, error_capacity, &st);
         if (st != S3D_OK) return st;
         if (e != cudaSuccess) return cuda_fail(error, error_capacity, e, bf16_kernel_name(kern));
@@ -131,24 +137,64 @@ extern "C" S3DSP_API s3d_status s3dsp_conv(s3dsp_context* ctx, const s3dsp_kmap*
         if (flags & (S3DSP_PRO_AFFINE_SILU | S3DSP_CONV_CTA_PAIR))
             return fail(error, error_capacity, S3D_INVALID_ARGUMENT,
                         "3XTF32 conv takes pre-normalised input and runs without CTA pairs");
-        if (cin % 4 || ((uintptr_t)in & 15) || ((uintptr_t)weight & 15) || ((uintptr_t)out & 15) ||
-            ((uintptr_t)residual & 15))
+        if (cin % 4 || ca % 4 || ((uintptr_t)in & 15) || ((uintptr_t)in_b & 15) || ((uintptr_t)weight & 15) ||
+            ((uintptr_t)out & 15) || ((uintptr_t)residual & 15))
             return fail(error, error_capacity, S3D_INVALID_ARGUMENT,
-                        "3XTF32 needs cin %% 4 == 0 and 16-byte aligned in/weight/out/residual");
-        // the input split once into TF32 high parts and remainders (stream-ordered scratch)
-        const size_t nel = (size_t)n_in * (size_t)cin;
+                        "3XTF32 needs cin %% 4 == 0 (each source) and 16-byte aligned in/weight/out/residual");
+        // each source split once into TF32 high parts and remainders (stream-ordered scratch)
+        const size_t nel_a = (size_t)n_in * (size_t)ca;
+        const size_t nel_b = in_b ? (size_t)n_in * (size_t)(cin - ca) : 0;
+        const size_t nel = nel_a + nel_b;
         float* split = nullptr;
         S3DSP_CUDA(s3dsp::malloc_async(&split, 8 * (nel > 0 ? nel : 1), ctx->stream), "3xTF32 split buffer");
-        e = split_tf32(ctx, (const float*)in, (int64_t)nel, split, split + nel);
+        float* hi_a = split;
+        float* lo_a = split + nel_a;
+        float* hi_b = split + 2 * nel_a;
+        float* lo_b = hi_b + nel_b;
+        e = split_tf32(ctx, (const float*)in, (int64_t)nel_a, hi_a, lo_a);
+        if (e == cudaSuccess && in_b) e = split_tf32(ctx, (const float*)in_b, (int64_t)nel_b, hi_b, lo_b);
         s3d_status st = S3D_OK;
         if (e == cudaSuccess)
-            e = launch_conv_tf32x3(ctx, kmap, kvol, split, split + nel, (int)cin, in_shift, (const float*)weight, bias,
-                                   residual, res_dtype, res_shift, out, out_dtype, n_out, (int)cout, flags,
-                                   gn_partials, gn_groups, error, error_capacity, &st);
+            e = launch_conv_tf32x3(ctx, kmap, kvol, hi_a, lo_a, in_b ? hi_b : nullptr, in_b ? lo_b : nullptr, ca,
+                                   (int)cin, in_shift, (const float*)weight, bias, residual, res_dtype, res_shift, out,
+                                   out_dtype, n_out, (int)cout, flags, gn_partials, gn_groups, error, error_capacity,
+                                   &st);
         cudaFreeAsync(split, ctx->stream);
         if (st != S3D_OK) return st;
         if (e != cudaSuccess) return cuda_fail(error, error_capacity, e, "conv_tc_kernel<tf32x3>");
         return S3D_OK;
     }
     return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "unknown precision %u", precision);
+}
+
+}  // namespace
+
+extern "C" S3DSP_API s3d_status s3dsp_conv(s3dsp_context* ctx, const s3dsp_kmap* kmap, int32_t kvol,
+                                           uint32_t precision, const void* in, uint32_t in_dtype, int64_t n_in,
+                                           int64_t cin, int32_t in_shift, const void* weight, const float* bias,
+                                           const void* residual, uint32_t res_dtype, int32_t res_shift, void* out,
+                                           uint32_t out_dtype, int64_t n_out, int64_t cout, uint32_t flags,
+                                           const float* pro_sub, const float* pro_mul, const float* pro_add,
+                                           double* gn_partials, int32_t gn_groups, char* error,
+                                           uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    return conv_impl(ctx, kmap, kvol, precision, in, nullptr, cin, in_dtype, n_in, cin, in_shift, weight, bias,
+                     residual, res_dtype, res_shift, out, out_dtype, n_out, cout, flags, pro_sub, pro_mul, pro_add,
+                     gn_partials, gn_groups, error, error_capacity);
+}
+
+extern "C" S3DSP_API s3d_status s3dsp_conv_concat(s3dsp_context* ctx, const s3dsp_kmap* kmap, int32_t kvol,
+                                                  uint32_t precision, const void* in_a, int64_t cin_a,
+                                                  const void* in_b, int64_t cin_b, uint32_t in_dtype, int64_t n_in,
+                                                  int32_t in_shift, const void* weight, const float* bias,
+                                                  const void* residual, uint32_t res_dtype, int32_t res_shift,
+                                                  void* out, uint32_t out_dtype, int64_t n_out, int64_t cout,
+                                                  uint32_t flags, const float* pro_sub, const float* pro_mul,
+                                                  const float* pro_add, double* gn_partials, int32_t gn_groups,
+                                                  char* error, uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!in_b || cin_b <= 0) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "second source missing");
+    return conv_impl(ctx, kmap, kvol, precision, in_a, in_b, cin_a, in_dtype, n_in, cin_a + cin_b, in_shift, weight,
+                     bias, residual, res_dtype, res_shift, out, out_dtype, n_out, cout, flags, pro_sub, pro_mul,
+                     pro_add, gn_partials, gn_groups, error, error_capacity);
 }

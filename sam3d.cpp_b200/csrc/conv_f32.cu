@@ -25,6 +25,8 @@ constexpr int NT = 256;
 
 struct F32ConvParams {
     const float* in;
+    const float* in_b;         // second source (channels [cin_a, cin)) or null
+    int cin_a;
     int64_t n_in;
     int cin;
     int in_shift;
@@ -107,7 +109,10 @@ __global__ void __launch_bounds__(NT) conv_f32_kernel(const F32ConvParams p) {
         for (int i = 0; i < 2; ++i) {
             float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
             if (src[i] >= 0 && k0 < p.cin) {
-                v = *reinterpret_cast<const float4*>(p.in + (int64_t)src[i] * p.cin + k0);
+                const bool from_a = k0 < p.cin_a;
+                const float* g = from_a ? p.in + (int64_t)src[i] * p.cin_a + k0
+                                        : p.in_b + (int64_t)src[i] * (p.cin - p.cin_a) + (k0 - p.cin_a);
+                v = *reinterpret_cast<const float4*>(g);
                 if (p.flags & S3DSP_PRO_AFFINE_SILU) {
                     v.x = silu_f((v.x - p.pro_sub[k0 + 0]) * p.pro_mul[k0 + 0] + p.pro_add[k0 + 0]);
                     v.y = silu_f((v.y - p.pro_sub[k0 + 1]) * p.pro_mul[k0 + 1] + p.pro_add[k0 + 1]);
@@ -227,13 +232,15 @@ __global__ void __launch_bounds__(NT) conv_f32_kernel(const F32ConvParams p) {
 namespace s3dsp {
 
 cudaError_t launch_conv_f32(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol, const float* in,
-                            int64_t n_in, int cin, int in_shift, const float* w,
+                            const float* in_b, int cin_a, int64_t n_in, int cin, int in_shift, const float* w,
                             const float* bias, const void* residual, uint32_t res_dtype,
                             int res_shift, void* out, uint32_t out_dtype, int64_t n_out, int cout,
                             uint32_t flags, const float* pro_sub, const float* pro_mul,
                             const float* pro_add, double* gn_partials, int gn_groups) {
     F32ConvParams p;
     p.in = in;
+    p.in_b = in_b;
+    p.cin_a = in_b ? cin_a : cin;
     p.n_in = n_in;
     p.cin = cin;
     p.in_shift = in_shift;

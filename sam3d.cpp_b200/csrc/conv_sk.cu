@@ -55,6 +55,8 @@ constexpr int kSmemMax = kSmemOptIn;
 
 struct SkParams {
     const __nv_bfloat16* in;
+    const __nv_bfloat16* in_b;  // second source (channels [cin_a, cin)) or null
+    int cin_a;
     int cin;
     int in_shift;
     const int32_t* nbr;         // [kvol][n_out] or null (identity)
@@ -226,12 +228,18 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
                 }
                 const int k0 = kc * kKC + c16 * 8;
                 const uint32_t a_base = smem_u32(sA + (size_t)s * kAStage);
+                // channel concat of two sources: the source holding channel k0
+                // and its row stride, fixed for the whole stage
+                const bool kin = k0 < p.cin;
+                const bool from_a = k0 < p.cin_a;
+                const __nv_bfloat16* base = from_a ? p.in + k0 : p.in_b + (k0 - p.cin_a);
+                const int64_t ld = from_a ? p.cin_a : p.cin - p.cin_a;
 #pragma unroll
                 for (int i = 0; i < kMine; ++i) {
                     const int row = rg + kRowStep * i;
                     const int32_t src = cur[i];
-                    const bool valid = src >= 0 && k0 < p.cin;
-                    const void* g = valid ? (const void*)(p.in + (int64_t)src * p.cin + k0) : (const void*)p.in;
+                    const bool valid = kin && src >= 0;
+                    const void* g = valid ? (const void*)(base + (int64_t)src * ld) : (const void*)p.in;
                     cp_async_16(a_base + row * (2 * kKC) + ((c16 ^ kmajor_swz<kKC>(row)) << 4), g, valid ? 16u : 0u);
                 }
                 cp_async_arrive_noinc(smem_u32(full + s));
@@ -521,7 +529,7 @@ namespace s3dsp {
 int tc_pick_bn(int cout);
 
 cudaError_t launch_conv_sk(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol, const __nv_bfloat16* in,
-                           int64_t n_in, int cin, int in_shift, const __nv_bfloat16* w, const float* bias,
+                           const __nv_bfloat16* in_b, int cin_a, int64_t n_in, int cin, int in_shift, const __nv_bfloat16* w, const float* bias,
                            const void* residual, uint32_t res_dtype, int res_shift, void* out, uint32_t out_dtype,
                            int64_t n_out, int cout, uint32_t flags, double* gn_partials, int gn_groups, int rows,
                            char* error, uint64_t error_capacity, s3d_status* st) {
@@ -582,6 +590,8 @@ cudaError_t launch_conv_sk(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
 
     SkParams p;
     p.in = in;
+    p.in_b = in_b;
+    p.cin_a = in_b ? cin_a : cin;
     p.cin = cin;
     p.in_shift = in_shift;
     p.nbr = kmap ? kmap->nbr : nullptr;

@@ -65,11 +65,15 @@ constexpr int kThreads = 21 * 32;
 constexpr int kFullSplit = 1;
 
 struct TcParams {
-    const __nv_bfloat16* in;    // BF16 input [n_in, cin]
+    const __nv_bfloat16* in;    // BF16 input [n_in, cin_a]
+    const __nv_bfloat16* in_b;  // BF16 second source [n_in, cin - cin_a] (channels [cin_a, cin)) or null
     const float* in_hi;         // 3xTF32: input split into TF32 high parts ...
-    const float* in_lo;         // ... and the f32 remainders, [n_in, cin] each
+    const float* in_lo;         // ... and the f32 remainders, [n_in, cin_a] each
+    const float* in_hi_b;       // 3xTF32: the second source's parts, [n_in, cin - cin_a] each
+    const float* in_lo_b;
+    int cin_a;                  // channels read from the first source (== cin for one source)
     int lo_rows;                // 3xTF32: row of the low weight block in the weight tensor map
-    int tf_groups;              // 3xTF32: groups of four TMEM accumulators (1, or 2 alternating by stage)
+    int tf_groups;              // 3xTF32: groups of four TMEM accumulators (1, 2, 4 or 8, taken in turn by stage)
     int cin;
     int in_shift;
     const int32_t* nbr;         // [kvol][n_out] or null (identity)
@@ -323,19 +327,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             const int k0 = kc * KC + c16 * (16 / kEs);
             const uint32_t a_base = smem_u32(sA + (size_t)s * kAStage);
+            // channel concat of two sources: the source holding channel k0, its
+            // row stride and column, fixed for the whole stage
+            const bool kin = k0 < p.cin;
+            const bool from_a = k0 < p.cin_a;
+            const int64_t ld = from_a ? p.cin_a : p.cin - p.cin_a;
+            const int kk = from_a ? k0 : k0 - p.cin_a;
 #pragma unroll
             for (int i = 0; i < kMine; ++i) {
                 const int row = rg + kRowStep * i;
                 const int32_t src = cur[i];
-                const bool valid = src >= 0 && k0 < p.cin;
+                const bool valid = kin && src >= 0;
+                // an invalid copy reads nothing; it keeps the first source's base address
+                const int64_t off = valid ? (int64_t)src * ld + kk : 0;
                 const uint32_t d = a_base + row * kRowB + ((c16 ^ kmajor_swz<KCB>(row)) << 4);
                 if constexpr (kTF32) {
-                    const int64_t off = valid ? (int64_t)src * p.cin + k0 : 0;
-                    cp_async_16(d, p.in_hi + off, valid ? 16u : 0u);
-                    cp_async_16(d + kAHalf, p.in_lo + off, valid ? 16u : 0u);
+                    cp_async_16(d, (valid && !from_a ? p.in_hi_b : p.in_hi) + off, valid ? 16u : 0u);
+                    cp_async_16(d + kAHalf, (valid && !from_a ? p.in_lo_b : p.in_lo) + off, valid ? 16u : 0u);
                 } else {
-                    const void* g = valid ? (const void*)(p.in + (int64_t)src * p.cin + k0) : (const void*)p.in;
-                    cp_async_16(d, g, valid ? 16u : 0u);
+                    cp_async_16(d, (valid && !from_a ? p.in_b : p.in) + off, valid ? 16u : 0u);
                 }
             }
             cp_async_arrive_noinc(smem_u32(full + s * kFS + warp / (kProdWarps / kFS)));
@@ -429,7 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             // accumulator of K step k
                             const uint64_t ah = kmajor_desc<KCB>(a0 + 32 * k), al = kmajor_desc<KCB>(a0 + kAHalf + 32 * k);
                             const uint64_t bh = kmajor_desc<KCB>(b0 + 32 * k), bl = kmajor_desc<KCB>(b0 + bhalf + 32 * k);
-                            const int grp = tf_groups > 1 ? (it & 1) : 0;
+                            const int grp = it % tf_groups;
                             const uint32_t dk = tmem + (uint32_t)((grp * kTfStep + k) * p.bn);
                             mma_tf32(dk, al, bh, p.idesc, it >= tf_groups ? 1u : 0u);
                             mma_tf32(dk, ah, bl, p.idesc, 1u);
@@ -629,7 +639,7 @@ int tc_pick_bn(int cout) {
 // (in = high parts, in_lo = remainders, both f32; weights packed as a high
 // block followed by a low block).
 static cudaError_t launch_tc_impl(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol, const void* in, const float* in_lo,
-                           int cin, int in_shift, const void* w, const float* bias, const void* residual,
+                           const void* in_b, const float* in_lo_b, int cin_a, int cin, int in_shift, const void* w, const float* bias, const void* residual,
                            uint32_t res_dtype, int res_shift, void* out, uint32_t out_dtype, int64_t n_out, int cout,
                            uint32_t flags, double* gn_partials, int gn_groups, char* error, uint64_t error_capacity,
                            s3d_status* st) {
@@ -639,10 +649,14 @@ static cudaError_t launch_tc_impl(s3dsp_context* ctx, const s3dsp_kmap* kmap, in
     const int cin_pad = tf32 ? (cin + 31) / 32 * 32 : (cin + 63) / 64 * 64;
     int bn = tc_pick_bn(cout);
     // 3xTF32: two-part stages (at most 128 columns keeps three stages), and
-    // TMEM for 4 accumulators per group; long reductions take 64-column tiles
-    // so that 8 accumulators fit (the tensor core's f32 accumulation truncates)
+    // TMEM for 4 accumulators per group. The tensor core's f32 accumulation
+    // truncates once per MMA, so the error grows with the products each
+    // accumulator takes: longer reductions take narrower tiles and more
+    // groups (tile columns x 4 x groups = 512 TMEM columns), i.e. at most
+    // about 1,100-1,700 products per accumulator for the 1024- and 2048-wide
+    // SLat layers (27 x 1024 and 27 x 2048)
     const int64_t kred = (int64_t)cin * kvol;
-    const int tf_cap = kred > 4096 ? 64 : 128;
+    const int tf_cap = kred > 32768 ? 16 : kred > 16384 ? 32 : kred > 4096 ? 64 : 128;
     if (tf32 && bn > tf_cap) {
         bn = 16;
         for (int c = tf_cap; c >= 16; c -= 16)
@@ -688,10 +702,14 @@ static cudaError_t launch_tc_impl(s3dsp_context* ctx, const s3dsp_kmap* kmap, in
     }
     TcParams p;
     p.in = tf32 ? nullptr : static_cast<const __nv_bfloat16*>(in);
+    p.in_b = tf32 ? nullptr : static_cast<const __nv_bfloat16*>(in_b);
     p.in_hi = tf32 ? static_cast<const float*>(in) : nullptr;
     p.in_lo = in_lo;
+    p.in_hi_b = tf32 ? static_cast<const float*>(in_b) : nullptr;
+    p.in_lo_b = in_lo_b;
+    p.cin_a = in_b ? cin_a : cin;
     p.lo_rows = kvol * cout_pad;
-    p.tf_groups = tf32 && bn <= 64 ? 2 : 1;
+    p.tf_groups = tf32 ? (bn <= 16 ? 8 : bn <= 32 ? 4 : bn <= 64 ? 2 : 1) : 1;
     p.cin = cin;
     p.in_shift = in_shift;
     p.nbr = kmap ? kmap->nbr : nullptr;
@@ -756,23 +774,26 @@ static cudaError_t launch_tc_impl(s3dsp_context* ctx, const s3dsp_kmap* kmap, in
 }
 
 cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
-                           const __nv_bfloat16* in, int64_t n_in, int cin, int in_shift,
-                           const __nv_bfloat16* w, const float* bias, const void* residual,
+                           const __nv_bfloat16* in, const __nv_bfloat16* in_b, int cin_a, int64_t n_in, int cin,
+                           int in_shift, const __nv_bfloat16* w, const float* bias, const void* residual,
                            uint32_t res_dtype, int res_shift, void* out, uint32_t out_dtype,
                            int64_t n_out, int cout, uint32_t flags, double* gn_partials,
                            int gn_groups, char* error, uint64_t error_capacity, s3d_status* st) {
     (void)n_in;
-    return launch_tc_impl(ctx, kmap, kvol, in, nullptr, cin, in_shift, w, bias, residual, res_dtype, res_shift, out,
-                          out_dtype, n_out, cout, flags, gn_partials, gn_groups, error, error_capacity, st);
+    return launch_tc_impl(ctx, kmap, kvol, in, nullptr, in_b, nullptr, cin_a, cin, in_shift, w, bias, residual,
+                          res_dtype, res_shift, out, out_dtype, n_out, cout, flags, gn_partials, gn_groups, error,
+                          error_capacity, st);
 }
 
 cudaError_t launch_conv_tf32x3(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol, const float* in_hi,
-                               const float* in_lo, int cin, int in_shift, const float* w, const float* bias,
+                               const float* in_lo, const float* in_hi_b, const float* in_lo_b, int cin_a, int cin,
+                               int in_shift, const float* w, const float* bias,
                                const void* residual, uint32_t res_dtype, int res_shift, void* out, uint32_t out_dtype,
                                int64_t n_out, int cout, uint32_t flags, double* gn_partials, int gn_groups,
                                char* error, uint64_t error_capacity, s3d_status* st) {
-    return launch_tc_impl(ctx, kmap, kvol, in_hi, in_lo, cin, in_shift, w, bias, residual, res_dtype, res_shift, out,
-                          out_dtype, n_out, cout, flags, gn_partials, gn_groups, error, error_capacity, st);
+    return launch_tc_impl(ctx, kmap, kvol, in_hi, in_lo, in_hi_b, in_lo_b, cin_a, cin, in_shift, w, bias, residual,
+                          res_dtype, res_shift, out, out_dtype, n_out, cout, flags, gn_partials, gn_groups, error,
+                          error_capacity, st);
 }
 
 }  // namespace s3dsp

@@ -577,6 +577,58 @@ extern "C" S3DSP_API void s3dsp_kmap_free(s3dsp_context* ctx, s3dsp_kmap* k) {
 
 extern "C" S3DSP_API int64_t s3dsp_kmap_rows(const s3dsp_kmap* k) { return k ? k->n_out : 0; }
 
+namespace {
+// out[o][r] = rows[nbr[o][r]] (-1 stays -1); an entry of rows outside
+// [0, n_rows_in) becomes -1 and sets kErrRowRange
+__global__ void kmap_compose_kernel(const int32_t* __restrict__ nbr, int64_t total, const int32_t* __restrict__ rows,
+                                    int64_t n_rows, int64_t n_rows_in, int32_t* __restrict__ out,
+                                    uint32_t* __restrict__ status) {
+    pdl_wait();
+    pdl_trigger();
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int32_t v = nbr[i];
+        int32_t u = -1;
+        if (v >= 0 && v < n_rows) {
+            u = __ldg(rows + v);
+            if (u < 0 || u >= n_rows_in) {
+                atomicOr(status, kErrRowRange);
+                u = -1;
+            }
+        }
+        out[i] = u;
+    }
+}
+}  // namespace
+
+extern "C" S3DSP_API s3d_status s3dsp_kmap_compose(s3dsp_context* ctx, const s3dsp_kmap* k, const int32_t* d_rows,
+                                                   int64_t n_rows_in, s3dsp_kmap** out, char* error,
+                                                   uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx || !k || !d_rows || !out) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
+    *out = nullptr;
+    if (n_rows_in < 0 || n_rows_in > INT32_MAX) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "bad n_rows_in");
+    S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    cudaError_t e;
+    s3dsp_kmap* c = new_kmap(ctx, k->n_out, n_rows_in, k->kvol, false, &e);
+    if (!c) return cuda_fail(error, error_capacity, e, "kmap allocation");
+    const int64_t total = (int64_t)k->kvol * k->n_out;
+    if (total > 0) {
+        launch_pdl(kmap_compose_kernel, dim3(grid_for(total, 256, ctx->sm_count)), dim3(256), 0, ctx->stream, k->nbr,
+                   total, d_rows, k->n_in, n_rows_in, c->nbr, ctx->d_status);
+        e = cudaGetLastError();
+        // the composed map has a neighbour exactly where the original has one
+        if (e == cudaSuccess && k->n_tiles > 0)
+            e = cudaMemcpyAsync(c->tile_mask, k->tile_mask, sizeof(uint32_t) * (size_t)k->n_tiles,
+                                cudaMemcpyDeviceToDevice, ctx->stream);
+        if (e != cudaSuccess) {
+            s3dsp_kmap_free(ctx, c);
+            return cuda_fail(error, error_capacity, e, "kmap_compose_kernel");
+        }
+    }
+    *out = c;
+    return S3D_OK;
+}
+
 extern "C" S3DSP_API s3d_status s3dsp_kmap_export_dense(s3dsp_context* ctx, const s3dsp_kmap* k,
                                                         uint32_t sentinel_mode, int32_t* d_out,
                                                         char* error, uint64_t error_capacity) {

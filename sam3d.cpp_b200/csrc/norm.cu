@@ -116,12 +116,33 @@ __global__ void channel_affine_kernel(const void* __restrict__ x, uint32_t xd, i
     }
 }
 
-// vectorised variant: f32 in, bf16 out, c % 8 == 0
-// f32 -> affine (+SiLU) -> bf16, 8 channels per item, 4 items per thread per
+// vectorised variant: f32 or bf16 in, bf16 out, c % 8 == 0
+// x -> affine (+SiLU) -> bf16, 8 channels per item, 4 items per thread per
 // iteration with all loads issued before any use (bytes in flight per SM is
 // what bounds a streaming kernel). (x - sub) * mul + add is evaluated as
 // written, with the per-channel vectors read as float4.
-__global__ void channel_affine_f32_bf16_kernel(const float4* __restrict__ x, int64_t total8, uint32_t c8,
+template <typename InT>
+__device__ __forceinline__ void load8(const void* x, int64_t i, float (&v)[8]);
+template <>
+__device__ __forceinline__ void load8<float>(const void* x, int64_t i, float (&v)[8]) {
+    const float4 a = __ldcs(reinterpret_cast<const float4*>(x) + 2 * i);
+    const float4 b = __ldcs(reinterpret_cast<const float4*>(x) + 2 * i + 1);
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+}
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const void* x, int64_t i, float (&v)[8]) {
+    const uint4 u = __ldcs(reinterpret_cast<const uint4*>(x) + i);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[q]));
+        v[2 * q] = f.x;
+        v[2 * q + 1] = f.y;
+    }
+}
+
+template <typename InT>
+__global__ void channel_affine_bf16_out_kernel(const void* __restrict__ x, int64_t total8, uint32_t c8,
                                                const float4* __restrict__ sub, const float4* __restrict__ mul,
                                                const float4* __restrict__ add, int silu, uint4* __restrict__ y) {
     pdl_wait();
@@ -130,14 +151,11 @@ __global__ void channel_affine_f32_bf16_kernel(const float4* __restrict__ x, int
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const bool narrow = total8 <= 0xffffffffll;
     for (int64_t i0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < total8; i0 += stride * U) {
-        float4 a[U], b[U];
+        float a[U][8];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int64_t i = i0 + u * stride;
-            if (i < total8) {
-                a[u] = __ldcs(x + 2 * i);
-                b[u] = __ldcs(x + 2 * i + 1);
-            }
+            if (i < total8) load8<InT>(x, i, a[u]);
         }
 #pragma unroll
         for (int u = 0; u < U; ++u) {
@@ -148,9 +166,10 @@ __global__ void channel_affine_f32_bf16_kernel(const float4* __restrict__ x, int
             const float4 s0 = __ldg(sub + 2 * q8), s1 = __ldg(sub + 2 * q8 + 1);
             const float4 m0 = __ldg(mul + 2 * q8), m1 = __ldg(mul + 2 * q8 + 1);
             const float4 d0 = __ldg(add + 2 * q8), d1 = __ldg(add + 2 * q8 + 1);
-            float v[8] = {(a[u].x - s0.x) * m0.x + d0.x, (a[u].y - s0.y) * m0.y + d0.y, (a[u].z - s0.z) * m0.z + d0.z,
-                          (a[u].w - s0.w) * m0.w + d0.w, (b[u].x - s1.x) * m1.x + d1.x, (b[u].y - s1.y) * m1.y + d1.y,
-                          (b[u].z - s1.z) * m1.z + d1.z, (b[u].w - s1.w) * m1.w + d1.w};
+            float v[8] = {(a[u][0] - s0.x) * m0.x + d0.x, (a[u][1] - s0.y) * m0.y + d0.y,
+                          (a[u][2] - s0.z) * m0.z + d0.z, (a[u][3] - s0.w) * m0.w + d0.w,
+                          (a[u][4] - s1.x) * m1.x + d1.x, (a[u][5] - s1.y) * m1.y + d1.y,
+                          (a[u][6] - s1.z) * m1.z + d1.z, (a[u][7] - s1.w) * m1.w + d1.w};
             if (silu) {
 #pragma unroll
                 for (int q = 0; q < 8; ++q) v[q] = silu_fast(v[q]);
@@ -168,29 +187,35 @@ __global__ void channel_affine_f32_bf16_kernel(const float4* __restrict__ x, int
 
 // one warp per row; two passes over the row (mean, then centred variance),
 // both in double like ggml_norm's ggml_float sums
-__global__ void layer_norm_kernel(const void* __restrict__ x, uint32_t xd, int64_t n, int c, float eps,
-                                  const float* __restrict__ gamma, const float* __restrict__ beta,
-                                  const float* __restrict__ ms, const float* __restrict__ msh, int silu,
-                                  void* __restrict__ y, uint32_t yd) {
+// x: one source [n, c], or the channel concat of xa [n, ca] and xb [n, c - ca]
+// (xb non-null); y [n, c]
+__global__ void layer_norm_kernel(const void* __restrict__ x, const void* __restrict__ xb, int ca, uint32_t xd,
+                                  int64_t n, int c, float eps, const float* __restrict__ gamma,
+                                  const float* __restrict__ beta, const float* __restrict__ ms,
+                                  const float* __restrict__ msh, int silu, void* __restrict__ y, uint32_t yd) {
     pdl_wait();
     pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int64_t row = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= n) return;
-    const int64_t base = row * c;
+    const int cb = c - ca;
+    auto ld = [&](int k) {
+        return k < ca ? ld_f(x, xd, row * ca + k) : ld_f(xb, xd, row * cb + (k - ca));
+    };
     double s = 0.0;
-    for (int k = lane; k < c; k += 32) s += ld_f(x, xd, base + k);
+    for (int k = lane; k < c; k += 32) s += ld(k);
     for (int d = 16; d > 0; d >>= 1) s += __shfl_xor_sync(0xffffffffu, s, d);
     const float mean = (float)(s / c);
     double s2 = 0.0;
     for (int k = lane; k < c; k += 32) {
-        const float v = ld_f(x, xd, base + k) - mean;
+        const float v = ld(k) - mean;
         s2 += (double)v * v;
     }
     for (int d = 16; d > 0; d >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, d);
     const float rstd = 1.0f / sqrtf((float)(s2 / c) + eps);
+    const int64_t base = row * c;
     for (int k = lane; k < c; k += 32) {
-        float v = (ld_f(x, xd, base + k) - mean) * rstd;
+        float v = (ld(k) - mean) * rstd;
         if (gamma) v *= gamma[k];
         if (beta) v += beta[k];
         if (ms) v = v * ms[k] + v;
@@ -362,13 +387,14 @@ extern "C" S3DSP_API s3d_status s3dsp_channel_affine(s3dsp_context* ctx, const v
     S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
     const bool vec_ok = !((uintptr_t)x & 15) && !((uintptr_t)y & 15) && !((uintptr_t)sub & 15) &&
                         !((uintptr_t)mul & 15) && !((uintptr_t)add & 15);
-    if (xd == S3DSP_F32 && yd == S3DSP_BF16 && c % 8 == 0 && vec_ok) {
+    if ((xd == S3DSP_F32 || xd == S3DSP_BF16) && yd == S3DSP_BF16 && c % 8 == 0 && vec_ok) {
         const int64_t total8 = n * c / 8;
-        S3DSP_CUDA(launch_pdl(channel_affine_f32_bf16_kernel, dim3(grid_for((total8 + 3) / 4, 256, ctx->sm_count)),
-                              dim3(256), 0, ctx->stream, reinterpret_cast<const float4*>(x), total8, (uint32_t)(c / 8),
+        const dim3 grid(grid_for((total8 + 3) / 4, 256, ctx->sm_count));
+        auto kern = xd == S3DSP_F32 ? channel_affine_bf16_out_kernel<float> : channel_affine_bf16_out_kernel<__nv_bfloat16>;
+        S3DSP_CUDA(launch_pdl(kern, grid, dim3(256), 0, ctx->stream, x, total8, (uint32_t)(c / 8),
                               reinterpret_cast<const float4*>(sub), reinterpret_cast<const float4*>(mul),
                               reinterpret_cast<const float4*>(add), (int)silu, reinterpret_cast<uint4*>(y)),
-                   "channel_affine_f32_bf16_kernel");
+                   "channel_affine_bf16_out_kernel");
     } else {
         launch_pdl(channel_affine_kernel, dim3(grid_for(n * c, 256, ctx->sm_count)), dim3(256), 0, ctx->stream, x, xd,
                    n, (int)c, sub, mul, add, silu, y, yd);
@@ -388,8 +414,26 @@ extern "C" S3DSP_API s3d_status s3dsp_layer_norm(s3dsp_context* ctx, const void*
     if (n == 0) return S3D_OK;
     S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
     const int64_t blocks = (n + 7) / 8;
-    launch_pdl(layer_norm_kernel, dim3((unsigned)blocks), dim3(256), 0, ctx->stream, x, xd, n, (int)c, eps, gamma,
-               beta, ms, msh, silu, y, yd);
+    launch_pdl(layer_norm_kernel, dim3((unsigned)blocks), dim3(256), 0, ctx->stream, x, (const void*)nullptr, (int)c,
+               xd, n, (int)c, eps, gamma, beta, ms, msh, silu, y, yd);
+    S3DSP_LAUNCH_CHECK("layer_norm_kernel");
+    return S3D_OK;
+}
+
+extern "C" S3DSP_API s3d_status s3dsp_layer_norm_concat(s3dsp_context* ctx, const void* xa, int64_t ca,
+                                                        const void* xb, int64_t cb, uint32_t xd, int64_t n, float eps,
+                                                        const float* gamma, const float* beta, const float* ms,
+                                                        const float* msh, int32_t silu, void* y, uint32_t yd,
+                                                        char* error, uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx || !xa || !xb || !y) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "NULL argument");
+    if (!dtype_ok(xd) || !dtype_ok(yd) || n < 0 || ca <= 0 || cb <= 0 || ca + cb > (1 << 20))
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "bad shape/dtype");
+    if (n == 0) return S3D_OK;
+    S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    const int64_t blocks = (n + 7) / 8;
+    launch_pdl(layer_norm_kernel, dim3((unsigned)blocks), dim3(256), 0, ctx->stream, xa, xb, (int)ca, xd, n,
+               (int)(ca + cb), eps, gamma, beta, ms, msh, silu, y, yd);
     S3DSP_LAUNCH_CHECK("layer_norm_kernel");
     return S3D_OK;
 }

@@ -24,6 +24,7 @@ enum : uint32_t {
     kErrHashFull = 1u << 1,     // probe bound exceeded (never with load <= 1/2)
     kErrDuplicate = 1u << 2,    // duplicate coordinate where duplicates are rejected
     kErrPipelineTimeout = 1u << 3,  // a bounded device wait gave up
+    kErrRowRange = 1u << 4,     // a caller-supplied row index outside its table (read as "no row")
 };
 
 struct s3dsp_context {
@@ -31,7 +32,8 @@ struct s3dsp_context {
     cudaStream_t stream = nullptr;
     bool owns_stream = false;
     uint32_t flags = 0;
-    int sm_count = 0;
+    int sm_count = 0;      // SMs the context's grids are sized for (s3dsp_context_set_sm_limit)
+    int sm_device = 0;     // SMs of the device
     uint32_t* d_status = nullptr;  // [4] error bits, duplicate count, ...
 };
 
@@ -160,22 +162,30 @@ inline bool dtype_ok(uint32_t dt) { return dt == S3DSP_F32 || dt == S3DSP_BF16 |
 s3d_status check_status(s3dsp_context* ctx, char* error, uint64_t error_capacity);
 
 // launch helpers implemented in the .cu files
+//
+// Every conv gathers its input rows from one or two sources: channels
+// [0, cin_a) of a row come from `in` (row stride cin_a), channels [cin_a, cin)
+// from `in_b` (row stride cin - cin_a), the same row index in both -- the
+// channel concat of two tensors (ggml_concat(a, b, 0)) without building it.
+// One source: in_b == nullptr, cin_a == cin.
 cudaError_t launch_conv_f32(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol, const float* in,
-                            int64_t n_in, int cin, int in_shift, const float* w,
+                            const float* in_b, int cin_a, int64_t n_in, int cin, int in_shift, const float* w,
                             const float* bias, const void* residual, uint32_t res_dtype,
                             int res_shift, void* out, uint32_t out_dtype, int64_t n_out, int cout,
                             uint32_t flags, const float* pro_sub, const float* pro_mul,
                             const float* pro_add, double* gn_partials, int gn_groups);
 cudaError_t launch_conv_tc(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
-                           const __nv_bfloat16* in, int64_t n_in, int cin, int in_shift,
-                           const __nv_bfloat16* w, const float* bias, const void* residual,
+                           const __nv_bfloat16* in, const __nv_bfloat16* in_b, int cin_a, int64_t n_in, int cin,
+                           int in_shift, const __nv_bfloat16* w, const float* bias, const void* residual,
                            uint32_t res_dtype, int res_shift, void* out, uint32_t out_dtype,
                            int64_t n_out, int cout, uint32_t flags, double* gn_partials,
                            int gn_groups, char* error, uint64_t error_capacity, s3d_status* st);
-// 3xTF32 on the 128-row tensor-core kernel: in_hi / in_lo are the input split
-// by s3dsp::split_tf32, w a weight packed for S3DSP_PREC_F32_3XTF32
+// 3xTF32 on the 128-row tensor-core kernel: in_hi / in_lo (and in_hi_b /
+// in_lo_b for a second source) are the input split by s3dsp::split_tf32, w a
+// weight packed for S3DSP_PREC_F32_3XTF32
 cudaError_t launch_conv_tf32x3(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol, const float* in_hi,
-                               const float* in_lo, int cin, int in_shift, const float* w, const float* bias,
+                               const float* in_lo, const float* in_hi_b, const float* in_lo_b, int cin_a, int cin,
+                               int in_shift, const float* w, const float* bias,
                                const void* residual, uint32_t res_dtype, int res_shift, void* out, uint32_t out_dtype,
                                int64_t n_out, int cout, uint32_t flags, double* gn_partials, int gn_groups,
                                char* error, uint64_t error_capacity, s3d_status* st);
@@ -183,8 +193,8 @@ cudaError_t launch_conv_tf32x3(s3dsp_context* ctx, const s3dsp_kmap* kmap, int k
 cudaError_t split_tf32(s3dsp_context* ctx, const float* x, int64_t n, float* hi, float* lo);
 // rows: 128 or 256 output rows per stream-K work tile
 cudaError_t launch_conv_sk(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
-                           const __nv_bfloat16* in, int64_t n_in, int cin, int in_shift,
-                           const __nv_bfloat16* w, const float* bias, const void* residual,
+                           const __nv_bfloat16* in, const __nv_bfloat16* in_b, int cin_a, int64_t n_in, int cin,
+                           int in_shift, const __nv_bfloat16* w, const float* bias, const void* residual,
                            uint32_t res_dtype, int res_shift, void* out, uint32_t out_dtype,
                            int64_t n_out, int cout, uint32_t flags, double* gn_partials,
                            int gn_groups, int rows, char* error, uint64_t error_capacity, s3d_status* st);

@@ -30,8 +30,9 @@ CONTEXT_OWN_STREAM = 2
 
 # every symbol include/s3dsp.h declares (tests check the library exports them)
 EXPORTED = [
-    "s3dsp_abi_version", "s3dsp_context_create", "s3dsp_context_free", "s3dsp_context_stream",
-    "s3dsp_context_check", "s3dsp_memory_stats", "s3dsp_hash_build", "s3dsp_hash_free", "s3dsp_hash_size",
+    "s3dsp_abi_version", "s3dsp_context_create", "s3dsp_context_free", "s3dsp_context_stream", "s3dsp_context_set_sm_limit",
+    "s3dsp_context_check", "s3dsp_memory_stats", "s3dsp_device_alloc", "s3dsp_device_free", "s3dsp_copy_to_device",
+    "s3dsp_copy_to_host", "s3dsp_hash_build", "s3dsp_hash_free", "s3dsp_hash_size",
     "s3dsp_hash_lookup", "s3dsp_gs_window_tables", "s3dsp_ape", "s3dsp_flexicubes_tables_create",
     "s3dsp_flexicubes_tables_free", "s3dsp_flexicubes_extract", "s3dsp_mesh_info", "s3dsp_mesh_device", "s3dsp_mesh_copy",
     "s3dsp_mesh_free", "s3dsp_gguf_open", "s3dsp_gguf_close", "s3dsp_gguf_n_tensors", "s3dsp_gguf_find",
@@ -42,7 +43,8 @@ EXPORTED = [
     "s3dsp_nccl_comm_create", "s3dsp_nccl_comm_free", "s3dsp_halo_exchange", "s3dsp_occupancy_coords", "s3dsp_prune_surface", "s3dsp_downsample_coords",
     "s3dsp_kmap_build_subm3", "s3dsp_kmap_build_subm3_rows", "s3dsp_kmap_build_subm3_range", "s3dsp_subdivide", "s3dsp_kmap_free",
     "s3dsp_kmap_rows", "s3dsp_kmap_export_dense", "s3dsp_kmap_pairs", "s3dsp_kmap_pairs_noalloc",
-    "s3dsp_weights_packed_bytes", "s3dsp_weights_pack", "s3dsp_gn_partials_count", "s3dsp_conv", "s3dsp_conv_kernel",
+    "s3dsp_weights_packed_bytes", "s3dsp_weights_pack", "s3dsp_gn_partials_count", "s3dsp_conv", "s3dsp_conv_concat",
+    "s3dsp_conv_kernel", "s3dsp_layer_norm_concat", "s3dsp_kmap_compose", "s3dsp_slat_res_block_concat",
     "s3dsp_gn_stats", "s3dsp_gn_finalize", "s3dsp_channel_affine", "s3dsp_layer_norm",
     "s3dsp_convert", "s3dsp_slat_tables_build", "s3dsp_slat_tables_free", "s3dsp_slat_tables_coarse_rows",
     "s3dsp_slat_tables_coarse_kmap", "s3dsp_slat_tables_export", "s3dsp_slat_downsample", "s3dsp_slat_upsample",
@@ -81,7 +83,12 @@ def load(path: str = LIB_PATH):
         "s3dsp_context_create": (_u32, [_i32, _vp, _u32, ctypes.POINTER(_vp), _cp, _u64]),
         "s3dsp_context_free": (None, [_vp]),
         "s3dsp_context_stream": (_vp, [_vp]),
+        "s3dsp_context_set_sm_limit": (_u32, [_vp, _i32, _cp, _u64]),
         "s3dsp_context_check": (_u32, [_vp, _cp, _u64]),
+        "s3dsp_device_alloc": (_u32, [_vp, _u64, ctypes.POINTER(_vp), _cp, _u64]),
+        "s3dsp_device_free": (None, [_vp, _vp]),
+        "s3dsp_copy_to_device": (_u32, [_vp, _vp, _vp, _u64, _cp, _u64]),
+        "s3dsp_copy_to_host": (_u32, [_vp, _vp, _vp, _u64, _cp, _u64]),
         "s3dsp_memory_stats": (_u32, [_i32, ctypes.POINTER(_u64), ctypes.POINTER(_u64), ctypes.POINTER(_u64), _i32,
                                       _cp, _u64]),
         "s3dsp_hash_build": (_u32, [_vp, _vp, _i64, _i32, ctypes.POINTER(_vp), _cp, _u64]),
@@ -147,6 +154,13 @@ def load(path: str = LIB_PATH):
         "s3dsp_conv_kernel": (_cp, [_vp, _i64, _i32, _i64, _i64, _u32, _u32]),
         "s3dsp_conv": (_u32, [_vp, _vp, _i32, _u32, _vp, _u32, _i64, _i64, _i32, _vp, _vp, _vp, _u32, _i32,
                               _vp, _u32, _i64, _i64, _u32, _vp, _vp, _vp, _vp, _i32, _cp, _u64]),
+        "s3dsp_conv_concat": (_u32, [_vp, _vp, _i32, _u32, _vp, _i64, _vp, _i64, _u32, _i64, _i32, _vp, _vp, _vp,
+                                     _u32, _i32, _vp, _u32, _i64, _i64, _u32, _vp, _vp, _vp, _vp, _i32, _cp, _u64]),
+        "s3dsp_layer_norm_concat": (_u32, [_vp, _vp, _i64, _vp, _i64, _u32, _i64, _f, _vp, _vp, _vp, _vp, _i32, _vp,
+                                           _u32, _cp, _u64]),
+        "s3dsp_kmap_compose": (_u32, [_vp, _vp, _vp, _i64, ctypes.POINTER(_vp), _cp, _u64]),
+        "s3dsp_slat_res_block_concat": (_u32, [_vp, _vp, _vp, _u32, _vp, _i64, _vp, _i64, _i64, _i64] + [_vp] * 11
+                                        + [_cp, _u64]),
         "s3dsp_gn_stats": (_u32, [_vp, _vp, _u32, _i64, _i64, _i32, _vp, _cp, _u64]),
         "s3dsp_gn_finalize": (_u32, [_vp, _vp, _i64, _i64, _i32, _f, _vp, _vp, _vp, _vp, _vp, _cp, _u64]),
         "s3dsp_channel_affine": (_u32, [_vp, _vp, _u32, _i64, _i64, _vp, _vp, _vp, _i32, _vp, _u32, _cp, _u64]),
@@ -521,6 +535,10 @@ class Context:
     def check(self):
         _call(load().s3dsp_context_check, self.handle)
 
+    def set_sm_limit(self, sms: int):
+        """Size this context's SM-proportional grids for `sms` SMs (0: all)."""
+        _call(load().s3dsp_context_set_sm_limit, self.handle, sms)
+
     # ---- coordinate hash / kernel maps --------------------------------------------------------
     def hash_build(self, coords, reject_duplicates: bool = False) -> Hash:
         h = _vp()
@@ -663,6 +681,24 @@ class Context:
               dtype_code(residual) if residual is not None else 0, res_shift, ptr(out), dtype_code(out), n_out,
               cout, flags, ptr(sub), ptr(mul), ptr(add), ptr(gn_partials), gn_groups)
 
+    def conv_concat(self, kmap: Kmap | None, kvol: int, precision: int, xa, xb, weight, bias, out, cout: int,
+                    in_shift: int = 0, residual=None, res_shift: int = 0, flags: int = 0, pro=None,
+                    gn_partials=None, gn_groups: int = 0, n_out: int | None = None):
+        """conv over the channel concat of xa [n_in, ca] and xb [n_in, cb] (never built)."""
+        assert xa.dtype == xb.dtype and xa.shape[0] == xb.shape[0]
+        n_out = out.shape[0] if n_out is None else n_out
+        sub, mul, add = pro if pro is not None else (None, None, None)
+        _call(load().s3dsp_conv_concat, self.handle, kmap.handle if kmap else None, kvol, precision, ptr(xa),
+              xa.shape[1], ptr(xb), xb.shape[1], dtype_code(xa), xa.shape[0], in_shift, ptr(weight), ptr(bias),
+              ptr(residual), dtype_code(residual) if residual is not None else 0, res_shift, ptr(out),
+              dtype_code(out), n_out, cout, flags, ptr(sub), ptr(mul), ptr(add), ptr(gn_partials), gn_groups)
+
+    def kmap_compose(self, kmap: Kmap, rows, n_rows_in: int) -> Kmap:
+        """Map whose entries are rows[kmap entry] (rows: device int32 [kmap input rows])."""
+        k = _vp()
+        _call(load().s3dsp_kmap_compose, self.handle, kmap.handle, ptr(rows), n_rows_in, ctypes.byref(k))
+        return Kmap(self, k.value, kmap.rows)
+
     # ---- norms -----------------------------------------------------------
     @staticmethod
     def gn_partials_count(n_rows: int, channels: int, groups: int) -> int:
@@ -684,6 +720,14 @@ class Context:
                    silu: bool = False):
         _call(load().s3dsp_layer_norm, self.handle, ptr(x), dtype_code(x), x.shape[0], x.shape[1], eps, ptr(gamma),
               ptr(beta), ptr(mod_scale), ptr(mod_shift), int(silu), ptr(y), dtype_code(y))
+
+    def layer_norm_concat(self, xa, xb, eps: float, y, gamma=None, beta=None, mod_scale=None, mod_shift=None,
+                          silu: bool = False):
+        """LayerNorm over the channel concat of xa [n, ca] and xb [n, cb] into y [n, ca + cb]."""
+        assert xa.dtype == xb.dtype and xa.shape[0] == xb.shape[0]
+        _call(load().s3dsp_layer_norm_concat, self.handle, ptr(xa), xa.shape[1], ptr(xb), xb.shape[1], dtype_code(xa),
+              xa.shape[0], eps, ptr(gamma), ptr(beta), ptr(mod_scale), ptr(mod_shift), int(silu), ptr(y),
+              dtype_code(y))
 
     def convert(self, x, y):
         _call(load().s3dsp_convert, self.handle, ptr(x), dtype_code(x), ptr(y), dtype_code(y), x.numel())
@@ -728,6 +772,15 @@ class Context:
               parent_coords_h.shape[0], ptr(x_h), x_h.shape[1], cout, ptr(gn1_w), ptr(gn1_b), ptr(conv1_w),
               ptr(conv1_b), ptr(gn2_w), ptr(gn2_b), ptr(conv2_w), ptr(conv2_b), ptr(skip_w), ptr(skip_b),
               ptr(child_coords_h), ptr(out_h))
+
+    def slat_res_block_concat(self, kmap: Kmap, precision: int, xa, xb, cout, norm1_w, norm1_b, conv1_w, conv1_b,
+                              mod_scale, mod_shift, conv2_w, conv2_b, skip_w, skip_b, out, up_rows=None):
+        """s3dsp_slat_res_block_concat: xb None for one source; up_rows (device
+        int32 [kmap rows]) for a block on the nearest upsample of coarse xa/xb."""
+        _call(load().s3dsp_slat_res_block_concat, self.handle, kmap.handle, ptr(up_rows), precision, ptr(xa),
+              xa.shape[1], ptr(xb), 0 if xb is None else xb.shape[1], xa.shape[0], cout, ptr(norm1_w), ptr(norm1_b),
+              ptr(conv1_w), ptr(conv1_b), ptr(mod_scale), ptr(mod_shift), ptr(conv2_w), ptr(conv2_b), ptr(skip_w),
+              ptr(skip_b), ptr(out))
 
     def slat_res_block(self, kmap: Kmap, precision: int, x, cout, norm1_w, norm1_b, conv1_w, conv1_b, mod_scale,
                        mod_shift, conv2_w, conv2_b, skip_w, skip_b, out):

@@ -49,6 +49,44 @@ def ellipsoid_shell(res: int = 64, seed: int = 0, thickness: float = 1.5,
     return np.ascontiguousarray(coords)
 
 
+def ellipsoid_shell_device(res: int = 64, seed: int = 0, thickness: float = 1.5,
+                           axes_range=(16.0, 30.0), centre_jitter: float = 4.0, batch: int = 0,
+                           device="cuda") -> np.ndarray:
+    """`ellipsoid_shell` evaluated with torch on `device` (for large grids: the
+    512^3 volume takes seconds in numpy). Identical output: the same seeded
+    draws on the host, then the same IEEE float64 operations in the same
+    order (products, sums left to right, correctly rounded divide and square
+    root; no fused multiply-add), and the kept voxels in lexicographic order.
+    Returns int32 [N, 4] on the host."""
+    import torch
+
+    rng = np.random.default_rng(seed)
+    scale = res / 64.0
+    a = rng.uniform(axes_range[0], axes_range[1], size=3) * scale
+    c = res / 2.0 + rng.uniform(-centre_jitter, centre_jitter, size=3) * scale
+    ax = torch.arange(res, dtype=torch.float64, device=device) + 0.5
+    dy = (ax - float(c[1])).view(1, -1, 1)
+    dz = (ax - float(c[2])).view(1, 1, -1)
+    qy, qz = dy / float(a[1]), dz / float(a[2])
+    out = []
+    chunk = max(1, (1 << 24) // (res * res))  # x-slabs per pass, ~16M voxels
+    for i0 in range(0, res, chunk):
+        dx = (ax[i0:i0 + chunk] - float(c[0])).view(-1, 1, 1)
+        qx = dx / float(a[0])
+        r = torch.sqrt(dx * dx + dy * dy + dz * dz)
+        q = torch.sqrt(qx * qx + qy * qy + qz * qz)
+        dist = torch.abs(r * (1.0 - 1.0 / q))
+        dist = torch.where(q == 0, torch.full_like(dist, float("inf")), dist)
+        idx = torch.nonzero(dist <= thickness)
+        idx[:, 0] += i0
+        out.append(idx)
+    ijk = torch.cat(out).to(torch.int32).cpu().numpy()
+    coords = np.empty((len(ijk), 4), np.int32)
+    coords[:, 0] = batch
+    coords[:, 1:] = ijk
+    return np.ascontiguousarray(coords)
+
+
 def normal(shape, seed: int, std: float = 1.0) -> np.ndarray:
     """float32 N(0, std^2) with a numpy default_rng seed."""
     rng = np.random.default_rng(seed)
