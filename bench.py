@@ -757,6 +757,8 @@ def sub_volume(args, rank, world, local_rank, stream, flush, steps=None, warmup=
     xstream.synchronize()
     if world > 1:
         torch.distributed.barrier()
+    sampler = ClockSampler(local_rank)
+    sampler.start()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     per_layer = []
@@ -766,6 +768,7 @@ def sub_volume(args, rank, world, local_rank, stream, flush, steps=None, warmup=
         ends[i].record(stream)
     stream.synchronize()
     xstream.synchronize()
+    clocks = sampler.stop()
     dev_ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends))
     halo_ms = float(np.mean([e[3].elapsed_time(e[4]) for e in per_layer])) if comm is not None else 0.0
     int_ms = float(np.mean([e[0].elapsed_time(e[1]) for e in per_layer]))
@@ -826,6 +829,7 @@ def sub_volume(args, rank, world, local_rank, stream, flush, steps=None, warmup=
                    "rows_checked": int(rows_checked), "mismatched_rows": int(mismatched),
                    "ghost_rows_exact": ghost_bad == 0, "bit_exact": mismatched == 0 and ghost_bad == 0},
         "setup_s_rank0": setup_s,
+        "clocks_rank0": clocks,
         "gpu_launches": VOLUME_LAYERS * steps * ((k_int is not None) + (k_bnd is not None) +
                                                  (2 if comm is not None else 0)),
     }
@@ -887,6 +891,8 @@ def sub_objects(args, rank, world, local_rank, stream, flush, steps=None, warmup
     stream.synchronize()
     if world > 1:
         torch.distributed.barrier()
+    sampler = ClockSampler(local_rank)
+    sampler.start()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     for i in range(steps):
@@ -894,10 +900,11 @@ def sub_objects(args, rank, world, local_rank, stream, flush, steps=None, warmup
         step()
         ends[i].record(stream)
     stream.synchronize()
+    clocks = sampler.stop()
     dev_ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends))
     ctx.check()
     per_rank = gather_rows(torch, world, [dev_ms / steps, float(len(mine)), float(sum(sizes[i] for i in mine)),
-                                          float(units_rank)])
+                                          float(units_rank), float(clocks.get("sm_mhz") or 0.0)])
     vals = torch.tensor([dev_ms], dtype=torch.float64, device=device)
     units = torch.tensor([float(units_rank) * steps], dtype=torch.float64, device=device)
     if world > 1:
@@ -916,7 +923,8 @@ def sub_objects(args, rank, world, local_rank, stream, flush, steps=None, warmup
                    "objects": OBJECTS, "voxels_total": int(sum(sizes)),
                    "parallelism": f"objects-dp{world} (largest-first assignment)",
                    "per_rank": [{"rank": r, "objects": int(v[1]), "voxels": int(v[2]), "units": int(v[3]),
-                                 "ms_per_step": v[0]} for r, v in enumerate(per_rank)]},
+                                 "ms_per_step": v[0], "sm_mhz_median": v[4]} for r, v in enumerate(per_rank)]},
+        "clocks_rank0": clocks,
     }
 
 

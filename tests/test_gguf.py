@@ -10,7 +10,9 @@ import gguf
 import s3dsp
 from gguf_fixtures import QTYPES, stored, write
 
-REF_SAMT = "/root/reference/tests/objects_runtime/fixtures/ss_occ_f32.samt"
+# the reference tree (read only when present; the same variable __graft_entry__.build() reads)
+REFERENCE_ROOT = os.environ.get("S3D_REFERENCE_ROOT", "/root/reference")
+REF_SAMT = os.path.join(REFERENCE_ROOT, "tests", "objects_runtime", "fixtures", "ss_occ_f32.samt")
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 
 
