@@ -109,8 +109,10 @@ __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 512;" ::: 
 
 
 
-// kRows = 256: two 128-row accumulators per work tile; 128: one.
-template <int kRows>
+// kRows = 256: two 128-row accumulators per work tile; 128: one. kTwo: the
+// input is the channel concat of two sources (a separate instance, so the
+// one-source gather keeps its shorter address path).
+template <int kRows, bool kTwo = false>
 __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, const __grid_constant__ CUtensorMap wmap) {
     pdl_wait();
     pdl_trigger();
@@ -230,15 +232,14 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
                 const uint32_t a_base = smem_u32(sA + (size_t)s * kAStage);
                 // channel concat of two sources: the source holding channel k0
                 // and its row stride, fixed for the whole stage
-                const bool kin = k0 < p.cin;
-                const bool from_a = k0 < p.cin_a;
+                const bool from_a = !kTwo || k0 < p.cin_a;
                 const __nv_bfloat16* base = from_a ? p.in + k0 : p.in_b + (k0 - p.cin_a);
-                const int64_t ld = from_a ? p.cin_a : p.cin - p.cin_a;
+                const int64_t ld = kTwo ? (from_a ? p.cin_a : p.cin - p.cin_a) : p.cin;
 #pragma unroll
                 for (int i = 0; i < kMine; ++i) {
                     const int row = rg + kRowStep * i;
                     const int32_t src = cur[i];
-                    const bool valid = kin && src >= 0;
+                    const bool valid = src >= 0 && k0 < p.cin;
                     const void* g = valid ? (const void*)(base + (int64_t)src * ld) : (const void*)p.in;
                     cp_async_16(a_base + row * (2 * kKC) + ((c16 ^ kmajor_swz<kKC>(row)) << 4), g, valid ? 16u : 0u);
                 }
@@ -625,9 +626,12 @@ cudaError_t launch_conv_sk(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     p.status = ctx->d_status;
 
     cudaStream_t s = ctx->stream;
-    static std::atomic<uint64_t> optin128{0}, optin256{0};
-    cudaError_t e = rows == 256 ? smem_optin((const void*)conv_sk_kernel<256>, ctx->device, optin256)
-                                : smem_optin((const void*)conv_sk_kernel<128>, ctx->device, optin128);
+    static std::atomic<uint64_t> optin128{0}, optin256{0}, optin128_two{0}, optin256_two{0};
+    const bool two = in_b != nullptr;
+    auto kernel = rows == 256 ? (two ? conv_sk_kernel<256, true> : conv_sk_kernel<256>)
+                              : (two ? conv_sk_kernel<128, true> : conv_sk_kernel<128>);
+    cudaError_t e = smem_optin((const void*)kernel, ctx->device,
+                               rows == 256 ? (two ? optin256_two : optin256) : (two ? optin128_two : optin128));
     if (e != cudaSuccess) return e;
     if (gn_partials) {
         e = cudaMemsetAsync(gn_partials, 0, sizeof(double) * 2 * (size_t)gn_groups * (size_t)tiles, s);
@@ -648,10 +652,7 @@ cudaError_t launch_conv_sk(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
         p.ws = static_cast<float*>(ws);
         p.counters = static_cast<uint32_t*>(counters);
     }
-    if (rows == 256)
-        launch_pdl(conv_sk_kernel<256>, dim3(grid), dim3(kThreads), smem, s, p, wmap);
-    else
-        launch_pdl(conv_sk_kernel<128>, dim3(grid), dim3(kThreads), smem, s, p, wmap);
+    launch_pdl(kernel, dim3(grid), dim3(kThreads), smem, s, p, wmap);
     e = cudaGetLastError();
     if (ws) cudaFreeAsync(ws, s);
     if (counters) cudaFreeAsync(counters, s);

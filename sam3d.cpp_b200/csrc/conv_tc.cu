@@ -181,7 +181,9 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
 // tile, so weight traffic per output row halves. The leader (rank 0) issues
 // the MMAs; the peer's weight TMA completes on the leader's barrier and the
 // peer's gathered rows are relayed to it by a remote mbarrier arrive.
-template <bool kPair, int KC, bool kTF32 = false>
+// kTwo: the input is the channel concat of two sources (p.in_b / p.in_hi_b);
+// a separate instance, so the one-source gather keeps its shorter address path
+template <bool kPair, int KC, bool kTF32 = false, bool kTwo = false>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_tc_kernel(const TcParams p, const __grid_constant__ CUtensorMap wmap) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -327,25 +329,43 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             const int k0 = kc * KC + c16 * (16 / kEs);
             const uint32_t a_base = smem_u32(sA + (size_t)s * kAStage);
-            // channel concat of two sources: the source holding channel k0, its
-            // row stride and column, fixed for the whole stage
-            const bool kin = k0 < p.cin;
-            const bool from_a = k0 < p.cin_a;
-            const int64_t ld = from_a ? p.cin_a : p.cin - p.cin_a;
-            const int kk = from_a ? k0 : k0 - p.cin_a;
+            if constexpr (kTwo) {
+                // channel concat of two sources: the source holding channel k0, its
+                // row stride and column, fixed for the whole stage
+                const bool kin = k0 < p.cin;
+                const bool from_a = k0 < p.cin_a;
+                const int64_t ld = from_a ? p.cin_a : p.cin - p.cin_a;
+                const int kk = from_a ? k0 : k0 - p.cin_a;
 #pragma unroll
-            for (int i = 0; i < kMine; ++i) {
-                const int row = rg + kRowStep * i;
-                const int32_t src = cur[i];
-                const bool valid = kin && src >= 0;
-                // an invalid copy reads nothing; it keeps the first source's base address
-                const int64_t off = valid ? (int64_t)src * ld + kk : 0;
-                const uint32_t d = a_base + row * kRowB + ((c16 ^ kmajor_swz<KCB>(row)) << 4);
-                if constexpr (kTF32) {
-                    cp_async_16(d, (valid && !from_a ? p.in_hi_b : p.in_hi) + off, valid ? 16u : 0u);
-                    cp_async_16(d + kAHalf, (valid && !from_a ? p.in_lo_b : p.in_lo) + off, valid ? 16u : 0u);
-                } else {
-                    cp_async_16(d, (valid && !from_a ? p.in_b : p.in) + off, valid ? 16u : 0u);
+                for (int i = 0; i < kMine; ++i) {
+                    const int row = rg + kRowStep * i;
+                    const int32_t src = cur[i];
+                    const bool valid = kin && src >= 0;
+                    // an invalid copy reads nothing; it keeps the first source's base address
+                    const int64_t off = valid ? (int64_t)src * ld + kk : 0;
+                    const uint32_t d = a_base + row * kRowB + ((c16 ^ kmajor_swz<KCB>(row)) << 4);
+                    if constexpr (kTF32) {
+                        cp_async_16(d, (valid && !from_a ? p.in_hi_b : p.in_hi) + off, valid ? 16u : 0u);
+                        cp_async_16(d + kAHalf, (valid && !from_a ? p.in_lo_b : p.in_lo) + off, valid ? 16u : 0u);
+                    } else {
+                        cp_async_16(d, (valid && !from_a ? p.in_b : p.in) + off, valid ? 16u : 0u);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < kMine; ++i) {
+                    const int row = rg + kRowStep * i;
+                    const int32_t src = cur[i];
+                    const bool valid = src >= 0 && k0 < p.cin;
+                    const uint32_t d = a_base + row * kRowB + ((c16 ^ kmajor_swz<KCB>(row)) << 4);
+                    if constexpr (kTF32) {
+                        const int64_t off = valid ? (int64_t)src * p.cin + k0 : 0;
+                        cp_async_16(d, p.in_hi + off, valid ? 16u : 0u);
+                        cp_async_16(d + kAHalf, p.in_lo + off, valid ? 16u : 0u);
+                    } else {
+                        const void* g = valid ? (const void*)(p.in + (int64_t)src * p.cin + k0) : (const void*)p.in;
+                        cp_async_16(d, g, valid ? 16u : 0u);
+                    }
                 }
             }
             cp_async_arrive_noinc(smem_u32(full + s * kFS + warp / (kProdWarps / kFS)));
@@ -667,7 +687,8 @@ static cudaError_t launch_tc_impl(s3dsp_context* ctx, const s3dsp_kmap* kmap, in
     }
     const int64_t tiles = (n_out + 127) / 128;
     // CTA pairs need an even row-tile count (the last pair may hold one empty tile)
-    const bool pair = !tf32 && (flags & S3DSP_CONV_CTA_PAIR) != 0;
+    // CTA pairs read one source; a concat runs on the one-CTA kernel
+    const bool pair = !tf32 && !in_b && (flags & S3DSP_CONV_CTA_PAIR) != 0;
     const int brows = pair ? bn / 2 : bn;
     const int parts = tf32 ? 2 : 1;
     // 128-byte row chunks per stage (64 bf16 / 32 f32): 64-byte bf16 stages
@@ -740,9 +761,15 @@ static cudaError_t launch_tc_impl(s3dsp_context* ctx, const s3dsp_kmap* kmap, in
 
     const size_t smem = smem_bytes(stages, brows, parts, bn);
     static std::atomic<uint64_t> optin_pair{0}, optin_single{0}, optin_tf32{0};
-    cudaError_t e = tf32   ? smem_optin((const void*)conv_tc_kernel<false, 32, true>, ctx->device, optin_tf32)
+    const bool two = in_b != nullptr;
+    static std::atomic<uint64_t> optin_tf32_two{0}, optin_single_two{0};
+    cudaError_t e = tf32 ? (two ? smem_optin((const void*)conv_tc_kernel<false, 32, true, true>, ctx->device,
+                                             optin_tf32_two)
+                                : smem_optin((const void*)conv_tc_kernel<false, 32, true>, ctx->device, optin_tf32))
                     : pair ? smem_optin((const void*)conv_tc_kernel<true, 64>, ctx->device, optin_pair)
-                           : smem_optin((const void*)conv_tc_kernel<false, 64>, ctx->device, optin_single);
+                           : (two ? smem_optin((const void*)conv_tc_kernel<false, 64, false, true>, ctx->device,
+                                               optin_single_two)
+                                  : smem_optin((const void*)conv_tc_kernel<false, 64>, ctx->device, optin_single));
     if (e == cudaSuccess && smem > (size_t)kSmemOptIn) e = cudaErrorInvalidValue;
     if (e != cudaSuccess) return e;
     if (gn_partials && !p.gn_store) {
@@ -751,8 +778,13 @@ static cudaError_t launch_tc_impl(s3dsp_context* ctx, const s3dsp_kmap* kmap, in
     }
     if (!pair) {
         const dim3 grid((unsigned)tiles, (unsigned)(cout_pad / bn));
-        e = tf32 ? launch_pdl(conv_tc_kernel<false, 32, true>, grid, dim3(kThreads), smem, ctx->stream, p, wmap)
-                 : launch_pdl(conv_tc_kernel<false, 64>, grid, dim3(kThreads), smem, ctx->stream, p, wmap);
+        if (tf32)
+            e = two ? launch_pdl(conv_tc_kernel<false, 32, true, true>, grid, dim3(kThreads), smem, ctx->stream, p, wmap)
+                    : launch_pdl(conv_tc_kernel<false, 32, true>, grid, dim3(kThreads), smem, ctx->stream, p, wmap);
+        else
+            e = two ? launch_pdl(conv_tc_kernel<false, 64, false, true>, grid, dim3(kThreads), smem, ctx->stream, p,
+                                 wmap)
+                    : launch_pdl(conv_tc_kernel<false, 64>, grid, dim3(kThreads), smem, ctx->stream, p, wmap);
         if (e != cudaSuccess) return e;
         return cudaGetLastError();
     }
