@@ -329,69 +329,62 @@ def time_graphs(torch, stream, path, flush, steps, warmup, n_marks):
     return dev_ms, np.array(phase_ms)
 
 
-def e2e_workers(s3dsp, torch, device, main_stream, host_call, ref_out, steps, warmup, workers_n, flush):
+E2E_STREAMS = 4  # contexts (each its own stream) that one host thread keeps busy in the e2e measurement
+
+
+def e2e_queued(s3dsp, torch, device, main_stream, queued_call, ref_out, steps, warmup, flush):
     """Device time of `steps` host-buffer calls (rounded up to a multiple of
-    workers_n) made by workers_n threads, each with its own context, stream
-    and pinned output. Each call is preceded, on its stream, by the L2 flush,
-    inside the timed region. The span runs from one event that every worker
-    stream waits on to the last worker's end event. Every worker's last output
-    must equal `ref_out` bit for bit. Returns (ms, calls timed)."""
-    per = max(1, -(-steps // workers_n))
-    workers = []
-    for _ in range(workers_n):
+    E2E_STREAMS) issued by one host thread round-robin over E2E_STREAMS
+    contexts, each with its own stream and pinned output: the queued entry
+    point returns once its copies in, kernels and copy out are on the stream,
+    so one call's PCIe copies overlap another's kernels. Each call is preceded,
+    on its stream, by the L2 flush, inside the timed region. The span runs from
+    one event that every stream waits on to the last stream's end event. Every
+    context's last output must equal `ref_out` bit for bit. Returns (ms,
+    calls timed)."""
+    per = max(1, -(-steps // E2E_STREAMS))
+    lanes = []
+    for _ in range(E2E_STREAMS):
         st = torch.cuda.Stream(device)
-        workers.append((st, s3dsp.Context(device.index, stream=st.cuda_stream, flags=s3dsp.CONTEXT_DEFERRED_CHECKS),
-                        torch.empty_like(ref_out).pin_memory()))
+        lanes.append((st, s3dsp.Context(device.index, stream=st.cuda_stream, flags=s3dsp.CONTEXT_DEFERRED_CHECKS),
+                      torch.empty_like(ref_out).pin_memory()))
+    # warm-up: at least `warmup` rounds and two seconds of queued calls before
+    # the timed region (on a freshly started box the overlapped copies run at
+    # about half speed for the first seconds of such traffic)
+    t_end = time.perf_counter() + 2.0
+    rounds = 0
+    while rounds < max(8, warmup) or time.perf_counter() < t_end:
+        for st, cx, out in lanes:
+            with torch.cuda.stream(st):
+                flush()  # as in the timed loop (torch's per-stream workspace exists before it)
+            queued_call(cx, out)
+        rounds += 1
+        if rounds % 8 == 0:
+            for st, _, _ in lanes:
+                st.synchronize()
+    for st, _, _ in lanes:
+        st.synchronize()
     start = torch.cuda.Event(enable_timing=True)
     final = torch.cuda.Event(enable_timing=True)
-    ends = [torch.cuda.Event() for _ in workers]
-    ready, go = threading.Barrier(workers_n + 1), threading.Barrier(workers_n + 1)
-    errors = []
-    flush_lock = threading.Lock()
-
-    def body(i):
-        st, cx, out = workers[i]
-        try:
-            torch.cuda.set_device(device)
+    start.record(main_stream)
+    for st, _, _ in lanes:
+        st.wait_event(start)
+    for _ in range(per):
+        for st, cx, out in lanes:
             with torch.cuda.stream(st):
-                for _ in range(max(2, warmup // workers_n)):
-                    host_call(cx, out)
-                st.synchronize()
-                ready.wait()
-                go.wait()
-                st.wait_event(start)
-                for _ in range(per):
-                    with flush_lock:  # one flush buffer, queued on this worker's stream
-                        flush()
-                    host_call(cx, out)
-                ends[i].record(st)
-        except Exception as e:  # surfaced after the join
-            errors.append(e)
-            ready.abort()
-            go.abort()
-
-    threads = [threading.Thread(target=body, args=(i,)) for i in range(workers_n)]
-    for t in threads:
-        t.start()
-    try:
-        ready.wait()
-        start.record(main_stream)
-        go.wait()
-    except threading.BrokenBarrierError:
-        pass
-    for t in threads:
-        t.join()
-    if errors:
-        raise errors[0]
-    for e in ends:
-        main_stream.wait_event(e)
+                flush()
+            queued_call(cx, out)
+    for st, _, _ in lanes:
+        ev = torch.cuda.Event()
+        ev.record(st)
+        main_stream.wait_event(ev)
     final.record(main_stream)
     main_stream.synchronize()
-    for _, cx, out in workers:
+    for _, cx, out in lanes:
         cx.check()
         if not torch.equal(out, ref_out):
-            raise RuntimeError("a concurrent host call's output differs from the serial call's")
-    return start.elapsed_time(final), per * workers_n
+            raise RuntimeError("a queued host call's output differs from the synchronous call's")
+    return start.elapsed_time(final), per * E2E_STREAMS
 
 
 def gather_rows(torch, world, values):
@@ -484,21 +477,21 @@ def run_ours(args, rank, world, local_rank):
     ce.record(stream)
     stream.synchronize()
     copy_ms = cs.elapsed_time(ce) / args.steps
-    host_call(ctx, out_h)  # the reference output of the concurrent callers
+    host_call(ctx, out_h)  # the reference output of the queued calls
     stream.synchronize()
-    # serving: host threads of this rank, each with its own context, stream
-    # and output buffer, call the same entry point concurrently, so one call's
-    # copies overlap another's kernels; one thread per spare host CPU of the
-    # rank (at most 4)
-    workers_n = max(1, min(4, n_cpus - 1))
-    pipe_ms, pipe_steps = e2e_workers(s3dsp, torch, device, stream, host_call, out_h, args.steps, args.warmup,
-                                      workers_n, flush)
+
+    def queued_call(cx, out):
+        cx.res_block_gn_host_queued(s3dsp.PREC_BF16, coords_h, x_h, path.w1, path.b1, path.gamma, path.beta,
+                                    path.w2, path.b2, out)
+
+    pipe_ms, pipe_steps = e2e_queued(s3dsp, torch, device, stream, queued_call, out_h, args.steps, args.warmup,
+                                     flush)
     clocks = sampler.stop()
     h2d = coords_h.numel() * 4 + x_h.numel() * 4
     d2h = out_h.numel() * 4
     ctx.check()
     per_rank = gather_rows(torch, world, [dev_ms / args.steps, copy_ms, serial_ms / args.steps,
-                                          pipe_ms / pipe_steps, float(workers_n), float(n_cpus)])
+                                          pipe_ms / pipe_steps, float(E2E_STREAMS), float(n_cpus)])
 
     # max over ranks
     vals = torch.tensor([dev_ms, serial_ms, pipe_ms], dtype=torch.float64, device=device)
@@ -531,19 +524,22 @@ def run_ours(args, rank, world, local_rank):
                        "l2": "flushed between steps (512 MiB write, then 256 MiB read of another buffer)",
                        "timing": "device steps replayed as a CUDA graph of the library calls (the breakdown and "
                                  "the roofline's conv time from a second capture with events between the phases); "
-                                 "e2e = s3dsp_res_block_gn_host (host buffers in/out) per step, called by concurrent "
-                                 "host threads of each rank (serial figure beside it)"},
+                                 "e2e = the host-buffer block entry point (host coords and features in, result out) "
+                                 "per step, queued round-robin over several streams by one host thread (the "
+                                 "synchronous one-call-at-a-time figure beside it)"},
             "roofline": roof,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": pipe_ms / pipe_steps,
-                    "mode": "per rank: host threads (one per spare CPU of the rank's share of its GPU's NUMA node, "
-                            "at most 4), each its own context and stream, calling s3dsp_res_block_gn_host "
-                            "concurrently; L2 flushed on the calling stream before every call (inside the timed "
-                            "region); device-timed from one start event to the last call's end; max over ranks",
+                    "mode": f"per rank: one host thread (pinned to its GPU's NUMA node) issuing "
+                            f"s3dsp_res_block_gn_host_queued round-robin over {E2E_STREAMS} contexts (one stream "
+                            "each), so one call's copies overlap another's kernels; L2 flushed on the calling "
+                            "stream before every call (inside the timed region); device-timed from one start "
+                            "event to the last call's end; max over ranks. serial_* = the synchronous "
+                            "s3dsp_res_block_gn_host, one call at a time",
                     "steps": pipe_steps, "serial_value": total_units / (serial_ms / 1e3),
                     "serial_ms_per_step": serial_ms / args.steps,
                     "per_rank_ms": [{"rank": r, "device_step": v[0], "copies_only": v[1], "call_serial": v[2],
-                                     "call_concurrent": v[3], "workers": int(v[4]), "cpus": int(v[5])}
+                                     "call_queued": v[3], "streams": int(v[4]), "cpus": int(v[5])}
                                     for r, v in enumerate(per_rank)]},
             # inside the timed regions: both graphs' replays, serial host calls, worker calls
             "gpu_launches": path.launches_per_step * (3 * args.steps + pipe_steps),

@@ -646,6 +646,22 @@ S3DSP_API s3d_status s3dsp_res_block_gn_host(s3dsp_context *ctx, uint32_t precis
                                              const float *gamma, const float *beta, const void *w2,
                                              const float *b2, int32_t groups, float eps,
                                              float *h_out, char *error, uint64_t error_capacity);
+/* s3dsp_res_block_gn_host without the wait: the copies in, the tables, the
+ * block and the copy out are queued on the context's stream and the call
+ * returns; h_out holds the result once that stream reaches the end of this
+ * work (synchronise the stream or an event recorded after the call). Needs a
+ * context created with S3DSP_CONTEXT_DEFERRED_CHECKS (device-detected input
+ * errors are read by s3dsp_context_check). The host buffers must stay valid
+ * until then; pinned host memory lets the copies of one call overlap another
+ * context's kernels, which is how one host thread keeps several contexts
+ * busy. No counterpart in the reference (its Backend::run is synchronous,
+ * backend.hpp:16-92). */
+S3DSP_API s3d_status s3dsp_res_block_gn_host_queued(s3dsp_context *ctx, uint32_t precision,
+                                                    const int32_t *h_coords, int64_t n, const float *h_x,
+                                                    int64_t c, const void *w1, const float *b1,
+                                                    const float *gamma, const float *beta, const void *w2,
+                                                    const float *b2, int32_t groups, float eps, float *h_out,
+                                                    char *error, uint64_t error_capacity);
 S3DSP_API s3d_status s3dsp_mesh_upsample_level_host(
     s3dsp_context *ctx, uint32_t precision, const int32_t *h_parent_coords, int64_t np,
     const float *h_x, int64_t cin, int64_t cout, const float *gn1_w, const float *gn1_b,

@@ -25,6 +25,12 @@ cudaError_t lib_pool(int device, cudaMemPool_t* out) {
         if (e != cudaSuccess) return e;
         uint64_t keep = ~0ull;
         e = cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+        // no reuse of a block freed on another stream whose free has not run
+        // yet: the pool would make this stream wait for that one, and contexts
+        // on separate streams would serialise on each other's scratch
+        int no_deps = 0;
+        if (e == cudaSuccess)
+            e = cudaMemPoolSetAttribute(pool, cudaMemPoolReuseAllowInternalDependencies, &no_deps);
         if (e != cudaSuccess) {
             cudaMemPoolDestroy(pool);
             return e;

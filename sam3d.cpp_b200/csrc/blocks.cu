@@ -337,15 +337,19 @@ extern "C" S3DSP_API s3d_status s3dsp_slat_res_block_concat(
 // Backend (upload coords + features, run, read back: session.cpp:927-962), as
 // one call. Weights stay device-resident (packed once at model load).
 // ---------------------------------------------------------------------------
-extern "C" S3DSP_API s3d_status s3dsp_res_block_gn_host(s3dsp_context* ctx, uint32_t precision,
-                                                        const int32_t* h_coords, int64_t n, const float* h_x, int64_t c,
-                                                        const void* w1, const float* b1, const float* gamma,
-                                                        const float* beta, const void* w2, const float* b2,
-                                                        int32_t groups, float eps, float* h_out, char* error,
-                                                        uint64_t error_capacity) {
-    clear_error(error, error_capacity);
+namespace {
+// host coords + features in, the block, host output out, on the context's
+// stream; `wait` = synchronise and report device-detected errors before
+// returning (the synchronous entry point), else return once queued
+s3d_status res_block_gn_host_impl(s3dsp_context* ctx, uint32_t precision, const int32_t* h_coords, int64_t n,
+                                  const float* h_x, int64_t c, const void* w1, const float* b1, const float* gamma,
+                                  const float* beta, const void* w2, const float* b2, int32_t groups, float eps,
+                                  float* h_out, bool wait, char* error, uint64_t error_capacity) {
     if (!ctx || !h_coords || !h_x || !h_out || n <= 0 || c <= 0)
         return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "bad argument");
+    if (!wait && !(ctx->flags & S3DSP_CONTEXT_DEFERRED_CHECKS))
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT,
+                    "the queued form needs a context with S3DSP_CONTEXT_DEFERRED_CHECKS");
     S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
     Scratch sc(ctx->stream);
     int32_t* d_coords;
@@ -368,12 +372,35 @@ extern "C" S3DSP_API s3d_status s3dsp_res_block_gn_host(s3dsp_context* ctx, uint
     }
     s3dsp_kmap_free(ctx, k);
     s3dsp_hash_free(ctx, h);
-    if (s == S3D_OK) {
+    if (s == S3D_OK && wait) {
         const cudaError_t e = cudaStreamSynchronize(ctx->stream);
         if (e != cudaSuccess) s = cuda_fail(error, error_capacity, e, "cudaStreamSynchronize");
+        if (s == S3D_OK && (ctx->flags & S3DSP_CONTEXT_DEFERRED_CHECKS)) s = check_status(ctx, error, error_capacity);
     }
-    if (s == S3D_OK && (ctx->flags & S3DSP_CONTEXT_DEFERRED_CHECKS)) s = check_status(ctx, error, error_capacity);
     return s;
+}
+}  // namespace
+
+extern "C" S3DSP_API s3d_status s3dsp_res_block_gn_host(s3dsp_context* ctx, uint32_t precision,
+                                                        const int32_t* h_coords, int64_t n, const float* h_x, int64_t c,
+                                                        const void* w1, const float* b1, const float* gamma,
+                                                        const float* beta, const void* w2, const float* b2,
+                                                        int32_t groups, float eps, float* h_out, char* error,
+                                                        uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    return res_block_gn_host_impl(ctx, precision, h_coords, n, h_x, c, w1, b1, gamma, beta, w2, b2, groups, eps, h_out,
+                                  true, error, error_capacity);
+}
+
+extern "C" S3DSP_API s3d_status s3dsp_res_block_gn_host_queued(s3dsp_context* ctx, uint32_t precision,
+                                                               const int32_t* h_coords, int64_t n, const float* h_x,
+                                                               int64_t c, const void* w1, const float* b1,
+                                                               const float* gamma, const float* beta, const void* w2,
+                                                               const float* b2, int32_t groups, float eps,
+                                                               float* h_out, char* error, uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    return res_block_gn_host_impl(ctx, precision, h_coords, n, h_x, c, w1, b1, gamma, beta, w2, b2, groups, eps, h_out,
+                                  false, error, error_capacity);
 }
 
 extern "C" S3DSP_API s3d_status s3dsp_mesh_upsample_level_host(

@@ -48,7 +48,7 @@ EXPORTED = [
     "s3dsp_gn_stats", "s3dsp_gn_finalize", "s3dsp_channel_affine", "s3dsp_layer_norm",
     "s3dsp_convert", "s3dsp_slat_tables_build", "s3dsp_slat_tables_free", "s3dsp_slat_tables_coarse_rows",
     "s3dsp_slat_tables_coarse_kmap", "s3dsp_slat_tables_export", "s3dsp_slat_downsample", "s3dsp_slat_upsample",
-    "s3dsp_res_block_gn", "s3dsp_mesh_upsample_level", "s3dsp_slat_res_block", "s3dsp_res_block_gn_host",
+    "s3dsp_res_block_gn", "s3dsp_mesh_upsample_level", "s3dsp_slat_res_block", "s3dsp_res_block_gn_host", "s3dsp_res_block_gn_host_queued",
     "s3dsp_mesh_upsample_level_host",
 ]
 
@@ -180,6 +180,8 @@ def load(path: str = LIB_PATH):
         "s3dsp_slat_res_block": (_u32, [_vp, _vp, _u32, _vp, _i64, _i64, _i64] + [_vp] * 11 + [_cp, _u64]),
         "s3dsp_res_block_gn_host": (_u32, [_vp, _u32, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _f,
                                            _vp, _cp, _u64]),
+        "s3dsp_res_block_gn_host_queued": (_u32, [_vp, _u32, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp,
+                                                  _i32, _f, _vp, _cp, _u64]),
         "s3dsp_mesh_upsample_level_host": (_u32, [_vp, _u32, _vp, _i64, _vp, _i64, _i64] + [_vp] * 12 + [_cp, _u64]),
     }
     for name, (res, args) in sig.items():
@@ -759,6 +761,15 @@ class Context:
                           eps=1e-5):
         _call(load().s3dsp_res_block_gn_host, self.handle, precision, ptr(coords_h), coords_h.shape[0], ptr(x_h),
               x_h.shape[1], ptr(w1), ptr(b1), ptr(gamma), ptr(beta), ptr(w2), ptr(b2), groups, eps, ptr(out_h))
+
+    def res_block_gn_host_queued(self, precision: int, coords_h, x_h, w1, b1, gamma, beta, w2, b2, out_h,
+                                 groups=32, eps=1e-5):
+        """Queued form of res_block_gn_host: returns once the work is on the
+        context's stream (a DEFERRED_CHECKS context); out_h is ready when the
+        stream gets there."""
+        _call(load().s3dsp_res_block_gn_host_queued, self.handle, precision, ptr(coords_h), coords_h.shape[0],
+              ptr(x_h), x_h.shape[1], ptr(w1), ptr(b1), ptr(gamma), ptr(beta), ptr(w2), ptr(b2), groups, eps,
+              ptr(out_h))
 
     def mesh_upsample_level(self, parents: Hash, precision: int, x, cout, gn1_w, gn1_b, conv1_w, conv1_b, gn2_w,
                             gn2_b, conv2_w, conv2_b, skip_w, skip_b, child_coords, out):

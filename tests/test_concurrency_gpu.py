@@ -85,3 +85,38 @@ def test_concurrent_host_blocks_bit_exact(setup, flags):
     for t in range(THREADS):
         for o in results[t]:
             assert torch.equal(o, expected[t]), f"thread {t}: output differs from the call made alone"
+
+
+def test_queued_host_blocks_round_robin_bit_exact(setup):
+    """One host thread queues host-buffer blocks on several contexts
+    (s3dsp_res_block_gn_host_queued), round robin; after the streams drain,
+    every output equals the synchronous call's, bit for bit."""
+    params, objs, expected = setup
+    lanes = []
+    for t in range(THREADS):
+        st = torch.cuda.Stream()
+        lanes.append((st, s3dsp.Context(0, stream=st.cuda_stream, flags=s3dsp.CONTEXT_DEFERRED_CHECKS)))
+    outs = [[torch.empty((objs[t][0].shape[0], C), dtype=torch.float32).pin_memory() for _ in range(CALLS)]
+            for t in range(THREADS)]
+    for i in range(CALLS):
+        for t, (st, cx) in enumerate(lanes):
+            coords, x = objs[t]
+            cx.res_block_gn_host_queued(s3dsp.PREC_BF16, coords, x, params["w1"], params["b1"], params["gamma"],
+                                        params["beta"], params["w2"], params["b2"], outs[t][i])
+    for st, cx in lanes:
+        st.synchronize()
+        cx.check()
+    for t in range(THREADS):
+        for o in outs[t]:
+            assert torch.equal(o, expected[t]), f"context {t}: queued output differs from the synchronous call's"
+
+
+def test_queued_host_block_needs_deferred_checks(setup):
+    params, objs, _ = setup
+    cx = s3dsp.Context(0)
+    coords, x = objs[0]
+    out = torch.empty((coords.shape[0], C), dtype=torch.float32).pin_memory()
+    with pytest.raises(s3dsp.S3dError) as ei:
+        cx.res_block_gn_host_queued(s3dsp.PREC_BF16, coords, x, params["w1"], params["b1"], params["gamma"],
+                                    params["beta"], params["w2"], params["b2"], out)
+    assert ei.value.status == s3dsp.S3D_INVALID_ARGUMENT
