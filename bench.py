@@ -1151,6 +1151,85 @@ def run_slat(args, rank, world, local_rank):
 
 
 # ---------------------------------------------------------------------------
+# the GS decoder's Swin torso (the producer of the mesh decoder's 768-channel input)
+# ---------------------------------------------------------------------------
+def run_gs_torso(args, rank, world, local_rank):
+    """The GS decoder (gs_decoder_graph.cpp:13-155) on the config-2
+    coordinates (15,159 tokens): input Linear + APE, 12 Swin blocks (window
+    attention in f32 + Linears), final LayerNorm + Linear 768 -> 448. The
+    window tables and APE are built once (per object); a step is one pass,
+    the L2 flushed between steps. Unit: one output row of a Linear or of the
+    attention. Replicas only at N > 1."""
+    import torch
+    import s3dsp
+    import oracle
+    import gs
+    import workloads
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    stream = torch.cuda.Stream(device)
+    torch.cuda.set_stream(stream)
+    ctx = s3dsp.Context(local_rank, stream=stream.cuda_stream, flags=s3dsp.CONTEXT_DEFERRED_CHECKS)
+    prec = {"f32": s3dsp.PREC_F32_STRICT, "tf32": s3dsp.PREC_F32_3XTF32, "bf16": s3dsp.PREC_BF16}[args.precision]
+    coords = workloads.config2(seed=0)["coords"]
+    n = len(coords)
+    params = gs.gs_params(0)
+    x_h = workloads.normal((n, gs.IN_CH), 3)
+    tb = gs.GsTablesDev(s3dsp, ctx, torch.from_numpy(coords).to(device), torch)
+    torso = gs.GsTorso(s3dsp, ctx, params, prec, device)
+    x = torch.from_numpy(x_h).to(device)
+    flush = L2Flush(torch, device)
+    out = None
+    for _ in range(args.warmup):
+        out = torso.forward(tb, x)
+        flush()
+    stream.synchronize()
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for i in range(args.steps):
+        starts[i].record(stream)
+        out = torso.forward(tb, x)
+        ends[i].record(stream)
+        flush()
+    stream.synchronize()
+    clocks = sampler.stop()
+    ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends)) / args.steps
+    ctx.check()
+    vals = torch.tensor([ms], dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX)
+    ms = vals.item()
+    if rank != 0:
+        return None
+    # CPU: the oracle's float64 restatement with the first two blocks (a bounded sample), scaled per unit
+    p2 = dict(params, blocks=params["blocks"][:2])
+    t0 = time.perf_counter()
+    exp2 = oracle.gs_torso_forward(coords, x_h, p2)
+    cpu_s = time.perf_counter() - t0
+    got2 = gs.GsTorso(s3dsp, ctx, p2, prec, device).forward(tb, x).double().cpu().numpy()
+    rel = float(np.sqrt(((got2 - exp2) ** 2).sum() / (exp2 ** 2).sum()))
+    u = gs.units(n)
+    return {
+        "metric": "token rows/s (GS decoder Swin torso, one pass)", "value": u * world / (ms / 1e3),
+        "unit": "rows/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": args.precision,
+        "data": "synthetic (the config-2 64^3 shell's coordinates, random latent and weights)",
+        "config": {"workload": "GS decoder: Linear 8->768 + APE, 12 Swin blocks (C=768, 12 heads, window 8, shifts "
+                               "0/4; attention f32), LayerNorm + Linear 768->448",
+                   "tokens": n, "windows": [len(w) for w in tb.windows], "units_per_step": u,
+                   "l2": "flushed between steps (512 MiB write + 256 MiB read)", "parallelism": f"replicas{world}"},
+        "rel_l2_vs_oracle_two_blocks": rel,
+        "cpu_baseline": {"value": gs.units(n, 2) / cpu_s, "unit": "rows/s", "cores": len(os.sched_getaffinity(0)),
+                         "kind": "port", "sample": "input layer + the first two blocks + head through the oracle's "
+                                                   "float64 numpy restatement"},
+        "clocks": clocks,
+    }
+
+
+# ---------------------------------------------------------------------------
 # the coordinate pipeline in front of the path (session.cpp argwhere, prune, downsample)
 # ---------------------------------------------------------------------------
 def run_coords(args, rank, world, local_rank):
@@ -1560,15 +1639,16 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="config2",
-                    choices=["config2", "config1", "config3", "volume", "objects", "slat", "coords", "gs_tables",
-                             "flexicubes"],
+                    choices=["config2", "config1", "config3", "volume", "objects", "slat", "gs_torso", "coords",
+                             "gs_tables", "flexicubes"],
                     help="config2: the headline (default); volume: config 5b, one volume split across ranks; "
                          "objects: config 5a, 64 objects through config 4 sharded by object; "
-                         "config1 / config3: single layers; slat: the SLat generator's sparse stages; coords: the coordinate pipeline before the path; "
+                         "config1 / config3: single layers; slat: the SLat generator's sparse stages; gs_torso: the GS decoder's "
+                         "Swin torso; coords: the coordinate pipeline before the path; "
                          "gs_tables: the GS decoder's Swin window tables and APE; flexicubes: the mesh extraction after "
                          "the path")
     ap.add_argument("--precision", default=None, choices=["f32", "tf32", "bf16"],
-                    help="config1 / config3 (default f32) and slat (default bf16): f32 = F32-strict FFMA, "
+                    help="config1 / config3 (default f32), slat and gs_torso (default bf16): f32 = F32-strict FFMA, "
                          "tf32 = 3xTF32 tensor cores, bf16")
     ap.add_argument("--no-sub", action="store_true", help="config2: skip the f32 / 5a / 5b sub-records")
     ap.add_argument("--profile-case", choices=sorted(PROFILE_CASES),
@@ -1577,7 +1657,7 @@ def main():
     ap.add_argument("--reps", type=int, default=3, help="--profile-case repetitions after one warm-up")
     args = ap.parse_args()
     if args.precision is None:
-        args.precision = "bf16" if args.workload == "slat" else "f32"
+        args.precision = "bf16" if args.workload in ("slat", "gs_torso") else "f32"
     if args.profile_case:
         profile_case(args.profile_case, args.reps)
         return
@@ -1594,6 +1674,7 @@ def main():
             torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                                  device_id=torch.device("cuda", local_rank))
         runner = {"config2": run_ours, "volume": run_volume, "objects": run_objects, "slat": run_slat,
+                  "gs_torso": run_gs_torso,
                   "config1": run_layers,
                   "config3": run_layers, "coords": run_coords, "gs_tables": run_gs_tables,
                   "flexicubes": run_flexicubes}[args.workload]

@@ -80,6 +80,8 @@ typedef struct s3dsp_shard s3dsp_shard;
 /* conv epilogue / prologue flags */
 #define S3DSP_EPI_SILU UINT32_C(1)      /* apply SiLU after bias (and residual) */
 #define S3DSP_PRO_AFFINE_SILU UINT32_C(2) /* gathered x -> silu((x - sub[c]) * mul[c] + add[c]) */
+#define S3DSP_EPI_GELU UINT32_C(64)     /* apply GELU, tanh form 0.5x(1 + tanh(sqrt(2/pi)(x + 0.044715x^3))),
+                                           after bias (and residual); the MLP of gs_decoder_graph.cpp:140 */
 #define S3DSP_CONV_TILE128 UINT32_C(8)   /* BF16: force one CTA per 128-row tile */
 #define S3DSP_CONV_STREAM_K UINT32_C(16) /* BF16: force 256-row tiles split evenly over all SMs
                                           (stream-K). No kernel flag: chosen by size, see s3dsp_conv_kernel */
@@ -316,6 +318,31 @@ S3DSP_API s3d_status s3dsp_samt_read(const char *path, void *h_dst, uint64_t cap
 S3DSP_API s3d_status s3dsp_samt_write(const char *path, int32_t n_dims, const int64_t *ne,
                                       int32_t ggml_type, const void *data, uint64_t nbytes,
                                       char *error, uint64_t error_capacity);
+
+/* ---------------------------------------------------------------------------
+ * GS decoder torso (gs_decoder_graph.cpp:13-155): its Linears are s3dsp_conv
+ * with kmap NULL (S3DSP_EPI_GELU for the MLP, `residual` for the skips), its
+ * norms s3dsp_layer_norm; these two calls are the rest.
+ * ------------------------------------------------------------------------- */
+/* y[i] = x[rows[i]] for i < n_out (x [n_in, c] of x_dtype, y [n_out, c] of
+ * y_dtype): ggml_get_rows with the window tables' bucket order (:64). A row
+ * index outside [0, n_in) gives a zero row and is reported by the next
+ * status check. */
+S3DSP_API s3d_status s3dsp_gather_rows(s3dsp_context *ctx, const void *x, uint32_t x_dtype, int64_t n_in,
+                                       int64_t c, const int32_t *d_rows, int64_t n_out, void *y,
+                                       uint32_t y_dtype, char *error, uint64_t error_capacity);
+/* Swin window attention (:88-121). qkv f32 [n, 3c], rows in bucket order,
+ * each row q | k | v with head h at columns h*d .. h*d+d-1 (d = c / heads:
+ * 32 or 64). d_windows int32 [n_windows, 2] = (first row, rows) of each
+ * window (the buckets' windows, consecutive rows). For every head and
+ * window: softmax(q k^T / sqrt(d)) v over the window's rows, in f32 (max,
+ * exp, sum, weighted values, as ggml_soft_max + ggml_mul_mat). Row i of the
+ * result goes to out[d_scatter[i]] (the bucket order back to token order,
+ * get_rows by bwd_idx), or out[i] when d_scatter is NULL. out f32 [n, c]. */
+S3DSP_API s3d_status s3dsp_window_attention(s3dsp_context *ctx, const float *qkv, int64_t n, int64_t c,
+                                            int32_t heads, const int32_t *d_windows, int64_t n_windows,
+                                            const int32_t *d_scatter, float *out, char *error,
+                                            uint64_t error_capacity);
 
 /* ---------------------------------------------------------------------------
  * FlexiCubes extraction at resolution 256 (extract_object_mesh,

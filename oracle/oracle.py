@@ -462,3 +462,67 @@ def flexicubes(raw: np.ndarray, coords: np.ndarray, tables=None, use_ref: bool =
                edges=np.zeros((ne, 2), np.int32))
     fetch(*(_ptr(out[k]) for k in ("vertices", "attrs", "faces", "surface", "cases", "edges")))
     return out
+
+
+# ---------------------------------------------------------------------------
+# GS decoder Swin torso (src/objects_runtime/gs_decoder_graph.cpp:13-155)
+# ---------------------------------------------------------------------------
+def _norm64(x, eps):
+    """ggml_norm: (x - mean) / sqrt(var + eps), biased variance, no affine."""
+    m = x.mean(axis=1, keepdims=True)
+    d = x - m
+    return d / np.sqrt((d * d).mean(axis=1, keepdims=True) + eps)
+
+
+def _gelu64(x):
+    """GELU, tanh form (the approximation ggml_gelu evaluates; GGML's CPU
+    path reads it from an f16 table, which this float64 restatement does not)."""
+    return 0.5 * x * (1.0 + np.tanh(np.sqrt(2.0 / np.pi) * (x + 0.044715 * x ** 3)))
+
+
+def window_attention(qkv, heads, buckets, bkt_idx):
+    """The bucket loop of gs_decoder_graph.cpp:88-121 in float64: qkv [n, 3c]
+    rows in bucket order; per bucket {len, off, n_win} and per head,
+    softmax(q k^T / sqrt(d)) v within each window of `len` consecutive rows;
+    the result back in token order (row i -> token bkt_idx[i])."""
+    qkv = np.asarray(qkv, np.float64)
+    n, c3 = qkv.shape
+    c = c3 // 3
+    d = c // heads
+    acc = np.zeros((n, c), np.float64)
+    for len_, off, nw in buckets:
+        blk = qkv[off:off + len_ * nw].reshape(nw, len_, 3, heads, d)
+        q, k, v = blk[:, :, 0], blk[:, :, 1], blk[:, :, 2]          # [nw, len, H, d]
+        s = np.einsum("wqhd,wkhd->whqk", q, k) / np.sqrt(d)
+        s = np.exp(s - s.max(axis=-1, keepdims=True))
+        s /= s.sum(axis=-1, keepdims=True)
+        o = np.einsum("whqk,wkhd->wqhd", s, v)
+        acc[off:off + len_ * nw] = o.reshape(len_ * nw, c)
+    out = np.zeros_like(acc)
+    out[np.asarray(bkt_idx)] = acc
+    return out
+
+
+def gs_torso_forward(coords, x, p, taps=None):
+    """The GS decoder in the reference's op order, float64: input Linear +
+    APE (:37-48); per block (tables of shift 0 for even blocks, (4,4,4) for
+    odd): norm(1e-6) -> bucket-order gather -> q, k, v Linears -> window
+    attention -> token order -> to_out Linear -> + h; norm(1e-6) -> Linear ->
+    GELU -> Linear -> + h (:55-142); final norm(1e-5) -> out Linear
+    (:146-151). Tables and APE by the restated GsTables::build. p as
+    sam3d.cpp_b200/gs.py makes it."""
+    heads = 12
+    tabs = [gs_window_tables(coords, si) for si in (0, 1)]
+    h = np.asarray(x, np.float64) @ np.asarray(p["input_layer"]["w"], np.float64).T + p["input_layer"]["b"]
+    h = h + ape(coords, h.shape[1]).astype(np.float64)
+    for i, b in enumerate(p["blocks"]):
+        bkt, _, buckets = tabs[i % 2]
+        hb = _norm64(h, 1e-6)[bkt]
+        qkv = hb @ np.asarray(b["qkv"]["w"], np.float64).T + b["qkv"]["b"]
+        ao = window_attention(qkv, heads, buckets, bkt)
+        h = h + ao @ np.asarray(b["out"]["w"], np.float64).T + b["out"]["b"]
+        g = _gelu64(_norm64(h, 1e-6) @ np.asarray(b["mlp0"]["w"], np.float64).T + b["mlp0"]["b"])
+        h = h + g @ np.asarray(b["mlp2"]["w"], np.float64).T + b["mlp2"]["b"]
+        if taps is not None:
+            taps[f"block{i}"] = h
+    return _norm64(h, 1e-5) @ np.asarray(p["out_layer"]["w"], np.float64).T + p["out_layer"]["b"]

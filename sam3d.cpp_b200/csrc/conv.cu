@@ -87,6 +87,8 @@ s3d_status conv_impl(s3dsp_context* ctx, const s3dsp_kmap* kmap, int32_t kvol, u
     if (gn_partials && (gn_groups <= 0 || gn_groups > 64 || cout % gn_groups))
         return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "GroupNorm groups %d must divide cout %lld (<= 64)",
                     gn_groups, (long long)cout);
+    if ((flags & S3DSP_EPI_SILU) && (flags & S3DSP_EPI_GELU))
+        return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "SiLU and GELU epilogues are exclusive");
     if ((flags & S3DSP_PRO_AFFINE_SILU) && (!pro_sub || !pro_mul || !pro_add))
         return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "prologue arrays missing");
     const int ca = (int)(in_b ? cin_a : cin);

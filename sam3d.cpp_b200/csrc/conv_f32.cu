@@ -191,6 +191,7 @@ __global__ void __launch_bounds__(NT) conv_f32_kernel(const F32ConvParams p) {
                 csq[j] += (double)v * (double)v;
             }
             if (p.flags & S3DSP_EPI_SILU) v = silu_f(v);
+            if (p.flags & S3DSP_EPI_GELU) v = 0.5f * v * (1.0f + tanhf(0.7978845608028654f * (v + 0.044715f * v * v * v)));
             if (p.out_dtype == S3DSP_F32)
                 reinterpret_cast<float*>(p.out)[r * p.cout + col] = v;
             else if (p.out_dtype == S3DSP_BF16)

@@ -380,7 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
                 const int out_k = (p.cout & 3) ? -1 : p.out_dtype == S3DSP_F32 ? 0 : p.out_dtype == S3DSP_BF16 ? 1 : -1;
                 const int res_k = !p.residual ? 0 : p.res_dtype == S3DSP_F32 ? 1 : p.res_dtype == S3DSP_BF16 ? 2 : -1;
                 const int silu_k = (p.flags & S3DSP_EPI_SILU) ? 1 : 0;
-                const int sel = (out_k < 0 || res_k < 0) ? -1 : ((out_k * 3 + res_k) * 2 + silu_k) * 2 + (stats ? 1 : 0);
+                const int sel = (out_k < 0 || res_k < 0 || (p.flags & S3DSP_EPI_GELU)) ? -1 : ((out_k * 3 + res_k) * 2 + silu_k) * 2 + (stats ? 1 : 0);
                 const uint32_t so_base = smem_u32(stage_out);
                 for (int sub = 0; sub < kSub; ++sub) {
                     const int64_t ms = m0 + 128 * sub;

@@ -141,6 +141,10 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&f)[16]) {
 }
 
 __device__ __forceinline__ float silu_f(float v) { return v / (1.0f + __expf(-v)); }
+// GELU, tanh form (the approximation ggml_gelu evaluates)
+__device__ __forceinline__ float gelu_f(float v) {
+    return 0.5f * v * (1.0f + tanhf(0.7978845608028654f * (v + 0.044715f * v * v * v)));
+}
 
 __device__ __forceinline__ float load1(const void* p, uint32_t dt, int64_t i) {
     if (dt == S3DSP_F32) return reinterpret_cast<const float*>(p)[i];
@@ -289,6 +293,7 @@ __device__ __forceinline__ void writeout_generic(const P& p, const float* stage_
                     s2[q][j] += (double)v * v;
                 }
                 if (p.flags & S3DSP_EPI_SILU) v = silu_f(v);
+                if (p.flags & S3DSP_EPI_GELU) v = gelu_f(v);
                 store1(p.out, p.out_dtype, r * p.cout + col, v);
             }
         }

@@ -24,7 +24,7 @@ F32, BF16, F16 = 0, 1, 2
 PREC_F32_STRICT, PREC_BF16, PREC_F32_3XTF32 = 0, 1, 2
 LAYOUT_SLAT_ROW, LAYOUT_MESH_PACKED, LAYOUT_LINEAR, LAYOUT_SPCONV_1X1, LAYOUT_TRANSPOSED_2X2X2 = 0, 1, 2, 3, 4
 SENTINEL_SLAT_N, SENTINEL_MESH_NEG1 = 0, 1
-EPI_SILU, PRO_AFFINE_SILU, CONV_CTA_PAIR, CONV_TILE128, CONV_STREAM_K, CONV_STREAM_K128 = 1, 2, 4, 8, 16, 32
+EPI_SILU, PRO_AFFINE_SILU, CONV_CTA_PAIR, CONV_TILE128, CONV_STREAM_K, CONV_STREAM_K128, EPI_GELU = 1, 2, 4, 8, 16, 32, 64
 CONTEXT_DEFERRED_CHECKS = 1
 CONTEXT_OWN_STREAM = 2
 
@@ -33,7 +33,7 @@ EXPORTED = [
     "s3dsp_abi_version", "s3dsp_context_create", "s3dsp_context_free", "s3dsp_context_stream", "s3dsp_context_set_sm_limit",
     "s3dsp_context_check", "s3dsp_memory_stats", "s3dsp_device_alloc", "s3dsp_device_free", "s3dsp_copy_to_device",
     "s3dsp_copy_to_host", "s3dsp_hash_build", "s3dsp_hash_free", "s3dsp_hash_size",
-    "s3dsp_hash_lookup", "s3dsp_gs_window_tables", "s3dsp_ape", "s3dsp_flexicubes_tables_create",
+    "s3dsp_hash_lookup", "s3dsp_gs_window_tables", "s3dsp_ape", "s3dsp_gather_rows", "s3dsp_window_attention", "s3dsp_flexicubes_tables_create",
     "s3dsp_flexicubes_tables_free", "s3dsp_flexicubes_extract", "s3dsp_mesh_info", "s3dsp_mesh_device", "s3dsp_mesh_copy",
     "s3dsp_mesh_free", "s3dsp_gguf_open", "s3dsp_gguf_close", "s3dsp_gguf_n_tensors", "s3dsp_gguf_find",
     "s3dsp_gguf_tensor_info", "s3dsp_gguf_u32", "s3dsp_gguf_i32", "s3dsp_gguf_f32", "s3dsp_gguf_str",
@@ -98,6 +98,8 @@ def load(path: str = LIB_PATH):
         "s3dsp_gs_window_tables": (_u32, [_vp, _vp, _i64, _i32, _i32, _vp, _vp, _vp, _i64, ctypes.POINTER(_i64), _cp,
                                           _u64]),
         "s3dsp_ape": (_u32, [_vp, _vp, _i64, _i32, _vp, _cp, _u64]),
+        "s3dsp_gather_rows": (_u32, [_vp, _vp, _u32, _i64, _i64, _vp, _i64, _vp, _u32, _cp, _u64]),
+        "s3dsp_window_attention": (_u32, [_vp, _vp, _i64, _i64, _i32, _vp, _i64, _vp, _vp, _cp, _u64]),
         "s3dsp_flexicubes_tables_create": (_u32, [_vp, _vp, _vp, _vp, ctypes.POINTER(_vp), _cp, _u64]),
         "s3dsp_flexicubes_tables_free": (None, [_vp, _vp]),
         "s3dsp_flexicubes_extract": (_u32, [_vp, _vp, _vp, _vp, _i64, ctypes.POINTER(_vp), _cp, _u64]),
@@ -578,6 +580,17 @@ class Context:
     def halo_exchange(self, plan: ShardPlan, comm: int, x):
         """Fill x's ghost rows [n_own, n_own + n_ghost) from the peers (x on this device)."""
         _call(load().s3dsp_halo_exchange, self.handle, plan.handle, comm, ptr(x), x.shape[1], dtype_code(x))
+
+    def gather_rows(self, x, rows, y):
+        """y[i] = x[rows[i]] (rows: device int32 [len(y)]), with y's dtype."""
+        _call(load().s3dsp_gather_rows, self.handle, ptr(x), dtype_code(x), x.shape[0], x.shape[1], ptr(rows),
+              y.shape[0], ptr(y), dtype_code(y))
+
+    def window_attention(self, qkv, heads: int, windows, out, scatter=None):
+        """Swin window attention over qkv [n, 3c] f32 in bucket order; windows:
+        device int32 [nw, 2] (first row, rows); row i to out[scatter[i]]."""
+        _call(load().s3dsp_window_attention, self.handle, ptr(qkv), qkv.shape[0], qkv.shape[1] // 3, heads,
+              ptr(windows), windows.shape[0], ptr(scatter), ptr(out))
 
     # ---- FlexiCubes extraction ---------------------------------------------
     def flexicubes_tables(self, dmc, num_dual, check) -> FlexiCubesTables:
