@@ -86,6 +86,9 @@ typedef struct s3dsp_shard s3dsp_shard;
 #define S3DSP_CONV_STREAM_K UINT32_C(16) /* BF16: force 256-row tiles split evenly over all SMs
                                           (stream-K). No kernel flag: chosen by size, see s3dsp_conv_kernel */
 #define S3DSP_CONV_STREAM_K128 UINT32_C(32) /* BF16: force 128-row tiles split evenly over all SMs */
+#define S3DSP_CONV_SPLIT_PAIRS UINT32_C(128) /* BF16: force 256-row tiles, each on a CTA pair (a cluster of
+                                            2) that splits the kernel offsets and adds its two partial
+                                            sums in distributed shared memory */
 #define S3DSP_CONV_CTA_PAIR UINT32_C(4)  /* BF16: tcgen05 CTA pairs (256-row MMA over two tiles) instead of
                                           one CTA per 128-row tile; same results, slower on B200 today */
 

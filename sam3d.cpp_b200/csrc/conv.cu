@@ -7,31 +7,41 @@ using namespace s3dsp;
 namespace {
 
 // BF16 kernel choice by estimated time, in units of one wave of 128-row
-// tiles (every SM running one full tile). 128-row tiles: ceil(tiles / SMs)
-// waves. Stream-K (256-row tiles split evenly over the SMs): a fixed ~0.55
-// wave for the split-tile fix-up and pipeline refills, plus 1.525 / kvol of a
-// wave per (256-row tile, offset) unit and SM. Fitted to a B200 sweep of
-// 64^3..256^3 shells at C = 128 and 256 (15k-242k rows); a quarter-empty
-// second wave is where stream-K wins most (155 tiles: 2 waves vs ~1.35).
-// Maps with few offsets (linear layers) always use 128-row tiles.
-enum class Bf16Kernel { kTile128, kStreamK128, kStreamK256 };
+// tiles (every SM running one full tile; column blocks of 256 count as
+// tiles). 128-row tiles: ceil(tiles / SMs) waves. Stream-K (256-row tiles
+// split evenly over the SMs): a fixed ~0.55 wave for the split-tile fix-up
+// and pipeline refills, plus 1.525 / kvol of a wave per (256-row tile,
+// offset) unit and SM. Split-K pairs (one cluster of two CTAs per 256-row
+// tile, half the offsets each): 0.95 of a wave per wave of pairs. Fitted to
+// B200 sweeps of 32^3..256^3 shells at C = 64..1024 (2k-242k rows): pairs
+// win while the pairs fill one or two waves (config 2, 15k rows: 84 vs 88 us
+// for 128-row tiles), stream-K for wide layers and for a thin last wave
+// (155 tiles: 2 waves vs ~1.35). Maps with few offsets (linear layers)
+// always use 128-row tiles.
+enum class Bf16Kernel { kTile128, kStreamK128, kStreamK256, kSplit256 };
 
-Bf16Kernel pick_bf16_kernel(const s3dsp_context* ctx, int64_t n_out, int32_t kvol, uint32_t flags) {
+Bf16Kernel pick_bf16_kernel(const s3dsp_context* ctx, int64_t n_out, int32_t kvol, int64_t cout, uint32_t flags) {
     if (flags & (S3DSP_CONV_TILE128 | S3DSP_CONV_CTA_PAIR)) return Bf16Kernel::kTile128;
     if (flags & S3DSP_CONV_STREAM_K128) return Bf16Kernel::kStreamK128;
     if (flags & S3DSP_CONV_STREAM_K) return Bf16Kernel::kStreamK256;
+    if (flags & S3DSP_CONV_SPLIT_PAIRS) return Bf16Kernel::kSplit256;
     if (kvol < 8) return Bf16Kernel::kTile128;
-    const double sms = (double)ctx->sm_count;
-    const int64_t tiles = (n_out + 127) / 128;
-    const double waves128 = (double)((tiles + ctx->sm_count - 1) / ctx->sm_count);
-    const double units = (double)((n_out + 255) / 256) * kvol;
-    const double est_sk = 0.55 + (units / sms) * 1.525 / kvol;
+    const int64_t sm = ctx->sm_count;
+    const int64_t nnb = ((cout + 15) / 16 * 16) / tc_pick_bn((int)cout);  // column blocks
+    const int64_t tiles = (n_out + 127) / 128 * nnb;
+    const int64_t work = (n_out + 255) / 256 * nnb;  // 256-row work tiles
+    const double waves128 = (double)((tiles + sm - 1) / sm);
+    const double est_sk = 0.55 + ((double)(work * kvol) / (double)sm) * 1.525 / kvol;
+    const double est_pairs = 0.95 * (double)((2 * work + sm - 1) / sm);
+    if (est_pairs <= est_sk && est_pairs < waves128) return Bf16Kernel::kSplit256;
     return est_sk < 0.95 * waves128 ? Bf16Kernel::kStreamK256 : Bf16Kernel::kTile128;
 }
 
 const char* bf16_kernel_name(Bf16Kernel k) {
-    return k == Bf16Kernel::kTile128 ? "conv_tc_kernel" : k == Bf16Kernel::kStreamK128 ? "conv_sk_kernel<128>"
-                                                                                        : "conv_sk_kernel<256>";
+    return k == Bf16Kernel::kTile128      ? "conv_tc_kernel"
+           : k == Bf16Kernel::kStreamK128 ? "conv_sk_kernel<128>"
+           : k == Bf16Kernel::kSplit256   ? "conv_sk_kernel<256>:pairs"
+                                          : "conv_sk_kernel<256>";
 }
 
 }  // namespace
@@ -39,12 +49,12 @@ const char* bf16_kernel_name(Bf16Kernel k) {
 extern "C" S3DSP_API const char* s3dsp_conv_kernel(const s3dsp_context* ctx, int64_t n_out, int32_t kvol, int64_t cin,
                                                    int64_t cout, uint32_t precision, uint32_t flags) {
     (void)cin;
-    (void)cout;
     if (!ctx) return nullptr;
     if (precision == S3DSP_PREC_F32_STRICT) return "conv_f32_kernel";
     if (precision == S3DSP_PREC_F32_3XTF32) return "conv_tc_kernel<tf32x3>";
     if (precision != S3DSP_PREC_BF16) return nullptr;
-    return bf16_kernel_name(pick_bf16_kernel(ctx, n_out, kvol, flags));
+    if (cout <= 0) return nullptr;
+    return bf16_kernel_name(pick_bf16_kernel(ctx, n_out, kvol, cout, flags));
 }
 
 namespace {
@@ -118,7 +128,7 @@ s3d_status conv_impl(s3dsp_context* ctx, const s3dsp_kmap* kmap, int32_t kvol, u
             return fail(error, error_capacity, S3D_INVALID_ARGUMENT,
                         "BF16 needs cin %% 8 == 0 (each source) and 16-byte aligned in/weight/out/residual");
         s3d_status st = S3D_OK;
-        const Bf16Kernel kern = pick_bf16_kernel(ctx, n_out, kvol, flags);
+        const Bf16Kernel kern = pick_bf16_kernel(ctx, n_out, kvol, cout, flags);
         if (kern == Bf16Kernel::kTile128)
             e = launch_conv_tc(ctx, kmap, kvol, (const __nv_bfloat16*)in, (const __nv_bfloat16*)in_b, ca, n_in,
                                (int)cin, in_shift, (const __nv_bfloat16*)weight, bias, residual, res_dtype, res_shift,
@@ -128,7 +138,8 @@ s3d_status conv_impl(s3dsp_context* ctx, const s3dsp_kmap* kmap, int32_t kvol, u
             e = launch_conv_sk(ctx, kmap, kvol, (const __nv_bfloat16*)in, (const __nv_bfloat16*)in_b, ca, n_in,
                                (int)cin, in_shift, (const __nv_bfloat16*)weight, bias, residual, res_dtype, res_shift,
                                out, out_dtype, n_out, (int)cout, flags, gn_partials, gn_groups,
-                               kern == Bf16Kernel::kStreamK128 ? 128 : 256, error, error_capacity, &st);
+                               kern == Bf16Kernel::kStreamK128 ? 128 : 256, kern == Bf16Kernel::kSplit256 ? 2 : 1,
+                               error, error_capacity, &st);
         if (st != S3D_OK) return st;
         if (e != cudaSuccess) return cuda_fail(error, error_capacity, e, bf16_kernel_name(kern));
         return S3D_OK;

@@ -81,6 +81,8 @@ struct SkParams {
     int nnb;                    // column blocks per 256-row tile
     int64_t units;              // work tiles x kvol
     int grid;
+    int csplit;                 // 2: split-K over CTA pairs (clusters of 2, kRows = 256); 1: stream-K
+    int gn_store;               // one column block: GroupNorm partials stored, not added onto zeroed slots
     float* ws;                  // [2 * grid][rows / 128][bn / 16][4][128] float4 raw accumulators, or null
     uint32_t* counters;         // [work tiles] pieces arrived, zeroed before launch
     int cout;
@@ -107,6 +109,9 @@ __device__ __forceinline__ int64_t ws_slot(const SkParams& p, int i, int64_t wt)
 }
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
 
+// the area after the staged f32 tile: per-warp GroupNorm column sums (f64 pairs)
+__host__ __device__ constexpr size_t colsum_bytes(int bn) { return (size_t)kProdWarps * bn * 16; }
+
 
 
 // kRows = 256: two 128-row accumulators per work tile; 128: one. kTwo: the
@@ -126,7 +131,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
     // layout: region0 = max(ring A | ring B, epilogue tile | GN column sums),
     // then barriers, tmem holder, flags
     const size_t ring = (size_t)S * (kAStage + bstage);
-    const size_t epi = (size_t)128 * ostride * 4 + (size_t)kProdWarps * p.bn * 16;
+    const size_t epi = (size_t)128 * ostride * 4 + colsum_bytes(p.bn);
     uint8_t* sA = smem;
     uint8_t* sB = smem + (size_t)S * kAStage;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + (ring > epi ? ring : epi));
@@ -164,11 +169,16 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
 
     uint32_t it = 0;      // pipeline step counter, identical in every role
     uint32_t acc_ph = 0;  // accum barrier phase
-    const int64_t u_end = unit_begin(p, me + 1);
-    for (int64_t u = unit_begin(p, me); u < u_end;) {
-        const int64_t wt = u / p.kvol;
-        const int64_t seg_end = min(u_end, (wt + 1) * p.kvol);
-        const int ob = (int)(u - wt * p.kvol), oe = (int)(seg_end - wt * p.kvol);
+    // split-K pairs: the CTA pair (a cluster of 2) shares work tile me / 2, one
+    // segment each; rank r keeps its half of the tile's kernel offsets and
+    // finishes accumulator r (rows 128 r ..) with the peer's part added in
+    const bool csp = kRows == 256 && p.csplit == 2;
+    const uint32_t crank = csp ? cluster_rank() : 0u;
+    const int64_t u_end = csp ? 1 : unit_begin(p, me + 1);
+    for (int64_t u = csp ? 0 : unit_begin(p, me); u < u_end;) {
+        const int64_t wt = csp ? (int64_t)(me >> 1) : u / p.kvol;
+        const int64_t seg_end = csp ? 1 : min(u_end, (wt + 1) * p.kvol);
+        const int ob = csp ? 0 : (int)(u - wt * p.kvol), oe = csp ? p.kvol : (int)(seg_end - wt * p.kvol);
         u = seg_end;
         const int64_t st = wt / p.nnb;
         const int n0 = (int)(wt - st * p.nnb) * p.bn;
@@ -185,6 +195,15 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
             }
         }
         mask &= (oe >= 32 ? 0xffffffffu : ((1u << oe) - 1u)) & ~((1u << ob) - 1u);
+        if (csp) {
+            // rank 0: the first ceil(m / 2) active offsets, rank 1: the rest
+            uint32_t lo = 0u, rest = mask;
+            for (int q = (__popc(mask) + 1) / 2; q > 0; --q) {
+                lo |= rest & (0u - rest);
+                rest &= rest - 1u;
+            }
+            mask = crank ? (mask & ~lo) : lo;
+        }
         const int T = __popc(mask) * p.kchunks;
 
         bool prod_ok = true;
@@ -306,30 +325,72 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
             // them into L2 while the last MMAs finish
             const int esz = p.res_dtype == S3DSP_F32 ? 4 : 2;
             constexpr int kTpr = kEpiThreads / kRows;  // threads per row
-            const int64_t r = m0 + tid / kTpr;
+            // split-K pairs: only the rows this CTA finishes, two threads each
+            const int64_t r = csp ? m0 + 128 * (int64_t)crank + (tid >> 2) : m0 + tid / kTpr;
             const int len = min(p.bn, p.cout - n0) * esz;
             if (r < p.n_out) {
                 const char* row = static_cast<const char*>(p.residual) +
                                   (((r >> p.res_shift) * p.cout + n0) * (int64_t)esz);
-                for (int b = (tid % kTpr) * 128; b < len; b += kTpr * 128)
+                const int tpr = csp ? 4 : kTpr;
+                for (int b = (tid % tpr) * 128; b < len; b += tpr * 128)
                     asm volatile("prefetch.global.L2 [%0];" ::"l"(row + b));
             }
         }
 
-        if (warp < kProdWarps) {
-            // ============ epilogue (warps 0-15) ============
-            bool have_acc = false;
-            if (T > 0) {
-                have_acc = prod_ok && mbar_wait(smem_u32(accum), acc_ph, abort_flag, p.status);
-                have_acc = __all_sync(0xffffffffu, have_acc);
+        // ============ epilogue (warps 0-15) ============
+        const int lq = warp & 3;                  // TMEM lane quarter (rows 32*lq ..)
+        const int row = 32 * lq + lane;           // accumulator row of this thread
+        const uint32_t tl = tmem + ((uint32_t)(32 * lq) << 16);
+        const int nch = p.bn / 16;                // 16-column chunks
+        bool have_acc = false;
+        if (warp < kProdWarps && T > 0) {
+            have_acc = prod_ok && mbar_wait(smem_u32(accum), acc_ph, abort_flag, p.status);
+            have_acc = __all_sync(0xffffffffu, have_acc);
+        }
+        if (csp) {
+            // split-K pairs, every thread of both CTAs at the cluster barriers:
+            // (1) once both rings are drained (the MMAs that read them completed
+            // before `accum`), accumulator `crank ^ 1` goes into the peer's staged
+            // f32 tile by 16-byte distributed-shared-memory stores; (2) each CTA
+            // adds its own accumulator `crank` to what it received: one add per
+            // element, own + peer, so the result is the same on every run.
+            // (Remote f32 atomic adds measured ~100 us per tile; a receive buffer
+            // taking the columns in two halves, 5 cluster barriers, ~9 us.)
+            cluster_sync();
+            if (warp < kProdWarps) {
+                tc_fence_after();
+                const uint32_t peer = map_to_rank(smem_u32(stage_out), crank ^ 1u);
+                for (int c = warp >> 2; c < nch; c += 4) {
+                    float f[16];
+#pragma unroll
+                    for (int q = 0; q < 16; ++q) f[q] = 0.f;
+                    if (have_acc) tmem_ld16(tl + (crank ^ 1u) * p.thalf + 16 * c, f);
+                    const uint32_t a = peer + (uint32_t)(row * ostride + 16 * c) * 4u;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        st_cluster_v4(a + 16u * q, f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
+                }
             }
+            cluster_sync();
+            if (warp < kProdWarps && have_acc) {
+                for (int c = warp >> 2; c < nch; c += 4) {
+                    float f[16];
+                    tmem_ld16(tl + crank * p.thalf + 16 * c, f);
+                    float4* dst = reinterpret_cast<float4*>(stage_out + (size_t)row * ostride + 16 * c);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        float4 a = dst[q];
+                        a.x += f[4 * q], a.y += f[4 * q + 1], a.z += f[4 * q + 2], a.w += f[4 * q + 3];
+                        dst[q] = a;
+                    }
+                }
+            }
+            // the write-out's barrier after phase 1 orders these adds before it reads the tile
+        }
+        if (warp < kProdWarps) {
             tc_fence_after();
-            const int lq = warp & 3;                  // TMEM lane quarter (rows 32*lq ..)
-            const int row = 32 * lq + lane;           // accumulator row of this thread
-            const uint32_t tl = tmem + ((uint32_t)(32 * lq) << 16);
-            const int nch = p.bn / 16;                // 16-column chunks
             const int64_t tb = wt * p.kvol;
-            const int i_first = cta_of(p, tb), i_last = cta_of(p, tb + p.kvol - 1);
+            const int i_first = csp ? me : cta_of(p, tb), i_last = csp ? me : cta_of(p, tb + p.kvol - 1);
             const int k = i_last - i_first + 1;
             // piece pc > 0 starts inside this tile (its first tile: slot 2i); piece 0
             // may have started in an earlier tile (then this is its last: slot 2i+1)
@@ -382,11 +443,12 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
                 const int silu_k = (p.flags & S3DSP_EPI_SILU) ? 1 : 0;
                 const int sel = (out_k < 0 || res_k < 0 || (p.flags & S3DSP_EPI_GELU)) ? -1 : ((out_k * 3 + res_k) * 2 + silu_k) * 2 + (stats ? 1 : 0);
                 const uint32_t so_base = smem_u32(stage_out);
-                for (int sub = 0; sub < kSub; ++sub) {
+                for (int sub = csp ? (int)crank : 0; sub < (csp ? (int)crank + 1 : kSub); ++sub) {
                     const int64_t ms = m0 + 128 * sub;
                     if (ms >= p.n_out) break;
                     // phase 1: accumulator (TMEM, or the pieces summed in piece order) -> smem tile
-                    for (int c = warp >> 2; c < nch; c += 4) {
+                    // (split-K pairs: staged already)
+                    for (int c = warp >> 2; c < (csp ? 0 : nch); c += 4) {
                         float f[16];
 #pragma unroll
                         for (int q = 0; q < 16; ++q) f[q] = 0.f;
@@ -463,38 +525,13 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
                                              stats ? colw : nullptr);
                     }
                     if (stats) {
-                        // deterministic GroupNorm partials of the 128-row tile: the write-out
-                        // left per-warp column sums; each group summed over warps, columns in order
+                        // deterministic GroupNorm partials of the 128-row tile from the
+                        // write-out's per-warp column sums
                         epi_bar();
                         const int64_t t128 = kSub * st + sub;
-                        const int g_lo = n0 / gs;
-                        const int g_hi = min(p.gn_groups - 1, (n0 + limit - 1) / gs);
-                        // 16 lanes per group (lane w: warp w's columns), fixed shuffle tree
-                        const int items = (g_hi - g_lo + 1) * kProdWarps;
-                        for (int base = 0; base < items; base += kEpiThreads) {  // warp-uniform
-                            const int idx = base + tid;
-                            const int g = g_lo + idx / kProdWarps, w = idx % kProdWarps;
-                            const bool act = idx < items;
-                            double a = 0.0, b = 0.0;
-                            if (act) {
-                                const int c_lo = max(g * gs - n0, 0), c_hi = min((g + 1) * gs - n0, limit);
-                                for (int c = c_lo; c < c_hi; ++c) {
-                                    a += colp[((size_t)w * p.bn + c) * 2 + 0];
-                                    b += colp[((size_t)w * p.bn + c) * 2 + 1];
-                                }
-                            }
-#pragma unroll
-                            for (int off = kProdWarps / 2; off > 0; off >>= 1) {
-                                a += __shfl_down_sync(0xffffffffu, a, off, kProdWarps);
-                                b += __shfl_down_sync(0xffffffffu, b, off, kProdWarps);
-                            }
-                            // a group split across two column blocks gets exactly two adds
-                            // onto a zeroed slot, which is order independent
-                            if (act && w == 0) {
-                                atomicAdd(p.gn_partials + (t128 * p.gn_groups + g) * 2 + 0, a);
-                                atomicAdd(p.gn_partials + (t128 * p.gn_groups + g) * 2 + 1, b);
-                            }
-                        }
+                        gn_tile_partials<kProdWarps, kEpiThreads>(colp, p.bn, n0, limit, gs, p.gn_groups, tid,
+                                                                  p.gn_partials + t128 * p.gn_groups * 2,
+                                                                  p.gn_store != 0, epi_bar);
                     }
                     epi_bar();  // the tile and column sums are reused by the next subtile
                 }
@@ -519,7 +556,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
 
 size_t sk_smem_bytes(int stages, int bn, int rows) {
     const size_t ring = (size_t)stages * ((size_t)rows * 2 * kKC + (size_t)bn * 2 * kKC);
-    const size_t epi = (size_t)128 * (bn + 4) * 4 + (size_t)kProdWarps * bn * 16;
+    const size_t epi = (size_t)128 * (bn + 4) * 4 + colsum_bytes(bn);
     return 1024 /*align slack*/ + (ring > epi ? ring : epi) + (2 * stages + 1) * 8 + 16;
 }
 
@@ -527,17 +564,15 @@ size_t sk_smem_bytes(int stages, int bn, int rows) {
 
 namespace s3dsp {
 
-int tc_pick_bn(int cout);
-
 cudaError_t launch_conv_sk(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol, const __nv_bfloat16* in,
                            const __nv_bfloat16* in_b, int cin_a, int64_t n_in, int cin, int in_shift, const __nv_bfloat16* w, const float* bias,
                            const void* residual, uint32_t res_dtype, int res_shift, void* out, uint32_t out_dtype,
                            int64_t n_out, int cout, uint32_t flags, double* gn_partials, int gn_groups, int rows,
-                           char* error, uint64_t error_capacity, s3d_status* st) {
+                           int csplit, char* error, uint64_t error_capacity, s3d_status* st) {
     *st = S3D_OK;
     (void)n_in;
-    if (rows != 128 && rows != 256) {
-        *st = fail(error, error_capacity, S3D_INTERNAL_ERROR, "stream-K tile rows %d", rows);
+    if ((rows != 128 && rows != 256) || (csplit != 1 && csplit != 2) || (csplit == 2 && rows != 256)) {
+        *st = fail(error, error_capacity, S3D_INTERNAL_ERROR, "stream-K tile rows %d, split %d", rows, csplit);
         return cudaErrorInvalidValue;
     }
     const int cout_pad = (cout + 15) / 16 * 16;
@@ -561,9 +596,17 @@ cudaError_t launch_conv_sk(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     int64_t g = (units + min_units - 1) / min_units;
     if (g > ctx->sm_count) g = ctx->sm_count;
     if (g < 1) g = 1;
+    if (csplit == 2) {
+        // one CTA pair per work tile (the grid may exceed the SM count: pairs then run in waves)
+        if (work_tiles > 0x3fffffff) {
+            *st = fail(error, error_capacity, S3D_INVALID_ARGUMENT, "too many work tiles for split-K pairs");
+            return cudaErrorInvalidValue;
+        }
+        g = 2 * work_tiles;
+    }
     const int grid = (int)g;
     bool split = false;
-    for (int i = 1; i < grid && !split; ++i) split = ((int64_t)i * units / grid) % kvol != 0;
+    for (int i = 1; i < grid && !split && csplit == 1; ++i) split = ((int64_t)i * units / grid) % kvol != 0;
 
     auto encode = get_encode_fn();
     if (!encode) {
@@ -617,6 +660,8 @@ cudaError_t launch_conv_sk(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     p.nnb = nnb;
     p.units = units;
     p.grid = grid;
+    p.csplit = csplit;
+    p.gn_store = nnb == 1;
     p.ws = nullptr;
     p.counters = nullptr;
     p.cout = cout;
@@ -633,7 +678,7 @@ cudaError_t launch_conv_sk(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     cudaError_t e = smem_optin((const void*)kernel, ctx->device,
                                rows == 256 ? (two ? optin256_two : optin256) : (two ? optin128_two : optin128));
     if (e != cudaSuccess) return e;
-    if (gn_partials) {
+    if (gn_partials && !p.gn_store) {
         e = cudaMemsetAsync(gn_partials, 0, sizeof(double) * 2 * (size_t)gn_groups * (size_t)tiles, s);
         if (e != cudaSuccess) return e;
     }
@@ -652,7 +697,26 @@ cudaError_t launch_conv_sk(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
         p.ws = static_cast<float*>(ws);
         p.counters = static_cast<uint32_t*>(counters);
     }
-    launch_pdl(kernel, dim3(grid), dim3(kThreads), smem, s, p, wmap);
+    if (csplit == 2) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)grid);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[2];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 2;
+        e = cudaLaunchKernelEx(&cfg, kernel, p, wmap);
+        if (e != cudaSuccess) return e;
+    } else {
+        launch_pdl(kernel, dim3(grid), dim3(kThreads), smem, s, p, wmap);
+    }
     e = cudaGetLastError();
     if (ws) cudaFreeAsync(ws, s);
     if (counters) cudaFreeAsync(counters, s);

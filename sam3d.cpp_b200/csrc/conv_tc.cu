@@ -103,21 +103,7 @@ struct TcParams {
 // named barrier of the 16 gather/epilogue warps
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
 
-// --- CTA-pair (cluster of 2) helpers ---
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-// shared::cluster address of the same smem variable in CTA `rank` of the cluster
-__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
-    uint32_t out;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(addr), "r"(rank));
-    return out;
-}
-__device__ __forceinline__ void cluster_sync() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
+// --- CTA-pair (cluster of 2) helpers (cluster_rank, map_to_rank, cluster_sync: tc_common.cuh) ---
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
@@ -579,46 +565,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             default:
                 writeout_generic(p, stage_out, ostride, lane_base, lane, m0, n0, limit, nrows, bias4, stats ? colw : nullptr);
         }
-        if (stats) {
-            // deterministic GroupNorm partials: per-warp column sums to smem;
-            // 16 lanes per group, lane w summing warp w's columns of the group,
-            // then a fixed shuffle tree over the 16 warps
+        // deterministic GroupNorm partials of the tile from the write-out's
+        // per-warp column sums (the padding CTA of an odd pair count, tile ==
+        // n_tiles, has no rows and no slot)
+        if (stats && tile < p.n_tiles) {
             epi_bar();
-            const int g_lo = n0 / gs;
-            const int g_hi = min(p.gn_groups - 1, (n0 + limit - 1) / gs);
-            const int items = (g_hi - g_lo + 1) * kProdWarps;
-            // warp-uniform trip count: every lane of a warp takes part in the shuffles
-            for (int base = 0; base < items; base += kProdWarps * 32) {
-                const int idx = base + tid;
-                const int g = g_lo + idx / kProdWarps, w = idx % kProdWarps;
-                // the padding CTA of an odd pair count (tile == n_tiles) has no rows and no slot
-                const bool act = tile < p.n_tiles && idx < items;
-                double a = 0.0, b = 0.0;
-                if (act) {
-                    const int c_lo = max(g * gs - n0, 0), c_hi = min((g + 1) * gs - n0, limit);
-                    for (int c = c_lo; c < c_hi; ++c) {
-                        a += colp[((size_t)w * p.bn + c) * 2 + 0];
-                        b += colp[((size_t)w * p.bn + c) * 2 + 1];
-                    }
-                }
-#pragma unroll
-                for (int off = kProdWarps / 2; off > 0; off >>= 1) {
-                    a += __shfl_down_sync(0xffffffffu, a, off, kProdWarps);
-                    b += __shfl_down_sync(0xffffffffu, b, off, kProdWarps);
-                }
-                if (act && w == 0) {
-                    double* slot = p.gn_partials + ((int64_t)tile * p.gn_groups + g) * 2;
-                    if (p.gn_store) {
-                        slot[0] = a;
-                        slot[1] = b;
-                    } else {
-                        // a group split across two column tiles gets exactly two
-                        // adds onto a zeroed slot, which is order independent
-                        atomicAdd(slot + 0, a);
-                        atomicAdd(slot + 1, b);
-                    }
-                }
-            }
+            gn_tile_partials<kProdWarps, kProdWarps * 32>(colp, p.bn, n0, limit, gs, p.gn_groups, tid,
+                                                          p.gn_partials + (int64_t)tile * p.gn_groups * 2,
+                                                          p.gn_store != 0, epi_bar);
         }
         tc_fence_before();
     }

@@ -191,12 +191,16 @@ cudaError_t launch_conv_tf32x3(s3dsp_context* ctx, const s3dsp_kmap* kmap, int k
                                char* error, uint64_t error_capacity, s3d_status* st);
 // x -> (TF32 high part, f32 remainder), n elements, on ctx's stream
 cudaError_t split_tf32(s3dsp_context* ctx, const float* x, int64_t n, float* hi, float* lo);
-// rows: 128 or 256 output rows per stream-K work tile
+// output columns per tensor-core tile for a layer of `cout` channels
+int tc_pick_bn(int cout);
+// rows: 128 or 256 output rows per stream-K work tile; csplit 2: one CTA pair
+// (a cluster of 2) per 256-row work tile, the kernel offsets split between them
 cudaError_t launch_conv_sk(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
                            const __nv_bfloat16* in, const __nv_bfloat16* in_b, int cin_a, int64_t n_in, int cin,
                            int in_shift, const __nv_bfloat16* w, const float* bias, const void* residual,
                            uint32_t res_dtype, int res_shift, void* out, uint32_t out_dtype,
                            int64_t n_out, int cout, uint32_t flags, double* gn_partials,
-                           int gn_groups, int rows, char* error, uint64_t error_capacity, s3d_status* st);
+                           int gn_groups, int rows, int csplit, char* error, uint64_t error_capacity,
+                           s3d_status* st);
 
 }  // namespace s3dsp

@@ -26,6 +26,27 @@ __device__ __forceinline__ unsigned long long global_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
+// --- clusters: rank, peer shared-memory addresses, the all-thread cluster barrier ---
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// shared::cluster address of the same smem variable in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
+    uint32_t out;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(addr), "r"(rank));
+    return out;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// 16-byte store into shared memory of a CTA of the cluster (address from map_to_rank)
+__device__ __forceinline__ void st_cluster_v4(uint32_t cluster_addr, float a, float b, float c, float d) {
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "f"(a), "f"(b), "f"(c),
+                 "f"(d)
+                 : "memory");
+}
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
 }
@@ -205,6 +226,52 @@ __device__ __forceinline__ void store_colsums(double* colw, int bn, int lane, in
                 colw[lc * 2 + 1] = lc < limit ? s2[q][j] : 0.0;
             }
         }
+}
+
+// GroupNorm partial sums (sum, sum of squares) of one 128-row tile from the
+// per-warp column sums colp[kWarps][bn] (f64 pairs, left by the write-out):
+// pass 1, one thread per column, sums that column over the warps in warp
+// order and leaves the total in warp 0's row (each column is read and
+// written by its own thread only); after `bar`, pass 2, one thread per
+// group, sums the group's columns in column order into its slot. Fixed
+// orders: the same result on every run. `store`: the column block holds
+// whole groups, the slot is written; else a group split across two column
+// blocks gets exactly two adds onto a zeroed slot (order independent).
+// Lanes read consecutive 16-byte pairs in pass 1 (no bank conflicts).
+template <int kWarps, int kThreads, typename Bar>
+__device__ __forceinline__ void gn_tile_partials(double* colp, int bn, int n0, int limit, int gs, int groups, int tid,
+                                                 double* slots, bool store, Bar bar) {
+    double2* col2 = reinterpret_cast<double2*>(colp);
+    for (int c = tid; c < limit; c += kThreads) {
+        double a = 0.0, b = 0.0;
+#pragma unroll 4
+        for (int w = 0; w < kWarps; ++w) {
+            const double2 v = col2[(size_t)w * bn + c];
+            a += v.x;
+            b += v.y;
+        }
+        col2[c] = make_double2(a, b);
+    }
+    bar();
+    const int g_lo = n0 / gs;
+    const int g_hi = min(groups - 1, (n0 + limit - 1) / gs);
+    for (int g = g_lo + tid; g <= g_hi; g += kThreads) {
+        const int c_lo = max(g * gs - n0, 0), c_hi = min((g + 1) * gs - n0, limit);
+        double a = 0.0, b = 0.0;
+        for (int c = c_lo; c < c_hi; ++c) {
+            const double2 v = col2[c];
+            a += v.x;
+            b += v.y;
+        }
+        double* slot = slots + (size_t)g * 2;
+        if (store) {
+            slot[0] = a;
+            slot[1] = b;
+        } else {
+            atomicAdd(slot + 0, a);
+            atomicAdd(slot + 1, b);
+        }
+    }
 }
 
 // Rows lane_base .. lane_base+nrows-1 of the staged f32 tile -> global, four

@@ -25,6 +25,7 @@ PREC_F32_STRICT, PREC_BF16, PREC_F32_3XTF32 = 0, 1, 2
 LAYOUT_SLAT_ROW, LAYOUT_MESH_PACKED, LAYOUT_LINEAR, LAYOUT_SPCONV_1X1, LAYOUT_TRANSPOSED_2X2X2 = 0, 1, 2, 3, 4
 SENTINEL_SLAT_N, SENTINEL_MESH_NEG1 = 0, 1
 EPI_SILU, PRO_AFFINE_SILU, CONV_CTA_PAIR, CONV_TILE128, CONV_STREAM_K, CONV_STREAM_K128, EPI_GELU = 1, 2, 4, 8, 16, 32, 64
+CONV_SPLIT_PAIRS = 128
 CONTEXT_DEFERRED_CHECKS = 1
 CONTEXT_OWN_STREAM = 2
 

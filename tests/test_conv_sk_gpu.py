@@ -1,8 +1,11 @@
 """BF16 conv, stream-K kernel (256-row tiles split evenly over the
-SMs, pieces of a split tile summed in a fixed order): against the 128-row
-kernel and the oracle, over split and unsplit tiles, several column blocks,
-ragged row counts, subdivide gathers and every epilogue option. Each launch is
-repeated: results must be bit-identical from run to run."""
+SMs, pieces of a split tile summed in a fixed order) and its split-K pair
+form (one cluster of two CTAs per 256-row tile, the kernel offsets split
+between them, the two partial sums added in distributed shared memory):
+against the 128-row kernel and the oracle, over split and unsplit tiles,
+several column blocks, ragged row counts, subdivide gathers and every epilogue
+option. Each launch is repeated: results must be bit-identical from run to
+run."""
 import numpy as np
 import pytest
 import torch
@@ -66,7 +69,8 @@ def same(a, b):
     return np.array_equal(a, b)
 
 
-SK_FLAGS = [s3dsp.CONV_STREAM_K, s3dsp.CONV_STREAM_K128]  # 256- and 128-row work tiles
+# 256- and 128-row work tiles; 256-row tiles on CTA pairs
+SK_FLAGS = [s3dsp.CONV_STREAM_K, s3dsp.CONV_STREAM_K128, s3dsp.CONV_SPLIT_PAIRS]
 
 
 @pytest.mark.parametrize("skflag", SK_FLAGS)
@@ -138,15 +142,17 @@ def test_sk_epilogue_gn_and_subdivide(ctx, out_dtype, res_dtype, silu, skflag):
     assert rel_l2(sk[0][0], ref) < 1e-2
 
 
+@pytest.mark.parametrize("skflag", [s3dsp.CONV_STREAM_K, s3dsp.CONV_SPLIT_PAIRS])
 @pytest.mark.parametrize("n", [1, 255, 256, 257, 3 * 256 + 17, 40000])
-def test_sk_identity_linear(ctx, n):
+def test_sk_identity_linear(ctx, n, skflag):
     cin, cout = 256, 128
     x = workloads.normal((n, cin), 50)
     w = workloads.normal((cout, cin), 51, 0.05)
     b = workloads.normal((cout,), 52, 0.1)
     wp = pack(ctx, w, s3dsp.LAYOUT_LINEAR, 1, cin, cout)
     xb = dev(x).to(torch.bfloat16)
-    sk = run(ctx, None, 1, xb, wp, dev(b), cout, n, out_dtype=torch.bfloat16, reps=2)
+    # CTA pairs: rank 0 takes the one offset, rank 1 none (adds nothing)
+    sk = run(ctx, None, 1, xb, wp, dev(b), cout, n, flags=skflag, out_dtype=torch.bfloat16, reps=2)
     t128 = run(ctx, None, 1, xb, wp, dev(b), cout, n, flags=s3dsp.CONV_TILE128, out_dtype=torch.bfloat16, reps=1)
     assert np.array_equal(sk[0], sk[1])
     assert np.array_equal(sk[0], t128[0])  # whole tiles, same MMA order: bit-identical
@@ -156,11 +162,17 @@ def test_sk_identity_linear(ctx, n):
 def test_kernel_choice(ctx):
     P = s3dsp.PREC_BF16
     sms = torch.cuda.get_device_properties(0).multi_processor_count
-    assert ctx.conv_kernel(128 * sms - 5, 27, 256, 256, P) == "conv_tc_kernel"   # one full wave
+    pairs = "conv_sk_kernel<256>:pairs"
+    assert ctx.conv_kernel(15159, 27, 256, 256, P) == pairs   # config 2: 60 pairs, one wave
+    assert ctx.conv_kernel(128 * sms - 5, 27, 256, 256, P) == pairs  # 74 pairs: still one wave
+    assert ctx.conv_kernel(34060, 27, 256, 256, P) == pairs   # two waves of pairs
+    assert ctx.conv_kernel(3815, 27, 512, 512, P) == "conv_sk_kernel<256>"  # wide: stream-K
+    assert ctx.conv_kernel(2153, 27, 1024, 1024, P) == "conv_sk_kernel<256>"
     assert ctx.conv_kernel(128 * sms + 900, 27, 256, 256, P) == "conv_sk_kernel<256>"  # a thin second wave
     assert ctx.conv_kernel(128 * 8 * sms, 27, 256, 256, P) == "conv_sk_kernel<256>"
     assert ctx.conv_kernel(128 * 8 * sms, 1, 256, 256, P) == "conv_tc_kernel"     # linear layers
     assert ctx.conv_kernel(1000, 27, 256, 256, P, s3dsp.CONV_STREAM_K) == "conv_sk_kernel<256>"
     assert ctx.conv_kernel(1000, 27, 256, 256, P, s3dsp.CONV_STREAM_K128) == "conv_sk_kernel<128>"
+    assert ctx.conv_kernel(1000, 27, 256, 256, P, s3dsp.CONV_SPLIT_PAIRS) == "conv_sk_kernel<256>:pairs"
     assert ctx.conv_kernel(128 * 3 * sms, 27, 256, 256, P, s3dsp.CONV_TILE128) == "conv_tc_kernel"
     assert ctx.conv_kernel(1000, 27, 256, 256, s3dsp.PREC_F32_STRICT) == "conv_f32_kernel"
