@@ -109,8 +109,14 @@ __device__ __forceinline__ int64_t ws_slot(const SkParams& p, int i, int64_t wt)
 }
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
 
-// the area after the staged f32 tile: per-warp GroupNorm column sums (f64 pairs)
-__host__ __device__ constexpr size_t colsum_bytes(int bn) { return (size_t)kProdWarps * bn * 16; }
+// the area after the staged f32 tile: per-warp GroupNorm column sums (f64 pairs),
+// or, for split-K pairs, the staging area of the larger half of the columns
+// (128 rows of 4 float4s per 16-column chunk, plus one float4 of padding)
+__host__ __device__ constexpr size_t colsum_bytes(int bn) {
+    const size_t sums = (size_t)kProdWarps * bn * 16;
+    const size_t stage = (size_t)128 * (4 * ((bn / 16 + 1) / 2) + 1) * 16;
+    return sums > stage ? sums : stage;
+}
 
 
 
@@ -195,16 +201,22 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
             }
         }
         mask &= (oe >= 32 ? 0xffffffffu : ((1u << oe) - 1u)) & ~((1u << ob) - 1u);
+        // this CTA's reduction steps: T steps of kKC channels, starting at
+        // chunk kc0 of the first offset left in `mask`
+        int T = __popc(mask) * p.kchunks;
+        int kc0 = 0;
         if (csp) {
-            // rank 0: the first ceil(m / 2) active offsets, rank 1: the rest
-            uint32_t lo = 0u, rest = mask;
-            for (int q = (__popc(mask) + 1) / 2; q > 0; --q) {
-                lo |= rest & (0u - rest);
-                rest &= rest - 1u;
+            // rank 0: the first ceil(steps / 2) steps of the tile's offsets,
+            // rank 1: the rest (it may start inside an offset)
+            const int half = (T + 1) / 2;
+            if (crank) {
+                for (int q = half / p.kchunks; q > 0; --q) mask &= mask - 1u;
+                kc0 = half % p.kchunks;
+                T -= half;
+            } else {
+                T = half;
             }
-            mask = crank ? (mask & ~lo) : lo;
         }
-        const int T = __popc(mask) * p.kchunks;
 
         bool prod_ok = true;
         if (warp < kProdWarps) {
@@ -234,8 +246,8 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
                 const uint32_t pit = it + (uint32_t)j;
                 const int s = (int)(pit % (uint32_t)S);
                 const uint32_t ph = (pit / (uint32_t)S) & 1u;
-                const int kc = j % p.kchunks;
-                if (kc == 0) {  // next kernel offset: its entries were loaded one offset ago
+                const int kc = (kc0 + j) % p.kchunks;
+                if (kc == 0 || j == 0) {  // next kernel offset: its entries were loaded one offset ago
 #pragma unroll
                     for (int i = 0; i < kMine; ++i) cur[i] = nxt[i];
                     if (mrem) {
@@ -276,8 +288,8 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
                     const uint32_t pit = it + (uint32_t)j;
                     const int s = (int)(pit % (uint32_t)S);
                     const uint32_t ph = (pit / (uint32_t)S) & 1u;
-                    const int kc = j % p.kchunks;
-                    if (kc == 0) {
+                    const int kc = (kc0 + j) % p.kchunks;
+                    if (kc == 0 || j == 0) {
                         o = __ffs(mrem) - 1;
                         mrem &= mrem - 1;
                     }
@@ -348,34 +360,54 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
             have_acc = __all_sync(0xffffffffu, have_acc);
         }
         if (csp) {
-            // split-K pairs, every thread of both CTAs at the cluster barriers:
-            // (1) once both rings are drained (the MMAs that read them completed
-            // before `accum`), accumulator `crank ^ 1` goes into the peer's staged
-            // f32 tile by 16-byte distributed-shared-memory stores; (2) each CTA
-            // adds its own accumulator `crank` to what it received: one add per
-            // element, own + peer, so the result is the same on every run.
-            // (Remote f32 atomic adds measured ~100 us per tile; a receive buffer
-            // taking the columns in two halves, 5 cluster barriers, ~9 us.)
+            // split-K pairs, every thread of both CTAs at the cluster barriers.
+            // Once both rings are drained (the MMAs that read them completed
+            // before `accum`), accumulator `crank ^ 1` goes into the peer's
+            // staged f32 tile, in two halves of the columns: TMEM -> a local
+            // staging area (the GroupNorm column-sum area, rows padded by 16
+            // bytes) -> 16-byte distributed-shared-memory stores, a warp writing
+            // 512 contiguous bytes of one row (row-scattered remote stores ran at
+            // a third of the speed; remote f32 atomic adds at ~1/10). Then each
+            // CTA adds its own accumulator `crank` to what it received: one add
+            // per element, own + peer, so the result is the same on every run.
+            float4* stg = reinterpret_cast<float4*>(colp);
+            const uint32_t peer = map_to_rank(smem_u32(stage_out), crank ^ 1u);
+            const int hch = nch / 2;      // chunks in the first half (the second takes the odd one)
+            const int sw = 4 * (nch - hch) + 1;  // staging row stride in float4s
+            cluster_sync();
+            for (int h = 0; h < 2; ++h) {
+                const int c_lo = h * hch, c_hi = h ? nch : hch;
+                if (warp < kProdWarps) {
+                    tc_fence_after();
+                    for (int c = c_lo + (warp >> 2); c < c_hi; c += 4) {
+                        float f[16];
+#pragma unroll
+                        for (int q = 0; q < 16; ++q) f[q] = 0.f;
+                        if (have_acc) tmem_ld16(tl + (crank ^ 1u) * p.thalf + 16 * c, f);
+#pragma unroll
+                        for (int q = 0; q < 4; ++q)
+                            stg[row * sw + (c - c_lo) * 4 + q] = make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
+                    }
+                    epi_bar();
+                    const int w4 = 4 * (c_hi - c_lo);  // float4s per row in this half
+                    for (int rr = 0; rr < 8; ++rr) {
+                        const int r = 8 * warp + rr;
+                        for (int j = lane; j < w4; j += 32) {
+                            const float4 v = stg[r * sw + j];
+                            st_cluster_v4(peer + (uint32_t)(r * ostride + 16 * c_lo + 4 * j) * 4u, v.x, v.y, v.z, v.w);
+                        }
+                    }
+                    epi_bar();  // the staging area is refilled by the next half
+                }
+            }
             cluster_sync();
             if (warp < kProdWarps) {
                 tc_fence_after();
-                const uint32_t peer = map_to_rank(smem_u32(stage_out), crank ^ 1u);
                 for (int c = warp >> 2; c < nch; c += 4) {
                     float f[16];
 #pragma unroll
                     for (int q = 0; q < 16; ++q) f[q] = 0.f;
-                    if (have_acc) tmem_ld16(tl + (crank ^ 1u) * p.thalf + 16 * c, f);
-                    const uint32_t a = peer + (uint32_t)(row * ostride + 16 * c) * 4u;
-#pragma unroll
-                    for (int q = 0; q < 4; ++q)
-                        st_cluster_v4(a + 16u * q, f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
-                }
-            }
-            cluster_sync();
-            if (warp < kProdWarps && have_acc) {
-                for (int c = warp >> 2; c < nch; c += 4) {
-                    float f[16];
-                    tmem_ld16(tl + crank * p.thalf + 16 * c, f);
+                    if (have_acc) tmem_ld16(tl + crank * p.thalf + 16 * c, f);
                     float4* dst = reinterpret_cast<float4*>(stage_out + (size_t)row * ostride + 16 * c);
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {

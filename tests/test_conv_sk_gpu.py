@@ -151,11 +151,15 @@ def test_sk_identity_linear(ctx, n, skflag):
     b = workloads.normal((cout,), 52, 0.1)
     wp = pack(ctx, w, s3dsp.LAYOUT_LINEAR, 1, cin, cout)
     xb = dev(x).to(torch.bfloat16)
-    # CTA pairs: rank 0 takes the one offset, rank 1 none (adds nothing)
     sk = run(ctx, None, 1, xb, wp, dev(b), cout, n, flags=skflag, out_dtype=torch.bfloat16, reps=2)
     t128 = run(ctx, None, 1, xb, wp, dev(b), cout, n, flags=s3dsp.CONV_TILE128, out_dtype=torch.bfloat16, reps=1)
     assert np.array_equal(sk[0], sk[1])
-    assert np.array_equal(sk[0], t128[0])  # whole tiles, same MMA order: bit-identical
+    if skflag == s3dsp.CONV_STREAM_K:
+        assert np.array_equal(sk[0], t128[0])  # whole tiles, same MMA order: bit-identical
+    else:
+        # CTA pairs split the 4 channel chunks 2 / 2 and add the two halves: f32
+        # reordering, then the bf16 rounding of the output
+        assert rel_l2(sk[0], t128[0]) < 1e-3
     assert rel_l2(sk[0], oracle.linear(x, w, b)) < 1e-2
 
 
