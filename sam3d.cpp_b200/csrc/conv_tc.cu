@@ -103,61 +103,6 @@ struct TcParams {
 // named barrier of the 16 gather/epilogue warps
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
 
-// --- CTA-pair (cluster of 2) helpers (cluster_rank, map_to_rank, cluster_sync: tc_common.cuh) ---
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_cluster(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// TMA tile load into this CTA's smem whose completion is counted on `bar`,
-// which may be the pair leader's barrier (shared::cluster address)
-__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
-        "l"((unsigned long long)map), "r"(x), "r"(y), "r"(bar)
-        : "memory");
-}
-__device__ __forceinline__ void mma_bf16_pair(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(a), "l"(b), "r"(idesc), "r"(acc)
-        : "memory");
-}
-// arrive on `bar` (shared::cluster address, this CTA's or the peer's) when
-// all prior pair MMAs of this thread complete
-__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
-    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-}
-// bounded wait with cluster-scope acquire (arrivals released by the peer CTA)
-__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                                  uint32_t* status) {
-    if (mbar_try_cluster(bar, parity)) return true;
-    const unsigned long long t0 = global_ns();
-    for (uint32_t it = 1;; ++it) {
-        if (mbar_try_cluster(bar, parity)) return true;
-        if ((it & 255u) == 0) {
-            if (*abort_flag) return false;
-            if (global_ns() - t0 > kWaitNs) {
-                *abort_flag = 1;
-                atomicOr(status, kErrPipelineTimeout);
-                return false;
-            }
-        }
-    }
-}
-
-
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
@@ -502,78 +447,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
         epi_bar();
-        // phase 2: coalesced row write-out, rows 8w .. 8w+7; lane owns columns 4*lane + 128*q.
-        const bool stats = p.gn_partials != nullptr;
-        const int gs = stats ? p.cout / p.gn_groups : 1;
-        constexpr int kQ = 2;  // bn <= 256 -> at most two 128-column slabs
-        const int limit = min(p.bn, p.cout - n0);  // valid columns of this tile
-        float4 bias4[kQ];
-#pragma unroll
-        for (int q = 0; q < kQ; ++q) {
-            const int col = n0 + 128 * q + 4 * lane;
-            bias4[q] = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (p.bias && 128 * q + 4 * lane < limit) {
-                bias4[q].x = __ldg(p.bias + col + 0);
-                bias4[q].y = col + 1 < p.cout ? __ldg(p.bias + col + 1) : 0.f;
-                bias4[q].z = col + 2 < p.cout ? __ldg(p.bias + col + 2) : 0.f;
-                bias4[q].w = col + 3 < p.cout ? __ldg(p.bias + col + 3) : 0.f;
-            }
-        }
-        const int lane_base = 8 * warp;
-        const int nrows = (int)max((int64_t)0, min((int64_t)8, p.n_out - (m0 + lane_base)));
-        const uint32_t so_base = smem_u32(stage_out);
-        // [16][bn][2]: may run past the rings (region0 is sized for it)
-        double* colp = reinterpret_cast<double*>(smem + (size_t)128 * ostride * 4);
-        double* colw = colp + (size_t)warp * p.bn * 2;
-        // One compact loop body per (out dtype, residual dtype, SiLU, stats)
-        // combination: a single generic body with every variant inlined runs
-        // several times slower (instruction-cache misses).
-        const int out_k = (p.cout & 3) ? -1 : p.out_dtype == S3DSP_F32 ? 0 : p.out_dtype == S3DSP_BF16 ? 1 : -1;
-        const int res_k = !p.residual ? 0 : p.res_dtype == S3DSP_F32 ? 1 : p.res_dtype == S3DSP_BF16 ? 2 : -1;
-        const int silu_k = (p.flags & S3DSP_EPI_SILU) ? 1 : 0;
-        const int sel = (out_k < 0 || res_k < 0 || (p.flags & S3DSP_EPI_GELU)) ? -1 : ((out_k * 3 + res_k) * 2 + silu_k) * 2 + (stats ? 1 : 0);
-        switch (sel) {
-#define S3DSP_WO(idx, OT, RT, SL, ST)                                                                            \
-    case idx:                                                                                                \
-        writeout_fast<OT, RT, SL, ST>(p, so_base, ostride, lane_base, lane, m0, n0, limit, nrows, bias4, colw); \
-        break;
-            S3DSP_WO(0, float, NoRes, false, false)
-            S3DSP_WO(1, float, NoRes, false, true)
-            S3DSP_WO(2, float, NoRes, true, false)
-            S3DSP_WO(3, float, NoRes, true, true)
-            S3DSP_WO(4, float, float, false, false)
-            S3DSP_WO(5, float, float, false, true)
-            S3DSP_WO(6, float, float, true, false)
-            S3DSP_WO(7, float, float, true, true)
-            S3DSP_WO(8, float, __nv_bfloat16, false, false)
-            S3DSP_WO(9, float, __nv_bfloat16, false, true)
-            S3DSP_WO(10, float, __nv_bfloat16, true, false)
-            S3DSP_WO(11, float, __nv_bfloat16, true, true)
-            S3DSP_WO(12, __nv_bfloat16, NoRes, false, false)
-            S3DSP_WO(13, __nv_bfloat16, NoRes, false, true)
-            S3DSP_WO(14, __nv_bfloat16, NoRes, true, false)
-            S3DSP_WO(15, __nv_bfloat16, NoRes, true, true)
-            S3DSP_WO(16, __nv_bfloat16, float, false, false)
-            S3DSP_WO(17, __nv_bfloat16, float, false, true)
-            S3DSP_WO(18, __nv_bfloat16, float, true, false)
-            S3DSP_WO(19, __nv_bfloat16, float, true, true)
-            S3DSP_WO(20, __nv_bfloat16, __nv_bfloat16, false, false)
-            S3DSP_WO(21, __nv_bfloat16, __nv_bfloat16, false, true)
-            S3DSP_WO(22, __nv_bfloat16, __nv_bfloat16, true, false)
-            S3DSP_WO(23, __nv_bfloat16, __nv_bfloat16, true, true)
-#undef S3DSP_WO
-            default:
-                writeout_generic(p, stage_out, ostride, lane_base, lane, m0, n0, limit, nrows, bias4, stats ? colw : nullptr);
-        }
-        // deterministic GroupNorm partials of the tile from the write-out's
-        // per-warp column sums (the padding CTA of an odd pair count, tile ==
-        // n_tiles, has no rows and no slot)
-        if (stats && tile < p.n_tiles) {
-            epi_bar();
-            gn_tile_partials<kProdWarps, kProdWarps * 32>(colp, p.bn, n0, limit, gs, p.gn_groups, tid,
-                                                          p.gn_partials + (int64_t)tile * p.gn_groups * 2,
-                                                          p.gn_store != 0, epi_bar);
-        }
+        // phase 2: bias / residual / SiLU / GroupNorm partials on the way out
+        tile_writeout<kProdWarps>(p, smem, ostride, warp, lane, tid, m0, n0,
+                                  p.gn_partials && tile < p.n_tiles ? p.gn_partials + (int64_t)tile * p.gn_groups * 2 : nullptr,
+                                  epi_bar);
         tc_fence_before();
     }
 
