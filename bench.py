@@ -49,10 +49,11 @@ METRIC = "active-voxel outputs/s, all GPUs (C=256 subm conv residual block)"
 UNIT = "voxel-outputs/s"
 L2_FLUSH_BYTES = 512 << 20  # > 126 MB L2
 # DRAM bytes (read + write) per launch, from one ncu capture of
-# `python bench.py --profile-case conv2`, keyed by (kernel, output rows,
-# channels): it holds only for that kernel on that shape; other shapes report
-# null until captured.
-CONV_TRAFFIC_BYTES = {("conv_tc_kernel", 15159, 256): 13.02e6}
+# `python bench.py --profile-case conv2` (128-row kernel) and of
+# `--profile-case conv2_pairs` (the dispatched split-K pair kernel), keyed by
+# (kernel, output rows, channels): each holds only for that kernel on that
+# shape; other shapes report null until captured.
+CONV_TRAFFIC_BYTES = {("conv_tc_kernel", 15159, 256): 13.02e6, ("conv_sk_kernel<256>:pairs", 15159, 256): 13.09e6}
 FFMA_PEAK_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12  # nominal FP32 FMA peak of B200 (148 SMs x 128 lanes x 2 x 1.965 GHz)
 
 
@@ -1539,6 +1540,7 @@ def run_reference(args, rank, world):
 # ---------------------------------------------------------------------------
 PROFILE_CASES = {
     "conv2": "config-2 conv (C=256, 15,159 voxels), 128-row kernel",
+    "conv2_pairs": "config-2 conv (C=256, 15,159 voxels), the kernel s3dsp_conv picks (split-K CTA pairs)",
     "conv_sk": "256^3 shell (241,978 voxels), C=256, stream-K kernel",
     "tables": "hash + submanifold kmap of the 2.58M-voxel 512^3 shell",
     "flexicubes": "FlexiCubes extraction of 970,176 cubes at 256^3",
@@ -1560,8 +1562,8 @@ def profile_case(case, reps):
 
     ctx = s3dsp.Context(0)
     P = s3dsp.PREC_BF16
-    if case in ("conv2", "conv_sk"):
-        coords = workloads.ellipsoid_shell(64 if case == "conv2" else 256, 0)
+    if case in ("conv2", "conv2_pairs", "conv_sk"):
+        coords = workloads.ellipsoid_shell(256 if case == "conv_sk" else 64, 0)
         n, c = len(coords), 256
         h = ctx.hash_build(torch.from_numpy(coords).cuda())
         k = ctx.kmap_subm3(h)
@@ -1570,7 +1572,7 @@ def profile_case(case, reps):
         x = torch.from_numpy(workloads.normal((n, c), 1)).cuda().to(torch.bfloat16)
         b = torch.from_numpy(workloads.normal((c,), 3, 0.1)).cuda()
         out = torch.empty((n, c), device="cuda")
-        flags = s3dsp.CONV_TILE128 if case == "conv2" else s3dsp.CONV_STREAM_K
+        flags = {"conv2": s3dsp.CONV_TILE128, "conv2_pairs": 0, "conv_sk": s3dsp.CONV_STREAM_K}[case]
         for _ in range(1 + reps):
             ctx.conv(k, 27, P, x, w, b, out, c, flags=flags)
     elif case == "step2":
