@@ -5,8 +5,12 @@
 // One CTA owns a 128-row x BN-column output tile and walks (offset, 16-channel
 // chunk) steps; gathered rows are staged through registers into shared memory
 // (transposed, so each thread reads 4 consecutive rows as one float4), double
-// buffered. Outputs are accumulated in registers, no atomics. Offsets with no
-// neighbour in the tile (per-tile bitmask from the kmap) are skipped.
+// buffered. Each thread accumulates 8 rows x BN/16 columns in registers (no
+// atomics); with BN >= 64 its columns are groups of four at a stride of 64
+// (4tx.., 64+4tx..), so a warp's weight reads are contiguous 16-byte loads.
+// Every output sums its products in the same order (offset, then channel) for
+// any BN. Offsets with no neighbour in the tile (per-tile bitmask from the
+// kmap) are skipped.
 //
 // Replaces the f32 GGML get_rows + mul_mat chains of slat_flow_graph.cpp:
 // 112-155 and mesh_decoder_graph.cpp:81-103; the optional prologue applies
@@ -59,14 +63,25 @@ __device__ __forceinline__ float load_as_f32(const void* p, uint32_t dt, int64_t
     return __half2float(reinterpret_cast<const __half*>(p)[i]);
 }
 
+// column of the tile held by thread tx as its j-th column
 template <int BN>
-__global__ void __launch_bounds__(NT) conv_f32_kernel(const F32ConvParams p) {
+__device__ __forceinline__ int f32_col(int tx, int j) {
+    if constexpr (BN >= 64) return 64 * (j >> 2) + 4 * tx + (j & 3);
+    else return tx * (BN / 16) + j;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(NT, BN >= 128 ? 2 : 1) conv_f32_kernel(const F32ConvParams p) {
     pdl_wait();
     pdl_trigger();
     constexpr int TN = BN / 16;
-    __shared__ __align__(16) float As[2][BK][BM];
-    __shared__ __align__(16) float Bs[2][BK][BN];
-    __shared__ double colsum[16][BN][2];  // per row group ty: column sums, summed in a fixed order
+    // the two stages of A and B, and after the main loop the GroupNorm column sums
+    constexpr int kStageBytes = 2 * BK * BM * 4 + 2 * BK * BN * 4;
+    constexpr int kColBytes = 16 * BN * 2 * 8;
+    __shared__ __align__(16) unsigned char smem_raw[kStageBytes > kColBytes ? kStageBytes : kColBytes];
+    auto As = reinterpret_cast<float (*)[BK][BM]>(smem_raw);
+    auto Bs = reinterpret_cast<float (*)[BK][BN]>(smem_raw + 2 * BK * BM * 4);
+    auto colsum = reinterpret_cast<double (*)[BN][2]>(smem_raw);  // per row group ty, fixed-order sums
 
     const int tid = threadIdx.x;
     const int64_t m0 = (int64_t)blockIdx.x * BM;
@@ -81,13 +96,12 @@ __global__ void __launch_bounds__(NT) conv_f32_kernel(const F32ConvParams p) {
     // A-load mapping: 2 float4 per thread: rows (tid/4) and (tid/4 + 64), k quad tid%4
     const int a_row = tid >> 2;
     const int a_kq = tid & 3;
-    // B-load mapping
+    // B-load mapping: BK x BN floats as float4s, NB4 per thread
     constexpr int B_F4 = BK * BN / 4;
-    const int b_k = tid / (BN / 4);
-    const int b_c4 = tid % (BN / 4);
+    constexpr int NB4 = (B_F4 + NT - 1) / NT;
 
     int32_t src[2] = {-1, -1};
-    float4 ra[2], rb;
+    float4 ra[2], rb[NB4];
     int cur_o = -1;
     uint32_t mrem = mask;
 
@@ -122,9 +136,14 @@ __global__ void __launch_bounds__(NT) conv_f32_kernel(const F32ConvParams p) {
             }
             ra[i] = v;
         }
-        if (tid < B_F4) {
-            const int k = kc * BK + b_k;  // < cin_pad (packed weights are zero padded)
-            rb = *reinterpret_cast<const float4*>(p.w + ((int64_t)cur_o * p.cin_pad + k) * p.cout_pad + n0 + 4 * b_c4);
+#pragma unroll
+        for (int q = 0; q < NB4; ++q) {
+            const int f = tid + NT * q;
+            if (f < B_F4) {
+                const int k = kc * BK + f / (BN / 4);  // < cin_pad (packed weights are zero padded)
+                rb[q] = *reinterpret_cast<const float4*>(p.w + ((int64_t)cur_o * p.cin_pad + k) * p.cout_pad + n0 +
+                                                         4 * (f % (BN / 4)));
+            }
         }
     };
     auto stash = [&](int buf) {
@@ -135,7 +154,11 @@ __global__ void __launch_bounds__(NT) conv_f32_kernel(const F32ConvParams p) {
             As[buf][a_kq * 4 + 2][a_row + 64 * i] = ra[i].z;
             As[buf][a_kq * 4 + 3][a_row + 64 * i] = ra[i].w;
         }
-        if (tid < B_F4) *reinterpret_cast<float4*>(&Bs[buf][b_k][4 * b_c4]) = rb;
+#pragma unroll
+        for (int q = 0; q < NB4; ++q) {
+            const int f = tid + NT * q;
+            if (f < B_F4) *reinterpret_cast<float4*>(&Bs[buf][f / (BN / 4)][4 * (f % (BN / 4))]) = rb[q];
+        }
     };
 
     const int ty = tid >> 4, tx = tid & 15;
@@ -158,8 +181,19 @@ __global__ void __launch_bounds__(NT) conv_f32_kernel(const F32ConvParams p) {
                 const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][k][64 + ty * 4]);
                 const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
                 float b[TN];
+                if constexpr (BN >= 64) {
 #pragma unroll
-                for (int j = 0; j < TN; ++j) b[j] = Bs[buf][k][tx * TN + j];
+                    for (int g = 0; g < TN / 4; ++g) {
+                        const float4 b4 = *reinterpret_cast<const float4*>(&Bs[buf][k][64 * g + 4 * tx]);
+                        b[4 * g + 0] = b4.x;
+                        b[4 * g + 1] = b4.y;
+                        b[4 * g + 2] = b4.z;
+                        b[4 * g + 3] = b4.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < TN; ++j) b[j] = Bs[buf][k][tx * TN + j];
+                }
 #pragma unroll
                 for (int i = 0; i < 8; ++i)
 #pragma unroll
@@ -170,44 +204,52 @@ __global__ void __launch_bounds__(NT) conv_f32_kernel(const F32ConvParams p) {
         }
     }
 
-    // epilogue
+    // epilogue, by groups of GJ columns (GJ f64 column sums live at a time);
+    // the column sums reuse the stage buffers, which the last step's barrier freed
     const bool stats = p.gn_partials != nullptr;
     const int gs = stats ? p.cout / p.gn_groups : 1;
-    double csum[TN], csq[TN];
+    constexpr int GJ = TN >= 4 ? 4 : TN;
 #pragma unroll
-    for (int j = 0; j < TN; ++j) csum[j] = csq[j] = 0.0;
+    for (int g = 0; g < TN / GJ; ++g) {
+        double csum[GJ], csq[GJ];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const int64_t r = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
-        if (r >= p.n_out) continue;
+        for (int jj = 0; jj < GJ; ++jj) csum[jj] = csq[jj] = 0.0;
 #pragma unroll
-        for (int j = 0; j < TN; ++j) {
-            const int col = n0 + tx * TN + j;
-            if (col >= p.cout) continue;
-            float v = acc[i][j] + (p.bias ? p.bias[col] : 0.f);
-            if (p.residual) v += load_as_f32(p.residual, p.res_dtype, (r >> p.res_shift) * p.cout + col);
-            if (stats) {
-                csum[j] += (double)v;
-                csq[j] += (double)v * (double)v;
+        for (int i = 0; i < 8; ++i) {
+            const int64_t r = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+            if (r >= p.n_out) continue;
+#pragma unroll
+            for (int jj = 0; jj < GJ; ++jj) {
+                const int j = g * GJ + jj;
+                const int col = n0 + f32_col<BN>(tx, j);
+                if (col >= p.cout) continue;
+                float v = acc[i][j] + (p.bias ? p.bias[col] : 0.f);
+                if (p.residual) v += load_as_f32(p.residual, p.res_dtype, (r >> p.res_shift) * p.cout + col);
+                if (stats) {
+                    csum[jj] += (double)v;
+                    csq[jj] += (double)v * (double)v;
+                }
+                if (p.flags & S3DSP_EPI_SILU) v = silu_f(v);
+                if (p.flags & S3DSP_EPI_GELU)
+                    v = 0.5f * v * (1.0f + tanhf(0.7978845608028654f * (v + 0.044715f * v * v * v)));
+                if (p.out_dtype == S3DSP_F32)
+                    reinterpret_cast<float*>(p.out)[r * p.cout + col] = v;
+                else if (p.out_dtype == S3DSP_BF16)
+                    reinterpret_cast<__nv_bfloat16*>(p.out)[r * p.cout + col] = __float2bfloat16(v);
+                else
+                    reinterpret_cast<__half*>(p.out)[r * p.cout + col] = __float2half(v);
             }
-            if (p.flags & S3DSP_EPI_SILU) v = silu_f(v);
-            if (p.flags & S3DSP_EPI_GELU) v = 0.5f * v * (1.0f + tanhf(0.7978845608028654f * (v + 0.044715f * v * v * v)));
-            if (p.out_dtype == S3DSP_F32)
-                reinterpret_cast<float*>(p.out)[r * p.cout + col] = v;
-            else if (p.out_dtype == S3DSP_BF16)
-                reinterpret_cast<__nv_bfloat16*>(p.out)[r * p.cout + col] = __float2bfloat16(v);
-            else
-                reinterpret_cast<__half*>(p.out)[r * p.cout + col] = __float2half(v);
+        }
+        if (stats) {
+#pragma unroll
+            for (int jj = 0; jj < GJ; ++jj) {
+                colsum[ty][f32_col<BN>(tx, g * GJ + jj)][0] = csum[jj];
+                colsum[ty][f32_col<BN>(tx, g * GJ + jj)][1] = csq[jj];
+            }
         }
     }
     if (stats) {
-        // deterministic: every thread's column sums to smem, then each group
-        // summed over row groups and columns in a fixed order
-#pragma unroll
-        for (int j = 0; j < TN; ++j) {
-            colsum[ty][tx * TN + j][0] = csum[j];
-            colsum[ty][tx * TN + j][1] = csq[j];
-        }
+        // deterministic: each group summed over row groups and columns in a fixed order
         __syncthreads();
         const int limit = min(BN, p.cout - n0);
         const int g_lo = n0 / gs;
@@ -250,8 +292,11 @@ cudaError_t launch_conv_f32(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol
     p.kvol = kvol;
     p.w = w;
     p.cin_pad = (cin + BK - 1) / BK * BK;
-    const int bn = (cout % 64 == 0 || cout > 64) ? 64 : 32;
     p.cout_pad = (cout + 63) / 64 * 64;
+    // 128-column tiles (8 x 8 outputs per thread) for layers of at least two
+    // such blocks: on B200, config 2 (C = 256) 1.56 vs 1.70 ms per conv; at
+    // C = 128 the halved CTA count made them slower (0.56 vs 0.46 ms)
+    const int bn = p.cout_pad % 256 == 0 ? 128 : (cout % 64 == 0 || cout > 64) ? 64 : 32;
     p.bias = bias;
     p.residual = residual;
     p.res_dtype = res_dtype;
@@ -273,7 +318,9 @@ cudaError_t launch_conv_f32(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol
         if (e != cudaSuccess) return e;
     }
     const dim3 grid((unsigned)tiles, (unsigned)((cout + bn - 1) / bn));
-    if (bn == 64)
+    if (bn == 128)
+        launch_pdl(conv_f32_kernel<128>, dim3(grid), dim3(NT), 0, ctx->stream, p);
+    else if (bn == 64)
         launch_pdl(conv_f32_kernel<64>, dim3(grid), dim3(NT), 0, ctx->stream, p);
     else
         launch_pdl(conv_f32_kernel<32>, dim3(grid), dim3(NT), 0, ctx->stream, p);
