@@ -370,11 +370,13 @@ def e2e_queued(s3dsp, torch, device, main_stream, queued_call, ref_out, steps, w
     start.record(main_stream)
     for st, _, _ in lanes:
         st.wait_event(start)
+    t_issue = time.perf_counter()
     for _ in range(per):
         for st, cx, out in lanes:
             with torch.cuda.stream(st):
                 flush()
             queued_call(cx, out)
+    issue_ms = (time.perf_counter() - t_issue) * 1e3
     for st, _, _ in lanes:
         ev = torch.cuda.Event()
         ev.record(st)
@@ -385,7 +387,7 @@ def e2e_queued(s3dsp, torch, device, main_stream, queued_call, ref_out, steps, w
         cx.check()
         if not torch.equal(out, ref_out):
             raise RuntimeError("a queued host call's output differs from the synchronous call's")
-    return start.elapsed_time(final), per * E2E_STREAMS
+    return start.elapsed_time(final), per * E2E_STREAMS, issue_ms
 
 
 def gather_rows(torch, world, values):
@@ -485,14 +487,15 @@ def run_ours(args, rank, world, local_rank):
         cx.res_block_gn_host_queued(s3dsp.PREC_BF16, coords_h, x_h, path.w1, path.b1, path.gamma, path.beta,
                                     path.w2, path.b2, out)
 
-    pipe_ms, pipe_steps = e2e_queued(s3dsp, torch, device, stream, queued_call, out_h, args.steps, args.warmup,
+    pipe_ms, pipe_steps, issue_ms = e2e_queued(s3dsp, torch, device, stream, queued_call, out_h, args.steps, args.warmup,
                                      flush)
     clocks = sampler.stop()
     h2d = coords_h.numel() * 4 + x_h.numel() * 4
     d2h = out_h.numel() * 4
     ctx.check()
     per_rank = gather_rows(torch, world, [dev_ms / args.steps, copy_ms, serial_ms / args.steps,
-                                          pipe_ms / pipe_steps, float(E2E_STREAMS), float(n_cpus)])
+                                          pipe_ms / pipe_steps, float(E2E_STREAMS), float(n_cpus),
+                                          issue_ms / pipe_steps])
 
     # max over ranks
     vals = torch.tensor([dev_ms, serial_ms, pipe_ms], dtype=torch.float64, device=device)
@@ -540,7 +543,8 @@ def run_ours(args, rank, world, local_rank):
                     "steps": pipe_steps, "serial_value": total_units / (serial_ms / 1e3),
                     "serial_ms_per_step": serial_ms / args.steps,
                     "per_rank_ms": [{"rank": r, "device_step": v[0], "copies_only": v[1], "call_serial": v[2],
-                                     "call_queued": v[3], "streams": int(v[4]), "cpus": int(v[5])}
+                                     "call_queued": v[3], "streams": int(v[4]), "cpus": int(v[5]),
+                                     "host_issue_per_call": v[6]}
                                     for r, v in enumerate(per_rank)]},
             # inside the timed regions: both graphs' replays, serial host calls, worker calls
             "gpu_launches": path.launches_per_step * (3 * args.steps + pipe_steps),
