@@ -90,6 +90,8 @@ struct SkParams {
     double* gn_partials;
     int gn_groups;
     uint32_t* status;
+    const void* w;              // packed weights (for the L2 prefetch before the dependency wait)
+    uint64_t w_bytes;
 };
 
 __device__ __forceinline__ int64_t unit_begin(const SkParams& p, int i) {
@@ -125,8 +127,6 @@ __host__ __device__ constexpr size_t colsum_bytes(int bn) {
 // one-source gather keeps its shorter address path).
 template <int kRows, bool kTwo = false>
 __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, const __grid_constant__ CUtensorMap wmap) {
-    pdl_wait();
-    pdl_trigger();
     constexpr int kSub = kRows / 128;              // 128-row accumulators per work tile
     constexpr int kAStage = kRows * 2 * kKC;       // bytes: kRows gathered rows x kKC bf16
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -168,10 +168,16 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
+    // the weights do not depend on the previous kernel: start bringing this
+    // CTA's share into L2 while it finishes
+    if (tid == 32) prefetch_share_l2(p.w, p.w_bytes, (uint32_t)me, (uint32_t)p.grid);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
+    // everything above touched shared memory, TMEM, parameters and the L2 hint only
+    pdl_wait();
+    pdl_trigger();
 
     uint32_t it = 0;      // pipeline step counter, identical in every role
     uint32_t acc_ph = 0;  // accum barrier phase
@@ -701,6 +707,8 @@ cudaError_t launch_conv_sk(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
     p.gn_partials = gn_partials;
     p.gn_groups = gn_groups;
     p.status = ctx->d_status;
+    p.w = w;
+    p.w_bytes = (uint64_t)kvol * (uint64_t)cout_pad * (uint64_t)cin_pad * 2;
 
     cudaStream_t s = ctx->stream;
     static std::atomic<uint64_t> optin128{0}, optin256{0}, optin128_two{0}, optin256_two{0};

@@ -98,6 +98,8 @@ struct TcParams {
     int gn_store;  // one column tile covers every channel: each slot has one writer
     int gn_groups;
     uint32_t* status;
+    const void* w;              // packed weights (for the L2 prefetch before the dependency wait)
+    uint64_t w_bytes;
 };
 
 // named barrier of the 16 gather/epilogue warps
@@ -194,13 +196,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
         }
     }
+    // the weights do not depend on the previous kernel: start bringing this
+    // CTA's share into L2 while it finishes
+    if (tid == 32)
+        prefetch_share_l2(p.w, p.w_bytes, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
     tc_fence_before();
     __syncthreads();
     if (kPair) cluster_sync();  // the peer's barriers exist before any remote arrive
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
 
-    // everything above touched shared memory, TMEM and parameters only
+    // everything above touched shared memory, TMEM, parameters and the L2 hint only
     pdl_wait();
     pdl_trigger();
     // both CTAs of a pair walk the union of their tiles' active offsets
@@ -589,6 +595,8 @@ static cudaError_t launch_tc_impl(s3dsp_context* ctx, const s3dsp_kmap* kmap, in
     p.gn_groups = gn_groups;
     p.gn_store = cout_pad == bn;
     p.status = ctx->d_status;
+    p.w = w;
+    p.w_bytes = (uint64_t)parts * kvol * (uint64_t)cout_pad * (uint64_t)cin_pad * (tf32 ? 4 : 2);
 
     const size_t smem = smem_bytes(stages, brows, parts, bn);
     static std::atomic<uint64_t> optin_pair{0}, optin_single{0}, optin_tf32{0};

@@ -88,6 +88,19 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         "l"((unsigned long long)map), "r"(x), "r"(y), "r"(bar)
         : "memory");
 }
+// L2 prefetch of this CTA's share of a constant tensor (the packed weights):
+// CTA `i` of `n` takes bytes [i * chunk, (i + 1) * chunk), chunk a multiple of
+// 16 (bytes and the base must be 16-byte multiples). A cache hint only, so it
+// may run before griddepcontrol.wait: it reads nothing the kernel consumes.
+__device__ __forceinline__ void prefetch_share_l2(const void* base, uint64_t bytes, uint32_t i, uint32_t n) {
+    const uint64_t chunk = (bytes / n + 15) / 16 * 16;
+    const uint64_t b0 = (uint64_t)i * chunk;
+    if (!base || b0 >= bytes) return;
+    const uint64_t len = bytes - b0 < chunk ? bytes - b0 : chunk;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(static_cast<const char*>(base) + b0),
+                 "r"((uint32_t)len)
+                 : "memory");
+}
 __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
