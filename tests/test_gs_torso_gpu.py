@@ -12,6 +12,7 @@ import gs
 import oracle
 import s3dsp
 import workloads
+from gates import gate
 
 pytestmark = pytest.mark.gpu
 
@@ -62,7 +63,7 @@ def test_window_attention(ctx, shift):
     err = rel_l2(out.cpu().numpy(), exp)
     print(f"\nwindow attention shift {shift}: rel-L2 {err:.3e}, {len(tb.windows[shift])} windows, "
           f"longest {int(buckets[:, 0].max())} tokens")
-    assert err <= 1e-5
+    gate(err, 1e-5 * (1 + 1e-12))
 
 
 @pytest.mark.parametrize("name,prec,tol", PRECS)
@@ -80,10 +81,10 @@ def test_two_blocks(ctx, name, prec, tol):
     for k in ("block0", "block1"):
         e = rel_l2(got_taps[k].cpu().numpy(), taps[k])
         print(f"\nGS torso {name} {k}: rel-L2 {e:.3e} (gate {tol:g})")
-        assert e <= tol
+        gate(e, tol * (1 + 1e-12))
     err = rel_l2(got.cpu().numpy(), exp)
     print(f"GS torso {name} two blocks + head: rel-L2 {err:.3e} (gate {tol:g})")
-    assert err <= tol
+    gate(err, tol * (1 + 1e-12))
 
 
 @pytest.mark.parametrize("name,prec,tol", [PRECS[0], PRECS[2]])
@@ -98,4 +99,4 @@ def test_twelve_blocks_end_to_end(ctx, name, prec, tol):
     ctx.check()
     err = rel_l2(got.cpu().numpy(), exp)
     print(f"\nGS torso {name}, 12 blocks, {len(coords)} tokens: rel-L2 {err:.3e} (gate {tol:g})")
-    assert err <= tol
+    gate(err, tol * (1 + 1e-12))

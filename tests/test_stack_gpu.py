@@ -10,6 +10,7 @@ import oracle
 import s3dsp
 import stack
 import workloads
+from gates import gate
 
 pytestmark = pytest.mark.gpu
 
@@ -54,7 +55,7 @@ def test_config4_end_to_end(ctx, case, prec, tol):
     assert np.array_equal(cc.cpu().numpy(), ref_coords)
     assert out.shape == (64 * len(coords), stack.HEAD)
     err = rel_l2(out.cpu().numpy(), ref)
-    assert err < tol, err
+    gate(err, tol, "stack end to end")
 
 
 def test_units():
