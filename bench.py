@@ -1545,6 +1545,7 @@ def run_reference(args, rank, world):
 PROFILE_CASES = {
     "conv2": "config-2 conv (C=256, 15,159 voxels), 128-row kernel",
     "conv2_pairs": "config-2 conv (C=256, 15,159 voxels), the kernel s3dsp_conv picks (split-K CTA pairs)",
+    "conv2_f32": "config-2 conv (C=256, 15,159 voxels) in F32 strict (FFMA kernel)",
     "conv_sk": "256^3 shell (241,978 voxels), C=256, stream-K kernel",
     "tables": "hash + submanifold kmap of the 2.58M-voxel 512^3 shell",
     "flexicubes": "FlexiCubes extraction of 970,176 cubes at 256^3",
@@ -1579,6 +1580,18 @@ def profile_case(case, reps):
         flags = {"conv2": s3dsp.CONV_TILE128, "conv2_pairs": 0, "conv_sk": s3dsp.CONV_STREAM_K}[case]
         for _ in range(1 + reps):
             ctx.conv(k, 27, P, x, w, b, out, c, flags=flags)
+    elif case == "conv2_f32":
+        coords = workloads.ellipsoid_shell(64, 0)
+        n, c = len(coords), 256
+        PF = s3dsp.PREC_F32_STRICT
+        k = ctx.kmap_subm3(ctx.hash_build(torch.from_numpy(coords).cuda()))
+        w = torch.empty(s3dsp.Context.packed_bytes(PF, 27, c, c), dtype=torch.uint8, device="cuda")
+        ctx.weights_pack(torch.from_numpy(workloads.kaiming_normal_slat(c, c, 2)), s3dsp.LAYOUT_SLAT_ROW, 27, c, c, PF, w)
+        x = torch.from_numpy(workloads.normal((n, c), 1)).cuda()
+        b = torch.from_numpy(workloads.normal((c,), 3, 0.1)).cuda()
+        out = torch.empty((n, c), device="cuda")
+        for _ in range(1 + reps):
+            ctx.conv(k, 27, PF, x, w, b, out, c)
     elif case == "step2":
         stream = torch.cuda.current_stream()
         ctx2 = s3dsp.Context(0, stream=stream.cuda_stream, flags=s3dsp.CONTEXT_DEFERRED_CHECKS)

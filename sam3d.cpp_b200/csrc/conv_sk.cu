@@ -171,6 +171,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_sk_kernel(const SkParams p, 
     // the weights do not depend on the previous kernel: start bringing this
     // CTA's share into L2 while it finishes
     if (tid == 32) prefetch_share_l2(p.w, p.w_bytes, (uint32_t)me, (uint32_t)p.grid);
+    if (warp == 2) prefetch_lines_l2(p.bias, (uint64_t)p.cout * 4, lane);  // read by the epilogue
     tc_fence_before();
     __syncthreads();
     tc_fence_after();

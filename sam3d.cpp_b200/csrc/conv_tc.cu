@@ -200,6 +200,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // CTA's share into L2 while it finishes
     if (tid == 32)
         prefetch_share_l2(p.w, p.w_bytes, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
+    if (warp == 2) prefetch_lines_l2(p.bias, (uint64_t)p.cout * 4, lane);  // read by the epilogue
     tc_fence_before();
     __syncthreads();
     if (kPair) cluster_sync();  // the peer's barriers exist before any remote arrive

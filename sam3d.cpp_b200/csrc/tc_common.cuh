@@ -101,6 +101,13 @@ __device__ __forceinline__ void prefetch_share_l2(const void* base, uint64_t byt
                  "r"((uint32_t)len)
                  : "memory");
 }
+// L2 prefetch of a small constant array (a bias vector): one line per lane of
+// the calling warp. A hint like prefetch_share_l2.
+__device__ __forceinline__ void prefetch_lines_l2(const void* p, uint64_t bytes, int lane) {
+    if (!p) return;
+    for (uint64_t b = (uint64_t)lane * 128; b < bytes; b += 32 * 128)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(static_cast<const char*>(p) + b));
+}
 __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
