@@ -305,20 +305,6 @@ __device__ __forceinline__ void cp16(float* dst, const float* src, bool valid, c
                  : "memory");
 }
 
-// (d0, d1) = (a * b0 + d0, a * b1 + d1), one packed two-lane FP32 FMA: each
-// lane rounds once, like fmaf, so the sums are the same bits; half the FMA
-// instructions of the scalar loop
-__device__ __forceinline__ void fma2(float& d0, float& d1, float a, float b0, float b1) {
-    asm("{\n\t.reg .b64 d, x, y;\n\t"
-        "mov.b64 d, {%0, %1};\n\t"
-        "mov.b64 x, {%2, %2};\n\t"
-        "mov.b64 y, {%3, %4};\n\t"
-        "fma.rn.f32x2 d, x, y, d;\n\t"
-        "mov.b64 {%0, %1}, d;\n\t}"
-        : "+f"(d0), "+f"(d1)
-        : "f"(a), "f"(b0), "f"(b1));
-}
-
 template <int BN>
 constexpr int ms_stage_floats() { return BM * kAPad + BK * BN; }
 template <int BN>

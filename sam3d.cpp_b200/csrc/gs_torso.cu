@@ -21,7 +21,6 @@ using namespace s3dsp;
 
 namespace {
 
-constexpr int kAttThreads = 128;
 constexpr int kKeyChunk = 64;
 
 __device__ __forceinline__ float ld_any(const void* p, uint32_t dt, int64_t i) {
@@ -57,29 +56,20 @@ __global__ void gather_rows_kernel(const void* __restrict__ x, uint32_t xd, int6
     }
 }
 
-// qkv [n, 3c] f32 rows in bucket order: q | k | v, head h = columns h*d .. h*d+d-1
-template <int D>
-__global__ void __launch_bounds__(kAttThreads) window_attention_kernel(const float* __restrict__ qkv, int64_t n, int c,
-                                                                      const int2* __restrict__ windows, float scale,
-                                                                      const int32_t* __restrict__ scatter,
-                                                                      float* __restrict__ out,
-                                                                      uint32_t* __restrict__ status) {
-    pdl_wait();
-    pdl_trigger();
-    __shared__ float sk[kKeyChunk][D];
-    __shared__ float sv[kKeyChunk][D];
-    const int2 w = windows[blockIdx.x];
-    const int h = blockIdx.y;
-    const int64_t start = w.x;
-    const int len = w.y;
-    if (start < 0 || len <= 0 || start + len > n) {
-        if (threadIdx.x == 0) atomicOr(status, kErrRowRange);
-        return;
-    }
+// One window of one head, one query row per thread and pass (the path for
+// windows longer than kMaxWindow): keys and values staged through shared
+// memory in chunks of 64 rows (sk, sv: [kKeyChunk][D] each); per query the row
+// maximum of the scaled scores first, then exp(s - max), their sum and the
+// value rows weighted by exp(s - max), divided by the sum at the end.
+template <int D, int kThreads>
+__device__ __forceinline__ void attend_per_query(const float* __restrict__ qkv, int64_t n, int c, int64_t start,
+                                                 int len, int h, float scale, const int32_t* __restrict__ scatter,
+                                                 float* __restrict__ out, uint32_t* __restrict__ status,
+                                                 float (*sk)[D], float (*sv)[D]) {
     const int64_t ld = 3 * (int64_t)c;
-    const int passes = (len + kAttThreads - 1) / kAttThreads;
+    const int passes = (len + kThreads - 1) / kThreads;
     for (int pass = 0; pass < passes; ++pass) {
-        const int qi = pass * kAttThreads + threadIdx.x;
+        const int qi = pass * kThreads + threadIdx.x;
         const bool have_q = qi < len;
         float q[D];
         if (have_q) {
@@ -99,7 +89,7 @@ __global__ void __launch_bounds__(kAttThreads) window_attention_kernel(const flo
             for (int k0 = 0; k0 < len; k0 += kKeyChunk) {
                 const int kn = min(kKeyChunk, len - k0);
                 __syncthreads();
-                for (int e = threadIdx.x; e < kn * (D / 4); e += kAttThreads) {
+                for (int e = threadIdx.x; e < kn * (D / 4); e += kThreads) {
                     const int r = e / (D / 4), j = e - r * (D / 4);
                     const float* row = qkv + (start + k0 + r) * ld + (int64_t)h * D + 4 * j;
                     *reinterpret_cast<float4*>(&sk[r][4 * j]) = __ldg(reinterpret_cast<const float4*>(row + c));
@@ -136,6 +126,169 @@ __global__ void __launch_bounds__(kAttThreads) window_attention_kernel(const flo
                     dst[j] = make_float4(acc[4 * j] * inv, acc[4 * j + 1] * inv, acc[4 * j + 2] * inv,
                                          acc[4 * j + 3] * inv);
             }
+        }
+    }
+}
+
+// Tiled form, one CTA per (window, head), windows of at most kMaxWindow rows,
+// 64 queries at a time:
+//  1. S = (Q K^T) * scale in 4 x 4 register blocks per thread (the dot over the
+//     head's channels in channel order), kept key-major in shared memory;
+//  2. the softmax in the reference's order: the row maximum, then
+//     exp(s - max) in place, then one thread per query sums them in key order;
+//  3. O = P V in 4 x (D / 16) register blocks, accumulated in key order, times
+//     1 / sum.
+// Every score, sum and accumulation is evaluated in the same order as in
+// attend_per_query, so both give the same bits; longer windows take that path
+// (the window tables of a 64^3 shell hold at most ~235 tokens per window).
+// About 97 KB of shared memory and at most 128 registers: two CTAs per SM.
+constexpr int kTileThreads = 256;
+constexpr int kQB = 64;          // queries per block, and keys per chunk
+constexpr int kMaxWindow = 256;  // score rows kept in shared memory: two CTAs per SM
+
+template <int D>
+constexpr size_t tiled_smem_bytes() {
+    return sizeof(float) * ((size_t)kMaxWindow * kQB + 2 * (size_t)D * kQB + 5 * (size_t)kQB);
+}
+
+template <int D>
+__global__ void __launch_bounds__(kTileThreads, 2)
+    window_attention_tiled_kernel(const float* __restrict__ qkv, int64_t n, int c, const int2* __restrict__ windows,
+                                  float scale, const int32_t* __restrict__ scatter, float* __restrict__ out,
+                                  uint32_t* __restrict__ status) {
+    pdl_wait();
+    pdl_trigger();
+    constexpr int DPT = D / 16;  // output channels per thread in phase 3
+    extern __shared__ __align__(16) float sm[];
+    float* St = sm;                          // [kMaxWindow][kQB] scores, then exp(s - max)
+    float* Qt = St + kMaxWindow * kQB;       // [D][kQB] the query block, transposed
+    float* Kt = Qt + D * kQB;                // [D][kQB] a key chunk, transposed (phase 1)
+    float* Vs = Kt;                          // [kQB][D] a value chunk (phase 3, same space)
+    float* pmax = Kt + D * kQB;              // [4][kQB] partial row maxima
+    float* inv = pmax + 4 * kQB;             // [kQB] 1 / sum
+    const int2 w = windows[blockIdx.x];
+    const int h = blockIdx.y;
+    const int64_t start = w.x;
+    const int len = w.y;
+    if (start < 0 || len <= 0 || start + len > n) {
+        if (threadIdx.x == 0) atomicOr(status, kErrRowRange);
+        return;
+    }
+    if (len > kMaxWindow) {
+        attend_per_query<D, kTileThreads>(qkv, n, c, start, len, h, scale, scatter, out, status,
+                                          reinterpret_cast<float(*)[D]>(Qt), reinterpret_cast<float(*)[D]>(Kt));
+        return;
+    }
+    const int64_t ld = 3 * (int64_t)c;
+    const float* base = qkv + start * ld + (int64_t)h * D;  // q of the window's first row
+    const int tid = threadIdx.x;
+    const int ti = tid & 15;   // queries 4 ti .. 4 ti + 3
+    const int tr = tid >> 4;   // phase 1: keys 4 tr ..; phase 3: channels DPT tr ..
+    for (int q0 = 0; q0 < len; q0 += kQB) {
+        const int qn = min(kQB, len - q0);
+        __syncthreads();  // the previous block is done with St, Qt, Vs and inv
+        for (int e = tid; e < kQB * (D / 4); e += kTileThreads) {
+            const int i = e % kQB, j4 = e / kQB;  // a warp: 32 consecutive rows (no bank conflicts)
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (i < qn) v = __ldg(reinterpret_cast<const float4*>(base + (q0 + i) * ld + 4 * j4));
+            Qt[(4 * j4 + 0) * kQB + i] = v.x;
+            Qt[(4 * j4 + 1) * kQB + i] = v.y;
+            Qt[(4 * j4 + 2) * kQB + i] = v.z;
+            Qt[(4 * j4 + 3) * kQB + i] = v.w;
+        }
+        // ---- phase 1: scaled scores ----
+        for (int k0 = 0; k0 < len; k0 += kQB) {
+            const int kn = min(kQB, len - k0);
+            __syncthreads();  // Kt is free (and Qt complete)
+            for (int e = tid; e < kQB * (D / 4); e += kTileThreads) {
+                const int r = e % kQB, j4 = e / kQB;
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (r < kn) v = __ldg(reinterpret_cast<const float4*>(base + (k0 + r) * ld + c + 4 * j4));
+                Kt[(4 * j4 + 0) * kQB + r] = v.x;
+                Kt[(4 * j4 + 1) * kQB + r] = v.y;
+                Kt[(4 * j4 + 2) * kQB + r] = v.z;
+                Kt[(4 * j4 + 3) * kQB + r] = v.w;
+            }
+            __syncthreads();
+            float acc[4][4];
+#pragma unroll
+            for (int x = 0; x < 4; ++x)
+#pragma unroll
+                for (int y = 0; y < 4; ++y) acc[x][y] = 0.f;
+#pragma unroll 8
+            for (int j = 0; j < D; ++j) {
+                const float4 a = *reinterpret_cast<const float4*>(Qt + j * kQB + 4 * ti);
+                const float4 b = *reinterpret_cast<const float4*>(Kt + j * kQB + 4 * tr);
+                const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+                for (int x = 0; x < 4; ++x)
+#pragma unroll
+                    for (int y = 0; y < 4; y += 2) fma2(acc[x][y], acc[x][y + 1], av[x], bv[y], bv[y + 1]);
+            }
+#pragma unroll
+            for (int y = 0; y < 4; ++y) {
+                const int r = 4 * tr + y;
+                if (r < kn)
+                    *reinterpret_cast<float4*>(St + (k0 + r) * kQB + 4 * ti) =
+                        make_float4(acc[0][y] * scale, acc[1][y] * scale, acc[2][y] * scale, acc[3][y] * scale);
+            }
+        }
+        __syncthreads();
+        // ---- phase 2: the softmax (maximum, exp(s - max), sum in key order) ----
+        {
+            const int i = tid & (kQB - 1), part = tid / kQB;  // four threads per query
+            float m = -INFINITY;
+            for (int r = part; r < len; r += 4) m = fmaxf(m, St[r * kQB + i]);
+            pmax[part * kQB + i] = m;
+            __syncthreads();
+            const float mx = fmaxf(fmaxf(pmax[i], pmax[kQB + i]), fmaxf(pmax[2 * kQB + i], pmax[3 * kQB + i]));
+            for (int r = part; r < len; r += 4) St[r * kQB + i] = expf(St[r * kQB + i] - mx);
+            __syncthreads();
+            if (tid < kQB) {
+                float sum = 0.f;
+                for (int r = 0; r < len; ++r) sum += St[r * kQB + tid];
+                inv[tid] = 1.0f / sum;
+            }
+        }
+        // ---- phase 3: O = P V ----
+        float o[4][DPT];
+#pragma unroll
+        for (int x = 0; x < 4; ++x)
+#pragma unroll
+            for (int y = 0; y < DPT; ++y) o[x][y] = 0.f;
+        for (int k0 = 0; k0 < len; k0 += kQB) {
+            const int kn = min(kQB, len - k0);
+            __syncthreads();  // Vs is free (and the sums are done)
+            for (int e = tid; e < kn * (D / 4); e += kTileThreads) {
+                const int r = e / (D / 4), j4 = e % (D / 4);
+                *reinterpret_cast<float4*>(Vs + r * D + 4 * j4) =
+                    __ldg(reinterpret_cast<const float4*>(base + (k0 + r) * ld + 2 * c + 4 * j4));
+            }
+            __syncthreads();
+            for (int r = 0; r < kn; ++r) {
+                const float4 p4 = *reinterpret_cast<const float4*>(St + (k0 + r) * kQB + 4 * ti);
+                const float pv[4] = {p4.x, p4.y, p4.z, p4.w};
+                float v[DPT];
+#pragma unroll
+                for (int y = 0; y < DPT; ++y) v[y] = Vs[r * D + DPT * tr + y];
+#pragma unroll
+                for (int x = 0; x < 4; ++x)
+#pragma unroll
+                    for (int y = 0; y < DPT; y += 2) fma2(o[x][y], o[x][y + 1], pv[x], v[y], v[y + 1]);
+            }
+        }
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+            const int i = 4 * ti + x;
+            if (i >= qn) continue;
+            const int64_t orow = scatter ? (int64_t)scatter[start + q0 + i] : start + q0 + i;
+            if (orow < 0 || orow >= n) {
+                atomicOr(status, kErrRowRange);
+                continue;
+            }
+            float* dst = out + orow * (int64_t)c + (int64_t)h * D + DPT * tr;
+#pragma unroll
+            for (int y = 0; y < DPT; ++y) dst[y] = o[x][y] * inv[i];
         }
     }
 }
@@ -184,12 +337,18 @@ extern "C" S3DSP_API s3d_status s3dsp_window_attention(s3dsp_context* ctx, const
     const float scale = 1.0f / sqrtf((float)d);
     const int2* win = reinterpret_cast<const int2*>(d_windows);
     cudaError_t e;
-    if (d == 32)
-        e = launch_pdl(window_attention_kernel<32>, grid, dim3(kAttThreads), 0, ctx->stream, qkv, n, (int)c, win, scale,
-                       d_scatter, out, ctx->d_status);
-    else
-        e = launch_pdl(window_attention_kernel<64>, grid, dim3(kAttThreads), 0, ctx->stream, qkv, n, (int)c, win, scale,
-                       d_scatter, out, ctx->d_status);
+    static std::atomic<uint64_t> optin32{0}, optin64{0};
+    if (d == 32) {
+        e = smem_optin((const void*)window_attention_tiled_kernel<32>, ctx->device, optin32);
+        if (e == cudaSuccess)
+            e = launch_pdl(window_attention_tiled_kernel<32>, grid, dim3(kTileThreads), tiled_smem_bytes<32>(),
+                           ctx->stream, qkv, n, (int)c, win, scale, d_scatter, out, ctx->d_status);
+    } else {
+        e = smem_optin((const void*)window_attention_tiled_kernel<64>, ctx->device, optin64);
+        if (e == cudaSuccess)
+            e = launch_pdl(window_attention_tiled_kernel<64>, grid, dim3(kTileThreads), tiled_smem_bytes<64>(),
+                           ctx->stream, qkv, n, (int)c, win, scale, d_scatter, out, ctx->d_status);
+    }
     if (e != cudaSuccess) return cuda_fail(error, error_capacity, e, "window_attention_kernel");
     S3DSP_LAUNCH_CHECK("window_attention_kernel");
     return S3D_OK;
