@@ -637,7 +637,7 @@ def sub_f32(args, rank, world, local_rank, stream, flush):
 # config 5b: one large volume split in Morton slabs, NCCL halo exchange
 # ---------------------------------------------------------------------------
 VOLUME_RES, VOLUME_THICKNESS, VOLUME_C, VOLUME_LAYERS = 512, 4.0, 128, 8  # ~2.5M voxels
-EXCHANGE_SM_RESERVE = 8  # SMs the interior conv leaves to the halo exchange's NCCL kernel
+EXCHANGE_SM_RESERVES = (8, 4)  # SMs the interior conv may leave to the halo exchange's NCCL kernel
 
 
 def sub_volume(args, rank, world, local_rank, stream, flush, steps=None, warmup=None):
@@ -648,7 +648,7 @@ def sub_volume(args, rank, world, local_rank, stream, flush, steps=None, warmup=
     swapped by s3dsp_halo_exchange (one NCCL group of send / receive per
     peer, on a second context and stream), while the rank's interior rows
     (no halo needed) are convolved on a context that leaves
-    EXCHANGE_SM_RESERVE SMs to the exchange; the boundary rows' conv waits
+    some SMs (EXCHANGE_SM_RESERVES) to the exchange; the boundary rows' conv waits
     for the halo. Strong scaling: the volume is fixed, ranks split it.
 
     On-box parity: after timing, layer 0 is recomputed from features that
@@ -683,7 +683,7 @@ def sub_volume(args, rank, world, local_rank, stream, flush, steps=None, warmup=
         torch.distributed.broadcast(uid, 0)
         comm = ctx_x.nccl_comm(world, rank, bytes(uid.cpu().numpy().tobytes()))
         ctx_int.set_sm_limit(max(1, torch.cuda.get_device_properties(local_rank).multi_processor_count
-                                 - EXCHANGE_SM_RESERVE))
+                                 - EXCHANGE_SM_RESERVES[0]))
     h = ctx.hash_build(shard_coords)
     k_int = ctx.kmap_subm3_range(h, 0, ni) if ni > 0 else None
     k_bnd = ctx.kmap_subm3_range(h, ni, n_own) if n_own > ni else None
@@ -704,11 +704,13 @@ def sub_volume(args, rank, world, local_rank, stream, flush, steps=None, warmup=
     setup_s = time.perf_counter() - t_setup
 
     # schedule of a layer at N > 1: "overlap" runs the interior rows' conv on
-    # SMs - EXCHANGE_SM_RESERVE beside the exchange; "serial" runs the exchange
-    # first and the interior conv on every SM (better where the exchange is
-    # short: 0.03 ms at 2 GPUs against a 5 % slower conv). Both are timed after
-    # the warm-up and the faster one (max over ranks) is kept.
-    sched = {"overlap": True}
+    # SMs - reserve beside the exchange (reserve in EXCHANGE_SM_RESERVES);
+    # "serial" runs the exchange first and the interior conv on every SM
+    # (better where the exchange is short: 0.03 ms at 2 GPUs against a 5 %
+    # slower conv). All are timed after the warm-up and the fastest (max over
+    # ranks) is kept.
+    sched = {"overlap": True, "reserve": EXCHANGE_SM_RESERVES[0]}
+    n_sms = torch.cuda.get_device_properties(local_rank).multi_processor_count
 
     def layer(cur, nxt, li, e=None, conv_flags=0):
         ready = torch.cuda.Event()
@@ -769,8 +771,11 @@ def sub_volume(args, rank, world, local_rank, stream, flush, steps=None, warmup=
     xstream.synchronize()
     calib = {}
     if comm is not None:
-        for mode in (True, False):
+        modes = [(True, r) for r in EXCHANGE_SM_RESERVES] + [(False, 0)]
+        for mode, reserve in modes:
             sched["overlap"] = mode
+            sched["reserve"] = reserve
+            ctx_int.set_sm_limit(max(1, n_sms - reserve) if mode else 0)
             step()  # one untimed pass in this schedule
             stream.synchronize()
             xstream.synchronize()
@@ -784,8 +789,11 @@ def sub_volume(args, rank, world, local_rank, stream, flush, steps=None, warmup=
             xstream.synchronize()
             t = torch.tensor([c0.elapsed_time(c1) / 2], dtype=torch.float64, device=device)
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-            calib["overlap" if mode else "serial"] = t.item()
-        sched["overlap"] = calib["overlap"] <= calib["serial"]
+            calib[f"overlap, SMs - {reserve}" if mode else "serial"] = t.item()
+        best = min(range(len(modes)), key=lambda i: list(calib.values())[i])
+        sched["overlap"], sched["reserve"] = modes[best]
+        ctx_int.set_sm_limit(max(1, n_sms - sched["reserve"]) if sched["overlap"] else 0)
+        kernel = (ctx_int if sched["overlap"] else ctx).conv_kernel(max(ni, 1), 27, c, c, P)
     if world > 1:
         torch.distributed.barrier()
     sampler = ClockSampler(local_rank)
@@ -850,7 +858,7 @@ def sub_volume(args, rank, world, local_rank, stream, flush, steps=None, warmup=
                                f"{VOLUME_LAYERS} subm conv layers (+SiLU), Morton slabs + C-ABI NCCL halo exchange",
                    "voxels": n, "parallelism": f"morton-slabs{world}", "conv_kernel_interior": kernel,
                    "interior_conv_sms": "all" if comm is None or not sched["overlap"]
-                   else f"SMs - {EXCHANGE_SM_RESERVE}",
+                   else f"SMs - {sched['reserve']}",
                    "schedule": "one GPU" if comm is None else
                    ("overlap: interior conv beside the exchange" if sched["overlap"]
                     else "serial: exchange, then the interior conv on every SM"),
