@@ -91,6 +91,8 @@ typedef struct s3dsp_shard s3dsp_shard;
                                             sums in distributed shared memory */
 #define S3DSP_CONV_CTA_PAIR UINT32_C(4)  /* BF16: tcgen05 CTA pairs (256-row MMA over two tiles) instead of
                                           one CTA per 128-row tile; same results, slower on B200 today */
+#define S3DSP_CONV_HALO UINT32_C(256)    /* BF16: force the per-tile input halo kernel (one source, cin <= 256,
+                                            cout <= 128, kvol <= 27; other layers ignore the flag) */
 
 /* context flags */
 #define S3DSP_CONTEXT_DEFERRED_CHECKS UINT32_C(1) /* device-detected input errors are reported by
@@ -529,11 +531,16 @@ S3DSP_API s3d_status s3dsp_conv_concat(s3dsp_context *ctx, const s3dsp_kmap *kma
 
 /* Name of the kernel s3dsp_conv launches for this shape on ctx's device
  * ("conv_f32_kernel", "conv_tc_kernel" = 128-row tiles, "conv_sk_kernel<256>"
- * / "conv_sk_kernel<128>" = stream-K over 256- / 128-row tiles), or NULL for
- * a NULL ctx / unknown precision. No reference counterpart: a query for
- * profiling and tests. */
+ * / "conv_sk_kernel<128>" = stream-K over 256- / 128-row tiles,
+ * "conv_sk_kernel<256>:pairs" = split-K CTA pairs, "conv_halo_kernel" =
+ * 128-row tiles with per-tile input halos), or NULL for a NULL ctx / unknown
+ * precision. s3dsp_conv_kernel is the in_shift = 0 form (the halo kernel's
+ * choice depends on in_shift: a subdivide conv reads few distinct parents).
+ * No reference counterpart: a query for profiling and tests. */
 S3DSP_API const char *s3dsp_conv_kernel(const s3dsp_context *ctx, int64_t n_out, int32_t kvol, int64_t cin,
                                         int64_t cout, uint32_t precision, uint32_t flags);
+S3DSP_API const char *s3dsp_conv_kernel_shift(const s3dsp_context *ctx, int64_t n_out, int32_t kvol, int64_t cin,
+                                              int64_t cout, int32_t in_shift, uint32_t precision, uint32_t flags);
 
 /* ---------------------------------------------------------------------------
  * Normalisations (sparse_group_norm mesh_decoder_graph.cpp:16-30;

@@ -18,15 +18,27 @@ namespace {
 // for 128-row tiles), stream-K for wide layers and for a thin last wave
 // (155 tiles: 2 waves vs ~1.35). Maps with few offsets (linear layers)
 // always use 128-row tiles.
-enum class Bf16Kernel { kTile128, kStreamK128, kStreamK256, kSplit256 };
+enum class Bf16Kernel { kTile128, kStreamK128, kStreamK256, kSplit256, kHalo };
 
-Bf16Kernel pick_bf16_kernel(const s3dsp_context* ctx, int64_t n_out, int32_t kvol, int64_t cout, uint32_t flags) {
+// halo: the one-source layers the per-tile halo kernel takes (cin <= 256,
+// cout <= 128 in one column tile, kvol <= 27)
+Bf16Kernel pick_bf16_kernel(const s3dsp_context* ctx, int64_t n_out, int32_t kvol, int64_t cin, int64_t cout,
+                            int in_shift, bool two_sources, uint32_t flags) {
+    int hs = 0, hc = 0, hp = 0;
+    const bool halo_ok = !two_sources && kvol > 1 && cin <= 256 && cout <= 128 &&
+                         conv_halo_plan((int)cin, (int)cout, kvol, in_shift, &hs, &hc, &hp);
+    if ((flags & S3DSP_CONV_HALO) && halo_ok) return Bf16Kernel::kHalo;
     if (flags & (S3DSP_CONV_TILE128 | S3DSP_CONV_CTA_PAIR)) return Bf16Kernel::kTile128;
     if (flags & S3DSP_CONV_STREAM_K128) return Bf16Kernel::kStreamK128;
     if (flags & S3DSP_CONV_STREAM_K) return Bf16Kernel::kStreamK256;
     if (flags & S3DSP_CONV_SPLIT_PAIRS) return Bf16Kernel::kSplit256;
     if (kvol < 8) return Bf16Kernel::kTile128;
     const int64_t sm = ctx->sm_count;
+    // layers of at most 64 output channels whose halo fits two CTAs per SM, at
+    // least one wave of 128-row tiles: the halo kernel (B200, twice-subdivided
+    // 64^3 shell: C = 64 at 970k rows 852 vs 1,150 us for stream-K, the
+    // 128 -> 64 subdivide conv 1,287 vs 1,572 us; 121k rows 125 vs 151 us)
+    if (halo_ok && hp == 2 && cout <= 64 && (n_out + 127) / 128 >= sm) return Bf16Kernel::kHalo;
     const int64_t nnb = ((cout + 15) / 16 * 16) / tc_pick_bn((int)cout);  // column blocks
     const int64_t tiles = (n_out + 127) / 128 * nnb;
     const int64_t work = (n_out + 255) / 256 * nnb;  // 256-row work tiles
@@ -41,20 +53,26 @@ const char* bf16_kernel_name(Bf16Kernel k) {
     return k == Bf16Kernel::kTile128      ? "conv_tc_kernel"
            : k == Bf16Kernel::kStreamK128 ? "conv_sk_kernel<128>"
            : k == Bf16Kernel::kSplit256   ? "conv_sk_kernel<256>:pairs"
+           : k == Bf16Kernel::kHalo       ? "conv_halo_kernel"
                                           : "conv_sk_kernel<256>";
 }
 
 }  // namespace
 
-extern "C" S3DSP_API const char* s3dsp_conv_kernel(const s3dsp_context* ctx, int64_t n_out, int32_t kvol, int64_t cin,
-                                                   int64_t cout, uint32_t precision, uint32_t flags) {
-    (void)cin;
-    if (!ctx) return nullptr;
+extern "C" S3DSP_API const char* s3dsp_conv_kernel_shift(const s3dsp_context* ctx, int64_t n_out, int32_t kvol,
+                                                         int64_t cin, int64_t cout, int32_t in_shift,
+                                                         uint32_t precision, uint32_t flags) {
+    if (!ctx || in_shift < 0 || in_shift > 8) return nullptr;
     if (precision == S3DSP_PREC_F32_STRICT) return "conv_f32_kernel";
     if (precision == S3DSP_PREC_F32_3XTF32) return "conv_tc_kernel<tf32x3>";
     if (precision != S3DSP_PREC_BF16) return nullptr;
     if (cout <= 0) return nullptr;
-    return bf16_kernel_name(pick_bf16_kernel(ctx, n_out, kvol, cout, flags));
+    return bf16_kernel_name(pick_bf16_kernel(ctx, n_out, kvol, cin, cout, in_shift, false, flags));
+}
+
+extern "C" S3DSP_API const char* s3dsp_conv_kernel(const s3dsp_context* ctx, int64_t n_out, int32_t kvol, int64_t cin,
+                                                   int64_t cout, uint32_t precision, uint32_t flags) {
+    return s3dsp_conv_kernel_shift(ctx, n_out, kvol, cin, cout, 0, precision, flags);
 }
 
 namespace {
@@ -128,8 +146,12 @@ s3d_status conv_impl(s3dsp_context* ctx, const s3dsp_kmap* kmap, int32_t kvol, u
             return fail(error, error_capacity, S3D_INVALID_ARGUMENT,
                         "BF16 needs cin %% 8 == 0 (each source) and 16-byte aligned in/weight/out/residual");
         s3d_status st = S3D_OK;
-        const Bf16Kernel kern = pick_bf16_kernel(ctx, n_out, kvol, cout, flags);
-        if (kern == Bf16Kernel::kTile128)
+        const Bf16Kernel kern = pick_bf16_kernel(ctx, n_out, kvol, cin, cout, in_shift, in_b != nullptr, flags);
+        if (kern == Bf16Kernel::kHalo)
+            e = launch_conv_halo(ctx, kmap, kvol, (const __nv_bfloat16*)in, (int)cin, in_shift,
+                                 (const __nv_bfloat16*)weight, bias, residual, res_dtype, res_shift, out, out_dtype,
+                                 n_out, (int)cout, flags, gn_partials, gn_groups, error, error_capacity, &st);
+        else if (kern == Bf16Kernel::kTile128)
             e = launch_conv_tc(ctx, kmap, kvol, (const __nv_bfloat16*)in, (const __nv_bfloat16*)in_b, ca, n_in,
                                (int)cin, in_shift, (const __nv_bfloat16*)weight, bias, residual, res_dtype, res_shift,
                                out, out_dtype, n_out, (int)cout, flags, gn_partials, gn_groups, error,

@@ -216,5 +216,13 @@ cudaError_t launch_conv_sk(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol,
                            int64_t n_out, int cout, uint32_t flags, double* gn_partials,
                            int gn_groups, int rows, int csplit, char* error, uint64_t error_capacity,
                            s3d_status* st);
+// per-tile input halos (one source, cin <= 256, cout <= 128): the plan for a
+// layer (false: the kernel does not take it), and the launch
+bool conv_halo_plan(int cin, int cout, int kvol, int in_shift, int* stages, int* halo_cap, int* per_sm);
+cudaError_t launch_conv_halo(s3dsp_context* ctx, const s3dsp_kmap* kmap, int kvol, const __nv_bfloat16* in, int cin,
+                             int in_shift, const __nv_bfloat16* w, const float* bias, const void* residual,
+                             uint32_t res_dtype, int res_shift, void* out, uint32_t out_dtype, int64_t n_out, int cout,
+                             uint32_t flags, double* gn_partials, int gn_groups, char* error, uint64_t error_capacity,
+                             s3d_status* st);
 
 }  // namespace s3dsp

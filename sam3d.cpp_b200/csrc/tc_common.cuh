@@ -444,7 +444,7 @@ __device__ __forceinline__ void writeout_generic(const P& p, const float* stage_
 
 // Phase 2 of a 128-row tile's epilogue, run by kWarps warps after the
 // accumulator was staged as f32 rows of `ostride` floats at the start of
-// `smem` (phase 1): warp w writes rows 8w .. 8w+7, lane l owns columns
+// `smem` (phase 1): warp w writes the 128 / kWarps rows from (128 / kWarps) * w, lane l owns columns
 // 4l + 128q; bias, residual (row r >> res_shift), SiLU / GELU and the
 // GroupNorm column sums are applied on the way out. The f64 column-sum table
 // [kWarps][bn][2] follows the staged tile. gn_slot: this tile's GroupNorm
@@ -472,8 +472,9 @@ __device__ __forceinline__ void tile_writeout(const P& p, uint8_t* smem, int ost
             bias4[q].w = col + 3 < p.cout ? __ldg(p.bias + col + 3) : 0.f;
         }
     }
-    const int lane_base = 8 * warp;
-    const int nrows = (int)max((int64_t)0, min((int64_t)8, p.n_out - (m0 + lane_base)));
+    constexpr int kRowsPerWarp = 128 / kWarps;
+    const int lane_base = kRowsPerWarp * warp;
+    const int nrows = (int)max((int64_t)0, min((int64_t)kRowsPerWarp, p.n_out - (m0 + lane_base)));
     const uint32_t so_base = smem_u32(stage_out);
     // [kWarps][bn][2]: may run past the rings (the kernels size region 0 for it)
     double* colp = reinterpret_cast<double*>(smem + (size_t)128 * ostride * 4);

@@ -26,6 +26,7 @@ LAYOUT_SLAT_ROW, LAYOUT_MESH_PACKED, LAYOUT_LINEAR, LAYOUT_SPCONV_1X1, LAYOUT_TR
 SENTINEL_SLAT_N, SENTINEL_MESH_NEG1 = 0, 1
 EPI_SILU, PRO_AFFINE_SILU, CONV_CTA_PAIR, CONV_TILE128, CONV_STREAM_K, CONV_STREAM_K128, EPI_GELU = 1, 2, 4, 8, 16, 32, 64
 CONV_SPLIT_PAIRS = 128
+CONV_HALO = 256
 CONTEXT_DEFERRED_CHECKS = 1
 CONTEXT_OWN_STREAM = 2
 
@@ -45,7 +46,7 @@ EXPORTED = [
     "s3dsp_kmap_build_subm3", "s3dsp_kmap_build_subm3_rows", "s3dsp_kmap_build_subm3_range", "s3dsp_subdivide", "s3dsp_kmap_free",
     "s3dsp_kmap_rows", "s3dsp_kmap_export_dense", "s3dsp_kmap_pairs", "s3dsp_kmap_pairs_noalloc",
     "s3dsp_weights_packed_bytes", "s3dsp_weights_pack", "s3dsp_gn_partials_count", "s3dsp_conv", "s3dsp_conv_concat",
-    "s3dsp_conv_kernel", "s3dsp_layer_norm_concat", "s3dsp_kmap_compose", "s3dsp_slat_res_block_concat",
+    "s3dsp_conv_kernel", "s3dsp_conv_kernel_shift", "s3dsp_layer_norm_concat", "s3dsp_kmap_compose", "s3dsp_slat_res_block_concat",
     "s3dsp_gn_stats", "s3dsp_gn_finalize", "s3dsp_channel_affine", "s3dsp_layer_norm",
     "s3dsp_convert", "s3dsp_slat_tables_build", "s3dsp_slat_tables_free", "s3dsp_slat_tables_coarse_rows",
     "s3dsp_slat_tables_coarse_kmap", "s3dsp_slat_tables_export", "s3dsp_slat_downsample", "s3dsp_slat_upsample",
@@ -155,6 +156,7 @@ def load(path: str = LIB_PATH):
         "s3dsp_weights_pack": (_u32, [_vp, _vp, _u32, _i32, _u32, _i32, _i64, _i64, _u32, _vp, _cp, _u64]),
         "s3dsp_gn_partials_count": (_i64, [_i64, _i64, _i32]),
         "s3dsp_conv_kernel": (_cp, [_vp, _i64, _i32, _i64, _i64, _u32, _u32]),
+        "s3dsp_conv_kernel_shift": (_cp, [_vp, _i64, _i32, _i64, _i64, _i32, _u32, _u32]),
         "s3dsp_conv": (_u32, [_vp, _vp, _i32, _u32, _vp, _u32, _i64, _i64, _i32, _vp, _vp, _vp, _u32, _i32,
                               _vp, _u32, _i64, _i64, _u32, _vp, _vp, _vp, _vp, _i32, _cp, _u64]),
         "s3dsp_conv_concat": (_u32, [_vp, _vp, _i32, _u32, _vp, _i64, _vp, _i64, _u32, _i64, _i32, _vp, _vp, _vp,
@@ -682,9 +684,10 @@ class Context:
               precision, ptr(dst))
 
     # ---- conv ------------------------------------------------------------
-    def conv_kernel(self, n_out: int, kvol: int, cin: int, cout: int, precision: int, flags: int = 0) -> str:
+    def conv_kernel(self, n_out: int, kvol: int, cin: int, cout: int, precision: int, flags: int = 0,
+                    in_shift: int = 0) -> str:
         """Name of the kernel s3dsp_conv launches for this shape."""
-        name = load().s3dsp_conv_kernel(self.handle, n_out, kvol, cin, cout, precision, flags)
+        name = load().s3dsp_conv_kernel_shift(self.handle, n_out, kvol, cin, cout, in_shift, precision, flags)
         return name.decode() if name else ""
 
     def conv(self, kmap: Kmap | None, kvol: int, precision: int, x, weight, bias, out, cout: int,
