@@ -78,6 +78,8 @@ def same(a, b):
     (96, 48, 32, 3, None),     # a half-filled second chunk, 48 columns
     (256, 128, 24, 4, None),   # four chunks
     (192, 100, 20, 5, None),   # ragged cout (112 padded columns), generic write-out
+    (192, 42, 20, 5, None),    # ragged cout (48 padded columns), two CTAs per SM
+    (256, 64, 24, 4, None),    # four chunks, 64 columns
     (64, 16, 8, 6, None),      # a handful of rows (one partial tile)
 ])
 def test_halo_matches_tile128_and_oracle(ctx, cin, cout, res, seed, shuffle):
@@ -174,3 +176,31 @@ def test_halo_kernel_choice(ctx):
     assert ctx.conv_kernel(15159, 27, 256, 256, P, H) == "conv_sk_kernel<256>:pairs"
     assert ctx.conv_kernel(15159, 27, 320, 64, P, H) != "conv_halo_kernel"
     assert ctx.conv_kernel(15159, 1, 64, 64, P, H) == "conv_tc_kernel"
+
+
+@pytest.mark.parametrize("cin,in_shift", [(64, 0), (128, 3)])
+def test_halo_auto_on_subdivided_level(ctx, cin, in_shift):
+    """A subdivided 64^3 shell (~121k rows, ~950 tiles): the automatic choice
+    takes the halo kernel for the C = 64 conv and the 128 -> 64 subdivide conv;
+    with GroupNorm partials and SiLU, the outputs match the 128-row kernel
+    (bit for bit with one channel chunk)."""
+    parents = workloads.ellipsoid_shell(64, 12)
+    hp = ctx.hash_build(dev(parents), reject_duplicates=True)
+    cc = torch.empty((8 * len(parents), 4), dtype=torch.int32, device="cuda")
+    k = ctx.subdivide(hp, cc)
+    n_out = 8 * len(parents)
+    n_in = len(parents) if in_shift else n_out
+    cout = 64
+    assert ctx.conv_kernel(n_out, 27, cin, cout, s3dsp.PREC_BF16, in_shift=in_shift) == "conv_halo_kernel"
+    x = dev(workloads.normal((n_in, cin), 60)).to(torch.bfloat16)
+    w = pack(ctx, workloads.conv_weight_slat(cin, cout, 61), s3dsp.LAYOUT_SLAT_ROW, 27, cin, cout)
+    b = dev(workloads.normal((cout,), 62, 0.1))
+    kw = dict(in_shift=in_shift, gn=True, epi=s3dsp.EPI_SILU)
+    auto = run(ctx, k, x, w, b, cout, n_out, 0, reps=2, **kw)
+    t128 = run(ctx, k, x, w, b, cout, n_out, s3dsp.CONV_TILE128, reps=1, **kw)
+    assert same(auto[0], auto[1]), "halo kernel not deterministic"
+    if cin <= 64:
+        assert np.array_equal(auto[0][0], t128[0][0])
+    else:
+        gate(rel_l2(auto[0][0], t128[0][0]), ORDER_TOL)
+    gate(rel_l2(auto[0][1], t128[0][1]), ORDER_TOL)
