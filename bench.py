@@ -48,6 +48,7 @@ for sub in ("sam3d.cpp_b200", "oracle"):
 METRIC = "active-voxel outputs/s, all GPUs (C=256 subm conv residual block)"
 UNIT = "voxel-outputs/s"
 L2_FLUSH_BYTES = 512 << 20  # > 126 MB L2
+E2E_FLUSH_BYTES = 256 << 20  # twice the L2: the flush inside the e2e timed region
 # DRAM bytes (read + write) per launch, from one ncu capture of
 # `python bench.py --profile-case conv2` (128-row kernel) and of
 # `--profile-case conv2_pairs` (the dispatched split-K pair kernel), keyed by
@@ -285,6 +286,18 @@ class L2Flush:
         self.t.sum(self.r, dim=0, out=self.acc)
 
 
+class L2WriteFlush:
+    """One write of a buffer twice the size of L2: evicts everything a call
+    touched. Used inside the e2e timed region, where the write-backs of the
+    dirty lines it leaves are charged to the call that follows it."""
+
+    def __init__(self, torch, device):
+        self.w = torch.empty(E2E_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+
+    def __call__(self):
+        self.w.fill_(1.0)
+
+
 def time_graphs(torch, stream, path, flush, steps, warmup, n_marks):
     """Captures `path.step` twice (plain, and with events between its phases),
     replays warm-up rounds, then times `steps` plain replays (the L2 flushed
@@ -390,6 +403,59 @@ def e2e_queued(s3dsp, torch, device, main_stream, queued_call, ref_out, steps, w
     return start.elapsed_time(final), per * E2E_STREAMS, issue_ms
 
 
+def e2e_piped(s3dsp, torch, device, main_stream, queued_call, ref_out, steps, warmup, flush):
+    """Device time of `steps` host-buffer calls queued by one host thread on
+    one context with copy streams (CONTEXT_COPY_STREAMS): a call's upload runs
+    on the context's copy-in stream, its tables and block on the context's
+    stream, its download on the copy-out stream, so successive calls overlap
+    (the library's three staging slots). Each call is preceded on the
+    context's stream by the L2 flush, inside the timed region. The span runs
+    from one start event (the context forked after it) to the end of the last
+    download (the context joined before the end event). Both host outputs the
+    calls alternate between must equal `ref_out` bit for bit. Returns (ms,
+    calls timed, host issue ms)."""
+    st = torch.cuda.Stream(device)
+    cx = s3dsp.Context(device.index, stream=st.cuda_stream,
+                       flags=s3dsp.CONTEXT_DEFERRED_CHECKS | s3dsp.CONTEXT_COPY_STREAMS)
+    outs = [torch.empty_like(ref_out).pin_memory() for _ in range(2)]
+
+    def issue(i):
+        with torch.cuda.stream(st):
+            flush()
+        queued_call(cx, outs[i % 2])
+
+    # warm-up as in e2e_queued: at least `warmup` calls and two seconds of traffic
+    t_end = time.perf_counter() + 2.0
+    i = 0
+    while i < max(8, warmup) or time.perf_counter() < t_end:
+        issue(i)
+        i += 1
+        if i % 8 == 0:
+            cx.check()
+    cx.check()
+    start = torch.cuda.Event(enable_timing=True)
+    final = torch.cuda.Event(enable_timing=True)
+    start.record(main_stream)
+    st.wait_event(start)
+    cx.fork()
+    t_issue = time.perf_counter()
+    for i in range(steps):
+        issue(i)
+    issue_ms = (time.perf_counter() - t_issue) * 1e3
+    cx.join()
+    ev = torch.cuda.Event()
+    ev.record(st)
+    main_stream.wait_event(ev)
+    final.record(main_stream)
+    main_stream.synchronize()
+    cx.check()
+    for o in outs:
+        if not torch.equal(o, ref_out):
+            raise RuntimeError("a copy-stream host call's output differs from the synchronous call's")
+    cx.close()
+    return start.elapsed_time(final), steps, issue_ms
+
+
 def gather_rows(torch, world, values):
     """Every rank's list of floats, on every rank ([world][len])."""
     t = torch.tensor(values, dtype=torch.float64, device="cuda")
@@ -487,24 +553,29 @@ def run_ours(args, rank, world, local_rank):
         cx.res_block_gn_host_queued(s3dsp.PREC_BF16, coords_h, x_h, path.w1, path.b1, path.gamma, path.beta,
                                     path.w2, path.b2, out)
 
-    pipe_ms, pipe_steps, issue_ms = e2e_queued(s3dsp, torch, device, stream, queued_call, out_h, args.steps, args.warmup,
-                                     flush)
+    e2e_flush = L2WriteFlush(torch, device)
+    lanes_ms, lanes_steps, lanes_issue_ms = e2e_queued(s3dsp, torch, device, stream, queued_call, out_h, args.steps,
+                                                       args.warmup, e2e_flush)
+    pipe_ms, pipe_steps, issue_ms = e2e_piped(s3dsp, torch, device, stream, queued_call, out_h, args.steps,
+                                              args.warmup, e2e_flush)
     clocks = sampler.stop()
     h2d = coords_h.numel() * 4 + x_h.numel() * 4
     d2h = out_h.numel() * 4
     ctx.check()
     per_rank = gather_rows(torch, world, [dev_ms / args.steps, copy_ms, serial_ms / args.steps,
-                                          pipe_ms / pipe_steps, float(E2E_STREAMS), float(n_cpus),
+                                          lanes_ms / lanes_steps, float(E2E_STREAMS), float(n_cpus),
+                                          lanes_issue_ms / lanes_steps, pipe_ms / pipe_steps,
                                           issue_ms / pipe_steps])
 
     # max over ranks
-    vals = torch.tensor([dev_ms, serial_ms, pipe_ms], dtype=torch.float64, device=device)
-    units = torch.tensor([2.0 * n * args.steps, 2.0 * n * pipe_steps], dtype=torch.float64, device=device)
+    vals = torch.tensor([dev_ms, serial_ms, pipe_ms, lanes_ms], dtype=torch.float64, device=device)
+    units = torch.tensor([2.0 * n * args.steps, 2.0 * n * pipe_steps, 2.0 * n * lanes_steps], dtype=torch.float64,
+                         device=device)
     if world > 1:
         torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX)
         torch.distributed.all_reduce(units, op=torch.distributed.ReduceOp.SUM)
-    dev_ms, serial_ms, pipe_ms = vals.tolist()
-    total_units, pipe_units = units.tolist()
+    dev_ms, serial_ms, pipe_ms, lanes_ms = vals.tolist()
+    total_units, pipe_units, lanes_units = units.tolist()
 
     line = None
     if rank == 0:
@@ -529,25 +600,32 @@ def run_ours(args, rank, world, local_rank):
                        "timing": "device steps replayed as a CUDA graph of the library calls (the breakdown and "
                                  "the roofline's conv time from a second capture with events between the phases); "
                                  "e2e = the host-buffer block entry point (host coords and features in, result out) "
-                                 "per step, queued round-robin over several streams by one host thread (the "
-                                 "synchronous one-call-at-a-time figure beside it)"},
+                                 "per step, queued by one host thread on a context with copy streams (the "
+                                 "round-robin over several contexts and the synchronous one-call-at-a-time "
+                                 "figures beside it)"},
             "roofline": roof,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": pipe_ms / pipe_steps,
-                    "mode": f"per rank: one host thread (pinned to its GPU's NUMA node) issuing "
-                            f"s3dsp_res_block_gn_host_queued round-robin over {E2E_STREAMS} contexts (one stream "
-                            "each), so one call's copies overlap another's kernels; L2 flushed on the calling "
-                            "stream before every call (inside the timed region); device-timed from one start "
-                            "event to the last call's end; max over ranks. serial_* = the synchronous "
+                    "mode": "per rank: one host thread (pinned to its GPU's NUMA node) issuing "
+                            "s3dsp_res_block_gn_host_queued on one context with S3DSP_CONTEXT_COPY_STREAMS "
+                            "(uploads on its copy-in stream, tables and block on its stream, downloads on its "
+                            "copy-out stream: one call's upload, the next one's kernels and the previous one's "
+                            "download overlap); L2 flushed on the context's stream before every call (a 256 MiB "
+                            "write, inside the timed region); device-timed from one start event to the last "
+                            "download's end; max over ranks. lanes_* = the same calls round-robin over "
+                            f"{E2E_STREAMS} contexts of one stream each; serial_* = the synchronous "
                             "s3dsp_res_block_gn_host, one call at a time",
-                    "steps": pipe_steps, "serial_value": total_units / (serial_ms / 1e3),
+                    "steps": pipe_steps, "lanes_value": lanes_units / (lanes_ms / 1e3),
+                    "lanes_ms_per_step": lanes_ms / lanes_steps,
+                    "serial_value": total_units / (serial_ms / 1e3),
                     "serial_ms_per_step": serial_ms / args.steps,
                     "per_rank_ms": [{"rank": r, "device_step": v[0], "copies_only": v[1], "call_serial": v[2],
-                                     "call_queued": v[3], "streams": int(v[4]), "cpus": int(v[5]),
-                                     "host_issue_per_call": v[6]}
+                                     "call_lanes": v[3], "lanes": int(v[4]), "cpus": int(v[5]),
+                                     "host_issue_per_call_lanes": v[6], "call_copy_streams": v[7],
+                                     "host_issue_per_call": v[8]}
                                     for r, v in enumerate(per_rank)]},
-            # inside the timed regions: both graphs' replays, serial host calls, worker calls
-            "gpu_launches": path.launches_per_step * (3 * args.steps + pipe_steps),
+            # inside the timed regions: both graphs' replays, serial host calls, e2e calls
+            "gpu_launches": path.launches_per_step * (3 * args.steps + lanes_steps + pipe_steps),
             "clocks": clocks,
             "wall_s": wall,
             "breakdown_ms": breakdown,

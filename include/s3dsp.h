@@ -98,6 +98,9 @@ typedef struct s3dsp_shard s3dsp_shard;
 #define S3DSP_CONTEXT_DEFERRED_CHECKS UINT32_C(1) /* device-detected input errors are reported by
                                                      s3dsp_context_check instead of at each call */
 #define S3DSP_CONTEXT_OWN_STREAM UINT32_C(2)      /* create (and own) a new non-blocking stream */
+#define S3DSP_CONTEXT_COPY_STREAMS UINT32_C(4)    /* the context also owns a copy-in and a copy-out
+                                                     stream for its host-buffer calls (see
+                                                     s3dsp_context_fork / s3dsp_context_join) */
 
 S3DSP_API uint32_t s3dsp_abi_version(void);
 
@@ -120,9 +123,29 @@ S3DSP_API void *s3dsp_context_stream(const s3dsp_context *ctx);
  * reference (one stream per Backend). */
 S3DSP_API s3d_status s3dsp_context_set_sm_limit(s3dsp_context *ctx, int32_t sms, char *error,
                                                 uint64_t error_capacity);
-/* Waits for the stream and reports (then clears) any device-detected input
- * error recorded since the last check. */
+/* Waits for the stream (and, with S3DSP_CONTEXT_COPY_STREAMS, the copy
+ * streams) and reports (then clears) any device-detected input error
+ * recorded since the last check. */
 S3DSP_API s3d_status s3dsp_context_check(s3dsp_context *ctx, char *error, uint64_t error_capacity);
+/* Copy streams (S3DSP_CONTEXT_COPY_STREAMS). Such a context runs the
+ * host-buffer entry points (s3dsp_res_block_gn_host and its queued form) over
+ * three streams: the host -> device copies on its copy-in stream, the tables
+ * and kernels on its stream, the device -> host copy on its copy-out stream,
+ * through a ring of three staging slots that the context keeps (device
+ * memory from the library pool, sized by the largest call so far, freed with
+ * the context). Successive queued calls then overlap one call's upload, the
+ * next one's kernels and the previous one's download; on PCIe the two copy
+ * directions run at the same time. s3dsp_context_fork orders the copy
+ * streams after everything queued on the context's stream so far (call it
+ * before queued calls whose host inputs earlier stream work produces);
+ * s3dsp_context_join orders the context's stream after everything queued on
+ * the copy streams so far (an event recorded on the stream after a join, or
+ * s3dsp_context_check, then covers every queued call's read-back). Without
+ * the flag both return S3D_OK and do nothing. No counterpart in the
+ * reference (its Backend::run copies and computes on one queue,
+ * backend.hpp:16-92). */
+S3DSP_API s3d_status s3dsp_context_fork(s3dsp_context *ctx, char *error, uint64_t error_capacity);
+S3DSP_API s3d_status s3dsp_context_join(s3dsp_context *ctx, char *error, uint64_t error_capacity);
 
 /* Device buffers for a host that links only this library (the counterpart of
  * the reference's Backend::alloc / set_input_f32 / set_input_i32 /
@@ -691,8 +714,11 @@ S3DSP_API s3d_status s3dsp_res_block_gn_host(s3dsp_context *ctx, uint32_t precis
  * errors are read by s3dsp_context_check). The host buffers must stay valid
  * until then; pinned host memory lets the copies of one call overlap another
  * context's kernels, which is how one host thread keeps several contexts
- * busy. No counterpart in the reference (its Backend::run is synchronous,
- * backend.hpp:16-92). */
+ * busy. On a context with S3DSP_CONTEXT_COPY_STREAMS the copies run on the
+ * context's copy streams instead, and h_out holds the result once the
+ * copy-out stream gets there (s3dsp_context_join, then the stream; or
+ * s3dsp_context_check). No counterpart in the reference (its Backend::run is
+ * synchronous, backend.hpp:16-92). */
 S3DSP_API s3d_status s3dsp_res_block_gn_host_queued(s3dsp_context *ctx, uint32_t precision,
                                                     const int32_t *h_coords, int64_t n, const float *h_x,
                                                     int64_t c, const void *w1, const float *b1,

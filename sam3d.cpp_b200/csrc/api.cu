@@ -91,6 +91,28 @@ extern "C" S3DSP_API s3d_status s3dsp_context_create(int32_t device, void* strea
         s3dsp_context_free(ctx);
         return cuda_fail(error, error_capacity, e, "status buffer");
     }
+    if (flags & S3DSP_CONTEXT_COPY_STREAMS) {
+        // two more non-blocking streams and the slot events; the slots' device
+        // buffers are allocated by the first call that uses each slot
+        ctx->pipe = new (std::nothrow) s3dsp_host_pipe();
+        if (!ctx->pipe) {
+            s3dsp_context_free(ctx);
+            return fail(error, error_capacity, S3D_OUT_OF_MEMORY, "context allocation");
+        }
+        s3dsp_host_pipe* p = ctx->pipe;
+        e = cudaStreamCreateWithFlags(&p->copy_in, cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&p->copy_out, cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->order, cudaEventDisableTiming);
+        for (auto& s : p->slots) {
+            if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s.in_done, cudaEventDisableTiming);
+            if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s.comp_done, cudaEventDisableTiming);
+            if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s.out_done, cudaEventDisableTiming);
+        }
+        if (e != cudaSuccess) {
+            s3dsp_context_free(ctx);
+            return cuda_fail(error, error_capacity, e, "copy streams");
+        }
+    }
     *out = ctx;
     return S3D_OK;
 }
@@ -99,9 +121,62 @@ extern "C" S3DSP_API void s3dsp_context_free(s3dsp_context* ctx) {
     if (!ctx) return;
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    if (s3dsp_host_pipe* p = ctx->pipe) {
+        if (p->copy_in) cudaStreamSynchronize(p->copy_in);
+        if (p->copy_out) cudaStreamSynchronize(p->copy_out);
+        for (auto& s : p->slots) {
+            // pool memory: freed (and synchronised) on the copy-in stream, which allocated it
+            if (s.d_coords) cudaFreeAsync(s.d_coords, p->copy_in);
+            if (s.d_x) cudaFreeAsync(s.d_x, p->copy_in);
+            if (s.d_out) cudaFreeAsync(s.d_out, p->copy_in);
+            if (s.in_done) cudaEventDestroy(s.in_done);
+            if (s.comp_done) cudaEventDestroy(s.comp_done);
+            if (s.out_done) cudaEventDestroy(s.out_done);
+        }
+        if (p->copy_in) {
+            cudaStreamSynchronize(p->copy_in);
+            cudaStreamDestroy(p->copy_in);
+        }
+        if (p->copy_out) cudaStreamDestroy(p->copy_out);
+        if (p->order) cudaEventDestroy(p->order);
+        delete p;
+    }
     if (ctx->d_status) cudaFree(ctx->d_status);
     if (ctx->owns_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
+}
+
+namespace s3dsp {
+cudaError_t pipe_join(s3dsp_context* ctx) {
+    s3dsp_host_pipe* p = ctx->pipe;
+    if (!p) return cudaSuccess;
+    // one event, recorded and waited on in turn: a wait uses the record made before it
+    cudaError_t e = cudaEventRecord(p->order, p->copy_in);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(ctx->stream, p->order, 0);
+    if (e == cudaSuccess) e = cudaEventRecord(p->order, p->copy_out);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(ctx->stream, p->order, 0);
+    return e;
+}
+}  // namespace s3dsp
+
+extern "C" S3DSP_API s3d_status s3dsp_context_fork(s3dsp_context* ctx, char* error, uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "ctx is NULL");
+    s3dsp_host_pipe* p = ctx->pipe;
+    if (!p) return S3D_OK;
+    S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    S3DSP_CUDA(cudaEventRecord(p->order, ctx->stream), "cudaEventRecord");
+    S3DSP_CUDA(cudaStreamWaitEvent(p->copy_in, p->order, 0), "cudaStreamWaitEvent");
+    S3DSP_CUDA(cudaStreamWaitEvent(p->copy_out, p->order, 0), "cudaStreamWaitEvent");
+    return S3D_OK;
+}
+
+extern "C" S3DSP_API s3d_status s3dsp_context_join(s3dsp_context* ctx, char* error, uint64_t error_capacity) {
+    clear_error(error, error_capacity);
+    if (!ctx) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "ctx is NULL");
+    S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    S3DSP_CUDA(pipe_join(ctx), "join copy streams");
+    return S3D_OK;
 }
 
 extern "C" S3DSP_API void* s3dsp_context_stream(const s3dsp_context* ctx) {
@@ -149,6 +224,7 @@ extern "C" S3DSP_API s3d_status s3dsp_context_check(s3dsp_context* ctx, char* er
     clear_error(error, error_capacity);
     if (!ctx) return fail(error, error_capacity, S3D_INVALID_ARGUMENT, "ctx is NULL");
     S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    S3DSP_CUDA(pipe_join(ctx), "join copy streams");  // the wait then covers the copy streams too
     return check_status(ctx, error, error_capacity);
 }
 

@@ -341,6 +341,65 @@ namespace {
 // host coords + features in, the block, host output out, on the context's
 // stream; `wait` = synchronise and report device-detected errors before
 // returning (the synchronous entry point), else return once queued
+// The host-buffer block on a context with S3DSP_CONTEXT_COPY_STREAMS: staging
+// slot j % 3 for call j; copies in on the copy-in stream, the tables and the
+// block on the context's stream, the copy out on the copy-out stream, so that
+// call j + 1's upload and call j - 1's download run beside call j's kernels.
+// Returns with the work queued.
+s3d_status res_block_gn_host_piped(s3dsp_context* ctx, uint32_t precision, const int32_t* h_coords, int64_t n,
+                                   const float* h_x, int64_t c, const void* w1, const float* b1, const float* gamma,
+                                   const float* beta, const void* w2, const float* b2, int32_t groups, float eps,
+                                   float* h_out, char* error, uint64_t error_capacity) {
+    s3dsp_host_pipe* p = ctx->pipe;
+    s3dsp_host_pipe::Slot& s = p->slots[p->calls % s3dsp_host_pipe::kSlots];
+    const size_t cb = 16 * (size_t)n, xb = 4 * (size_t)(n * c), ob = 4 * (size_t)(n * c);
+    // the slot's previous call must have consumed its inputs before they are overwritten
+    if (s.used) S3DSP_CUDA(cudaStreamWaitEvent(p->copy_in, s.comp_done, 0), "cudaStreamWaitEvent");
+    if (s.coords_bytes < cb || s.x_bytes < xb || s.out_bytes < ob) {
+        // larger buffers: the old ones go once the slot's previous output is copied out
+        if (s.used) S3DSP_CUDA(cudaStreamWaitEvent(p->copy_in, s.out_done, 0), "cudaStreamWaitEvent");
+        void** bufs[3] = {&s.d_coords, &s.d_x, &s.d_out};
+        size_t* have[3] = {&s.coords_bytes, &s.x_bytes, &s.out_bytes};
+        const size_t want[3] = {cb, xb, ob};
+        for (int i = 0; i < 3; ++i) {
+            if (*have[i] >= want[i]) continue;
+            if (*bufs[i]) S3DSP_CUDA(cudaFreeAsync(*bufs[i], p->copy_in), "cudaFreeAsync");
+            *bufs[i] = nullptr;
+            *have[i] = 0;
+            S3DSP_CUDA(s3dsp::malloc_async(bufs[i], want[i], p->copy_in), "staging allocation");
+            *have[i] = want[i];
+        }
+    }
+    S3DSP_CUDA(cudaMemcpyAsync(s.d_coords, h_coords, cb, cudaMemcpyHostToDevice, p->copy_in), "H2D coords");
+    S3DSP_CUDA(cudaMemcpyAsync(s.d_x, h_x, xb, cudaMemcpyHostToDevice, p->copy_in), "H2D features");
+    S3DSP_CUDA(cudaEventRecord(s.in_done, p->copy_in), "cudaEventRecord");
+    S3DSP_CUDA(cudaStreamWaitEvent(ctx->stream, s.in_done, 0), "cudaStreamWaitEvent");
+    // d_out is rewritten only after the slot's previous output has been copied out
+    if (s.used) S3DSP_CUDA(cudaStreamWaitEvent(ctx->stream, s.out_done, 0), "cudaStreamWaitEvent");
+    s3dsp_hash* h = nullptr;
+    s3dsp_kmap* k = nullptr;
+    s3d_status st = s3dsp_hash_build(ctx, static_cast<const int32_t*>(s.d_coords), n, 0, &h, error, error_capacity);
+    if (st == S3D_OK) st = s3dsp_kmap_build_subm3(ctx, h, &k, error, error_capacity);
+    if (st == S3D_OK)
+        st = s3dsp_res_block_gn(ctx, k, precision, static_cast<const float*>(s.d_x), n, c, w1, b1, gamma, beta, w2,
+                                b2, groups, eps, static_cast<float*>(s.d_out), error, error_capacity);
+    s3dsp_kmap_free(ctx, k);
+    s3dsp_hash_free(ctx, h);
+    // the slot's events are recorded whatever happened, so later calls order correctly
+    cudaError_t e = cudaEventRecord(s.comp_done, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(p->copy_out, s.comp_done, 0);
+    if (e == cudaSuccess && st == S3D_OK) {
+        e = cudaMemcpyAsync(h_out, s.d_out, ob, cudaMemcpyDeviceToHost, p->copy_out);
+        if (e != cudaSuccess) st = cuda_fail(error, error_capacity, e, "D2H output");
+    }
+    const cudaError_t e2 = cudaEventRecord(s.out_done, p->copy_out);
+    if (e == cudaSuccess) e = e2;
+    s.used = true;
+    ++p->calls;
+    if (st == S3D_OK && e != cudaSuccess) st = cuda_fail(error, error_capacity, e, "copy-stream ordering");
+    return st;
+}
+
 s3d_status res_block_gn_host_impl(s3dsp_context* ctx, uint32_t precision, const int32_t* h_coords, int64_t n,
                                   const float* h_x, int64_t c, const void* w1, const float* b1, const float* gamma,
                                   const float* beta, const void* w2, const float* b2, int32_t groups, float eps,
@@ -351,6 +410,17 @@ s3d_status res_block_gn_host_impl(s3dsp_context* ctx, uint32_t precision, const 
         return fail(error, error_capacity, S3D_INVALID_ARGUMENT,
                     "the queued form needs a context with S3DSP_CONTEXT_DEFERRED_CHECKS");
     S3DSP_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    if (ctx->pipe) {
+        s3d_status s = res_block_gn_host_piped(ctx, precision, h_coords, n, h_x, c, w1, b1, gamma, beta, w2, b2,
+                                               groups, eps, h_out, error, error_capacity);
+        if (s == S3D_OK && wait) {
+            cudaError_t e = pipe_join(ctx);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+            if (e != cudaSuccess) s = cuda_fail(error, error_capacity, e, "cudaStreamSynchronize");
+            if (s == S3D_OK && (ctx->flags & S3DSP_CONTEXT_DEFERRED_CHECKS)) s = check_status(ctx, error, error_capacity);
+        }
+        return s;
+    }
     Scratch sc(ctx->stream);
     int32_t* d_coords;
     float *d_x, *d_out;

@@ -27,6 +27,28 @@ enum : uint32_t {
     kErrRowRange = 1u << 4,     // a caller-supplied row index outside its table (read as "no row")
 };
 
+// S3DSP_CONTEXT_COPY_STREAMS: the host-buffer pipeline of a context. Call j
+// of the queued host-buffer entry points uses staging slot j % kSlots: its
+// host -> device copies run on copy_in, its kernels on the context's stream,
+// its device -> host copy on copy_out, ordered by the slot's events. A slot
+// is reused three calls later, once its previous inputs are consumed
+// (comp_done) and its previous output copied out (out_done).
+struct s3dsp_host_pipe {
+    static constexpr int kSlots = 3;
+    struct Slot {
+        void* d_coords = nullptr;
+        void* d_x = nullptr;
+        void* d_out = nullptr;
+        size_t coords_bytes = 0, x_bytes = 0, out_bytes = 0;
+        cudaEvent_t in_done = nullptr, comp_done = nullptr, out_done = nullptr;
+        bool used = false;
+    };
+    cudaStream_t copy_in = nullptr, copy_out = nullptr;
+    cudaEvent_t order = nullptr;  // fork / join
+    Slot slots[kSlots];
+    uint64_t calls = 0;
+};
+
 struct s3dsp_context {
     int device = 0;
     cudaStream_t stream = nullptr;
@@ -35,6 +57,7 @@ struct s3dsp_context {
     int sm_count = 0;      // SMs the context's grids are sized for (s3dsp_context_set_sm_limit)
     int sm_device = 0;     // SMs of the device
     uint32_t* d_status = nullptr;  // [4] error bits, duplicate count, ...
+    s3dsp_host_pipe* pipe = nullptr;  // S3DSP_CONTEXT_COPY_STREAMS only
 };
 
 struct s3dsp_hash {
@@ -174,6 +197,10 @@ inline bool dtype_ok(uint32_t dt) { return dt == S3DSP_F32 || dt == S3DSP_BF16 |
     } while (0)
 
 s3d_status check_status(s3dsp_context* ctx, char* error, uint64_t error_capacity);
+
+// Orders the context's stream after everything queued so far on its copy
+// streams (no-op without S3DSP_CONTEXT_COPY_STREAMS).
+cudaError_t pipe_join(s3dsp_context* ctx);
 
 // launch helpers implemented in the .cu files
 //

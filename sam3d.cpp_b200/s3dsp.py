@@ -29,11 +29,12 @@ CONV_SPLIT_PAIRS = 128
 CONV_HALO = 256
 CONTEXT_DEFERRED_CHECKS = 1
 CONTEXT_OWN_STREAM = 2
+CONTEXT_COPY_STREAMS = 4
 
 # every symbol include/s3dsp.h declares (tests check the library exports them)
 EXPORTED = [
     "s3dsp_abi_version", "s3dsp_context_create", "s3dsp_context_free", "s3dsp_context_stream", "s3dsp_context_set_sm_limit",
-    "s3dsp_context_check", "s3dsp_memory_stats", "s3dsp_device_alloc", "s3dsp_device_free", "s3dsp_copy_to_device",
+    "s3dsp_context_check", "s3dsp_context_fork", "s3dsp_context_join", "s3dsp_memory_stats", "s3dsp_device_alloc", "s3dsp_device_free", "s3dsp_copy_to_device",
     "s3dsp_copy_to_host", "s3dsp_hash_build", "s3dsp_hash_free", "s3dsp_hash_size",
     "s3dsp_hash_lookup", "s3dsp_gs_window_tables", "s3dsp_ape", "s3dsp_gather_rows", "s3dsp_window_attention", "s3dsp_flexicubes_tables_create",
     "s3dsp_flexicubes_tables_free", "s3dsp_flexicubes_extract", "s3dsp_mesh_info", "s3dsp_mesh_device", "s3dsp_mesh_copy",
@@ -87,6 +88,8 @@ def load(path: str = LIB_PATH):
         "s3dsp_context_stream": (_vp, [_vp]),
         "s3dsp_context_set_sm_limit": (_u32, [_vp, _i32, _cp, _u64]),
         "s3dsp_context_check": (_u32, [_vp, _cp, _u64]),
+        "s3dsp_context_fork": (_u32, [_vp, _cp, _u64]),
+        "s3dsp_context_join": (_u32, [_vp, _cp, _u64]),
         "s3dsp_device_alloc": (_u32, [_vp, _u64, ctypes.POINTER(_vp), _cp, _u64]),
         "s3dsp_device_free": (None, [_vp, _vp]),
         "s3dsp_copy_to_device": (_u32, [_vp, _vp, _vp, _u64, _cp, _u64]),
@@ -541,6 +544,14 @@ class Context:
 
     def check(self):
         _call(load().s3dsp_context_check, self.handle)
+
+    def fork(self):
+        """CONTEXT_COPY_STREAMS: order the copy streams after the context's stream."""
+        _call(load().s3dsp_context_fork, self.handle)
+
+    def join(self):
+        """CONTEXT_COPY_STREAMS: order the context's stream after its copy streams."""
+        _call(load().s3dsp_context_join, self.handle)
 
     def set_sm_limit(self, sms: int):
         """Size this context's SM-proportional grids for `sms` SMs (0: all)."""

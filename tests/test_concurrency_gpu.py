@@ -111,6 +111,38 @@ def test_queued_host_blocks_round_robin_bit_exact(setup):
             assert torch.equal(o, expected[t]), f"context {t}: queued output differs from the synchronous call's"
 
 
+def test_copy_stream_host_blocks_bit_exact(setup):
+    """A context with copy streams (CONTEXT_COPY_STREAMS) pipelines queued
+    host-buffer blocks over its three staging slots: one call's upload, the
+    next one's kernels and the previous one's download overlap. Objects of
+    four sizes in turn make the slots grow (and then serve smaller calls);
+    after check (which joins the copy streams) every output equals the
+    synchronous call's on a plain context, bit for bit, and so does a
+    synchronous call on the same context."""
+    params, objs, expected = setup
+    st = torch.cuda.Stream()
+    cx = s3dsp.Context(0, stream=st.cuda_stream, flags=s3dsp.CONTEXT_DEFERRED_CHECKS | s3dsp.CONTEXT_COPY_STREAMS)
+    order = [0, 1, 2, 3, 3, 2, 1, 0, 0, 2, 1, 3]  # every slot reused several times
+    outs = [torch.empty((objs[t][0].shape[0], C), dtype=torch.float32).pin_memory() for t in order]
+    cx.fork()
+    for j, t in enumerate(order):
+        coords, x = objs[t]
+        cx.res_block_gn_host_queued(s3dsp.PREC_BF16, coords, x, params["w1"], params["b1"], params["gamma"],
+                                    params["beta"], params["w2"], params["b2"], outs[j])
+    cx.check()
+    for j, t in enumerate(order):
+        assert torch.equal(outs[j], expected[t]), f"call {j} (object {t}): output differs from the synchronous call's"
+    coords, x = objs[2]
+    out = torch.empty((coords.shape[0], C), dtype=torch.float32).pin_memory()
+    cx.res_block_gn_host(s3dsp.PREC_BF16, coords, x, params["w1"], params["b1"], params["gamma"], params["beta"],
+                         params["w2"], params["b2"], out)
+    assert torch.equal(out, expected[2])
+    cx.close()
+    plain = s3dsp.Context(0)
+    plain.fork()  # no copy streams: both are no-ops
+    plain.join()
+
+
 def test_queued_host_block_needs_deferred_checks(setup):
     params, objs, _ = setup
     cx = s3dsp.Context(0)
